@@ -1,0 +1,155 @@
+/*
+ * roaster_cuda.h -- C-ABI of the B200 (sm_100a) hybrid-attention hot path.
+ *
+ * Plain C, in the style of the reference's src/kernels.h: size_t dims, caller-owned buffers,
+ * no ownership transfer, `int` 0 = ok / -1 = failed (the caller maps -1 to
+ * MODEL_FORWARD_ERROR, model.h:43-44). There is no CPU fallback: with no usable GPU every
+ * compute entry point returns -1.
+ *
+ * The reference keeps the attention and DeltaNet math inline in src/model.c; each entry point
+ * below names the model.c lines it replaces. The KV cache and the recurrent state become
+ * device-resident ("buffer residency"): allocate them with kernel_cuda_alloc. The KV cache is
+ * f16 [capacity][2 kv heads][256] for K and V separately (the reference's fp32 layout,
+ * model.c:369-380, at half the bytes); the DeltaNet state keeps the reference layout
+ * fp32 [32 value heads][128 key rows][128 value cols] (model.c:412-428).
+ *
+ * Threading: calls may come from any host thread but must not overlap (the reference
+ * serialises model steps with its slot step lock, slots.c:864-891). All work goes to one CUDA
+ * stream per process (kernel_cuda_set_stream). "Device" entry points are asynchronous on that
+ * stream; "host" entry points stage their small per-step inputs/outputs through pinned memory
+ * and return when the results are in the caller's buffers.
+ *
+ * Device faults are never used for error reporting: kernels record failures (e.g. a bounded
+ * wait that ran out) in a device error word, reported by kernel_cuda_synchronize().
+ */
+#ifndef ROASTER_CUDA_H
+#define ROASTER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Shapes fixed by the model (reference src/model.h:15-41). */
+#define KERNEL_ATTN_Q_HEADS    16
+#define KERNEL_ATTN_KV_HEADS   2
+#define KERNEL_ATTN_HEAD_DIM   256
+#define KERNEL_DN_K_HEADS      16
+#define KERNEL_DN_V_HEADS      32
+#define KERNEL_DN_HEAD_DIM     128
+/* Floats in one split-KV softmax partial of a (slot, kv head): m[8], l[8], o[8][256]. */
+#define KERNEL_ATTN_PARTIAL_FLOATS (8 + 8 + 8 * 256)
+
+/* ------------------------------------------------------------------ lifecycle
+ * Mirrors kernel_vk_shutdown / kernel_vk_trim_scratch (kernels.h:95-100). */
+
+/* Select and initialise a device (primary context). 0 = ok, -1 = no usable sm_100 device. */
+int  kernel_cuda_init(int device);
+/* Free every library-owned device/pinned buffer. The library can be re-initialised. */
+void kernel_cuda_shutdown(void);
+/* Free the grow-only scratch (split-KV partials, staging); recreated on demand. */
+void kernel_cuda_trim_scratch(void);
+/* Stream for all subsequent work (a cudaStream_t; NULL = the legacy default stream). */
+int  kernel_cuda_set_stream(void *stream);
+/* Wait for the stream; 0 = ok, -1 = a CUDA error or a kernel-recorded failure (cleared). */
+int  kernel_cuda_synchronize(void);
+/* Text of the last failure recorded by the library (never NULL). */
+const char *kernel_cuda_last_error(void);
+/* Number of kernels this library launched since load (diagnostics / bench accounting). */
+uint64_t kernel_cuda_launch_count(void);
+
+/* ------------------------------------------------------------------ buffer residency
+ * Replaces locked_calloc_checked / locked_buffer_free for KVCache.k/.v and SSMState.state
+ * (model.c:54-99, 355-461) and the host memcpy/memmove that touch them (kvwindow.c, state.c). */
+
+void *kernel_cuda_alloc(size_t bytes);                 /* zero-filled device memory, NULL on failure */
+int   kernel_cuda_free(void *ptr);
+int   kernel_cuda_upload(void *dst_dev, const void *src_host, size_t bytes);   /* synchronous */
+int   kernel_cuda_download(void *dst_host, const void *src_dev, size_t bytes); /* synchronous */
+int   kernel_cuda_memmove(void *dst_dev, const void *src_dev, size_t bytes);   /* overlap-safe, async */
+
+/* ------------------------------------------------------------------ gated attention, decode
+ * Replaces model.c:801-861 (Q|G split, q/k RMSNorm, partial RoPE, KV append, GQA softmax
+ * attention over the window, sigmoid output gate) for one token per slot. */
+
+typedef struct {
+    const float *q;          /* 16 rows of 256 floats, `qg_stride` floats apart                */
+    const float *gate;       /* 16 rows of 256 gate logits, same stride                        */
+    size_t qg_stride;        /* 256 for separate buffers, 512 for the interleaved projection    */
+                             /* [Q0|G0|Q1|G1|...] (then q = qg, gate = qg + 256)                */
+    const float *k_new;      /* [2][256] raw K projection of the new token                       */
+    const float *v_new;      /* [2][256] V projection of the new token                           */
+    const float *q_norm;     /* [256] attn_q_norm weight                                         */
+    const float *k_norm;     /* [256] attn_k_norm weight                                         */
+    uint16_t *k_cache;       /* f16 [capacity][2][256], device, 16-byte aligned                  */
+    uint16_t *v_cache;       /* f16 [capacity][2][256]                                           */
+    size_t capacity;         /* window capacity in tokens                                        */
+    size_t length;           /* cached tokens before this step; the new token is written at     */
+                             /* index `length` (must be < capacity when append != 0)            */
+    size_t position;         /* absolute RoPE position of the new token                          */
+    float *out;              /* [16][256] gated attention output                                 */
+    int append;              /* 1 = normal decode. 0 = this window slice takes no new token and  */
+                             /* k_new/v_new/gate/out are unused (split-KV partial mode only)     */
+} KernelAttnDecodeJob;
+
+/* Device-pointer batch: every pointer in every job is device memory. Asynchronous. The new
+ * token attends at fp32 in this step and is stored rounded to f16 for later steps. */
+int kernel_attn_decode_batch(const KernelAttnDecodeJob *jobs, int n);
+
+/* Same, with q/gate/k_new/v_new/q_norm/k_norm/out in HOST memory (caches on the device).
+ * Synchronous: returns when every `out` holds its result. */
+int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n);
+
+/* Drop-in for full_attention's core (model.c:801-861) with model.c's own host buffers:
+ * q_gate = the interleaved [16][512] projection, k_new/v_new = attn_k/attn_v [512],
+ * q_norm/k_norm = R->qnorm/R->knorm, caches = the device-resident KVCache.k/.v, out = attn_out
+ * [4096]. The caller then increments kv->length. Synchronous. */
+int kernel_attn_decode(const float *q_gate, const float *k_new, const float *v_new,
+                       const float *q_norm, const float *k_norm,
+                       uint16_t *k_cache, uint16_t *v_cache, size_t capacity,
+                       size_t length, size_t position, float *out);
+
+/* Split-KV partial mode (long-context decode with the window split across GPUs): each job
+ * covers this GPU's slice of a slot's window (`length` cached tokens in its own cache buffers);
+ * the job with append = 1 also appends and scores the new token. Writes, per job and kv head,
+ * one merged softmax partial of KERNEL_ATTN_PARTIAL_FLOATS floats to
+ * partials[(job * 2 + kv_head) * KERNEL_ATTN_PARTIAL_FLOATS]: m[8] (max score, log2 units),
+ * l[8] (sum of exp2(s - m)), o[8][256] (output normalised by l). Device pointers, async. */
+int kernel_attn_decode_partial_batch(const KernelAttnDecodeJob *jobs, int n, float *partials);
+
+/* Merge `nparts` partial buffers laid out [nparts][n][2][KERNEL_ATTN_PARTIAL_FLOATS] (e.g. one
+ * per GPU after an all-gather) and apply the sigmoid gate: out_j = merged o * sigmoid(gate_j).
+ * gates/outs: n device pointers each (16 rows of 256, gate rows `qg_stride` apart). Async. */
+int kernel_attn_merge_partials(const float *partials, int nparts, int n,
+                               const float *const *gates, size_t qg_stride,
+                               float *const *outs);
+
+/* ------------------------------------------------------------------ Gated DeltaNet, decode
+ * Replaces recurrent_delta_step (model.c:272-323): per value head vh (key head vh % 16),
+ * d = exp(g), delta = (v - d S^T k) beta, out = (d S^T q + (k.q) delta) / sqrt(128),
+ * S <- d S + k delta^T, one read and one write of the state. */
+
+typedef struct {
+    float *state;            /* fp32 [32][128][128], device, updated in place                    */
+    const float *q;          /* [16][128] L2-normalised                                          */
+    const float *k;          /* [16][128] L2-normalised                                          */
+    const float *v;          /* [32][128]                                                        */
+    const float *g;          /* [32] log decay (the `decay`/alpha argument of model.c:272)       */
+    const float *beta;       /* [32] sigmoid(beta)                                               */
+    float *out;              /* [32][128]                                                        */
+} KernelDeltaStepJob;
+
+/* Device-pointer batch (independent states: slots and/or layers). Asynchronous. */
+int kernel_deltanet_step_batch(const KernelDeltaStepJob *jobs, int n);
+
+/* Drop-in for recurrent_delta_step(&ssm_state[layer], q, k, v, alpha, beta, out) with host
+ * q/k/v/g/beta/out and the device-resident state. Synchronous. */
+int kernel_deltanet_step(float *state, const float *q, const float *k, const float *v,
+                         const float *g, const float *beta, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,256 @@
+"""CPU oracle for the hybrid-attention hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, bench.py's CPU-baseline leg and __graft_entry__.smoke() import this package; it is
+the checker, never the thing measured as the product or shipped with it. Two implementations sit
+behind the same numpy-level functions:
+
+* ``impl="port"``: the plain-C restatement in ``roaster_oracle.c`` (liboracle.so), each function
+  citing the reference lines it follows;
+* ``impl="ref"``: the reference's own CPU code (KKB007X/Roaster ``src/model.c`` +
+  ``src/kernels.c`` lines 1-721) compiled from its sources into ``_ref/libroaster_ref.so`` by
+  ``oracle/Makefile`` (see ``ref_harness.c`` for how its static functions are driven).
+
+Shapes (fp32 unless stated): q/gate ``[16, 256]`` (or interleaved ``[16, 512]``), k/v new
+``[2, 256]``, KV cache f16 ``[L, 2, 256]``, DeltaNet state ``[32, 128, 128]``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_PORT = os.path.join(HERE, "liboracle.so")
+_REF = os.path.join(HERE, "_ref", "libroaster_ref.so")
+
+_fp = C.POINTER(C.c_float)
+_u16p = C.POINTER(C.c_uint16)
+_libs: dict = {}
+
+
+def build(quiet: bool = True) -> None:
+    """Compile liboracle.so and, when the reference sources are present, _ref (make)."""
+    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def have_ref() -> bool:
+    return os.path.exists(_REF)
+
+
+def _load(which: str):
+    if which in _libs:
+        return _libs[which]
+    path = _PORT if which == "port" else _REF
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"oracle library missing: {path} (run make -C oracle)")
+    lib = C.CDLL(path)
+    if which == "port":
+        lib.orc_attn_prefill.argtypes = [C.c_size_t, _fp, _fp, C.c_size_t, C.c_size_t, _fp, _fp,
+                                         _fp, _fp, _u16p, _u16p, C.c_size_t, C.c_size_t,
+                                         _fp, _fp, _fp]
+        lib.orc_attn_prefill.restype = C.c_int
+        lib.orc_attn_decode_partial.argtypes = [_fp, C.c_size_t, _fp, _u16p, _u16p, C.c_size_t,
+                                                C.c_size_t, C.c_size_t, _fp, _fp, _fp]
+        lib.orc_attn_decode_partial.restype = C.c_int
+        lib.orc_delta_step.argtypes = [_fp] * 7
+        lib.orc_delta_step.restype = None
+        lib.orc_delta_prefill.argtypes = [_fp, C.c_size_t] + [_fp] * 6
+        lib.orc_delta_prefill.restype = None
+        lib.orc_f32_to_f16.argtypes = [C.c_float]
+        lib.orc_f32_to_f16.restype = C.c_uint16
+    else:
+        lib.ref_attn_decode.argtypes = [_fp] * 7 + [C.c_size_t, C.c_size_t, _fp, _fp, _fp]
+        lib.ref_attn_decode.restype = C.c_int
+        lib.ref_attn_prefill.argtypes = [C.c_int] + [_fp] * 7 + [C.c_size_t, C.c_size_t,
+                                                                   _fp, _fp, _fp]
+        lib.ref_attn_prefill.restype = C.c_int
+        lib.ref_delta_step.argtypes = [_fp] * 7
+        lib.ref_delta_step.restype = None
+        lib.ref_delta_prefill.argtypes = [_fp, C.c_int] + [_fp] * 6
+        lib.ref_delta_prefill.restype = None
+        lib.ref_decode_ctx_new.argtypes = [C.c_size_t, _fp, _fp]
+        lib.ref_decode_ctx_new.restype = C.c_void_p
+        lib.ref_decode_ctx_k.argtypes = [C.c_void_p]
+        lib.ref_decode_ctx_k.restype = _fp
+        lib.ref_decode_ctx_v.argtypes = [C.c_void_p]
+        lib.ref_decode_ctx_v.restype = _fp
+        lib.ref_decode_ctx_step.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t]
+        lib.ref_decode_ctx_step.restype = C.c_int
+        lib.ref_decode_ctx_projections.argtypes = [C.c_void_p]
+        lib.ref_decode_ctx_projections.restype = None
+        lib.ref_decode_ctx_free.argtypes = [C.c_void_p]
+        lib.ref_decode_ctx_free.restype = None
+        lib.ref_max_threads.argtypes = []
+        lib.ref_max_threads.restype = C.c_int
+    _libs[which] = lib
+    return lib
+
+
+def _f(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous, (a.dtype, a.flags)
+    return a.ctypes.data_as(_fp)
+
+
+def _h(a: np.ndarray):
+    assert a.dtype == np.float16 and a.flags.c_contiguous
+    return a.ctypes.data_as(_u16p)
+
+
+def maxrel(a, b) -> float:
+    """max|a-b| / max|ref| -- the reference's test metric (src/test_kernels.c:31)."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    ref = float(np.abs(b).max()) if b.size else 0.0
+    return float(np.abs(a - b).max()) / (ref if ref > 0 else 1.0)
+
+
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> f16 (numpy's conversion is RNE as well)."""
+    return np.asarray(x, np.float32).astype(np.float16)
+
+
+# ----------------------------------------------------------------------------- attention
+
+def attn_decode(q, gate, k_new, v_new, qnorm, knorm, k_cache, v_cache, length, position,
+                impl: str = "port"):
+    """One gated-attention decode step for one slot.
+
+    q, gate: [16, 256]; k_new, v_new: [2, 256]; k_cache, v_cache: f16 [>=length, 2, 256].
+    Returns (out [16, 256], k_appended [2, 256], v_appended [2, 256]) in fp32."""
+    q = np.ascontiguousarray(q, np.float32)
+    gate = np.ascontiguousarray(gate, np.float32)
+    k_new = np.ascontiguousarray(k_new, np.float32)
+    v_new = np.ascontiguousarray(v_new, np.float32)
+    qnorm = np.ascontiguousarray(qnorm, np.float32)
+    knorm = np.ascontiguousarray(knorm, np.float32)
+    kc = np.ascontiguousarray(k_cache[:length], np.float16)
+    vc = np.ascontiguousarray(v_cache[:length], np.float16)
+    out = np.zeros((16, 256), np.float32)
+    ka = np.zeros((2, 256), np.float32)
+    va = np.zeros((2, 256), np.float32)
+    if impl == "port":
+        lib = _load("port")
+        kcp = kc if length else np.zeros((1, 2, 256), np.float16)
+        vcp = vc if length else np.zeros((1, 2, 256), np.float16)
+        rc = lib.orc_attn_prefill(1, _f(q), _f(gate), 256, 0, _f(k_new), _f(v_new), _f(qnorm),
+                                  _f(knorm), _h(kcp), _h(vcp), length, position, _f(out),
+                                  _f(ka), _f(va))
+    else:
+        lib = _load("ref")
+        qg = np.ascontiguousarray(np.concatenate([q, gate], axis=1), np.float32)
+        kcf = np.ascontiguousarray(kc.astype(np.float32)) if length else np.zeros(512, np.float32)
+        vcf = np.ascontiguousarray(vc.astype(np.float32)) if length else np.zeros(512, np.float32)
+        rc = lib.ref_attn_decode(_f(qg), _f(k_new), _f(v_new), _f(qnorm), _f(knorm), _f(kcf),
+                                 _f(vcf), length, position, _f(out), _f(ka), _f(va))
+    if rc != 0:
+        raise RuntimeError(f"oracle attn_decode ({impl}) failed")
+    return out, ka, va
+
+
+def attn_decode_partial(q, qnorm, k_cache, v_cache, t0, t1, position):
+    """Softmax partial (m [16], l [16], o [16, 256]) over cached tokens [t0, t1) (port only)."""
+    lib = _load("port")
+    q = np.ascontiguousarray(q, np.float32)
+    qnorm = np.ascontiguousarray(qnorm, np.float32)
+    kc = np.ascontiguousarray(k_cache, np.float16)
+    vc = np.ascontiguousarray(v_cache, np.float16)
+    m = np.zeros(16, np.float32)
+    l = np.zeros(16, np.float32)
+    o = np.zeros((16, 256), np.float32)
+    if lib.orc_attn_decode_partial(_f(q), 256, _f(qnorm), _h(kc), _h(vc), t0, t1, position,
+                                   _f(m), _f(l), _f(o)) != 0:
+        raise RuntimeError("oracle attn_decode_partial failed")
+    return m, l, o
+
+
+def attn_prefill(q, gate, k, v, qnorm, knorm, k_cache, v_cache, kbase, base, impl: str = "port"):
+    """Causal prefill of T tokens. q, gate: [T, 16, 256]; k, v: [T, 2, 256];
+    k_cache, v_cache: f16 [>=kbase, 2, 256]. Returns (out [T,16,256], k_app, v_app [T,2,256]).
+    impl="ref" goes through the reference's pf_attention, 256 tokens per call (PF_MAX_T)."""
+    q = np.ascontiguousarray(q, np.float32)
+    gate = np.ascontiguousarray(gate, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    qnorm = np.ascontiguousarray(qnorm, np.float32)
+    knorm = np.ascontiguousarray(knorm, np.float32)
+    T = q.shape[0]
+    out = np.zeros((T, 16, 256), np.float32)
+    ka = np.zeros((T, 2, 256), np.float32)
+    va = np.zeros((T, 2, 256), np.float32)
+    if impl == "port":
+        lib = _load("port")
+        kc = np.ascontiguousarray(k_cache[:kbase] if kbase else np.zeros((1, 2, 256)), np.float16)
+        vc = np.ascontiguousarray(v_cache[:kbase] if kbase else np.zeros((1, 2, 256)), np.float16)
+        rc = lib.orc_attn_prefill(T, _f(q), _f(gate), 256, 16 * 256, _f(k), _f(v), _f(qnorm),
+                                  _f(knorm), _h(kc), _h(vc), kbase, base, _f(out), _f(ka), _f(va))
+        if rc != 0:
+            raise RuntimeError("oracle attn_prefill (port) failed")
+        return out, ka, va
+    lib = _load("ref")
+    # The reference window is fp32: earlier chunks' appends stay unrounded, as in model.c.
+    win_k = np.zeros((kbase + T, 2, 256), np.float32)
+    win_v = np.zeros((kbase + T, 2, 256), np.float32)
+    if kbase:
+        win_k[:kbase] = np.asarray(k_cache[:kbase], np.float16).astype(np.float32)
+        win_v[:kbase] = np.asarray(v_cache[:kbase], np.float16).astype(np.float32)
+    qg = np.ascontiguousarray(np.concatenate([q, gate], axis=2), np.float32)  # [T,16,512]
+    t0 = 0
+    while t0 < T:
+        n = min(256, T - t0)
+        cur = kbase + t0
+        kcf = np.ascontiguousarray(win_k[:cur]) if cur else np.zeros(512, np.float32)
+        vcf = np.ascontiguousarray(win_v[:cur]) if cur else np.zeros(512, np.float32)
+        o = np.zeros((n, 16, 256), np.float32)
+        kk = np.zeros((n, 2, 256), np.float32)
+        vv = np.zeros((n, 2, 256), np.float32)
+        rc = lib.ref_attn_prefill(n, _f(np.ascontiguousarray(qg[t0:t0 + n])),
+                                  _f(np.ascontiguousarray(k[t0:t0 + n])),
+                                  _f(np.ascontiguousarray(v[t0:t0 + n])), _f(qnorm), _f(knorm),
+                                  _f(kcf), _f(vcf), cur, base + t0, _f(o), _f(kk), _f(vv))
+        if rc != 0:
+            raise RuntimeError("oracle attn_prefill (ref) failed")
+        out[t0:t0 + n] = o
+        ka[t0:t0 + n] = kk
+        va[t0:t0 + n] = vv
+        win_k[cur:cur + n] = kk
+        win_v[cur:cur + n] = vv
+        t0 += n
+    return out, ka, va
+
+
+# ----------------------------------------------------------------------------- DeltaNet
+
+def delta_step(state, q, k, v, g, beta, impl: str = "port"):
+    """One DeltaNet decode step; `state` [32,128,128] fp32 is updated IN PLACE.
+    q, k: [16,128]; v: [32,128]; g, beta: [32]. Returns out [32,128]."""
+    assert state.dtype == np.float32 and state.flags.c_contiguous
+    args = [np.ascontiguousarray(x, np.float32) for x in (q, k, v, g, beta)]
+    out = np.zeros((32, 128), np.float32)
+    fn = _load("port").orc_delta_step if impl == "port" else _load("ref").ref_delta_step
+    fn(_f(state), *[_f(a) for a in args], _f(out))
+    return out
+
+
+def delta_prefill(state, q, k, v, g, beta, impl: str = "port"):
+    """T sequential DeltaNet steps; `state` updated IN PLACE. q,k: [T,16,128]; v: [T,32,128];
+    g, beta: [T,32]. Returns out [T,32,128]."""
+    assert state.dtype == np.float32 and state.flags.c_contiguous
+    args = [np.ascontiguousarray(x, np.float32) for x in (q, k, v, g, beta)]
+    T = args[0].shape[0]
+    out = np.zeros((T, 32, 128), np.float32)
+    if impl == "port":
+        _load("port").orc_delta_prefill(_f(state), T, *[_f(a) for a in args], _f(out))
+    else:
+        _load("ref").ref_delta_prefill(_f(state), T, *[_f(a) for a in args], _f(out))
+    return out
+
+
+def ref_lib():
+    """The reference build's ctypes handle (for the timed CPU baseline)."""
+    return _load("ref")

@@ -1,0 +1,307 @@
+/*
+ * Drives the reference's OWN CPU implementation of the hot path (KKB007X/Roaster src/model.c,
+ * src/kernels.c lines 1-721), compiled from its sources by oracle/Makefile into
+ * oracle/_ref/libroaster_ref.so. TEST INFRASTRUCTURE ONLY (checker and timed CPU baseline).
+ *
+ * Nothing of the reference is copied here: this file #includes the reference's model.c from
+ * the path given to the compiler (-I<reference>/src), which reaches its static functions
+ * full_attention (model.c:783-863), pf_attention (1536-1602), recurrent_delta_step (272-323)
+ * and delta_head (1507-1534).
+ *
+ * The attention functions take their inputs through projections. They are driven literally with
+ * f32 (GGUF type 0) weight tensors, which the reference multiplies with kernel_matvec_f32
+ * (model.c:113-121):
+ *   - decode: normed = e0 and column 0 of W_q / W_k / W_v holds the wanted [Q|G], k and v, so the
+ *     projections return them exactly; W_o rows are one-hot selectors of the gated output, so
+ *     two calls (window length reset in between) read all 4096 values back through `residual`.
+ *   - prefill: token t's normed row is e_t, so column t of each W holds token t's projection; the
+ *     gated output is read from the prefill scratch (g_pf.rec) before the O projection.
+ */
+#include "model.c"
+
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- link stubs: the hot path never reaches these (quantized / Vulkan / window / weights). */
+static void unreachable(const char *what)
+{
+    fprintf(stderr, "ref_harness: unexpected call to %s\n", what);
+    abort();
+}
+int kernel_ffn_fused(const KernelFfnExpert *e, int n, const float *x, size_t i, size_t h)
+{ (void)e; (void)n; (void)x; (void)i; (void)h; unreachable("kernel_ffn_fused"); return 0; }
+int kernel_matmul_quant_batch(const KernelMatmulJob *j, int n)
+{ (void)j; (void)n; unreachable("kernel_matmul_quant_batch"); return -1; }
+void kernel_matvec_q4_k(const void *m, const float *v, float *o, size_t r, size_t c)
+{ (void)m; (void)v; (void)o; (void)r; (void)c; unreachable("kernel_matvec_q4_k"); }
+void kernel_matvec_q6_k(const void *m, const float *v, float *o, size_t r, size_t c)
+{ (void)m; (void)v; (void)o; (void)r; (void)c; unreachable("kernel_matvec_q6_k"); }
+void kernel_matvec_quant_batch(const KernelMatvecJob *j, int n)
+{ (void)j; (void)n; unreachable("kernel_matvec_quant_batch"); }
+int kernel_matvec_quant_begin(const KernelMatvecJob *j, int n)
+{ (void)j; (void)n; unreachable("kernel_matvec_quant_begin"); return 0; }
+void kernel_matvec_quant_end(void) { unreachable("kernel_matvec_quant_end"); }
+int kernel_moe_prefill(const KernelMoeExpert *e, int c, const float *x, float *d, size_t i, size_t h)
+{ (void)e; (void)c; (void)x; (void)d; (void)i; (void)h; unreachable("kernel_moe_prefill"); return -1; }
+void kernel_vk_trim_scratch(void) {}
+void kvspill_clear(KVSpill *sp) { (void)sp; }
+int kvw_ensure_room(Model *m, size_t need) { (void)m; (void)need; unreachable("kvw_ensure_room"); return -1; }
+size_t kvw_max_chunk(const Model *m) { (void)m; unreachable("kvw_max_chunk"); return 0; }
+int kvw_realloc(Model *m, size_t n) { (void)m; (void)n; unreachable("kvw_realloc"); return -1; }
+int kvw_refill(Model *m) { (void)m; unreachable("kvw_refill"); return -1; }
+int kvw_shrink_to_fit(Model *m, size_t n) { (void)m; (void)n; unreachable("kvw_shrink_to_fit"); return -1; }
+TensorInfo *weights_find_tensor(Weights *w, const char *n) { (void)w; (void)n; return NULL; }
+CachedExpert *weights_get_expert(Weights *w, int l, int e)
+{ (void)w; (void)l; (void)e; unreachable("weights_get_expert"); return NULL; }
+int weights_prefetch_experts(Weights *w, int l, const int *ids, int c)
+{ (void)w; (void)l; (void)ids; (void)c; unreachable("weights_prefetch_experts"); return -1; }
+
+/* ---- synthetic f32 weights (type 0 = F32 in GGUF) */
+#define ATT_LAYER 3                                 /* (3+1) % 4 == 0: a full-attention layer */
+
+static TensorInfo t_q, t_k, t_v, t_o;
+static float *W_q, *W_k, *W_v, *W_o;               /* [rows][2048] / [2048][4096] */
+static ModelRefs *R;
+
+static int ensure_weights(void)
+{
+    if (R)
+        return 0;
+    W_q = calloc((size_t)MODEL_ATTN_Q_SIZE * MODEL_HIDDEN_SIZE, sizeof(float));
+    W_k = calloc((size_t)MODEL_ATTN_K_SIZE * MODEL_HIDDEN_SIZE, sizeof(float));
+    W_v = calloc((size_t)MODEL_ATTN_V_SIZE * MODEL_HIDDEN_SIZE, sizeof(float));
+    W_o = calloc((size_t)MODEL_HIDDEN_SIZE * 4096, sizeof(float));
+    R = calloc(1, sizeof(*R));
+    if (!W_q || !W_k || !W_v || !W_o || !R)
+        return -1;
+    t_q.type = t_k.type = t_v.type = t_o.type = 0;
+    LayerRefs *L = &R->layer[ATT_LAYER];
+    L->q = (TRef){ &t_q, W_q };
+    L->k = (TRef){ &t_k, W_k };
+    L->v = (TRef){ &t_v, W_v };
+    L->o = (TRef){ &t_o, W_o };
+    return 0;
+}
+
+/* Column `col` of a [rows][2048] matrix := x. */
+static void set_col(float *W, size_t rows, size_t col, const float *x)
+{
+    for (size_t r = 0; r < rows; r++)
+        W[r * MODEL_HIDDEN_SIZE + col] = x[r];
+}
+
+typedef struct {
+    Model m;
+    KVCache kv[MODEL_NUM_LAYERS];
+    float *normed, *attn_q, *attn_k, *attn_v, *residual;
+} Rig;
+
+static int rig_init(Rig *g, size_t capacity, const float *kc, const float *vc, size_t length,
+                    const float *qnorm, const float *knorm)
+{
+    memset(g, 0, sizeof(*g));
+    KVCache *kv = &g->kv[ATT_LAYER];
+    kv->capacity = capacity;
+    kv->k = calloc(capacity * 512, sizeof(float));
+    kv->v = calloc(capacity * 512, sizeof(float));
+    g->normed = calloc(MODEL_HIDDEN_SIZE, sizeof(float));
+    g->attn_q = calloc(MODEL_ATTN_Q_SIZE, sizeof(float));
+    g->attn_k = calloc(MODEL_ATTN_K_SIZE, sizeof(float));
+    g->attn_v = calloc(MODEL_ATTN_V_SIZE, sizeof(float));
+    g->residual = calloc(MODEL_HIDDEN_SIZE, sizeof(float));
+    g->m.attn_scratch = calloc(16 * capacity, sizeof(float));
+    if (!kv->k || !kv->v || !g->normed || !g->attn_q || !g->attn_k || !g->attn_v ||
+        !g->residual || !g->m.attn_scratch)
+        return -1;
+    if (length) {
+        memcpy(kv->k, kc, length * 512 * sizeof(float));
+        memcpy(kv->v, vc, length * 512 * sizeof(float));
+    }
+    kv->length = length;
+    R->layer[ATT_LAYER].qnorm = qnorm;
+    R->layer[ATT_LAYER].knorm = knorm;
+    g->m.kv_cache = g->kv;
+    g->m.refs = R;
+    g->m.normed = g->normed;
+    g->m.attn_q = g->attn_q;
+    g->m.attn_k = g->attn_k;
+    g->m.attn_v = g->attn_v;
+    g->m.residual = g->residual;
+    g->m.context_length = capacity;
+    g->m.initialized = true;
+    return 0;
+}
+
+static void rig_free(Rig *g)
+{
+    free(g->kv[ATT_LAYER].k);
+    free(g->kv[ATT_LAYER].v);
+    free(g->normed);
+    free(g->attn_q);
+    free(g->attn_k);
+    free(g->attn_v);
+    free(g->residual);
+    free(g->m.attn_scratch);
+}
+
+/* One decode step through full_attention. q_gate: [16][512] interleaved Q|G; k_new, v_new:
+ * [512]; kc/vc: fp32 window [length][512]. out: [4096] gated attention output; k_app/v_app:
+ * [512] what the step appended. 0 = ok. */
+int ref_attn_decode(const float *q_gate, const float *k_new, const float *v_new,
+                    const float *qnorm, const float *knorm, const float *kc, const float *vc,
+                    size_t length, size_t position, float *out, float *k_app, float *v_app)
+{
+    if (ensure_weights() != 0)
+        return -1;
+    Rig g;
+    if (rig_init(&g, length + 1, kc, vc, length, qnorm, knorm) != 0) {
+        rig_free(&g);
+        return -1;
+    }
+    set_col(W_q, MODEL_ATTN_Q_SIZE, 0, q_gate);
+    set_col(W_k, MODEL_ATTN_K_SIZE, 0, k_new);
+    set_col(W_v, MODEL_ATTN_V_SIZE, 0, v_new);
+    g.normed[0] = 1.0f;
+    int rc = 0;
+    for (int half = 0; half < 2 && rc == 0; half++) {
+        memset(W_o, 0, (size_t)MODEL_HIDDEN_SIZE * 4096 * sizeof(float));
+        for (size_t r = 0; r < MODEL_HIDDEN_SIZE; r++)
+            W_o[r * 4096 + (size_t)half * MODEL_HIDDEN_SIZE + r] = 1.0f;
+        g.kv[ATT_LAYER].length = length;
+        g.m.position = position;
+        rc = full_attention(&g.m, ATT_LAYER);
+        memcpy(out + (size_t)half * MODEL_HIDDEN_SIZE, g.residual, MODEL_HIDDEN_SIZE * sizeof(float));
+    }
+    if (rc == 0) {
+        memcpy(k_app, g.kv[ATT_LAYER].k + length * 512, 512 * sizeof(float));
+        memcpy(v_app, g.kv[ATT_LAYER].v + length * 512, 512 * sizeof(float));
+    }
+    for (size_t r = 0; r < MODEL_ATTN_Q_SIZE; r++)
+        W_q[r * MODEL_HIDDEN_SIZE] = 0.0f;
+    rig_free(&g);
+    return rc;
+}
+
+/* Causal prefill of T <= 256 tokens through pf_attention. q_gate: [T][16][512]; k, v: [T][512];
+ * kc/vc: fp32 window [kbase][512]. out: [T][4096] gated output; k_app/v_app: [T][512]. */
+int ref_attn_prefill(int T, const float *q_gate, const float *k, const float *v,
+                     const float *qnorm, const float *knorm, const float *kc, const float *vc,
+                     size_t kbase, size_t base, float *out, float *k_app, float *v_app)
+{
+    if (T <= 0 || T > PF_MAX_T || ensure_weights() != 0)
+        return -1;
+    Rig g;
+    if (rig_init(&g, kbase + (size_t)T, kc, vc, kbase, qnorm, knorm) != 0 ||
+        pf_ensure(kbase + (size_t)T) != 0) {
+        rig_free(&g);
+        return -1;
+    }
+    memset(g_pf.nrm, 0, (size_t)T * PF_H * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        g_pf.nrm[(size_t)t * PF_H + (size_t)t] = 1.0f;
+        set_col(W_q, MODEL_ATTN_Q_SIZE, (size_t)t, q_gate + (size_t)t * MODEL_ATTN_Q_SIZE);
+        set_col(W_k, MODEL_ATTN_K_SIZE, (size_t)t, k + (size_t)t * 512);
+        set_col(W_v, MODEL_ATTN_V_SIZE, (size_t)t, v + (size_t)t * 512);
+    }
+    memset(W_o, 0, (size_t)MODEL_HIDDEN_SIZE * 4096 * sizeof(float));
+    int rc = pf_attention(&g.m, ATT_LAYER, T, base);
+    if (rc == 0) {
+        memcpy(out, g_pf.rec, (size_t)T * 4096 * sizeof(float));
+        memcpy(k_app, g.kv[ATT_LAYER].k + kbase * 512, (size_t)T * 512 * sizeof(float));
+        memcpy(v_app, g.kv[ATT_LAYER].v + kbase * 512, (size_t)T * 512 * sizeof(float));
+    }
+    memset(W_q, 0, (size_t)MODEL_ATTN_Q_SIZE * MODEL_HIDDEN_SIZE * sizeof(float));
+    memset(W_k, 0, (size_t)MODEL_ATTN_K_SIZE * MODEL_HIDDEN_SIZE * sizeof(float));
+    memset(W_v, 0, (size_t)MODEL_ATTN_V_SIZE * MODEL_HIDDEN_SIZE * sizeof(float));
+    rig_free(&g);
+    return rc;
+}
+
+/* A reusable full_attention rig for the timed CPU baseline: the caller fills the fp32 window
+ * (ref_decode_ctx_k / _v) once and times ref_decode_ctx_step. full_attention also runs its
+ * Q/K/V/O projections as f32 matvecs; ref_decode_ctx_projections runs exactly those four
+ * kernel_matvec_f32 calls so the baseline can subtract their time and report the attention
+ * work alone. */
+typedef struct RefDecodeCtx { Rig g; } RefDecodeCtx;
+
+RefDecodeCtx *ref_decode_ctx_new(size_t capacity, const float *qnorm, const float *knorm)
+{
+    if (ensure_weights() != 0)
+        return NULL;
+    RefDecodeCtx *c = calloc(1, sizeof(*c));
+    if (!c)
+        return NULL;
+    if (rig_init(&c->g, capacity, NULL, NULL, 0, qnorm, knorm) != 0) {
+        rig_free(&c->g);
+        free(c);
+        return NULL;
+    }
+    return c;
+}
+
+float *ref_decode_ctx_k(RefDecodeCtx *c) { return c->g.kv[ATT_LAYER].k; }
+float *ref_decode_ctx_v(RefDecodeCtx *c) { return c->g.kv[ATT_LAYER].v; }
+
+void ref_decode_ctx_free(RefDecodeCtx *c)
+{
+    if (!c)
+        return;
+    rig_free(&c->g);
+    free(c);
+}
+
+/* Run full_attention once over a window of `length` cached tokens (plus the appended one). */
+int ref_decode_ctx_step(RefDecodeCtx *c, size_t length, size_t position)
+{
+    c->g.kv[ATT_LAYER].length = length;
+    c->g.m.position = position;
+    c->g.normed[0] = 1.0f;
+    return full_attention(&c->g.m, ATT_LAYER);
+}
+
+/* The four projection matvecs full_attention issues (model.c:796-800 and 862), same shapes. */
+void ref_decode_ctx_projections(RefDecodeCtx *c)
+{
+    static float qg[MODEL_ATTN_Q_SIZE];
+    kernel_matvec_f32(W_q, c->g.normed, qg, MODEL_ATTN_Q_SIZE, MODEL_HIDDEN_SIZE);
+    kernel_matvec_f32(W_k, c->g.normed, c->g.attn_k, MODEL_ATTN_K_SIZE, MODEL_HIDDEN_SIZE);
+    kernel_matvec_f32(W_v, c->g.normed, c->g.attn_v, MODEL_ATTN_V_SIZE, MODEL_HIDDEN_SIZE);
+    kernel_matvec_f32(W_o, qg, c->g.residual, MODEL_HIDDEN_SIZE, 4096);
+}
+
+/* recurrent_delta_step on a caller state [32][128][128]. */
+void ref_delta_step(float *state, const float *q, const float *k, const float *v,
+                    const float *g, const float *beta, float *out)
+{
+    SSMState s;
+    memset(&s, 0, sizeof(s));
+    s.state = state;
+    s.state_elements = (size_t)MODEL_LINEAR_V_HEADS * 128 * 128;
+    recurrent_delta_step(&s, q, k, v, g, beta, out);
+}
+
+/* T tokens of delta_head per value head, heads in parallel (the recurrence of pf_ssm,
+ * model.c:1644-1658, without its norm/gate post-ops). q,k: [T][16][128]; v: [T][32][128];
+ * g, beta: [T][32]; out: [T][32][128]. */
+void ref_delta_prefill(float *state, int T, const float *q, const float *k, const float *v,
+                       const float *g, const float *beta, float *out)
+{
+    #pragma omp parallel for schedule(static)
+    for (int vh = 0; vh < MODEL_LINEAR_V_HEADS; vh++) {
+        const int kh = vh % MODEL_LINEAR_K_HEADS;
+        float *st = state + (size_t)vh * 128 * 128;
+        for (int t = 0; t < T; t++)
+            delta_head(st, q + ((size_t)t * 16 + kh) * 128, k + ((size_t)t * 16 + kh) * 128,
+                       v + ((size_t)t * 32 + vh) * 128, g[(size_t)t * 32 + vh],
+                       beta[(size_t)t * 32 + vh], out + ((size_t)t * 32 + vh) * 128);
+    }
+}
+
+int ref_max_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

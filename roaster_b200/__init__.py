@@ -1,0 +1,177 @@
+"""roaster_b200 -- B200 (sm_100a) hybrid-attention hot path behind a plain-C ABI.
+
+The product is ``libroaster_b200.so`` (CUDA kernels + the C-ABI declared in
+``include/roaster_cuda.h``). This module is a thin ctypes binding for Python callers (tests,
+bench.py): it mirrors the C job structs and forwards to the library. There is no fallback --
+if the library is missing, or no B200 is present, calls raise.
+
+Device buffers are passed as raw addresses (e.g. ``torch.Tensor.data_ptr()``); the library never
+sees torch types.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libroaster_b200.so")
+HEADER = os.path.join(HERE, "..", "include", "roaster_cuda.h")
+
+ATTN_Q_HEADS = 16
+ATTN_KV_HEADS = 2
+ATTN_HEAD_DIM = 256
+DN_K_HEADS = 16
+DN_V_HEADS = 32
+DN_HEAD_DIM = 128
+ATTN_PARTIAL_FLOATS = 8 + 8 + 8 * 256
+
+_vp = C.c_void_p
+_sz = C.c_size_t
+
+
+class KernelAttnDecodeJob(C.Structure):
+    """Mirror of ``KernelAttnDecodeJob`` (include/roaster_cuda.h)."""
+    _fields_ = [
+        ("q", _vp), ("gate", _vp), ("qg_stride", _sz), ("k_new", _vp), ("v_new", _vp),
+        ("q_norm", _vp), ("k_norm", _vp), ("k_cache", _vp), ("v_cache", _vp),
+        ("capacity", _sz), ("length", _sz), ("position", _sz), ("out", _vp), ("append", C.c_int),
+    ]
+
+
+class KernelDeltaStepJob(C.Structure):
+    """Mirror of ``KernelDeltaStepJob`` (include/roaster_cuda.h)."""
+    _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp),
+                ("out", _vp)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libroaster_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m roaster_b200.build`")
+    L = C.CDLL(LIB_PATH)
+    sig = {
+        "kernel_cuda_init": (C.c_int, [C.c_int]),
+        "kernel_cuda_shutdown": (None, []),
+        "kernel_cuda_trim_scratch": (None, []),
+        "kernel_cuda_set_stream": (C.c_int, [_vp]),
+        "kernel_cuda_synchronize": (C.c_int, []),
+        "kernel_cuda_last_error": (C.c_char_p, []),
+        "kernel_cuda_launch_count": (C.c_uint64, []),
+        "kernel_cuda_alloc": (_vp, [_sz]),
+        "kernel_cuda_free": (C.c_int, [_vp]),
+        "kernel_cuda_upload": (C.c_int, [_vp, _vp, _sz]),
+        "kernel_cuda_download": (C.c_int, [_vp, _vp, _sz]),
+        "kernel_cuda_memmove": (C.c_int, [_vp, _vp, _sz]),
+        "kernel_attn_decode_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
+        "kernel_attn_decode_batch_host": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
+        "kernel_attn_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+        "kernel_attn_decode_partial_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int,
+                                                       _vp]),
+        "kernel_attn_merge_partials": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp), _sz,
+                                                 C.POINTER(_vp)]),
+        "kernel_deltanet_step_batch": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
+        "kernel_deltanet_step": (C.c_int, [_vp] * 7),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def header_symbols(path: str = HEADER) -> list[str]:
+    """Names of the functions include/roaster_cuda.h declares."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kernel_\w+)\s*\(", text)))
+
+
+def last_error() -> str:
+    return (lib().kernel_cuda_last_error() or b"").decode()
+
+
+def check(rc: int, what: str = "roaster_b200") -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: {last_error()}")
+
+
+def init(device: int = 0) -> None:
+    check(lib().kernel_cuda_init(device), "kernel_cuda_init")
+
+
+def set_stream(stream) -> None:
+    """Use a CUDA stream (torch.cuda.Stream, raw handle int, or None for the default)."""
+    handle = getattr(stream, "cuda_stream", stream)
+    check(lib().kernel_cuda_set_stream(_vp(handle or 0)), "kernel_cuda_set_stream")
+
+
+def synchronize() -> None:
+    check(lib().kernel_cuda_synchronize(), "kernel_cuda_synchronize")
+
+
+def launch_count() -> int:
+    return int(lib().kernel_cuda_launch_count())
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def attn_job(q, gate, k_new, v_new, q_norm, k_norm, k_cache, v_cache, length, position, out,
+             qg_stride: int = 256, append: bool = True, capacity: int | None = None):
+    """Build a KernelAttnDecodeJob from tensors (or raw addresses)."""
+    cap = capacity if capacity is not None else int(k_cache.shape[0])
+    return KernelAttnDecodeJob(_ptr(q), _ptr(gate), qg_stride, _ptr(k_new), _ptr(v_new),
+                               _ptr(q_norm), _ptr(k_norm), _ptr(k_cache), _ptr(v_cache), cap,
+                               int(length), int(position), _ptr(out), 1 if append else 0)
+
+
+def delta_job(state, q, k, v, g, beta, out):
+    return KernelDeltaStepJob(_ptr(state), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                              _ptr(out))
+
+
+def _arr(struct, jobs):
+    arr = (struct * len(jobs))(*jobs)
+    return arr, len(jobs)
+
+
+def attn_decode_batch(jobs) -> None:
+    arr, n = _arr(KernelAttnDecodeJob, jobs)
+    check(lib().kernel_attn_decode_batch(arr, n), "kernel_attn_decode_batch")
+
+
+def attn_decode_batch_host(jobs) -> None:
+    arr, n = _arr(KernelAttnDecodeJob, jobs)
+    check(lib().kernel_attn_decode_batch_host(arr, n), "kernel_attn_decode_batch_host")
+
+
+def attn_decode_partial_batch(jobs, partials) -> None:
+    arr, n = _arr(KernelAttnDecodeJob, jobs)
+    check(lib().kernel_attn_decode_partial_batch(arr, n, _ptr(partials)),
+          "kernel_attn_decode_partial_batch")
+
+
+def attn_merge_partials(partials, nparts: int, gates, outs, qg_stride: int = 256) -> None:
+    n = len(gates)
+    g = (_vp * n)(*[_ptr(x) for x in gates])
+    o = (_vp * n)(*[_ptr(x) for x in outs])
+    check(lib().kernel_attn_merge_partials(_ptr(partials), nparts, n, g, qg_stride, o),
+          "kernel_attn_merge_partials")
+
+
+def deltanet_step_batch(jobs) -> None:
+    arr, n = _arr(KernelDeltaStepJob, jobs)
+    check(lib().kernel_deltanet_step_batch(arr, n), "kernel_deltanet_step_batch")

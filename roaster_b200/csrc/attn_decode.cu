@@ -1,0 +1,759 @@
+// Gated GQA attention, decode: split-KV, bandwidth-bound, one launch per step for any number
+// of slots.
+//
+// Replaces reference src/model.c:801-861 (full_attention without its projections): per query
+// head h (kv head h/8) RMSNorm(q) * qnorm, RMSNorm(k) * knorm, partial NeoX RoPE on dims 0..63
+// (theta 1e7), K/V append at the window index `length`, softmax(q.k/16) over the window plus the
+// new token, times V, times sigmoid(gate).
+//
+// Work decomposition. A work item is (slot, kv head, split): `chunk` consecutive cached
+// positions of one kv head. Items are spread round-robin over persistent CTAs (one per SM).
+// In each CTA
+//   * warp 4 (producer) streams 16-position tiles of K rows and V rows (512 B each) into an
+//     8-stage shared-memory ring with cp.async.bulk (the TMA engine; no multicast), rows padded
+//     to 528 B so the warp matrix loads below are bank-conflict free. It runs ahead across item
+//     boundaries, so the stream stays busy while the consumers finish an item.
+//   * warps 0-3 (consumers) take every 4th tile. The 8 query heads of the GQA group share each
+//     tile: S^T[16 pos x 8 heads] = K[16 x 256] Q^T with f16 mma.sync (fp32 accumulate; K is the
+//     A operand via ldmatrix, Q^T the B operand held in registers), an online softmax across the
+//     tile's positions with warp shuffles (exp2 domain), then O^T[256 x 8] += V^T P^T with V^T
+//     loaded by ldmatrix.trans and P^T made by transposing the probability fragment in
+//     registers (movmatrix). The 8 x 16-position tile is exactly one m16n8k16 shape, so no MMA
+//     lane is padding.
+//   * at the end of an item the 4 warps' (m, l, O) are merged and written as one partial record;
+//     the last item of a (slot, kv head) to finish (an atomic counter) merges all of them plus
+//     the new token's own partial (scored at fp32 by the split-0 item, which also appends the
+//     token's K/V to the f16 cache), applies the gate and writes the output.
+//
+// Every mbarrier wait is bounded; a timeout sets the device error word instead of hanging.
+#include "ptx.cuh"
+#include "runtime.h"
+#include "../../include/roaster_cuda.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace rb {
+namespace {
+
+constexpr int kHD = 256;                          // head dim
+constexpr int kTile = 16;                         // positions per stage
+constexpr int kStages = 8;
+constexpr int kCons = 4;                          // consumer warps
+constexpr int kThreads = (kCons + 1) * 32;        // + producer warp
+constexpr int kRowBytes = 528;                    // 512 B row + 16 B pad
+constexpr int kStageBytes = 2 * kTile * kRowBytes;  // K rows then V rows
+constexpr int kTxBytes = 2 * kTile * 512;
+constexpr int kMaxJobs = 64;
+constexpr int kPF = KERNEL_ATTN_PARTIAL_FLOATS;   // m[8] l[8] o[8][256]
+constexpr int kMaxSplits = 256;
+constexpr int kOStride = 260;                     // padded head stride of the merge buffer
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DJob {
+    const float *q, *gate;
+    const float *k_new, *v_new, *q_norm, *k_norm;
+    __half *k_cache, *v_cache;
+    float *out;
+    long long qg_stride, length, position;
+    int item_base, nsplit, append, pad;
+};
+
+struct DParams {
+    DJob jobs[kMaxJobs];
+    float inv_freq[32];
+    float *part;        // [nitems][kPF]
+    float *newpart;     // [njobs][2][kPF]
+    int *counters;      // [njobs][2]
+    float *pout;        // partial mode: [njobs][2][kPF], else null
+    unsigned *err;
+    int njobs, nitems, chunk;
+};
+
+struct Smem {
+    alignas(128) unsigned char stage[kStages][kStageBytes];
+    float qf[8][kHD];                     // prepped q (fp32) of the current item
+    float kf[kHD];                        // prepped new k
+    float ow[kCons][8][kOStride];         // per-warp O (merge)
+    float mw[kCons][8], lw[kCons][8];
+    float cw[kMaxSplits + 1][8];          // combine weights
+    float red[8];
+    alignas(8) unsigned long long full[kStages], empty[kStages];
+    int flag, abort;
+};
+
+__device__ __forceinline__ void item_decode(const DParams &p, int item, int &j, int &kvh, int &split)
+{
+    int lo = 0, hi = p.njobs - 1;
+    while (lo < hi) {                       // last job with item_base <= item
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.jobs[mid].item_base <= item)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    j = lo;
+    const int local = item - p.jobs[lo].item_base;
+    kvh = local & 1;
+    split = local >> 1;
+}
+
+__device__ __forceinline__ void item_range(const DParams &p, const DJob &J, int split, long long &t0,
+                                           long long &t1)
+{
+    t0 = (long long)split * p.chunk;
+    t1 = t0 + p.chunk < J.length ? t0 + p.chunk : J.length;
+    if (t1 < t0)
+        t1 = t0;
+}
+
+__device__ __forceinline__ void set_error(const DParams &p, unsigned bits, Smem &sm)
+{
+    atomicOr(p.err, bits);
+    *reinterpret_cast<volatile int *>(&sm.abort) = 1;
+}
+
+__device__ __forceinline__ bool aborted(Smem &sm)
+{
+    return *reinterpret_cast<volatile int *>(&sm.abort) != 0;
+}
+
+// RMSNorm * w then RoPE of the 8 query heads of kv head `kvh` into sm.qf (128 consumer threads).
+__device__ void prep_q(const DParams &p, const DJob &J, int kvh, Smem &sm, int t)
+{
+    const int h = t >> 4, g = t & 15;
+    const float *src = J.q + (long long)(kvh * 8 + h) * J.qg_stride;
+    float x[16], ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        x[i] = __ldg(src + g + 16 * i);
+        ss = fmaf(x[i], x[i], ss);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / (float)kHD + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        sm.qf[h][g + 16 * i] = x[i] * inv * __ldg(J.q_norm + g + 16 * i);
+    named_bar_sync(1, 128);
+    const float pos = (float)J.position;
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int pi = t + 128 * k, hh = pi >> 5, jj = pi & 31;
+        float sn, cs;
+        sincosf(pos * p.inv_freq[jj], &sn, &cs);
+        const float a = sm.qf[hh][jj], b = sm.qf[hh][jj + 32];
+        sm.qf[hh][jj] = a * cs - b * sn;
+        sm.qf[hh][jj + 32] = b * cs + a * sn;
+    }
+    named_bar_sync(1, 128);
+}
+
+// New token of (job, kvh): normalise + rotate k, append K/V (f16) at index `length`, and write
+// its fp32 softmax partial (m = q.k/16 in log2 units, l = 1, o = v).
+__device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, Smem &sm, int t)
+{
+    const float *kn = J.k_new + kvh * kHD;
+    const float x0 = __ldg(kn + t), x1 = __ldg(kn + t + 128);
+    float ss = x0 * x0 + x1 * x1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((t & 31) == 0)
+        sm.red[t >> 5] = ss;
+    named_bar_sync(1, 128);
+    ss = sm.red[0] + sm.red[1] + sm.red[2] + sm.red[3];
+    const float inv = 1.0f / sqrtf(ss / (float)kHD + 1e-6f);
+    sm.kf[t] = x0 * inv * __ldg(J.k_norm + t);
+    sm.kf[t + 128] = x1 * inv * __ldg(J.k_norm + t + 128);
+    named_bar_sync(1, 128);
+    if (t < 32) {
+        float sn, cs;
+        sincosf((float)J.position * p.inv_freq[t], &sn, &cs);
+        const float a = sm.kf[t], b = sm.kf[t + 32];
+        sm.kf[t] = a * cs - b * sn;
+        sm.kf[t + 32] = b * cs + a * sn;
+    }
+    named_bar_sync(1, 128);
+    // append (cached K is normed + rotated, V raw; model.c:815-819)
+    const long long row = (J.length * 2 + kvh) * kHD;
+    const float *vn = J.v_new + kvh * kHD;
+    J.k_cache[row + t] = __float2half_rn(sm.kf[t]);
+    J.k_cache[row + t + 128] = __float2half_rn(sm.kf[t + 128]);
+    J.v_cache[row + t] = __float2half_rn(__ldg(vn + t));
+    J.v_cache[row + t + 128] = __float2half_rn(__ldg(vn + t + 128));
+    // scores of the 8 heads against the new key, fp32
+    const int h = t >> 4, g = t & 15;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        s = fmaf(sm.qf[h][g + 16 * i], sm.kf[g + 16 * i], s);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    float *rec = p.newpart + ((long long)jidx * 2 + kvh) * kPF;
+    if (g == 0) {
+        rec[h] = s * (kLog2e / 16.0f);
+        rec[8 + h] = 1.0f;
+    }
+    for (int e = t; e < 8 * kHD; e += 128)
+        rec[16 + e] = __ldg(vn + (e & (kHD - 1)));
+}
+
+// Merge `nparts` partial records (pointers computed by `rec_at`) of one (job, kvh) into either
+// the gated output (pout == null) or one merged record.
+template <typename RecAt>
+__device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int nparts, RecAt rec_at,
+                        Smem &sm, int t)
+{
+    // per head: M = max m_i, w_i = l_i * exp2(m_i - M), L = sum w_i
+    if (t < 8) {
+        float M = -INFINITY;
+        for (int i = 0; i < nparts; i++)
+            M = fmaxf(M, __ldcg(rec_at(i) + t));
+        float L = 0.f;
+        for (int i = 0; i < nparts; i++) {
+            const float m = __ldcg(rec_at(i) + t), l = __ldcg(rec_at(i) + 8 + t);
+            const float w = (m == -INFINITY) ? 0.f : l * exp2f(m - M);
+            sm.cw[i][t] = w;
+            L += w;
+        }
+        sm.mw[0][t] = M;
+        sm.lw[0][t] = L;
+    }
+    named_bar_sync(1, 128);
+    float *dst = p.pout ? p.pout + ((long long)jidx * 2 + kvh) * kPF : nullptr;
+    if (dst && t < 8) {
+        dst[t] = sm.mw[0][t];
+        dst[8 + t] = sm.lw[0][t];
+    }
+    for (int e = t; e < 8 * kHD; e += 128) {
+        const int h = e >> 8, d = e & (kHD - 1);
+        float acc = 0.f;
+        for (int i = 0; i < nparts; i++)
+            acc = fmaf(sm.cw[i][h], __ldcg(rec_at(i) + 16 + e), acc);
+        const float L = sm.lw[0][h];
+        const float o = L > 0.f ? acc / L : 0.f;
+        if (dst) {
+            dst[16 + e] = o;
+        } else {
+            const float g = __ldg(J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d);
+            J.out[(kvh * 8 + h) * kHD + d] = o * (1.0f / (1.0f + expf(-g)));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ DParams p)
+{
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(smem_addr(&sm.full[s]), 1);
+            mbar_init(smem_addr(&sm.empty[s]), 1);
+        }
+        sm.abort = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    if (warp == kCons) {
+        // ------------------------------------------------------------ producer
+        unsigned seq = 0;
+        for (int item = blockIdx.x; item < p.nitems && !aborted(sm); item += gridDim.x) {
+            int j, kvh, split;
+            item_decode(p, item, j, kvh, split);
+            const DJob &J = p.jobs[j];
+            long long t0, t1;
+            item_range(p, J, split, t0, t1);
+            const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
+            for (int i = 0; i < ntiles; i++, seq++) {
+                const int s = seq % kStages;
+                const unsigned f = seq / kStages;
+                if (f > 0 && !mbar_wait(smem_addr(&sm.empty[s]), (f - 1) & 1)) {
+                    if (lane == 0)
+                        set_error(p, kErrWaitTimeout, sm);
+                    break;
+                }
+                if (lane == 0)
+                    mbar_arrive_expect_tx(smem_addr(&sm.full[s]), kTxBytes);
+                __syncwarp();
+                const int row = lane & 15, isv = lane >> 4;
+                long long pos = t0 + (long long)i * kTile + row;
+                if (pos > t1 - 1)
+                    pos = t1 - 1;               // ragged tail: repeat a valid row (masked later)
+                const __half *src = (isv ? J.v_cache : J.k_cache) + (pos * 2 + kvh) * kHD;
+                bulk_g2s(smem_addr(&sm.stage[s][0]) + isv * kTile * kRowBytes + row * kRowBytes, src,
+                         512, smem_addr(&sm.full[s]));
+            }
+        }
+        // Drain: every fill issued must land before this CTA's shared memory is released.
+        if (lane == 0 && aborted(sm)) {
+            for (unsigned q = seq > kStages ? seq - kStages : 0; q < seq; q++)
+                mbar_wait(smem_addr(&sm.full[q % kStages]), (q / kStages) & 1);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers (128 threads)
+    const int t = tid;
+    unsigned seq = 0;
+    const float sc = kLog2e / 16.0f;
+    const int r = lane >> 2, cpair = (lane & 3) * 2;
+    // per-lane shared-memory offsets of the ldmatrix row addresses
+    const uint32_t koff = (lane & 15) * kRowBytes + (lane >> 4) * 16;
+    const uint32_t voff = kTile * kRowBytes + ((lane & 7) + ((lane >> 4) << 3)) * kRowBytes + ((lane >> 3) & 1) * 16;
+
+    for (int item = blockIdx.x; item < p.nitems; item += gridDim.x) {
+        int j, kvh, split;
+        item_decode(p, item, j, kvh, split);
+        const DJob &J = p.jobs[j];
+        long long t0, t1;
+        item_range(p, J, split, t0, t1);
+        const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
+
+        prep_q(p, J, kvh, sm, t);
+        if (split == 0 && J.append)
+            new_token(p, J, j, kvh, sm, t);
+
+        uint32_t qb[16][2];
+#pragma unroll
+        for (int ks = 0; ks < 16; ks++) {
+            const float *qr = &sm.qf[r][ks * 16 + cpair];
+            qb[ks][0] = pack_f16x2(qr[0], qr[1]);
+            qb[ks][1] = pack_f16x2(qr[8], qr[9]);
+        }
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        float o[16][4];
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++)
+            o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+        for (int i = 0; i < ntiles; i++) {
+            const unsigned q = seq + i;
+            if ((int)(q % kCons) != warp)
+                continue;
+            const int s = q % kStages;
+            if (!mbar_wait(smem_addr(&sm.full[s]), (q / kStages) & 1)) {
+                if (lane == 0)
+                    set_error(p, kErrWaitTimeout, sm);
+                break;
+            }
+            const uint32_t base = smem_addr(&sm.stage[s][0]);
+            // S^T = K Q^T: four independent accumulation chains over the 16 k-steps
+            float acc[4][4];
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < 16; ks++) {
+                uint32_t a[4];
+                ldsm_x4(base + koff + ks * 32, a);
+                mma_f16(acc[ks & 3], a, qb[ks][0], qb[ks][1]);
+            }
+            const long long p0 = t0 + (long long)i * kTile + r;
+            const bool v0 = p0 < t1, v1 = p0 + 8 < t1;
+            const float x0 = v0 ? (acc[0][0] + acc[1][0] + acc[2][0] + acc[3][0]) * sc : -INFINITY;
+            const float x1 = v0 ? (acc[0][1] + acc[1][1] + acc[2][1] + acc[3][1]) * sc : -INFINITY;
+            const float x2 = v1 ? (acc[0][2] + acc[1][2] + acc[2][2] + acc[3][2]) * sc : -INFINITY;
+            const float x3 = v1 ? (acc[0][3] + acc[1][3] + acc[2][3] + acc[3][3]) * sc : -INFINITY;
+            float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);   // finite: row 0 is valid
+            const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
+            const float e0 = exp2f(x0 - n0), e1 = exp2f(x1 - n1);
+            const float e2 = exp2f(x2 - n0), e3 = exp2f(x3 - n1);
+            l0 = fmaf(l0, c0, e0 + e2);
+            l1 = fmaf(l1, c1, e1 + e3);
+            m0 = n0;
+            m1 = n1;
+            const uint32_t pb0 = movmatrix_t(pack_f16x2(e0, e1));
+            const uint32_t pb1 = movmatrix_t(pack_f16x2(e2, e3));
+#pragma unroll
+            for (int mt = 0; mt < 16; mt++) {
+                o[mt][0] *= c0;
+                o[mt][1] *= c1;
+                o[mt][2] *= c0;
+                o[mt][3] *= c1;
+                uint32_t a[4];
+                ldsm_x4_t(base + voff + mt * 32, a);
+                mma_f16(o[mt], a, pb0, pb1);
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(smem_addr(&sm.empty[s]));
+        }
+        seq += ntiles;
+
+        // ------------------------------------------------ merge the 4 warps into one record
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+        }
+        if (lane < 4) {
+            sm.mw[warp][cpair] = m0;
+            sm.mw[warp][cpair + 1] = m1;
+            sm.lw[warp][cpair] = l0;
+            sm.lw[warp][cpair + 1] = l1;
+        }
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            const int d = mt * 16 + r;
+            sm.ow[warp][cpair][d] = o[mt][0];
+            sm.ow[warp][cpair + 1][d] = o[mt][1];
+            sm.ow[warp][cpair][d + 8] = o[mt][2];
+            sm.ow[warp][cpair + 1][d + 8] = o[mt][3];
+        }
+        named_bar_sync(1, 128);
+        float *rec = p.part + (long long)item * kPF;
+        for (int e = t; e < 8 * kHD; e += 128) {
+            const int h = e >> 8, d = e & (kHD - 1);
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kCons; w++)
+                M = fmaxf(M, sm.mw[w][h]);
+            float L = 0.f, acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCons; w++) {
+                const float f = sm.mw[w][h] == -INFINITY ? 0.f : exp2f(sm.mw[w][h] - M);
+                L = fmaf(f, sm.lw[w][h], L);
+                acc = fmaf(f, sm.ow[w][h][d], acc);
+            }
+            rec[16 + e] = L > 0.f ? acc / L : 0.f;
+            if (d == 0) {
+                rec[h] = M;
+                rec[8 + h] = L;
+            }
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (t == 0) {
+            const int prev = atomicAdd(p.counters + j * 2 + kvh, 1);
+            sm.flag = (prev == J.nsplit - 1);
+        }
+        named_bar_sync(1, 128);
+        if (sm.flag) {
+            __threadfence();
+            const int ns = J.nsplit;
+            const float *part0 = p.part + (long long)(J.item_base + kvh) * kPF;
+            const float *np = p.newpart + ((long long)j * 2 + kvh) * kPF;
+            auto rec_at = [&](int i) -> const float * {
+                return i < ns ? part0 + (long long)i * 2 * kPF : np;
+            };
+            combine(p, J, j, kvh, ns + (J.append ? 1 : 0), rec_at, sm, t);
+            if (t == 0)
+                p.counters[j * 2 + kvh] = 0;
+        }
+        named_bar_sync(1, 128);
+        if (aborted(sm))
+            break;
+    }
+}
+
+// Merge of per-GPU partial records: grid (n jobs x 2 kv heads), 256 threads.
+struct MParams {
+    const float *partials;
+    const float *gates[kMaxJobs];
+    float *outs[kMaxJobs];
+    long long qg_stride;
+    int nparts, n, job0;
+};
+
+__global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__ MParams p)
+{
+    __shared__ float w[64][8], Ms[8], Ls[8];
+    const int j = blockIdx.x >> 1, kvh = blockIdx.x & 1, t = threadIdx.x;
+    const long long stride = (long long)p.n * 2 * kPF;
+    const float *rec0 = p.partials + ((long long)(p.job0 + j) * 2 + kvh) * kPF;
+    if (t < 8) {
+        float M = -INFINITY, L = 0.f;
+        for (int i = 0; i < p.nparts; i++)
+            M = fmaxf(M, rec0[i * stride + t]);
+        for (int i = 0; i < p.nparts; i++) {
+            const float m = rec0[i * stride + t];
+            const float x = m == -INFINITY ? 0.f : rec0[i * stride + 8 + t] * exp2f(m - M);
+            w[i][t] = x;
+            L += x;
+        }
+        Ms[t] = M;
+        Ls[t] = L;
+    }
+    __syncthreads();
+    for (int e = t; e < 8 * kHD; e += 256) {
+        const int h = e >> 8, d = e & (kHD - 1);
+        float acc = 0.f;
+        for (int i = 0; i < p.nparts; i++)
+            acc = fmaf(w[i][h], rec0[i * stride + 16 + e], acc);
+        const float o = Ls[h] > 0.f ? acc / Ls[h] : 0.f;
+        const float g = p.gates[j][(long long)(kvh * 8 + h) * p.qg_stride + d];
+        p.outs[j][(kvh * 8 + h) * kHD + d] = o * (1.0f / (1.0f + expf(-g)));
+    }
+}
+
+int validate(const KernelAttnDecodeJob &j, int i, bool partial)
+{
+    if (!j.q || !j.q_norm || !j.k_cache || !j.v_cache)
+        return fail("attn decode: job %d has a null pointer", i);
+    if (!aligned16(j.k_cache) || !aligned16(j.v_cache))
+        return fail("attn decode: job %d cache not 16-byte aligned", i);
+    if (j.qg_stride < 256)
+        return fail("attn decode: job %d qg_stride %zu < 256", i, j.qg_stride);
+    if (j.append) {
+        if (!j.k_new || !j.v_new || !j.k_norm)
+            return fail("attn decode: job %d has a null new-token pointer", i);
+        if (j.length >= j.capacity)
+            return fail("attn decode: job %d window full (length %zu, capacity %zu)", i, j.length,
+                        j.capacity);
+    } else if (j.length > j.capacity) {
+        return fail("attn decode: job %d length %zu > capacity %zu", i, j.length, j.capacity);
+    }
+    if (!partial && (!j.gate || !j.out))
+        return fail("attn decode: job %d has a null gate/out pointer", i);
+    return 0;
+}
+
+bool g_attr_set = false;
+
+// One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode.
+int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
+{
+    Runtime &R = rt();
+    long long total = 0;
+    for (int i = 0; i < n; i++) {
+        if (validate(jobs[i], i, pout != nullptr) != 0)
+            return -1;
+        total += (long long)jobs[i].length;
+    }
+    // Split size: about 4 items per SM and kv head, multiple of the tile, >= 64 positions, and
+    // at most kMaxSplits splits per (slot, kv head).
+    long long chunk = (total + 4ll * R.num_sms - 1) / (4ll * R.num_sms);
+    chunk = (chunk + kTile - 1) / kTile * kTile;
+    if (chunk < 64)
+        chunk = 64;
+    for (int i = 0; i < n; i++) {
+        long long need = ((long long)jobs[i].length + kMaxSplits - 1) / kMaxSplits;
+        need = (need + kTile - 1) / kTile * kTile;
+        if (need > chunk)
+            chunk = need;
+    }
+    if (chunk > (1ll << 30))
+        return fail("attn decode: window too long");
+    DParams p;
+    memset(&p, 0, sizeof(p));
+    int items = 0;
+    for (int i = 0; i < n; i++) {
+        const KernelAttnDecodeJob &s = jobs[i];
+        DJob &d = p.jobs[i];
+        d.q = s.q;
+        d.gate = s.gate;
+        d.k_new = s.k_new;
+        d.v_new = s.v_new;
+        d.q_norm = s.q_norm;
+        d.k_norm = s.k_norm;
+        d.k_cache = reinterpret_cast<__half *>(s.k_cache);
+        d.v_cache = reinterpret_cast<__half *>(s.v_cache);
+        d.out = s.out;
+        d.qg_stride = (long long)s.qg_stride;
+        d.length = (long long)s.length;
+        d.position = (long long)s.position;
+        d.append = s.append ? 1 : 0;
+        long long ns = ((long long)s.length + chunk - 1) / chunk;
+        d.nsplit = ns < 1 ? 1 : (int)ns;
+        d.item_base = items;
+        items += 2 * d.nsplit;
+    }
+    memcpy(p.inv_freq, R.inv_freq, sizeof(p.inv_freq));
+    const size_t part_floats = (size_t)items * kPF, new_floats = (size_t)n * 2 * kPF;
+    float *ws = static_cast<float *>(scratch((part_floats + new_floats) * sizeof(float)));
+    int *cnt = counters((size_t)kMaxJobs * 2);
+    if (!ws || !cnt)
+        return -1;
+    p.part = ws;
+    p.newpart = ws + part_floats;
+    p.counters = cnt;
+    p.pout = pout;
+    p.err = R.err_word;
+    p.njobs = n;
+    p.nitems = items;
+    p.chunk = (int)chunk;
+    if (!g_attr_set) {
+        if (check(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(Smem)), "attn decode smem attribute") != 0)
+            return -1;
+        g_attr_set = true;
+    }
+    const int grid = items < R.num_sms ? items : R.num_sms;
+    attn_decode_kernel<<<grid, kThreads, sizeof(Smem), R.stream>>>(p);
+    return launched("attn_decode_kernel");
+}
+
+}  // namespace
+
+int attn_decode_batch(const KernelAttnDecodeJob *jobs, int n, float *pout)
+{
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("attn decode: bad job array");
+    for (int i = 0; i < n; i += kMaxJobs) {
+        const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
+        if (launch(jobs + i, m, pout ? pout + (size_t)i * 2 * kPF : nullptr) != 0)
+            return -1;
+    }
+    return 0;
+}
+
+int attn_merge(const float *partials, int nparts, int n, const float *const *gates, size_t qg_stride,
+               float *const *outs)
+{
+    if (nparts < 1 || nparts > 64 || n < 0 || !partials || (n && (!gates || !outs)))
+        return fail("attn merge: bad arguments (nparts %d, n %d)", nparts, n);
+    for (int i = 0; i < n; i += kMaxJobs) {
+        MParams p;
+        memset(&p, 0, sizeof(p));
+        const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
+        for (int k = 0; k < m; k++) {
+            p.gates[k] = gates[i + k];
+            p.outs[k] = outs[i + k];
+            if (!p.gates[k] || !p.outs[k])
+                return fail("attn merge: null gate/out for job %d", i + k);
+        }
+        p.partials = partials;
+        p.qg_stride = (long long)qg_stride;
+        p.nparts = nparts;
+        p.n = n;
+        p.job0 = i;
+        attn_merge_kernel<<<m * 2, 256, 0, rt().stream>>>(p);
+        if (launched("attn_merge_kernel") != 0)
+            return -1;
+    }
+    return 0;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" int kernel_attn_decode_batch(const KernelAttnDecodeJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    return attn_decode_batch(jobs, n, nullptr);
+}
+
+extern "C" int kernel_attn_decode_partial_batch(const KernelAttnDecodeJob *jobs, int n, float *partials)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!partials)
+        return fail("kernel_attn_decode_partial_batch: null partials");
+    return attn_decode_batch(jobs, n, partials);
+}
+
+extern "C" int kernel_attn_merge_partials(const float *partials, int nparts, int n,
+                                          const float *const *gates, size_t qg_stride,
+                                          float *const *outs)
+{
+    if (ensure() != 0)
+        return -1;
+    return attn_merge(partials, nparts, n, gates, qg_stride, outs);
+}
+
+// Host-buffer batch: pack every job's q/gate rows, new K/V, norms into one pinned block, one
+// H2D copy, the device batch, one D2H copy of the outputs.
+extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_attn_decode_batch_host: bad job array");
+    if (n == 0)
+        return 0;
+    // per job: q 4096, gate 4096, k 512, v 512, qnorm 256, knorm 256 in; out 4096
+    const size_t in_f = 4096 * 2 + 512 * 2 + 256 * 2, out_f = 4096;
+    const size_t total = (size_t)n * (in_f + out_f);
+    float *h = static_cast<float *>(pinned(total * sizeof(float)));
+    if (!h)
+        return -1;
+    std::vector<KernelAttnDecodeJob> dj(jobs, jobs + n);
+    for (int i = 0; i < n; i++) {
+        const KernelAttnDecodeJob &s = jobs[i];
+        if (!s.q || !s.gate || !s.out || !s.q_norm || (s.append && (!s.k_new || !s.v_new || !s.k_norm)))
+            return fail("kernel_attn_decode_batch_host: job %d has a null pointer", i);
+        float *b = h + (size_t)i * in_f;
+        for (int r = 0; r < 16; r++) {
+            memcpy(b + r * 256, s.q + r * s.qg_stride, 256 * 4);
+            memcpy(b + 4096 + r * 256, s.gate + r * s.qg_stride, 256 * 4);
+        }
+        if (s.append) {
+            memcpy(b + 8192, s.k_new, 512 * 4);
+            memcpy(b + 8704, s.v_new, 512 * 4);
+            memcpy(b + 9472, s.k_norm, 256 * 4);
+        }
+        memcpy(b + 9216, s.q_norm, 256 * 4);
+    }
+    float *dev_in = static_cast<float *>(dstage(total * sizeof(float)));
+    if (!dev_in)
+        return -1;
+    cudaStream_t st = rt().stream;
+    if (check(cudaMemcpyAsync(dev_in, h, (size_t)n * in_f * 4, cudaMemcpyHostToDevice, st), "stage in") != 0)
+        return -1;
+    float *dout = dev_in + (size_t)n * in_f;
+    for (int i = 0; i < n; i++) {
+        float *b = dev_in + (size_t)i * in_f;
+        dj[i].q = b;
+        dj[i].gate = b + 4096;
+        dj[i].qg_stride = 256;
+        dj[i].k_new = b + 8192;
+        dj[i].v_new = b + 8704;
+        dj[i].q_norm = b + 9216;
+        dj[i].k_norm = b + 9472;
+        dj[i].out = dout + (size_t)i * out_f;
+    }
+    if (attn_decode_batch(dj.data(), n, nullptr) != 0)
+        return -1;
+    float *hout = h + (size_t)n * in_f;
+    if (check(cudaMemcpyAsync(hout, dout, (size_t)n * out_f * 4, cudaMemcpyDeviceToHost, st), "stage out") != 0)
+        return -1;
+    if (kernel_cuda_synchronize() != 0)
+        return -1;
+    for (int i = 0; i < n; i++)
+        memcpy(jobs[i].out, hout + (size_t)i * out_f, out_f * 4);
+    return 0;
+}
+
+extern "C" int kernel_attn_decode(const float *q_gate, const float *k_new, const float *v_new,
+                                  const float *q_norm, const float *k_norm, uint16_t *k_cache,
+                                  uint16_t *v_cache, size_t capacity, size_t length, size_t position,
+                                  float *out)
+{
+    if (!q_gate)
+        return fail("kernel_attn_decode: null q_gate");
+    KernelAttnDecodeJob j;
+    memset(&j, 0, sizeof(j));
+    j.q = q_gate;
+    j.gate = q_gate + 256;
+    j.qg_stride = 512;
+    j.k_new = k_new;
+    j.v_new = v_new;
+    j.q_norm = q_norm;
+    j.k_norm = k_norm;
+    j.k_cache = k_cache;
+    j.v_cache = v_cache;
+    j.capacity = capacity;
+    j.length = length;
+    j.position = position;
+    j.out = out;
+    j.append = 1;
+    return kernel_attn_decode_batch_host(&j, 1);
+}

@@ -1,0 +1,311 @@
+// Runtime and the lifecycle / residency part of the C-ABI (include/roaster_cuda.h).
+#include "runtime.h"
+#include "../../include/roaster_cuda.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+namespace rb {
+
+static Runtime g_rt;
+static char g_err[512] = "";
+static std::atomic<uint64_t> g_launches{0};
+
+Runtime &rt() { return g_rt; }
+
+int fail(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return -1;
+}
+
+int check(cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess)
+        return 0;
+    return fail("%s: %s", what, cudaGetErrorString(e));
+}
+
+int launched(const char *what)
+{
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check(cudaGetLastError(), what);
+}
+
+static int init_device(int device)
+{
+    int count = 0;
+    if (check(cudaGetDeviceCount(&count), "cudaGetDeviceCount") != 0)
+        return -1;
+    if (device < 0 || device >= count)
+        return fail("kernel_cuda_init: device %d not present (%d devices)", device, count);
+    cudaDeviceProp prop;
+    if (check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties") != 0)
+        return -1;
+    if (prop.major != 10)
+        return fail("kernel_cuda_init: device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    if (check(cudaSetDevice(device), "cudaSetDevice") != 0)
+        return -1;
+    unsigned *err = nullptr;
+    if (check(cudaMalloc(&err, 256), "cudaMalloc(error word)") != 0)
+        return -1;
+    if (check(cudaMemset(err, 0, 256), "cudaMemset(error word)") != 0) {
+        cudaFree(err);
+        return -1;
+    }
+    g_rt.device = device;
+    g_rt.num_sms = prop.multiProcessorCount;
+    g_rt.err_word = err;
+    // RoPE inverse frequencies with the host libm powf, the same call the reference makes
+    // (apply_rope_64, model.c:765), so both sides rotate by bit-identical angles.
+    for (int j = 0; j < 32; j++)
+        g_rt.inv_freq[j] = powf(10000000.0f, -2.0f * (float)j / 64.0f);
+    return 0;
+}
+
+int ensure()
+{
+    if (g_rt.device < 0 && init_device(0) != 0)
+        return -1;
+    return check(cudaSetDevice(g_rt.device), "cudaSetDevice");
+}
+
+void *scratch(size_t bytes)
+{
+    if (bytes <= g_rt.scratch_bytes)
+        return g_rt.scratch;
+    if (g_rt.scratch) {
+        cudaStreamSynchronize(g_rt.stream);
+        cudaFree(g_rt.scratch);
+        g_rt.scratch = nullptr;
+        g_rt.scratch_bytes = 0;
+    }
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes + bytes / 4;
+    void *p = nullptr;
+    if (check(cudaMalloc(&p, want), "cudaMalloc(scratch)") != 0)
+        return nullptr;
+    g_rt.scratch = p;
+    g_rt.scratch_bytes = want;
+    return p;
+}
+
+void *dstage(size_t bytes)
+{
+    if (bytes <= g_rt.dstage_bytes)
+        return g_rt.dstage;
+    if (g_rt.dstage) {
+        cudaStreamSynchronize(g_rt.stream);
+        cudaFree(g_rt.dstage);
+        g_rt.dstage = nullptr;
+        g_rt.dstage_bytes = 0;
+    }
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes + bytes / 4;
+    void *p = nullptr;
+    if (check(cudaMalloc(&p, want), "cudaMalloc(staging)") != 0)
+        return nullptr;
+    g_rt.dstage = p;
+    g_rt.dstage_bytes = want;
+    return p;
+}
+
+int *counters(size_t n)
+{
+    if (n <= g_rt.counters_n)
+        return g_rt.counters;
+    if (g_rt.counters) {
+        cudaStreamSynchronize(g_rt.stream);
+        cudaFree(g_rt.counters);
+        g_rt.counters = nullptr;
+        g_rt.counters_n = 0;
+    }
+    size_t want = n < 4096 ? 4096 : n * 2;
+    int *p = nullptr;
+    if (check(cudaMalloc(&p, want * sizeof(int)), "cudaMalloc(counters)") != 0)
+        return nullptr;
+    if (check(cudaMemset(p, 0, want * sizeof(int)), "cudaMemset(counters)") != 0) {
+        cudaFree(p);
+        return nullptr;
+    }
+    g_rt.counters = p;
+    g_rt.counters_n = want;
+    return p;
+}
+
+void *pinned(size_t bytes)
+{
+    if (bytes <= g_rt.pinned_bytes)
+        return g_rt.pinned;
+    if (g_rt.pinned) {
+        cudaStreamSynchronize(g_rt.stream);
+        cudaFreeHost(g_rt.pinned);
+        g_rt.pinned = nullptr;
+        g_rt.pinned_bytes = 0;
+    }
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes + bytes / 4;
+    void *p = nullptr;
+    if (check(cudaHostAlloc(&p, want, cudaHostAllocDefault), "cudaHostAlloc(staging)") != 0)
+        return nullptr;
+    g_rt.pinned = p;
+    g_rt.pinned_bytes = want;
+    return p;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" {
+
+int kernel_cuda_init(int device)
+{
+    if (g_rt.device == device)
+        return check(cudaSetDevice(device), "cudaSetDevice");
+    if (g_rt.device >= 0)
+        kernel_cuda_shutdown();
+    return init_device(device);
+}
+
+void kernel_cuda_trim_scratch(void)
+{
+    if (g_rt.device < 0)
+        return;
+    cudaSetDevice(g_rt.device);
+    cudaStreamSynchronize(g_rt.stream);
+    if (g_rt.scratch)
+        cudaFree(g_rt.scratch);
+    if (g_rt.pinned)
+        cudaFreeHost(g_rt.pinned);
+    if (g_rt.dstage)
+        cudaFree(g_rt.dstage);
+    g_rt.dstage = nullptr;
+    g_rt.dstage_bytes = 0;
+    g_rt.scratch = nullptr;
+    g_rt.scratch_bytes = 0;
+    g_rt.pinned = nullptr;
+    g_rt.pinned_bytes = 0;
+}
+
+void kernel_cuda_shutdown(void)
+{
+    if (g_rt.device < 0)
+        return;
+    kernel_cuda_trim_scratch();
+    if (g_rt.err_word)
+        cudaFree(g_rt.err_word);
+    if (g_rt.counters)
+        cudaFree(g_rt.counters);
+    g_rt = Runtime();
+}
+
+int kernel_cuda_set_stream(void *stream)
+{
+    if (ensure() != 0)
+        return -1;
+    g_rt.stream = static_cast<cudaStream_t>(stream);
+    return 0;
+}
+
+int kernel_cuda_synchronize(void)
+{
+    if (ensure() != 0)
+        return -1;
+    if (check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize") != 0)
+        return -1;
+    unsigned word = 0;
+    if (check(cudaMemcpy(&word, g_rt.err_word, sizeof(word), cudaMemcpyDeviceToHost),
+              "read error word") != 0)
+        return -1;
+    if (word) {
+        cudaMemset(g_rt.err_word, 0, sizeof(unsigned));
+        return fail("kernel-recorded failure 0x%x (%s%s)", word,
+                    (word & kErrWaitTimeout) ? "bounded wait timed out " : "",
+                    (word & kErrBadArgument) ? "bad argument" : "");
+    }
+    return 0;
+}
+
+const char *kernel_cuda_last_error(void) { return g_err; }
+
+uint64_t kernel_cuda_launch_count(void) { return g_launches.load(); }
+
+void *kernel_cuda_alloc(size_t bytes)
+{
+    if (ensure() != 0 || bytes == 0)
+        return nullptr;
+    void *p = nullptr;
+    if (check(cudaMalloc(&p, bytes), "kernel_cuda_alloc") != 0)
+        return nullptr;
+    if (check(cudaMemset(p, 0, bytes), "kernel_cuda_alloc memset") != 0) {
+        cudaFree(p);
+        return nullptr;
+    }
+    return p;
+}
+
+int kernel_cuda_free(void *ptr)
+{
+    if (!ptr)
+        return 0;
+    if (ensure() != 0)
+        return -1;
+    return check(cudaFree(ptr), "kernel_cuda_free");
+}
+
+int kernel_cuda_upload(void *dst, const void *src, size_t bytes)
+{
+    if (ensure() != 0)
+        return -1;
+    if (check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, g_rt.stream), "upload") != 0)
+        return -1;
+    return check(cudaStreamSynchronize(g_rt.stream), "upload sync");
+}
+
+int kernel_cuda_download(void *dst, const void *src, size_t bytes)
+{
+    if (ensure() != 0)
+        return -1;
+    if (check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, g_rt.stream), "download") != 0)
+        return -1;
+    return check(cudaStreamSynchronize(g_rt.stream), "download sync");
+}
+
+int kernel_cuda_memmove(void *dst, const void *src, size_t bytes)
+{
+    if (ensure() != 0)
+        return -1;
+    if (bytes == 0 || dst == src)
+        return 0;
+    const char *s = static_cast<const char *>(src);
+    char *d = static_cast<char *>(dst);
+    // Device-to-device cudaMemcpy does not promise overlap safety: move in chunks that never
+    // overlap their own destination, walking in the safe direction.
+    size_t gap = d > s ? (size_t)(d - s) : (size_t)(s - d);
+    if (gap >= bytes)
+        return check(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, g_rt.stream), "memmove");
+    if (d < s) {
+        for (size_t off = 0; off < bytes; off += gap) {
+            size_t n = bytes - off < gap ? bytes - off : gap;
+            if (check(cudaMemcpyAsync(d + off, s + off, n, cudaMemcpyDeviceToDevice, g_rt.stream),
+                      "memmove") != 0)
+                return -1;
+        }
+    } else {
+        for (size_t end = bytes; end > 0;) {
+            size_t n = end < gap ? end : gap;
+            end -= n;
+            if (check(cudaMemcpyAsync(d + end, s + end, n, cudaMemcpyDeviceToDevice, g_rt.stream),
+                      "memmove") != 0)
+                return -1;
+        }
+    }
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Internal runtime of libroaster_b200: device selection, the work stream, grow-only device
+// scratch and pinned staging, the device error word, and failure reporting. Not part of the
+// C-ABI (include/roaster_cuda.h is).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace rb {
+
+// Device error word bits, set by kernels instead of faulting.
+enum : unsigned {
+    kErrWaitTimeout = 1u << 0,   // a bounded mbarrier wait ran out
+    kErrBadArgument = 1u << 1,   // a kernel found an argument it cannot process
+};
+
+struct Runtime {
+    int device = -1;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    unsigned *err_word = nullptr;      // device, one word
+    void *scratch = nullptr;           // device, grow-only
+    size_t scratch_bytes = 0;
+    int *counters = nullptr;           // device, zero-initialised, grow-only
+    size_t counters_n = 0;
+    void *dstage = nullptr;            // device staging of host-buffer calls, grow-only
+    size_t dstage_bytes = 0;
+    void *pinned = nullptr;            // host pinned, grow-only
+    size_t pinned_bytes = 0;
+    float inv_freq[32];                // RoPE inverse frequencies, computed with host powf
+};
+
+Runtime &rt();
+// Ensure the library is initialised (device 0 by default, or the one kernel_cuda_init chose)
+// and make that device current on this thread. 0 = ok.
+int ensure();
+// Record a failure message; always returns -1.
+int fail(const char *fmt, ...);
+// Check a CUDA status; on error record it with `what` and return -1.
+int check(cudaError_t e, const char *what);
+// Check for a launch error after a kernel launch and count the launch.
+int launched(const char *what);
+// Device scratch of at least `bytes` (grow-only; growing synchronises the stream).
+void *scratch(size_t bytes);
+// Zero-initialised device int counters (grow-only, separate from scratch). Kernels that use
+// them return every counter to zero before they exit.
+int *counters(size_t n);
+// Device staging for the host-buffer entry points (grow-only, separate from scratch).
+void *dstage(size_t bytes);
+// Pinned host staging of at least `bytes` (grow-only; growing synchronises the stream).
+void *pinned(size_t bytes);
+// 16-byte alignment check for pointers handed to bulk-copy engines.
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace rb
