@@ -9,17 +9,22 @@
 // Work decomposition. A work item is (slot, kv head, split): `chunk` consecutive cached
 // positions of one kv head. Items are spread round-robin over persistent CTAs (one per SM).
 // In each CTA
-//   * warp 4 (producer) streams 16-position tiles of K rows and V rows (512 B each) into an
-//     8-stage shared-memory ring with cp.async.bulk (the TMA engine; no multicast), rows padded
-//     to 528 B so the warp matrix loads below are bank-conflict free. It runs ahead across item
-//     boundaries, so the stream stays busy while the consumers finish an item.
-//   * warps 0-3 (consumers) take every 4th tile. The 8 query heads of the GQA group share each
+//   * warps 4-7 (producers) stream 32-position stages of K and V into a 5-stage shared-memory
+//     ring with 16-byte cp.async copies: one warp instruction moves one 512-byte row (one kv
+//     head of one position), placed in a [4 chunks][32 pos][128 B] tile with the 16-byte units of
+//     row p XOR-swizzled by (p & 7), so the warp matrix loads below are bank-conflict free.
+//     Completion is tracked per stage on an mbarrier (cp.async.mbarrier.arrive). Rows past the
+//     window end are never read. The producers run ahead across item boundaries, so the stream
+//     stays busy while the consumers finish an item. (Per-row bulk copies are request-rate
+//     bound on B200: 512-byte requests top out near 2.4 TB/s, while 16-byte cp.async from four
+//     warps streams 512-byte rows at a 1 KB pitch -- this cache's layout -- at about 6.7 TB/s.)
+//   * warps 0-3 (consumers) take every 4th stage. The 8 query heads of the GQA group share each
 //     tile: S^T[16 pos x 8 heads] = K[16 x 256] Q^T with f16 mma.sync (fp32 accumulate; K is the
 //     A operand via ldmatrix, Q^T the B operand held in registers), an online softmax across the
-//     tile's positions with warp shuffles (exp2 domain), then O^T[256 x 8] += V^T P^T with V^T
-//     loaded by ldmatrix.trans and P^T made by transposing the probability fragment in
-//     registers (movmatrix). The 8 x 16-position tile is exactly one m16n8k16 shape, so no MMA
-//     lane is padding.
+//     stage's 32 positions with warp shuffles (exp2 domain), then O^T[256 x 8] += V^T P^T with
+//     V^T loaded by ldmatrix.trans and P^T made by transposing the probability fragment in
+//     registers (movmatrix). The 16-position x 8-head tile is exactly one m16n8k16 shape, so no
+//     MMA lane is padding.
 //   * at the end of an item the 4 warps' (m, l, O) are merged and written as one partial record;
 //     the last item of a (slot, kv head) to finish (an atomic counter) merges all of them plus
 //     the new token's own partial (scored at fp32 by the split-0 item, which also appends the
@@ -41,13 +46,14 @@ namespace rb {
 namespace {
 
 constexpr int kHD = 256;                          // head dim
-constexpr int kTile = 16;                         // positions per stage
-constexpr int kStages = 8;
+constexpr int kTile = 32;                         // positions per stage
+constexpr int kStages = 5;
 constexpr int kCons = 4;                          // consumer warps
-constexpr int kThreads = (kCons + 1) * 32;        // + producer warp
-constexpr int kRowBytes = 528;                    // 512 B row + 16 B pad
-constexpr int kStageBytes = 2 * kTile * kRowBytes;  // K rows then V rows
-constexpr int kTxBytes = 2 * kTile * 512;
+constexpr int kProd = 4;                          // producer warps
+constexpr int kThreads = (kCons + kProd) * 32;
+constexpr int kChunkBytes = kTile * 128;          // one 64-dim chunk of kTile positions (4 KB)
+constexpr int kHalfBytes = 4 * kChunkBytes;       // K (or V) of one stage: [4 chunks][kTile][128 B]
+constexpr int kStageBytes = 2 * kHalfBytes;       // K then V
 constexpr int kMaxJobs = 64;
 constexpr int kPF = KERNEL_ATTN_PARTIAL_FLOATS;   // m[8] l[8] o[8][256]
 constexpr int kMaxSplits = 256;
@@ -75,16 +81,21 @@ struct DParams {
 };
 
 struct Smem {
-    alignas(128) unsigned char stage[kStages][kStageBytes];
+    unsigned char stage[kStages][kStageBytes];   // [K|V][4 chunks][32 pos][128 B], swizzled
     float qf[8][kHD];                     // prepped q (fp32) of the current item
     float kf[kHD];                        // prepped new k
-    float ow[kCons][8][kOStride];         // per-warp O (merge)
+    union {
+        float ow[kCons][8][kOStride];     // per-warp O (merge of the 4 warps)
+        struct {                          // combine of all partials of a (slot, kv head)
+            float m[kMaxSplits + 1][8], l[kMaxSplits + 1][8], w[kMaxSplits + 1][8];
+        } c;
+    } u;
     float mw[kCons][8], lw[kCons][8];
-    float cw[kMaxSplits + 1][8];          // combine weights
     float red[8];
     alignas(8) unsigned long long full[kStages], empty[kStages];
     int flag, abort;
 };
+constexpr size_t kSmemBytes = sizeof(Smem) + 128;   // + alignment slack
 
 __device__ __forceinline__ void item_decode(const DParams &p, int item, int &j, int &kvh, int &split)
 {
@@ -205,22 +216,28 @@ __device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, Sm
         rec[16 + e] = __ldg(vn + (e & (kHD - 1)));
 }
 
-// Merge `nparts` partial records (pointers computed by `rec_at`) of one (job, kvh) into either
-// the gated output (pout == null) or one merged record.
+// Merge `nparts` partial records (pointers from `rec_at`) of one (job, kvh) into either the
+// gated output (p.pout == null) or one merged record. All loads of a pass are independent, so a
+// pass costs one memory round trip rather than one per part.
 template <typename RecAt>
 __device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int nparts, RecAt rec_at,
                         Smem &sm, int t)
 {
-    // per head: M = max m_i, w_i = l_i * exp2(m_i - M), L = sum w_i
-    if (t < 8) {
+    for (int idx = t; idx < nparts * 8; idx += 128) {
+        const int i = idx >> 3, h = idx & 7;
+        sm.u.c.m[i][h] = __ldcg(rec_at(i) + h);
+        sm.u.c.l[i][h] = __ldcg(rec_at(i) + 8 + h);
+    }
+    named_bar_sync(1, 128);
+    if (t < 8) {               // per head: M = max m_i, w_i = l_i exp2(m_i - M), L = sum w_i
         float M = -INFINITY;
         for (int i = 0; i < nparts; i++)
-            M = fmaxf(M, __ldcg(rec_at(i) + t));
+            M = fmaxf(M, sm.u.c.m[i][t]);
         float L = 0.f;
         for (int i = 0; i < nparts; i++) {
-            const float m = __ldcg(rec_at(i) + t), l = __ldcg(rec_at(i) + 8 + t);
-            const float w = (m == -INFINITY) ? 0.f : l * exp2f(m - M);
-            sm.cw[i][t] = w;
+            const float m = sm.u.c.m[i][t];
+            const float w = (m == -INFINITY) ? 0.f : sm.u.c.l[i][t] * exp2f(m - M);
+            sm.u.c.w[i][t] = w;
             L += w;
         }
         sm.mw[0][t] = M;
@@ -232,40 +249,69 @@ __device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int 
         dst[t] = sm.mw[0][t];
         dst[8 + t] = sm.lw[0][t];
     }
-    for (int e = t; e < 8 * kHD; e += 128) {
-        const int h = e >> 8, d = e & (kHD - 1);
-        float acc = 0.f;
-        for (int i = 0; i < nparts; i++)
-            acc = fmaf(sm.cw[i][h], __ldcg(rec_at(i) + 16 + e), acc);
+    // thread t owns float4 groups e = 4t + 512k (k = 0..3): head (t >> 6) + 2k, dims 4t % 256
+    float4 acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+    for (int i = 0; i < nparts; i++) {
+        const float *rec = rec_at(i) + 16;
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            v[k] = __ldcg(reinterpret_cast<const float4 *>(rec + 4 * t + 512 * k));
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float w = sm.u.c.w[i][(t >> 6) + 2 * k];
+            acc[k].x = fmaf(w, v[k].x, acc[k].x);
+            acc[k].y = fmaf(w, v[k].y, acc[k].y);
+            acc[k].z = fmaf(w, v[k].z, acc[k].z);
+            acc[k].w = fmaf(w, v[k].w, acc[k].w);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int h = (t >> 6) + 2 * k, d = (4 * t) & (kHD - 1);
         const float L = sm.lw[0][h];
-        const float o = L > 0.f ? acc / L : 0.f;
+        const float inv = L > 0.f ? 1.0f / L : 0.f;
+        float o[4] = {acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv};
         if (dst) {
-            dst[16 + e] = o;
+            *reinterpret_cast<float4 *>(dst + 16 + h * kHD + d) = make_float4(o[0], o[1], o[2], o[3]);
         } else {
-            const float g = __ldg(J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d);
-            J.out[(kvh * 8 + h) * kHD + d] = o * (1.0f / (1.0f + expf(-g)));
+            const float *g = J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d;
+            float *out = J.out + (kvh * 8 + h) * kHD + d;
+#pragma unroll
+            for (int x = 0; x < 4; x++)
+                out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
         }
     }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ DParams p)
 {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw + ((128u - (raw & 127u)) & 127u));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; s++) {
-            mbar_init(smem_addr(&sm.full[s]), 1);
-            mbar_init(smem_addr(&sm.empty[s]), 1);
+            mbar_init(smem_addr(&sm.full[s]), kProd * 32);   // one cp.async arrival per producer thread
+            mbar_init(smem_addr(&sm.empty[s]), 1);           // the consuming warp
         }
         sm.abort = 0;
         mbar_init_fence();
     }
     __syncthreads();
 
-    if (warp == kCons) {
-        // ------------------------------------------------------------ producer
+    if (warp >= kCons) {
+        // ------------------------------------------------------------ producers (128 threads)
+        // Warp pw copies rows pos = pw + 4k (k < 8) of both K and V each stage; lane -> dims
+        // lane*8 .. lane*8+7 = chunk lane >> 3, 16-byte unit lane & 7, stored at unit
+        // (lane & 7) ^ (pos & 7) of the chunk's row.
+        const int pw = warp - kCons;
+        const uint32_t ldst = (uint32_t)(lane >> 3) * kChunkBytes;
         unsigned seq = 0;
         for (int item = blockIdx.x; item < p.nitems && !aborted(sm); item += gridDim.x) {
             int j, kvh, split;
@@ -274,31 +320,36 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             long long t0, t1;
             item_range(p, J, split, t0, t1);
             const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
+            const long long avail = J.length - t0;          // rows that exist from t0 on
+            const __half *kg = J.k_cache + (t0 * 2 + kvh) * kHD + lane * 8;
+            const __half *vg = J.v_cache + (t0 * 2 + kvh) * kHD + lane * 8;
+            bool ok = true;
             for (int i = 0; i < ntiles; i++, seq++) {
                 const int s = seq % kStages;
                 const unsigned f = seq / kStages;
                 if (f > 0 && !mbar_wait(smem_addr(&sm.empty[s]), (f - 1) & 1)) {
                     if (lane == 0)
                         set_error(p, kErrWaitTimeout, sm);
+                    ok = false;
                     break;
                 }
-                if (lane == 0)
-                    mbar_arrive_expect_tx(smem_addr(&sm.full[s]), kTxBytes);
-                __syncwarp();
-                const int row = lane & 15, isv = lane >> 4;
-                long long pos = t0 + (long long)i * kTile + row;
-                if (pos > t1 - 1)
-                    pos = t1 - 1;               // ragged tail: repeat a valid row (masked later)
-                const __half *src = (isv ? J.v_cache : J.k_cache) + (pos * 2 + kvh) * kHD;
-                bulk_g2s(smem_addr(&sm.stage[s][0]) + isv * kTile * kRowBytes + row * kRowBytes, src,
-                         512, smem_addr(&sm.full[s]));
+                const uint32_t st = smem_addr(&sm.stage[s][0]) + ldst;
+#pragma unroll
+                for (int k = 0; k < kTile / kProd; k++) {
+                    const int pos = pw + kProd * k;
+                    const long long row = (long long)i * kTile + pos;
+                    if (row < avail) {
+                        const uint32_t d = st + pos * 128 + (((lane & 7) ^ (pos & 7)) << 4);
+                        cp_async16(d, kg + row * 2 * kHD);
+                        cp_async16(d + kHalfBytes, vg + row * 2 * kHD);
+                    }
+                }
+                cp_async_arrive(smem_addr(&sm.full[s]));
             }
+            if (!ok)
+                break;
         }
-        // Drain: every fill issued must land before this CTA's shared memory is released.
-        if (lane == 0 && aborted(sm)) {
-            for (unsigned q = seq > kStages ? seq - kStages : 0; q < seq; q++)
-                mbar_wait(smem_addr(&sm.full[q % kStages]), (q / kStages) & 1);
-        }
+        cp_async_wait_all();     // nothing of ours may still be landing when the CTA retires
         return;
     }
 
@@ -307,9 +358,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     unsigned seq = 0;
     const float sc = kLog2e / 16.0f;
     const int r = lane >> 2, cpair = (lane & 3) * 2;
-    // per-lane shared-memory offsets of the ldmatrix row addresses
-    const uint32_t koff = (lane & 15) * kRowBytes + (lane >> 4) * 16;
-    const uint32_t voff = kTile * kRowBytes + ((lane & 7) + ((lane >> 4) << 3)) * kRowBytes + ((lane >> 3) & 1) * 16;
+    // Swizzled ldmatrix addressing. Row p of a [chunk][32 pos][128 B] tile holds 16-byte unit u at
+    // unit u ^ (p & 7). K (A operand) rows: position (lane & 15) (+16 for the second half), units
+    // ((ks & 3) * 2 + (lane >> 4)); V^T (A via .trans) rows: position (lane & 7) + 8 * (lane >> 4),
+    // units ((mt & 3) * 2 + ((lane >> 3) & 1)). For both, p & 7 == lane & 7.
+    const uint32_t kx = (uint32_t)((lane >> 4) ^ (lane & 7));
+    const uint32_t vx = (uint32_t)(((lane >> 3) & 1) ^ (lane & 7));
+    const uint32_t krow = (uint32_t)(lane & 15) * 128;
+    const uint32_t vrow = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * 128;
 
     for (int item = blockIdx.x; item < p.nitems; item += gridDim.x) {
         int j, kvh, split;
@@ -346,25 +402,41 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                     set_error(p, kErrWaitTimeout, sm);
                 break;
             }
-            const uint32_t base = smem_addr(&sm.stage[s][0]);
-            // S^T = K Q^T: four independent accumulation chains over the 16 k-steps
-            float acc[4][4];
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < 16; ks++) {
-                uint32_t a[4];
-                ldsm_x4(base + koff + ks * 32, a);
-                mma_f16(acc[ks & 3], a, qb[ks][0], qb[ks][1]);
+            const uint32_t kb = smem_addr(&sm.stage[s][0]), vb = kb + kHalfBytes;
+            const long long tile0 = t0 + (long long)i * kTile;
+            // Rows past the window end are not loaded and hold stale data (possibly NaN bit
+            // patterns): zero their V so P = 0 contributes exactly nothing. K rows there are
+            // masked below.
+            const long long live = J.length - tile0;
+            const bool ragged = live < kTile;
+            if (ragged) {
+                for (int row = (int)(live > 0 ? live : 0); row < kTile; row++)
+                    sts_zero16(vb + (lane >> 3) * kChunkBytes + row * 128 + (lane & 7) * 16);
+                __syncwarp();
             }
-            const long long p0 = t0 + (long long)i * kTile + r;
-            const bool v0 = p0 < t1, v1 = p0 + 8 < t1;
-            const float x0 = v0 ? (acc[0][0] + acc[1][0] + acc[2][0] + acc[3][0]) * sc : -INFINITY;
-            const float x1 = v0 ? (acc[0][1] + acc[1][1] + acc[2][1] + acc[3][1]) * sc : -INFINITY;
-            const float x2 = v1 ? (acc[0][2] + acc[1][2] + acc[2][2] + acc[3][2]) * sc : -INFINITY;
-            const float x3 = v1 ? (acc[0][3] + acc[1][3] + acc[2][3] + acc[3][3]) * sc : -INFINITY;
-            float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+            float x[2][4];
+#pragma unroll
+            for (int hf = 0; hf < 2; hf++) {
+                float acc[2][4];
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+                    acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+#pragma unroll
+                for (int ks = 0; ks < 16; ks++) {
+                    uint32_t a[4];
+                    ldsm_x4(kb + (ks >> 2) * kChunkBytes + hf * 16 * 128 + krow +
+                                ((((uint32_t)(ks & 3) << 1) ^ kx) << 4), a);
+                    mma_f16(acc[ks & 1], a, qb[ks][0], qb[ks][1]);
+                }
+                const long long p0 = tile0 + hf * 16 + r;
+                const bool v0 = p0 < t1, v1 = p0 + 8 < t1;
+                x[hf][0] = v0 ? (acc[0][0] + acc[1][0]) * sc : -INFINITY;
+                x[hf][1] = v0 ? (acc[0][1] + acc[1][1]) * sc : -INFINITY;
+                x[hf][2] = v1 ? (acc[0][2] + acc[1][2]) * sc : -INFINITY;
+                x[hf][3] = v1 ? (acc[0][3] + acc[1][3]) * sc : -INFINITY;
+            }
+            float mx0 = fmaxf(fmaxf(x[0][0], x[0][2]), fmaxf(x[1][0], x[1][2]));
+            float mx1 = fmaxf(fmaxf(x[0][1], x[0][3]), fmaxf(x[1][1], x[1][3]));
 #pragma unroll
             for (int off = 4; off < 32; off <<= 1) {
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
@@ -372,23 +444,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             }
             const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);   // finite: row 0 is valid
             const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
-            const float e0 = exp2f(x0 - n0), e1 = exp2f(x1 - n1);
-            const float e2 = exp2f(x2 - n0), e3 = exp2f(x3 - n1);
-            l0 = fmaf(l0, c0, e0 + e2);
-            l1 = fmaf(l1, c1, e1 + e3);
+            uint32_t pb[2][2];
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int hf = 0; hf < 2; hf++) {
+                const float e0 = exp2f(x[hf][0] - n0), e1 = exp2f(x[hf][1] - n1);
+                const float e2 = exp2f(x[hf][2] - n0), e3 = exp2f(x[hf][3] - n1);
+                s0 += e0 + e2;
+                s1 += e1 + e3;
+                pb[hf][0] = movmatrix_t(pack_f16x2(e0, e1));
+                pb[hf][1] = movmatrix_t(pack_f16x2(e2, e3));
+            }
+            l0 = fmaf(l0, c0, s0);
+            l1 = fmaf(l1, c1, s1);
             m0 = n0;
             m1 = n1;
-            const uint32_t pb0 = movmatrix_t(pack_f16x2(e0, e1));
-            const uint32_t pb1 = movmatrix_t(pack_f16x2(e2, e3));
 #pragma unroll
             for (int mt = 0; mt < 16; mt++) {
                 o[mt][0] *= c0;
                 o[mt][1] *= c1;
                 o[mt][2] *= c0;
                 o[mt][3] *= c1;
-                uint32_t a[4];
-                ldsm_x4_t(base + voff + mt * 32, a);
-                mma_f16(o[mt], a, pb0, pb1);
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    uint32_t a[4];
+                    ldsm_x4_t(vb + (mt >> 2) * kChunkBytes + hf * 16 * 128 + vrow +
+                                  ((((uint32_t)(mt & 3) << 1) ^ vx) << 4), a);
+                    mma_f16(o[mt], a, pb[hf][0], pb[hf][1]);
+                }
             }
             __syncwarp();
             if (lane == 0)
@@ -411,10 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 #pragma unroll
         for (int mt = 0; mt < 16; mt++) {
             const int d = mt * 16 + r;
-            sm.ow[warp][cpair][d] = o[mt][0];
-            sm.ow[warp][cpair + 1][d] = o[mt][1];
-            sm.ow[warp][cpair][d + 8] = o[mt][2];
-            sm.ow[warp][cpair + 1][d + 8] = o[mt][3];
+            sm.u.ow[warp][cpair][d] = o[mt][0];
+            sm.u.ow[warp][cpair + 1][d] = o[mt][1];
+            sm.u.ow[warp][cpair][d + 8] = o[mt][2];
+            sm.u.ow[warp][cpair + 1][d + 8] = o[mt][3];
         }
         named_bar_sync(1, 128);
         float *rec = p.part + (long long)item * kPF;
@@ -429,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             for (int w = 0; w < kCons; w++) {
                 const float f = sm.mw[w][h] == -INFINITY ? 0.f : exp2f(sm.mw[w][h] - M);
                 L = fmaf(f, sm.lw[w][h], L);
-                acc = fmaf(f, sm.ow[w][h][d], acc);
+                acc = fmaf(f, sm.u.ow[w][h][d], acc);
             }
             rec[16 + e] = L > 0.f ? acc / L : 0.f;
             if (d == 0) {
@@ -536,12 +619,12 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
             return -1;
         total += (long long)jobs[i].length;
     }
-    // Split size: about 4 items per SM and kv head, multiple of the tile, >= 64 positions, and
-    // at most kMaxSplits splits per (slot, kv head).
+    // Split size: about 4 items per SM and kv head, a multiple of the stage, and at most
+    // kMaxSplits splits per (slot, kv head).
     long long chunk = (total + 4ll * R.num_sms - 1) / (4ll * R.num_sms);
     chunk = (chunk + kTile - 1) / kTile * kTile;
-    if (chunk < 64)
-        chunk = 64;
+    if (chunk < kTile)
+        chunk = kTile;
     for (int i = 0; i < n; i++) {
         long long need = ((long long)jobs[i].length + kMaxSplits - 1) / kMaxSplits;
         need = (need + kTile - 1) / kTile * kTile;
@@ -551,7 +634,7 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
     if (chunk > (1ll << 30))
         return fail("attn decode: window too long");
     DParams p;
-    memset(&p, 0, sizeof(p));
+    memset(static_cast<void *>(&p), 0, sizeof(p));
     int items = 0;
     for (int i = 0; i < n; i++) {
         const KernelAttnDecodeJob &s = jobs[i];
@@ -590,12 +673,12 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
     p.chunk = (int)chunk;
     if (!g_attr_set) {
         if (check(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(Smem)), "attn decode smem attribute") != 0)
+                                       (int)kSmemBytes), "attn decode smem attribute") != 0)
             return -1;
         g_attr_set = true;
     }
     const int grid = items < R.num_sms ? items : R.num_sms;
-    attn_decode_kernel<<<grid, kThreads, sizeof(Smem), R.stream>>>(p);
+    attn_decode_kernel<<<grid, kThreads, kSmemBytes, R.stream>>>(p);
     return launched("attn_decode_kernel");
 }
 

@@ -76,6 +76,31 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
         : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async (16-byte LDGSTS)
+
+// Asynchronous 16-byte global -> shared copy, cached in L2 only.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Arrive on `bar` once all of this thread's earlier cp.async copies have landed (the barrier's
+// expected count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void sts_zero16(uint32_t addr)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+}
+
 // ---------------------------------------------------------------- warp matrix ops
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4])

@@ -157,6 +157,7 @@ void *pinned(size_t bytes)
     return p;
 }
 
+
 }  // namespace rb
 
 using namespace rb;
