@@ -6,8 +6,10 @@
 // (theta 1e7), K/V append at the window index `length`, softmax(q.k/16) over the window plus the
 // new token, times V, times sigmoid(gate).
 //
-// Work decomposition. A work item is (slot, kv head, split): `chunk` consecutive cached
-// positions of one kv head. Items are spread round-robin over persistent CTAs (one per SM).
+// Work decomposition. A work item is (slot, kv head, split): a run of consecutive cached
+// positions of one kv head; each slot's window is cut into equal splits of about
+// total/(SMs x items_per_sm) positions. The host assigns items to persistent CTAs (one per SM)
+// longest-first onto the least-loaded CTA and passes each CTA its item list.
 // In each CTA
 //   * warps 4-7 (producers) stream 32-position stages of K and V into a 5-stage shared-memory
 //     ring with 16-byte cp.async copies: one warp instruction moves one 512-byte row (one kv
@@ -39,7 +41,10 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <queue>
+#include <utility>
 #include <vector>
 
 namespace rb {
@@ -57,6 +62,8 @@ constexpr int kStageBytes = 2 * kHalfBytes;       // K then V
 constexpr int kMaxJobs = 64;
 constexpr int kPF = KERNEL_ATTN_PARTIAL_FLOATS;   // m[8] l[8] o[8][256]
 constexpr int kMaxSplits = 256;
+constexpr int kMaxItems = 2048;                   // per launch (sched entries)
+constexpr int kMaxCtas = 160;
 constexpr int kOStride = 260;                     // padded head stride of the merge buffer
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -65,19 +72,21 @@ struct DJob {
     const float *k_new, *v_new, *q_norm, *k_norm;
     __half *k_cache, *v_cache;
     float *out;
-    long long qg_stride, length, position;
+    long long qg_stride, length, position, chunk;
     int item_base, nsplit, append, pad;
 };
 
 struct DParams {
     DJob jobs[kMaxJobs];
+    unsigned short sched[kMaxItems];    // (job << 9) | (split << 1) | kv head, grouped by CTA
+    unsigned short cta_off[kMaxCtas + 1];
     float inv_freq[32];
     float *part;        // [nitems][kPF]
     float *newpart;     // [njobs][2][kPF]
     int *counters;      // [njobs][2]
     float *pout;        // partial mode: [njobs][2][kPF], else null
     unsigned *err;
-    int njobs, nitems, chunk;
+    int njobs, nitems;
 };
 
 struct Smem {
@@ -97,27 +106,19 @@ struct Smem {
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 128;   // + alignment slack
 
-__device__ __forceinline__ void item_decode(const DParams &p, int item, int &j, int &kvh, int &split)
+__device__ __forceinline__ void item_decode(const DParams &p, int idx, int &j, int &kvh, int &split, int &item)
 {
-    int lo = 0, hi = p.njobs - 1;
-    while (lo < hi) {                       // last job with item_base <= item
-        const int mid = (lo + hi + 1) >> 1;
-        if (p.jobs[mid].item_base <= item)
-            lo = mid;
-        else
-            hi = mid - 1;
-    }
-    j = lo;
-    const int local = item - p.jobs[lo].item_base;
-    kvh = local & 1;
-    split = local >> 1;
+    const unsigned e = p.sched[idx];
+    j = (int)(e >> 9);
+    split = (int)((e >> 1) & 255u);
+    kvh = (int)(e & 1u);
+    item = p.jobs[j].item_base + 2 * split + kvh;
 }
 
-__device__ __forceinline__ void item_range(const DParams &p, const DJob &J, int split, long long &t0,
-                                           long long &t1)
+__device__ __forceinline__ void item_range(const DJob &J, int split, long long &t0, long long &t1)
 {
-    t0 = (long long)split * p.chunk;
-    t1 = t0 + p.chunk < J.length ? t0 + p.chunk : J.length;
+    t0 = (long long)split * J.chunk;
+    t1 = t0 + J.chunk < J.length ? t0 + J.chunk : J.length;
     if (t1 < t0)
         t1 = t0;
 }
@@ -313,12 +314,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         const int pw = warp - kCons;
         const uint32_t ldst = (uint32_t)(lane >> 3) * kChunkBytes;
         unsigned seq = 0;
-        for (int item = blockIdx.x; item < p.nitems && !aborted(sm); item += gridDim.x) {
-            int j, kvh, split;
-            item_decode(p, item, j, kvh, split);
+        for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1] && !aborted(sm); idx++) {
+            int j, kvh, split, item;
+            item_decode(p, idx, j, kvh, split, item);
             const DJob &J = p.jobs[j];
             long long t0, t1;
-            item_range(p, J, split, t0, t1);
+            item_range(J, split, t0, t1);
             const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
             const long long avail = J.length - t0;          // rows that exist from t0 on
             const __half *kg = J.k_cache + (t0 * 2 + kvh) * kHD + lane * 8;
@@ -367,12 +368,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const uint32_t krow = (uint32_t)(lane & 15) * 128;
     const uint32_t vrow = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * 128;
 
-    for (int item = blockIdx.x; item < p.nitems; item += gridDim.x) {
-        int j, kvh, split;
-        item_decode(p, item, j, kvh, split);
+    for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1]; idx++) {
+        int j, kvh, split, item;
+        item_decode(p, idx, j, kvh, split, item);
         const DJob &J = p.jobs[j];
         long long t0, t1;
-        item_range(p, J, split, t0, t1);
+        item_range(J, split, t0, t1);
         const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
 
         prep_q(p, J, kvh, sm, t);
@@ -609,6 +610,17 @@ int validate(const KernelAttnDecodeJob &j, int i, bool partial)
 
 bool g_attr_set = false;
 
+// Items per SM the planner aims for (per kv head pair). ROASTER_DECODE_ITEMS_PER_SM overrides.
+double decode_items_per_sm()
+{
+    static double v = [] {
+        const char *e = getenv("ROASTER_DECODE_ITEMS_PER_SM");
+        const double x = e ? atof(e) : 1.0;
+        return x > 0.05 && x < 64.0 ? x : 1.0;
+    }();
+    return v;
+}
+
 // One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode.
 int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
 {
@@ -619,23 +631,78 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
             return -1;
         total += (long long)jobs[i].length;
     }
-    // Split size: about 4 items per SM and kv head, a multiple of the stage, and at most
-    // kMaxSplits splits per (slot, kv head).
-    long long chunk = (total + 4ll * R.num_sms - 1) / (4ll * R.num_sms);
-    chunk = (chunk + kTile - 1) / kTile * kTile;
-    if (chunk < kTile)
-        chunk = kTile;
-    for (int i = 0; i < n; i++) {
-        long long need = ((long long)jobs[i].length + kMaxSplits - 1) / kMaxSplits;
-        need = (need + kTile - 1) / kTile * kTile;
-        if (need > chunk)
-            chunk = need;
-    }
-    if (chunk > (1ll << 30))
-        return fail("attn decode: window too long");
+    // Equal splits of about `target` positions per slot, then longest-first assignment of the
+    // (slot, kv head, split) items onto the least-loaded CTA.
+    const double per_sm = decode_items_per_sm();
+    long long target = (long long)((double)total / ((double)R.num_sms * per_sm)) + 1;
+    if (target < 2 * kTile)
+        target = 2 * kTile;
     DParams p;
     memset(static_cast<void *>(&p), 0, sizeof(p));
     int items = 0;
+    for (int attempt = 0;; attempt++) {
+        items = 0;
+        for (int i = 0; i < n; i++) {
+            const long long L = (long long)jobs[i].length;
+            long long ns = (L + target / 2) / target;
+            if (ns < 1)
+                ns = 1;
+            if (ns > kMaxSplits)
+                ns = kMaxSplits;
+            long long ch = (L + ns - 1) / ns;
+            ch = (ch + kTile - 1) / kTile * kTile;
+            if (ch < kTile)
+                ch = kTile;
+            ns = (L + ch - 1) / ch;
+            if (ns < 1)
+                ns = 1;
+            p.jobs[i].chunk = ch;
+            p.jobs[i].nsplit = (int)ns;
+            p.jobs[i].item_base = items;
+            items += 2 * (int)ns;
+        }
+        if (items <= kMaxItems)
+            break;
+        if (attempt > 40)
+            return fail("attn decode: cannot plan %d slots within %d items", n, kMaxItems);
+        target *= 2;
+    }
+    const int grid = items < R.num_sms ? items : (R.num_sms < kMaxCtas ? R.num_sms : kMaxCtas);
+    {
+        // cost of an item ~ its positions plus a fixed per-item overhead
+        std::vector<std::pair<long long, unsigned short>> order;
+        order.reserve(items);
+        for (int i = 0; i < n; i++) {
+            const DJob &d = p.jobs[i];
+            for (int sp = 0; sp < d.nsplit; sp++) {
+                long long t0 = (long long)sp * d.chunk, t1 = std::min<long long>(t0 + d.chunk, (long long)jobs[i].length);
+                const long long cost = (t1 > t0 ? t1 - t0 : 0) + 256;
+                for (int kvh = 0; kvh < 2; kvh++)
+                    order.emplace_back(cost, (unsigned short)((i << 9) | (sp << 1) | kvh));
+            }
+        }
+        std::stable_sort(order.begin(), order.end(),
+                         [](const std::pair<long long, unsigned short> &a,
+                            const std::pair<long long, unsigned short> &b) { return a.first > b.first; });
+        std::vector<std::vector<unsigned short>> per(grid);
+        std::priority_queue<std::pair<long long, int>, std::vector<std::pair<long long, int>>,
+                            std::greater<std::pair<long long, int>>> heap;
+        for (int c = 0; c < grid; c++)
+            heap.emplace(0ll, c);
+        for (const auto &it : order) {
+            auto top = heap.top();
+            heap.pop();
+            per[top.second].push_back(it.second);
+            heap.emplace(top.first + it.first, top.second);
+        }
+        int k = 0;
+        for (int c = 0; c < grid; c++) {
+            p.cta_off[c] = (unsigned short)k;
+            for (unsigned short e : per[c])
+                p.sched[k++] = e;
+        }
+        p.cta_off[grid] = (unsigned short)k;
+    }
     for (int i = 0; i < n; i++) {
         const KernelAttnDecodeJob &s = jobs[i];
         DJob &d = p.jobs[i];
@@ -652,10 +719,6 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
         d.length = (long long)s.length;
         d.position = (long long)s.position;
         d.append = s.append ? 1 : 0;
-        long long ns = ((long long)s.length + chunk - 1) / chunk;
-        d.nsplit = ns < 1 ? 1 : (int)ns;
-        d.item_base = items;
-        items += 2 * d.nsplit;
     }
     memcpy(p.inv_freq, R.inv_freq, sizeof(p.inv_freq));
     const size_t part_floats = (size_t)items * kPF, new_floats = (size_t)n * 2 * kPF;
@@ -670,14 +733,12 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
     p.err = R.err_word;
     p.njobs = n;
     p.nitems = items;
-    p.chunk = (int)chunk;
     if (!g_attr_set) {
         if (check(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes), "attn decode smem attribute") != 0)
             return -1;
         g_attr_set = true;
     }
-    const int grid = items < R.num_sms ? items : R.num_sms;
     attn_decode_kernel<<<grid, kThreads, kSmemBytes, R.stream>>>(p);
     return launched("attn_decode_kernel");
 }
