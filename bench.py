@@ -1,0 +1,462 @@
+#!/usr/bin/env python
+"""Hybrid-attention decode benchmark on B200.
+
+One step = one decode token for every slot: per slot one gated-attention layer (16 q / 2 kv heads,
+d 256, q/k RMSNorm, partial RoPE, sigmoid gate) over an f16 KV window of L ~ U[1k, 32k] tokens
+that grows by the appended token each step, plus 3 Gated DeltaNet layers (32 x 128 x 128 fp32
+state each). 64 slots per GPU; slots shard across GPUs with no communication (weak scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+The device-timed `value` runs both kernels on resident inputs (CUDA events on the launching
+stream, max over ranks). `e2e` runs the same step through the host-buffer C-ABI entry points
+(inputs copied host->device and outputs device->host inside the timed region). `cpu_baseline`
+and `--impl reference` time the reference's own CPU code (compiled from its sources into
+oracle/_ref) on this host's cores. Inputs are seeded synthetic data (no dataset exists for the
+path); the KV windows (2.2 GB) and states (0.4 GB) per GPU exceed the 126 MB L2, so no flush is
+needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SLOTS = 64
+DN_LAYERS = 3
+METRIC = "hybrid-attn decode tok/s (config 2: 64 slots/GPU, 1 gated-attn + 3 DeltaNet layers)"
+# DRAM bytes per launch / algorithmic bytes for the decode-attention kernel, from one ncu capture
+# of a 64-slot launch with windows U[1024, 4096] (dram__bytes_read 338.06 MB + write 6.69 MB for
+# 338.31 MB algorithmic). Traffic grows with the KV positions streamed, so the ratio scales to
+# the full launch.
+ATTN_TRAFFIC_RATIO = (338.057984e6 + 6.689792e6) / 338309120
+
+
+def args_parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
+    ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
+    ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def slot_lengths(rank: int, lo: int = 1024, hi: int = 32768):
+    from roaster_b200 import synth
+    return [int(x) for x in synth.slot_lengths(1000 + rank, SLOTS, lo, hi)]
+
+
+# ------------------------------------------------------------------------------ CPU reference leg
+
+def cpu_reference(lens, tokens: int, warmup: int, threads: int) -> dict:
+    """Time the reference's own CPU path (oracle/_ref): per token one slot's full_attention (its
+    four projection matvecs timed separately and subtracted) + 3 recurrent_delta_step calls, the
+    slots served one at a time as the reference's step lock does (slots.c:864-891). Runs
+    `tokens` slot-steps, cycling through the slots. Returns tok/s."""
+    import ctypes as C
+
+    import numpy as np
+
+    import oracle
+    lib = oracle.ref_lib()
+    rng = np.random.default_rng(5)
+    cap = max(lens) + 2
+    qn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    fp = C.POINTER(C.c_float)
+    ctx = lib.ref_decode_ctx_new(cap, qn.ctypes.data_as(fp), kn.ctypes.data_as(fp))
+    if not ctx:
+        raise RuntimeError("reference rig allocation failed")
+    kw = np.ctypeslib.as_array(lib.ref_decode_ctx_k(ctx), shape=(cap * 512,))
+    vw = np.ctypeslib.as_array(lib.ref_decode_ctx_v(ctx), shape=(cap * 512,))
+    kw[:] = rng.standard_normal(cap * 512).astype(np.float16).astype(np.float32)
+    vw[:] = rng.standard_normal(cap * 512).astype(np.float16).astype(np.float32)
+    state = (0.02 * rng.standard_normal((DN_LAYERS, 32, 128, 128))).astype(np.float32)
+    from roaster_b200 import synth
+    dn = synth.delta_step_inputs(rng, DN_LAYERS)
+    out = np.zeros((32, 128), np.float32)
+    args = [np.ascontiguousarray(dn[k]) for k in ("q", "k", "v", "g", "beta")]
+
+    def one(slot):
+        L = lens[slot % len(lens)]
+        t0 = time.perf_counter()
+        if lib.ref_decode_ctx_step(ctx, L, L) != 0:
+            raise RuntimeError("reference full_attention failed")
+        for l in range(DN_LAYERS):
+            lib.ref_delta_step(state[l].ctypes.data_as(fp),
+                               *[a[l].ctypes.data_as(fp) for a in args], out.ctypes.data_as(fp))
+        return time.perf_counter() - t0
+
+    for i in range(warmup):
+        one(i)
+    # projection matvecs full_attention runs (W_q 8192x2048, W_k, W_v 512x2048, W_o 2048x4096)
+    pt = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        lib.ref_decode_ctx_projections(ctx)
+        pt.append(time.perf_counter() - t0)
+    proj = statistics.median(pt)
+    total = 0.0
+    for i in range(tokens):
+        total += max(one(i) - proj, 1e-9)
+    lib.ref_decode_ctx_free(ctx)
+    return {"tok_s": tokens / total, "seconds": total, "tokens": tokens, "threads": threads,
+            "projection_ms_subtracted": proj * 1e3}
+
+
+def cpu_leg(lens, tokens, warmup):
+    """Run cpu_reference in a fresh process (its OpenMP runtime never meets torch's)."""
+    threads = os.cpu_count() or 1
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), CUDA_VISIBLE_DEVICES="")
+    spec = json.dumps({"lens": lens, "tokens": tokens, "warmup": warmup, "threads": threads})
+    out = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-json", spec],
+                         capture_output=True, text=True, env=env, timeout=1800)
+    if out.returncode != 0:
+        raise RuntimeError("CPU reference leg failed: " + out.stderr[-2000:])
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+# ------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        import tempfile
+        self.path = os.path.join(tempfile.gettempdir(), f"roaster_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) < 9:
+                    continue
+                try:
+                    sm.append(float(c[1]))
+                    mx.append(float(c[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, c[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ GPU arm
+
+def run_ours(a):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import roaster_b200 as R
+    from roaster_b200 import synth
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    R.init(local)
+    stream = torch.cuda.current_stream()
+    R.set_stream(stream)
+
+    K, W = a.steps, a.warmup
+    lens = slot_lengths(rank, a.kv_lo, a.kv_hi)
+    grow = K + W + 8
+    caps = [L + grow for L in lens]
+    offs = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
+    # KV windows of all slots in one pool (per slot [cap][2][256] f16, 1 KB per position)
+    kpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), 11 + rank, dev, torch.float16)
+    vpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), 12 + rank, dev, torch.float16)
+    states = synth.device_normal(torch, (SLOTS, DN_LAYERS, 32, 128, 128), 13 + rank, dev,
+                                 torch.float32, std=0.02)
+    NP = 4                                            # rotating pools of per-step inputs
+    g = torch.Generator(device=dev)
+    g.manual_seed(14 + rank)
+    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    q, gate = rn(NP, SLOTS, 16, 256), rn(NP, SLOTS, 16, 256)
+    kn, vn = rn(NP, SLOTS, 2, 256), rn(NP, SLOTS, 2, 256)
+    qn = 1 + 0.1 * rn(256)
+    kw = 1 + 0.1 * rn(256)
+    dq = torch.nn.functional.normalize(rn(NP, SLOTS, DN_LAYERS, 16, 128), dim=-1)
+    dk = torch.nn.functional.normalize(rn(NP, SLOTS, DN_LAYERS, 16, 128), dim=-1)
+    dv = rn(NP, SLOTS, DN_LAYERS, 32, 128)
+    dbeta = torch.sigmoid(rn(NP, SLOTS, DN_LAYERS, 32))
+    dgl = -torch.exp(-1 + 0.5 * rn(NP, SLOTS, DN_LAYERS, 32)) * torch.nn.functional.softplus(
+        rn(NP, SLOTS, DN_LAYERS, 32))
+    aout = torch.empty(SLOTS, 16, 256, device=dev)
+    dout = torch.empty(SLOTS, DN_LAYERS, 32, 128, device=dev)
+    es = kpool.element_size()
+
+    attn_arrs, dn_arrs = [], []
+    for pi in range(NP):
+        jobs = [R.attn_job(q[pi, s], gate[pi, s], kn[pi, s], vn[pi, s], qn, kw,
+                           kpool.data_ptr() + int(offs[s]) * 512 * es,
+                           vpool.data_ptr() + int(offs[s]) * 512 * es, lens[s], lens[s], aout[s],
+                           capacity=caps[s]) for s in range(SLOTS)]
+        attn_arrs.append((R.KernelAttnDecodeJob * SLOTS)(*jobs))
+        dj = [R.delta_job(states[s, l], dq[pi, s, l], dk[pi, s, l], dv[pi, s, l], dgl[pi, s, l],
+                          dbeta[pi, s, l], dout[s, l]) for s in range(SLOTS) for l in range(DN_LAYERS)]
+        dn_arrs.append((R.KernelDeltaStepJob * len(dj))(*dj))
+    lib = R.lib()
+    cur = list(lens)
+
+    def step(i, ev=None):
+        arr = attn_arrs[i % NP]
+        for s in range(SLOTS):
+            arr[s].length = cur[s]
+            arr[s].position = cur[s]
+        if ev:
+            ev[0].record(stream)
+        rc = lib.kernel_attn_decode_batch(arr, SLOTS)
+        if ev:
+            ev[1].record(stream)
+        rc |= lib.kernel_deltanet_step_batch(dn_arrs[i % NP], SLOTS * DN_LAYERS)
+        if ev:
+            ev[2].record(stream)
+        if rc != 0:
+            raise RuntimeError(R.last_error())
+        for s in range(SLOTS):
+            cur[s] += 1
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(W):
+        step(i)
+    R.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local if not os.environ.get("CUDA_VISIBLE_DEVICES") else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = R.launch_count()
+    lens_at_start = list(cur)
+    t_start.record(stream)
+    for i in range(K):
+        step(W + i, evs[i])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = R.launch_count() - launches0
+    clk = clocks.stop()
+    R.synchronize()
+    ms = t_start.elapsed_time(t_end)
+    attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    dn_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    t = torch.tensor([ms, statistics.mean(attn_ms), statistics.mean(dn_ms)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, attn_avg, dn_avg = [float(x) for x in t.tolist()]
+    ms_step = ms / K
+    value = SLOTS * world / (ms_step / 1e3)
+
+    # algorithmic bytes per launch (mean over the timed steps: windows grow by 1 per step)
+    mean_L = statistics.mean(lens_at_start) + (K - 1) / 2
+    attn_bytes = SLOTS * (mean_L * 2048 + 2048 + 3 * 16 * 256 * 4 + 2 * 2 * 256 * 4)
+    dn_bytes = SLOTS * DN_LAYERS * (2 * 32 * 128 * 128 * 4 + (2 * 16 + 2 * 32) * 128 * 4 + 2 * 32 * 4)
+    hbm, _, src = peaks()
+    attn_gbs = attn_bytes / (attn_avg / 1e3) / 1e9
+    dn_gbs = dn_bytes / (dn_avg / 1e3) / 1e9
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    e2e = None
+    if not a.no_e2e:
+        hq = q.cpu().numpy()
+        hg = gate.cpu().numpy()
+        hkn, hvn = kn.cpu().numpy(), vn.cpu().numpy()
+        hqn, hkw = qn.cpu().numpy(), kw.cpu().numpy()
+        hdq, hdk, hdv = dq.cpu().numpy(), dk.cpu().numpy(), dv.cpu().numpy()
+        hdg, hdb = dgl.cpu().numpy(), dbeta.cpu().numpy()
+        hao = np.zeros((SLOTS, 16, 256), np.float32)
+        hdo = np.zeros((SLOTS, DN_LAYERS, 32, 128), np.float32)
+        ha, hd = [], []
+        for pi in range(NP):
+            jobs = [R.attn_job(hq[pi, s].ctypes.data, hg[pi, s].ctypes.data, hkn[pi, s].ctypes.data,
+                               hvn[pi, s].ctypes.data, hqn.ctypes.data, hkw.ctypes.data,
+                               kpool.data_ptr() + int(offs[s]) * 512 * es,
+                               vpool.data_ptr() + int(offs[s]) * 512 * es, 0, 0,
+                               hao[s].ctypes.data, capacity=caps[s]) for s in range(SLOTS)]
+            ha.append((R.KernelAttnDecodeJob * SLOTS)(*jobs))
+            dj = [R.delta_job(states[s, l], hdq[pi, s, l].ctypes.data, hdk[pi, s, l].ctypes.data,
+                              hdv[pi, s, l].ctypes.data, hdg[pi, s, l].ctypes.data,
+                              hdb[pi, s, l].ctypes.data, hdo[s, l].ctypes.data)
+                  for s in range(SLOTS) for l in range(DN_LAYERS)]
+            hd.append((R.KernelDeltaStepJob * len(dj))(*dj))
+        # e2e continues the windows from where the device run left them; same K
+        KE = max(1, min(K, 200))
+
+        def estep(i):
+            arr = ha[i % NP]
+            for s in range(SLOTS):
+                arr[s].length = cur[s]
+                arr[s].position = cur[s]
+            rc = lib.kernel_attn_decode_batch_host(arr, SLOTS)
+            rc |= lib.kernel_deltanet_step_batch_host(hd[i % NP], SLOTS * DN_LAYERS)
+            if rc != 0:
+                raise RuntimeError(R.last_error())
+            for s in range(SLOTS):
+                cur[s] += 1
+
+        # windows were sized for K+W+8 appends: wind them back and append again (KE <= K)
+        for s in range(SLOTS):
+            cur[s] = lens[s]
+        for i in range(2):
+            estep(i)
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(KE):
+            estep(i)
+        el = time.perf_counter() - t0
+        te = torch.tensor([el], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        el = float(te.item())
+        h2d = SLOTS * (4096 * 2 + 512 * 2 + 256 * 2) * 4 + SLOTS * DN_LAYERS * (
+            2 * 2048 + 4096 + 64) * 4
+        d2h = SLOTS * 4096 * 4 + SLOTS * DN_LAYERS * 4096 * 4
+        e2e = {"value": round(SLOTS * world * KE / el, 1), "unit": "tok/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": KE,
+               "api": "kernel_attn_decode_batch_host + kernel_deltanet_step_batch_host"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        try:
+            r = cpu_leg(lens, tokens=SLOTS, warmup=2)
+            cpu = {"value": round(r["tok_s"], 3), "unit": "tok/s", "cores": r["threads"],
+                   "kind": "reference",
+                   "sample": f"{r['tokens']} slot-steps (every slot once, lengths of this run), "
+                             f"reference full_attention minus its projection matvecs "
+                             f"({r['projection_ms_subtracted']:.2f} ms) + 3 recurrent_delta_step, "
+                             f"OpenMP {r['threads']} threads, slots serialised as in slots.c"}
+        except Exception as e:  # reported, not fatal
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                   "sample": f"failed: {e}"[:300]}
+
+    if rank == 0:
+        traffic = None if ATTN_TRAFFIC_RATIO is None else round(ATTN_TRAFFIC_RATIO * attn_bytes)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV / fp32 state",
+            "data": "synthetic (seeded N(0,1) KV and inputs; no dataset exists for this path)",
+            "config": {"workload": "config 2: batched hybrid-layer decode", "slots_per_gpu": SLOTS,
+                       "global_slots": SLOTS * world,
+                       "kv_len": f"U[{a.kv_lo}, {a.kv_hi}] per slot, +1 per step",
+                       "mean_kv_len": round(mean_L, 1), "deltanet_layers_per_slot": DN_LAYERS,
+                       "parallelism": f"slot-sharded x{world} (no collective)",
+                       "l2": "inputs (>2.5 GB per GPU) exceed L2; no flush needed"},
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel",
+                         "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(attn_gbs / hbm, 4), "traffic": traffic,
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
+                         "algorithmic_bytes_per_launch": round(attn_bytes)},
+            "kernels": {
+                "attn_decode_kernel": {"ms": round(attn_avg, 4), "GB/s": round(attn_gbs, 1),
+                                       "frac": round(attn_gbs / hbm, 4), "bytes": round(attn_bytes)},
+                "deltanet_step_kernel": {"ms": round(dn_avg, 4), "GB/s": round(dn_gbs, 1),
+                                         "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
+            "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    lens = slot_lengths(0, a.kv_lo, a.kv_hi)
+    r = cpu_leg(lens, tokens=max(1, a.steps), warmup=max(0, a.warmup))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(r["tok_s"], 3), "unit": "tok/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(1e3 * r["seconds"] / r["tokens"], 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "config 2: batched hybrid-layer decode", "slots_per_gpu": SLOTS,
+                   "kv_len": "U[1024, 32768] per slot", "deltanet_layers_per_slot": DN_LAYERS,
+                   "parallelism": "host CPU, slots serialised (reference step lock)"},
+        "cpu_baseline": {"value": round(r["tok_s"], 3), "unit": "tok/s", "cores": r["threads"],
+                         "kind": "reference",
+                         "sample": f"each step = one slot-step (cycling the 64 slots): reference "
+                                   f"full_attention minus its projection matvecs + 3 "
+                                   f"recurrent_delta_step; OpenMP {r['threads']} threads"},
+        "e2e": {"value": round(r["tok_s"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = args_parse()
+    if a.cpu_json:
+        spec = json.loads(a.cpu_json)
+        r = cpu_reference(spec["lens"], spec["tokens"], spec["warmup"], spec["threads"])
+        print(json.dumps(r))
+        return
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

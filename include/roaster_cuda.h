@@ -69,6 +69,7 @@ int   kernel_cuda_free(void *ptr);
 int   kernel_cuda_upload(void *dst_dev, const void *src_host, size_t bytes);   /* synchronous */
 int   kernel_cuda_download(void *dst_host, const void *src_dev, size_t bytes); /* synchronous */
 int   kernel_cuda_memmove(void *dst_dev, const void *src_dev, size_t bytes);   /* overlap-safe, async */
+int   kernel_cuda_memset(void *dst_dev, int value, size_t bytes);              /* async (model_reset) */
 
 /* ------------------------------------------------------------------ gated attention, decode
  * Replaces model.c:801-861 (Q|G split, q/k RMSNorm, partial RoPE, KV append, GQA softmax
@@ -143,6 +144,10 @@ typedef struct {
 
 /* Device-pointer batch (independent states: slots and/or layers). Asynchronous. */
 int kernel_deltanet_step_batch(const KernelDeltaStepJob *jobs, int n);
+
+/* Same, with q/k/v/g/beta/out in HOST memory (states on the device). Synchronous: one packed
+ * host->device copy of all inputs, the device batch, one device->host copy of all outputs. */
+int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, int n);
 
 /* Drop-in for recurrent_delta_step(&ssm_state[layer], q, k, v, alpha, beta, out) with host
  * q/k/v/g/beta/out and the device-resident state. Synchronous. */

@@ -69,6 +69,7 @@ def lib():
         "kernel_cuda_upload": (C.c_int, [_vp, _vp, _sz]),
         "kernel_cuda_download": (C.c_int, [_vp, _vp, _sz]),
         "kernel_cuda_memmove": (C.c_int, [_vp, _vp, _sz]),
+        "kernel_cuda_memset": (C.c_int, [_vp, C.c_int, _sz]),
         "kernel_attn_decode_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
         "kernel_attn_decode_batch_host": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
         "kernel_attn_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
@@ -78,6 +79,7 @@ def lib():
                                                  C.POINTER(_vp)]),
         "kernel_deltanet_step_batch": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_step": (C.c_int, [_vp] * 7),
+        "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -170,6 +172,11 @@ def attn_merge_partials(partials, nparts: int, gates, outs, qg_stride: int = 256
     o = (_vp * n)(*[_ptr(x) for x in outs])
     check(lib().kernel_attn_merge_partials(_ptr(partials), nparts, n, g, qg_stride, o),
           "kernel_attn_merge_partials")
+
+
+def deltanet_step_batch_host(jobs) -> None:
+    arr, n = _arr(KernelDeltaStepJob, jobs)
+    check(lib().kernel_deltanet_step_batch_host(arr, n), "kernel_deltanet_step_batch_host")
 
 
 def deltanet_step_batch(jobs) -> None:

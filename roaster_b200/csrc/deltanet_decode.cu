@@ -15,6 +15,7 @@
 
 #include <cuda_runtime.h>
 #include <cstring>
+#include <vector>
 
 namespace rb {
 namespace {
@@ -149,6 +150,57 @@ extern "C" int kernel_deltanet_step_batch(const KernelDeltaStepJob *jobs, int n)
     if (ensure() != 0)
         return -1;
     return deltanet_step_batch(jobs, n);
+}
+
+extern "C" int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_deltanet_step_batch_host: bad job array");
+    if (n == 0)
+        return 0;
+    // per job: q, k [16x128], v [32x128], g, beta [32] in; out [32x128]
+    const size_t nq = 16 * 128, nv = 32 * 128, nh = 32;
+    const size_t in_f = 2 * nq + nv + 2 * nh, out_f = nv;
+    const size_t total = (size_t)n * (in_f + out_f);
+    float *h = static_cast<float *>(pinned(total * sizeof(float)));
+    float *d = static_cast<float *>(dstage(total * sizeof(float)));
+    if (!h || !d)
+        return -1;
+    std::vector<KernelDeltaStepJob> dj(jobs, jobs + n);
+    for (int i = 0; i < n; i++) {
+        const KernelDeltaStepJob &s = jobs[i];
+        if (!s.state || !s.q || !s.k || !s.v || !s.g || !s.beta || !s.out)
+            return fail("kernel_deltanet_step_batch_host: job %d has a null pointer", i);
+        float *b = h + (size_t)i * in_f;
+        memcpy(b, s.q, nq * 4);
+        memcpy(b + nq, s.k, nq * 4);
+        memcpy(b + 2 * nq, s.v, nv * 4);
+        memcpy(b + 2 * nq + nv, s.g, nh * 4);
+        memcpy(b + 2 * nq + nv + nh, s.beta, nh * 4);
+        float *db = d + (size_t)i * in_f;
+        dj[i].q = db;
+        dj[i].k = db + nq;
+        dj[i].v = db + 2 * nq;
+        dj[i].g = db + 2 * nq + nv;
+        dj[i].beta = db + 2 * nq + nv + nh;
+        dj[i].out = d + (size_t)n * in_f + (size_t)i * out_f;
+    }
+    cudaStream_t st = rt().stream;
+    if (check(cudaMemcpyAsync(d, h, (size_t)n * in_f * 4, cudaMemcpyHostToDevice, st), "stage in") != 0)
+        return -1;
+    if (deltanet_step_batch(dj.data(), n) != 0)
+        return -1;
+    float *hout = h + (size_t)n * in_f;
+    if (check(cudaMemcpyAsync(hout, d + (size_t)n * in_f, (size_t)n * out_f * 4, cudaMemcpyDeviceToHost, st),
+              "stage out") != 0)
+        return -1;
+    if (kernel_cuda_synchronize() != 0)
+        return -1;
+    for (int i = 0; i < n; i++)
+        memcpy(jobs[i].out, hout + (size_t)i * out_f, out_f * 4);
+    return 0;
 }
 
 extern "C" int kernel_deltanet_step(float *state, const float *q, const float *k, const float *v,

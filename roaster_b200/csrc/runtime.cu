@@ -277,6 +277,13 @@ int kernel_cuda_download(void *dst, const void *src, size_t bytes)
     return check(cudaStreamSynchronize(g_rt.stream), "download sync");
 }
 
+int kernel_cuda_memset(void *dst, int value, size_t bytes)
+{
+    if (ensure() != 0)
+        return -1;
+    return check(cudaMemsetAsync(dst, value, bytes, g_rt.stream), "kernel_cuda_memset");
+}
+
 int kernel_cuda_memmove(void *dst, const void *src, size_t bytes)
 {
     if (ensure() != 0)
