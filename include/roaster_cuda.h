@@ -103,6 +103,21 @@ int kernel_attn_decode_batch(const KernelAttnDecodeJob *jobs, int n);
  * Synchronous: returns when every `out` holds its result. */
 int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n);
 
+/* Allocation-free form of kernel_attn_decode_batch. It has no counterpart in the reference: it
+ * exists for callers that must not allocate device memory once they are serving -- a host
+ * running under a device-memory budget fixed at start-up, or code that may not enter the CUDA
+ * allocator (or an allocating library such as torch's caching allocator) at decode time.
+ * It never calls cudaMalloc/cudaFree: its scratch (split softmax partials, completion counters,
+ * an error word) is one statically sized 8 MiB device array that every GPU loading this library
+ * holds until the process exits. Limits: at most 64 slots per call (more is rejected with an
+ * error); windows of any length (the split size grows so the partials fit the array).
+ * The first call on each device does a one-time set-up (it looks up the array's device address
+ * and the SM count) and should come before any stream capture. Every call shares the one array
+ * and clears its counters at the start, so calls whose work overlaps on the GPU (different
+ * streams, or different threads) race and must be serialised by the caller. Same job semantics,
+ * results and asynchrony as kernel_attn_decode_batch; all pointers device memory. */
+int kernel_attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n);
+
 /* Drop-in for full_attention's core (model.c:801-861) with model.c's own host buffers:
  * q_gate = the interleaved [16][512] projection, k_new/v_new = attn_k/attn_v [512],
  * q_norm/k_norm = R->qnorm/R->knorm, caches = the device-resident KVCache.k/.v, out = attn_out

@@ -72,6 +72,7 @@ def lib():
         "kernel_cuda_memset": (C.c_int, [_vp, C.c_int, _sz]),
         "kernel_attn_decode_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
         "kernel_attn_decode_batch_host": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
+        "kernel_attn_decode_batch_noalloc": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
         "kernel_attn_decode": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _vp]),
         "kernel_attn_decode_partial_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int,
                                                        _vp]),
@@ -153,6 +154,12 @@ def _arr(struct, jobs):
 def attn_decode_batch(jobs) -> None:
     arr, n = _arr(KernelAttnDecodeJob, jobs)
     check(lib().kernel_attn_decode_batch(arr, n), "kernel_attn_decode_batch")
+
+
+def attn_decode_batch_noalloc(jobs) -> None:
+    """The allocation-free decode entry point (static 8 MiB device scratch, <= 64 slots)."""
+    arr, n = _arr(KernelAttnDecodeJob, jobs)
+    check(lib().kernel_attn_decode_batch_noalloc(arr, n), "kernel_attn_decode_batch_noalloc")
 
 
 def attn_decode_batch_host(jobs) -> None:

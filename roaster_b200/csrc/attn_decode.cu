@@ -743,6 +743,213 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
     return launched("attn_decode_kernel");
 }
 
+// ---------------------------------------------------------------- allocation-free variant
+//
+// Some callers cannot allocate device memory while they decode: a host that runs under a fixed
+// device-memory budget handed out up front, code that must not enter the CUDA allocator (or any
+// allocating library, torch's caching allocator included) once serving has started, or a
+// process where allocation would serialise against other streams. For them,
+// kernel_attn_decode_batch_noalloc runs the same decode kernel with its scratch (the split
+// softmax partial records, the per-(slot, kv head) completion counters and an error word) in
+// this statically sized device array instead of library-allocated memory. Every GPU that loads
+// the library holds the array until the process exits.
+constexpr size_t kNoAllocBytes = 8u << 20;                     // 8 MiB per device
+constexpr int kNoAllocCounterInts = 2 * kMaxJobs + 64;         // counters, then the error word
+constexpr size_t kNoAllocHeadBytes = 1024;                     // counters + error word, padded
+constexpr size_t kNoAllocNewFloats = (size_t)kMaxJobs * 2 * kPF;
+constexpr int kNoAllocMaxItems =
+    (int)((kNoAllocBytes - kNoAllocHeadBytes - kNoAllocNewFloats * sizeof(float)) / (kPF * sizeof(float)));
+static_assert(kNoAllocCounterInts * sizeof(int) <= kNoAllocHeadBytes, "head too small");
+static_assert(kNoAllocMaxItems >= 4 * kMaxJobs, "static scratch too small for a full batch");
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+
+struct NoAllocDevice {
+    bool ready;
+    unsigned char *base;       // device address of g_noalloc_scratch on that device
+    int num_sms;
+};
+NoAllocDevice g_noalloc_dev[64];
+
+// Per-device set-up, once, with `device` current: resolve the array's device address (host code
+// must not use the symbol itself, which on the host is only a stand-in) and the SM count; set the
+// kernel's shared-memory limit. Nothing here allocates.
+int noalloc_setup(int device)
+{
+    NoAllocDevice &d = g_noalloc_dev[device];
+    if (d.ready)
+        return 0;
+    void *ptr = nullptr;
+    if (check(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)") != 0)
+        return -1;
+    int sms = 0;
+    if (check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count") != 0)
+        return -1;
+    if (check(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemBytes), "attn decode smem attribute") != 0)
+        return -1;
+    d.base = static_cast<unsigned char *>(ptr);
+    d.num_sms = sms < kMaxCtas ? sms : kMaxCtas;
+    d.ready = true;
+    return 0;
+}
+
+struct NoAllocItem {
+    long long cost;
+    unsigned short code;
+    short cta;
+};
+
+}  // namespace
+
+int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
+{
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_attn_decode_batch_noalloc: bad job array");
+    if (n > kMaxJobs)
+        return fail("kernel_attn_decode_batch_noalloc: %d slots in one call; the static scratch "
+                    "serves at most %d (split the batch into several calls)", n, kMaxJobs);
+    if (n == 0)
+        return 0;
+    int device = 0;
+    if (check(cudaGetDevice(&device), "cudaGetDevice") != 0)
+        return -1;
+    if (device < 0 || device >= 64)
+        return fail("kernel_attn_decode_batch_noalloc: device %d out of range", device);
+    if (noalloc_setup(device) != 0)
+        return -1;
+    const NoAllocDevice &dev = g_noalloc_dev[device];
+    long long total = 0;
+    for (int i = 0; i < n; i++) {
+        if (validate(jobs[i], i, false) != 0)
+            return -1;
+        total += (long long)jobs[i].length;
+    }
+    // Same split rule as the allocating path, capped at the items the static array holds.
+    long long target = (long long)((double)total / ((double)dev.num_sms * decode_items_per_sm())) + 1;
+    if (target < 2 * kTile)
+        target = 2 * kTile;
+    DParams p;
+    memset(static_cast<void *>(&p), 0, sizeof(p));
+    const int cap_items = kNoAllocMaxItems < kMaxItems ? kNoAllocMaxItems : kMaxItems;
+    int items = 0;
+    for (int attempt = 0;; attempt++) {
+        items = 0;
+        for (int i = 0; i < n; i++) {
+            const long long L = (long long)jobs[i].length;
+            long long ns = (L + target / 2) / target;
+            ns = ns < 1 ? 1 : (ns > kMaxSplits ? kMaxSplits : ns);
+            long long ch = (L + ns - 1) / ns;
+            ch = (ch + kTile - 1) / kTile * kTile;
+            if (ch < kTile)
+                ch = kTile;
+            ns = (L + ch - 1) / ch;
+            if (ns < 1)
+                ns = 1;
+            p.jobs[i].chunk = ch;
+            p.jobs[i].nsplit = (int)ns;
+            p.jobs[i].item_base = items;
+            items += 2 * (int)ns;
+        }
+        if (items <= cap_items)
+            break;
+        if (attempt > 40)
+            return fail("kernel_attn_decode_batch_noalloc: cannot plan within %d items", cap_items);
+        target *= 2;
+    }
+    const int grid = items < dev.num_sms ? items : dev.num_sms;
+    // Longest-first onto the least-loaded CTA, with fixed-size arrays only (no heap use).
+    NoAllocItem order[kMaxItems];
+    int k = 0;
+    for (int i = 0; i < n; i++) {
+        const DJob &d = p.jobs[i];
+        for (int sp = 0; sp < d.nsplit; sp++) {
+            const long long t0 = (long long)sp * d.chunk;
+            const long long t1 = std::min<long long>(t0 + d.chunk, (long long)jobs[i].length);
+            for (int kvh = 0; kvh < 2; kvh++)
+                order[k++] = NoAllocItem{(t1 > t0 ? t1 - t0 : 0) + 256,
+                                         (unsigned short)((i << 9) | (sp << 1) | kvh), 0};
+        }
+    }
+    std::sort(order, order + items, [](const NoAllocItem &a, const NoAllocItem &b) {
+        return a.cost != b.cost ? a.cost > b.cost : a.code < b.code;
+    });
+    long long load[kMaxCtas] = {0};
+    int heap[kMaxCtas];                      // binary min-heap of CTA ids by (load, id)
+    auto less = [&](int a, int b) { return load[a] != load[b] ? load[a] < load[b] : a < b; };
+    for (int c = 0; c < grid; c++) {
+        load[c] = 0;
+        heap[c] = c;
+    }
+    for (int it = 0; it < items; it++) {
+        const int c = heap[0];
+        order[it].cta = (short)c;
+        load[c] += order[it].cost;
+        int pos = 0;                          // sift the grown root down
+        for (;;) {
+            int l = 2 * pos + 1, r = l + 1, m = pos;
+            if (l < grid && less(heap[l], heap[m]))
+                m = l;
+            if (r < grid && less(heap[r], heap[m]))
+                m = r;
+            if (m == pos)
+                break;
+            std::swap(heap[pos], heap[m]);
+            pos = m;
+        }
+    }
+    int count[kMaxCtas + 1];
+    for (int c = 0; c <= grid; c++)
+        count[c] = 0;
+    for (int it = 0; it < items; it++)
+        count[order[it].cta + 1]++;
+    for (int c = 0; c < grid; c++)
+        count[c + 1] += count[c];
+    for (int c = 0; c <= grid; c++)
+        p.cta_off[c] = (unsigned short)count[c];
+    for (int it = 0; it < items; it++)
+        p.sched[count[order[it].cta]++] = order[it].code;
+    for (int i = 0; i < n; i++) {
+        const KernelAttnDecodeJob &s = jobs[i];
+        DJob &d = p.jobs[i];
+        d.q = s.q;
+        d.gate = s.gate;
+        d.k_new = s.k_new;
+        d.v_new = s.v_new;
+        d.q_norm = s.q_norm;
+        d.k_norm = s.k_norm;
+        d.k_cache = reinterpret_cast<__half *>(s.k_cache);
+        d.v_cache = reinterpret_cast<__half *>(s.v_cache);
+        d.out = s.out;
+        d.qg_stride = (long long)s.qg_stride;
+        d.length = (long long)s.length;
+        d.position = (long long)s.position;
+        d.append = s.append ? 1 : 0;
+    }
+    for (int j = 0; j < 32; j++)           // same host libm powf the reference uses
+        p.inv_freq[j] = powf(10000000.0f, -2.0f * (float)j / 64.0f);
+    int *cnt = reinterpret_cast<int *>(dev.base);
+    unsigned *own_err = reinterpret_cast<unsigned *>(dev.base) + 2 * kMaxJobs;
+    float *ws = reinterpret_cast<float *>(dev.base + kNoAllocHeadBytes);
+    p.newpart = ws;
+    p.part = ws + kNoAllocNewFloats;
+    p.counters = cnt;
+    p.pout = nullptr;
+    // Kernel-recorded failures go to the library's error word when the caller initialised the
+    // library (so kernel_cuda_synchronize reports them), else to the array's own word.
+    p.err = rt().err_word ? rt().err_word : own_err;
+    p.njobs = n;
+    p.nitems = items;
+    cudaStream_t st = rt().stream;
+    // The array keeps whatever the previous call left: the counters must start at zero.
+    if (check(cudaMemsetAsync(dev.base, 0, kNoAllocHeadBytes, st), "clear noalloc counters") != 0)
+        return -1;
+    attn_decode_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+    return launched("attn_decode_kernel (noalloc)");
+}
+
 }  // namespace
 
 int attn_decode_batch(const KernelAttnDecodeJob *jobs, int n, float *pout)
@@ -793,6 +1000,11 @@ extern "C" int kernel_attn_decode_batch(const KernelAttnDecodeJob *jobs, int n)
     if (ensure() != 0)
         return -1;
     return attn_decode_batch(jobs, n, nullptr);
+}
+
+extern "C" int kernel_attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
+{
+    return attn_decode_batch_noalloc(jobs, n);
 }
 
 extern "C" int kernel_attn_decode_partial_batch(const KernelAttnDecodeJob *jobs, int n, float *partials)
