@@ -142,6 +142,44 @@ int kernel_attn_merge_partials(const float *partials, int nparts, int n,
                                const float *const *gates, size_t qg_stride,
                                float *const *outs);
 
+/* ------------------------------------------------------------------ gated attention, prefill
+ * Replaces pf_attention's attention part (model.c:1553-1600): per token q/k RMSNorm and partial
+ * RoPE at position base + t, append of all T tokens' K/V at window index kbase + t, then causal
+ * GQA attention of token t over window entries [0, kbase + t], times sigmoid(gate). */
+
+#define KERNEL_DTYPE_F32  0
+#define KERNEL_DTYPE_BF16 1
+
+typedef struct {
+    const void *q;           /* token t, head h at q + t*qg_tok_stride + h*qg_stride (elements)  */
+    const void *gate;        /* same strides as q                                                */
+    size_t qg_stride;        /* 256, or 512 for the interleaved [Q0|G0|Q1|G1|...] projection     */
+    size_t qg_tok_stride;    /* elements from one token to the next (4096 or 8192)                */
+    const void *k;           /* [T][2][256] raw K projections                                    */
+    const void *v;           /* [T][2][256] V projections                                        */
+    const float *q_norm;     /* [256]                                                            */
+    const float *k_norm;     /* [256]                                                            */
+    uint16_t *k_cache;       /* f16 [capacity][2][256], device, 16-byte aligned                  */
+    uint16_t *v_cache;
+    size_t capacity;         /* kbase + T must not exceed it                                     */
+    size_t kbase;            /* tokens already in the window (the chunk appends after them)     */
+    size_t base;             /* absolute RoPE position of token 0                                */
+    size_t T;                /* tokens in this chunk (>= 1)                                      */
+    float *out;              /* [T][16][256] gated attention output                              */
+    int dtype;               /* element type of q, gate, k, v: KERNEL_DTYPE_F32 or _BF16         */
+} KernelAttnPrefillJob;
+
+/* Device-pointer batch (e.g. several prompts). Asynchronous. Tensor-core operands are f16. */
+int kernel_attn_prefill_batch(const KernelAttnPrefillJob *jobs, int n);
+
+/* Drop-in for pf_attention's core with its own host buffers (T <= 256 in the reference):
+ * q_gate = p->qkv [T][8192] interleaved Q|G, k/v = p->k, p->v [T][512], caches device-resident,
+ * kbase = kv->length, base = the absolute position; out = p->rec [T][4096]. The caller then sets
+ * kv->length = kbase + T. Synchronous. */
+int kernel_attn_prefill(const float *q_gate, const float *k, const float *v, const float *q_norm,
+                        const float *k_norm, uint16_t *k_cache, uint16_t *v_cache, size_t capacity,
+                        size_t kbase, size_t base, size_t T, float *out);
+
 /* ------------------------------------------------------------------ Gated DeltaNet, decode
  * Replaces recurrent_delta_step (model.c:272-323): per value head vh (key head vh % 16),
  * d = exp(g), delta = (v - d S^T k) beta, out = (d S^T q + (k.q) delta) / sqrt(128),

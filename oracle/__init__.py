@@ -58,6 +58,10 @@ def _load(which: str):
         lib.orc_attn_decode_partial.argtypes = [_fp, C.c_size_t, _fp, _u16p, _u16p, C.c_size_t,
                                                 C.c_size_t, C.c_size_t, _fp, _fp, _fp]
         lib.orc_attn_decode_partial.restype = C.c_int
+        lib.orc_attn_prefill_rows.argtypes = [C.c_size_t, _fp, _fp, C.c_size_t, C.c_size_t, _fp,
+                                              _fp, _fp, _fp, _u16p, _u16p, C.c_size_t, C.c_size_t,
+                                              C.POINTER(C.c_long), C.c_size_t, _fp]
+        lib.orc_attn_prefill_rows.restype = C.c_int
         lib.orc_delta_step.argtypes = [_fp] * 7
         lib.orc_delta_step.restype = None
         lib.orc_delta_prefill.argtypes = [_fp, C.c_size_t] + [_fp] * 6
@@ -222,6 +226,28 @@ def attn_prefill(q, gate, k, v, qnorm, knorm, k_cache, v_cache, kbase, base, imp
         win_v[cur:cur + n] = vv
         t0 += n
     return out, ka, va
+
+
+def attn_prefill_rows(q, gate, k, v, qnorm, knorm, k_cache, v_cache, kbase, base, rows):
+    """Prefill outputs for the listed token indices only (port). Returns [len(rows), 16, 256]."""
+    lib = _load("port")
+    q = np.ascontiguousarray(q, np.float32)
+    gate = np.ascontiguousarray(gate, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    qnorm = np.ascontiguousarray(qnorm, np.float32)
+    knorm = np.ascontiguousarray(knorm, np.float32)
+    T = q.shape[0]
+    r = np.ascontiguousarray(rows, np.int64)
+    kc = np.ascontiguousarray(k_cache[:kbase] if kbase else np.zeros((1, 2, 256)), np.float16)
+    vc = np.ascontiguousarray(v_cache[:kbase] if kbase else np.zeros((1, 2, 256)), np.float16)
+    out = np.zeros((len(r), 16, 256), np.float32)
+    rc = lib.orc_attn_prefill_rows(T, _f(q), _f(gate), 256, 16 * 256, _f(k), _f(v), _f(qnorm),
+                                   _f(knorm), _h(kc), _h(vc), kbase, base,
+                                   r.ctypes.data_as(C.POINTER(C.c_long)), len(r), _f(out))
+    if rc != 0:
+        raise RuntimeError("oracle attn_prefill_rows failed")
+    return out
 
 
 # ----------------------------------------------------------------------------- DeltaNet

@@ -279,6 +279,68 @@ done:
     return rc;
 }
 
+int orc_attn_prefill_rows(size_t T, const float *q, const float *gate, size_t qg_stride,
+                          size_t qg_tok_stride, const float *k, const float *v,
+                          const float *qnorm, const float *knorm,
+                          const uint16_t *k_cache, const uint16_t *v_cache,
+                          size_t kbase, size_t base, const long *rows, size_t nrows, float *out)
+{
+    if (!q || !gate || !k || !v || !qnorm || !knorm || !out || !rows || T == 0)
+        return -1;
+    if (kbase && (!k_cache || !v_cache))
+        return -1;
+    const size_t n = kbase * ORC_KVH * ORC_D;
+    float *kc = widen(k_cache, n), *vc = widen(v_cache, n);
+    float *kp = (float *)malloc(T * ORC_KVH * ORC_D * sizeof(float));
+    int rc = -1;
+    if (!kc || !vc || !kp)
+        goto done;
+    for (size_t t = 0; t < T; t++) {
+        for (int h = 0; h < ORC_KVH; h++)
+            orc_rmsnorm(kp + (t * ORC_KVH + h) * ORC_D, k + (t * ORC_KVH + h) * ORC_D, knorm, ORC_D, 1e-6f);
+        orc_rope64(kp + t * ORC_KVH * ORC_D, ORC_KVH, ORC_D, base + t);
+    }
+    {
+        Window w = { kc, vc, kbase, kp, v };
+        int bad = 0;
+        #pragma omp parallel
+        {
+            float *scores = (float *)malloc((kbase + T) * sizeof(float));
+            float qh[ORC_D];
+            if (!scores) {
+                #pragma omp atomic write
+                bad = 1;
+            }
+            #pragma omp for schedule(dynamic, 1)
+            for (long idx = 0; idx < (long)(nrows * ORC_QH); idx++) {
+                if (!scores)
+                    continue;
+                const size_t i = (size_t)idx / ORC_QH;
+                const int h = (int)(idx % ORC_QH);
+                const long t = rows[i];
+                if (t < 0 || (size_t)t >= T)
+                    continue;
+                orc_rmsnorm(qh, q + (size_t)t * qg_tok_stride + (size_t)h * qg_stride, qnorm, ORC_D, 1e-6f);
+                orc_rope64(qh, 1, ORC_D, base + (size_t)t);
+                float *o = out + (i * ORC_QH + h) * ORC_D;
+                attend_row(qh, kbase + (size_t)t + 1, win_k, win_v, &w, h / 8, scores, o);
+                const float *g = gate + (size_t)t * qg_tok_stride + (size_t)h * qg_stride;
+                for (int d = 0; d < ORC_D; d++)
+                    o[d] *= sigm(g[d]);
+            }
+            free(scores);
+        }
+        if (bad)
+            goto done;
+    }
+    rc = 0;
+done:
+    free(kc);
+    free(vc);
+    free(kp);
+    return rc;
+}
+
 int orc_attn_decode_partial(const float *q, size_t qg_stride, const float *qnorm,
                             const uint16_t *k_cache, const uint16_t *v_cache,
                             size_t t0, size_t t1, size_t position,

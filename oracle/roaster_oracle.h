@@ -75,6 +75,15 @@ int orc_attn_prefill(size_t T, const float *q, const float *gate, size_t qg_stri
                      size_t kbase, size_t base,
                      float *out, float *k_app, float *v_app);
 
+/* Same as orc_attn_prefill but computes the outputs of the `nrows` tokens listed in `rows`
+ * only (out: [nrows][16][256]); every token's K is still prepared and appended. For checking
+ * long prompts on a sample of rows. */
+int orc_attn_prefill_rows(size_t T, const float *q, const float *gate, size_t qg_stride,
+                          size_t qg_tok_stride, const float *k, const float *v,
+                          const float *qnorm, const float *knorm,
+                          const uint16_t *k_cache, const uint16_t *v_cache,
+                          size_t kbase, size_t base, const long *rows, size_t nrows, float *out);
+
 /* One Gated DeltaNet decode step (model.c:272-323). state: [32][128][128], updated in place.
  * q,k: [16][128]; v: [32][128]; g: [32] log-decay; beta: [32]; out: [32][128]. */
 void orc_delta_step(float *state, const float *q, const float *k, const float *v,

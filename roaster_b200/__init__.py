@@ -39,6 +39,16 @@ class KernelAttnDecodeJob(C.Structure):
     ]
 
 
+class KernelAttnPrefillJob(C.Structure):
+    """Mirror of ``KernelAttnPrefillJob`` (include/roaster_cuda.h)."""
+    _fields_ = [
+        ("q", _vp), ("gate", _vp), ("qg_stride", _sz), ("qg_tok_stride", _sz), ("k", _vp),
+        ("v", _vp), ("q_norm", _vp), ("k_norm", _vp), ("k_cache", _vp), ("v_cache", _vp),
+        ("capacity", _sz), ("kbase", _sz), ("base", _sz), ("T", _sz), ("out", _vp),
+        ("dtype", C.c_int),
+    ]
+
+
 class KernelDeltaStepJob(C.Structure):
     """Mirror of ``KernelDeltaStepJob`` (include/roaster_cuda.h)."""
     _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp),
@@ -78,6 +88,8 @@ def lib():
                                                        _vp]),
         "kernel_attn_merge_partials": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp), _sz,
                                                  C.POINTER(_vp)]),
+        "kernel_attn_prefill_batch": (C.c_int, [C.POINTER(KernelAttnPrefillJob), C.c_int]),
+        "kernel_attn_prefill": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]),
         "kernel_deltanet_step_batch": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_step": (C.c_int, [_vp] * 7),
         "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
@@ -179,6 +191,13 @@ def attn_merge_partials(partials, nparts: int, gates, outs, qg_stride: int = 256
     o = (_vp * n)(*[_ptr(x) for x in outs])
     check(lib().kernel_attn_merge_partials(_ptr(partials), nparts, n, g, qg_stride, o),
           "kernel_attn_merge_partials")
+
+
+def attn_prefill_batch(jobs) -> None:
+    """jobs: KernelAttnPrefillJob instances or tuples of its fields in order."""
+    js = [j if isinstance(j, KernelAttnPrefillJob) else KernelAttnPrefillJob(*j) for j in jobs]
+    arr, n = _arr(KernelAttnPrefillJob, js)
+    check(lib().kernel_attn_prefill_batch(arr, n), "kernel_attn_prefill_batch")
 
 
 def deltanet_step_batch_host(jobs) -> None:

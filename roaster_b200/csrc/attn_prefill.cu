@@ -1,0 +1,727 @@
+// Gated GQA attention, causal prefill, on sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Replaces the attention part of pf_attention (reference src/model.c:1553-1600):
+//   per token t: RMSNorm(q_h) * qnorm, RMSNorm(k) * knorm, partial NeoX RoPE (dims 0..63,
+//   theta 1e7) at position base + t, append K/V at window index kbase + t; then for each query
+//   head h (kv head h / 8): softmax over window entries [0, kbase + t] of q.k / 16, times V,
+//   times sigmoid(gate).
+//
+// Two kernels.
+//  1. prefill_prep_kernel (HBM-bound, one CTA per token): norms + RoPE; writes the prepared
+//     queries as f16 to scratch and appends K/V (f16) to the cache.
+//  2. prefill_attn_kernel (tensor-bound): a work item is (prompt, query head, 128-token query
+//     tile); persistent CTAs take items longest-first. Per CTA (256 threads):
+//       warp 0      one thread issues every tcgen05.mma and commit;
+//       warps 1-3   producers: 16-byte cp.async into 128-byte-swizzled tiles -- the Q tile
+//                   (128 x 256 f16, 64 KB) once per item, then K_j, V_j tiles (64 keys x 256,
+//                   32 KB each) through a 5-stage ring;
+//       warps 4-7   softmax + epilogue: one thread per query row (= TMEM lane).
+//     Tensor memory (512 columns): S_j = Q K_j^T (128 x 64 fp32) double-buffered in columns
+//     [0,64) and [64,128); the softmax writes P_j as packed f16 over the first 32 columns of its
+//     own S buffer, and O += P_j V_j reads P straight from TMEM (A operand in tensor memory, V as
+//     an MN-major B operand); O (128 x 256 fp32) lives in columns [256, 512).
+//     The MMA issue order S_0, S_1, PV_0, S_2, PV_1, ... overlaps each QK^T with the softmax of
+//     the previous tile. The running max is raised only when a tile exceeds it by more than 2^8
+//     (log2 units), so O is rescaled (a TMEM read-modify-write) rarely; P values stay <= 256.
+//
+// Synchronisation (all mbarrier waits bounded; a timeout sets the device error word):
+//   q_full / q_empty       Q tile of the current item loaded / all its QK^T MMAs done
+//   kv_full[s] / kv_empty[s]  ring stage loaded / consumed by its MMA
+//   s_full[b]              S buffer b written (tcgen05.commit)
+//   p_full[b]              P of buffer b written by all 128 softmax threads
+//   pv_done[k % 2]         O += P_k V_k finished (two barriers so no waiter is ever two phases
+//                          behind: a commit fires only after every earlier MMA, so when S_j is
+//                          complete every PV up to j-2 is too)
+// Producers publish a stage one cp.async group late (wait_group 1, then a generic->async proxy
+// fence, then arrive), so the tensor core reads data the copies have actually landed.
+#include "ptx.cuh"
+#include "runtime.h"
+#include "tcgen05.cuh"
+#include "../../include/roaster_cuda.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <queue>
+#include <vector>
+
+namespace rb {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kBM = 128;                     // query rows per item
+constexpr int kBN = 64;                      // keys per tile
+constexpr int kStages = 5;
+constexpr int kChunkQ = kBM * 128;           // one 64-dim chunk of the Q tile (16 KB)
+constexpr int kQBytes = 4 * kChunkQ;         // 64 KB
+constexpr int kChunkKV = kBN * 128;          // 8 KB
+constexpr int kKVBytes = 4 * kChunkKV;       // 32 KB
+constexpr int kProdWarps = 3;
+constexpr int kProdThreads = kProdWarps * 32;
+constexpr int kThreads = 256;
+constexpr int kMaxJobs = 64;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;
+
+struct PJob {
+    const __half *qp;           // prepared queries of this job, [T][16][256] f16
+    const void *gate;
+    const __half *k_cache, *v_cache;
+    float *out;
+    long long qg_stride, qg_tok_stride, kbase, T;
+    int dtype, pad;
+};
+
+struct PParams {
+    PJob jobs[kMaxJobs];
+    const unsigned *sched;      // (job << 26) | (head << 22) | query tile, grouped by CTA
+    const int *cta_off;         // [grid + 1]
+    unsigned *err;
+    int njobs;
+};
+
+struct Smem {
+    unsigned char q[kQBytes];                   // 1024-byte aligned (swizzle atoms)
+    unsigned char kv[kStages][kKVBytes];
+    unsigned long long q_full, q_empty, kv_full[kStages], kv_empty[kStages];
+    unsigned long long s_full[2], p_full[2], pv_done[2], drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+__device__ __forceinline__ bool aborted(Smem &sm) { return *(volatile int *)&sm.abort != 0; }
+
+// Bounded wait whose outcome is the same for every lane of the warp (the warp then runs
+// warp-collective tcgen05 loads/stores together).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity)
+{
+    const bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void set_abort(const PParams &p, Smem &sm)
+{
+    atomicOr(p.err, kErrWaitTimeout);
+    *(volatile int *)&sm.abort = 1;
+}
+
+struct Item {
+    int job, head, kvh;
+    long long t0, rows, kend;     // first query token of the tile, valid rows, keys needed
+    int nt;                       // key tiles
+};
+
+__device__ __forceinline__ Item decode_item(const PParams &p, unsigned e)
+{
+    Item it;
+    it.job = (int)(e >> 26);
+    it.head = (int)((e >> 22) & 15u);
+    it.kvh = it.head >> 3;
+    const PJob &J = p.jobs[it.job];
+    it.t0 = (long long)(e & 0x3FFFFFu) * kBM;
+    it.rows = J.T - it.t0 < kBM ? J.T - it.t0 : kBM;
+    it.kend = J.kbase + it.t0 + it.rows;
+    it.nt = (int)((it.kend + kBN - 1) / kBN);
+    return it;
+}
+
+__device__ __forceinline__ void cp_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_group0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ float load_in(const void *base, long long idx, int dtype)
+{
+    if (dtype == KERNEL_DTYPE_BF16)
+        return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(base)[idx]);
+    return reinterpret_cast<const float *>(base)[idx];
+}
+
+// ---------------------------------------------------------------------------- prep kernel
+
+struct PrepJob {
+    const void *q, *k, *v;
+    const float *q_norm, *k_norm;
+    __half *qp, *k_cache, *v_cache;
+    long long qg_stride, qg_tok_stride, kbase, base, tok0;
+    int dtype, pad;
+};
+
+struct PrepParams {
+    PrepJob jobs[kMaxJobs];
+    float inv_freq[32];
+    int njobs;
+};
+
+// One CTA per token: warp w handles rows w, w + 8, w + 16 of the token's 16 q heads, 2 k heads
+// and 2 v heads; lane l holds dims 8l .. 8l+7.
+__global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ PrepParams p)
+{
+    const int gtok = blockIdx.x;
+    int lo = 0, hi = p.njobs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.jobs[mid].tok0 <= gtok)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    const PrepJob &J = p.jobs[lo];
+    const long long t = gtok - J.tok0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float pos = (float)(J.base + t);
+    for (int row = warp; row < 20; row += 8) {
+        float x[8];
+        const bool isq = row < 16, isk = row >= 16 && row < 18;
+        const int h = isq ? row : (isk ? row - 16 : row - 18);
+        if (isq) {
+            const long long b = t * J.qg_tok_stride + (long long)h * J.qg_stride + lane * 8;
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                x[e] = load_in(J.q, b + e, J.dtype);
+        } else {
+            const long long b = t * 512 + h * 256 + lane * 8;
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                x[e] = load_in(isk ? J.k : J.v, b + e, J.dtype);
+        }
+        if (isq || isk) {
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                ss = fmaf(x[e], x[e], ss);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / sqrtf(ss / (float)kD + 1e-6f);
+            const float *w = isq ? J.q_norm : J.k_norm;
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                x[e] = x[e] * inv * __ldg(w + lane * 8 + e);
+            // RoPE: dims j and j + 32 (j < 32) live on lanes l and l + 4 (l < 4)
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float other = __shfl_xor_sync(0xffffffffu, x[e], 4);
+                if (lane < 8) {
+                    float sn, cs;
+                    sincosf(pos * p.inv_freq[(lane & 3) * 8 + e], &sn, &cs);
+                    x[e] = lane < 4 ? x[e] * cs - other * sn : x[e] * cs + other * sn;
+                }
+            }
+        }
+        __half hv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            hv[e] = __float2half_rn(x[e]);
+        __half *dst;
+        if (isq)
+            dst = J.qp + (t * 16 + h) * kD + lane * 8;
+        else
+            dst = (isk ? J.k_cache : J.v_cache) + ((J.kbase + t) * 2 + h) * kD + lane * 8;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(hv);
+    }
+}
+
+// ---------------------------------------------------------------------------- attention kernel
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_constant__ PParams p)
+{
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw + ((1024u - (raw & 1023u)) & 1023u));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int i0 = p.cta_off[blockIdx.x], i1 = p.cta_off[blockIdx.x + 1];
+
+    if (tid == 0) {
+        mbar_init(smem_addr(&sm.q_full), kProdThreads);
+        mbar_init(smem_addr(&sm.q_empty), 1);
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(smem_addr(&sm.kv_full[s]), kProdThreads);
+            mbar_init(smem_addr(&sm.kv_empty[s]), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(smem_addr(&sm.s_full[b]), 1);
+            mbar_init(smem_addr(&sm.p_full[b]), 128);
+            mbar_init(smem_addr(&sm.pv_done[b]), 1);
+        }
+        mbar_init(smem_addr(&sm.drain), 1);
+        sm.abort = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(smem_addr(&sm.tmem_base), kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tbase = sm.tmem_base;
+    const uint32_t sq = smem_addr(sm.q);
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idS = tc::idesc_f16(kBM, kBN, 0, 0);
+            const uint32_t idO = tc::idesc_f16(kBM, kD, 0, 1);
+            unsigned fill = 0, g = 0, nitem = 0;
+            bool ok = true;
+            auto wait = [&](unsigned long long &bar, unsigned parity) {
+                if (ok && !mbar_wait(smem_addr(&bar), parity)) {
+                    set_abort(p, sm);
+                    ok = false;
+                }
+                return ok;
+            };
+            auto pv = [&](unsigned gg, unsigned fv, bool first) {
+                if (!wait(sm.p_full[gg & 1], (gg >> 1) & 1))
+                    return;
+                const int sv = fv % kStages;
+                if (!wait(sm.kv_full[sv], (fv / kStages) & 1))
+                    return;
+                tc::fence_after_sync();
+                const uint32_t vb = smem_addr(sm.kv[sv]);
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; kk++) {
+                    const uint64_t bd = tc::smem_desc(vb + kk * 16 * 128, kChunkKV, 1024);
+                    tc::mma_ts_f16(tbase + kColO, tbase + (gg & 1) * kBN + kk * 8, bd, idO,
+                                   (first && kk == 0) ? 0u : 1u);
+                }
+                tc::commit(smem_addr(&sm.pv_done[gg & 1]));
+                tc::commit(smem_addr(&sm.kv_empty[sv]));
+            };
+            for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
+                const Item it = decode_item(p, p.sched[idx]);
+                if (!wait(sm.q_full, nitem & 1))
+                    break;
+                tc::fence_after_sync();
+                const unsigned fbase = fill;
+                for (int j = 0; j < it.nt && ok; j++) {
+                    const unsigned fk = fbase + 2 * j;
+                    const int sk = fk % kStages;
+                    if (!wait(sm.kv_full[sk], (fk / kStages) & 1))
+                        break;
+                    tc::fence_after_sync();
+                    const uint32_t kb = smem_addr(sm.kv[sk]);
+                    const unsigned gj = g + j;
+#pragma unroll
+                    for (int kk = 0; kk < kD / 16; kk++) {
+                        const uint64_t ad = tc::smem_desc(sq + (kk >> 2) * kChunkQ + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = tc::smem_desc(kb + (kk >> 2) * kChunkKV + (kk & 3) * 32, 16, 1024);
+                        tc::mma_ss_f16(tbase + (gj & 1) * kBN, ad, bd, idS, kk > 0 ? 1u : 0u);
+                    }
+                    tc::commit(smem_addr(&sm.s_full[gj & 1]));
+                    tc::commit(smem_addr(&sm.kv_empty[sk]));
+                    if (j == it.nt - 1)
+                        tc::commit(smem_addr(&sm.q_empty));
+                    if (j >= 1)
+                        pv(gj - 1, fbase + 2 * (j - 1) + 1, j - 1 == 0);
+                }
+                if (ok)
+                    pv(g + it.nt - 1, fbase + 2 * (it.nt - 1) + 1, it.nt == 1);
+                g += it.nt;
+                fill += 2 * it.nt;
+            }
+            // every MMA issued must finish before tensor memory is released
+            tc::commit(smem_addr(&sm.drain));
+            mbar_wait(smem_addr(&sm.drain), 0);
+        }
+    } else if (warp <= kProdWarps) {
+        // ---------------------------------------------------------------- producers
+        const int pw = warp - 1;
+        const uint32_t lofs = (uint32_t)(lane >> 3);          // chunk of this lane's 8 dims
+        const uint32_t lu = (uint32_t)(lane & 7);             // 16-byte unit within the chunk
+        unsigned fill = 0, nitem = 0;
+        uint32_t pending = 0;                                 // barrier of the last unpublished group
+        bool ok = true;
+        auto publish_prev = [&](uint32_t next_bar) {
+            cp_commit_group();
+            cp_wait_group1();
+            fence_proxy_async();
+            if (pending)
+                mbar_arrive(pending);
+            pending = next_bar;
+        };
+        for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
+            const Item it = decode_item(p, p.sched[idx]);
+            const PJob &J = p.jobs[it.job];
+            if (nitem > 0 && !mbar_wait(smem_addr(&sm.q_empty), (nitem - 1) & 1)) {
+                if (lane == 0)
+                    set_abort(p, sm);
+                ok = false;
+                break;
+            }
+            for (int r = pw; r < kBM; r += kProdWarps) {
+                const long long tok = it.t0 + (r < it.rows ? r : it.rows - 1);
+                const __half *src = J.qp + (tok * 16 + it.head) * kD + lane * 8;
+                cp_async16(sq + lofs * kChunkQ + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4), src);
+            }
+            publish_prev(smem_addr(&sm.q_full));
+            for (int j = 0; j < it.nt && ok; j++) {
+                for (int which = 0; which < 2; which++, fill++) {
+                    const int s = fill % kStages;
+                    const unsigned f = fill / kStages;
+                    if (f > 0 && !mbar_wait(smem_addr(&sm.kv_empty[s]), (f - 1) & 1)) {
+                        if (lane == 0)
+                            set_abort(p, sm);
+                        ok = false;
+                        break;
+                    }
+                    const __half *cache = which ? J.v_cache : J.k_cache;
+                    const uint32_t st = smem_addr(sm.kv[s]) + lofs * kChunkKV;
+                    for (int r = pw; r < kBN; r += kProdWarps) {
+                        long long key = (long long)j * kBN + r;
+                        if (key > it.kend - 1)
+                            key = it.kend - 1;                       // tail: a valid row, masked later
+                        cp_async16(st + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4),
+                                   cache + (key * 2 + it.kvh) * kD + lane * 8);
+                    }
+                    publish_prev(smem_addr(&sm.kv_full[s]));
+                }
+            }
+        }
+        cp_wait_group0();
+        fence_proxy_async();
+        if (pending && ok)
+            mbar_arrive(pending);
+    } else {
+        // ---------------------------------------------------------------- softmax + epilogue
+        const int row = tid - 128;                         // query row = TMEM lane
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const float sc = kLog2e / 16.0f;
+        unsigned g = 0;
+        bool ok = true;
+        for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++) {
+            const Item it = decode_item(p, p.sched[idx]);
+            const PJob &J = p.jobs[it.job];
+            const bool qvalid = row < it.rows;
+            const long long tq = it.t0 + row;
+            const long long qlimit = qvalid ? J.kbase + tq : -1;  // last key this row may see
+            float m_run = -INFINITY, l = 0.f;
+            for (int j = 0; j < it.nt; j++) {
+                const unsigned gj = g + j;
+                const uint32_t sb = tbase + lane_base + (gj & 1) * kBN;
+                if (!warp_wait(smem_addr(&sm.s_full[gj & 1]), (gj >> 1) & 1)) {
+                    if (lane == 0)
+                        set_abort(p, sm);
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                float x[kBN];
+                {
+                    float a[32], b[32];
+                    tc::tmem_ld32(sb, a);
+                    tc::tmem_ld32(sb + 32, b);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 32; c++) {
+                        x[c] = a[c];
+                        x[c + 32] = b[c];
+                    }
+                }
+                const long long key0 = (long long)j * kBN;
+                float mt = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < kBN; c++) {
+                    x[c] = (key0 + c <= qlimit) ? x[c] * sc : -INFINITY;
+                    mt = fmaxf(mt, x[c]);
+                }
+                float m_new = m_run;
+                if (mt > m_run + kRescale || (m_run == -INFINITY && mt != -INFINITY))
+                    m_new = mt;
+                const float m_use = m_new == -INFINITY ? 0.f : m_new;
+                const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_use);
+                float sum = 0.f;
+                uint32_t w[32];
+#pragma unroll
+                for (int c = 0; c < kBN; c += 2) {
+                    const float e0 = exp2f(x[c] - m_use), e1 = exp2f(x[c + 1] - m_use);
+                    sum += e0 + e1;
+                    w[c >> 1] = pack_f16x2(e0, e1);
+                }
+                l = l * alpha + sum;
+                tc::tmem_st32(sb, w);
+                tc::tmem_wait_st();
+                const bool need = m_run != -INFINITY && m_new != m_run;
+                if (__any_sync(0xffffffffu, need)) {
+                    // O holds sums relative to m_run: rescale once PV_{j-1} has landed
+                    const unsigned pj = gj - 1;
+                    if (!warp_wait(smem_addr(&sm.pv_done[pj & 1]), (pj >> 1) & 1)) {
+                        if (lane == 0)
+                            set_abort(p, sm);
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const float f = need ? alpha : 1.0f;
+#pragma unroll 1
+                    for (int c = 0; c < kD; c += 32) {
+                        float o[32];
+                        tc::tmem_ld32(tbase + lane_base + kColO + c, o);
+                        tc::tmem_wait_ld();
+                        uint32_t ow[32];
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            ow[i] = __float_as_uint(o[i] * f);
+                        tc::tmem_st32(tbase + lane_base + kColO + c, ow);
+                    }
+                    tc::tmem_wait_st();
+                }
+                m_run = m_new;
+                tc::fence_before_sync();
+                mbar_arrive(smem_addr(&sm.p_full[gj & 1]));
+            }
+            if (!ok)
+                break;
+            // epilogue: O / l * sigmoid(gate)
+            const unsigned pl = g + it.nt - 1;
+            if (!warp_wait(smem_addr(&sm.pv_done[pl & 1]), (pl >> 1) & 1)) {
+                if (lane == 0)
+                    set_abort(p, sm);
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+            const long long gbase = tq * J.qg_tok_stride + (long long)it.head * J.qg_stride;
+            float *orow = J.out + (tq * 16 + it.head) * kD;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                float o[32];
+                tc::tmem_ld32(tbase + lane_base + kColO + c, o);
+                tc::tmem_wait_ld();
+                if (qvalid) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 r;
+                        r.x = o[i] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i, J.dtype))));
+                        r.y = o[i + 1] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 1, J.dtype))));
+                        r.z = o[i + 2] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 2, J.dtype))));
+                        r.w = o[i + 3] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 3, J.dtype))));
+                        *reinterpret_cast<float4 *>(orow + c + i) = r;
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            g += it.nt;
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0)
+        tc::tmem_dealloc(tbase, kTmemCols);
+}
+
+bool g_attn_attr = false;
+
+int validate(const KernelAttnPrefillJob &j, int i)
+{
+    if (!j.q || !j.gate || !j.k || !j.v || !j.q_norm || !j.k_norm || !j.k_cache || !j.v_cache || !j.out)
+        return fail("attn prefill: job %d has a null pointer", i);
+    if (j.T == 0 || j.T > (1ull << 22) * kBM)
+        return fail("attn prefill: job %d T=%zu out of range", i, j.T);
+    if (j.kbase + j.T > j.capacity)
+        return fail("attn prefill: job %d window overflow (kbase %zu + T %zu > capacity %zu)", i, j.kbase,
+                    j.T, j.capacity);
+    if (j.dtype != KERNEL_DTYPE_F32 && j.dtype != KERNEL_DTYPE_BF16)
+        return fail("attn prefill: job %d bad dtype %d", i, j.dtype);
+    if (!aligned16(j.k_cache) || !aligned16(j.v_cache) || !aligned16(j.out))
+        return fail("attn prefill: job %d cache/out not 16-byte aligned", i);
+    if (j.qg_stride < 256 || j.qg_tok_stride < 16 * j.qg_stride / 2)
+        return fail("attn prefill: job %d bad q/gate strides", i);
+    return 0;
+}
+
+int prefill_launch(const KernelAttnPrefillJob *jobs, int n)
+{
+    Runtime &R = rt();
+    long long total_t = 0;
+    for (int i = 0; i < n; i++) {
+        if (validate(jobs[i], i) != 0)
+            return -1;
+        total_t += (long long)jobs[i].T;
+    }
+    // items: (job, head, query tile), longest first onto the least-loaded CTA
+    std::vector<std::pair<long long, unsigned>> items;
+    for (int i = 0; i < n; i++) {
+        const long long T = (long long)jobs[i].T, kb = (long long)jobs[i].kbase;
+        const long long nq = (T + kBM - 1) / kBM;
+        for (long long qt = 0; qt < nq; qt++) {
+            const long long rows = std::min<long long>(kBM, T - qt * kBM);
+            const long long nt = (kb + qt * kBM + rows + kBN - 1) / kBN;
+            for (int h = 0; h < 16; h++)
+                items.emplace_back(nt + 2, ((unsigned)i << 26) | ((unsigned)h << 22) | (unsigned)qt);
+        }
+    }
+    std::stable_sort(items.begin(), items.end(),
+                     [](const std::pair<long long, unsigned> &a, const std::pair<long long, unsigned> &b) {
+                         return a.first > b.first;
+                     });
+    const int grid = (int)std::min<size_t>(items.size(), (size_t)R.num_sms);
+    std::vector<std::vector<unsigned>> per(grid);
+    {
+        std::priority_queue<std::pair<long long, int>, std::vector<std::pair<long long, int>>,
+                            std::greater<std::pair<long long, int>>> heap;
+        for (int c = 0; c < grid; c++)
+            heap.emplace(0ll, c);
+        for (const auto &it : items) {
+            auto top = heap.top();
+            heap.pop();
+            per[top.second].push_back(it.second);
+            heap.emplace(top.first + it.first, top.second);
+        }
+    }
+    std::vector<unsigned> sched;
+    std::vector<int> off(grid + 1, 0);
+    sched.reserve(items.size());
+    for (int c = 0; c < grid; c++) {
+        off[c] = (int)sched.size();
+        sched.insert(sched.end(), per[c].begin(), per[c].end());
+    }
+    off[grid] = (int)sched.size();
+    // scratch: prepared queries (f16), then the schedule
+    const size_t qp_bytes = (size_t)total_t * 16 * kD * sizeof(__half);
+    const size_t sched_off = (qp_bytes + 255) / 256 * 256;
+    const size_t off_off = sched_off + (sched.size() * 4 + 255) / 256 * 256;
+    unsigned char *ws = static_cast<unsigned char *>(scratch(off_off + off.size() * 4));
+    if (!ws)
+        return -1;
+    cudaStream_t st = R.stream;
+    if (check(cudaMemcpyAsync(ws + sched_off, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, st),
+              "prefill schedule") != 0 ||
+        check(cudaMemcpyAsync(ws + off_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, st),
+              "prefill schedule offsets") != 0)
+        return -1;
+
+    PrepParams pp;
+    memset(static_cast<void *>(&pp), 0, sizeof(pp));
+    PParams ap;
+    memset(static_cast<void *>(&ap), 0, sizeof(ap));
+    long long tok0 = 0;
+    __half *qp = reinterpret_cast<__half *>(ws);
+    for (int i = 0; i < n; i++) {
+        const KernelAttnPrefillJob &s = jobs[i];
+        PrepJob &d = pp.jobs[i];
+        d.q = s.q;
+        d.k = s.k;
+        d.v = s.v;
+        d.q_norm = s.q_norm;
+        d.k_norm = s.k_norm;
+        d.qp = qp + tok0 * 16 * kD;
+        d.k_cache = reinterpret_cast<__half *>(s.k_cache);
+        d.v_cache = reinterpret_cast<__half *>(s.v_cache);
+        d.qg_stride = (long long)s.qg_stride;
+        d.qg_tok_stride = (long long)s.qg_tok_stride;
+        d.kbase = (long long)s.kbase;
+        d.base = (long long)s.base;
+        d.tok0 = tok0;
+        d.dtype = s.dtype;
+        PJob &a = ap.jobs[i];
+        a.qp = d.qp;
+        a.gate = s.gate;
+        a.k_cache = d.k_cache;
+        a.v_cache = d.v_cache;
+        a.out = s.out;
+        a.qg_stride = d.qg_stride;
+        a.qg_tok_stride = d.qg_tok_stride;
+        a.kbase = d.kbase;
+        a.T = (long long)s.T;
+        a.dtype = s.dtype;
+        tok0 += (long long)s.T;
+    }
+    memcpy(pp.inv_freq, R.inv_freq, sizeof(pp.inv_freq));
+    pp.njobs = n;
+    prefill_prep_kernel<<<(unsigned)total_t, 256, 0, st>>>(pp);
+    if (launched("prefill_prep_kernel") != 0)
+        return -1;
+    ap.sched = reinterpret_cast<const unsigned *>(ws + sched_off);
+    ap.cta_off = reinterpret_cast<const int *>(ws + off_off);
+    ap.err = R.err_word;
+    ap.njobs = n;
+    if (!g_attn_attr) {
+        if (check(cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes), "prefill smem attribute") != 0)
+            return -1;
+        g_attn_attr = true;
+    }
+    prefill_attn_kernel<<<grid, kThreads, kSmemBytes, st>>>(ap);
+    return launched("prefill_attn_kernel");
+}
+
+}  // namespace
+
+int attn_prefill_batch(const KernelAttnPrefillJob *jobs, int n)
+{
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("attn prefill: bad job array");
+    for (int i = 0; i < n; i += kMaxJobs) {
+        if (prefill_launch(jobs + i, std::min(kMaxJobs, n - i)) != 0)
+            return -1;
+    }
+    return 0;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" int kernel_attn_prefill_batch(const KernelAttnPrefillJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    return attn_prefill_batch(jobs, n);
+}
+
+extern "C" int kernel_attn_prefill(const float *q_gate, const float *k, const float *v, const float *q_norm,
+                                   const float *k_norm, uint16_t *k_cache, uint16_t *v_cache, size_t capacity,
+                                   size_t kbase, size_t base, size_t T, float *out)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!q_gate || !k || !v || !q_norm || !k_norm || !out || T == 0)
+        return fail("kernel_attn_prefill: bad arguments");
+    // device staging: q_gate [T][8192], k, v [T][512], norms [2][256]; out [T][4096]
+    const size_t nqg = T * 8192, nkv = T * 512, nout = T * 4096;
+    const size_t in_f = nqg + 2 * nkv + 512;
+    float *d = static_cast<float *>(dstage((in_f + nout) * sizeof(float)));
+    if (!d)
+        return -1;
+    cudaStream_t st = rt().stream;
+    if (check(cudaMemcpyAsync(d, q_gate, nqg * 4, cudaMemcpyHostToDevice, st), "stage q") != 0 ||
+        check(cudaMemcpyAsync(d + nqg, k, nkv * 4, cudaMemcpyHostToDevice, st), "stage k") != 0 ||
+        check(cudaMemcpyAsync(d + nqg + nkv, v, nkv * 4, cudaMemcpyHostToDevice, st), "stage v") != 0 ||
+        check(cudaMemcpyAsync(d + nqg + 2 * nkv, q_norm, 256 * 4, cudaMemcpyHostToDevice, st), "stage qn") != 0 ||
+        check(cudaMemcpyAsync(d + nqg + 2 * nkv + 256, k_norm, 256 * 4, cudaMemcpyHostToDevice, st), "stage kn") != 0)
+        return -1;
+    KernelAttnPrefillJob j;
+    memset(&j, 0, sizeof(j));
+    j.q = d;
+    j.gate = d + 256;
+    j.qg_stride = 512;
+    j.qg_tok_stride = 8192;
+    j.k = d + nqg;
+    j.v = d + nqg + nkv;
+    j.q_norm = d + nqg + 2 * nkv;
+    j.k_norm = d + nqg + 2 * nkv + 256;
+    j.k_cache = k_cache;
+    j.v_cache = v_cache;
+    j.capacity = capacity;
+    j.kbase = kbase;
+    j.base = base;
+    j.T = T;
+    j.out = d + in_f;
+    j.dtype = KERNEL_DTYPE_F32;
+    if (attn_prefill_batch(&j, 1) != 0)
+        return -1;
+    if (check(cudaMemcpyAsync(out, d + in_f, nout * 4, cudaMemcpyDeviceToHost, st), "stage out") != 0)
+        return -1;
+    return kernel_cuda_synchronize();
+}
