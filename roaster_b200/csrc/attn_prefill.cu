@@ -32,8 +32,9 @@
 //   pv_done[k % 2]         O += P_k V_k finished (two barriers so no waiter is ever two phases
 //                          behind: a commit fires only after every earlier MMA, so when S_j is
 //                          complete every PV up to j-2 is too)
-// Producers publish a stage one cp.async group late (wait_group 1, then a generic->async proxy
-// fence, then arrive), so the tensor core reads data the copies have actually landed.
+// Producers signal each stage from the copy hardware as soon as its cp.async copies land
+// (cp.async.mbarrier.arrive.noinc); the MMA thread, after acquiring a stage, orders those
+// generic-proxy writes before the tensor core's async-proxy reads with fence.proxy.async.
 #include "ptx.cuh"
 #include "runtime.h"
 #include "tcgen05.cuh"
@@ -131,10 +132,44 @@ __device__ __forceinline__ Item decode_item(const PParams &p, unsigned e)
     return it;
 }
 
-__device__ __forceinline__ void cp_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_group0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2^x on the special-function unit (flush-to-zero: results below 2^-126 become 0, which only
+// drops probabilities that are negligible against the row maximum).
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 32 consecutive gate values of one row, through the read-only path (no aliasing with `out`).
+__device__ __forceinline__ void load_gate32(const void *base, long long idx, int dtype, float (&g)[32])
+{
+    if (dtype == KERNEL_DTYPE_BF16) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(base) + idx);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 u = __ldg(src + i);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                g[8 * i + 2 * k] = __uint_as_float(w[k] << 16);
+                g[8 * i + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+            }
+        }
+    } else {
+        const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + idx);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 v = __ldg(src + i);
+            g[4 * i] = v.x;
+            g[4 * i + 1] = v.y;
+            g[4 * i + 2] = v.z;
+            g[4 * i + 3] = v.w;
+        }
+    }
+}
 
 __device__ __forceinline__ float load_in(const void *base, long long idx, int dtype)
 {
@@ -284,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 const int sv = fv % kStages;
                 if (!wait(sm.kv_full[sv], (fv / kStages) & 1))
                     return;
+                fence_proxy_async();
                 tc::fence_after_sync();
                 const uint32_t vb = smem_addr(sm.kv[sv]);
 #pragma unroll
@@ -299,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 const Item it = decode_item(p, p.sched[idx]);
                 if (!wait(sm.q_full, nitem & 1))
                     break;
+                fence_proxy_async();
                 tc::fence_after_sync();
                 const unsigned fbase = fill;
                 for (int j = 0; j < it.nt && ok; j++) {
@@ -306,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                     const int sk = fk % kStages;
                     if (!wait(sm.kv_full[sk], (fk / kStages) & 1))
                         break;
+                    fence_proxy_async();
                     tc::fence_after_sync();
                     const uint32_t kb = smem_addr(sm.kv[sk]);
                     const unsigned gj = g + j;
@@ -337,16 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         const uint32_t lofs = (uint32_t)(lane >> 3);          // chunk of this lane's 8 dims
         const uint32_t lu = (uint32_t)(lane & 7);             // 16-byte unit within the chunk
         unsigned fill = 0, nitem = 0;
-        uint32_t pending = 0;                                 // barrier of the last unpublished group
         bool ok = true;
-        auto publish_prev = [&](uint32_t next_bar) {
-            cp_commit_group();
-            cp_wait_group1();
-            fence_proxy_async();
-            if (pending)
-                mbar_arrive(pending);
-            pending = next_bar;
-        };
         for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
             const Item it = decode_item(p, p.sched[idx]);
             const PJob &J = p.jobs[it.job];
@@ -361,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 const __half *src = J.qp + (tok * 16 + it.head) * kD + lane * 8;
                 cp_async16(sq + lofs * kChunkQ + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4), src);
             }
-            publish_prev(smem_addr(&sm.q_full));
+            cp_async_arrive(smem_addr(&sm.q_full));
             for (int j = 0; j < it.nt && ok; j++) {
                 for (int which = 0; which < 2; which++, fill++) {
                     const int s = fill % kStages;
@@ -381,14 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                         cp_async16(st + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4),
                                    cache + (key * 2 + it.kvh) * kD + lane * 8);
                     }
-                    publish_prev(smem_addr(&sm.kv_full[s]));
+                    cp_async_arrive(smem_addr(&sm.kv_full[s]));
                 }
             }
         }
-        cp_wait_group0();
-        fence_proxy_async();
-        if (pending && ok)
-            mbar_arrive(pending);
+        cp_async_wait_all();     // nothing of ours may still be landing when the CTA retires
     } else {
         // ---------------------------------------------------------------- softmax + epilogue
         const int row = tid - 128;                         // query row = TMEM lane
@@ -402,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
             const bool qvalid = row < it.rows;
             const long long tq = it.t0 + row;
             const long long qlimit = qvalid ? J.kbase + tq : -1;  // last key this row may see
+            const long long it_qmin = J.kbase + it.t0;            // smallest last key of the tile
             float m_run = -INFINITY, l = 0.f;
             for (int j = 0; j < it.nt; j++) {
                 const unsigned gj = g + j;
@@ -425,23 +452,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                         x[c + 32] = b[c];
                     }
                 }
+                // causal mask only where the tile reaches past some row's last key
                 const long long key0 = (long long)j * kBN;
-                float mt = -INFINITY;
+                if (key0 + kBN - 1 > it_qmin) {
+                    const int lim = (int)(qlimit - key0);           // keys [key0, key0 + lim] visible
 #pragma unroll
-                for (int c = 0; c < kBN; c++) {
-                    x[c] = (key0 + c <= qlimit) ? x[c] * sc : -INFINITY;
-                    mt = fmaxf(mt, x[c]);
+                    for (int c = 0; c < kBN; c++)
+                        x[c] = c <= lim ? x[c] : -INFINITY;
                 }
+                float mt = x[0];
+#pragma unroll
+                for (int c = 1; c < kBN; c++)
+                    mt = fmaxf(mt, x[c]);
+                mt *= sc;                                            // row max in log2 units
                 float m_new = m_run;
                 if (mt > m_run + kRescale || (m_run == -INFINITY && mt != -INFINITY))
                     m_new = mt;
                 const float m_use = m_new == -INFINITY ? 0.f : m_new;
-                const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_use);
+                const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_use);
                 float sum = 0.f;
                 uint32_t w[32];
 #pragma unroll
                 for (int c = 0; c < kBN; c += 2) {
-                    const float e0 = exp2f(x[c] - m_use), e1 = exp2f(x[c + 1] - m_use);
+                    const float e0 = ex2(fmaf(x[c], sc, -m_use)), e1 = ex2(fmaf(x[c + 1], sc, -m_use));
                     sum += e0 + e1;
                     w[c >> 1] = pack_f16x2(e0, e1);
                 }
@@ -489,10 +522,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
             }
             tc::fence_after_sync();
             const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-            const long long gbase = tq * J.qg_tok_stride + (long long)it.head * J.qg_stride;
+            const long long gbase = (qvalid ? tq : it.t0) * J.qg_tok_stride + (long long)it.head * J.qg_stride;
             float *orow = J.out + (tq * 16 + it.head) * kD;
+            float gv[32], gn[32];
+            load_gate32(J.gate, gbase, J.dtype, gn);
 #pragma unroll 1
             for (int c = 0; c < kD; c += 32) {
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    gv[i] = gn[i];
+                if (c + 32 < kD)
+                    load_gate32(J.gate, gbase + c + 32, J.dtype, gn);     // next chunk in flight
                 float o[32];
                 tc::tmem_ld32(tbase + lane_base + kColO + c, o);
                 tc::tmem_wait_ld();
@@ -500,10 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
                         float4 r;
-                        r.x = o[i] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i, J.dtype))));
-                        r.y = o[i + 1] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 1, J.dtype))));
-                        r.z = o[i + 2] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 2, J.dtype))));
-                        r.w = o[i + 3] * inv_l * (1.0f / (1.0f + expf(-load_in(J.gate, gbase + c + i + 3, J.dtype))));
+                        r.x = o[i] * inv_l / (1.0f + __expf(-gv[i]));
+                        r.y = o[i + 1] * inv_l / (1.0f + __expf(-gv[i + 1]));
+                        r.z = o[i + 2] * inv_l / (1.0f + __expf(-gv[i + 2]));
+                        r.w = o[i + 3] * inv_l / (1.0f + __expf(-gv[i + 3]));
                         *reinterpret_cast<float4 *>(orow + c + i) = r;
                     }
                 }
@@ -535,8 +575,11 @@ int validate(const KernelAttnPrefillJob &j, int i)
         return fail("attn prefill: job %d bad dtype %d", i, j.dtype);
     if (!aligned16(j.k_cache) || !aligned16(j.v_cache) || !aligned16(j.out))
         return fail("attn prefill: job %d cache/out not 16-byte aligned", i);
-    if (j.qg_stride < 256 || j.qg_tok_stride < 16 * j.qg_stride / 2)
-        return fail("attn prefill: job %d bad q/gate strides", i);
+    if (j.qg_stride < 256 || j.qg_tok_stride < 16 * j.qg_stride / 2 || (j.qg_stride & 7) ||
+        (j.qg_tok_stride & 7))
+        return fail("attn prefill: job %d bad q/gate strides (>= 256, multiples of 8)", i);
+    if (!aligned16(j.gate))
+        return fail("attn prefill: job %d gate not 16-byte aligned", i);
     return 0;
 }
 
