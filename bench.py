@@ -47,6 +47,11 @@ def args_parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context decode")
+    ap.add_argument("--long-steps", type=int, default=30)
+    ap.add_argument("--long-window", type=int, default=262144)
     ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
     ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
     ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
@@ -187,6 +192,169 @@ class ClockSampler:
         os.remove(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ prefill (config 3)
+
+PREFILL_PROMPTS = 8
+PREFILL_T = 8192
+
+
+def run_prefill(R, torch, dev, stream, steps: int, rank: int):
+    """Config 3 attention part: 8 prompts x 8192 tokens, bf16 Q/K/V/gate ~ N(0,1), causal gated
+    attention (prep + tcgen05 kernel) into empty windows. Device-timed per step (both kernels)."""
+    from roaster_b200 import synth
+    keep, jobs = [], []
+    for p in range(PREFILL_PROMPTS):
+        s0 = 100 * (rank + 1) + 4 * p
+        q = synth.device_normal(torch, (PREFILL_T, 16, 256), s0, dev, torch.bfloat16)
+        g = synth.device_normal(torch, (PREFILL_T, 16, 256), s0 + 1, dev, torch.bfloat16)
+        k = synth.device_normal(torch, (PREFILL_T, 2, 256), s0 + 2, dev, torch.bfloat16)
+        v = synth.device_normal(torch, (PREFILL_T, 2, 256), s0 + 3, dev, torch.bfloat16)
+        qn = 1 + 0.1 * synth.device_normal(torch, (256,), s0 + 5, dev, torch.float32)
+        kn = 1 + 0.1 * synth.device_normal(torch, (256,), s0 + 6, dev, torch.float32)
+        kc = torch.zeros(PREFILL_T, 2, 256, dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        out = torch.empty(PREFILL_T, 16, 256, device=dev)
+        keep.append((q, g, k, v, qn, kn, kc, vc, out))
+        jobs.append(R.KernelAttnPrefillJob(q.data_ptr(), g.data_ptr(), 256, 4096, k.data_ptr(),
+                                           v.data_ptr(), qn.data_ptr(), kn.data_ptr(), kc.data_ptr(),
+                                           vc.data_ptr(), PREFILL_T, 0, 0, PREFILL_T, out.data_ptr(),
+                                           1))
+    arr = (R.KernelAttnPrefillJob * len(jobs))(*jobs)
+    lib = R.lib()
+    for _ in range(2):
+        if lib.kernel_attn_prefill_batch(arr, len(jobs)) != 0:
+            raise RuntimeError(R.last_error())
+    R.synchronize()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = R.launch_count()
+    e0.record(stream)
+    for _ in range(steps):
+        lib.kernel_attn_prefill_batch(arr, len(jobs))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    R.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    launches = R.launch_count() - n0
+    del keep
+    return ms, launches
+
+
+# ------------------------------------------------------------------------------ long context (config 4)
+
+LONG_SLOTS = 16
+
+
+def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window: int, steps: int,
+                     warmup: int = 3):
+    """Config 4: 16 slots x `window` f16 KV positions, each window split into contiguous slices
+    across the ranks (no data exchange except one all-gather of 8.3 KB softmax partials per slot
+    and kv head per step); the rank holding the newest slice appends. Plus 3 DeltaNet layers per
+    slot on the slot's home rank (slot % world). Strong scaling: the job is fixed, ranks split it."""
+    from roaster_b200 import splitkv, synth
+    lo, hi = splitkv.slice_bounds(window, world, rank)
+    app = splitkv.appends(world, rank)
+    local = hi - lo
+    cap = local + (steps + warmup + 8 if app else 0)
+    kpool = synth.device_normal(torch, (LONG_SLOTS * cap, 2, 256), 500 + rank, dev, torch.float16)
+    vpool = synth.device_normal(torch, (LONG_SLOTS * cap, 2, 256), 600 + rank, dev, torch.float16)
+    g = torch.Generator(device=dev)
+    g.manual_seed(700)                           # identical q / gate / new token on every rank
+    q = torch.randn(LONG_SLOTS, 16, 256, generator=g, device=dev)
+    gate = torch.randn(LONG_SLOTS, 16, 256, generator=g, device=dev)
+    kn = torch.randn(LONG_SLOTS, 2, 256, generator=g, device=dev)
+    vn = torch.randn(LONG_SLOTS, 2, 256, generator=g, device=dev)
+    qn = 1 + 0.1 * torch.randn(256, generator=g, device=dev)
+    kw = 1 + 0.1 * torch.randn(256, generator=g, device=dev)
+    out = torch.empty(LONG_SLOTS, 16, 256, device=dev)
+    home = [s for s in range(LONG_SLOTS) if s % world == rank]
+    states = synth.device_normal(torch, (max(1, len(home)), DN_LAYERS, 32, 128, 128), 800 + rank, dev,
+                                 torch.float32, std=0.02)
+    dq = torch.nn.functional.normalize(torch.randn(max(1, len(home)), DN_LAYERS, 16, 128, device=dev), dim=-1)
+    dk = torch.nn.functional.normalize(torch.randn(max(1, len(home)), DN_LAYERS, 16, 128, device=dev), dim=-1)
+    dv = torch.randn(max(1, len(home)), DN_LAYERS, 32, 128, device=dev)
+    db = torch.sigmoid(torch.randn(max(1, len(home)), DN_LAYERS, 32, device=dev))
+    dg = -torch.rand(max(1, len(home)), DN_LAYERS, 32, device=dev)
+    dout = torch.empty(max(1, len(home)), DN_LAYERS, 32, 128, device=dev)
+    es = kpool.element_size()
+    jobs = [R.attn_job(q[s], gate[s], kn[s], vn[s], qn, kw,
+                       kpool.data_ptr() + s * cap * 512 * es, vpool.data_ptr() + s * cap * 512 * es,
+                       local, window, out[s], append=app, capacity=cap) for s in range(LONG_SLOTS)]
+    arr = (R.KernelAttnDecodeJob * LONG_SLOTS)(*jobs)
+    dj = [R.delta_job(states[i, l], dq[i, l], dk[i, l], dv[i, l], dg[i, l], db[i, l], dout[i, l])
+          for i in range(len(home)) for l in range(DN_LAYERS)]
+    darr = (R.KernelDeltaStepJob * max(1, len(dj)))(*dj) if dj else None
+    part = torch.empty(LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
+    gathered = torch.empty(world, LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
+    lib = R.lib()
+    import ctypes as C
+    gates_p = (C.c_void_p * LONG_SLOTS)(*[gate[s].data_ptr() for s in range(LONG_SLOTS)])
+    outs_p = (C.c_void_p * LONG_SLOTS)(*[out[s].data_ptr() for s in range(LONG_SLOTS)])
+    pos = [window]
+
+    def one():
+        for s in range(LONG_SLOTS):
+            arr[s].position = pos[0]
+        if world == 1:
+            rc = lib.kernel_attn_decode_batch(arr, LONG_SLOTS)
+        else:
+            def partial_fn():
+                if lib.kernel_attn_decode_partial_batch(arr, LONG_SLOTS, C.c_void_p(part.data_ptr())) != 0:
+                    raise RuntimeError(R.last_error())
+                return part
+
+            def gather_fn(local_part):
+                dist.all_gather_into_tensor(gathered, local_part)
+                return gathered
+
+            def merge_fn(gt, w):
+                if lib.kernel_attn_merge_partials(C.c_void_p(gt.data_ptr()), w, LONG_SLOTS, gates_p, 256,
+                                                  outs_p) != 0:
+                    raise RuntimeError(R.last_error())
+
+            splitkv.step(world, partial_fn, gather_fn, merge_fn)
+            rc = 0
+        if darr is not None:
+            rc |= lib.kernel_deltanet_step_batch(darr, len(dj))
+        if rc != 0:
+            raise RuntimeError(R.last_error())
+        if app:
+            for s in range(LONG_SLOTS):
+                arr[s].length += 1
+        pos[0] += 1
+
+    for _ in range(warmup):
+        one()
+    R.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = R.launch_count()
+    e0.record(stream)
+    for _ in range(steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    R.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    launches = R.launch_count() - n0
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    kv_bytes = LONG_SLOTS * local * 2048
+    dn_bytes = len(home) * DN_LAYERS * (2 * 32 * 128 * 128 * 4)
+    del kpool, vpool
+    return {"metric": "long-context decode tok/s (config 4: 16 slots x 262144 f16 KV + 3 DeltaNet layers)",
+            "value": round(LONG_SLOTS / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
+            "steps": steps, "scaling": "strong", "window": window,
+            "kv_split": f"{world} contiguous slices per slot; NCCL all-gather of softmax partials",
+            "kv_bytes_per_gpu_per_step": kv_bytes + dn_bytes,
+            "achieved_GBps_per_gpu": round((kv_bytes + dn_bytes) / (ms / 1e3) / 1e9, 1),
+            "gpu_launches": int(launches)}
 
 
 # ------------------------------------------------------------------------------ GPU arm
@@ -373,6 +541,32 @@ def run_ours(a):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": KE,
                "api": "kernel_attn_decode_batch_host + kernel_deltanet_step_batch_host"}
 
+    prefill = None
+    if not a.no_prefill:
+        pms, pl = run_prefill(R, torch, dev, stream, a.prefill_steps, rank)
+        tp = torch.tensor([pms], device=dev)
+        if world > 1:
+            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+        pms = float(tp.item())
+        _, tflops, src = peaks()
+        flop = 2.0 * PREFILL_T * PREFILL_T * 256 * 16 * PREFILL_PROMPTS     # causal QK^T + PV
+        achieved = flop / (pms / 1e3) / 1e12
+        prefill = {"metric": "prefill tok/s (config 3 attention: 8 prompts x 8192, bf16 in, causal)",
+                   "value": round(PREFILL_PROMPTS * PREFILL_T * world / (pms / 1e3), 1),
+                   "unit": "tok/s", "ms_per_step": round(pms, 4), "steps": a.prefill_steps,
+                   "gpu_launches": int(pl),
+                   "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel (+ prefill_prep_kernel)",
+                                "achieved": round(achieved, 1), "peak": tflops, "unit": "TFLOP/s",
+                                "frac": round(achieved / tflops, 4),
+                                "peak_source": f"{src} bf16_tflops (burst; f16 operands run at the same rate)",
+                                "algorithmic_flop_per_step": flop},
+                   "not_included": "chunked DeltaNet prefill (not built yet)"}
+
+    long_ctx = None
+    if not a.no_long:
+        long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window,
+                                    a.long_steps)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
@@ -411,6 +605,7 @@ def run_ours(a):
                 "deltanet_step_kernel": {"ms": round(dn_avg, 4), "GB/s": round(dn_gbs, 1),
                                          "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
+            "prefill": prefill, "long_context": long_ctx,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -49,6 +49,10 @@
 #include <queue>
 #include <vector>
 
+#ifndef PREFILL_EXTRA_PROD
+#define PREFILL_EXTRA_PROD 0
+#endif
+
 namespace rb {
 namespace {
 
@@ -60,9 +64,9 @@ constexpr int kChunkQ = kBM * 128;           // one 64-dim chunk of the Q tile (
 constexpr int kQBytes = 4 * kChunkQ;         // 64 KB
 constexpr int kChunkKV = kBN * 128;          // 8 KB
 constexpr int kKVBytes = 4 * kChunkKV;       // 32 KB
-constexpr int kProdWarps = 3;
+constexpr int kProdWarps = 3 + PREFILL_EXTRA_PROD;      // warps 1-3 and 8.. (after the softmax warpgroup)
 constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kThreads = 256;
+constexpr int kThreads = 256 + 32 * PREFILL_EXTRA_PROD;
 constexpr int kMaxJobs = 64;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
@@ -369,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
             tc::commit(smem_addr(&sm.drain));
             mbar_wait(smem_addr(&sm.drain), 0);
         }
-    } else if (warp <= kProdWarps) {
+    } else if (warp <= 3 || warp >= 8) {
         // ---------------------------------------------------------------- producers
-        const int pw = warp - 1;
+        const int pw = warp <= 3 ? warp - 1 : warp - 5;
         const uint32_t lofs = (uint32_t)(lane >> 3);          // chunk of this lane's 8 dims
         const uint32_t lu = (uint32_t)(lane & 7);             // 16-byte unit within the chunk
         unsigned fill = 0, nitem = 0;

@@ -1,0 +1,97 @@
+"""Split-KV long-context decode host logic over a 2-rank gloo process group (CPU).
+
+Each rank holds one contiguous slice of the window (roaster_b200.splitkv.slice_bounds); the rank
+with the newest slice appends the new token. Partials come from the CPU oracle (stand-in for
+kernel_attn_decode_partial_batch), are all-gathered over gloo and merged with the same formula as
+kernel_attn_merge_partials; the result must equal one decode over the whole window."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+LOG2E = 1.4426950408889634
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, L, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    from roaster_b200 import splitkv, synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    d = synth.attn_decode_inputs(seed=21, length=L)
+    _, k_app, v_app = O.attn_decode(d["q"], d["gate"], d["k_new"], d["v_new"], d["q_norm"],
+                                    d["k_norm"], d["k_cache"], d["v_cache"], L, L)
+    lo, hi = splitkv.slice_bounds(L, world, rank)
+    kc = d["k_cache"][lo:hi]
+    vc = d["v_cache"][lo:hi]
+    if splitkv.appends(world, rank):                 # the newest slice takes the new token
+        kc = np.concatenate([kc, k_app[None].astype(np.float16)])
+        vc = np.concatenate([vc, v_app[None].astype(np.float16)])
+
+    def partial_fn():
+        m, l, o = O.attn_decode_partial(d["q"], d["q_norm"], kc, vc, 0, len(kc), L)
+        rec = np.zeros((1, 2, splitkv.PARTIAL_FLOATS), np.float32)
+        for kvh in range(2):
+            hs = slice(8 * kvh, 8 * kvh + 8)
+            rec[0, kvh, :8] = m[hs] * LOG2E
+            rec[0, kvh, 8:16] = l[hs]
+            rec[0, kvh, 16:] = o[hs].reshape(-1)
+        return rec
+
+    def gather_fn(local):
+        t = torch.from_numpy(local)
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return np.stack([x.numpy() for x in out])
+
+    def merge_fn(g, w):
+        return splitkv.merge_reference(g, d["gate"][None])
+
+    out = splitkv.step(world, partial_fn, gather_fn, merge_fn)
+    np.save(os.path.join(outdir, f"out{rank}.npy"), out)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("L", [1000, 4099])
+def test_two_rank_split_decode_equals_single_window(tmp_path, L):
+    import oracle as O
+    from roaster_b200 import synth
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, L, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    d = synth.attn_decode_inputs(seed=21, length=L)
+    ref, _, _ = O.attn_decode(d["q"], d["gate"], d["k_new"], d["v_new"], d["q_norm"], d["k_norm"],
+                              d["k_cache"], d["v_cache"], L, L)
+    for r in range(2):
+        got = np.load(tmp_path / f"out{r}.npy")[0]
+        assert O.maxrel(got, ref) < 2e-3, O.maxrel(got, ref)
+
+
+def test_slice_bounds_cover_window():
+    from roaster_b200 import splitkv
+    for L in (1, 7, 262144, 262147):
+        for world in (1, 2, 4, 8):
+            spans = [splitkv.slice_bounds(L, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == L
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert sum(splitkv.appends(world, r) for r in range(world)) == 1
