@@ -360,6 +360,8 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
 # ------------------------------------------------------------------------------ GPU arm
 
 def run_ours(a):
+    # NCCL prints its banner to stdout; keep stdout for the one JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     import numpy as np
     import torch
     import torch.distributed as dist

@@ -67,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
 // ---------------------------------------------------------------- bulk async copy (TMA engine)
 
 // Global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte aligned); completion
-// is signalled as transaction bytes on `bar`. No multicast.
+// is signalled as transaction bytes on `bar`. Plain single-CTA form.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
 {
     asm volatile(
