@@ -207,6 +207,30 @@ int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, int n);
 int kernel_deltanet_step(float *state, const float *q, const float *k, const float *v,
                          const float *g, const float *beta, float *out);
 
+/* ------------------------------------------------------------ Gated DeltaNet prefill
+ * Replaces the per-token delta_head loop of pf_ssm (reference src/model.c:1644-1658; the
+ * recurrence of delta_head, model.c:1507-1534) with the chunked form (chunk 64) on the tensor
+ * cores. Same layouts as that loop: q, k [T][16][128] (L2-normalised by the caller, value head
+ * vh reads key head vh % 16), v [T][32][128], g (log-decay) and beta [T][32], out
+ * [T][32][128] = S_t^T q_t / sqrt(128) per token, before the gated RMSNorm. The state
+ * [32][128 key][128 value] is read at the start and holds S_T on return. */
+typedef struct {
+    float *state;               /* device, [32][128][128] fp32, updated in place */
+    const float *q, *k;         /* device, [T][16][128], 16-byte aligned */
+    const float *v;             /* device, [T][32][128], 16-byte aligned */
+    const float *g, *beta;      /* device, [T][32] */
+    float *out;                 /* device, [T][32][128] */
+    size_t T;                   /* tokens (0 = nothing to do) */
+} KernelDeltaPrefillJob;
+
+/* Device-pointer batch: one job per prompt (independent states). Asynchronous. */
+int kernel_deltanet_prefill_batch(const KernelDeltaPrefillJob *jobs, int n);
+
+/* Drop-in for one pf_ssm recurrence: host q/k/v/g/beta/out, device-resident state.
+ * Synchronous. */
+int kernel_deltanet_prefill(float *state, size_t T, const float *q, const float *k, const float *v,
+                            const float *g, const float *beta, float *out);
+
 #ifdef __cplusplus
 }
 #endif

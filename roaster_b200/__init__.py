@@ -55,6 +55,12 @@ class KernelDeltaStepJob(C.Structure):
                 ("out", _vp)]
 
 
+class KernelDeltaPrefillJob(C.Structure):
+    """Mirror of ``KernelDeltaPrefillJob`` (include/roaster_cuda.h)."""
+    _fields_ = [("state", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp),
+                ("out", _vp), ("T", _sz)]
+
+
 _lib = None
 
 
@@ -93,6 +99,8 @@ def lib():
         "kernel_deltanet_step_batch": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_step": (C.c_int, [_vp] * 7),
         "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
+        "kernel_deltanet_prefill_batch": (C.c_int, [C.POINTER(KernelDeltaPrefillJob), C.c_int]),
+        "kernel_deltanet_prefill": (C.c_int, [_vp, _sz] + [_vp] * 6),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -158,6 +166,11 @@ def delta_job(state, q, k, v, g, beta, out):
                               _ptr(out))
 
 
+def delta_prefill_job(state, q, k, v, g, beta, out, T: int):
+    return KernelDeltaPrefillJob(_ptr(state), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                 _ptr(out), int(T))
+
+
 def _arr(struct, jobs):
     arr = (struct * len(jobs))(*jobs)
     return arr, len(jobs)
@@ -208,3 +221,8 @@ def deltanet_step_batch_host(jobs) -> None:
 def deltanet_step_batch(jobs) -> None:
     arr, n = _arr(KernelDeltaStepJob, jobs)
     check(lib().kernel_deltanet_step_batch(arr, n), "kernel_deltanet_step_batch")
+
+
+def deltanet_prefill_batch(jobs) -> None:
+    arr, n = _arr(KernelDeltaPrefillJob, jobs)
+    check(lib().kernel_deltanet_prefill_batch(arr, n), "kernel_deltanet_prefill_batch")

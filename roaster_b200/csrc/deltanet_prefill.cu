@@ -1,0 +1,827 @@
+// Gated DeltaNet prefill on sm_100a tensor cores: the chunked (WY) form of the delta rule.
+//
+// Replaces the per-token loop of pf_ssm (reference src/model.c:1644-1658, which calls
+// delta_head, model.c:1507-1534, once per token and value head). Per value head vh (key head
+// vh % 16) and token t, with d_t = exp(g_t):
+//     delta_t = beta_t (v_t - d_t S_{t-1}^T k_t),  S_t = d_t S_{t-1} + k_t delta_t^T,
+//     o_t = S_t^T q_t / sqrt(128).
+// Over a chunk of C = 64 tokens starting from state S_0, with G_i = sum_{l<=i} g_l and
+// gamma_i = exp(G_i) (row i = token i of the chunk):
+//     L_ij  = beta_i exp(G_i - G_j) k_i.k_j        (j < i)      T = (I + L)^-1
+//     M_ij  = exp(G_i - G_j) q_i.k_j               (j <= i)
+//     U = T diag(beta) V,  W = T diag(beta gamma) K,  Delta = U - W S_0
+//     O = (diag(gamma) Q S_0 + M Delta) / sqrt(128)
+//     S_C = gamma_C S_0 + K^T diag(exp(G_C - G_j)) Delta
+// which is the same recurrence regrouped (no approximation).
+//
+// One CTA per (prompt, value head) walks the prompt's chunks in order. Everything is computed
+// transposed, so that each product lands in tensor memory with one value (or key) dimension
+// per TMEM lane and one thread owns each lane:
+//   (a) [K;Q] K^T            128 x 64, K = 128 keys
+//   (b) U^T = V^T (T b)^T,  W^T = K^T (T bg)^T       128 x 64 each, K = 64 tokens
+//   (c) S_0^T W^T,  (d1) S_0^T Q^T                    128 x 64, A = S_0^T from TMEM
+//   (d2) Delta^T M^T                                  128 x 64
+//   (e) Delta''^T K                                   128 x 128 (state update)
+// The fp32 state S^T stays in TMEM for the whole prompt (128 columns). T = (I + L)^-1 is formed
+// on the CUDA cores (16 x 16 diagonal blocks by substitution, then three levels of block
+// products).
+//
+// Precision: every operand is split into two f16 parts, x = hi + lo, and each product is
+// hi*hi + hi*lo + lo*hi with fp32 accumulation -- about 22 significant bits, which keeps the
+// state within 1e-6 of the sequential fp32 recurrence. Before a split each operand row is scaled
+// by a power of two so its largest magnitude is in [1, 2) (exact, and undone on the result):
+// a scale along a product's M or N dimension factors out of the result; scales along the
+// contraction dimension (the token rows of K and V) are folded into the other operand.
+//
+// Roles (384 threads): warps 0-3 own TMEM lanes 0-127 and do the chunk arithmetic; thread 0
+// also issues every tcgen05.mma. Warps 4-11 load the next chunk's q/k/v rows into registers
+// while the current chunk runs, then scale, split and store them once the chunk's last MMA
+// has committed.
+#include "ptx.cuh"
+#include "runtime.h"
+#include "tcgen05.cuh"
+#include "../../include/roaster_cuda.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstring>
+#include <vector>
+
+namespace rb {
+namespace {
+
+constexpr int kC = 64;                 // chunk length (tokens)
+constexpr int kD = 128;                // head dim
+constexpr int kThreads = 384;
+constexpr int kProdThreads = 256;
+constexpr int kMaxJobs = 64;
+constexpr uint32_t kTmemCols = 512;
+constexpr double kLog2eD = 1.4426950408889634;
+constexpr float kOutScale = 0.08838834764831845f;   // 1 / sqrt(128)
+
+// TMEM columns
+constexpr uint32_t kColS = 0;          // master state S^T (fp32)
+constexpr uint32_t kColS0 = 128;       // S_0^T split: hi [128,192), lo [192,256); also (e)'s result
+constexpr uint32_t kColA = 256;        // (a), later (c)
+constexpr uint32_t kColU = 320;        // U^T, later (d2)
+constexpr uint32_t kColW = 384;        // W^T
+constexpr uint32_t kColD1 = 448;       // (d1)
+
+// Shared-memory regions (byte offsets from a 1024-aligned base). Tiles are 128-byte-swizzled
+// [rows][128 B] blocks; a "half" is 8 KB (64 rows) or 16 KB (128 rows).
+constexpr uint32_t kOffKQH = 0;        // [K c0 | Q c0 | K c1 | Q c1] hi, 4 x 8 KB
+constexpr uint32_t kOffKQL = 32768;    // same, lo
+constexpr uint32_t kOffV = 65536;      // V hi [c0|c1] 16 KB, V lo 16 KB;  later Delta''^T hi|lo
+constexpr uint32_t kOffB = 98304;      // BV hi, BV lo, BK hi, BK lo (8 KB each); L + X scratch;
+                                       // later Delta^T hi|lo
+constexpr uint32_t kOffW = 131072;     // T (fp32 scratch), later W' hi|lo
+constexpr uint32_t kOffM = 163840;     // M hi, M lo (8 KB each)
+constexpr uint32_t kOffConst = 180224; // ChunkConst[2]
+constexpr int kLd = 65;                // fp32 scratch row stride (floats)
+
+struct ChunkConst {
+    double gl[kC];                     // prefix sums of g * log2(e)
+    float gam[kC];                     // exp(G_j)
+    float beta[kC];
+    float isk[kC], isq[kC], isv[kC];   // inverse row scales of K, Q, V
+    float df[kC];                      // exp(G_C - G_j) / s^k_j
+    float gC;                          // exp(G_C)
+    float pad[15];
+};
+static_assert(sizeof(ChunkConst) % 16 == 0, "");
+constexpr uint32_t kOffCons = kOffConst + 2 * sizeof(ChunkConst);   // consumer scratch
+struct ConsScratch {
+    float iu_v[kC], iu_k[kC], imu[kC];
+    float red[4];
+};
+constexpr uint32_t kOffBars = kOffCons + ((sizeof(ConsScratch) + 15) / 16) * 16;
+constexpr size_t kSmemBytes = kOffBars + 64 + 1024;
+
+struct DJob {
+    float *state;
+    const float *q, *k, *v, *g, *beta;
+    float *out;
+    long long T;
+};
+
+struct DPParams {
+    DJob jobs[kMaxJobs];
+    unsigned *err;
+};
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// AND of `ok` over the `n` threads of named barrier `id` (also a barrier).
+__device__ __forceinline__ bool bar_all(int id, int n, bool ok)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
+// Power of two s with amax * s in [1, 2) (1 for zero or non-finite amax).
+__device__ __forceinline__ float pow2_scale(float amax)
+{
+    const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 127;
+    if (!(amax > 0.f) || e == 128)
+        return 1.f;
+    const int ec = e < -100 ? -100 : (e > 100 ? 100 : e);
+    return __uint_as_float((uint32_t)(127 - ec) << 23);
+}
+
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hw, uint32_t &lw)
+{
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    hw = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+    lw = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+__device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y)
+{
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+
+// Row r (64 values, times s) of a K-major swizzled tile pair (hi, lo): 8 x 16-byte units.
+__device__ __forceinline__ void store_row_split(uint32_t hi, uint32_t lo, int r, const float (&x)[kC], float s)
+{
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+            split2(x[8 * u + 2 * p] * s, x[8 * u + 2 * p + 1] * s, h[p], l[p]);
+        const uint32_t off = (uint32_t)r * 128u + (((uint32_t)u ^ (uint32_t)(r & 7)) << 4);
+        sts128(hi + off, h[0], h[1], h[2], h[3]);
+        sts128(lo + off, l[0], l[1], l[2], l[3]);
+    }
+}
+
+__device__ __forceinline__ float row_amax(const float (&x)[kC])
+{
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kC; i++)
+        m = fmaxf(m, fabsf(x[i]));
+    return m;
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[kC])
+{
+    float a[32], b[32];
+    tc::tmem_ld32(taddr, a);
+    tc::tmem_ld32(taddr + 32, b);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        x[i] = a[i];
+        x[i + 32] = b[i];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __grid_constant__ DPParams p)
+{
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    unsigned char *gbase = smem_raw + (base - smem_addr(smem_raw));
+    ChunkConst *cc = reinterpret_cast<ChunkConst *>(gbase + kOffConst);
+    ConsScratch *cs = reinterpret_cast<ConsScratch *>(gbase + kOffCons);
+    unsigned long long *bars = reinterpret_cast<unsigned long long *>(gbase + kOffBars);
+    const uint32_t in_full = smem_addr(&bars[0]), mma_bar = smem_addr(&bars[1]);
+    const uint32_t done_bar = smem_addr(&bars[2]), drain_bar = smem_addr(&bars[3]);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[4]);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(&bars[5]);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int vh = blockIdx.x, kh = vh & 15;
+    const DJob &J = p.jobs[blockIdx.y];
+    const long long T = J.T;
+    const int nchunks = (int)((T + kC - 1) / kC);
+
+    if (tid == 0) {
+        mbar_init(in_full, kProdThreads);
+        mbar_init(mma_bar, 1);
+        mbar_init(done_bar, 1);
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tb = *tmem_slot;
+
+    auto set_abort = [&]() {
+        atomicOr(p.err, kErrWaitTimeout);
+        *abort_flag = 1;
+    };
+
+    if (warp >= 4) {
+        // ============================================================ producers
+        const int pw = warp - 4;                       // 0..7, rows pw + 8 s
+        float4 buf[24];
+        float gv0 = 0.f, gv1 = 0.f, bv0 = 0.f, bv1 = 0.f;
+        auto issue_loads = [&](int n) {
+            const long long t0 = (long long)n * kC;
+            const int tc_ = (int)(T - t0 < kC ? T - t0 : kC);
+#pragma unroll
+            for (int s = 0; s < 24; s++) {
+                const int rr = pw + 8 * s, which = rr >> 6, j = rr & 63;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j < tc_) {
+                    const long long t = t0 + j;
+                    const float *src = which == 0 ? J.k + (t * 16 + kh) * kD
+                                     : which == 1 ? J.q + (t * 16 + kh) * kD
+                                                  : J.v + (t * 32 + vh) * kD;
+                    x = __ldg(reinterpret_cast<const float4 *>(src) + lane);
+                }
+                buf[s] = x;
+            }
+            if (pw == 0) {
+                gv0 = gv1 = bv0 = bv1 = 0.f;
+                if (lane < tc_) {
+                    gv0 = __ldg(J.g + (t0 + lane) * 32 + vh);
+                    bv0 = __ldg(J.beta + (t0 + lane) * 32 + vh);
+                }
+                if (lane + 32 < tc_) {
+                    gv1 = __ldg(J.g + (t0 + lane + 32) * 32 + vh);
+                    bv1 = __ldg(J.beta + (t0 + lane + 32) * 32 + vh);
+                }
+            }
+        };
+        issue_loads(0);
+        for (int n = 0; n < nchunks; n++) {
+            bool ok = true;
+            if (n > 0)
+                ok = mbar_wait(done_bar, (uint32_t)(n - 1) & 1u);
+            if (!bar_all(3, kProdThreads, ok && !*abort_flag)) {
+                if (tid == kThreads - kProdThreads)
+                    set_abort();
+                break;
+            }
+            ChunkConst &C = cc[n & 1];
+            // scale, split and store this chunk's rows
+#pragma unroll
+            for (int s = 0; s < 24; s++) {
+                const int rr = pw + 8 * s, which = rr >> 6, j = rr & 63;
+                const float4 x = buf[s];
+                float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float sc = pow2_scale(m);
+                uint32_t h0, l0, h1, l1;
+                split2(x.x * sc, x.y * sc, h0, l0);
+                split2(x.z * sc, x.w * sc, h1, l1);
+                const uint32_t c = (uint32_t)lane >> 4;                    // 64-column chunk
+                const uint32_t unit = ((uint32_t)(lane & 15) >> 1) ^ (uint32_t)(j & 7);
+                const uint32_t inner = (uint32_t)j * 128u + (unit << 4) + (uint32_t)(lane & 1) * 8u;
+                uint32_t hi, lo;
+                if (which == 2) {
+                    hi = base + kOffV + c * 8192u;
+                    lo = hi + 16384u;
+                } else {
+                    hi = base + kOffKQH + c * 16384u + (uint32_t)which * 8192u;
+                    lo = hi + (kOffKQL - kOffKQH);
+                }
+                sts64(hi + inner, h0, h1);
+                sts64(lo + inner, l0, l1);
+                if (lane == 0) {
+                    const float inv = 1.0f / sc;
+                    if (which == 0) C.isk[j] = inv;
+                    else if (which == 1) C.isq[j] = inv;
+                    else C.isv[j] = inv;
+                }
+            }
+            if (pw == 0) {
+                // prefix sums of g * log2(e) in double
+                double a = (double)gv0 * kLog2eD, b = (double)gv1 * kLog2eD;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double ua = __shfl_up_sync(0xffffffffu, a, o);
+                    const double ub = __shfl_up_sync(0xffffffffu, b, o);
+                    if (lane >= o) {
+                        a += ua;
+                        b += ub;
+                    }
+                }
+                b += __shfl_sync(0xffffffffu, a, 31);
+                C.gl[lane] = a;
+                C.gl[lane + 32] = b;
+                C.gam[lane] = ex2((float)a);
+                C.gam[lane + 32] = ex2((float)b);
+                C.beta[lane] = bv0;
+                C.beta[lane + 32] = bv1;
+            }
+            named_bar_sync(3, kProdThreads);
+            if (pw == 0) {
+                const double gl_last = C.gl[kC - 1];
+                C.df[lane] = ex2((float)(gl_last - C.gl[lane])) * C.isk[lane];
+                C.df[lane + 32] = ex2((float)(gl_last - C.gl[lane + 32])) * C.isk[lane + 32];
+                if (lane == 0)
+                    C.gC = ex2((float)gl_last);
+            }
+            fence_proxy_async();
+            mbar_arrive(in_full);
+            if (n + 1 < nchunks)
+                issue_loads(n + 1);
+        }
+    } else {
+        // ============================================================ chunk arithmetic
+        const int r = tid;                                  // TMEM lane: value (or key) index
+        const uint32_t lrow = (uint32_t)(32 * warp) << 16;  // lane offset of this warp
+        const float *Lm = reinterpret_cast<const float *>(gbase + kOffB);
+        float *Lw = reinterpret_cast<float *>(gbase + kOffB);
+        float *Xs = reinterpret_cast<float *>(gbase + kOffB) + kC * kLd;
+        float *Tm = reinterpret_cast<float *>(gbase + kOffW);
+        float inv_sigma = 1.f, inv_rho = 1.f, inv_rho2 = 1.f, inv_omega = 1.f;
+        uint32_t mphase = 0;
+        bool ok = true;
+
+        auto wait_mma = [&]() -> bool {
+            const bool w = mbar_wait(mma_bar, mphase & 1u);
+            mphase++;
+            const bool all = bar_all(1, 128, w && !*abort_flag);
+            if (!all && tid == 0)
+                set_abort();
+            if (all)
+                tc::fence_after_sync();
+            return all;
+        };
+
+        // S_0^T split into TMEM columns [128, 256) from the master, with row scale sigma.
+        auto write_s0 = [&]() {
+            float amax = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                float x[32];
+                tc::tmem_ld32(tb + lrow + kColS + c, x);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    amax = fmaxf(amax, fabsf(x[i]));
+            }
+            const float sg = pow2_scale(amax);
+            inv_sigma = 1.0f / sg;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                float x[32];
+                tc::tmem_ld32(tb + lrow + kColS + c, x);
+                tc::tmem_wait_ld();
+                uint32_t h[16], l[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    split2(x[2 * i] * sg, x[2 * i + 1] * sg, h[i], l[i]);
+                tc::tmem_st16(tb + lrow + kColS0 + (c >> 1), h);
+                tc::tmem_st16(tb + lrow + kColS0 + 64 + (c >> 1), l);
+            }
+            tc::tmem_wait_st();
+        };
+
+        // Outputs and state update of chunk n (its last MMAs have committed to done_bar).
+        auto finish = [&](int n, bool last) -> bool {
+            const bool w = mbar_wait(done_bar, (uint32_t)n & 1u);
+            if (!bar_all(1, 128, w && !*abort_flag)) {
+                if (tid == 0)
+                    set_abort();
+                return false;
+            }
+            tc::fence_after_sync();
+            const ChunkConst &C = cc[n & 1];
+            const long long t0 = (long long)n * kC;
+            const int tcn = (int)(T - t0 < kC ? T - t0 : kC);
+            {
+                float d1[kC], d2[kC];
+                tmem_ld64(tb + lrow + kColD1, d1);
+                tmem_ld64(tb + lrow + kColU, d2);
+                float *o = J.out + (t0 * 32 + vh) * kD + r;
+#pragma unroll
+                for (int i = 0; i < kC; i++) {
+                    if (i < tcn)
+                        o[(long long)i * 32 * kD] =
+                            kOutScale * (C.gam[i] * C.isq[i] * inv_sigma * d1[i] + cs->imu[i] * inv_rho * d2[i]);
+                }
+            }
+            const float gC = C.gC;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                float s[32], e[32];
+                tc::tmem_ld32(tb + lrow + kColS + c, s);
+                tc::tmem_ld32(tb + lrow + kColS0 + c, e);
+                tc::tmem_wait_ld();
+                uint32_t w32[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    w32[i] = __float_as_uint(fmaf(gC, s[i], e[i] * inv_rho2));
+                tc::tmem_st32(tb + lrow + kColS + c, w32);
+            }
+            tc::tmem_wait_st();
+            if (!last)
+                write_s0();
+            tc::fence_before_sync();
+            return true;
+        };
+
+        // initial state: S^T into the master (thread r holds column r of S)
+        {
+            const float *S = J.state + (size_t)vh * kD * kD;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                uint32_t w32[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    w32[i] = __float_as_uint(__ldg(S + (size_t)(c + i) * kD + r));
+                tc::tmem_st32(tb + lrow + kColS + c, w32);
+            }
+            tc::tmem_wait_st();
+            write_s0();
+            tc::fence_before_sync();
+        }
+
+        for (int n = 0; n < nchunks && ok; n++) {
+            const ChunkConst &C = cc[n & 1];
+            // ---- inputs of chunk n staged
+            {
+                const bool w = mbar_wait(in_full, (uint32_t)n & 1u);
+                if (!bar_all(1, 128, w && !*abort_flag)) {
+                    if (tid == 0)
+                        set_abort();
+                    ok = false;
+                    break;
+                }
+            }
+            // ---- (a): [K;Q] K^T
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t id = tc::idesc_f16(128, 64, 0, 0);
+#pragma unroll 1
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint32_t A = base + (pp == 2 ? kOffKQL : kOffKQH);
+                    const uint32_t B = base + (pp == 1 ? kOffKQL : kOffKQH);
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+                        tc::mma_ss_f16(tb + kColA, tc::smem_desc(A + off, 16, 1024), tc::smem_desc(B + off, 16, 1024),
+                                       id, (pp | kk) ? 1u : 0u);
+                    }
+                }
+                tc::commit(mma_bar);
+            }
+            // ---- outputs + state update of the previous chunk (overlaps (a))
+            if (n > 0 && !finish(n - 1, false)) {
+                ok = false;
+                break;
+            }
+            named_bar_sync(1, 128);
+            // ---- L (warps 0-1) and M (warps 2-3) from (a)
+            if (!wait_mma()) {
+                ok = false;
+                break;
+            }
+            {
+                float x[kC];
+                tmem_ld64(tb + lrow + kColA, x);
+                if (r < kC) {
+                    const int i = r;
+                    const double gi = C.gl[i];
+                    const float f = C.beta[i] * C.isk[i];
+#pragma unroll
+                    for (int j = 0; j < kC; j++) {
+                        float l = 0.f;
+                        if (j < i)
+                            l = f * ex2((float)(gi - C.gl[j])) * x[j] * C.isk[j];
+                        Lw[i * kLd + j] = l;
+                    }
+                    named_bar_sync(2, 64);
+                    // diagonal 16x16 blocks of T by forward substitution (thread = column)
+                    const int col = r, b16 = col >> 4, cl = col & 15;
+                    float y[16];
+#pragma unroll
+                    for (int rr = 0; rr < 16; rr++) {
+                        float acc = 0.f;
+#pragma unroll
+                        for (int m = 0; m < rr; m++)
+                            acc = fmaf(Lm[(16 * b16 + rr) * kLd + 16 * b16 + m], y[m], acc);
+                        y[rr] = rr < cl ? 0.f : (rr == cl ? 1.f : -acc);
+                    }
+#pragma unroll
+                    for (int rr = 0; rr < 16; rr++)
+                        Tm[(16 * b16 + rr) * kLd + col] = y[rr];
+                } else {
+                    const int i = r - kC;
+                    const double gi = C.gl[i];
+                    const float f = C.isq[i];
+#pragma unroll
+                    for (int j = 0; j < kC; j++)
+                        x[j] = j <= i ? f * ex2((float)(gi - C.gl[j])) * x[j] * C.isk[j] : 0.f;
+                    const float mu = pow2_scale(row_amax(x));
+                    store_row_split(base + kOffM, base + kOffM + 8192, i, x, mu);
+                    cs->imu[i] = 1.0f / mu;
+                }
+            }
+            named_bar_sync(1, 128);
+            // ---- off-diagonal blocks of T: T_ij = -D_i sum_{m=j}^{i-1} L_im T_mj, by distance
+#pragma unroll 1
+            for (int d = 1; d <= 3; d++) {
+                const int nel = (4 - d) * 256;
+                for (int e = r; e < nel; e += 128) {
+                    const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
+                    float acc = 0.f;
+                    const float *lrow_p = Lm + (16 * bi + rr) * kLd;
+#pragma unroll 4
+                    for (int m = 16 * bj; m < 16 * bi; m++)
+                        acc = fmaf(lrow_p[m], Tm[m * kLd + 16 * bj + c2], acc);
+                    Xs[e] = acc;
+                }
+                named_bar_sync(1, 128);
+                for (int e = r; e < nel; e += 128) {
+                    const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
+                    float acc = 0.f;
+                    const float *drow = Tm + (16 * bi + rr) * kLd + 16 * bi;
+                    const float *xb = Xs + (e & ~255);
+#pragma unroll
+                    for (int m = 0; m < 16; m++)
+                        acc = fmaf(m <= rr ? drow[m] : 0.f, xb[m * 16 + c2], acc);
+                    Tm[(16 * bi + rr) * kLd + 16 * bj + c2] = -acc;
+                }
+                named_bar_sync(1, 128);
+            }
+            // ---- B operands of (b): rows of T diag(beta / s^v) and T diag(beta gamma / s^k)
+            {
+                const int i = r & 63;
+                const bool isv = r < kC;
+                float x[kC];
+#pragma unroll
+                for (int j = 0; j < kC; j++) {
+                    const float t = j <= i ? Tm[i * kLd + j] : 0.f;
+                    x[j] = isv ? t * C.beta[j] * C.isv[j] : t * C.beta[j] * C.gam[j] * C.isk[j];
+                }
+                const float u = pow2_scale(row_amax(x));
+                const uint32_t hi = base + kOffB + (isv ? 0u : 16384u);
+                store_row_split(hi, hi + 8192, i, x, u);
+                if (isv)
+                    cs->iu_v[i] = 1.0f / u;
+                else
+                    cs->iu_k[i] = 1.0f / u;
+                fence_proxy_async();
+            }
+            named_bar_sync(1, 128);
+            // ---- (b): U^T = V'^T BV'^T, W^T = K'^T BK'^T
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t id = tc::idesc_f16(128, 64, 1, 0);
+#pragma unroll 1
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint32_t Va = base + kOffV + (pp == 2 ? 16384u : 0u);
+                    const uint32_t Ka = base + (pp == 2 ? kOffKQL : kOffKQH);
+                    const uint32_t Bv = base + kOffB + (pp == 1 ? 8192u : 0u);
+                    const uint32_t Bk = base + kOffB + 16384u + (pp == 1 ? 8192u : 0u);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint32_t acc = (pp | kk) ? 1u : 0u;
+                        tc::mma_ss_f16(tb + kColU, tc::smem_desc(Va + kk * 2048u, 8192, 1024),
+                                       tc::smem_desc(Bv + kk * 32u, 16, 1024), id, acc);
+                        tc::mma_ss_f16(tb + kColW, tc::smem_desc(Ka + kk * 2048u, 16384, 1024),
+                                       tc::smem_desc(Bk + kk * 32u, 16, 1024), id, acc);
+                    }
+                }
+                tc::commit(mma_bar);
+            }
+            if (!wait_mma()) {
+                ok = false;
+                break;
+            }
+            // ---- W' = omega W^T (uniform power-of-two scale), B operand of (c)
+            {
+                float x[kC];
+                tmem_ld64(tb + lrow + kColW, x);
+                float m = row_amax(x);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (lane == 0)
+                    cs->red[warp] = m;
+                named_bar_sync(1, 128);
+                const float om = pow2_scale(fmaxf(fmaxf(cs->red[0], cs->red[1]), fmaxf(cs->red[2], cs->red[3])));
+                inv_omega = 1.0f / om;
+                store_row_split(base + kOffW, base + kOffW + 16384, r, x, om);
+                fence_proxy_async();
+                tc::fence_before_sync();
+            }
+            named_bar_sync(1, 128);
+            // ---- (c) S_0^T W'  and  (d1) S_0^T Q'^T, A = S_0^T from TMEM
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t idc = tc::idesc_f16(128, 64, 0, 1);
+                const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
+#pragma unroll 1
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint32_t Aa = tb + kColS0 + (pp == 2 ? 64u : 0u);
+                    const uint32_t Wb = base + kOffW + (pp == 1 ? 16384u : 0u);
+                    const uint32_t Qb = base + (pp == 1 ? kOffKQL : kOffKQH) + 8192u;
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t acc = (pp | kk) ? 1u : 0u;
+                        tc::mma_ts_f16(tb + kColA, Aa + kk * 8u, tc::smem_desc(Wb + kk * 2048u, 8192, 1024), idc, acc);
+                        tc::mma_ts_f16(tb + kColD1, Aa + kk * 8u,
+                                       tc::smem_desc(Qb + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
+                                       idd, acc);
+                    }
+                }
+                tc::commit(mma_bar);
+            }
+            if (!wait_mma()) {
+                ok = false;
+                break;
+            }
+            // ---- Delta^T = U^T - S_0^T W^T; its split (A of d2) and Delta''^T (A of e)
+            {
+                float dl[kC];
+                {
+                    float u[kC], c[kC];
+                    tmem_ld64(tb + lrow + kColU, u);
+                    tmem_ld64(tb + lrow + kColA, c);
+                    const float f = inv_sigma * inv_omega;
+#pragma unroll
+                    for (int i = 0; i < kC; i++)
+                        dl[i] = u[i] * cs->iu_v[i] - c[i] * (cs->iu_k[i] * f);
+                }
+                const float rho = pow2_scale(row_amax(dl));
+                inv_rho = 1.0f / rho;
+                store_row_split(base + kOffB, base + kOffB + 16384, r, dl, rho);
+#pragma unroll
+                for (int j = 0; j < kC; j++)
+                    dl[j] *= C.df[j];
+                const float rho2 = pow2_scale(row_amax(dl));
+                inv_rho2 = 1.0f / rho2;
+                store_row_split(base + kOffV, base + kOffV + 16384, r, dl, rho2);
+                fence_proxy_async();
+                tc::fence_before_sync();
+            }
+            named_bar_sync(1, 128);
+            // ---- (d2) Delta^T M^T and (e) Delta''^T K -> done_bar
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
+                const uint32_t ide = tc::idesc_f16(128, 128, 0, 1);
+#pragma unroll 1
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint32_t Da = base + kOffB + (pp == 2 ? 16384u : 0u);
+                    const uint32_t Mb = base + kOffM + (pp == 1 ? 8192u : 0u);
+                    const uint32_t Ea = base + kOffV + (pp == 2 ? 16384u : 0u);
+                    const uint32_t Kb = base + (pp == 1 ? kOffKQL : kOffKQH);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint32_t acc = (pp | kk) ? 1u : 0u;
+                        tc::mma_ss_f16(tb + kColU, tc::smem_desc(Da + kk * 32u, 16, 1024),
+                                       tc::smem_desc(Mb + kk * 32u, 16, 1024), idd, acc);
+                        tc::mma_ss_f16(tb + kColS0, tc::smem_desc(Ea + kk * 32u, 16, 1024),
+                                       tc::smem_desc(Kb + kk * 2048u, 16384, 1024), ide, acc);
+                    }
+                }
+                tc::commit(done_bar);
+            }
+        }
+        // last chunk: outputs, state update, state back to global memory
+        if (ok && nchunks > 0 && finish(nchunks - 1, true)) {
+            tc::fence_after_sync();
+            float *S = J.state + (size_t)vh * kD * kD;
+#pragma unroll 1
+            for (int c = 0; c < kD; c += 32) {
+                float x[32];
+                tc::tmem_ld32(tb + lrow + kColS + c, x);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    S[(size_t)(c + i) * kD + r] = x[i];
+            }
+        }
+        if (tid == 0) {
+            // every MMA issued must finish before tensor memory is released
+            tc::commit(drain_bar);
+            mbar_wait(drain_bar, 0);
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0)
+        tc::tmem_dealloc(tb, kTmemCols);
+}
+
+bool g_attr = false;
+
+int launch(const KernelDeltaPrefillJob *jobs, int n)
+{
+    Runtime &R = rt();
+    DPParams prm;
+    memset(static_cast<void *>(&prm), 0, sizeof(prm));
+    int m = 0;
+    for (int i = 0; i < n; i++) {
+        const KernelDeltaPrefillJob &j = jobs[i];
+        if (!j.state || !j.q || !j.k || !j.v || !j.g || !j.beta || !j.out)
+            return fail("kernel_deltanet_prefill_batch: job %d has a null pointer", i);
+        if (!aligned16(j.q) || !aligned16(j.k) || !aligned16(j.v))
+            return fail("kernel_deltanet_prefill_batch: job %d q/k/v not 16-byte aligned", i);
+        if (j.T == 0)
+            continue;
+        prm.jobs[m++] = DJob{j.state, j.q, j.k, j.v, j.g, j.beta, j.out, (long long)j.T};
+    }
+    if (m == 0)
+        return 0;
+    prm.err = R.err_word;
+    if (!g_attr) {
+        if (check(cudaFuncSetAttribute(deltanet_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes), "deltanet prefill smem attribute") != 0)
+            return -1;
+        g_attr = true;
+    }
+    deltanet_prefill_kernel<<<dim3(32, m), kThreads, kSmemBytes, R.stream>>>(prm);
+    return launched("deltanet_prefill_kernel");
+}
+
+}  // namespace
+
+int deltanet_prefill_batch(const KernelDeltaPrefillJob *jobs, int n)
+{
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_deltanet_prefill_batch: bad job array");
+    for (int i = 0; i < n; i += kMaxJobs) {
+        const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
+        if (launch(jobs + i, m) != 0)
+            return -1;
+    }
+    return 0;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" int kernel_deltanet_prefill_batch(const KernelDeltaPrefillJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    return deltanet_prefill_batch(jobs, n);
+}
+
+extern "C" int kernel_deltanet_prefill(float *state, size_t T, const float *q, const float *k, const float *v,
+                                       const float *g, const float *beta, float *out)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!state || !q || !k || !v || !g || !beta || !out)
+        return fail("kernel_deltanet_prefill: null pointer");
+    if (T == 0)
+        return 0;
+    // host q, k [T][16][128], v [T][32][128], g, beta [T][32] in; out [T][32][128]
+    const size_t nq = T * 16 * 128, nv = T * 32 * 128, nh = T * 32;
+    const size_t oq = 0, ok_ = nq, ov = 2 * nq, og = 2 * nq + nv, ob = og + nh;
+    const size_t in_f = ob + nh, out_f = nv;
+    const size_t in_pad = (in_f + 3) / 4 * 4;
+    float *h = static_cast<float *>(pinned((in_pad + out_f) * sizeof(float)));
+    float *d = static_cast<float *>(dstage((in_pad + out_f) * sizeof(float)));
+    if (!h || !d)
+        return -1;
+    memcpy(h + oq, q, nq * 4);
+    memcpy(h + ok_, k, nq * 4);
+    memcpy(h + ov, v, nv * 4);
+    memcpy(h + og, g, nh * 4);
+    memcpy(h + ob, beta, nh * 4);
+    cudaStream_t s = rt().stream;
+    if (check(cudaMemcpyAsync(d, h, in_f * 4, cudaMemcpyHostToDevice, s), "stage in") != 0)
+        return -1;
+    KernelDeltaPrefillJob j{state, d + oq, d + ok_, d + ov, d + og, d + ob, d + in_pad, T};
+    if (deltanet_prefill_batch(&j, 1) != 0)
+        return -1;
+    if (check(cudaMemcpyAsync(h + in_pad, d + in_pad, out_f * 4, cudaMemcpyDeviceToHost, s), "stage out") != 0)
+        return -1;
+    if (kernel_cuda_synchronize() != 0)
+        return -1;
+    memcpy(out, h + in_pad, out_f * 4);
+    return 0;
+}

@@ -73,6 +73,21 @@ def delta_sequence(seed: int, steps: int, layers: int = 1):
     return {k: np.stack([p[k] for p in per]) for k in per[0]}
 
 
+def delta_prompt(seed: int, T: int):
+    """One prompt of config-3 DeltaNet inputs (config-1 distributions), drawn vectorised:
+    q, k [T,16,128] L2-normalised per head, v [T,32,128] ~ N(0,1), beta = sigmoid(N(0,1)) and
+    g = -exp(N(-1, 0.5)) * softplus(N(0,1)), both [T,32]."""
+    rng = np.random.default_rng(seed)
+    q = _n(rng, T, 16, 128)
+    k = _n(rng, T, 16, 128)
+    q /= np.sqrt((q * q).sum(-1, keepdims=True) + 1e-6)
+    k /= np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+    v = _n(rng, T, 32, 128)
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((T, 32))))).astype(np.float32)
+    g = (-np.exp(rng.normal(-1.0, 0.5, (T, 32))) * softplus(rng.standard_normal((T, 32)))).astype(np.float32)
+    return {"q": q.astype(np.float32), "k": k.astype(np.float32), "v": v, "beta": beta, "g": g}
+
+
 def slot_lengths(seed: int, slots: int, lo: int = 1024, hi: int = 32768):
     """Config 2: per-slot context lengths ~ U[lo, hi] (integers, inclusive)."""
     rng = np.random.default_rng(seed)

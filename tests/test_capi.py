@@ -23,7 +23,7 @@ def test_library_exports_every_declared_symbol():
 def test_header_compiles_as_c(tmp_path):
     src = tmp_path / "t.c"
     src.write_text('#include "roaster_cuda.h"\nint main(void){ KernelAttnDecodeJob j; '
-                   'KernelDeltaStepJob d; (void)j; (void)d; return 0; }\n')
+                   'KernelDeltaStepJob d; KernelDeltaPrefillJob e; (void)j; (void)d; (void)e; return 0; }\n')
     inc = os.path.join(os.path.dirname(R.LIB_PATH), "..", "include")
     out = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", inc, str(src), "-o",
                           str(tmp_path / "t")], capture_output=True, text=True)
@@ -34,15 +34,20 @@ def test_struct_layouts_match_c(tmp_path):
     """ctypes mirrors have the C sizes and offsets."""
     src = tmp_path / "s.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "roaster_cuda.h"\n'
-                   'int main(void){ printf("%zu %zu %zu %zu\\n", sizeof(KernelAttnDecodeJob), '
-                   'offsetof(KernelAttnDecodeJob, append), sizeof(KernelDeltaStepJob), '
-                   'offsetof(KernelAttnDecodeJob, out)); return 0; }\n')
+                   'int main(void){ printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", '
+                   'sizeof(KernelAttnDecodeJob), offsetof(KernelAttnDecodeJob, append), '
+                   'sizeof(KernelDeltaStepJob), offsetof(KernelAttnDecodeJob, out), '
+                   'sizeof(KernelAttnPrefillJob), offsetof(KernelAttnPrefillJob, dtype), '
+                   'sizeof(KernelDeltaPrefillJob), offsetof(KernelDeltaPrefillJob, T)); '
+                   'return 0; }\n')
     inc = os.path.join(os.path.dirname(R.LIB_PATH), "..", "include")
     exe = tmp_path / "s"
     subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     assert vals == [C.sizeof(R.KernelAttnDecodeJob), R.KernelAttnDecodeJob.append.offset,
-                    C.sizeof(R.KernelDeltaStepJob), R.KernelAttnDecodeJob.out.offset]
+                    C.sizeof(R.KernelDeltaStepJob), R.KernelAttnDecodeJob.out.offset,
+                    C.sizeof(R.KernelAttnPrefillJob), R.KernelAttnPrefillJob.dtype.offset,
+                    C.sizeof(R.KernelDeltaPrefillJob), R.KernelDeltaPrefillJob.T.offset]
 
 
 def _has_gpu():
