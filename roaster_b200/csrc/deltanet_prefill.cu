@@ -80,13 +80,15 @@ constexpr uint32_t kOffConst = 180224; // ChunkConst[2]
 constexpr int kLd = 65;                // fp32 scratch row stride (floats)
 
 struct ChunkConst {
-    double gl[kC];                     // prefix sums of g * log2(e)
-    float gam[kC];                     // exp(G_j)
+    float glf[kC];                     // G_j * log2(e) (summed in double, rounded once)
     float beta[kC];
     float isk[kC], isq[kC], isv[kC];   // inverse row scales of K, Q, V
+    float gq[kC];                      // exp(G_j) / s^q_j
+    float bv[kC];                      // beta_j / s^v_j
+    float bk[kC];                      // beta_j exp(G_j) / s^k_j
     float df[kC];                      // exp(G_C - G_j) / s^k_j
     float gC;                          // exp(G_C)
-    float pad[15];
+    float pad[3];
 };
 static_assert(sizeof(ChunkConst) % 16 == 0, "");
 constexpr uint32_t kOffCons = kOffConst + 2 * sizeof(ChunkConst);   // consumer scratch
@@ -143,12 +145,20 @@ __device__ __forceinline__ float pow2_scale(float amax)
     return __uint_as_float((uint32_t)(127 - ec) << 23);
 }
 
+// x = hi + lo for a pair (a, b): packed f16x2 hi and lo words (a in the low half).
 __device__ __forceinline__ void split2(float a, float b, uint32_t &hw, uint32_t &lw)
 {
-    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-    hw = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-    lw = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hw = *reinterpret_cast<const uint32_t *>(&h);
+    lw = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// 1 / s for a power of two s in [2^-100, 2^100] (exact, no divide).
+__device__ __forceinline__ float pow2_inv(float s)
+{
+    return __uint_as_float((254u << 23) - __float_as_uint(s));
 }
 
 __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w)
@@ -243,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         // ============================================================ producers
         const int pw = warp - 4;                       // 0..7, rows pw + 8 s
         float4 buf[24];
-        float gv0 = 0.f, gv1 = 0.f, bv0 = 0.f, bv1 = 0.f;
+        float gv0 = 0.f, gv1 = 0.f, bv0 = 0.f, bv1 = 0.f, dfa = 0.f, dfb = 0.f;
+        double ga = 0.0, gb = 0.0;
         auto issue_loads = [&](int n) {
             const long long t0 = (long long)n * kC;
             const int tc_ = (int)(T - t0 < kC ? T - t0 : kC);
@@ -276,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         for (int n = 0; n < nchunks; n++) {
             bool ok = true;
             if (n > 0)
-                ok = mbar_wait(done_bar, (uint32_t)(n - 1) & 1u);
+                ok = mbar_wait_sleep(done_bar, (uint32_t)(n - 1) & 1u, 256);
             if (!bar_all(3, kProdThreads, ok && !*abort_flag)) {
                 if (tid == kThreads - kProdThreads)
                     set_abort();
@@ -288,11 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             for (int s = 0; s < 24; s++) {
                 const int rr = pw + 8 * s, which = rr >> 6, j = rr & 63;
                 const float4 x = buf[s];
-                float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1)
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                const float sc = pow2_scale(m);
+                // non-negative floats order like their bit patterns: one warp max-reduction
+                const float m0 = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+                const float sc = pow2_scale(__uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m0))));
                 uint32_t h0, l0, h1, l1;
                 split2(x.x * sc, x.y * sc, h0, l0);
                 split2(x.z * sc, x.w * sc, h1, l1);
@@ -310,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 sts64(hi + inner, h0, h1);
                 sts64(lo + inner, l0, l1);
                 if (lane == 0) {
-                    const float inv = 1.0f / sc;
+                    const float inv = pow2_inv(sc);
                     if (which == 0) C.isk[j] = inv;
                     else if (which == 1) C.isq[j] = inv;
                     else C.isv[j] = inv;
@@ -329,20 +338,30 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                     }
                 }
                 b += __shfl_sync(0xffffffffu, a, 31);
-                C.gl[lane] = a;
-                C.gl[lane + 32] = b;
-                C.gam[lane] = ex2((float)a);
-                C.gam[lane + 32] = ex2((float)b);
+                const double gl_last = __shfl_sync(0xffffffffu, b, 31);
+                ga = a;
+                gb = b;
+                C.glf[lane] = (float)a;
+                C.glf[lane + 32] = (float)b;
                 C.beta[lane] = bv0;
                 C.beta[lane + 32] = bv1;
+                dfa = ex2((float)(gl_last - a));
+                dfb = ex2((float)(gl_last - b));
+                if (lane == 0)
+                    C.gC = ex2((float)gl_last);
             }
             named_bar_sync(3, kProdThreads);
             if (pw == 0) {
-                const double gl_last = C.gl[kC - 1];
-                C.df[lane] = ex2((float)(gl_last - C.gl[lane])) * C.isk[lane];
-                C.df[lane + 32] = ex2((float)(gl_last - C.gl[lane + 32])) * C.isk[lane + 32];
-                if (lane == 0)
-                    C.gC = ex2((float)gl_last);
+                // per-token factors that need every row scale
+                const float e0 = ex2((float)ga), e1 = ex2((float)gb);
+                C.gq[lane] = e0 * C.isq[lane];
+                C.gq[lane + 32] = e1 * C.isq[lane + 32];
+                C.bv[lane] = bv0 * C.isv[lane];
+                C.bv[lane + 32] = bv1 * C.isv[lane + 32];
+                C.bk[lane] = bv0 * e0 * C.isk[lane];
+                C.bk[lane + 32] = bv1 * e1 * C.isk[lane + 32];
+                C.df[lane] = dfa * C.isk[lane];
+                C.df[lane + 32] = dfb * C.isk[lane + 32];
             }
             fence_proxy_async();
             mbar_arrive(in_full);
@@ -362,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         bool ok = true;
 
         auto wait_mma = [&]() -> bool {
-            const bool w = mbar_wait(mma_bar, mphase & 1u);
+            const bool w = mbar_wait_sleep(mma_bar, mphase & 1u, 32);
             mphase++;
             const bool all = bar_all(1, 128, w && !*abort_flag);
             if (!all && tid == 0)
@@ -385,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                     amax = fmaxf(amax, fabsf(x[i]));
             }
             const float sg = pow2_scale(amax);
-            inv_sigma = 1.0f / sg;
+            inv_sigma = pow2_inv(sg);
 #pragma unroll 1
             for (int c = 0; c < kD; c += 32) {
                 float x[32];
@@ -403,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
 
         // Outputs and state update of chunk n (its last MMAs have committed to done_bar).
         auto finish = [&](int n, bool last) -> bool {
-            const bool w = mbar_wait(done_bar, (uint32_t)n & 1u);
+            const bool w = mbar_wait_sleep(done_bar, (uint32_t)n & 1u, 32);
             if (!bar_all(1, 128, w && !*abort_flag)) {
                 if (tid == 0)
                     set_abort();
@@ -422,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 for (int i = 0; i < kC; i++) {
                     if (i < tcn)
                         o[(long long)i * 32 * kD] =
-                            kOutScale * (C.gam[i] * C.isq[i] * inv_sigma * d1[i] + cs->imu[i] * inv_rho * d2[i]);
+                            kOutScale * (C.gq[i] * inv_sigma * d1[i] + cs->imu[i] * inv_rho * d2[i]);
                 }
             }
             const float gC = C.gC;
@@ -465,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             const ChunkConst &C = cc[n & 1];
             // ---- inputs of chunk n staged
             {
-                const bool w = mbar_wait(in_full, (uint32_t)n & 1u);
+                const bool w = mbar_wait_sleep(in_full, (uint32_t)n & 1u, 64);
                 if (!bar_all(1, 128, w && !*abort_flag)) {
                     if (tid == 0)
                         set_abort();
@@ -506,13 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tmem_ld64(tb + lrow + kColA, x);
                 if (r < kC) {
                     const int i = r;
-                    const double gi = C.gl[i];
+                    const float gi = C.glf[i];
                     const float f = C.beta[i] * C.isk[i];
 #pragma unroll
                     for (int j = 0; j < kC; j++) {
                         float l = 0.f;
                         if (j < i)
-                            l = f * ex2((float)(gi - C.gl[j])) * x[j] * C.isk[j];
+                            l = f * ex2(gi - C.glf[j]) * x[j] * C.isk[j];
                         Lw[i * kLd + j] = l;
                     }
                     named_bar_sync(2, 64);
@@ -532,14 +551,14 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                         Tm[(16 * b16 + rr) * kLd + col] = y[rr];
                 } else {
                     const int i = r - kC;
-                    const double gi = C.gl[i];
+                    const float gi = C.glf[i];
                     const float f = C.isq[i];
 #pragma unroll
                     for (int j = 0; j < kC; j++)
-                        x[j] = j <= i ? f * ex2((float)(gi - C.gl[j])) * x[j] * C.isk[j] : 0.f;
+                        x[j] = j <= i ? f * ex2(gi - C.glf[j]) * x[j] * C.isk[j] : 0.f;
                     const float mu = pow2_scale(row_amax(x));
                     store_row_split(base + kOffM, base + kOffM + 8192, i, x, mu);
-                    cs->imu[i] = 1.0f / mu;
+                    cs->imu[i] = pow2_inv(mu);
                 }
             }
             named_bar_sync(1, 128);
@@ -577,15 +596,15 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
 #pragma unroll
                 for (int j = 0; j < kC; j++) {
                     const float t = j <= i ? Tm[i * kLd + j] : 0.f;
-                    x[j] = isv ? t * C.beta[j] * C.isv[j] : t * C.beta[j] * C.gam[j] * C.isk[j];
+                    x[j] = t * (isv ? C.bv[j] : C.bk[j]);
                 }
                 const float u = pow2_scale(row_amax(x));
                 const uint32_t hi = base + kOffB + (isv ? 0u : 16384u);
                 store_row_split(hi, hi + 8192, i, x, u);
                 if (isv)
-                    cs->iu_v[i] = 1.0f / u;
+                    cs->iu_v[i] = pow2_inv(u);
                 else
-                    cs->iu_k[i] = 1.0f / u;
+                    cs->iu_k[i] = pow2_inv(u);
                 fence_proxy_async();
             }
             named_bar_sync(1, 128);
@@ -618,15 +637,12 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             {
                 float x[kC];
                 tmem_ld64(tb + lrow + kColW, x);
-                float m = row_amax(x);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1)
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(row_amax(x))));
                 if (lane == 0)
                     cs->red[warp] = m;
                 named_bar_sync(1, 128);
                 const float om = pow2_scale(fmaxf(fmaxf(cs->red[0], cs->red[1]), fmaxf(cs->red[2], cs->red[3])));
-                inv_omega = 1.0f / om;
+                inv_omega = pow2_inv(om);
                 store_row_split(base + kOffW, base + kOffW + 16384, r, x, om);
                 fence_proxy_async();
                 tc::fence_before_sync();
@@ -670,13 +686,13 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                         dl[i] = u[i] * cs->iu_v[i] - c[i] * (cs->iu_k[i] * f);
                 }
                 const float rho = pow2_scale(row_amax(dl));
-                inv_rho = 1.0f / rho;
+                inv_rho = pow2_inv(rho);
                 store_row_split(base + kOffB, base + kOffB + 16384, r, dl, rho);
 #pragma unroll
                 for (int j = 0; j < kC; j++)
                     dl[j] *= C.df[j];
                 const float rho2 = pow2_scale(row_amax(dl));
-                inv_rho2 = 1.0f / rho2;
+                inv_rho2 = pow2_inv(rho2);
                 store_row_split(base + kOffV, base + kOffV + 16384, r, dl, rho2);
                 fence_proxy_async();
                 tc::fence_before_sync();

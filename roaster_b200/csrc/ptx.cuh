@@ -64,6 +64,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
     return true;
 }
 
+// Same, sleeping `ns` nanoseconds between polls: for long waits that share the SM sub-partition
+// with warps doing work (a polling loop would take their issue slots).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, unsigned ns,
+                                                long long budget = 2000000000ll)
+{
+    if (mbar_try_wait(bar, parity))
+        return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(ns);
+        if (clock64() - t0 > budget)
+            return false;
+    }
+    return true;
+}
+
 // ---------------------------------------------------------------- bulk async copy (TMA engine)
 
 // Global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte aligned); completion
