@@ -10,25 +10,29 @@
 //  1. prefill_prep_kernel (HBM-bound, one CTA per token): norms + RoPE; writes the prepared
 //     queries as f16 to scratch and appends K/V (f16) to the cache.
 //  2. prefill_attn_kernel (tensor-bound): a work item is (prompt, query head, 128-token query
-//     tile); persistent CTAs take items longest-first. Per CTA (256 threads):
+//     tile); persistent CTAs take items longest-first. Per CTA (416 threads):
 //       warp 0      one thread issues every tcgen05.mma and commit;
-//       warps 1-3   producers: 16-byte cp.async into 128-byte-swizzled tiles -- the Q tile
-//                   (128 x 256 f16, 64 KB) once per item, then K_j, V_j tiles (64 keys x 256,
-//                   32 KB each) through a 5-stage ring;
-//       warps 4-7   softmax + epilogue: one thread per query row (= TMEM lane).
-//     Tensor memory (512 columns): S_j = Q K_j^T (128 x 64 fp32) double-buffered in columns
-//     [0,64) and [64,128); the softmax writes P_j as packed f16 over the first 32 columns of its
-//     own S buffer, and O += P_j V_j reads P straight from TMEM (A operand in tensor memory, V as
-//     an MN-major B operand); O (128 x 256 fp32) lives in columns [256, 512).
-//     The MMA issue order S_0, S_1, PV_0, S_2, PV_1, ... overlaps each QK^T with the softmax of
-//     the previous tile. The running max is raised only when a tile exceeds it by more than 2^8
-//     (log2 units), so O is rescaled (a TMEM read-modify-write) rarely; P values stay <= 256.
+//       warps 1-3, 12  producers: 16-byte cp.async into 128-byte-swizzled tiles -- the Q tile
+//                   (128 x 256 f16, 64 KB) once per item, then each 128-key K and V tile as
+//                   two 32 KB halves through a 5-stage ring, in the order the MMAs use them;
+//       warps 4-11  softmax + epilogue: two warps per query row (= TMEM lane), each owning half
+//                   of the tile's columns and half of the output dims.
+//     Tensor memory (512 columns): S_j = Q K_j^T (128 x 128 fp32) double-buffered in columns
+//     [0,128) and [128,256); each softmax warp writes its 64 columns of P_j as packed f16 back
+//     into the S buffer, and O += P_j V_j reads P straight from TMEM (A operand in tensor
+//     memory, V as an MN-major B operand); O (128 x 256 fp32) lives in columns [256, 512).
+//     128-key tiles make every QK^T MMA N = 128: a tcgen05.mma with both operands in shared
+//     memory costs about as much to issue at N = 64 as at N = 128 (measured), so the wider tile
+//     halves the issue cost per key. The MMA issue order S_0, S_1, PV_0, S_2, PV_1, ... overlaps
+//     each QK^T with the softmax of the previous tile. The running max is raised only when a
+//     tile exceeds it by more than 2^8 (log2 units), so O is rescaled (a TMEM read-modify-write)
+//     rarely; P values stay <= 256.
 //
 // Synchronisation (all mbarrier waits bounded; a timeout sets the device error word):
 //   q_full / q_empty       Q tile of the current item loaded / all its QK^T MMAs done
 //   kv_full[s] / kv_empty[s]  ring stage loaded / consumed by its MMA
 //   s_full[b]              S buffer b written (tcgen05.commit)
-//   p_full[b]              P of buffer b written by all 128 softmax threads
+//   p_full[b]              P of buffer b written by all 256 softmax threads
 //   pv_done[k % 2]         O += P_k V_k finished (two barriers so no waiter is ever two phases
 //                          behind: a commit fires only after every earlier MMA, so when S_j is
 //                          complete every PV up to j-2 is too)
@@ -49,24 +53,30 @@
 #include <queue>
 #include <vector>
 
-#ifndef PREFILL_EXTRA_PROD
-#define PREFILL_EXTRA_PROD 0
-#endif
 
 namespace rb {
 namespace {
 
 constexpr int kD = 256;
 constexpr int kBM = 128;                     // query rows per item
-constexpr int kBN = 64;                      // keys per tile
+constexpr int kBN = 128;                     // keys per tile (S MMAs with N = 128)
 constexpr int kStages = 5;
 constexpr int kChunkQ = kBM * 128;           // one 64-dim chunk of the Q tile (16 KB)
 constexpr int kQBytes = 4 * kChunkQ;         // 64 KB
-constexpr int kChunkKV = kBN * 128;          // 8 KB
-constexpr int kKVBytes = 4 * kChunkKV;       // 32 KB
-constexpr int kProdWarps = 3 + PREFILL_EXTRA_PROD;      // warps 1-3 and 8.. (after the softmax warpgroup)
+// A ring stage holds half of a K or V tile (32 KB):
+//   K half h: dims [128h, 128h + 128) of all 128 keys, [2 dim chunks][128 keys][128 B]
+//   V half h: keys [64h, 64h + 64) with all 256 dims, [4 dim chunks][64 keys][128 B]
+// Fills follow the order the MMAs consume them -- K_0, K_1, V_0, K_2, V_1, ..., V_{nt-1} (each
+// as two halves) -- so K runs two tiles ahead of the tensor core; a half-stage is released as
+// soon as the MMAs reading it complete.
+__host__ __device__ constexpr unsigned kfill(int j) { return j == 0 ? 0u : 4u * (unsigned)j - 2u; }
+__host__ __device__ constexpr unsigned vfill(int j, int nt) { return j + 1 == nt ? 4u * (unsigned)j + 2u : 4u * (unsigned)j + 4u; }
+constexpr int kStageBytes = 32768;
+constexpr int kKChunk = kBN * 128;           // 16 KB: one 64-dim chunk of 128 keys
+constexpr int kVChunk = 64 * 128;            // 8 KB: one 64-dim chunk of 64 keys
+constexpr int kProdWarps = 4;                // warps 1-3 and 12
 constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kThreads = 256 + 32 * PREFILL_EXTRA_PROD;
+constexpr int kThreads = 416;                 // + 8 softmax warps (4-11)
 constexpr int kMaxJobs = 64;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
@@ -92,9 +102,10 @@ struct PParams {
 
 struct Smem {
     unsigned char q[kQBytes];                   // 1024-byte aligned (swizzle atoms)
-    unsigned char kv[kStages][kKVBytes];
+    unsigned char kv[kStages][kStageBytes];
     unsigned long long q_full, q_empty, kv_full[kStages], kv_empty[kStages];
     unsigned long long s_full[2], p_full[2], pv_done[2], drain;
+    float lsum[2][kBM];                         // row-sum halves of the two softmax warps of a row
     uint32_t tmem_base;
     int abort;
 };
@@ -175,13 +186,6 @@ __device__ __forceinline__ void load_gate32(const void *base, long long idx, int
     }
 }
 
-__device__ __forceinline__ float load_in(const void *base, long long idx, int dtype)
-{
-    if (dtype == KERNEL_DTYPE_BF16)
-        return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(base)[idx]);
-    return reinterpret_cast<const float *>(base)[idx];
-}
-
 // ---------------------------------------------------------------------------- prep kernel
 
 struct PrepJob {
@@ -198,10 +202,31 @@ struct PrepParams {
     int njobs;
 };
 
-// One CTA per token: warp w handles rows w, w + 8, w + 16 of the token's 16 q heads, 2 k heads
-// and 2 v heads; lane l holds dims 8l .. 8l+7.
+// Eight consecutive inputs (dims 8 lane .. 8 lane + 7 of one row) as fp32; 16-byte loads.
+__device__ __forceinline__ void load8(const void *base, long long idx, int dtype, float (&x)[8])
+{
+    if (dtype == KERNEL_DTYPE_BF16) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(base) + idx));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            x[2 * k] = __uint_as_float(w[k] << 16);
+            x[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+    } else {
+        const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(base) + idx);
+        const float4 a = __ldg(src), b = __ldg(src + 1);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+}
+
+// One CTA per token. The token's 32 RoPE angles (position * inv_freq[j], rotated with one
+// sincosf each) are shared by its 18 rotated rows; then warp w handles rows w, w + 8, w + 16 of
+// the token's 16 q heads, 2 k heads and 2 v heads, lane l holding dims 8l .. 8l+7.
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ PrepParams p)
 {
+    __shared__ float rc[32], rs[32];
     const int gtok = blockIdx.x;
     int lo = 0, hi = p.njobs - 1;
     while (lo < hi) {
@@ -214,22 +239,22 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
     const PrepJob &J = p.jobs[lo];
     const long long t = gtok - J.tok0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float pos = (float)(J.base + t);
+    if (threadIdx.x < 32) {
+        const float pos = (float)(J.base + t);
+        float sn, cs;
+        sincosf(pos * p.inv_freq[threadIdx.x], &sn, &cs);
+        rc[threadIdx.x] = cs;
+        rs[threadIdx.x] = sn;
+    }
+    __syncthreads();
     for (int row = warp; row < 20; row += 8) {
         float x[8];
         const bool isq = row < 16, isk = row >= 16 && row < 18;
         const int h = isq ? row : (isk ? row - 16 : row - 18);
-        if (isq) {
-            const long long b = t * J.qg_tok_stride + (long long)h * J.qg_stride + lane * 8;
-#pragma unroll
-            for (int e = 0; e < 8; e++)
-                x[e] = load_in(J.q, b + e, J.dtype);
-        } else {
-            const long long b = t * 512 + h * 256 + lane * 8;
-#pragma unroll
-            for (int e = 0; e < 8; e++)
-                x[e] = load_in(isk ? J.k : J.v, b + e, J.dtype);
-        }
+        if (isq)
+            load8(J.q, t * J.qg_tok_stride + (long long)h * J.qg_stride + lane * 8, J.dtype, x);
+        else
+            load8(isk ? J.k : J.v, t * 512 + h * 256 + lane * 8, J.dtype, x);
         if (isq || isk) {
             float ss = 0.f;
 #pragma unroll
@@ -239,18 +264,19 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
             for (int o = 16; o > 0; o >>= 1)
                 ss += __shfl_xor_sync(0xffffffffu, ss, o);
             const float inv = 1.0f / sqrtf(ss / (float)kD + 1e-6f);
-            const float *w = isq ? J.q_norm : J.k_norm;
+            const float4 *w4 = reinterpret_cast<const float4 *>((isq ? J.q_norm : J.k_norm) + lane * 8);
+            const float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
             for (int e = 0; e < 8; e++)
-                x[e] = x[e] * inv * __ldg(w + lane * 8 + e);
+                x[e] = x[e] * inv * w[e];
             // RoPE: dims j and j + 32 (j < 32) live on lanes l and l + 4 (l < 4)
 #pragma unroll
             for (int e = 0; e < 8; e++) {
                 const float other = __shfl_xor_sync(0xffffffffu, x[e], 4);
                 if (lane < 8) {
-                    float sn, cs;
-                    sincosf(pos * p.inv_freq[(lane & 3) * 8 + e], &sn, &cs);
-                    x[e] = lane < 4 ? x[e] * cs - other * sn : x[e] * cs + other * sn;
+                    const int j = (lane & 3) * 8 + e;
+                    x[e] = lane < 4 ? x[e] * rc[j] - other * rs[j] : x[e] * rc[j] + other * rs[j];
                 }
             }
         }
@@ -286,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_addr(&sm.s_full[b]), 1);
-            mbar_init(smem_addr(&sm.p_full[b]), 128);
+            mbar_init(smem_addr(&sm.p_full[b]), 256);
             mbar_init(smem_addr(&sm.pv_done[b]), 1);
         }
         mbar_init(smem_addr(&sm.drain), 1);
@@ -307,6 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             const uint32_t idS = tc::idesc_f16(kBM, kBN, 0, 0);
+            const uint64_t qd = tc::smem_desc(sq, 16, 1024);
             const uint32_t idO = tc::idesc_f16(kBM, kD, 0, 1);
             unsigned fill = 0, g = 0, nitem = 0;
             bool ok = true;
@@ -317,23 +344,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 }
                 return ok;
             };
+            auto acquire = [&](unsigned f) {                 // ring fill f loaded
+                if (!wait(sm.kv_full[f % kStages], (f / kStages) & 1))
+                    return 0u;
+                fence_proxy_async();
+                return smem_addr(sm.kv[f % kStages]);
+            };
+            // O += P_g V_g; V_g occupies fills fv (keys 0-63) and fv + 1 (keys 64-127)
             auto pv = [&](unsigned gg, unsigned fv, bool first) {
                 if (!wait(sm.p_full[gg & 1], (gg >> 1) & 1))
                     return;
-                const int sv = fv % kStages;
-                if (!wait(sm.kv_full[sv], (fv / kStages) & 1))
+                const uint32_t v0 = acquire(fv), v1 = ok ? acquire(fv + 1) : 0u;
+                if (!ok)
                     return;
-                fence_proxy_async();
                 tc::fence_after_sync();
-                const uint32_t vb = smem_addr(sm.kv[sv]);
+                const uint64_t vd0 = tc::smem_desc(v0, kVChunk, 1024), vd1 = tc::smem_desc(v1, kVChunk, 1024);
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; kk++) {
-                    const uint64_t bd = tc::smem_desc(vb + kk * 16 * 128, kChunkKV, 1024);
-                    tc::mma_ts_f16(tbase + kColO, tbase + (gg & 1) * kBN + kk * 8, bd, idO,
-                                   (first && kk == 0) ? 0u : 1u);
+                    // P for keys 0-63 sits in columns [0, 32) of the tile, keys 64-127 in [64, 96)
+                    tc::mma_ts_f16(tbase + kColO, tbase + (gg & 1) * kBN + (kk < 4 ? kk * 8 : 32 + kk * 8),
+                                   tc::desc_adv(kk < 4 ? vd0 : vd1, (kk & 3) * 2048), idO, (first && kk == 0) ? 0u : 1u);
+                    if (kk == 3)
+                        tc::commit(smem_addr(&sm.kv_empty[fv % kStages]));
                 }
                 tc::commit(smem_addr(&sm.pv_done[gg & 1]));
-                tc::commit(smem_addr(&sm.kv_empty[sv]));
+                tc::commit(smem_addr(&sm.kv_empty[(fv + 1) % kStages]));
             };
             for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
                 const Item it = decode_item(p, p.sched[idx]);
@@ -343,39 +378,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 tc::fence_after_sync();
                 const unsigned fbase = fill;
                 for (int j = 0; j < it.nt && ok; j++) {
-                    const unsigned fk = fbase + 2 * j;
-                    const int sk = fk % kStages;
-                    if (!wait(sm.kv_full[sk], (fk / kStages) & 1))
+                    const unsigned fk = fbase + kfill(j);
+                    const uint32_t k0 = acquire(fk), k1 = ok ? acquire(fk + 1) : 0u;
+                    if (!ok)
                         break;
-                    fence_proxy_async();
                     tc::fence_after_sync();
-                    const uint32_t kb = smem_addr(sm.kv[sk]);
                     const unsigned gj = g + j;
+                    const uint64_t kd0 = tc::smem_desc(k0, 16, 1024), kd1 = tc::smem_desc(k1, 16, 1024);
 #pragma unroll
                     for (int kk = 0; kk < kD / 16; kk++) {
-                        const uint64_t ad = tc::smem_desc(sq + (kk >> 2) * kChunkQ + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = tc::smem_desc(kb + (kk >> 2) * kChunkKV + (kk & 3) * 32, 16, 1024);
-                        tc::mma_ss_f16(tbase + (gj & 1) * kBN, ad, bd, idS, kk > 0 ? 1u : 0u);
+                        tc::mma_ss_f16(tbase + (gj & 1) * kBN, tc::desc_adv(qd, (kk >> 2) * kChunkQ + (kk & 3) * 32),
+                                       tc::desc_adv(kk < 8 ? kd0 : kd1, ((kk >> 2) & 1) * kKChunk + (kk & 3) * 32), idS,
+                                       kk > 0 ? 1u : 0u);
+                        if (kk == 7)
+                            tc::commit(smem_addr(&sm.kv_empty[fk % kStages]));
                     }
                     tc::commit(smem_addr(&sm.s_full[gj & 1]));
-                    tc::commit(smem_addr(&sm.kv_empty[sk]));
+                    tc::commit(smem_addr(&sm.kv_empty[(fk + 1) % kStages]));
                     if (j == it.nt - 1)
                         tc::commit(smem_addr(&sm.q_empty));
                     if (j >= 1)
-                        pv(gj - 1, fbase + 2 * (j - 1) + 1, j - 1 == 0);
+                        pv(gj - 1, fbase + vfill(j - 1, it.nt), j - 1 == 0);
                 }
                 if (ok)
-                    pv(g + it.nt - 1, fbase + 2 * (it.nt - 1) + 1, it.nt == 1);
+                    pv(g + it.nt - 1, fbase + vfill(it.nt - 1, it.nt), it.nt == 1);
                 g += it.nt;
-                fill += 2 * it.nt;
+                fill += 4 * it.nt;
             }
             // every MMA issued must finish before tensor memory is released
             tc::commit(smem_addr(&sm.drain));
             mbar_wait(smem_addr(&sm.drain), 0);
         }
-    } else if (warp <= 3 || warp >= 8) {
+    } else if (warp <= 3 || warp >= 12) {
         // ---------------------------------------------------------------- producers
-        const int pw = warp <= 3 ? warp - 1 : warp - 5;
+        const int pw = warp <= 3 ? warp - 1 : warp - 9;
         const uint32_t lofs = (uint32_t)(lane >> 3);          // chunk of this lane's 8 dims
         const uint32_t lu = (uint32_t)(lane & 7);             // 16-byte unit within the chunk
         unsigned fill = 0, nitem = 0;
@@ -395,8 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 cp_async16(sq + lofs * kChunkQ + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4), src);
             }
             cp_async_arrive(smem_addr(&sm.q_full));
-            for (int j = 0; j < it.nt && ok; j++) {
-                for (int which = 0; which < 2; which++, fill++) {
+            for (int step = 0; step <= it.nt && ok; step++) {
+                for (int part = 0; part < 4; part++) {
+                    // step s: K_s (parts 0, 1) if s < nt, then V_{s-1} (parts 2, 3) if s >= 1
+                    const int j = part < 2 ? step : step - 1;
+                    if ((part < 2 && step == it.nt) || (part >= 2 && step == 0))
+                        continue;
                     const int s = fill % kStages;
                     const unsigned f = fill / kStages;
                     if (f > 0 && !mbar_wait(smem_addr(&sm.kv_empty[s]), (f - 1) & 1)) {
@@ -405,24 +445,45 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                         ok = false;
                         break;
                     }
-                    const __half *cache = which ? J.v_cache : J.k_cache;
-                    const uint32_t st = smem_addr(sm.kv[s]) + lofs * kChunkKV;
-                    for (int r = pw; r < kBN; r += kProdWarps) {
-                        long long key = (long long)j * kBN + r;
-                        if (key > it.kend - 1)
-                            key = it.kend - 1;                       // tail: a valid row, masked later
-                        cp_async16(st + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4),
-                                   cache + (key * 2 + it.kvh) * kD + lane * 8);
+                    const uint32_t st = smem_addr(sm.kv[s]);
+                    const long long key0 = (long long)j * kBN;
+                    if (part < 2) {
+                        // K half: dims [128 part, +128) of 128 keys; 16 lanes per key
+                        const uint32_t c = (uint32_t)(lane >> 3) & 1u, u = (uint32_t)(lane & 7);
+                        for (int r2 = pw; r2 < kBN / 2; r2 += kProdWarps) {
+                            const int r = 2 * r2 + (lane >> 4);
+                            long long key = key0 + r;
+                            if (key > it.kend - 1)
+                                key = it.kend - 1;                   // tail: a valid row, masked later
+                            cp_async16(st + c * kKChunk + r * 128 + ((u ^ (uint32_t)(r & 7)) << 4),
+                                       J.k_cache + (key * 2 + it.kvh) * kD + part * 128 + c * 64 + u * 8);
+                        }
+                    } else {
+                        // V half: keys [64 (part - 2), +64), all 256 dims; one warp per key
+                        for (int r = pw; r < 64; r += kProdWarps) {
+                            long long key = key0 + 64 * (part - 2) + r;
+                            if (key > it.kend - 1)
+                                key = it.kend - 1;
+                            cp_async16(st + lofs * kVChunk + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4),
+                                       J.v_cache + (key * 2 + it.kvh) * kD + lane * 8);
+                        }
                     }
                     cp_async_arrive(smem_addr(&sm.kv_full[s]));
+                    fill++;
                 }
             }
         }
         cp_async_wait_all();     // nothing of ours may still be landing when the CTA retires
     } else {
         // ---------------------------------------------------------------- softmax + epilogue
-        const int row = tid - 128;                         // query row = TMEM lane
+        // Two warps per query row: warps 4-7 take score columns 0-63 (and output dims 0-127),
+        // warps 8-11 columns 64-127 (dims 128-255). Both read the whole row for its max, so the
+        // pair agrees on it without exchanging values (a pair barrier then keeps P writes behind
+        // both reads); the row sums meet in shared memory once per query tile.
+        const int half = warp >= 8 ? 1 : 0;
+        const int row = (warp & 3) * 32 + lane;            // query row = TMEM lane
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const int c0 = 64 * half;
         const float sc = kLog2e / 16.0f;
         unsigned g = 0;
         bool ok = true;
@@ -444,50 +505,71 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                     break;
                 }
                 tc::fence_after_sync();
-                float x[kBN];
-                {
-                    float a[32], b[32];
-                    tc::tmem_ld32(sb, a);
-                    tc::tmem_ld32(sb + 32, b);
-                    tc::tmem_wait_ld();
-#pragma unroll
-                    for (int c = 0; c < 32; c++) {
-                        x[c] = a[c];
-                        x[c + 32] = b[c];
-                    }
-                }
                 // causal mask only where the tile reaches past some row's last key
                 const long long key0 = (long long)j * kBN;
-                if (key0 + kBN - 1 > it_qmin) {
-                    const int lim = (int)(qlimit - key0);           // keys [key0, key0 + lim] visible
+                const bool masked = key0 + kBN - 1 > it_qmin;
+                const int lim = masked ? (int)(qlimit - key0 < -1 ? -1 : qlimit - key0) : kBN;  // keys <= lim visible
+                // pass 1: max over the whole row (tree reduction, 32 columns at a time)
+                float mt = -INFINITY;
+#pragma unroll 1
+                for (int c = 0; c < kBN; c += 32) {
+                    float x[32];
+                    tc::tmem_ld32(sb + c, x);
+                    tc::tmem_wait_ld();
+                    if (masked) {
 #pragma unroll
-                    for (int c = 0; c < kBN; c++)
-                        x[c] = c <= lim ? x[c] : -INFINITY;
+                        for (int i = 0; i < 32; i++)
+                            x[i] = c + i <= lim ? x[i] : -INFINITY;
+                    }
+#pragma unroll
+                    for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+                        for (int i = 0; i < w; i++)
+                            x[i] = fmaxf(x[i], x[i + w]);
+                    mt = fmaxf(mt, x[0]);
                 }
-                float mt = x[0];
-#pragma unroll
-                for (int c = 1; c < kBN; c++)
-                    mt = fmaxf(mt, x[c]);
                 mt *= sc;                                            // row max in log2 units
+                // the partner warp reads this warp's columns in its pass 1; P overwrites them next
+                named_bar_sync(1 + (warp & 3), 64);
                 float m_new = m_run;
                 if (mt > m_run + kRescale || (m_run == -INFINITY && mt != -INFINITY))
                     m_new = mt;
                 const float m_use = m_new == -INFINITY ? 0.f : m_new;
                 const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_use);
-                float sum = 0.f;
-                uint32_t w[32];
+                // pass 2 over this warp's 64 columns: P = 2^(s sc - m) as f16, packed two per
+                // column into [c0, c0 + 32) (chunk c's P lands at c0 + (c - c0)/2, columns this
+                // warp has already read)
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 1
+                for (int c = c0; c < c0 + 64; c += 32) {
+                    float x[32];
+                    tc::tmem_ld32(sb + c, x);
+                    tc::tmem_wait_ld();
+                    if (masked) {
 #pragma unroll
-                for (int c = 0; c < kBN; c += 2) {
-                    const float e0 = ex2(fmaf(x[c], sc, -m_use)), e1 = ex2(fmaf(x[c + 1], sc, -m_use));
-                    sum += e0 + e1;
-                    w[c >> 1] = pack_f16x2(e0, e1);
+                        for (int i = 0; i < 32; i++)
+                            x[i] = c + i <= lim ? x[i] : -INFINITY;
+                    }
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float e0 = ex2(fmaf(x[i], sc, -m_use)), e1 = ex2(fmaf(x[i + 1], sc, -m_use));
+                        const float e2 = ex2(fmaf(x[i + 2], sc, -m_use)), e3 = ex2(fmaf(x[i + 3], sc, -m_use));
+                        s0 += e0;
+                        s1 += e1;
+                        s2 += e2;
+                        s3 += e3;
+                        w[i >> 1] = pack_f16x2(e0, e1);
+                        w[(i >> 1) + 1] = pack_f16x2(e2, e3);
+                    }
+                    tc::tmem_st16(sb + c0 + ((c - c0) >> 1), w);
                 }
+                const float sum = (s0 + s1) + (s2 + s3);
                 l = l * alpha + sum;
-                tc::tmem_st32(sb, w);
                 tc::tmem_wait_st();
                 const bool need = m_run != -INFINITY && m_new != m_run;
                 if (__any_sync(0xffffffffu, need)) {
-                    // O holds sums relative to m_run: rescale once PV_{j-1} has landed
+                    // O holds sums relative to m_run: rescale this warp's half once PV_{j-1} landed
                     const unsigned pj = gj - 1;
                     if (!warp_wait(smem_addr(&sm.pv_done[pj & 1]), (pj >> 1) & 1)) {
                         if (lane == 0)
@@ -498,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                     tc::fence_after_sync();
                     const float f = need ? alpha : 1.0f;
 #pragma unroll 1
-                    for (int c = 0; c < kD; c += 32) {
+                    for (int c = 128 * half; c < 128 * half + 128; c += 32) {
                         float o[32];
                         tc::tmem_ld32(tbase + lane_base + kColO + c, o);
                         tc::tmem_wait_ld();
@@ -516,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
             }
             if (!ok)
                 break;
-            // epilogue: O / l * sigmoid(gate)
+            // epilogue: O / l * sigmoid(gate) for this warp's 128 output dims
             const unsigned pl = g + it.nt - 1;
             if (!warp_wait(smem_addr(&sm.pv_done[pl & 1]), (pl >> 1) & 1)) {
                 if (lane == 0)
@@ -525,20 +607,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 break;
             }
             tc::fence_after_sync();
-            const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-            const long long gbase = (qvalid ? tq : it.t0) * J.qg_tok_stride + (long long)it.head * J.qg_stride;
-            float *orow = J.out + (tq * 16 + it.head) * kD;
+            sm.lsum[half][row] = l;
+            named_bar_sync(1 + (warp & 3), 64);
+            const float lt = sm.lsum[0][row] + sm.lsum[1][row];
+            const float inv_l = lt > 0.f ? 1.0f / lt : 0.f;
+            const int d0 = 128 * half;
+            const long long gbase = (qvalid ? tq : it.t0) * J.qg_tok_stride + (long long)it.head * J.qg_stride + d0;
+            float *orow = J.out + (tq * 16 + it.head) * kD + d0;
             float gv[32], gn[32];
             load_gate32(J.gate, gbase, J.dtype, gn);
 #pragma unroll 1
-            for (int c = 0; c < kD; c += 32) {
+            for (int c = 0; c < 128; c += 32) {
 #pragma unroll
                 for (int i = 0; i < 32; i++)
                     gv[i] = gn[i];
-                if (c + 32 < kD)
+                if (c + 32 < 128)
                     load_gate32(J.gate, gbase + c + 32, J.dtype, gn);     // next chunk in flight
                 float o[32];
-                tc::tmem_ld32(tbase + lane_base + kColO + c, o);
+                tc::tmem_ld32(tbase + lane_base + kColO + d0 + c, o);
                 tc::tmem_wait_ld();
                 if (qvalid) {
 #pragma unroll
@@ -552,6 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                     }
                 }
             }
+            // the pair's partner may still be reading lsum for this tile; the next write is a
+            // full query tile later, after its named barrier
             tc::fence_before_sync();
             g += it.nt;
         }
@@ -582,8 +670,9 @@ int validate(const KernelAttnPrefillJob &j, int i)
     if (j.qg_stride < 256 || j.qg_tok_stride < 16 * j.qg_stride / 2 || (j.qg_stride & 7) ||
         (j.qg_tok_stride & 7))
         return fail("attn prefill: job %d bad q/gate strides (>= 256, multiples of 8)", i);
-    if (!aligned16(j.gate))
-        return fail("attn prefill: job %d gate not 16-byte aligned", i);
+    if (!aligned16(j.gate) || !aligned16(j.q) || !aligned16(j.k) || !aligned16(j.v) ||
+        !aligned16(j.q_norm) || !aligned16(j.k_norm))
+        return fail("attn prefill: job %d q/gate/k/v/norm weights not 16-byte aligned", i);
     return 0;
 }
 
@@ -772,3 +861,4 @@ extern "C" int kernel_attn_prefill(const float *q_gate, const float *k, const fl
         return -1;
     return kernel_cuda_synchronize();
 }
+

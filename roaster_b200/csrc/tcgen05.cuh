@@ -25,6 +25,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return d;
 }
 
+// The same descriptor moved `bytes` further (16-byte multiple; stays inside the shared window,
+// so the 14-bit address field cannot carry). Building a descriptor once per tile and advancing
+// it by compile-time offsets keeps the issuing thread's work per MMA to one add; rebuilding
+// both descriptors per MMA costs more issue time than an N <= 128 MMA takes to execute.
+__device__ __forceinline__ uint64_t desc_adv(uint64_t d, uint32_t bytes)
+{
+    return d + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor, kind::f16 with f16 A/B and fp32 accumulate.
 // a_mn / b_mn: operand is MN-major (1) or K-major (0).
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn, int b_mn)
