@@ -376,6 +376,15 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         float *Lw = reinterpret_cast<float *>(gbase + kOffB);
         float *Xs = reinterpret_cast<float *>(gbase + kOffB) + kC * kLd;
         float *Tm = reinterpret_cast<float *>(gbase + kOffW);
+        // shared-memory operand descriptors (the layout is static; MMAs add compile-time offsets)
+        const uint64_t dKQH = tc::smem_desc(base + kOffKQH, 16, 1024), dKQL = tc::smem_desc(base + kOffKQL, 16, 1024);
+        const uint64_t dKQHm = tc::smem_desc(base + kOffKQH, 16384, 1024);     // K' as MN-major operand
+        const uint64_t dKQLm = tc::smem_desc(base + kOffKQL, 16384, 1024);
+        const uint64_t dVm = tc::smem_desc(base + kOffV, 8192, 1024);          // V' (MN-major); lo at +16 KB
+        const uint64_t dVk = tc::smem_desc(base + kOffV, 16, 1024);            // Delta''^T (K-major)
+        const uint64_t dB = tc::smem_desc(base + kOffB, 16, 1024);             // BV, BK; later Delta^T
+        const uint64_t dWm = tc::smem_desc(base + kOffW, 8192, 1024);          // W' (MN-major)
+        const uint64_t dM = tc::smem_desc(base + kOffM, 16, 1024);
         float inv_sigma = 1.f, inv_rho = 1.f, inv_rho2 = 1.f, inv_omega = 1.f;
         uint32_t mphase = 0;
         bool ok = true;
@@ -496,15 +505,13 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             if (tid == 0) {
                 tc::fence_after_sync();
                 const uint32_t id = tc::idesc_f16(128, 64, 0, 0);
-#pragma unroll 1
+#pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
-                    const uint32_t A = base + (pp == 2 ? kOffKQL : kOffKQH);
-                    const uint32_t B = base + (pp == 1 ? kOffKQL : kOffKQH);
+                    const uint64_t A = pp == 2 ? dKQL : dKQH, B = pp == 1 ? dKQL : dKQH;
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
                         const uint32_t off = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-                        tc::mma_ss_f16(tb + kColA, tc::smem_desc(A + off, 16, 1024), tc::smem_desc(B + off, 16, 1024),
-                                       id, (pp | kk) ? 1u : 0u);
+                        tc::mma_ss_f16(tb + kColA, tc::desc_adv(A, off), tc::desc_adv(B, off), id, (pp | kk) ? 1u : 0u);
                     }
                 }
                 tc::commit(mma_bar);
@@ -612,19 +619,17 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             if (tid == 0) {
                 tc::fence_after_sync();
                 const uint32_t id = tc::idesc_f16(128, 64, 1, 0);
-#pragma unroll 1
+#pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
-                    const uint32_t Va = base + kOffV + (pp == 2 ? 16384u : 0u);
-                    const uint32_t Ka = base + (pp == 2 ? kOffKQL : kOffKQH);
-                    const uint32_t Bv = base + kOffB + (pp == 1 ? 8192u : 0u);
-                    const uint32_t Bk = base + kOffB + 16384u + (pp == 1 ? 8192u : 0u);
+                    const uint64_t Va = tc::desc_adv(dVm, pp == 2 ? 16384u : 0u);
+                    const uint64_t Ka = pp == 2 ? dKQLm : dKQHm;
+                    const uint64_t Bv = tc::desc_adv(dB, pp == 1 ? 8192u : 0u);
+                    const uint64_t Bk = tc::desc_adv(dB, pp == 1 ? 24576u : 16384u);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
                         const uint32_t acc = (pp | kk) ? 1u : 0u;
-                        tc::mma_ss_f16(tb + kColU, tc::smem_desc(Va + kk * 2048u, 8192, 1024),
-                                       tc::smem_desc(Bv + kk * 32u, 16, 1024), id, acc);
-                        tc::mma_ss_f16(tb + kColW, tc::smem_desc(Ka + kk * 2048u, 16384, 1024),
-                                       tc::smem_desc(Bk + kk * 32u, 16, 1024), id, acc);
+                        tc::mma_ss_f16(tb + kColU, tc::desc_adv(Va, kk * 2048u), tc::desc_adv(Bv, kk * 32u), id, acc);
+                        tc::mma_ss_f16(tb + kColW, tc::desc_adv(Ka, kk * 2048u), tc::desc_adv(Bk, kk * 32u), id, acc);
                     }
                 }
                 tc::commit(mma_bar);
@@ -653,18 +658,17 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tc::fence_after_sync();
                 const uint32_t idc = tc::idesc_f16(128, 64, 0, 1);
                 const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
-#pragma unroll 1
+#pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
                     const uint32_t Aa = tb + kColS0 + (pp == 2 ? 64u : 0u);
-                    const uint32_t Wb = base + kOffW + (pp == 1 ? 16384u : 0u);
-                    const uint32_t Qb = base + (pp == 1 ? kOffKQL : kOffKQH) + 8192u;
+                    const uint64_t Wb = tc::desc_adv(dWm, pp == 1 ? 16384u : 0u);
+                    const uint64_t Qb = tc::desc_adv(pp == 1 ? dKQL : dKQH, 8192u);
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
                         const uint32_t acc = (pp | kk) ? 1u : 0u;
-                        tc::mma_ts_f16(tb + kColA, Aa + kk * 8u, tc::smem_desc(Wb + kk * 2048u, 8192, 1024), idc, acc);
+                        tc::mma_ts_f16(tb + kColA, Aa + kk * 8u, tc::desc_adv(Wb, kk * 2048u), idc, acc);
                         tc::mma_ts_f16(tb + kColD1, Aa + kk * 8u,
-                                       tc::smem_desc(Qb + (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u, 16, 1024),
-                                       idd, acc);
+                                       tc::desc_adv(Qb, (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u), idd, acc);
                     }
                 }
                 tc::commit(mma_bar);
@@ -703,19 +707,17 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tc::fence_after_sync();
                 const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
                 const uint32_t ide = tc::idesc_f16(128, 128, 0, 1);
-#pragma unroll 1
+#pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
-                    const uint32_t Da = base + kOffB + (pp == 2 ? 16384u : 0u);
-                    const uint32_t Mb = base + kOffM + (pp == 1 ? 8192u : 0u);
-                    const uint32_t Ea = base + kOffV + (pp == 2 ? 16384u : 0u);
-                    const uint32_t Kb = base + (pp == 1 ? kOffKQL : kOffKQH);
+                    const uint64_t Da = tc::desc_adv(dB, pp == 2 ? 16384u : 0u);
+                    const uint64_t Mb = tc::desc_adv(dM, pp == 1 ? 8192u : 0u);
+                    const uint64_t Ea = tc::desc_adv(dVk, pp == 2 ? 16384u : 0u);
+                    const uint64_t Kb = pp == 1 ? dKQLm : dKQHm;
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
                         const uint32_t acc = (pp | kk) ? 1u : 0u;
-                        tc::mma_ss_f16(tb + kColU, tc::smem_desc(Da + kk * 32u, 16, 1024),
-                                       tc::smem_desc(Mb + kk * 32u, 16, 1024), idd, acc);
-                        tc::mma_ss_f16(tb + kColS0, tc::smem_desc(Ea + kk * 32u, 16, 1024),
-                                       tc::smem_desc(Kb + kk * 2048u, 16384, 1024), ide, acc);
+                        tc::mma_ss_f16(tb + kColU, tc::desc_adv(Da, kk * 32u), tc::desc_adv(Mb, kk * 32u), idd, acc);
+                        tc::mma_ss_f16(tb + kColS0, tc::desc_adv(Ea, kk * 32u), tc::desc_adv(Kb, kk * 2048u), ide, acc);
                     }
                 }
                 tc::commit(done_bar);
