@@ -74,9 +74,7 @@ __host__ __device__ constexpr unsigned vfill(int j, int nt) { return j + 1 == nt
 constexpr int kStageBytes = 32768;
 constexpr int kKChunk = kBN * 128;           // 16 KB: one 64-dim chunk of 128 keys
 constexpr int kVChunk = 64 * 128;            // 8 KB: one 64-dim chunk of 64 keys
-constexpr int kProdWarps = 4;                // warps 1-3 and 12
-constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kThreads = 416;                 // + 8 softmax warps (4-11)
+constexpr int kThreads = 320;                 // MMA warp, TMA warp, 8 softmax warps (2-9)
 constexpr int kMaxJobs = 64;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
@@ -94,6 +92,7 @@ struct PJob {
 
 struct PParams {
     PJob jobs[kMaxJobs];
+    const CUtensorMap *maps;    // per job: prepared Q, K cache, V cache (global memory)
     const unsigned *sched;      // (job << 26) | (head << 22) | query tile, grouped by CTA
     const int *cta_off;         // [grid + 1]
     unsigned *err;
@@ -147,7 +146,15 @@ __device__ __forceinline__ Item decode_item(const PParams &p, unsigned e)
     return it;
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// One box of a 3-D tensor map (in global memory) into shared memory, completion as transaction
+// bytes on `bar`. x (the innermost coordinate) is a multiple of 64 f16 elements here.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
 
 // 2^x on the special-function unit (flush-to-zero: results below 2^-126 become 0, which only
 // drops probabilities that are negligible against the row maximum).
@@ -304,10 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
     const int i0 = p.cta_off[blockIdx.x], i1 = p.cta_off[blockIdx.x + 1];
 
     if (tid == 0) {
-        mbar_init(smem_addr(&sm.q_full), kProdThreads);
+        mbar_init(smem_addr(&sm.q_full), 1);
         mbar_init(smem_addr(&sm.q_empty), 1);
         for (int s = 0; s < kStages; s++) {
-            mbar_init(smem_addr(&sm.kv_full[s]), kProdThreads);
+            mbar_init(smem_addr(&sm.kv_full[s]), 1);
             mbar_init(smem_addr(&sm.kv_empty[s]), 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -345,9 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 return ok;
             };
             auto acquire = [&](unsigned f) {                 // ring fill f loaded
-                if (!wait(sm.kv_full[f % kStages], (f / kStages) & 1))
+                if (!wait(sm.kv_full[f % kStages], (f / kStages) & 1))   // TMA writes: async proxy
                     return 0u;
-                fence_proxy_async();
                 return smem_addr(sm.kv[f % kStages]);
             };
             // O += P_g V_g; V_g occupies fills fv (keys 0-63) and fv + 1 (keys 64-127)
@@ -374,7 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
                 const Item it = decode_item(p, p.sched[idx]);
                 if (!wait(sm.q_full, nitem & 1))
                     break;
-                fence_proxy_async();
                 tc::fence_after_sync();
                 const unsigned fbase = fill;
                 for (int j = 0; j < it.nt && ok; j++) {
@@ -409,78 +414,70 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const __grid_
             tc::commit(smem_addr(&sm.drain));
             mbar_wait(smem_addr(&sm.drain), 0);
         }
-    } else if (warp <= 3 || warp >= 12) {
-        // ---------------------------------------------------------------- producers
-        const int pw = warp <= 3 ? warp - 1 : warp - 9;
-        const uint32_t lofs = (uint32_t)(lane >> 3);          // chunk of this lane's 8 dims
-        const uint32_t lu = (uint32_t)(lane & 7);             // 16-byte unit within the chunk
-        unsigned fill = 0, nitem = 0;
-        bool ok = true;
-        for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
-            const Item it = decode_item(p, p.sched[idx]);
-            const PJob &J = p.jobs[it.job];
-            if (nitem > 0 && !mbar_wait(smem_addr(&sm.q_empty), (nitem - 1) & 1)) {
-                if (lane == 0)
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- producer (TMA)
+        // One thread issues every tile copy: the Q tile as four 64-dim boxes of 128 rows, each
+        // K half as two 64-dim x 128-key boxes, each V half as four 64-dim x 64-key boxes. The
+        // tensor maps (one per job and tensor, in global memory) clip at the valid extent, so
+        // rows past the end of a prompt arrive as zeros; the hardware writes the 128-byte
+        // swizzle the MMAs read.
+        if (lane == 0) {
+            unsigned fill = 0, nitem = 0;
+            bool ok = true;
+            for (int idx = i0; idx < i1 && ok && !aborted(sm); idx++, nitem++) {
+                const Item it = decode_item(p, p.sched[idx]);
+                const CUtensorMap *mq = p.maps + 3 * it.job, *mk = mq + 1, *mv = mq + 2;
+                if (nitem > 0 && !mbar_wait(smem_addr(&sm.q_empty), (nitem - 1) & 1)) {
                     set_abort(p, sm);
-                ok = false;
-                break;
-            }
-            for (int r = pw; r < kBM; r += kProdWarps) {
-                const long long tok = it.t0 + (r < it.rows ? r : it.rows - 1);
-                const __half *src = J.qp + (tok * 16 + it.head) * kD + lane * 8;
-                cp_async16(sq + lofs * kChunkQ + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4), src);
-            }
-            cp_async_arrive(smem_addr(&sm.q_full));
-            for (int step = 0; step <= it.nt && ok; step++) {
-                for (int part = 0; part < 4; part++) {
-                    // step s: K_s (parts 0, 1) if s < nt, then V_{s-1} (parts 2, 3) if s >= 1
-                    const int j = part < 2 ? step : step - 1;
-                    if ((part < 2 && step == it.nt) || (part >= 2 && step == 0))
-                        continue;
-                    const int s = fill % kStages;
-                    const unsigned f = fill / kStages;
-                    if (f > 0 && !mbar_wait(smem_addr(&sm.kv_empty[s]), (f - 1) & 1)) {
-                        if (lane == 0)
+                    ok = false;
+                    break;
+                }
+                const uint32_t qb = smem_addr(&sm.q_full);
+                mbar_arrive_expect_tx(qb, kQBytes);
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+                    tma_load_3d(sq + c * kChunkQ, mq, 64 * c, it.head, (int)it.t0, qb);
+                for (int step = 0; step <= it.nt && ok; step++) {
+                    for (int part = 0; part < 4; part++) {
+                        // step s: K_s (parts 0, 1) if s < nt, then V_{s-1} (parts 2, 3) if s >= 1
+                        const int j = part < 2 ? step : step - 1;
+                        if ((part < 2 && step == it.nt) || (part >= 2 && step == 0))
+                            continue;
+                        const int s = fill % kStages;
+                        const unsigned f = fill / kStages;
+                        if (f > 0 && !mbar_wait(smem_addr(&sm.kv_empty[s]), (f - 1) & 1)) {
                             set_abort(p, sm);
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t st = smem_addr(sm.kv[s]);
-                    const long long key0 = (long long)j * kBN;
-                    if (part < 2) {
-                        // K half: dims [128 part, +128) of 128 keys; 16 lanes per key
-                        const uint32_t c = (uint32_t)(lane >> 3) & 1u, u = (uint32_t)(lane & 7);
-                        for (int r2 = pw; r2 < kBN / 2; r2 += kProdWarps) {
-                            const int r = 2 * r2 + (lane >> 4);
-                            long long key = key0 + r;
-                            if (key > it.kend - 1)
-                                key = it.kend - 1;                   // tail: a valid row, masked later
-                            cp_async16(st + c * kKChunk + r * 128 + ((u ^ (uint32_t)(r & 7)) << 4),
-                                       J.k_cache + (key * 2 + it.kvh) * kD + part * 128 + c * 64 + u * 8);
+                            ok = false;
+                            break;
                         }
-                    } else {
-                        // V half: keys [64 (part - 2), +64), all 256 dims; one warp per key
-                        for (int r = pw; r < 64; r += kProdWarps) {
-                            long long key = key0 + 64 * (part - 2) + r;
-                            if (key > it.kend - 1)
-                                key = it.kend - 1;
-                            cp_async16(st + lofs * kVChunk + r * 128 + ((lu ^ (uint32_t)(r & 7)) << 4),
-                                       J.v_cache + (key * 2 + it.kvh) * kD + lane * 8);
+                        const uint32_t st = smem_addr(sm.kv[s]), fb = smem_addr(&sm.kv_full[s]);
+                        const int key0 = j * kBN;
+                        mbar_arrive_expect_tx(fb, kStageBytes);
+                        if (part < 2) {
+                            // K half: dims [128 part, +128) of the tile's 128 keys
+                            tma_load_3d(st, mk, 128 * part, it.kvh, key0, fb);
+                            tma_load_3d(st + kKChunk, mk, 128 * part + 64, it.kvh, key0, fb);
+                        } else {
+                            // V half: keys [64 (part - 2), +64), all 256 dims
+#pragma unroll
+                            for (int c = 0; c < 4; c++)
+                                tma_load_3d(st + c * kVChunk, mv, 64 * c, it.kvh, key0 + 64 * (part - 2), fb);
                         }
+                        fill++;
                     }
-                    cp_async_arrive(smem_addr(&sm.kv_full[s]));
-                    fill++;
                 }
             }
+            // nothing of ours may still be landing when the CTA retires
+            for (unsigned f = fill > (unsigned)kStages ? fill - kStages : 0u; f < fill; f++)
+                mbar_wait(smem_addr(&sm.kv_full[f % kStages]), (f / kStages) & 1);
         }
-        cp_async_wait_all();     // nothing of ours may still be landing when the CTA retires
     } else {
         // ---------------------------------------------------------------- softmax + epilogue
-        // Two warps per query row: warps 4-7 take score columns 0-63 (and output dims 0-127),
-        // warps 8-11 columns 64-127 (dims 128-255). Both read the whole row for its max, so the
+        // Two warps per query row: warps 2-5 take score columns 0-63 (and output dims 0-127),
+        // warps 6-9 columns 64-127 (dims 128-255); warp w owns TMEM lanes 32 (w % 4) ... Both read the whole row for its max, so the
         // pair agrees on it without exchanging values (a pair barrier then keeps P writes behind
         // both reads); the row sums meet in shared memory once per query tile.
-        const int half = warp >= 8 ? 1 : 0;
+        const int half = warp >= 6 ? 1 : 0;
         const int row = (warp & 3) * 32 + lane;            // query row = TMEM lane
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
         const int c0 = 64 * half;
@@ -727,14 +724,35 @@ int prefill_launch(const KernelAttnPrefillJob *jobs, int n)
     const size_t qp_bytes = (size_t)total_t * 16 * kD * sizeof(__half);
     const size_t sched_off = (qp_bytes + 255) / 256 * 256;
     const size_t off_off = sched_off + (sched.size() * 4 + 255) / 256 * 256;
-    unsigned char *ws = static_cast<unsigned char *>(scratch(off_off + off.size() * 4));
+    const size_t maps_off = (off_off + off.size() * 4 + 255) / 256 * 256;
+    unsigned char *ws = static_cast<unsigned char *>(scratch(maps_off + (size_t)n * 3 * sizeof(CUtensorMap)));
     if (!ws)
         return -1;
+    // tensor maps: per job the prepared queries [T][16][256], and the K and V windows
+    // [kbase + T][2][256] (f16), each clipped at its valid extent
+    std::vector<CUtensorMap> maps((size_t)n * 3);
+    {
+        long long t0 = 0;
+        for (int i = 0; i < n; i++) {
+            const KernelAttnPrefillJob &s = jobs[i];
+            const uint64_t qdims[3] = {256, 16, (uint64_t)s.T}, qstr[2] = {512, 8192};
+            const uint64_t kdims[3] = {256, 2, (uint64_t)(s.kbase + s.T)}, kstr[2] = {512, 1024};
+            const uint32_t qbox[3] = {64, 1, kBM}, kbox[3] = {64, 1, kBN}, vbox[3] = {64, 1, 64};
+            const __half *qpi = reinterpret_cast<const __half *>(ws) + t0 * 16 * kD;
+            if (encode_tmap_f16_3d(&maps[3 * i], qpi, qdims, qstr, qbox) != 0 ||
+                encode_tmap_f16_3d(&maps[3 * i + 1], s.k_cache, kdims, kstr, kbox) != 0 ||
+                encode_tmap_f16_3d(&maps[3 * i + 2], s.v_cache, kdims, kstr, vbox) != 0)
+                return -1;
+            t0 += (long long)s.T;
+        }
+    }
     cudaStream_t st = R.stream;
     if (check(cudaMemcpyAsync(ws + sched_off, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice, st),
               "prefill schedule") != 0 ||
         check(cudaMemcpyAsync(ws + off_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, st),
-              "prefill schedule offsets") != 0)
+              "prefill schedule offsets") != 0 ||
+        check(cudaMemcpyAsync(ws + maps_off, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice,
+                              st), "prefill tensor maps") != 0)
         return -1;
 
     PrepParams pp;
@@ -778,6 +796,7 @@ int prefill_launch(const KernelAttnPrefillJob *jobs, int n)
     prefill_prep_kernel<<<(unsigned)total_t, 256, 0, st>>>(pp);
     if (launched("prefill_prep_kernel") != 0)
         return -1;
+    ap.maps = reinterpret_cast<const CUtensorMap *>(ws + maps_off);
     ap.sched = reinterpret_cast<const unsigned *>(ws + sched_off);
     ap.cta_off = reinterpret_cast<const int *>(ws + off_off);
     ap.err = R.err_word;

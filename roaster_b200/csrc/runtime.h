@@ -3,6 +3,7 @@
 // C-ABI (include/roaster_cuda.h is).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -50,6 +51,11 @@ int *counters(size_t n);
 void *dstage(size_t bytes);
 // Pinned host staging of at least `bytes` (grow-only; growing synchronises the stream).
 void *pinned(size_t bytes);
+// Encode a tiled tensor map for a 3-D f16 tensor in global memory (dims innermost first,
+// strides in bytes of dims 1 and 2), 128-byte swizzle, zero fill outside the tensor. The map is
+// plain data (128 bytes) that kernels read from global memory. 0 = ok.
+int encode_tmap_f16_3d(CUtensorMap *map, const void *base, const uint64_t dims[3], const uint64_t strides[2],
+                       const uint32_t box[3]);
 // 16-byte alignment check for pointers handed to bulk-copy engines.
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
