@@ -231,6 +231,54 @@ int kernel_deltanet_prefill_batch(const KernelDeltaPrefillJob *jobs, int n);
 int kernel_deltanet_prefill(float *state, size_t T, const float *q, const float *k, const float *v,
                             const float *g, const float *beta, float *out);
 
+/* ------------------------------------------------------------ Gated DeltaNet pre/post ops
+ * Pre-ops (model.c:1291-1328 for a decode token; pf_ssm's prep loop 1619-1643 for a prompt), per
+ * token t of a recurrent layer: depthwise causal conv1d (kernel 4) of the qkv projection over
+ * the 3-token history (kernel_conv1d_causal_f32, kernels.c:693-719), SiLU, history shift, split
+ * into q | k | v with q, k L2-normalised per 128 (eps 1e-6), beta' = sigmoid(beta) and
+ * g = a * softplus(alpha + dt) (softplus(x) = x above 20). T = 1 is a decode step; T > 1 runs
+ * the tokens in order (token t's conv sees the raw inputs of t-3 .. t-1). */
+typedef struct {
+    const float *qkv;           /* device, [T][8192] raw projection */
+    const float *alpha, *beta;  /* device, [T][32] raw projections */
+    float *conv_state;          /* device, [3][8192] history (oldest row first), updated */
+    const float *conv_w;        /* device, [8192][4] (ssm_conv1d.weight), 16-byte aligned */
+    const float *dt, *a;        /* device, [32] */
+    float *q, *k;               /* device out, [T][16][128] */
+    float *v;                   /* device out, [T][32][128] */
+    float *g, *beta_out;        /* device out, [T][32] */
+    size_t T;
+} KernelDeltaPreopJob;
+
+/* Device-pointer batch (one job per layer and slot/prompt). Asynchronous. */
+int kernel_deltanet_preop_batch(const KernelDeltaPreopJob *jobs, int n);
+
+/* Post-op (model.c:1333-1343; pf_ssm 1655-1658): per (token, value head) row of 128,
+ * out = rmsnorm(out) * norm_w (eps 1e-6) * z * sigmoid(z), in place. */
+typedef struct {
+    float *out;                 /* device, [T][32][128], 16-byte aligned, updated */
+    const float *z;             /* device, [T][4096] gate projection */
+    const float *norm_w;        /* device, [128] (ssm_norm.weight) */
+    size_t T;
+} KernelDeltaPostopJob;
+
+int kernel_deltanet_postop_batch(const KernelDeltaPostopJob *jobs, int n);
+
+/* The whole recurrent-layer block of a decode step, model.c:1291-1343 without the projections:
+ * pre-ops, the delta-rule step, gated RMSNorm. Host qkv [8192], z [4096], alpha, beta [32] in;
+ * host out [4096] (before ssm_out). Device-resident state [32][128][128], conv_state [3][8192],
+ * conv_w [8192][4], dt, a [32], ssm_norm [128]. Synchronous. */
+int kernel_deltanet_layer_step(float *state, float *conv_state, const float *conv_w, const float *dt,
+                               const float *a, const float *ssm_norm, const float *qkv, const float *z,
+                               const float *alpha, const float *beta, float *out);
+
+/* The same for a prompt of T tokens: pf_ssm (model.c:1604-1660) without its projections, the
+ * recurrence in the chunked tensor-core form. Host qkv [T][8192], z [T][4096], alpha, beta
+ * [T][32]; host out [T][4096]. Synchronous. */
+int kernel_deltanet_layer_prefill(float *state, float *conv_state, const float *conv_w, const float *dt,
+                                  const float *a, const float *ssm_norm, size_t T, const float *qkv,
+                                  const float *z, const float *alpha, const float *beta, float *out);
+
 #ifdef __cplusplus
 }
 #endif

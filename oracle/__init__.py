@@ -66,6 +66,10 @@ def _load(which: str):
         lib.orc_delta_step.restype = None
         lib.orc_delta_prefill.argtypes = [_fp, C.c_size_t] + [_fp] * 6
         lib.orc_delta_prefill.restype = None
+        lib.orc_delta_preop.argtypes = [C.c_size_t] + [_fp] * 12
+        lib.orc_delta_preop.restype = None
+        lib.orc_delta_postop.argtypes = [C.c_size_t, _fp, _fp, _fp]
+        lib.orc_delta_postop.restype = None
         lib.orc_f32_to_f16.argtypes = [C.c_float]
         lib.orc_f32_to_f16.restype = C.c_uint16
     else:
@@ -78,6 +82,8 @@ def _load(which: str):
         lib.ref_delta_step.restype = None
         lib.ref_delta_prefill.argtypes = [_fp, C.c_int] + [_fp] * 6
         lib.ref_delta_prefill.restype = None
+        lib.ref_delta_layer_prefill.argtypes = [C.c_int] + [_fp] * 11
+        lib.ref_delta_layer_prefill.restype = C.c_int
         lib.ref_decode_ctx_new.argtypes = [C.c_size_t, _fp, _fp]
         lib.ref_decode_ctx_new.restype = C.c_void_p
         lib.ref_decode_ctx_k.argtypes = [C.c_void_p]
@@ -274,6 +280,50 @@ def delta_prefill(state, q, k, v, g, beta, impl: str = "port"):
         _load("port").orc_delta_prefill(_f(state), T, *[_f(a) for a in args], _f(out))
     else:
         _load("ref").ref_delta_prefill(_f(state), T, *[_f(a) for a in args], _f(out))
+    return out
+
+
+def delta_preop(qkv, alpha, beta, conv_state, conv_w, dt, a):
+    """Pre-ops of one recurrent layer over T tokens (model.c:1293-1328 per token).
+    qkv [T,8192], alpha/beta [T,32]; conv_state [3,8192] fp32 is updated IN PLACE; conv_w
+    [8192,4]; dt, a [32]. Returns dict q, k [T,16,128], v [T,32,128], g, beta [T,32]."""
+    assert conv_state.dtype == np.float32 and conv_state.flags.c_contiguous
+    qkv, alpha, beta, conv_w, dt, a = [np.ascontiguousarray(x, np.float32)
+                                       for x in (qkv, alpha, beta, conv_w, dt, a)]
+    T = qkv.shape[0]
+    o = {"q": np.zeros((T, 16, 128), np.float32), "k": np.zeros((T, 16, 128), np.float32),
+         "v": np.zeros((T, 32, 128), np.float32), "g": np.zeros((T, 32), np.float32),
+         "beta": np.zeros((T, 32), np.float32)}
+    _load("port").orc_delta_preop(T, _f(qkv), _f(alpha), _f(beta), _f(conv_state), _f(conv_w),
+                                  _f(dt), _f(a), _f(o["q"]), _f(o["k"]), _f(o["v"]), _f(o["g"]),
+                                  _f(o["beta"]))
+    return o
+
+
+def delta_postop(out, z, w):
+    """Gated RMSNorm (model.c:1333-1343) of rows of 128: returns a new array."""
+    x = np.ascontiguousarray(out, np.float32).copy()
+    z = np.ascontiguousarray(z, np.float32)
+    _load("port").orc_delta_postop(x.size // 128, _f(x), _f(z), _f(np.ascontiguousarray(w, np.float32)))
+    return x
+
+
+def delta_layer(state, conv_state, qkv, z, alpha, beta, conv_w, dt, a, ssm_norm, impl: str = "port"):
+    """One recurrent layer over T tokens: pre-ops, the delta rule, gated RMSNorm -- pf_ssm
+    (model.c:1604-1660) without its projections. state [32,128,128] and conv_state [3,8192]
+    are updated IN PLACE. Returns out [T,32,128]. impl="ref" drives the reference's pf_ssm
+    itself (T <= 256)."""
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    T = qkv.shape[0]
+    if impl == "port":
+        p = delta_preop(qkv, alpha, beta, conv_state, conv_w, dt, a)
+        out = delta_prefill(state, p["q"], p["k"], p["v"], p["g"], p["beta"])
+        return delta_postop(out, z, ssm_norm).reshape(T, 32, 128)
+    out = np.zeros((T, 32, 128), np.float32)
+    args = [np.ascontiguousarray(x, np.float32) for x in (z, alpha, beta, conv_w, dt, a, ssm_norm)]
+    rc = _load("ref").ref_delta_layer_prefill(T, _f(qkv), *[_f(x) for x in args], _f(state),
+                                              _f(conv_state), _f(out))
+    assert rc == 0, "ref_delta_layer_prefill failed"
     return out
 
 

@@ -297,6 +297,83 @@ void ref_delta_prefill(float *state, int T, const float *q, const float *k, cons
     }
 }
 
+/* ---- a whole Gated DeltaNet layer through pf_ssm (model.c:1604-1660).
+ * The four projections are one-hot f32 matvecs: token t's normed row is e_t and column t of
+ * W_qkv / W_gate / W_alpha / W_beta holds its qkv [8192], z [4096], alpha [32], beta [32]. pf_ssm
+ * then runs, on exactly those inputs, its per-token conv1d + SiLU + L2-norm + beta/g prep
+ * (1619-1643), the delta_head recurrence (1644-1658) and the gated RMSNorm (1655-1658). The
+ * layer output is read from the prefill scratch (g_pf.rec) before the ssm_out projection.
+ * T <= 256. state [32][128][128] and conv_state [3][8192] are updated in place. */
+#define DN_LAYER 0                                  /* (0+1) % 4 != 0: a recurrent layer */
+static TensorInfo t_qkv, t_gate, t_al, t_be, t_so;
+static float *W_qkv, *W_gate, *W_al, *W_be, *W_so;
+
+static void set_col_n(float *W, size_t rows, size_t col, const float *x)
+{
+    for (size_t r = 0; r < rows; r++)
+        W[r * MODEL_HIDDEN_SIZE + col] = x[r];
+}
+
+int ref_delta_layer_prefill(int T, const float *qkv, const float *z, const float *alpha,
+                            const float *beta, const float *conv_w, const float *dt, const float *a,
+                            const float *ssm_norm, float *state, float *conv_state, float *out)
+{
+    if (T <= 0 || T > PF_MAX_T || ensure_weights() != 0)
+        return -1;
+    if (!W_qkv) {
+        W_qkv = calloc((size_t)MODEL_LINEAR_QKV_SIZE * MODEL_HIDDEN_SIZE, sizeof(float));
+        W_gate = calloc((size_t)MODEL_LINEAR_GATE_SIZE * MODEL_HIDDEN_SIZE, sizeof(float));
+        W_al = calloc((size_t)MODEL_LINEAR_V_HEADS * MODEL_HIDDEN_SIZE, sizeof(float));
+        W_be = calloc((size_t)MODEL_LINEAR_V_HEADS * MODEL_HIDDEN_SIZE, sizeof(float));
+        W_so = calloc((size_t)MODEL_HIDDEN_SIZE * MODEL_LINEAR_V_SIZE, sizeof(float));
+        if (!W_qkv || !W_gate || !W_al || !W_be || !W_so)
+            return -1;
+        t_qkv.type = t_gate.type = t_al.type = t_be.type = t_so.type = 0;
+    }
+    LayerRefs *L = &R->layer[DN_LAYER];
+    L->qkv = (TRef){ &t_qkv, W_qkv };
+    L->gate = (TRef){ &t_gate, W_gate };
+    L->alpha = (TRef){ &t_al, W_al };
+    L->beta = (TRef){ &t_be, W_be };
+    L->ssm_out = (TRef){ &t_so, W_so };
+    L->conv = conv_w;
+    L->dt = dt;
+    L->a = a;
+    L->ssm_norm = ssm_norm;
+    static SSMState ss[MODEL_NUM_LAYERS];
+    memset(ss, 0, sizeof(ss));
+    ss[DN_LAYER].state = state;
+    ss[DN_LAYER].conv_state = conv_state;
+    ss[DN_LAYER].state_elements = (size_t)MODEL_LINEAR_V_HEADS * 128 * 128;
+    ss[DN_LAYER].conv_elements = (size_t)(MODEL_SSM_CONV_KERNEL - 1) * MODEL_LINEAR_QKV_SIZE;
+    static Model m;
+    memset(&m, 0, sizeof(m));
+    m.refs = R;
+    m.ssm_state = ss;
+    m.initialized = true;
+    if (pf_ensure((size_t)T) != 0)
+        return -1;
+    memset(g_pf.nrm, 0, (size_t)T * PF_H * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        g_pf.nrm[(size_t)t * PF_H + (size_t)t] = 1.0f;
+        set_col_n(W_qkv, MODEL_LINEAR_QKV_SIZE, (size_t)t, qkv + (size_t)t * MODEL_LINEAR_QKV_SIZE);
+        set_col_n(W_gate, MODEL_LINEAR_GATE_SIZE, (size_t)t, z + (size_t)t * MODEL_LINEAR_GATE_SIZE);
+        set_col_n(W_al, MODEL_LINEAR_V_HEADS, (size_t)t, alpha + (size_t)t * MODEL_LINEAR_V_HEADS);
+        set_col_n(W_be, MODEL_LINEAR_V_HEADS, (size_t)t, beta + (size_t)t * MODEL_LINEAR_V_HEADS);
+    }
+    const int rc = pf_ssm(&m, DN_LAYER, T);
+    if (rc == 0)
+        memcpy(out, g_pf.rec, (size_t)T * MODEL_LINEAR_V_SIZE * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        const float zero[MODEL_LINEAR_QKV_SIZE] = {0};
+        set_col_n(W_qkv, MODEL_LINEAR_QKV_SIZE, (size_t)t, zero);
+        set_col_n(W_gate, MODEL_LINEAR_GATE_SIZE, (size_t)t, zero);
+        set_col_n(W_al, MODEL_LINEAR_V_HEADS, (size_t)t, zero);
+        set_col_n(W_be, MODEL_LINEAR_V_HEADS, (size_t)t, zero);
+    }
+    return rc;
+}
+
 int ref_max_threads(void)
 {
 #ifdef _OPENMP

@@ -446,3 +446,70 @@ void orc_delta_prefill(float *state, size_t T, const float *q, const float *k, c
                       beta[t * ORC_DN_VH + vh], out + (t * ORC_DN_VH + vh) * ORC_DN_D);
     }
 }
+
+/* ---------------------------------------------------------------- Gated DeltaNet pre/post ops */
+
+/* Logistic function in the form that never overflows exp (kernel_sigmoid, kernels.c:628-638). */
+static float orc_sigmoid(float x)
+{
+    if (x >= 0.0f)
+        return 1.0f / (1.0f + expf(-x));
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+
+/* Pre-ops of one recurrent layer for T consecutive tokens: the decode block model.c:1293-1328
+ * applied token by token, which is also pf_ssm's prep loop (model.c:1619-1643).
+ *   conv:  cv[c] = sum_{j<3} hist[j][c] w[c][j] + in[c] w[c][3]     (kernel_conv1d_causal_f32,
+ *          kernels.c:693-719; hist holds the 3 previous raw inputs, oldest first)
+ *   SiLU:  cv[c] *= sigmoid(cv[c])                                  (kernels.c:644-651)
+ *   history: hist <- [hist[1], hist[2], in]                         (model.c:1299-1306)
+ *   q = cv[0:2048], k = cv[2048:4096] L2-normalised per 128 (eps 1e-6, kernels.c:607-622),
+ *   v = cv[4096:8192]; beta' = sigmoid(beta), g = a softplus(alpha + dt) with softplus(x) = x
+ *   for x > 20 (model.c:1324-1328).
+ * qkv [T][8192], alpha/beta [T][32] in; conv_state [3][8192] updated; conv_w [8192][4];
+ * q, k [T][16][128], v [T][32][128], g, b [T][32] out. */
+void orc_delta_preop(size_t T, const float *qkv, const float *alpha, const float *beta,
+                     float *conv_state, const float *conv_w, const float *dt, const float *a,
+                     float *q, float *k, float *v, float *g, float *b)
+{
+    const size_t Q = 8192;
+    float *cv = malloc(Q * sizeof(float));
+    for (size_t t = 0; t < T; t++) {
+        const float *in = qkv + t * Q;
+        for (size_t c = 0; c < Q; c++) {
+            float sum = 0.0f;
+            for (size_t j = 0; j < 3; j++)
+                sum += conv_state[j * Q + c] * conv_w[c * 4 + j];
+            sum += in[c] * conv_w[c * 4 + 3];
+            cv[c] = sum * orc_sigmoid(sum);
+        }
+        memmove(conv_state, conv_state + Q, 2 * Q * sizeof(float));
+        memcpy(conv_state + 2 * Q, in, Q * sizeof(float));
+        for (int h = 0; h < 16; h++) {
+            orc_l2norm(q + (t * 16 + h) * 128, cv + h * 128, 128, 1e-6f);
+            orc_l2norm(k + (t * 16 + h) * 128, cv + 2048 + h * 128, 128, 1e-6f);
+        }
+        memcpy(v + t * 4096, cv + 4096, 4096 * sizeof(float));
+        for (int h = 0; h < 32; h++) {
+            b[t * 32 + h] = 1.0f / (1.0f + expf(-beta[t * 32 + h]));
+            const float x = alpha[t * 32 + h] + dt[h];
+            g[t * 32 + h] = a[h] * (x > 20.0f ? x : log1pf(expf(x)));
+        }
+    }
+    free(cv);
+}
+
+/* Gated RMSNorm of `rows` value-head rows (model.c:1333-1343, pf_ssm 1655-1658): per row of 128,
+ * out = rmsnorm(out) * w (eps 1e-6), then out *= z sigmoid(z). */
+void orc_delta_postop(size_t rows, float *out, const float *z, const float *w)
+{
+    for (size_t r = 0; r < rows; r++) {
+        float *x = out + r * 128;
+        const float *zr = z + r * 128;
+        orc_rmsnorm(x, x, w, 128, 1e-6f);
+        for (int j = 0; j < 128; j++)
+            x[j] *= zr[j] * (1.0f / (1.0f + expf(-zr[j])));
+    }
+}
+

@@ -94,6 +94,17 @@ void orc_delta_step(float *state, const float *q, const float *k, const float *v
 void orc_delta_prefill(float *state, size_t T, const float *q, const float *k, const float *v,
                        const float *g, const float *beta, float *out);
 
+/* Pre-ops of one recurrent layer for T consecutive tokens (model.c:1293-1328 per token; pf_ssm
+ * 1619-1643): causal conv1d over the 3-token history + SiLU, history shift, q/k L2-norm, beta
+ * sigmoid, g = a softplus(alpha + dt). qkv [T][8192]; alpha, beta [T][32]; conv_state [3][8192]
+ * (updated); conv_w [8192][4]; dt, a [32]. Out: q, k [T][16][128], v [T][32][128], g, b [T][32]. */
+void orc_delta_preop(size_t T, const float *qkv, const float *alpha, const float *beta,
+                     float *conv_state, const float *conv_w, const float *dt, const float *a,
+                     float *q, float *k, float *v, float *g, float *b);
+
+/* Gated RMSNorm post-op (model.c:1333-1343) over `rows` rows of 128, in place. */
+void orc_delta_postop(size_t rows, float *out, const float *z, const float *w);
+
 #ifdef __cplusplus
 }
 #endif

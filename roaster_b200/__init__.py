@@ -61,6 +61,18 @@ class KernelDeltaPrefillJob(C.Structure):
                 ("out", _vp), ("T", _sz)]
 
 
+class KernelDeltaPreopJob(C.Structure):
+    """Mirror of ``KernelDeltaPreopJob`` (include/roaster_cuda.h)."""
+    _fields_ = [("qkv", _vp), ("alpha", _vp), ("beta", _vp), ("conv_state", _vp), ("conv_w", _vp),
+                ("dt", _vp), ("a", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp),
+                ("beta_out", _vp), ("T", _sz)]
+
+
+class KernelDeltaPostopJob(C.Structure):
+    """Mirror of ``KernelDeltaPostopJob`` (include/roaster_cuda.h)."""
+    _fields_ = [("out", _vp), ("z", _vp), ("norm_w", _vp), ("T", _sz)]
+
+
 _lib = None
 
 
@@ -101,6 +113,10 @@ def lib():
         "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_prefill_batch": (C.c_int, [C.POINTER(KernelDeltaPrefillJob), C.c_int]),
         "kernel_deltanet_prefill": (C.c_int, [_vp, _sz] + [_vp] * 6),
+        "kernel_deltanet_preop_batch": (C.c_int, [C.POINTER(KernelDeltaPreopJob), C.c_int]),
+        "kernel_deltanet_postop_batch": (C.c_int, [C.POINTER(KernelDeltaPostopJob), C.c_int]),
+        "kernel_deltanet_layer_step": (C.c_int, [_vp] * 11),
+        "kernel_deltanet_layer_prefill": (C.c_int, [_vp] * 6 + [_sz] + [_vp] * 5),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -226,3 +242,18 @@ def deltanet_step_batch(jobs) -> None:
 def deltanet_prefill_batch(jobs) -> None:
     arr, n = _arr(KernelDeltaPrefillJob, jobs)
     check(lib().kernel_deltanet_prefill_batch(arr, n), "kernel_deltanet_prefill_batch")
+
+
+def deltanet_preop_batch(jobs) -> None:
+    js = [j if isinstance(j, KernelDeltaPreopJob) else KernelDeltaPreopJob(*[_ptr(x) for x in j[:-1]], int(j[-1]))
+          for j in jobs]
+    arr, n = _arr(KernelDeltaPreopJob, js)
+    check(lib().kernel_deltanet_preop_batch(arr, n), "kernel_deltanet_preop_batch")
+
+
+def deltanet_postop_batch(jobs) -> None:
+    js = [j if isinstance(j, KernelDeltaPostopJob) else KernelDeltaPostopJob(*[_ptr(x) for x in j[:-1]], int(j[-1]))
+          for j in jobs]
+    arr, n = _arr(KernelDeltaPostopJob, js)
+    check(lib().kernel_deltanet_postop_batch(arr, n), "kernel_deltanet_postop_batch")
+

@@ -88,6 +88,20 @@ def delta_prompt(seed: int, T: int):
     return {"q": q.astype(np.float32), "k": k.astype(np.float32), "v": v, "beta": beta, "g": g}
 
 
+def delta_layer_inputs(seed: int, T: int):
+    """Raw inputs of one recurrent layer (before its pre-ops) for T tokens: qkv [T,8192] and z
+    [T,4096] ~ N(0,1); alpha, beta [T,32] ~ N(0,1); conv_w [8192,4] ~ 0.5 N(0,1); dt ~ N(0,1);
+    a = -exp(N(-1, 0.5)) [32]; ssm_norm ~ 1 + 0.1 N(0,1) [128]; conv_state [3,8192] ~ N(0,1)."""
+    rng = np.random.default_rng(seed)
+    return {
+        "qkv": _n(rng, T, 8192), "z": _n(rng, T, 4096), "alpha": _n(rng, T, 32), "beta": _n(rng, T, 32),
+        "conv_w": (0.5 * rng.standard_normal((8192, 4))).astype(np.float32),
+        "dt": _n(rng, 32), "a": (-np.exp(rng.normal(-1.0, 0.5, 32))).astype(np.float32),
+        "ssm_norm": (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32),
+        "conv_state": _n(rng, 3, 8192),
+    }
+
+
 def slot_lengths(seed: int, slots: int, lo: int = 1024, hi: int = 32768):
     """Config 2: per-slot context lengths ~ U[lo, hi] (integers, inclusive)."""
     rng = np.random.default_rng(seed)

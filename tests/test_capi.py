@@ -23,7 +23,7 @@ def test_library_exports_every_declared_symbol():
 def test_header_compiles_as_c(tmp_path):
     src = tmp_path / "t.c"
     src.write_text('#include "roaster_cuda.h"\nint main(void){ KernelAttnDecodeJob j; '
-                   'KernelDeltaStepJob d; KernelDeltaPrefillJob e; (void)j; (void)d; (void)e; return 0; }\n')
+                   'KernelDeltaStepJob d; KernelDeltaPrefillJob e; KernelDeltaPreopJob f; KernelDeltaPostopJob g; (void)j; (void)d; (void)e; (void)f; (void)g; return 0; }\n')
     inc = os.path.join(os.path.dirname(R.LIB_PATH), "..", "include")
     out = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", inc, str(src), "-o",
                           str(tmp_path / "t")], capture_output=True, text=True)
@@ -39,6 +39,8 @@ def test_struct_layouts_match_c(tmp_path):
                    'sizeof(KernelDeltaStepJob), offsetof(KernelAttnDecodeJob, out), '
                    'sizeof(KernelAttnPrefillJob), offsetof(KernelAttnPrefillJob, dtype), '
                    'sizeof(KernelDeltaPrefillJob), offsetof(KernelDeltaPrefillJob, T)); '
+                   'printf("%zu %zu %zu %zu\\n", sizeof(KernelDeltaPreopJob), offsetof(KernelDeltaPreopJob, T), '
+                   'sizeof(KernelDeltaPostopJob), offsetof(KernelDeltaPostopJob, T)); '
                    'return 0; }\n')
     inc = os.path.join(os.path.dirname(R.LIB_PATH), "..", "include")
     exe = tmp_path / "s"
@@ -47,7 +49,9 @@ def test_struct_layouts_match_c(tmp_path):
     assert vals == [C.sizeof(R.KernelAttnDecodeJob), R.KernelAttnDecodeJob.append.offset,
                     C.sizeof(R.KernelDeltaStepJob), R.KernelAttnDecodeJob.out.offset,
                     C.sizeof(R.KernelAttnPrefillJob), R.KernelAttnPrefillJob.dtype.offset,
-                    C.sizeof(R.KernelDeltaPrefillJob), R.KernelDeltaPrefillJob.T.offset]
+                    C.sizeof(R.KernelDeltaPrefillJob), R.KernelDeltaPrefillJob.T.offset,
+                    C.sizeof(R.KernelDeltaPreopJob), R.KernelDeltaPreopJob.T.offset,
+                    C.sizeof(R.KernelDeltaPostopJob), R.KernelDeltaPostopJob.T.offset]
 
 
 def _has_gpu():

@@ -111,3 +111,21 @@ def test_partial_merge_identity(oracle_lib):
     w = [p[1] * np.exp(p[0] - M) for p in parts]
     o = sum(wi[:, None] * p[2] for wi, p in zip(w, parts)) / sum(w)[:, None]
     assert O.maxrel(o, full[2]) < 1e-5
+
+
+@pytest.mark.parametrize("T", [1, 2, 7, 70])
+def test_port_vs_reference_delta_layer(oracle_lib, T):
+    """The oracle's pre-ops + recurrence + gated RMSNorm equal the reference's own pf_ssm
+    (model.c:1604-1660, driven with one-hot f32 projections) bit for bit."""
+    if not O.have_ref():
+        pytest.skip("reference build (oracle/_ref) not present")
+    d = synth.delta_layer_inputs(10 + T, T)
+    st0 = synth.delta_state(11, 1)[0]
+    s1, c1 = st0.copy(), d["conv_state"].copy()
+    s2, c2 = st0.copy(), d["conv_state"].copy()
+    args = (d["qkv"], d["z"], d["alpha"], d["beta"], d["conv_w"], d["dt"], d["a"], d["ssm_norm"])
+    a = O.delta_layer(s1, c1, *args, impl="port")
+    b = O.delta_layer(s2, c2, *args, impl="ref")
+    assert np.array_equal(a, b)
+    assert np.array_equal(s1, s2)
+    assert np.array_equal(c1, c2)
