@@ -279,6 +279,43 @@ int kernel_deltanet_layer_prefill(float *state, float *conv_state, const float *
                                   const float *a, const float *ssm_norm, size_t T, const float *qkv,
                                   const float *z, const float *alpha, const float *beta, float *out);
 
+/* ------------------------------------------------------------ attention window (device KV)
+ * The attention window of one slot with its K/V in device memory (f16 [ctx][2][256] per
+ * attention layer) and the policy of kvwindow.c: a kept head (slide_keep / slide_pin), sliding
+ * in blocks of a quarter of the free window when full, evicted tokens pushed to a spill store in
+ * kvspill.c's fp32 chunk format (a file when `spill_path` is non-empty, host memory otherwise),
+ * restore / rollback / context changes as in kvwindow.c:1-268 and model_set_context
+ * (model.c:1870-1899). Calls are synchronous with respect to the host (the spill moves data). */
+typedef struct KernelKvWindow KernelKvWindow;
+
+/* NULL on failure (kernel_cuda_last_error()). layers <= 64. */
+KernelKvWindow *kernel_kvw_create(int layers, size_t ctx, int slide, size_t keep, size_t pin,
+                                  const char *spill_path);
+void kernel_kvw_destroy(KernelKvWindow *w);
+int kernel_kvw_set_policy(KernelKvWindow *w, int slide, size_t keep, size_t pin);
+
+/* Device K/V of attention layer `layer` (0-based among the window's layers); the pointers change
+ * when the context size changes. */
+uint16_t *kernel_kvw_k(KernelKvWindow *w, int layer);
+uint16_t *kernel_kvw_v(KernelKvWindow *w, int layer);
+
+size_t kernel_kvw_len(const KernelKvWindow *w);        /* kvw_len: tokens in the window */
+size_t kernel_kvw_spilled(const KernelKvWindow *w);    /* kvw_spilled */
+size_t kernel_kvw_head(const KernelKvWindow *w);       /* kvw_head */
+size_t kernel_kvw_max_chunk(const KernelKvWindow *w);  /* kvw_max_chunk */
+size_t kernel_kvw_position(const KernelKvWindow *w);   /* absolute position of the next token */
+size_t kernel_kvw_context(const KernelKvWindow *w);    /* context_length */
+
+/* kvw_ensure_room: make room for `need` more tokens (sliding if enabled). Then the attention
+ * kernels append at index kernel_kvw_len() (position kernel_kvw_position()), and
+ * kernel_kvw_appended(w, need) records them. */
+int kernel_kvw_ensure_room(KernelKvWindow *w, size_t need);
+int kernel_kvw_appended(KernelKvWindow *w, size_t n);
+int kernel_kvw_evict(KernelKvWindow *w, size_t n);                    /* kvw_evict */
+int kernel_kvw_restore(KernelKvWindow *w, size_t n);                  /* kvw_restore */
+int kernel_kvw_rollback(KernelKvWindow *w, size_t p0, size_t s0);     /* kvw_rollback */
+int kernel_kvw_set_context(KernelKvWindow *w, size_t ctx);            /* model_set_context's window part */
+
 #ifdef __cplusplus
 }
 #endif

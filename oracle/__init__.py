@@ -84,6 +84,24 @@ def _load(which: str):
         lib.ref_delta_prefill.restype = None
         lib.ref_delta_layer_prefill.argtypes = [C.c_int] + [_fp] * 11
         lib.ref_delta_layer_prefill.restype = C.c_int
+        lib.ref_kvw_new.argtypes = [C.c_size_t, C.c_int, C.c_size_t, C.c_size_t, C.c_char_p]
+        lib.ref_kvw_new.restype = C.c_void_p
+        lib.ref_kvw_free.argtypes = [C.c_void_p]
+        lib.ref_kvw_free.restype = None
+        lib.ref_kvw_layers.argtypes = [C.c_void_p]
+        lib.ref_kvw_layers.restype = C.c_int
+        lib.ref_kvw_append.argtypes = [C.c_void_p, C.c_size_t, _fp, _fp]
+        lib.ref_kvw_append.restype = C.c_int
+        for nm in ("evict", "restore", "set_context"):
+            getattr(lib, "ref_kvw_" + nm).argtypes = [C.c_void_p, C.c_size_t]
+            getattr(lib, "ref_kvw_" + nm).restype = C.c_int
+        lib.ref_kvw_rollback.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t]
+        lib.ref_kvw_rollback.restype = C.c_int
+        for nm in ("len", "spilled", "head", "max_chunk", "position", "context"):
+            getattr(lib, "ref_kvw_" + nm).argtypes = [C.c_void_p]
+            getattr(lib, "ref_kvw_" + nm).restype = C.c_size_t
+        lib.ref_kvw_read.argtypes = [C.c_void_p, C.c_int, _fp, _fp]
+        lib.ref_kvw_read.restype = None
         lib.ref_decode_ctx_new.argtypes = [C.c_size_t, _fp, _fp]
         lib.ref_decode_ctx_new.restype = C.c_void_p
         lib.ref_decode_ctx_k.argtypes = [C.c_void_p]
@@ -325,6 +343,52 @@ def delta_layer(state, conv_state, qkv, z, alpha, beta, conv_w, dt, a, ssm_norm,
                                               _f(conv_state), _f(out))
     assert rc == 0, "ref_delta_layer_prefill failed"
     return out
+
+
+class RefWindow:
+    """The reference's own attention window (kvwindow.c + kvspill.c, compiled into oracle/_ref)
+    over a rig holding the 10 attention layers' fp32 KV; appends follow forward_impl
+    (kvw_ensure_room first). For checking the device window."""
+
+    def __init__(self, ctx: int, slide: bool, keep: int, pin: int, spill_path: str):
+        self.lib = _load("ref")
+        self.h = self.lib.ref_kvw_new(ctx, int(slide), keep, pin, spill_path.encode())
+        assert self.h, "ref_kvw_new failed"
+        self.layers = self.lib.ref_kvw_layers(self.h)
+
+    def append(self, k, v) -> int:
+        """k, v: [layers, n, 512]."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        return self.lib.ref_kvw_append(self.h, k.shape[1], _f(k), _f(v))
+
+    def evict(self, n) -> int:
+        return self.lib.ref_kvw_evict(self.h, n)
+
+    def restore(self, n) -> int:
+        return self.lib.ref_kvw_restore(self.h, n)
+
+    def rollback(self, p0, s0) -> int:
+        return self.lib.ref_kvw_rollback(self.h, p0, s0)
+
+    def set_context(self, ctx) -> int:
+        return self.lib.ref_kvw_set_context(self.h, ctx)
+
+    def state(self) -> dict:
+        return {k: int(getattr(self.lib, "ref_kvw_" + k)(self.h))
+                for k in ("len", "spilled", "head", "max_chunk", "position", "context")}
+
+    def read(self, a):
+        n = self.lib.ref_kvw_len(self.h)
+        k = np.zeros((n, 512), np.float32)
+        v = np.zeros((n, 512), np.float32)
+        self.lib.ref_kvw_read(self.h, a, _f(k), _f(v))
+        return k, v
+
+    def close(self):
+        if self.h:
+            self.lib.ref_kvw_free(self.h)
+            self.h = None
 
 
 def ref_lib():

@@ -6,7 +6,8 @@
  * Nothing of the reference is copied here: this file #includes the reference's model.c from
  * the path given to the compiler (-I<reference>/src), which reaches its static functions
  * full_attention (model.c:783-863), pf_attention (1536-1602), recurrent_delta_step (272-323)
- * and delta_head (1507-1534).
+ * and delta_head (1507-1534). The reference's kvwindow.c and kvspill.c are compiled alongside
+ * (oracle/Makefile) and driven through a small Model rig for the window tests.
  *
  * The attention functions take their inputs through projections. They are driven literally with
  * f32 (GGUF type 0) weight tensors, which the reference multiplies with kernel_matvec_f32
@@ -18,6 +19,7 @@
  *     gated output is read from the prefill scratch (g_pf.rec) before the O projection.
  */
 #include "model.c"
+#include "kvwindow.h"
 
 #include <stdlib.h>
 #include <string.h>
@@ -44,12 +46,6 @@ void kernel_matvec_quant_end(void) { unreachable("kernel_matvec_quant_end"); }
 int kernel_moe_prefill(const KernelMoeExpert *e, int c, const float *x, float *d, size_t i, size_t h)
 { (void)e; (void)c; (void)x; (void)d; (void)i; (void)h; unreachable("kernel_moe_prefill"); return -1; }
 void kernel_vk_trim_scratch(void) {}
-void kvspill_clear(KVSpill *sp) { (void)sp; }
-int kvw_ensure_room(Model *m, size_t need) { (void)m; (void)need; unreachable("kvw_ensure_room"); return -1; }
-size_t kvw_max_chunk(const Model *m) { (void)m; unreachable("kvw_max_chunk"); return 0; }
-int kvw_realloc(Model *m, size_t n) { (void)m; (void)n; unreachable("kvw_realloc"); return -1; }
-int kvw_refill(Model *m) { (void)m; unreachable("kvw_refill"); return -1; }
-int kvw_shrink_to_fit(Model *m, size_t n) { (void)m; (void)n; unreachable("kvw_shrink_to_fit"); return -1; }
 TensorInfo *weights_find_tensor(Weights *w, const char *n) { (void)w; (void)n; return NULL; }
 CachedExpert *weights_get_expert(Weights *w, int l, int e)
 { (void)w; (void)l; (void)e; unreachable("weights_get_expert"); return NULL; }
@@ -372,6 +368,93 @@ int ref_delta_layer_prefill(int T, const float *qkv, const float *z, const float
         set_col_n(W_be, MODEL_LINEAR_V_HEADS, (size_t)t, zero);
     }
     return rc;
+}
+
+/* ---- the attention window (kvwindow.c) over a rig holding only the 10 attention layers' KV.
+ * Appends follow forward_impl / prefill_chunk: kvw_ensure_room(n) first (model.c:1265, 1798),
+ * then the rows land at the window's end and position advances. Context changes go through
+ * model_set_context (model.c:1870-1899). */
+typedef struct RefWin {
+    Model m;
+    KVCache kv[MODEL_NUM_LAYERS];
+    KVSpill sp;
+    int att[MODEL_NUM_LAYERS], na;
+} RefWin;
+
+RefWin *ref_kvw_new(size_t ctx, int slide, size_t keep, size_t pin, const char *spill_path)
+{
+    RefWin *w = calloc(1, sizeof(*w));
+    if (!w)
+        return NULL;
+    for (int l = 0; l < MODEL_NUM_LAYERS; l++) {
+        if (!model_is_attention_layer(l))
+            continue;
+        w->kv[l].k = locked_calloc_checked(ctx * KV_FLOATS_PER_TOKEN, sizeof(float));
+        w->kv[l].v = locked_calloc_checked(ctx * KV_FLOATS_PER_TOKEN, sizeof(float));
+        w->kv[l].capacity = ctx;
+        w->att[w->na++] = l;
+    }
+    kvspill_init(&w->sp, spill_path);
+    w->m.kv_cache = w->kv;
+    w->m.context_length = ctx;
+    w->m.slide = slide != 0;
+    w->m.slide_keep = keep;
+    w->m.slide_pin = pin;
+    w->m.spill = &w->sp;
+    w->m.attn_scratch = calloc(16 * ctx, sizeof(float));
+    w->m.initialized = true;
+    return w;
+}
+
+void ref_kvw_free(RefWin *w)
+{
+    if (!w)
+        return;
+    kvspill_clear(&w->sp);
+    for (int l = 0; l < MODEL_NUM_LAYERS; l++) {
+        locked_buffer_free(w->kv[l].k);
+        locked_buffer_free(w->kv[l].v);
+    }
+    free(w->m.attn_scratch);
+    free(w);
+}
+
+int ref_kvw_layers(const RefWin *w) { return w->na; }
+
+/* k, v: [na][n][512] rows for the n new tokens of every attention layer. */
+int ref_kvw_append(RefWin *w, size_t n, const float *k, const float *v)
+{
+    if (kvw_ensure_room(&w->m, n) != 0)
+        return -1;
+    for (int a = 0; a < w->na; a++) {
+        KVCache *kv = &w->kv[w->att[a]];
+        memcpy(kv->k + kv->length * KV_FLOATS_PER_TOKEN, k + (size_t)a * n * KV_FLOATS_PER_TOKEN,
+               n * KV_FLOATS_PER_TOKEN * sizeof(float));
+        memcpy(kv->v + kv->length * KV_FLOATS_PER_TOKEN, v + (size_t)a * n * KV_FLOATS_PER_TOKEN,
+               n * KV_FLOATS_PER_TOKEN * sizeof(float));
+        kv->length += n;
+    }
+    w->m.position += n;
+    return 0;
+}
+
+int ref_kvw_evict(RefWin *w, size_t n) { return kvw_evict(&w->m, n); }
+int ref_kvw_restore(RefWin *w, size_t n) { return kvw_restore(&w->m, n); }
+int ref_kvw_rollback(RefWin *w, size_t p0, size_t s0) { return kvw_rollback(&w->m, p0, s0); }
+int ref_kvw_set_context(RefWin *w, size_t ctx) { return model_set_context(&w->m, ctx); }
+size_t ref_kvw_len(const RefWin *w) { return kvw_len(&w->m); }
+size_t ref_kvw_spilled(const RefWin *w) { return kvw_spilled(&w->m); }
+size_t ref_kvw_head(const RefWin *w) { return kvw_head(&w->m); }
+size_t ref_kvw_max_chunk(const RefWin *w) { return kvw_max_chunk(&w->m); }
+size_t ref_kvw_position(const RefWin *w) { return w->m.position; }
+size_t ref_kvw_context(const RefWin *w) { return w->m.context_length; }
+
+/* The window rows [0, len) of attention layer index a. */
+void ref_kvw_read(const RefWin *w, int a, float *k, float *v)
+{
+    const KVCache *kv = &w->kv[w->att[a]];
+    memcpy(k, kv->k, kv->length * KV_FLOATS_PER_TOKEN * sizeof(float));
+    memcpy(v, kv->v, kv->length * KV_FLOATS_PER_TOKEN * sizeof(float));
 }
 
 int ref_max_threads(void)

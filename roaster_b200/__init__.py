@@ -113,6 +113,23 @@ def lib():
         "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_prefill_batch": (C.c_int, [C.POINTER(KernelDeltaPrefillJob), C.c_int]),
         "kernel_deltanet_prefill": (C.c_int, [_vp, _sz] + [_vp] * 6),
+        "kernel_kvw_create": (_vp, [C.c_int, _sz, C.c_int, _sz, _sz, C.c_char_p]),
+        "kernel_kvw_destroy": (None, [_vp]),
+        "kernel_kvw_set_policy": (C.c_int, [_vp, C.c_int, _sz, _sz]),
+        "kernel_kvw_k": (_vp, [_vp, C.c_int]),
+        "kernel_kvw_v": (_vp, [_vp, C.c_int]),
+        "kernel_kvw_len": (_sz, [_vp]),
+        "kernel_kvw_spilled": (_sz, [_vp]),
+        "kernel_kvw_head": (_sz, [_vp]),
+        "kernel_kvw_max_chunk": (_sz, [_vp]),
+        "kernel_kvw_position": (_sz, [_vp]),
+        "kernel_kvw_context": (_sz, [_vp]),
+        "kernel_kvw_ensure_room": (C.c_int, [_vp, _sz]),
+        "kernel_kvw_appended": (C.c_int, [_vp, _sz]),
+        "kernel_kvw_evict": (C.c_int, [_vp, _sz]),
+        "kernel_kvw_restore": (C.c_int, [_vp, _sz]),
+        "kernel_kvw_rollback": (C.c_int, [_vp, _sz, _sz]),
+        "kernel_kvw_set_context": (C.c_int, [_vp, _sz]),
         "kernel_deltanet_preop_batch": (C.c_int, [C.POINTER(KernelDeltaPreopJob), C.c_int]),
         "kernel_deltanet_postop_batch": (C.c_int, [C.POINTER(KernelDeltaPostopJob), C.c_int]),
         "kernel_deltanet_layer_step": (C.c_int, [_vp] * 11),
