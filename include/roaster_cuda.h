@@ -279,6 +279,13 @@ int kernel_deltanet_layer_prefill(float *state, float *conv_state, const float *
                                   const float *a, const float *ssm_norm, size_t T, const float *qkv,
                                   const float *z, const float *alpha, const float *beta, float *out);
 
+/* Diagnostic: launch a kernel whose bounded mbarrier wait cannot complete (nothing arrives) with
+ * a budget of `budget_cycles` SM cycles, and return the device error bits it recorded (1 = a
+ * bounded wait timed out), clearing them; -1 if the launch failed. Exercises the path every
+ * pipelined kernel takes instead of hanging when a partner never signals: the kernel returns,
+ * the error surfaces at the next synchronize, the context stays usable. */
+int kernel_cuda_wait_probe(long long budget_cycles);
+
 /* ------------------------------------------------------------ attention window (device KV)
  * The attention window of one slot with its K/V in device memory (f16 [ctx][2][256] per
  * attention layer) and the policy of kvwindow.c: a kept head (slide_keep / slide_pin), sliding

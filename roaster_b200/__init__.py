@@ -113,6 +113,7 @@ def lib():
         "kernel_deltanet_step_batch_host": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
         "kernel_deltanet_prefill_batch": (C.c_int, [C.POINTER(KernelDeltaPrefillJob), C.c_int]),
         "kernel_deltanet_prefill": (C.c_int, [_vp, _sz] + [_vp] * 6),
+        "kernel_cuda_wait_probe": (C.c_int, [C.c_longlong]),
         "kernel_kvw_create": (_vp, [C.c_int, _sz, C.c_int, _sz, _sz, C.c_char_p]),
         "kernel_kvw_destroy": (None, [_vp]),
         "kernel_kvw_set_policy": (C.c_int, [_vp, C.c_int, _sz, _sz]),

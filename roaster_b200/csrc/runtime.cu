@@ -1,5 +1,6 @@
 // Runtime and the lifecycle / residency part of the C-ABI (include/roaster_cuda.h).
 #include "runtime.h"
+#include "ptx.cuh"
 #include "../../include/roaster_cuda.h"
 
 #include <atomic>
@@ -344,3 +345,43 @@ int kernel_cuda_memmove(void *dst, const void *src, size_t bytes)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- bounded-wait probe
+
+namespace {
+
+// Waits on an mbarrier that nothing ever arrives at, for at most `budget` cycles: the wait must
+// give up, record kErrWaitTimeout and return -- the path every pipelined kernel takes instead of
+// hanging when a partner never signals.
+__global__ void wait_probe_kernel(unsigned *err, long long budget)
+{
+    __shared__ unsigned long long bar;
+    if (threadIdx.x == 0) {
+        rb::mbar_init(rb::smem_addr(&bar), 1);
+        rb::mbar_init_fence();
+        if (!rb::mbar_wait(rb::smem_addr(&bar), 0, budget))
+            atomicOr(err, rb::kErrWaitTimeout);
+    }
+}
+
+}  // namespace
+
+extern "C" int kernel_cuda_wait_probe(long long budget_cycles)
+{
+    if (ensure() != 0)
+        return -1;
+    if (budget_cycles <= 0 || budget_cycles > 4000000000ll)
+        return fail("kernel_cuda_wait_probe: budget out of range");
+    wait_probe_kernel<<<1, 32, 0, g_rt.stream>>>(g_rt.err_word, budget_cycles);
+    if (launched("wait_probe_kernel") != 0)
+        return -1;
+    if (check(cudaStreamSynchronize(g_rt.stream), "wait probe") != 0)
+        return -1;
+    unsigned word = 0;
+    if (check(cudaMemcpy(&word, g_rt.err_word, sizeof(word), cudaMemcpyDeviceToHost), "read error word") != 0)
+        return -1;
+    if (check(cudaMemset(g_rt.err_word, 0, sizeof(unsigned)), "clear error word") != 0)
+        return -1;
+    return (int)word;
+}
+

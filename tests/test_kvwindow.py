@@ -77,7 +77,8 @@ def _compare(ref, dev, what):
         assert np.array_equal(rv, dv), (what, a, "V")
 
 
-def _run(rb, tmp_path, seed, ctx, slide, keep, pin, use_file, steps):
+def _run(rb, tmp_path, seed, ctx, slide, keep, pin, use_file, steps, script=None):
+    """Random operations (or the given `script` of (op, arg) pairs) on both windows."""
     if not O.have_ref():
         pytest.skip("reference build (oracle/_ref) not present")
     rng = np.random.default_rng(seed)
@@ -85,30 +86,35 @@ def _run(rb, tmp_path, seed, ctx, slide, keep, pin, use_file, steps):
     dev = DevWindow(rb, ref.layers, ctx, slide, keep, pin, str(tmp_path / f"dev{seed}.kv") if use_file else "")
     snaps = []
     seen = {"spilled": 0, "failed": 0}
+    ops = script if script is not None else [None] * steps
     try:
-        for step in range(steps):
-            op = rng.choice(["append", "append", "append", "evict", "restore", "rollback", "context"],
-                            p=[0.3, 0.15, 0.1, 0.1, 0.12, 0.13, 0.1])
+        for step, planned in enumerate(ops):
+            if planned is None:
+                op = rng.choice(["append", "append", "append", "evict", "restore", "rollback", "context"],
+                                p=[0.3, 0.15, 0.1, 0.1, 0.12, 0.13, 0.1])
+                arg = None
+            else:
+                op, arg = planned
             if op == "append":
-                n = int(rng.integers(1, max(2, ctx // 3)))
+                n = arg if arg is not None else int(rng.integers(1, max(2, ctx // 3)))
                 k = rng.standard_normal((ref.layers, n, 512)).astype(np.float16).astype(np.float32)
                 v = rng.standard_normal((ref.layers, n, 512)).astype(np.float16).astype(np.float32)
                 r1, r2 = ref.append(k, v), dev.append(k, v)
                 snaps.append((ref.state()["position"], ref.state()["spilled"]))
             elif op == "evict":
-                n = int(rng.integers(0, 20))
+                n = arg if arg is not None else int(rng.integers(0, 20))
                 r1, r2 = ref.evict(n), dev.evict(n)
             elif op == "restore":
-                n = int(rng.integers(0, 20))
+                n = arg if arg is not None else int(rng.integers(0, 20))
                 r1, r2 = ref.restore(n), dev.restore(n)
             elif op == "rollback":
                 if not snaps:
                     continue
-                p0, s0 = snaps[int(rng.integers(0, len(snaps)))]
+                p0, s0 = snaps[arg if arg is not None else int(rng.integers(0, len(snaps)))]
                 r1, r2 = ref.rollback(p0, s0), dev.rollback(p0, s0)
                 snaps = [s for s in snaps if s[0] <= p0]
             else:
-                new = int(rng.integers(max(8, ctx // 4), 2 * ctx))
+                new = arg if arg is not None else int(rng.integers(max(8, ctx // 4), 2 * ctx))
                 r1, r2 = ref.set_context(new), dev.set_context(new)
             assert (r1 == 0) == (r2 == 0), (step, op, r1, r2)
             _compare(ref, dev, (step, op))
@@ -133,7 +139,11 @@ def test_without_sliding(rb, tmp_path):
 
 
 def test_long_window_large_moves(rb, tmp_path):
-    """A 20k-token window: slides move ~15k rows per layer (direct block copies) and restores of
-    a few tokens shift the whole tail (scratch-staged blocks)."""
-    seen = _run(rb, tmp_path, 6, ctx=20000, slide=True, keep=64, pin=0, use_file=True, steps=12)
-    assert seen["spilled"] > 0
+    """A 20k-token window: a slide evicts ~5k rows and moves a ~10k-row tail by less than a move
+    block (scratch-staged), restores of a few tokens shift the whole tail, a large eviction moves
+    it in direct blocks, then rollback, growth (refill from the store) and shrinking."""
+    script = [("append", 15000), ("append", 8000), ("restore", 3), ("append", 400), ("evict", 9000),
+              ("restore", 2500), ("append", 6000), ("rollback", 2), ("context", 30000), ("context", 12000),
+              ("append", 5000)]
+    seen = _run(rb, tmp_path, 6, ctx=20000, slide=True, keep=64, pin=0, use_file=True, steps=0, script=script)
+    assert seen["spilled"] > 5000

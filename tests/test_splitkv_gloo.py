@@ -95,3 +95,45 @@ def test_slice_bounds_cover_window():
             assert spans[0][0] == 0 and spans[-1][1] == L
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert sum(splitkv.appends(world, r) for r in range(world)) == 1
+
+
+def _dying_worker(rank, world, port, outdir):
+    """Rank 1 dies before the partial gather; rank 0 must get an error, not hang."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)                                    # a rank lost between steps
+    t = torch.ones(4)
+    out = [torch.zeros(4) for _ in range(world)]
+    try:
+        dist.all_gather(out, t)
+        result = "no error"
+    except Exception as e:                             # the survivor sees the failure
+        result = "error: " + type(e).__name__
+    with open(os.path.join(outdir, "rank0.txt"), "w") as f:
+        f.write(result)
+    os._exit(0)
+
+
+def test_lost_rank_surfaces_as_error(tmp_path):
+    import time
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert time.time() - t0 < 90
+    assert procs[1].exitcode == 3
+    assert procs[0].exitcode == 0
+    assert open(tmp_path / "rank0.txt").read().startswith("error")
+
