@@ -208,6 +208,49 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[kC])
     }
 }
 
+// The off-diagonal blocks of T = (I + L)^-1 (16 x 16 blocks, fp32 scratch with row stride kLd),
+// by distance d = 1..3: X_ij = sum_{m=16j}^{16i-1} L[16i+rr][m] T[m][16j+cc], T_ij = -D_i X_ij
+// (D_i = the inverted diagonal block). Run by all 384 threads (q = thread index); the steps meet
+// on a CTA-wide mbarrier with bounded waits. Returns false on a wait timeout.
+__device__ __forceinline__ bool inv_levels(const float *Lm, float *Tm, float *Xs, int q, uint32_t lvbar,
+                                           uint32_t &lvphase)
+{
+    auto sync = [&]() -> bool {
+        mbar_arrive(lvbar);
+        const bool ok = mbar_wait(lvbar, lvphase & 1u);
+        lvphase++;
+        return ok;
+    };
+#pragma unroll 1
+    for (int d = 1; d <= 3; d++) {
+        const int nel = (4 - d) * 256;
+        for (int e = q; e < nel; e += kThreads) {
+            const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
+            float acc = 0.f;
+            const float *lrow_p = Lm + (16 * bi + rr) * kLd;
+#pragma unroll 4
+            for (int m = 16 * bj; m < 16 * bi; m++)
+                acc = fmaf(lrow_p[m], Tm[m * kLd + 16 * bj + c2], acc);
+            Xs[e] = acc;
+        }
+        if (!sync())
+            return false;
+        for (int e = q; e < nel; e += kThreads) {
+            const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
+            float acc = 0.f;
+            const float *drow = Tm + (16 * bi + rr) * kLd + 16 * bi;
+            const float *xb = Xs + (e & ~255);
+#pragma unroll
+            for (int m = 0; m < 16; m++)
+                acc = fmaf(m <= rr ? drow[m] : 0.f, xb[m * 16 + c2], acc);
+            Tm[(16 * bi + rr) * kLd + 16 * bj + c2] = -acc;
+        }
+        if (!sync())
+            return false;
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __grid_constant__ DPParams p)
 {
     extern __shared__ unsigned char smem_raw[];
@@ -220,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
     const uint32_t done_bar = smem_addr(&bars[2]), drain_bar = smem_addr(&bars[3]);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[4]);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(&bars[5]);
+    const uint32_t lv_bar = smem_addr(&bars[6]);      // all 384 threads meet here for T's levels
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int vh = blockIdx.x, kh = vh & 15;
@@ -232,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         mbar_init(mma_bar, 1);
         mbar_init(done_bar, 1);
         mbar_init(drain_bar, 1);
+        mbar_init(lv_bar, kThreads);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -283,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
             }
         };
+        uint32_t lvphase = 0;
         issue_loads(0);
         for (int n = 0; n < nchunks; n++) {
             bool ok = true;
@@ -367,6 +413,18 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             mbar_arrive(in_full);
             if (n + 1 < nchunks)
                 issue_loads(n + 1);
+            // help with this chunk's triangular inverse once its diagonal blocks are ready
+            mbar_arrive(lv_bar);
+            bool lv = mbar_wait_sleep(lv_bar, lvphase & 1u, 64);
+            lvphase++;
+            lv = lv && inv_levels(reinterpret_cast<const float *>(gbase + kOffB),
+                                  reinterpret_cast<float *>(gbase + kOffW),
+                                  reinterpret_cast<float *>(gbase + kOffB) + kC * kLd, tid, lv_bar, lvphase);
+            if (!lv) {
+                if (tid == kThreads - kProdThreads)
+                    set_abort();
+                break;
+            }
         }
     } else {
         // ============================================================ chunk arithmetic
@@ -386,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         const uint64_t dWm = tc::smem_desc(base + kOffW, 8192, 1024);          // W' (MN-major)
         const uint64_t dM = tc::smem_desc(base + kOffM, 16, 1024);
         float inv_sigma = 1.f, inv_rho = 1.f, inv_rho2 = 1.f, inv_omega = 1.f;
-        uint32_t mphase = 0;
+        uint32_t mphase = 0, lvphase = 0;
         bool ok = true;
 
         auto wait_mma = [&]() -> bool {
@@ -491,6 +549,13 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
 
         for (int n = 0; n < nchunks && ok; n++) {
             const ChunkConst &C = cc[n & 1];
+            // ---- outputs + state update of the previous chunk (overlaps the producers staging
+            //      this chunk's inputs)
+            if (n > 0 && !finish(n - 1, false)) {
+                ok = false;
+                break;
+            }
+            named_bar_sync(1, 128);
             // ---- inputs of chunk n staged
             {
                 const bool w = mbar_wait_sleep(in_full, (uint32_t)n & 1u, 64);
@@ -516,12 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
                 tc::commit(mma_bar);
             }
-            // ---- outputs + state update of the previous chunk (overlaps (a))
-            if (n > 0 && !finish(n - 1, false)) {
-                ok = false;
-                break;
-            }
-            named_bar_sync(1, 128);
             // ---- L (warps 0-1) and M (warps 2-3) from (a)
             if (!wait_mma()) {
                 ok = false;
@@ -569,31 +628,18 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
             }
             named_bar_sync(1, 128);
-            // ---- off-diagonal blocks of T: T_ij = -D_i sum_{m=j}^{i-1} L_im T_mj, by distance
-#pragma unroll 1
-            for (int d = 1; d <= 3; d++) {
-                const int nel = (4 - d) * 256;
-                for (int e = r; e < nel; e += 128) {
-                    const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
-                    float acc = 0.f;
-                    const float *lrow_p = Lm + (16 * bi + rr) * kLd;
-#pragma unroll 4
-                    for (int m = 16 * bj; m < 16 * bi; m++)
-                        acc = fmaf(lrow_p[m], Tm[m * kLd + 16 * bj + c2], acc);
-                    Xs[e] = acc;
+            // ---- off-diagonal blocks of T, with the producer warps (entry + 6 steps on lv_bar)
+            {
+                mbar_arrive(lv_bar);
+                bool lv = mbar_wait(lv_bar, lvphase & 1u);
+                lvphase++;
+                lv = lv && inv_levels(Lm, Tm, Xs, r, lv_bar, lvphase);
+                if (!bar_all(1, 128, lv && !*abort_flag)) {
+                    if (tid == 0)
+                        set_abort();
+                    ok = false;
+                    break;
                 }
-                named_bar_sync(1, 128);
-                for (int e = r; e < nel; e += 128) {
-                    const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
-                    float acc = 0.f;
-                    const float *drow = Tm + (16 * bi + rr) * kLd + 16 * bi;
-                    const float *xb = Xs + (e & ~255);
-#pragma unroll
-                    for (int m = 0; m < 16; m++)
-                        acc = fmaf(m <= rr ? drow[m] : 0.f, xb[m * 16 + c2], acc);
-                    Tm[(16 * bi + rr) * kLd + 16 * bj + c2] = -acc;
-                }
-                named_bar_sync(1, 128);
             }
             // ---- B operands of (b): rows of T diag(beta / s^v) and T diag(beta gamma / s^k)
             {
