@@ -216,7 +216,9 @@ __device__ __forceinline__ bool inv_levels(const float *Lm, float *Tm, float *Xs
                                            uint32_t &lvphase)
 {
     auto sync = [&]() -> bool {
-        mbar_arrive(lvbar);
+        __syncwarp();                        // the warp's writes, then one arrival per warp
+        if ((q & 31) == 0)
+            mbar_arrive(lvbar);
         const bool ok = mbar_wait(lvbar, lvphase & 1u);
         lvphase++;
         return ok;
@@ -272,11 +274,11 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
     const int nchunks = (int)((T + kC - 1) / kC);
 
     if (tid == 0) {
-        mbar_init(in_full, kProdThreads);
+        mbar_init(in_full, kProdThreads / 32);
         mbar_init(mma_bar, 1);
         mbar_init(done_bar, 1);
         mbar_init(drain_bar, 1);
-        mbar_init(lv_bar, kThreads);
+        mbar_init(lv_bar, kThreads / 32);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -410,11 +412,15 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 C.df[lane + 32] = dfb * C.isk[lane + 32];
             }
             fence_proxy_async();
-            mbar_arrive(in_full);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(in_full);
             if (n + 1 < nchunks)
                 issue_loads(n + 1);
             // help with this chunk's triangular inverse once its diagonal blocks are ready
-            mbar_arrive(lv_bar);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(lv_bar);
             bool lv = mbar_wait_sleep(lv_bar, lvphase & 1u, 64);
             lvphase++;
             lv = lv && inv_levels(reinterpret_cast<const float *>(gbase + kOffB),
@@ -630,7 +636,9 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             named_bar_sync(1, 128);
             // ---- off-diagonal blocks of T, with the producer warps (entry + 6 steps on lv_bar)
             {
-                mbar_arrive(lv_bar);
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(lv_bar);
                 bool lv = mbar_wait(lv_bar, lvphase & 1u);
                 lvphase++;
                 lv = lv && inv_levels(Lm, Tm, Xs, r, lv_bar, lvphase);
