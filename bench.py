@@ -52,6 +52,8 @@ def args_parse():
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context decode")
     ap.add_argument("--long-steps", type=int, default=30)
     ap.add_argument("--long-window", type=int, default=262144)
+    ap.add_argument("--no-proj", action="store_true", help="skip the k-quant projection measurement")
+    ap.add_argument("--proj-steps", type=int, default=20)
     ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
     ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
     ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
@@ -262,6 +264,79 @@ def run_prefill(R, torch, dev, stream, steps: int, rank: int):
     launches = R.launch_count() - n0
     del keep
     return ta / steps, td / steps, launches
+
+
+# ------------------------------------------------------------------------------ projections (section 8f row 3)
+
+# One decode token's projections of the 40-layer hybrid stack (kernel_matvec_quant_batch's jobs):
+# 10 full-attention layers (q+gate 8192x2048 Q4_K, k 512x2048 Q4_K, v 512x2048 Q6_K,
+# o 2048x4096 Q6_K) and 30 DeltaNet layers (qkv 8192x2048 Q4_K, z 4096x2048 Q4_K, alpha and beta
+# 32x2048 Q4_K, ssm_out 2048x4096 Q6_K).
+PROJ_ATT = [(False, 8192, 2048), (False, 512, 2048), (True, 512, 2048), (True, 2048, 4096)]
+PROJ_DN = [(False, 8192, 2048), (False, 4096, 2048), (False, 32, 2048), (False, 32, 2048), (True, 2048, 4096)]
+PROJ_SHAPES = PROJ_ATT * 10 + PROJ_DN * 30
+
+
+def proj_bytes(shapes) -> int:
+    return sum(r * (c // 256) * (210 if q6 else 144) for q6, r, c in shapes)
+
+
+def run_projections(R, torch, dev, stream, steps: int, rank: int):
+    """All projections of the stack for one token in one kernel_cuda_matvec_quant_batch call:
+    random k-quant blocks (uniform bytes) and N(0,1) activations. The weights (811 MB) exceed L2,
+    so each step streams them from HBM. Returns (ms per step, launches)."""
+    keep, jobs = [], []
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7000 + rank)
+    for q6, r, c in PROJ_SHAPES:
+        m = torch.randint(0, 256, (r * (c // 256) * (210 if q6 else 144),), dtype=torch.uint8, device=dev,
+                          generator=gen)
+        x = torch.randn(c, device=dev, generator=gen)
+        y = torch.empty(r, device=dev)
+        keep.append((m, x, y))
+        jobs.append(R.KernelCudaMatvecJob(int(q6), m.data_ptr(), x.data_ptr(), y.data_ptr(), r, c))
+    arr = (R.KernelCudaMatvecJob * len(jobs))(*jobs)
+    lib = R.lib()
+    for _ in range(3):
+        if lib.kernel_cuda_matvec_quant_batch(arr, len(jobs)) != 0:
+            raise RuntimeError(R.last_error())
+    R.synchronize()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = R.launch_count()
+    e0.record(stream)
+    for _ in range(steps):
+        lib.kernel_cuda_matvec_quant_batch(arr, len(jobs))
+    e1.record(stream)
+    R.synchronize()
+    torch.cuda.synchronize()
+    launches = R.launch_count() - n0
+    del keep
+    return e0.elapsed_time(e1) / steps, launches
+
+
+def proj_cpu_reference(seconds: float = 1.5) -> dict:
+    """The reference's own CPU k-quant matvec (kernel_dot_q4_k / kernel_dot_q6_k per row under
+    OpenMP, as matvec_q4_cpu / matvec_q6_cpu) on one DeltaNet layer's and one attention layer's
+    projections, repeated for about `seconds`."""
+    import numpy as np
+    import oracle as O
+    from roaster_b200 import synth
+    shapes = PROJ_ATT + PROJ_DN
+    mats = [(q6, synth.quant_matrix(11 + i, r, c, q6), np.random.default_rng(i).standard_normal(c).astype(np.float32),
+             r, c) for i, (q6, r, c) in enumerate(shapes)]
+    O.matvec_q(*mats[0][:2], mats[0][2], mats[0][3], mats[0][4], impl="ref")
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for q6, m, x, r, c in mats:
+            O.matvec_q(q6, m, x, r, c, impl="ref")
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > seconds:
+            break
+    nbytes = proj_bytes(shapes) * reps
+    return {"GBps": nbytes / el / 1e9, "threads": os.cpu_count(), "reps": reps,
+            "sample_MB": proj_bytes(shapes) / 1e6}
 
 
 # ------------------------------------------------------------------------------ long context (config 4)
@@ -602,6 +677,39 @@ def run_ours(a):
                                              "note": "each product runs as three f16 MMAs (hi*hi + hi*lo + lo*hi) "
                                                      "to keep the fp32 state within 1e-4"}}}
 
+    proj = None
+    if not a.no_proj:
+        pms, plaunch = run_projections(R, torch, dev, stream, a.proj_steps, rank)
+        tq = torch.tensor([pms], device=dev)
+        if world > 1:
+            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
+        pms = float(tq.item())
+        pbytes = proj_bytes(PROJ_SHAPES)
+        hbm_p, _, src_p = peaks()
+        gbs = pbytes / (pms / 1e3) / 1e9
+        proj = {"metric": "decode projections GB/s (one token through the 40-layer stack's Q4_K/Q6_K "
+                          "attention + DeltaNet projections, one kernel_cuda_matvec_quant_batch call)",
+                "value": round(gbs * world, 1), "unit": "GB/s", "ms_per_step": round(pms, 4),
+                "steps": a.proj_steps, "gpu_launches": int(plaunch), "jobs": len(PROJ_SHAPES),
+                "weight_bytes_per_step": pbytes,
+                "data": "synthetic: uniform random k-quant blocks, N(0,1) activations",
+                "roofline": {"bound": "hbm", "kernel": "quant_matvec_staged_kernel",
+                             "achieved": round(gbs, 1), "peak": hbm_p, "unit": "GB/s",
+                             "frac": round(gbs / hbm_p, 4),
+                             "peak_source": f"{src_p} hbm_gbs (burst)",
+                             "algorithmic_bytes_per_launch": pbytes,
+                             "l2": "weights (811 MB) exceed L2; no flush needed"}}
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            try:
+                c = proj_cpu_reference()
+                proj["cpu_baseline"] = {"value": round(c["GBps"], 2), "unit": "GB/s", "cores": c["threads"],
+                                        "kind": "reference",
+                                        "sample": f"{c['reps']} x one attention + one DeltaNet layer's projections "
+                                                  f"({c['sample_MB']:.1f} MB), the reference's kernel_dot_q4_k / "
+                                                  f"kernel_dot_q6_k per row under OpenMP"}
+            except Exception as e:  # reported, not fatal
+                proj["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
+
     long_ctx = None
     if not a.no_long:
         long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window,
@@ -645,7 +753,7 @@ def run_ours(a):
                 "deltanet_step_kernel": {"ms": round(dn_avg, 4), "GB/s": round(dn_gbs, 1),
                                          "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
-            "prefill": prefill, "long_context": long_ctx,
+            "prefill": prefill, "long_context": long_ctx, "projections": proj,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

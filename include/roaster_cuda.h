@@ -323,6 +323,23 @@ int kernel_kvw_restore(KernelKvWindow *w, size_t n);                  /* kvw_res
 int kernel_kvw_rollback(KernelKvWindow *w, size_t p0, size_t s0);     /* kvw_rollback */
 int kernel_kvw_set_context(KernelKvWindow *w, size_t ctx);            /* model_set_context's window part */
 
+/* ------------------------------------------------------------ k-quant projections (decode)
+ * Replaces kernel_matvec_quant_batch (kernels.h:30-44; CPU matvec_q4_cpu / matvec_q6_cpu,
+ * kernels.c:405-431, 553-578): y[r] = dot(W[r], x) for Q4_K (144-byte blocks) or Q6_K (210-byte
+ * blocks) rows of cols/256 blocks, weights resident in device memory (uploaded once). Jobs are
+ * independent (no job reads another's output). cols must be a positive multiple of 256; vector
+ * and output 16-byte aligned; a Q4_K matrix 16-byte aligned, a Q6_K matrix 2-byte aligned (16
+ * bytes for the fast path). Device pointers, asynchronous. */
+typedef struct {
+    int is_q6;                  /* 0 = Q4_K, 1 = Q6_K */
+    const void *matrix;         /* device, rows x cols quantized */
+    const float *vector;        /* device, [cols] */
+    float *output;              /* device, [rows] */
+    size_t rows, cols;
+} KernelCudaMatvecJob;
+
+int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, int n);
+
 #ifdef __cplusplus
 }
 #endif

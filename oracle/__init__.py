@@ -69,6 +69,8 @@ def _load(which: str):
         lib.orc_delta_preop.argtypes = [C.c_size_t] + [_fp] * 12
         lib.orc_delta_preop.restype = None
         lib.orc_delta_postop.argtypes = [C.c_size_t, _fp, _fp, _fp]
+        lib.orc_matvec_q.argtypes = [C.c_int, C.c_void_p, _fp, _fp, C.c_size_t, C.c_size_t]
+        lib.orc_matvec_q.restype = None
         lib.orc_delta_postop.restype = None
         lib.orc_f32_to_f16.argtypes = [C.c_float]
         lib.orc_f32_to_f16.restype = C.c_uint16
@@ -84,6 +86,8 @@ def _load(which: str):
         lib.ref_delta_prefill.restype = None
         lib.ref_delta_layer_prefill.argtypes = [C.c_int] + [_fp] * 11
         lib.ref_delta_layer_prefill.restype = C.c_int
+        lib.ref_matvec_q.argtypes = [C.c_int, C.c_void_p, _fp, _fp, C.c_size_t, C.c_size_t]
+        lib.ref_matvec_q.restype = None
         lib.ref_kvw_new.argtypes = [C.c_size_t, C.c_int, C.c_size_t, C.c_size_t, C.c_char_p]
         lib.ref_kvw_new.restype = C.c_void_p
         lib.ref_kvw_free.argtypes = [C.c_void_p]
@@ -389,6 +393,18 @@ class RefWindow:
         if self.h:
             self.lib.ref_kvw_free(self.h)
             self.h = None
+
+
+def matvec_q(is_q6: bool, m, x, rows: int, cols: int, impl: str = "port"):
+    """k-quant projection (matvec_q4_cpu / matvec_q6_cpu, kernels.c:405-431, 553-578): uint8
+    blocks ``m`` (rows x cols/256 Q4_K or Q6_K blocks) times fp32 ``x`` [cols] -> [rows]."""
+    m = np.ascontiguousarray(m, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    assert m.size == rows * (cols // 256) * (210 if is_q6 else 144) and x.size == cols
+    out = np.zeros(rows, np.float32)
+    fn = _load("port").orc_matvec_q if impl == "port" else _load("ref").ref_matvec_q
+    fn(int(bool(is_q6)), m.ctypes.data_as(C.c_void_p), _f(x), _f(out), rows, cols)
+    return out
 
 
 def ref_lib():

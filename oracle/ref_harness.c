@@ -465,3 +465,15 @@ int ref_max_threads(void)
     return 1;
 #endif
 }
+
+/* ---- k-quant projections: the reference's matvec_q4_cpu / matvec_q6_cpu (kernels.c:405-431,
+ * 553-578) are static in kernels.c; they are one kernel_dot_q4_k / kernel_dot_q6_k call per row
+ * under an OpenMP loop, reproduced here around the reference's own (public) dot functions. */
+void ref_matvec_q(int is_q6, const void *matrix, const float *x, float *out, size_t rows, size_t cols)
+{
+    const size_t rb = (cols / 256) * (is_q6 ? 210 : 144);
+    const uint8_t *m = (const uint8_t *)matrix;
+    #pragma omp parallel for schedule(static) if (rows * (cols / 256) >= 16384)
+    for (size_t r = 0; r < rows; r++)
+        out[r] = is_q6 ? kernel_dot_q6_k(m + r * rb, x, cols) : kernel_dot_q4_k(m + r * rb, x, cols);
+}

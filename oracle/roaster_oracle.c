@@ -513,3 +513,67 @@ void orc_delta_postop(size_t rows, float *out, const float *z, const float *w)
     }
 }
 
+/* Q4_K block (kernels.c:137-200): d, dmin (f16), 12 bytes of 6-bit scales/mins unpacked as in
+ * q4_k_get_scales (kernels.c:155-174), 128 bytes of nibbles; group g of 64 weights takes the low
+ * nibbles of qs[32g..32g+31] (scale/min 2g) then their high nibbles (2g+1);
+ * weight = d sc q - dmin m. */
+static float orc_dot_q4_block(const uint8_t *b, const float *x)
+{
+    const float d = orc_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    const float dmin = orc_f16_to_f32((uint16_t)(b[2] | (b[3] << 8)));
+    const uint8_t *sc = b + 4, *qs = b + 16;
+    float sum = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        int s, m;
+        if (j < 4) {
+            s = sc[j] & 63;
+            m = sc[j + 4] & 63;
+        } else {
+            s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+            m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+        }
+        const int g = j >> 1, hi = j & 1;
+        float part = 0.0f, xs = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const int q = hi ? (qs[32 * g + i] >> 4) : (qs[32 * g + i] & 15);
+            part += (float)q * x[32 * j + i];
+            xs += x[32 * j + i];
+        }
+        sum += d * (float)s * part - dmin * (float)m * xs;
+    }
+    return sum;
+}
+
+/* Q6_K block (kernels.c:437-488): ql[128], qh[64], int8 scales[16], d; for half n and l < 32 the
+ * weights 128n + l, +32, +64, +96 are the low nibbles of ql[64n+l], ql[64n+32+l], then their high
+ * nibbles, each with two bits of qh[32n+l] (bits 0-1, 2-3, 4-5, 6-7) on top, minus 32, scaled by
+ * d * scales[8n + l/16 + 0, 2, 4, 6]. */
+static float orc_dot_q6_block(const uint8_t *b, const float *x)
+{
+    const uint8_t *ql = b, *qh = b + 128;
+    const int8_t *sc = (const int8_t *)(b + 192);
+    const float d = orc_f16_to_f32((uint16_t)(b[208] | (b[209] << 8)));
+    float sum = 0.0f;
+    for (int n = 0; n < 2; n++)
+        for (int l = 0; l < 32; l++) {
+            const int a = ql[64 * n + l], c = ql[64 * n + 32 + l], h = qh[32 * n + l];
+            const int q[4] = {(a & 15) | ((h & 3) << 4), (c & 15) | (((h >> 2) & 3) << 4),
+                              (a >> 4) | (((h >> 4) & 3) << 4), (c >> 4) | (((h >> 6) & 3) << 4)};
+            for (int k = 0; k < 4; k++)
+                sum += d * (float)sc[8 * n + l / 16 + 2 * k] * (float)(q[k] - 32) * x[128 * n + 32 * k + l];
+        }
+    return sum;
+}
+
+void orc_matvec_q(int is_q6, const uint8_t *m, const float *x, float *out, size_t rows, size_t cols)
+{
+    const size_t nb = cols / 256, bs = is_q6 ? 210 : 144;
+    for (size_t r = 0; r < rows; r++) {
+        float acc = 0.0f;
+        for (size_t b = 0; b < nb; b++) {
+            const uint8_t *blk = m + (r * nb + b) * bs;
+            acc += is_q6 ? orc_dot_q6_block(blk, x + 256 * b) : orc_dot_q4_block(blk, x + 256 * b);
+        }
+        out[r] = acc;
+    }
+}

@@ -105,6 +105,10 @@ void orc_delta_preop(size_t T, const float *qkv, const float *alpha, const float
 /* Gated RMSNorm post-op (model.c:1333-1343) over `rows` rows of 128, in place. */
 void orc_delta_postop(size_t rows, float *out, const float *z, const float *w);
 
+/* k-quant matrix-vector product (matvec_q4_cpu / matvec_q6_cpu, kernels.c:405-431, 553-578):
+ * out[r] = sum of the dequantised row r (Q4_K 144-byte or Q6_K 210-byte blocks of 256) times x. */
+void orc_matvec_q(int is_q6, const uint8_t *m, const float *x, float *out, size_t rows, size_t cols);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,13 @@ class KernelDeltaPostopJob(C.Structure):
     _fields_ = [("out", _vp), ("z", _vp), ("norm_w", _vp), ("T", _sz)]
 
 
+class KernelCudaMatvecJob(C.Structure):
+    """Mirror of ``KernelCudaMatvecJob`` (include/roaster_cuda.h); the reference's KernelMatvecJob
+    (src/kernels.h:34-41) with device pointers."""
+    _fields_ = [("is_q6", C.c_int), ("matrix", _vp), ("vector", _vp), ("output", _vp), ("rows", _sz),
+                ("cols", _sz)]
+
+
 _lib = None
 
 
@@ -135,6 +142,7 @@ def lib():
         "kernel_deltanet_postop_batch": (C.c_int, [C.POINTER(KernelDeltaPostopJob), C.c_int]),
         "kernel_deltanet_layer_step": (C.c_int, [_vp] * 11),
         "kernel_deltanet_layer_prefill": (C.c_int, [_vp] * 6 + [_sz] + [_vp] * 5),
+        "kernel_cuda_matvec_quant_batch": (C.c_int, [C.POINTER(KernelCudaMatvecJob), C.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -275,3 +283,12 @@ def deltanet_postop_batch(jobs) -> None:
     arr, n = _arr(KernelDeltaPostopJob, js)
     check(lib().kernel_deltanet_postop_batch(arr, n), "kernel_deltanet_postop_batch")
 
+
+def matvec_quant_batch(jobs) -> None:
+    """kernel_cuda_matvec_quant_batch over jobs given as KernelCudaMatvecJob or
+    (is_q6, matrix, vector, output, rows, cols) with device tensors or addresses."""
+    js = [j if isinstance(j, KernelCudaMatvecJob) else
+          KernelCudaMatvecJob(int(bool(j[0])), _ptr(j[1]), _ptr(j[2]), _ptr(j[3]), int(j[4]), int(j[5]))
+          for j in jobs]
+    arr, n = _arr(KernelCudaMatvecJob, js)
+    check(lib().kernel_cuda_matvec_quant_batch(arr, n), "kernel_cuda_matvec_quant_batch")

@@ -120,21 +120,6 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-// AND of `ok` over the `n` threads of named barrier `id` (also a barrier).
-__device__ __forceinline__ bool bar_all(int id, int n, bool ok)
-{
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.and.pred p, %2, %3, q;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)ok), "r"(id), "r"(n)
-        : "memory");
-    return r != 0;
-}
-
 // Power of two s with amax * s in [1, 2) (1 for zero or non-finite amax).
 __device__ __forceinline__ float pow2_scale(float amax)
 {

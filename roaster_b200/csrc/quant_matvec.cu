@@ -1,0 +1,766 @@
+// k-quant matrix-vector products for the layer projections of a decode step: the batched
+// kernel_matvec_quant_batch of the reference (src/kernels.h:30-44; CPU path kernels.c:150-578)
+// with the weights resident in device memory.
+//
+//   y[r] = sum_c W[r][c] x[c],  W rows of 256-weight blocks:
+//   Q4_K (144 B): f16 d, f16 dmin, 12 bytes of packed 6-bit scales/mins, 128 bytes of nibbles;
+//        group g (64 weights): qs[32g + i] low nibble -> weight 64g + i (scale/min j = 2g), high
+//        nibble -> 64g + 32 + i (j = 2g + 1); weight = d sc_j q - dmin m_j
+//        (q4_k_get_scales, kernels.c:155-174).
+//   Q6_K (210 B): ql[128], qh[64], int8 scales[16], f16 d; half n, l < 32: the low nibbles of
+//        ql[64n + l], ql[64n + 32 + l] and the high ones, with the bit pairs of qh[32n + l],
+//        are weights 128n + l, +32, +64, +96 with scales sc[8n + l/16 + 0, 2, 4, 6];
+//        weight = d sc (q - 32) (kernels.c:437-488).
+//
+// The op streams the weights once (0.5625 B per weight for Q4_K, 0.8203 for Q6_K); at HBM rate
+// an SM has about 6 cycles per 144-byte block, so the per-weight work has to stay at a few
+// instructions per 8 weights. The staged kernel does the products on the tensor cores (warp MMA
+// m16n8k16, f16 inputs, fp32 accumulation):
+//
+//  * Sixteen warps per CTA, each streaming its own tiles of 16 rows one block at a time through a
+//    private ring of shared memory with 16-byte cp.async copies (Q4_K: 5 stages of 16 x 144 B;
+//    Q6_K: 3 stages of 16 x 240 B, each row slot the 16-byte-aligned window around its block).
+//    Warps never wait on one another inside a job, and each keeps about 8 KB in flight.
+//  * Lane (g, t) holds rows g and g + 8 of the tile. Weights enter the A fragment as exact f16
+//    subnormals: a Q4_K nibble field ANDed in place is q 2^-24 (low) or q 2^-20 (high), a Q6_K
+//    6-bit field q 2^-24 - one AND per two weights, no conversion.
+//  * The activation, scaled by a power of two so its largest element sits near 2^14, is split
+//    into f16 hi + lo (about 22 bits) and enters B as two columns. In each window of four scale
+//    groups (Q4_K: four 32-weight sub-blocks; Q6_K: four 16-weight groups) lane t's k-slots hold
+//    only group t and only lanes 2t, 2t+1 of the B fragment are non-zero, so accumulator columns
+//    2t, 2t+1 of lane t are exactly group t's dot product: one fp32 scale per lane per window.
+//  * The B fragments of a job (1 KB per block) and its activation sums per scale group (for the
+//    Q4_K min and the Q6_K -32 terms) are built in shared memory at the start of each job a CTA
+//    works on (the only CTA-wide syncs, on a bounded mbarrier). CTAs take contiguous tile ranges
+//    of equal bytes.
+//
+// Rows the staged kernel does not take (a matrix not 16-byte aligned, rows longer than 4096
+// weights, the last row of a Q6_K matrix whose end is not 16-byte aligned) run in the row kernel:
+// one warp per row reading global memory directly.
+#include "ptx.cuh"
+#include "runtime.h"
+#include "../../include/roaster_cuda.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstring>
+
+namespace rb {
+namespace {
+
+constexpr int kMaxJobs = 64;
+
+// ---------------------------------------------------------------- staged kernel geometry
+
+constexpr int kCWarps = 16;
+constexpr int kCThreads = kCWarps * 32;
+constexpr int kThreads = kCThreads;
+constexpr int kRingBytes = 12 * 1024;            // per warp
+constexpr int kQ4Slot = 144, kQ6Slot = 240;      // staged bytes per row of one block
+constexpr int kQ4Stages = kRingBytes / (16 * kQ4Slot);   // 5
+constexpr int kQ6Stages = kRingBytes / (16 * kQ6Slot);   // 3
+constexpr int kMaxNb = 16;                       // staged path: up to 16 blocks (4096 weights) a row
+constexpr int kOffBtab = kCWarps * kRingBytes;   // B fragments: 1 KB per block
+constexpr int kOffXsum = kOffBtab + kMaxNb * 1024;   // activation sums: 16 a block (Q6_K), 8 (Q4_K)
+constexpr int kOffMisc = kOffXsum + kMaxNb * 16 * 4; // max reduction (one float per warp)
+constexpr int kOffBar = kOffMisc + kCWarps * 4;      // job barrier
+constexpr int kSmemBytes = kOffBar + 8;
+constexpr int kMaxCtas = 160;
+static_assert(kSmemBytes <= 232448, "staged matvec exceeds the shared memory of a CTA");
+static_assert(kQ4Stages >= 3 && kQ6Stages >= 3, "rings too small");
+
+struct SJob {
+    const unsigned char *w;      // rows x nb blocks, 16-byte aligned
+    const float *x;
+    float *y;
+    long long tile0;             // first global tile (16 rows) of the job
+    long long rows;              // rows in tiles (the last Q6_K row may go to the row kernel)
+    int nb, is_q6;
+};
+
+struct SParams {
+    SJob jobs[kMaxJobs];
+    int njobs;
+    long long tiles;
+    long long cta_tile[kMaxCtas + 1];   // CTA c takes tiles [cta_tile[c], cta_tile[c + 1])
+    unsigned *err;
+};
+
+struct DJob {
+    const unsigned char *w;
+    const float *x;
+    float *y;
+    long long drow0;             // first global row of the job in the row kernel
+    long long rows;
+    int nb, is_q6;
+};
+
+struct DParams {
+    DJob jobs[kMaxJobs];
+    int njobs;
+    long long drows;
+};
+
+// ---------------------------------------------------------------- staged kernel
+
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// D += A * B, m16n8k16, f16 inputs, fp32 accumulation (not volatile: free to schedule).
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(const unsigned char *p)
+{
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+__device__ __forceinline__ uint32_t lds32(const unsigned char *p)
+{
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int i)
+{
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Byte `sel` of each word as 2^23 + byte, less 2^23 (exact small integers as floats).
+__device__ __forceinline__ float2 bytes_as_float2(uint32_t a, uint32_t b, uint32_t sel)
+{
+    const float2 f = make_float2(__uint_as_float(__byte_perm(a, 0x4B000000u, sel)),
+                                 __uint_as_float(__byte_perm(b, 0x4B000000u, sel)));
+    return __fadd2_rn(f, make_float2(-8388608.f, -8388608.f));
+}
+
+// Two int8 values (bytes 0, 1 of u) times d: (u ^ 0x80 bytes as 2^23 + 128 + v) - (2^23 + 128).
+__device__ __forceinline__ float2 int8_pair_times(uint32_t u, float d)
+{
+    u ^= 0x8080u;
+    const float2 f = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650u)),
+                                 __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651u)));
+    return __fmul2_rn(__fadd2_rn(f, make_float2(-8388736.f, -8388736.f)), make_float2(d, d));
+}
+
+// Per-lane constants of the staged kernel.
+struct Lane {
+    int g, t;
+    bool bnz;            // this lane's B fragment is non-zero (g >> 1 == t)
+    int l8;              // its index among the eight non-zero lanes
+    uint32_t sel;        // byte t of a word
+};
+
+// One Q4_K block of rows (g, g + 8) of a tile: window W covers sub-blocks 4W..4W+3, lane t's
+// k-slots hold sub-block 4W + t (byte group 2W + t/2, nibble t&1), eight MMAs per window.
+__device__ __forceinline__ void q4_mma_block(const unsigned char *pa, const unsigned char *pb, const uint4 *bt,
+                                             const float *xs, float f4, const Lane &L, float &acc_a, float &acc_b)
+{
+    const uint4 ha = lds128(pa), hb = lds128(pb);
+    // scales and mins of sub-blocks t and 4 + t (q4_k_get_scales, four bytes at a time)
+    float2 sa, ma, sb, mb;
+    {
+        const uint32_t scl = ha.y & 0x3F3F3F3Fu, mnl = ha.z & 0x3F3F3F3Fu;
+        const uint32_t sch = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+        const uint32_t mnh = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&ha.x));
+        const float ds = dd.x * f4;
+        sa = __fmul2_rn(bytes_as_float2(scl, sch, L.sel), make_float2(ds, ds));
+        ma = __fmul2_rn(bytes_as_float2(mnl, mnh, L.sel), make_float2(dd.y, dd.y));
+    }
+    {
+        const uint32_t scl = hb.y & 0x3F3F3F3Fu, mnl = hb.z & 0x3F3F3F3Fu;
+        const uint32_t sch = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+        const uint32_t mnh = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hb.x));
+        const float ds = dd.x * f4;
+        sb = __fmul2_rn(bytes_as_float2(scl, sch, L.sel), make_float2(ds, ds));
+        mb = __fmul2_rn(bytes_as_float2(mnl, mnh, L.sel), make_float2(dd.y, dd.y));
+    }
+    const uint32_t mask = (L.t & 1) ? 0x00F000F0u : 0x000F000Fu;
+#pragma unroll
+    for (int W = 0; W < 2; W++) {
+        const int G = 2 * W + (L.t >> 1);
+        const uint4 qa0 = lds128(pa + 16 + 32 * G), qa1 = lds128(pa + 32 + 32 * G);
+        const uint4 qb0 = lds128(pb + 16 + 32 * G), qb1 = lds128(pb + 32 + 32 * G);
+        uint4 bf[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                       make_uint4(0, 0, 0, 0)};
+        if (L.bnz) {
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                bf[i] = bt[(W * 4 + i) * 8 + L.l8];
+        }
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 8; s++) {
+            const uint32_t wa = word_of(s < 4 ? qa0 : qa1, s & 3), wb = word_of(s < 4 ? qb0 : qb1, s & 3);
+            const uint32_t b0 = (s & 1) ? bf[s >> 1].z : bf[s >> 1].x;
+            const uint32_t b1 = (s & 1) ? bf[s >> 1].w : bf[s >> 1].y;
+            mma16816(c, wa & mask, wb & mask, (wa >> 8) & mask, (wb >> 8) & mask, b0, b1);
+        }
+        const float xw = xs[4 * W + L.t];
+        const float2 s2 = W ? make_float2(sa.y, sb.y) : make_float2(sa.x, sb.x);
+        const float2 m2 = W ? make_float2(ma.y, mb.y) : make_float2(ma.x, mb.x);
+        acc_a = fmaf(s2.x, c[0] + c[1], fmaf(-m2.x, xw, acc_a));
+        acc_b = fmaf(s2.y, c[2] + c[3], fmaf(-m2.y, xw, acc_b));
+    }
+}
+
+// Four consecutive logical words at byte offset `off` of a Q6_K block starting at `bp` (any even
+// address): aligned loads, shifted by 16 bits when the words straddle.
+__device__ __forceinline__ void q6_words(const unsigned char *bp, int off, uint32_t (&w)[4])
+{
+    const unsigned char *a = bp + off;
+    const unsigned char *al = reinterpret_cast<const unsigned char *>(reinterpret_cast<uintptr_t>(a) & ~(uintptr_t)3);
+    const uint32_t sh = 8u * (uint32_t)(reinterpret_cast<uintptr_t>(a) & 3);
+    uint32_t prev = lds32(al);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t nxt = lds32(al + 4 * i + 4);
+        w[i] = __funnelshift_r(prev, nxt, sh);
+        prev = nxt;
+    }
+}
+
+// One Q6_K block of rows (g, g + 8): window (n, h) covers scale groups 8n + 2q + h, q = 0..3;
+// lane t's k-slots hold group q = t (16 weights 128n + 32t + 16h + l), four MMAs per window.
+__device__ __forceinline__ void q6_mma_block(const unsigned char *pa, const unsigned char *pb, const uint4 *bt,
+                                             const float *xs, float f6, const Lane &L, float &acc_a, float &acc_b)
+{
+    const int sl = 4 * (L.t >> 1);                   // nibble: low for groups q = 0, 1
+    const int rot = (2 * L.t - 4) & 31;              // qh bits 2t, 2t+1 of each byte to bits 4, 5
+    // scales 8n + 2t + h for (n, h) = (0,0), (0,1) [s01] and (1,0), (1,1) [s23], times d
+    const float da = __half2float(*reinterpret_cast<const __half *>(pa + 208));
+    const float db = __half2float(*reinterpret_cast<const __half *>(pb + 208));
+    const float2 sa01 = int8_pair_times(*reinterpret_cast<const unsigned short *>(pa + 192 + 2 * L.t), da);
+    const float2 sa23 = int8_pair_times(*reinterpret_cast<const unsigned short *>(pa + 200 + 2 * L.t), da);
+    const float2 sb01 = int8_pair_times(*reinterpret_cast<const unsigned short *>(pb + 192 + 2 * L.t), db);
+    const float2 sb23 = int8_pair_times(*reinterpret_cast<const unsigned short *>(pb + 200 + 2 * L.t), db);
+#pragma unroll
+    for (int win = 0; win < 4; win++) {
+        const int n = win >> 1, h = win & 1;
+        uint32_t la[4], lb[4], ha[4], hb[4];
+        q6_words(pa, 64 * n + 32 * (L.t & 1) + 16 * h, la);
+        q6_words(pb, 64 * n + 32 * (L.t & 1) + 16 * h, lb);
+        q6_words(pa, 128 + 32 * n + 16 * h, ha);
+        q6_words(pb, 128 + 32 * n + 16 * h, hb);
+        uint4 bf[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        if (L.bnz) {
+            bf[0] = bt[(win * 2 + 0) * 8 + L.l8];
+            bf[1] = bt[(win * 2 + 1) * 8 + L.l8];
+        }
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const uint32_t qa = ((la[s] >> sl) & 0x0F0F0F0Fu) | (__funnelshift_r(ha[s], ha[s], rot) & 0xF0F0F0F0u);
+            const uint32_t qb = ((lb[s] >> sl) & 0x0F0F0F0Fu) | (__funnelshift_r(hb[s], hb[s], rot) & 0xF0F0F0F0u);
+            const uint32_t b0 = (s & 1) ? bf[s >> 1].z : bf[s >> 1].x;
+            const uint32_t b1 = (s & 1) ? bf[s >> 1].w : bf[s >> 1].y;
+            mma16816(c, qa & 0x003F003Fu, qb & 0x003F003Fu, (qa >> 8) & 0x003F003Fu, (qb >> 8) & 0x003F003Fu,
+                     b0, b1);
+        }
+        // group k = 8n + 2t + h: d sc_k (sum q x - 32 sum x)
+        const float xk = xs[8 * n + 2 * L.t + h];
+        const float sa = n ? (h ? sa23.y : sa23.x) : (h ? sa01.y : sa01.x);
+        const float sb = n ? (h ? sb23.y : sb23.x) : (h ? sb01.y : sb01.x);
+        acc_a = fmaf(sa, fmaf(c[0] + c[1], f6, -32.f * xk), acc_a);
+        acc_b = fmaf(sb, fmaf(c[2] + c[3], f6, -32.f * xk), acc_b);
+    }
+}
+
+// CTA-wide sync on the job barrier (one arrival per warp, bounded wait). False on timeout.
+__device__ __forceinline__ bool jb_sync(uint32_t jb, uint32_t &jph, int lane)
+{
+    __syncwarp();
+    if (lane == 0)
+        mbar_arrive(jb);
+    const bool ok = mbar_wait(jb, jph & 1u);
+    jph++;
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Build the shared-memory tables of job J: B fragments (x scaled by 2^e, split f16 hi/lo) and the
+// activation sums per scale group. Called by every thread; one round of global loads, two syncs on
+// the job barrier. Sets e (the activation scale exponent); false if a sync timed out.
+//
+// B entry (b, window, MMA pair, lane8) = 16 bytes = (b0, b1) of two MMAs for one of the eight
+// non-zero lanes (lane8 = 2t + hi/lo). k-slots 2t, 2t+1 <- activations u = 0, 2 and 2t+8, 2t+9
+// <- u = 1, 3 of the four weights of MMA s in lane t's group. Q4_K: index (W * 4 + pair) * 8 +
+// lane8 within a block, group = sub-block 4W + t; Q6_K: (window (n, h) * 2 + pair) * 8 + lane8,
+// group 8n + 2t + h.
+__device__ bool build_tables(const SJob &J, unsigned char *sm, int tid, uint32_t jb, uint32_t &jph, int &e)
+{
+    const int cols = J.nb * 256, nent = J.nb * 64;
+    float v[2][8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int en = tid + i * kCThreads;
+        if (en < nent) {
+            const int l8 = en & 7, blk = en >> 6, t = l8 >> 1;
+            int base;
+            if (J.is_q6) {
+                const int pr = (en >> 3) & 1, win = (en >> 4) & 3;
+                base = blk * 256 + 128 * (win >> 1) + 32 * t + 16 * (win & 1) + 8 * pr;
+            } else {
+                const int pr = (en >> 3) & 3, W = (en >> 5) & 1;
+                base = blk * 256 + 32 * (4 * W + t) + 8 * pr;
+            }
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(J.x + base));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(J.x + base + 4));
+            v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+            v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                mx = fmaxf(mx, fabsf(v[i][k]));
+        }
+    }
+    // activation sums per scale group: Q4_K 32 weights (8 a block), Q6_K 16 weights indexed
+    // 8n + 2q + h like the scales (16 a block)
+    const int per = J.is_q6 ? 16 : 32, ngr = cols / per;
+    float xsum = 0.f;
+    if (tid < ngr) {
+        int start;
+        if (J.is_q6) {
+            const int blk = tid >> 4, k = tid & 15;
+            start = blk * 256 + 128 * (k >> 3) + 32 * ((k >> 1) & 3) + 16 * (k & 1);
+        } else {
+            start = tid * 32;
+        }
+        const float4 *xp = reinterpret_cast<const float4 *>(J.x + start);
+        float4 xv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            xv[i] = (i < per / 4) ? __ldg(xp + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            xsum += (xv[i].x + xv[i].y) + (xv[i].z + xv[i].w);
+    }
+    float *red = reinterpret_cast<float *>(sm + kOffMisc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0)
+        red[tid >> 5] = mx;
+    if (!jb_sync(jb, jph, tid & 31))
+        return false;
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kCWarps; i++)
+        mx = fmaxf(mx, red[i]);
+    int E = 0;
+    if (mx > 0.f && mx < 3.0e38f)
+        frexpf(mx, &E);
+    e = max(-100, min(100, 14 - E));
+    const float scale = ldexpf(1.f, e);
+    uint4 *bt = reinterpret_cast<uint4 *>(sm + kOffBtab);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int en = tid + i * kCThreads;
+        if (en < nent) {
+            const bool lo = en & 1;
+            uint32_t hw[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float s = v[i][k] * scale;
+                const __half hh = __float2half_rn(s);
+                hw[k] = (uint32_t)__half_as_ushort(lo ? __float2half_rn(s - __half2float(hh)) : hh);
+            }
+            bt[en] = make_uint4(hw[0] | (hw[2] << 16), hw[1] | (hw[3] << 16), hw[4] | (hw[6] << 16),
+                                hw[5] | (hw[7] << 16));
+        }
+    }
+    if (tid < ngr)
+        reinterpret_cast<float *>(sm + kOffXsum)[tid] = xsum;
+    return jb_sync(jb, jph, tid & 31);
+}
+
+__device__ __forceinline__ int tile_job(const SParams &p, long long t)
+{
+    int lo = 0, hi = p.njobs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.jobs[mid].tile0 <= t)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+// One warp's share of a CTA segment of job J: its tiles jt0 + warp, jt0 + warp + 16, ... < jt1
+// (job-relative), each streamed block by block through the warp's S-stage ring; the copies of the
+// item S - 1 ahead are issued before an item is multiplied. Tile, block and stage advance as
+// counters (no divisions in the loop); each lane's copy offsets within an item are fixed.
+template <int S, bool Q6>
+__device__ __forceinline__ void run_segment(const SJob &J, long long jt0, long long jt1, unsigned char *ring,
+                                            const uint4 *btab, const float *xsum, int e, const Lane &L, int warp,
+                                            int lane)
+{
+    constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
+    constexpr int kStage = 16 * kSlot;
+    constexpr int kChunks = kSlot / 16;                    // 16-byte chunks per row slot
+    constexpr int kCopies = (16 * kChunks + 31) / 32;      // per lane per item
+    constexpr int kBsz = Q6 ? 210 : 144;
+    const long long first = jt0 + warp;
+    if (first >= jt1)
+        return;
+    const int nb = J.nb;
+    const int rb = nb * kBsz;
+    const long long tstep = (long long)kCWarps * 16 * rb;  // bytes from one of this warp's tiles to the next
+    // this lane's copies: row r and chunk c of each slot
+    int cr[kCopies], coff[kCopies];
+#pragma unroll
+    for (int i = 0; i < kCopies; i++) {
+        const int k = lane + 32 * i;
+        cr[i] = k < 16 * kChunks ? k / kChunks : 0x40000000;   // beyond every row count: no copy
+        const int c = k - (k / kChunks) * kChunks;
+        coff[i] = cr[i] * kSlot + 16 * c;
+    }
+    const int ntiles = (int)((jt1 - first + kCWarps - 1) / kCWarps);
+    // issue state
+    int is_b = 0, is_s = 0, is_t = 0;
+    long long is_row0 = first * 16, is_off = first * 16 * (long long)rb;
+    auto issue = [&]() {
+        if (is_t < ntiles) {
+            unsigned char *st = ring + is_s * kStage;
+            const long long lim = J.rows - is_row0;
+#pragma unroll
+            for (int i = 0; i < kCopies; i++) {
+                if (cr[i] < lim) {
+                    if (!Q6) {
+                        cp_async16(smem_addr(st + coff[i]),
+                                   J.w + is_off + (long long)cr[i] * rb + is_b * 144 + (coff[i] - cr[i] * kSlot));
+                    } else {
+                        const long long o = is_off + (long long)cr[i] * rb + 210 * is_b, a = o & ~15ll;
+                        const int c16 = coff[i] - cr[i] * kSlot;
+                        if (c16 < (int)(o - a) + 210)
+                            cp_async16(smem_addr(st + coff[i]), J.w + a + c16);
+                    }
+                }
+            }
+            if (++is_b == nb) {
+                is_b = 0;
+                is_t++;
+                is_row0 += 16 * kCWarps;
+                is_off += tstep;
+            }
+            is_s = is_s + 1 == S ? 0 : is_s + 1;
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int q = 0; q < S - 1; q++)
+        issue();
+    const float f = ldexpf(1.f, Q6 ? 24 - e : 24 - 4 * (L.t & 1) - e);
+    float acc_a = 0.f, acc_b = 0.f;
+    int b = 0, cs = 0;
+    long long row0 = first * 16, off = first * 16 * (long long)rb;
+    for (int tleft = ntiles; tleft > 0;) {
+        cp_async_wait<S - 2>();
+        __syncwarp();        // every lane's copies of this item have landed; the previous stage is free
+        issue();
+        const unsigned char *st = ring + cs * kStage;
+        if (!Q6) {
+            q4_mma_block(st + L.g * kSlot, st + (L.g + 8) * kSlot, btab + b * 64, xsum + b * 8, f, L, acc_a, acc_b);
+        } else {
+            const int ma = (int)((off + (long long)L.g * rb + 210 * b) & 15);
+            const int mb = (int)((off + (long long)(L.g + 8) * rb + 210 * b) & 15);
+            q6_mma_block(st + L.g * kSlot + ma, st + (L.g + 8) * kSlot + mb, btab + b * 64, xsum + b * 16, f, L,
+                         acc_a, acc_b);
+        }
+        cs = cs + 1 == S ? 0 : cs + 1;
+        if (++b == nb) {
+            acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+            acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
+            acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+            acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
+            if (L.t == 0) {
+                if (row0 + L.g < J.rows)
+                    J.y[row0 + L.g] = acc_a;
+                if (row0 + L.g + 8 < J.rows)
+                    J.y[row0 + L.g + 8] = acc_b;
+            }
+            acc_a = acc_b = 0.f;
+            b = 0;
+            row0 += 16 * kCWarps;
+            off += tstep;
+            tleft--;
+        }
+    }
+    cp_async_wait<0>();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const __grid_constant__ SParams p)
+{
+    extern __shared__ __align__(128) unsigned char sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const uint32_t jb = smem_addr(sm + kOffBar);
+    if (tid == 0) {
+        mbar_init(jb, kCWarps);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    Lane L;
+    L.g = lane >> 2;
+    L.t = lane & 3;
+    L.bnz = (L.g >> 1) == L.t;
+    L.l8 = 2 * L.t + (L.g & 1);
+    L.sel = 0x7650u | (uint32_t)L.t;
+    unsigned char *ring = sm + warp * kRingBytes;
+    const uint4 *btab = reinterpret_cast<const uint4 *>(sm + kOffBtab);
+    const float *xsum = reinterpret_cast<const float *>(sm + kOffXsum);
+    uint32_t jph = 0;
+    long long t = p.cta_tile[blockIdx.x];
+    const long long t1 = p.cta_tile[blockIdx.x + 1];
+    while (t < t1) {
+        const int j = tile_job(p, t);
+        const SJob &J = p.jobs[j];
+        const long long jend = j + 1 < p.njobs ? p.jobs[j + 1].tile0 : p.tiles;
+        const long long send = min(t1, jend);
+        int e = 0;
+        // every warp is past the previous segment, then the tables of job j
+        if (!jb_sync(jb, jph, lane) || !build_tables(J, sm, tid, jb, jph, e)) {
+            if (tid == 0)
+                atomicOr(p.err, kErrWaitTimeout);
+            return;
+        }
+        if (J.is_q6)
+            run_segment<kQ6Stages, true>(J, t - J.tile0, send - J.tile0, ring, btab, xsum, e, L, warp, lane);
+        else
+            run_segment<kQ4Stages, false>(J, t - J.tile0, send - J.tile0, ring, btab, xsum, e, L, warp, lane);
+        t = send;
+    }
+}
+
+// ---------------------------------------------------------------- row kernel (global memory)
+
+// Scale and min j (0..7) of a Q4_K block from its 12 scale bytes held as three words.
+__device__ __forceinline__ void q4_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, float &sc, float &mn)
+{
+    const int k = (j & 3) * 8;
+    const uint32_t a = (s0 >> k) & 0xFFu, b = (s1 >> k) & 0xFFu, c = (s2 >> k) & 0xFFu;
+    if (j < 4) {
+        sc = (float)(a & 63u);
+        mn = (float)(b & 63u);
+    } else {
+        sc = (float)((c & 0x0Fu) | ((a >> 6) << 4));
+        mn = (float)((c >> 4) | ((b >> 6) << 4));
+    }
+}
+
+__device__ __forceinline__ float q4_row(const unsigned char *w, const float *x, int nb, int lane)
+{
+    const int g = lane >> 3, i0 = (lane & 7) * 4;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int b = 0; b < nb; b++) {
+        const unsigned char *blk = w + (size_t)b * 144;
+        const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+        const uint32_t qw = __ldg(reinterpret_cast<const uint32_t *>(blk + 16) + lane);
+        const float4 xl = __ldg(reinterpret_cast<const float4 *>(x + b * 256 + 64 * g + i0));
+        const float4 xh = __ldg(reinterpret_cast<const float4 *>(x + b * 256 + 64 * g + 32 + i0));
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+        float sc0, m0, sc1, m1;
+        q4_scale_min(hdr.y, hdr.z, hdr.w, 2 * g, sc0, m0);
+        q4_scale_min(hdr.y, hdr.z, hdr.w, 2 * g + 1, sc1, m1);
+        const float ql0 = (float)(qw & 15), ql1 = (float)((qw >> 8) & 15);
+        const float ql2 = (float)((qw >> 16) & 15), ql3 = (float)((qw >> 24) & 15);
+        const float qh0 = (float)((qw >> 4) & 15), qh1 = (float)((qw >> 12) & 15);
+        const float qh2 = (float)((qw >> 20) & 15), qh3 = (float)(qw >> 28);
+        const float dl = fmaf(ql3, xl.w, fmaf(ql2, xl.z, fmaf(ql1, xl.y, ql0 * xl.x)));
+        const float dh = fmaf(qh3, xh.w, fmaf(qh2, xh.z, fmaf(qh1, xh.y, qh0 * xh.x)));
+        const float sl = (xl.x + xl.y) + (xl.z + xl.w), sh = (xh.x + xh.y) + (xh.z + xh.w);
+        acc = fmaf(d * sc0, dl, acc);
+        acc = fmaf(-dmin * m0, sl, acc);
+        acc = fmaf(d * sc1, dh, acc);
+        acc = fmaf(-dmin * m1, sh, acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ float q6_row(const unsigned char *w, const float *x, int nb, int lane)
+{
+    const int hs = lane >> 4;
+    float acc = 0.f;
+#pragma unroll 2
+    for (int b = 0; b < nb; b++) {
+        const unsigned char *blk = w + (size_t)b * 210;
+        const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(blk + 208))));
+        const signed char *sc = reinterpret_cast<const signed char *>(blk + 192);
+        const float *xb = x + b * 256;
+        float part = 0.f;
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            const int a = __ldg(blk + 64 * n + lane), c = __ldg(blk + 64 * n + 32 + lane);
+            const int h = __ldg(blk + 128 + 32 * n + lane);
+            const int q1 = ((a & 15) | ((h & 3) << 4)) - 32;
+            const int q2 = ((c & 15) | (((h >> 2) & 3) << 4)) - 32;
+            const int q3 = ((a >> 4) | (((h >> 4) & 3) << 4)) - 32;
+            const int q4 = ((c >> 4) | (((h >> 6) & 3) << 4)) - 32;
+            const int is = 8 * n + hs;
+            const float x1 = __ldg(xb + 128 * n + lane), x2 = __ldg(xb + 128 * n + 32 + lane);
+            const float x3 = __ldg(xb + 128 * n + 64 + lane), x4 = __ldg(xb + 128 * n + 96 + lane);
+            part = fmaf((float)(__ldg(sc + is) * q1), x1, part);
+            part = fmaf((float)(__ldg(sc + is + 2) * q2), x2, part);
+            part = fmaf((float)(__ldg(sc + is + 4) * q3), x3, part);
+            part = fmaf((float)(__ldg(sc + is + 6) * q4), x4, part);
+        }
+        acc = fmaf(d, part, acc);
+    }
+    return acc;
+}
+
+constexpr int kRowWarps = 8;
+constexpr int kRowsPerWarp = 2;
+
+__global__ void __launch_bounds__(kRowWarps * 32) quant_matvec_row_kernel(const __grid_constant__ DParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long base = ((long long)blockIdx.x * kRowWarps + warp) * kRowsPerWarp;
+#pragma unroll 1
+    for (int rr = 0; rr < kRowsPerWarp; rr++) {
+        const long long grow = base + rr;
+        if (grow >= p.drows)
+            return;
+        int lo = 0, hi = p.njobs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.jobs[mid].drow0 <= grow)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        const DJob &J = p.jobs[lo];
+        const long long r = grow - J.drow0;
+        float acc;
+        if (J.is_q6)
+            acc = q6_row(J.w + (size_t)r * J.nb * 210, J.x, J.nb, lane);
+        else
+            acc = q4_row(J.w + (size_t)r * J.nb * 144, J.x, J.nb, lane);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0)
+            J.y[r] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- host
+
+int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
+{
+    static bool attr_set = false;
+    SParams sp;
+    DParams dp;
+    memset(static_cast<void *>(&sp), 0, sizeof(sp));
+    memset(static_cast<void *>(&dp), 0, sizeof(dp));
+    double tile_bytes[kMaxJobs];
+    double total = 0.0;
+    for (int i = 0; i < n; i++) {
+        const KernelCudaMatvecJob &j = jobs[i];
+        if (!j.matrix || !j.vector || !j.output)
+            return fail("kernel_cuda_matvec_quant_batch: job %d has a null pointer", i);
+        if (j.cols == 0 || j.cols % 256 != 0 || j.cols > (1u << 24))
+            return fail("kernel_cuda_matvec_quant_batch: job %d cols %zu must be a positive multiple of 256", i,
+                        j.cols);
+        if (!aligned16(j.vector) || (!j.is_q6 && !aligned16(j.matrix)) ||
+            (j.is_q6 && (reinterpret_cast<uintptr_t>(j.matrix) & 1)))
+            return fail("kernel_cuda_matvec_quant_batch: job %d misaligned (vector 16 B, Q4_K matrix 16 B, "
+                        "Q6_K matrix 2 B)", i);
+        if (j.rows == 0)
+            continue;
+        const int nb = (int)(j.cols / 256);
+        const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
+        const unsigned char *w = static_cast<const unsigned char *>(j.matrix);
+        long long srows = 0;
+        if (aligned16(j.matrix) && nb <= kMaxNb) {
+            srows = (long long)j.rows;
+            // the copies read whole 16-byte windows: a Q6_K matrix whose end is not 16-byte
+            // aligned keeps its last row out of the tiles, so no window reaches past the matrix
+            if (j.is_q6 && ((long long)j.rows * nb) % 8 != 0)
+                srows -= 1;
+        }
+        if (srows > 0) {
+            tile_bytes[sp.njobs] = 16.0 * (double)rb;
+            sp.jobs[sp.njobs++] = SJob{w, j.vector, j.output, sp.tiles, srows, nb, j.is_q6 ? 1 : 0};
+            sp.tiles += (srows + 15) / 16;
+            total += (double)srows * (double)rb;
+        }
+        if (srows < (long long)j.rows) {
+            dp.jobs[dp.njobs++] = DJob{w + srows * rb, j.vector, j.output + srows, dp.drows,
+                                       (long long)j.rows - srows, nb, j.is_q6 ? 1 : 0};
+            dp.drows += (long long)j.rows - srows;
+        }
+    }
+    Runtime &R = rt();
+    if (sp.tiles > 0) {
+        if (!attr_set) {
+            if (check(cudaFuncSetAttribute(quant_matvec_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kSmemBytes), "matvec shared memory") != 0)
+                return -1;
+            attr_set = true;
+        }
+        // contiguous tile ranges of about equal bytes per CTA
+        const int G = (int)std::min<long long>(std::min(R.num_sms, kMaxCtas), sp.tiles);
+        for (int c = 0; c <= G; c++) {
+            const double target = total * c / G;
+            long long idx = sp.tiles;
+            double cum = 0.0;
+            for (int q = 0; q < sp.njobs && c < G; q++) {
+                const long long nt = (q + 1 < sp.njobs ? sp.jobs[q + 1].tile0 : sp.tiles) - sp.jobs[q].tile0;
+                const double jb = tile_bytes[q] * (double)nt;
+                if (target < cum + jb) {
+                    idx = sp.jobs[q].tile0 + (long long)((target - cum) / tile_bytes[q]);
+                    break;
+                }
+                cum += jb;
+            }
+            sp.cta_tile[c] = c == 0 ? 0 : std::max(idx, sp.cta_tile[c - 1]);
+        }
+        sp.cta_tile[G] = sp.tiles;
+        sp.err = R.err_word;
+        quant_matvec_staged_kernel<<<(unsigned)G, kThreads, kSmemBytes, R.stream>>>(sp);
+        if (launched("quant_matvec_staged_kernel") != 0)
+            return -1;
+    }
+    if (dp.drows > 0) {
+        const long long per_cta = (long long)kRowWarps * kRowsPerWarp;
+        quant_matvec_row_kernel<<<(unsigned)((dp.drows + per_cta - 1) / per_cta), kRowWarps * 32, 0, R.stream>>>(dp);
+        if (launched("quant_matvec_row_kernel") != 0)
+            return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_cuda_matvec_quant_batch: bad job array");
+    for (int i = 0; i < n; i += kMaxJobs)
+        if (matvec_chunk(jobs + i, std::min(kMaxJobs, n - i)) != 0)
+            return -1;
+    return 0;
+}

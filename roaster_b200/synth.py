@@ -102,6 +102,25 @@ def delta_layer_inputs(seed: int, T: int):
     }
 
 
+def quant_matrix(seed: int, rows: int, cols: int, is_q6: bool):
+    """Random k-quant weights (uint8 blocks) with realistic scale ranges: Q4_K d, dmin ~ U[1e-3,
+    1e-2] as f16 and random 6-bit scales/mins and nibbles; Q6_K d ~ U[1e-3, 1e-2], int8 scales
+    in [-64, 63], random 6-bit values. Shape [rows * cols/256 * (210 | 144)]."""
+    rng = np.random.default_rng(seed)
+    nb = rows * (cols // 256)
+    if not is_q6:
+        blk = rng.integers(0, 256, (nb, 144), dtype=np.uint8)
+        d = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        m = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        blk[:, 0:2] = d
+        blk[:, 2:4] = m
+    else:
+        blk = rng.integers(0, 256, (nb, 210), dtype=np.uint8)
+        blk[:, 192:208] = rng.integers(-64, 64, (nb, 16)).astype(np.int8).view(np.uint8)
+        blk[:, 208:210] = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return blk.reshape(-1)
+
+
 def slot_lengths(seed: int, slots: int, lo: int = 1024, hi: int = 32768):
     """Config 2: per-slot context lengths ~ U[lo, hi] (integers, inclusive)."""
     rng = np.random.default_rng(seed)

@@ -129,3 +129,18 @@ def test_port_vs_reference_delta_layer(oracle_lib, T):
     assert np.array_equal(a, b)
     assert np.array_equal(s1, s2)
     assert np.array_equal(c1, c2)
+
+
+@pytest.mark.parametrize("q6", [False, True])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (300, 2048), (33, 4096)])
+def test_port_vs_reference_matvec_q(oracle_lib, q6, rows, cols):
+    """The oracle's Q4_K / Q6_K matvec against the reference's own kernel_dot_q4_k /
+    kernel_dot_q6_k per row (matvec_q4_cpu / matvec_q6_cpu): fp32 sums in a different order,
+    so 2e-6 maxrel rather than bit equality."""
+    if not O.have_ref():
+        pytest.skip("reference build (oracle/_ref) not present")
+    m = synth.quant_matrix(rows + cols, rows, cols, q6)
+    x = np.random.default_rng(rows).standard_normal(cols).astype(np.float32)
+    a = O.matvec_q(q6, m, x, rows, cols, impl="port")
+    b = O.matvec_q(q6, m, x, rows, cols, impl="ref")
+    assert O.maxrel(a, b) < 2e-6
