@@ -32,7 +32,8 @@
 //  * The B fragments of a job (1 KB per block) and its activation sums per scale group (for the
 //    Q4_K min and the Q6_K -32 terms) are built in shared memory at the start of each job a CTA
 //    works on (the only CTA-wide syncs, on a bounded mbarrier). CTAs take contiguous tile ranges
-//    of equal bytes.
+//    of about equal cost. When a call has fewer than two tiles per warp, tiles split into 2-16 parts
+//    along the blocks; parts leave fp32 partials and the last one of a tile sums them in order.
 //
 // Rows the staged kernel does not take (a matrix not 16-byte aligned, rows longer than 4096
 // weights, the last row of a Q6_K matrix whose end is not 16-byte aligned) run in the row kernel:
@@ -64,26 +65,33 @@ constexpr int kMaxNb = 16;                       // staged path: up to 16 blocks
 constexpr int kOffBtab = kCWarps * kRingBytes;   // B fragments: 1 KB per block
 constexpr int kOffXsum = kOffBtab + kMaxNb * 1024;   // activation sums: 16 a block (Q6_K), 8 (Q4_K)
 constexpr int kOffMisc = kOffXsum + kMaxNb * 16 * 4; // max reduction (one float per warp)
-constexpr int kOffBar = kOffMisc + kCWarps * 4;      // job barrier
+constexpr int kOffJobs = kOffMisc + kCWarps * 4;     // the job table, copied from the parameters
+constexpr int kOffZero = kOffJobs + kMaxJobs * 80;   // 1 KB of zeros: B fragments of the zero lanes
+constexpr int kOffBar = kOffZero + 1024;             // job barrier
 constexpr int kSmemBytes = kOffBar + 8;
 constexpr int kMaxCtas = 160;
 static_assert(kSmemBytes <= 232448, "staged matvec exceeds the shared memory of a CTA");
 static_assert(kQ4Stages >= 3 && kQ6Stages >= 3, "rings too small");
+static_assert(kOffJobs % 16 == 0, "job table alignment");
 
 struct SJob {
     const unsigned char *w;      // rows x nb blocks, 16-byte aligned
     const float *x;
     float *y;
-    long long tile0;             // first global tile (16 rows) of the job
+    float *part;                 // split tiles: partial sums [tile][part][16]
+    int *cnt;                    // split tiles: arrivals per tile (zero between calls)
+    long long item0;             // first global item (a tile of 16 rows, or a part of one) of the job
     long long rows;              // rows in tiles (the last Q6_K row may go to the row kernel)
-    int nb, is_q6;
+    int nb, is_q6, plog;         // blocks per row; format; log2 of the parts per tile
 };
+
+static_assert(sizeof(SJob) <= 80, "job table slot");
 
 struct SParams {
     SJob jobs[kMaxJobs];
     int njobs;
-    long long tiles;
-    long long cta_tile[kMaxCtas + 1];   // CTA c takes tiles [cta_tile[c], cta_tile[c + 1])
+    long long items;
+    long long cta_item[kMaxCtas + 1];   // CTA c takes items [cta_item[c], cta_item[c + 1])
     unsigned *err;
 };
 
@@ -107,6 +115,14 @@ struct DParams {
 __device__ __forceinline__ void cp_async_commit()
 {
     asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Device-scope acquire-release increment; returns the old value.
+__device__ __forceinline__ int arrive_acq_rel(int *p)
+{
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+    return old;
 }
 
 template <int N>
@@ -166,7 +182,8 @@ struct Lane {
 };
 
 // One Q4_K block of rows (g, g + 8) of a tile: window W covers sub-blocks 4W..4W+3, lane t's
-// k-slots hold sub-block 4W + t (byte group 2W + t/2, nibble t&1), eight MMAs per window.
+// k-slots hold sub-block 4W + t (byte group 2W + t/2, nibble t&1), eight MMAs per window. `bt` is
+// this lane's B column: its entries of the block's table, or the zero area for a zero lane.
 __device__ __forceinline__ void q4_mma_block(const unsigned char *pa, const unsigned char *pb, const uint4 *bt,
                                              const float *xs, float f4, const Lane &L, float &acc_a, float &acc_b)
 {
@@ -197,13 +214,10 @@ __device__ __forceinline__ void q4_mma_block(const unsigned char *pa, const unsi
         const int G = 2 * W + (L.t >> 1);
         const uint4 qa0 = lds128(pa + 16 + 32 * G), qa1 = lds128(pa + 32 + 32 * G);
         const uint4 qb0 = lds128(pb + 16 + 32 * G), qb1 = lds128(pb + 32 + 32 * G);
-        uint4 bf[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                       make_uint4(0, 0, 0, 0)};
-        if (L.bnz) {
+        uint4 bf[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                bf[i] = bt[(W * 4 + i) * 8 + L.l8];
-        }
+        for (int i = 0; i < 4; i++)
+            bf[i] = bt[(W * 4 + i) * 8];
         float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 8; s++) {
@@ -258,11 +272,7 @@ __device__ __forceinline__ void q6_mma_block(const unsigned char *pa, const unsi
         q6_words(pb, 64 * n + 32 * (L.t & 1) + 16 * h, lb);
         q6_words(pa, 128 + 32 * n + 16 * h, ha);
         q6_words(pb, 128 + 32 * n + 16 * h, hb);
-        uint4 bf[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-        if (L.bnz) {
-            bf[0] = bt[(win * 2 + 0) * 8 + L.l8];
-            bf[1] = bt[(win * 2 + 1) * 8 + L.l8];
-        }
+        const uint4 bf[2] = {bt[(win * 2 + 0) * 8], bt[(win * 2 + 1) * 8]};
         float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 4; s++) {
@@ -389,12 +399,12 @@ __device__ bool build_tables(const SJob &J, unsigned char *sm, int tid, uint32_t
     return jb_sync(jb, jph, tid & 31);
 }
 
-__device__ __forceinline__ int tile_job(const SParams &p, long long t)
+__device__ __forceinline__ int item_job(const SJob *jobs, int njobs, long long t)
 {
-    int lo = 0, hi = p.njobs - 1;
+    int lo = 0, hi = njobs - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (p.jobs[mid].tile0 <= t)
+        if (jobs[mid].item0 <= t)
             lo = mid;
         else
             hi = mid - 1;
@@ -402,62 +412,67 @@ __device__ __forceinline__ int tile_job(const SParams &p, long long t)
     return lo;
 }
 
-// One warp's share of a CTA segment of job J: its tiles jt0 + warp, jt0 + warp + 16, ... < jt1
-// (job-relative), each streamed block by block through the warp's S-stage ring; the copies of the
-// item S - 1 ahead are issued before an item is multiplied. Tile, block and stage advance as
-// counters (no divisions in the loop); each lane's copy offsets within an item are fixed.
+// One warp's share of a CTA segment of job J: its items it0 + warp, it0 + warp + 16, ... < it1
+// (job-relative). Item i is part i & (P-1) of tile i >> plog: blocks [part * nb/P, +nb/P) of 16
+// rows, streamed block by block through the warp's S-stage ring; the copies of the block S - 1
+// ahead are issued before a block is multiplied. Items, blocks and stages advance as counters;
+// each lane's copy offsets within a block are fixed. A whole tile (P = 1) stores y directly; the
+// parts of a split tile store fp32 partials, and the last part to arrive (a counter per tile,
+// returned to zero) sums them in part order into y.
 template <int S, bool Q6>
-__device__ __forceinline__ void run_segment(const SJob &J, long long jt0, long long jt1, unsigned char *ring,
-                                            const uint4 *btab, const float *xsum, int e, const Lane &L, int warp,
+__device__ __forceinline__ bool run_segment(const SJob &J, long long it0, long long it1, unsigned char *sm,
+                                            unsigned char *ring, uint32_t jb, uint32_t &jph, const Lane &L, int warp,
                                             int lane)
 {
     constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
     constexpr int kStage = 16 * kSlot;
     constexpr int kChunks = kSlot / 16;                    // 16-byte chunks per row slot
-    constexpr int kCopies = (16 * kChunks + 31) / 32;      // per lane per item
+    constexpr int kCopies = (16 * kChunks + 31) / 32;      // per lane per block
     constexpr int kBsz = Q6 ? 210 : 144;
-    const long long first = jt0 + warp;
-    if (first >= jt1)
-        return;
-    const int nb = J.nb;
+    const long long first = it0 + warp;
+    const int nb = J.nb, plog = J.plog, P = 1 << plog, nbp = nb >> plog;
     const int rb = nb * kBsz;
-    const long long tstep = (long long)kCWarps * 16 * rb;  // bytes from one of this warp's tiles to the next
-    // this lane's copies: row r and chunk c of each slot
+    // this lane's copies within a block: slot row cr (beyond every row count: no copy) and
+    // offset coff in the slot row (= in the block's bytes)
     int cr[kCopies], coff[kCopies];
 #pragma unroll
     for (int i = 0; i < kCopies; i++) {
         const int k = lane + 32 * i;
-        cr[i] = k < 16 * kChunks ? k / kChunks : 0x40000000;   // beyond every row count: no copy
-        const int c = k - (k / kChunks) * kChunks;
-        coff[i] = cr[i] * kSlot + 16 * c;
+        const int r = k / kChunks;
+        cr[i] = k < 16 * kChunks ? r : 0x40000000;
+        coff[i] = 16 * (k - r * kChunks);
     }
-    const int ntiles = (int)((jt1 - first + kCWarps - 1) / kCWarps);
-    // issue state
-    int is_b = 0, is_s = 0, is_t = 0;
-    long long is_row0 = first * 16, is_off = first * 16 * (long long)rb;
+    const int nitems = first < it1 ? (int)((it1 - first + kCWarps - 1) / kCWarps) : 0;
+    // issue state: item, block within the item, stage
+    int is_n = 0, is_b = 0, is_s = 0;
+    long long is_it = first;
     auto issue = [&]() {
-        if (is_t < ntiles) {
+        if (is_n < nitems) {
             unsigned char *st = ring + is_s * kStage;
-            const long long lim = J.rows - is_row0;
+            const long long row0 = (is_it >> plog) * 16;
+            const int b = (int)(is_it & (P - 1)) * nbp + is_b;
+            const int lim = (int)min(16ll, J.rows - row0);
+            if (!Q6) {
+                const unsigned char *src = J.w + row0 * rb + b * 144;
 #pragma unroll
-            for (int i = 0; i < kCopies; i++) {
-                if (cr[i] < lim) {
-                    if (!Q6) {
-                        cp_async16(smem_addr(st + coff[i]),
-                                   J.w + is_off + (long long)cr[i] * rb + is_b * 144 + (coff[i] - cr[i] * kSlot));
-                    } else {
-                        const long long o = is_off + (long long)cr[i] * rb + 210 * is_b, a = o & ~15ll;
-                        const int c16 = coff[i] - cr[i] * kSlot;
-                        if (c16 < (int)(o - a) + 210)
-                            cp_async16(smem_addr(st + coff[i]), J.w + a + c16);
+                for (int i = 0; i < kCopies; i++)
+                    if (cr[i] < lim)
+                        cp_async16(smem_addr(st + cr[i] * kSlot + coff[i]), src + cr[i] * rb + coff[i]);
+            } else {
+                const long long o0 = row0 * rb + 210 * b;
+#pragma unroll
+                for (int i = 0; i < kCopies; i++) {
+                    if (cr[i] < lim) {
+                        const long long o = o0 + (long long)cr[i] * rb, a = o & ~15ll;
+                        if (coff[i] < (int)(o - a) + 210)
+                            cp_async16(smem_addr(st + cr[i] * kSlot + coff[i]), J.w + a + coff[i]);
                     }
                 }
             }
-            if (++is_b == nb) {
+            if (++is_b == nbp) {
                 is_b = 0;
-                is_t++;
-                is_row0 += 16 * kCWarps;
-                is_off += tstep;
+                is_n++;
+                is_it += kCWarps;
             }
             is_s = is_s + 1 == S ? 0 : is_s + 1;
         }
@@ -466,43 +481,86 @@ __device__ __forceinline__ void run_segment(const SJob &J, long long jt0, long l
 #pragma unroll
     for (int q = 0; q < S - 1; q++)
         issue();
+    // the first copies are in flight: every warp past the previous segment, then the tables
+    int e = 0;
+    if (!jb_sync(jb, jph, lane) || !build_tables(J, sm, threadIdx.x, jb, jph, e)) {
+        cp_async_wait<0>();
+        return false;
+    }
+    // this lane's B column: its entries of each block's table, or the zero area
+    const uint4 *bcol = L.bnz ? reinterpret_cast<const uint4 *>(sm + kOffBtab) + L.l8
+                              : reinterpret_cast<const uint4 *>(sm + kOffZero);
+    const int bstep = L.bnz ? 64 : 0;
+    const float *xsum = reinterpret_cast<const float *>(sm + kOffXsum);
     const float f = ldexpf(1.f, Q6 ? 24 - e : 24 - 4 * (L.t & 1) - e);
     float acc_a = 0.f, acc_b = 0.f;
-    int b = 0, cs = 0;
-    long long row0 = first * 16, off = first * 16 * (long long)rb;
-    for (int tleft = ntiles; tleft > 0;) {
+    int bi = 0, cs = 0;
+    long long it = first;
+    for (int left = nitems; left > 0;) {
         cp_async_wait<S - 2>();
-        __syncwarp();        // every lane's copies of this item have landed; the previous stage is free
+        __syncwarp();        // every lane's copies of this block have landed; the previous stage is free
         issue();
         const unsigned char *st = ring + cs * kStage;
+        const long long row0 = (it >> plog) * 16;
+        const int b = (int)(it & (P - 1)) * nbp + bi;
         if (!Q6) {
-            q4_mma_block(st + L.g * kSlot, st + (L.g + 8) * kSlot, btab + b * 64, xsum + b * 8, f, L, acc_a, acc_b);
+            q4_mma_block(st + L.g * kSlot, st + (L.g + 8) * kSlot, bcol + b * bstep, xsum + b * 8, f, L, acc_a,
+                         acc_b);
         } else {
-            const int ma = (int)((off + (long long)L.g * rb + 210 * b) & 15);
-            const int mb = (int)((off + (long long)(L.g + 8) * rb + 210 * b) & 15);
-            q6_mma_block(st + L.g * kSlot + ma, st + (L.g + 8) * kSlot + mb, btab + b * 64, xsum + b * 16, f, L,
+            const int ma = (int)(((row0 + L.g) * rb + 210 * b) & 15);
+            const int mb = (int)(((row0 + L.g + 8) * rb + 210 * b) & 15);
+            q6_mma_block(st + L.g * kSlot + ma, st + (L.g + 8) * kSlot + mb, bcol + b * bstep, xsum + b * 16, f, L,
                          acc_a, acc_b);
         }
         cs = cs + 1 == S ? 0 : cs + 1;
-        if (++b == nb) {
+        if (++bi == nbp) {
             acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
             acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
             acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
             acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
-            if (L.t == 0) {
-                if (row0 + L.g < J.rows)
-                    J.y[row0 + L.g] = acc_a;
-                if (row0 + L.g + 8 < J.rows)
-                    J.y[row0 + L.g + 8] = acc_b;
+            if (P == 1) {
+                if (L.t == 0) {
+                    if (row0 + L.g < J.rows)
+                        J.y[row0 + L.g] = acc_a;
+                    if (row0 + L.g + 8 < J.rows)
+                        J.y[row0 + L.g + 8] = acc_b;
+                }
+            } else if (L.t == 0) {
+                float *pp = J.part + ((it >> plog) * P + (it & (P - 1))) * 16;
+                __stcg(pp + L.g, acc_a);
+                __stcg(pp + L.g + 8, acc_b);
             }
             acc_a = acc_b = 0.f;
-            b = 0;
-            row0 += 16 * kCWarps;
-            off += tstep;
-            tleft--;
+            bi = 0;
+            it += kCWarps;
+            left--;
         }
     }
     cp_async_wait<0>();
+    // split tiles: arrive once the warp's copies are done (the acquire-release waits for the
+    // warp's outstanding memory operations); the last part of a tile sums the partials in order
+    if (P > 1) {
+        __syncwarp();        // the partial stores of every lane precede lane 0's release
+        for (long long i = first; i < it1; i += kCWarps) {
+            const long long tile = i >> plog;
+            int last = 0;
+            if (lane == 0)
+                last = arrive_acq_rel(J.cnt + tile) == P - 1;
+            if (__shfl_sync(0xffffffffu, last, 0)) {   // lane 0's acquire covers the other parts
+                const long long row0 = tile * 16;
+                if (lane < 16 && row0 + lane < J.rows) {
+                    const float *tp = J.part + tile * P * 16 + lane;
+                    float v = 0.f;
+                    for (int q = 0; q < P; q++)
+                        v += __ldcg(tp + q * 16);
+                    J.y[row0 + lane] = v;
+                }
+                if (lane == 0)
+                    J.cnt[tile] = 0;
+            }
+        }
+    }
+    return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const __grid_constant__ SParams p)
@@ -510,6 +568,15 @@ __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const 
     extern __shared__ __align__(128) unsigned char sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const uint32_t jb = smem_addr(sm + kOffBar);
+    SJob *jobs = reinterpret_cast<SJob *>(sm + kOffJobs);
+    // the job table into shared memory: one job per warp, uniform parameter reads
+    for (int q = warp; q < p.njobs; q += kCWarps) {
+        const SJob src = p.jobs[q];
+        if (lane == 0)
+            jobs[q] = src;
+    }
+    if (tid < 64)
+        reinterpret_cast<uint4 *>(sm + kOffZero)[tid] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
         mbar_init(jb, kCWarps);
         mbar_init_fence();
@@ -522,27 +589,22 @@ __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const 
     L.l8 = 2 * L.t + (L.g & 1);
     L.sel = 0x7650u | (uint32_t)L.t;
     unsigned char *ring = sm + warp * kRingBytes;
-    const uint4 *btab = reinterpret_cast<const uint4 *>(sm + kOffBtab);
-    const float *xsum = reinterpret_cast<const float *>(sm + kOffXsum);
     uint32_t jph = 0;
-    long long t = p.cta_tile[blockIdx.x];
-    const long long t1 = p.cta_tile[blockIdx.x + 1];
+    long long t = p.cta_item[blockIdx.x];
+    const long long t1 = p.cta_item[blockIdx.x + 1];
     while (t < t1) {
-        const int j = tile_job(p, t);
-        const SJob &J = p.jobs[j];
-        const long long jend = j + 1 < p.njobs ? p.jobs[j + 1].tile0 : p.tiles;
+        const int j = item_job(jobs, p.njobs, t);
+        const SJob &J = jobs[j];
+        const long long jend = j + 1 < p.njobs ? jobs[j + 1].item0 : p.items;
         const long long send = min(t1, jend);
-        int e = 0;
-        // every warp is past the previous segment, then the tables of job j
-        if (!jb_sync(jb, jph, lane) || !build_tables(J, sm, tid, jb, jph, e)) {
+        const bool ok = J.is_q6
+            ? run_segment<kQ6Stages, true>(J, t - J.item0, send - J.item0, sm, ring, jb, jph, L, warp, lane)
+            : run_segment<kQ4Stages, false>(J, t - J.item0, send - J.item0, sm, ring, jb, jph, L, warp, lane);
+        if (!ok) {
             if (tid == 0)
                 atomicOr(p.err, kErrWaitTimeout);
             return;
         }
-        if (J.is_q6)
-            run_segment<kQ6Stages, true>(J, t - J.tile0, send - J.tile0, ring, btab, xsum, e, L, warp, lane);
-        else
-            run_segment<kQ4Stages, false>(J, t - J.tile0, send - J.tile0, ring, btab, xsum, e, L, warp, lane);
         t = send;
     }
 }
@@ -670,8 +732,8 @@ int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
     DParams dp;
     memset(static_cast<void *>(&sp), 0, sizeof(sp));
     memset(static_cast<void *>(&dp), 0, sizeof(dp));
-    double tile_bytes[kMaxJobs];
-    double total = 0.0;
+    long long tiles[kMaxJobs];
+    long long total_tiles = 0;
     for (int i = 0; i < n; i++) {
         const KernelCudaMatvecJob &j = jobs[i];
         if (!j.matrix || !j.vector || !j.output)
@@ -697,10 +759,9 @@ int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
                 srows -= 1;
         }
         if (srows > 0) {
-            tile_bytes[sp.njobs] = 16.0 * (double)rb;
-            sp.jobs[sp.njobs++] = SJob{w, j.vector, j.output, sp.tiles, srows, nb, j.is_q6 ? 1 : 0};
-            sp.tiles += (srows + 15) / 16;
-            total += (double)srows * (double)rb;
+            tiles[sp.njobs] = (srows + 15) / 16;
+            total_tiles += tiles[sp.njobs];
+            sp.jobs[sp.njobs++] = SJob{w, j.vector, j.output, nullptr, nullptr, 0, srows, nb, j.is_q6 ? 1 : 0, 0};
         }
         if (srows < (long long)j.rows) {
             dp.jobs[dp.njobs++] = DJob{w + srows * rb, j.vector, j.output + srows, dp.drows,
@@ -709,31 +770,67 @@ int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
         }
     }
     Runtime &R = rt();
-    if (sp.tiles > 0) {
+    if (sp.njobs > 0) {
         if (!attr_set) {
             if (check(cudaFuncSetAttribute(quant_matvec_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            kSmemBytes), "matvec shared memory") != 0)
                 return -1;
             attr_set = true;
         }
-        // contiguous tile ranges of about equal bytes per CTA
-        const int G = (int)std::min<long long>(std::min(R.num_sms, kMaxCtas), sp.tiles);
-        for (int c = 0; c <= G; c++) {
+        // split tiles into parts (along the blocks) when there are fewer than two tiles per warp
+        const long long warps = (long long)std::min(R.num_sms, kMaxCtas) * kCWarps;
+        int want = 1;
+        while (want < 16 && total_tiles * want < 2 * warps)
+            want <<= 1;
+        long long part_floats = 0, ncnt = 0;
+        double total = 0.0, item_bytes[kMaxJobs];
+        for (int q = 0; q < sp.njobs; q++) {
+            SJob &J = sp.jobs[q];
+            int plog = 0;
+            while ((1 << (plog + 1)) <= want && J.nb % (1 << (plog + 1)) == 0)
+                plog++;
+            J.plog = plog;
+            J.item0 = sp.items;
+            sp.items += tiles[q] << plog;
+            // cost of an item: its bytes, Q6_K weighted by its slower multiply (about 2x per byte)
+            item_bytes[q] = 16.0 * J.nb * (J.is_q6 ? 210 * 2.0 : 144) / (1 << plog);
+            total += item_bytes[q] * (double)(tiles[q] << plog);
+            if (plog > 0) {
+                part_floats += (tiles[q] << plog) * 16;
+                ncnt += tiles[q];
+            }
+        }
+        if (ncnt > 0) {
+            float *part = static_cast<float *>(scratch((size_t)part_floats * sizeof(float)));
+            int *cnt = counters((size_t)ncnt);
+            if (!part || !cnt)
+                return -1;
+            for (int q = 0; q < sp.njobs; q++)
+                if (sp.jobs[q].plog > 0) {
+                    sp.jobs[q].part = part;
+                    sp.jobs[q].cnt = cnt;
+                    part += (tiles[q] << sp.jobs[q].plog) * 16;
+                    cnt += tiles[q];
+                }
+        }
+        // contiguous item ranges of about equal cost per CTA
+        const int G = (int)std::min<long long>(std::min(R.num_sms, kMaxCtas), sp.items);
+        for (int c = 0; c < G; c++) {
             const double target = total * c / G;
-            long long idx = sp.tiles;
+            long long idx = sp.items;
             double cum = 0.0;
-            for (int q = 0; q < sp.njobs && c < G; q++) {
-                const long long nt = (q + 1 < sp.njobs ? sp.jobs[q + 1].tile0 : sp.tiles) - sp.jobs[q].tile0;
-                const double jb = tile_bytes[q] * (double)nt;
+            for (int q = 0; q < sp.njobs; q++) {
+                const long long ni = (q + 1 < sp.njobs ? sp.jobs[q + 1].item0 : sp.items) - sp.jobs[q].item0;
+                const double jb = item_bytes[q] * (double)ni;
                 if (target < cum + jb) {
-                    idx = sp.jobs[q].tile0 + (long long)((target - cum) / tile_bytes[q]);
+                    idx = sp.jobs[q].item0 + (long long)((target - cum) / item_bytes[q]);
                     break;
                 }
                 cum += jb;
             }
-            sp.cta_tile[c] = c == 0 ? 0 : std::max(idx, sp.cta_tile[c - 1]);
+            sp.cta_item[c] = c == 0 ? 0 : std::max(idx, sp.cta_item[c - 1]);
         }
-        sp.cta_tile[G] = sp.tiles;
+        sp.cta_item[G] = sp.items;
         sp.err = R.err_word;
         quant_matvec_staged_kernel<<<(unsigned)G, kThreads, kSmemBytes, R.stream>>>(sp);
         if (launched("quant_matvec_staged_kernel") != 0)

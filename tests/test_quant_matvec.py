@@ -90,6 +90,33 @@ def test_many_jobs(rb, oracle_lib):
         assert O.maxrel(host(y), ref) < TOL
 
 
+@pytest.mark.parametrize("q6", [False, True])
+def test_whole_tiles_and_repeat(rb, oracle_lib, q6):
+    """A call with more tiles (16 rows) than twice the warps keeps tiles whole (y stored directly);
+    small calls split tiles into parts whose partials meet in a per-tile counter that returns to
+    zero, so calling again gives the same result."""
+    rows, cols = 80000, 256
+    m = synth.quant_matrix(31, rows, cols, q6)
+    x = np.random.default_rng(32).standard_normal(cols).astype(np.float32)
+    ref = _ref(q6, m, x, rows, cols)
+    dm, dx = dev(m), dev(x)
+    for _ in range(2):
+        y = torch.zeros(rows, device="cuda")
+        rb.matvec_quant_batch([(q6, dm, dx, y, rows, cols)])
+        assert O.maxrel(host(y), ref) < TOL
+    m2 = synth.quant_matrix(33, 64, 4096, q6)
+    x2 = np.random.default_rng(34).standard_normal(4096).astype(np.float32)
+    ref2 = _ref(q6, m2, x2, 64, 4096)
+    dm2, dx2 = dev(m2), dev(x2)
+    outs = []
+    for _ in range(3):
+        y2 = torch.zeros(64, device="cuda")
+        rb.matvec_quant_batch([(q6, dm2, dx2, y2, 64, 4096)])
+        outs.append(host(y2))
+        assert O.maxrel(outs[-1], ref2) < TOL
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])   # fixed summation order
+
+
 def test_rejects_ragged_cols(rb):
     m = torch.zeros(144, dtype=torch.uint8, device="cuda")
     x = torch.zeros(300, device="cuda")
