@@ -340,6 +340,22 @@ typedef struct {
 
 int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, int n);
 
+/* Replaces kernel_matmul_quant_batch (kernels.h:51-64; CPU matmul_quant_cpu, kernels.c:1877-1913):
+ * multi-token (prefill) projections Y[t*rows + r] = dot(W[r], X[t*cols ...]) for t < T. Same
+ * job validity as the reference (non-null pointers, rows, cols, T > 0, cols a multiple of 256,
+ * each dimension at most 2^32 - 1; -1 otherwise) plus the alignment of
+ * kernel_cuda_matvec_quant_batch (X 16-byte aligned). Device pointers, asynchronous. Runs as
+ * T matrix-vector products per job sharing the (L2-resident) weights. */
+typedef struct {
+    int is_q6;                  /* 0 = Q4_K, 1 = Q6_K */
+    const void *matrix;         /* device, rows x cols quantized */
+    const float *X;             /* device, [T][cols] */
+    float *Y;                   /* device, [T][rows] */
+    size_t rows, cols, T;
+} KernelCudaMatmulJob;
+
+int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, int n);
+
 #ifdef __cplusplus
 }
 #endif

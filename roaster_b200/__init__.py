@@ -73,6 +73,13 @@ class KernelDeltaPostopJob(C.Structure):
     _fields_ = [("out", _vp), ("z", _vp), ("norm_w", _vp), ("T", _sz)]
 
 
+class KernelCudaMatmulJob(C.Structure):
+    """Mirror of ``KernelCudaMatmulJob`` (include/roaster_cuda.h); the reference's KernelMatmulJob
+    (src/kernels.h:57-63) with device pointers."""
+    _fields_ = [("is_q6", C.c_int), ("matrix", _vp), ("X", _vp), ("Y", _vp), ("rows", _sz), ("cols", _sz),
+                ("T", _sz)]
+
+
 class KernelCudaMatvecJob(C.Structure):
     """Mirror of ``KernelCudaMatvecJob`` (include/roaster_cuda.h); the reference's KernelMatvecJob
     (src/kernels.h:34-41) with device pointers."""
@@ -143,6 +150,7 @@ def lib():
         "kernel_deltanet_layer_step": (C.c_int, [_vp] * 11),
         "kernel_deltanet_layer_prefill": (C.c_int, [_vp] * 6 + [_sz] + [_vp] * 5),
         "kernel_cuda_matvec_quant_batch": (C.c_int, [C.POINTER(KernelCudaMatvecJob), C.c_int]),
+        "kernel_cuda_matmul_quant_batch": (C.c_int, [C.POINTER(KernelCudaMatmulJob), C.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -292,3 +300,13 @@ def matvec_quant_batch(jobs) -> None:
           for j in jobs]
     arr, n = _arr(KernelCudaMatvecJob, js)
     check(lib().kernel_cuda_matvec_quant_batch(arr, n), "kernel_cuda_matvec_quant_batch")
+
+
+def matmul_quant_batch(jobs) -> None:
+    """kernel_cuda_matmul_quant_batch over jobs given as KernelCudaMatmulJob or
+    (is_q6, matrix, X, Y, rows, cols, T) with device tensors or addresses."""
+    js = [j if isinstance(j, KernelCudaMatmulJob) else
+          KernelCudaMatmulJob(int(bool(j[0])), _ptr(j[1]), _ptr(j[2]), _ptr(j[3]), int(j[4]), int(j[5]), int(j[6]))
+          for j in jobs]
+    arr, n = _arr(KernelCudaMatmulJob, js)
+    check(lib().kernel_cuda_matmul_quant_batch(arr, n), "kernel_cuda_matmul_quant_batch")

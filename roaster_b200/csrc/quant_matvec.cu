@@ -46,6 +46,7 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <cstring>
+#include <vector>
 
 namespace rb {
 namespace {
@@ -860,4 +861,24 @@ extern "C" int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, i
         if (matvec_chunk(jobs + i, std::min(kMaxJobs, n - i)) != 0)
             return -1;
     return 0;
+}
+
+extern "C" int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, int n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n < 0 || (n > 0 && !jobs))
+        return fail("kernel_cuda_matmul_quant_batch: bad job array");
+    std::vector<KernelCudaMatvecJob> mv;
+    for (int i = 0; i < n; i++) {
+        const KernelCudaMatmulJob &j = jobs[i];
+        // the reference's mm_job_valid (kernels.c:1916-1920)
+        if (!j.matrix || !j.X || !j.Y || !j.rows || !j.cols || !j.T || j.cols % 256 != 0 ||
+            j.rows > 0xFFFFFFFFull || j.cols > 0xFFFFFFFFull || j.T > 0xFFFFFFFFull)
+            return fail("kernel_cuda_matmul_quant_batch: job %d invalid (null pointer, zero size, or cols not "
+                        "a multiple of 256)", i);
+        for (size_t t = 0; t < j.T; t++)
+            mv.push_back(KernelCudaMatvecJob{j.is_q6, j.matrix, j.X + t * j.cols, j.Y + t * j.rows, j.rows, j.cols});
+    }
+    return kernel_cuda_matvec_quant_batch(mv.data(), (int)mv.size());
 }

@@ -41,6 +41,8 @@ def test_struct_layouts_match_c(tmp_path):
                    'sizeof(KernelDeltaPrefillJob), offsetof(KernelDeltaPrefillJob, T)); '
                    'printf("%zu %zu %zu %zu\\n", sizeof(KernelDeltaPreopJob), offsetof(KernelDeltaPreopJob, T), '
                    'sizeof(KernelDeltaPostopJob), offsetof(KernelDeltaPostopJob, T)); '
+                   'printf("%zu %zu %zu %zu\\n", sizeof(KernelCudaMatvecJob), offsetof(KernelCudaMatvecJob, cols), '
+                   'sizeof(KernelCudaMatmulJob), offsetof(KernelCudaMatmulJob, T)); '
                    'return 0; }\n')
     inc = os.path.join(os.path.dirname(R.LIB_PATH), "..", "include")
     exe = tmp_path / "s"
@@ -51,7 +53,9 @@ def test_struct_layouts_match_c(tmp_path):
                     C.sizeof(R.KernelAttnPrefillJob), R.KernelAttnPrefillJob.dtype.offset,
                     C.sizeof(R.KernelDeltaPrefillJob), R.KernelDeltaPrefillJob.T.offset,
                     C.sizeof(R.KernelDeltaPreopJob), R.KernelDeltaPreopJob.T.offset,
-                    C.sizeof(R.KernelDeltaPostopJob), R.KernelDeltaPostopJob.T.offset]
+                    C.sizeof(R.KernelDeltaPostopJob), R.KernelDeltaPostopJob.T.offset,
+                    C.sizeof(R.KernelCudaMatvecJob), R.KernelCudaMatvecJob.cols.offset,
+                    C.sizeof(R.KernelCudaMatmulJob), R.KernelCudaMatmulJob.T.offset]
 
 
 def _has_gpu():

@@ -1,0 +1,59 @@
+"""Multi-token k-quant projections (kernel_cuda_matmul_quant_batch) on the reference's own test
+shapes (src/test_kernels.c:42-70: T in 1, 3, 8, 9, 16, 17, 100, 257; rows 512, 2048, 37; cols
+2048 or 512; Q4_K and Q6_K; several jobs sharing X), against the reference's CPU dot per row and
+token (oracle/_ref; the oracle restatement where it is absent). The reference's matmul dequantises
+a block then dots it (kernels.c:1877-1905), the same fp32 math in another order; its own test bar
+is 2e-4 maxrel, this one 1e-5."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from roaster_b200 import synth
+from tests.gpu_util import dev, host
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _ref(q6, m, X, rows, cols):
+    impl = "ref" if O.have_ref() else "port"
+    return np.stack([O.matvec_q(q6, m, X[t], rows, cols, impl=impl) for t in range(X.shape[0])])
+
+
+@pytest.mark.parametrize("q6", [False, True])
+@pytest.mark.parametrize("rows,cols", [(512, 2048), (2048, 512), (37, 2048)])
+@pytest.mark.parametrize("T", [1, 3, 8, 9, 16, 17, 100, 257])
+def test_matmul(rb, oracle_lib, q6, rows, cols, T):
+    m = synth.quant_matrix(rows * 7 + cols + int(q6), rows, cols, q6)
+    X = np.random.default_rng(T + rows).uniform(-1, 1, (T, cols)).astype(np.float32)
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dev(m), dev(X), Y, rows, cols, T)])
+    assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
+
+
+def test_shared_x(rb, oracle_lib):
+    """Three jobs sharing X in one call (the reference's shared-X case)."""
+    T, cols = 40, 2048
+    X = np.random.default_rng(5).uniform(-1, 1, (T, cols)).astype(np.float32)
+    dX = dev(X)
+    specs = [(False, 256), (True, 64), (False, 32)]
+    keep, jobs, refs = [], [], []
+    for i, (q6, r) in enumerate(specs):
+        m = synth.quant_matrix(50 + i, r, cols, q6)
+        dm, Y = dev(m), torch.zeros(T, r, device="cuda")
+        keep.append((dm, Y))
+        jobs.append((q6, dm, dX, Y, r, cols, T))
+        refs.append(_ref(q6, m, X, r, cols))
+    rb.matmul_quant_batch(jobs)
+    for (dm, Y), ref in zip(keep, refs):
+        assert O.maxrel(host(Y), ref) < TOL
+
+
+def test_rejects_invalid(rb):
+    m = torch.zeros(144, dtype=torch.uint8, device="cuda")
+    X = torch.zeros(256, device="cuda")
+    Y = torch.zeros(1, device="cuda")
+    for bad in [(False, m, X, Y, 1, 300, 1), (False, m, X, Y, 1, 256, 0), (False, m, X, Y, 0, 256, 1)]:
+        with pytest.raises(RuntimeError, match="invalid"):
+            rb.matmul_quant_batch([bad])
