@@ -46,6 +46,7 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <cstring>
+#include <unordered_map>
 #include <vector>
 
 namespace rb {
@@ -68,7 +69,8 @@ constexpr int kOffXsum = kOffBtab + kMaxNb * 1024;   // activation sums: 16 a bl
 constexpr int kOffMisc = kOffXsum + kMaxNb * 16 * 4; // max reduction (one float per warp)
 constexpr int kOffJobs = kOffMisc + kCWarps * 4;     // the job table, copied from the parameters
 constexpr int kOffZero = kOffJobs + kMaxJobs * 80;   // 1 KB of zeros: B fragments of the zero lanes
-constexpr int kOffBar = kOffZero + 1024;             // job barrier
+constexpr int kOffWBar = kOffZero + 1024;            // per warp: 8 stage barriers
+constexpr int kOffBar = kOffWBar + kCWarps * 64;     // job barrier
 constexpr int kSmemBytes = kOffBar + 8;
 constexpr int kMaxCtas = 160;
 static_assert(kSmemBytes <= 232448, "staged matvec exceeds the shared memory of a CTA");
@@ -76,6 +78,7 @@ static_assert(kQ4Stages >= 3 && kQ6Stages >= 3, "rings too small");
 static_assert(kOffJobs % 16 == 0, "job table alignment");
 
 struct SJob {
+    const CUtensorMap *map;      // the matrix as rows x (row bytes) uint8, box one slot x 16 rows
     const unsigned char *w;      // rows x nb blocks, 16-byte aligned
     const float *x;
     float *y;
@@ -113,9 +116,15 @@ struct DParams {
 
 // ---------------------------------------------------------------- staged kernel
 
-__device__ __forceinline__ void cp_async_commit()
+
+// One box of a 2-D tensor map (in global memory) into shared memory, completion as transaction
+// bytes on `bar`. x (bytes) is a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar)
 {
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
 }
 
 // Device-scope acquire-release increment; returns the old value.
@@ -126,11 +135,6 @@ __device__ __forceinline__ int arrive_acq_rel(int *p)
     return old;
 }
 
-template <int N>
-__device__ __forceinline__ void cp_async_wait()
-{
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // D += A * B, m16n8k16, f16 inputs, fp32 accumulation (not volatile: free to schedule).
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -415,79 +419,75 @@ __device__ __forceinline__ int item_job(const SJob *jobs, int njobs, long long t
 
 // One warp's share of a CTA segment of job J: its items it0 + warp, it0 + warp + 16, ... < it1
 // (job-relative). Item i is part i & (P-1) of tile i >> plog: blocks [part * nb/P, +nb/P) of 16
-// rows, streamed block by block through the warp's S-stage ring; the copies of the block S - 1
-// ahead are issued before a block is multiplied. Items, blocks and stages advance as counters;
-// each lane's copy offsets within a block are fixed. A whole tile (P = 1) stores y directly; the
-// parts of a split tile store fp32 partials, and the last part to arrive (a counter per tile,
-// returned to zero) sums them in part order into y.
+// rows. Items advance by 16, a multiple of P, so a warp keeps its part and moves 16/P tiles per
+// item. Each block of an item is one tensor-map box (16 rows x one slot; rows past the matrix
+// read as zeros) landing in the warp's S-stage ring; lane 0 issues the box S - 1 blocks ahead
+// before a block is multiplied. `ph` holds the parity each of the warp's stage barriers completes
+// next (kept across segments). A whole tile (P = 1) stores y directly; the parts of a split tile
+// store fp32 partials, and the last part to arrive (a counter per tile, returned to zero) sums
+// them in part order into y.
 template <int S, bool Q6>
-__device__ __forceinline__ bool run_segment(const SJob &J, long long it0, long long it1, unsigned char *sm,
-                                            unsigned char *ring, uint32_t jb, uint32_t &jph, const Lane &L, int warp,
-                                            int lane)
+__device__ __forceinline__ bool run_segment(const SJob &Jsm, long long it0, long long it1, unsigned char *sm,
+                                            unsigned char *ring, uint32_t wbar, uint32_t &ph, uint32_t jb,
+                                            uint32_t &jph, const Lane &L, int warp, int lane)
 {
     constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
     constexpr int kStage = 16 * kSlot;
-    constexpr int kChunks = kSlot / 16;                    // 16-byte chunks per row slot
-    constexpr int kCopies = (16 * kChunks + 31) / 32;      // per lane per block
     constexpr int kBsz = Q6 ? 210 : 144;
+    // the job's fields in registers (the table in shared memory would be re-read every block)
+    const CUtensorMap *const map = Jsm.map;
+    const long long rows = Jsm.rows;
+    const int nb = Jsm.nb, plog = Jsm.plog, P = 1 << plog, nbp = nb >> plog;
     const long long first = it0 + warp;
-    const int nb = J.nb, plog = J.plog, P = 1 << plog, nbp = nb >> plog;
-    const int rb = nb * kBsz;
-    // this lane's copies within a block: slot row cr (beyond every row count: no copy) and
-    // offset coff in the slot row (= in the block's bytes)
-    int cr[kCopies], coff[kCopies];
-#pragma unroll
-    for (int i = 0; i < kCopies; i++) {
-        const int k = lane + 32 * i;
-        const int r = k / kChunks;
-        cr[i] = k < 16 * kChunks ? r : 0x40000000;
-        coff[i] = 16 * (k - r * kChunks);
-    }
     const int nitems = first < it1 ? (int)((it1 - first + kCWarps - 1) / kCWarps) : 0;
-    // issue state: item, block within the item, stage
-    int is_n = 0, is_b = 0, is_s = 0;
-    long long is_it = first;
+    const int part = (int)(first & (P - 1));
+    const int b0 = part * nbp;                             // first block of every item of this warp
+    const int trow = (kCWarps >> plog) * 16;               // rows from one item to the next
+    const uint32_t ring_s = smem_addr(ring);
+    // issue state: item count, block within the item, stage, the item's first row
+    int is_n = 0, is_b = 0, is_s = 0, issued = 0;
+    int is_row0 = (int)((first >> plog) * 16);
     auto issue = [&]() {
         if (is_n < nitems) {
-            unsigned char *st = ring + is_s * kStage;
-            const long long row0 = (is_it >> plog) * 16;
-            const int b = (int)(is_it & (P - 1)) * nbp + is_b;
-            const int lim = (int)min(16ll, J.rows - row0);
-            if (!Q6) {
-                const unsigned char *src = J.w + row0 * rb + b * 144;
-#pragma unroll
-                for (int i = 0; i < kCopies; i++)
-                    if (cr[i] < lim)
-                        cp_async16(smem_addr(st + cr[i] * kSlot + coff[i]), src + cr[i] * rb + coff[i]);
-            } else {
-                const long long o0 = row0 * rb + 210 * b;
-#pragma unroll
-                for (int i = 0; i < kCopies; i++) {
-                    if (cr[i] < lim) {
-                        const long long o = o0 + (long long)cr[i] * rb, a = o & ~15ll;
-                        if (coff[i] < (int)(o - a) + 210)
-                            cp_async16(smem_addr(st + cr[i] * kSlot + coff[i]), J.w + a + coff[i]);
-                    }
-                }
+            if (lane == 0) {
+                const int bx = b0 + is_b;
+                const int x = Q6 ? (210 * bx) & ~15 : 144 * bx;
+                // the stage was last read through the generic proxy; the box writes it through the async one
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(wbar + 8u * is_s, (uint32_t)kStage);
+                tma_load_2d(ring_s + is_s * kStage, map, x, is_row0, wbar + 8u * is_s);
             }
+            issued++;
             if (++is_b == nbp) {
                 is_b = 0;
                 is_n++;
-                is_it += kCWarps;
+                is_row0 += trow;
             }
             is_s = is_s + 1 == S ? 0 : is_s + 1;
         }
-        cp_async_commit();
     };
 #pragma unroll
     for (int q = 0; q < S - 1; q++)
         issue();
-    // the first copies are in flight: every warp past the previous segment, then the tables
+    int cs = 0, consumed = 0;
+    // give up: the boxes already issued must land before the CTA exits
+    auto drain = [&]() {
+        if (lane == 0)
+            for (int k = consumed, s = cs; k < issued; k++, s = s + 1 == S ? 0 : s + 1) {
+                mbar_wait(wbar + 8u * s, (ph >> s) & 1u, 20000000ll);
+                ph ^= 1u << s;
+            }
+        __syncwarp();
+    };
+    // the first boxes are in flight: every warp past the previous segment, then the tables
     int e = 0;
-    if (!jb_sync(jb, jph, lane) || !build_tables(J, sm, threadIdx.x, jb, jph, e)) {
-        cp_async_wait<0>();
+    if (!jb_sync(jb, jph, lane) || !build_tables(Jsm, sm, threadIdx.x, jb, jph, e)) {
+        drain();
         return false;
     }
+    float *const y = Jsm.y;
+    float *const partials = Jsm.part;
+    int *const cnt = Jsm.cnt;
     // this lane's B column: its entries of each block's table, or the zero area
     const uint4 *bcol = L.bnz ? reinterpret_cast<const uint4 *>(sm + kOffBtab) + L.l8
                               : reinterpret_cast<const uint4 *>(sm + kOffZero);
@@ -495,22 +495,26 @@ __device__ __forceinline__ bool run_segment(const SJob &J, long long it0, long l
     const float *xsum = reinterpret_cast<const float *>(sm + kOffXsum);
     const float f = ldexpf(1.f, Q6 ? 24 - e : 24 - 4 * (L.t & 1) - e);
     float acc_a = 0.f, acc_b = 0.f;
-    int bi = 0, cs = 0;
-    long long it = first;
+    int bi = 0;
+    long long row0 = (first >> plog) * 16;
     for (int left = nitems; left > 0;) {
-        cp_async_wait<S - 2>();
-        __syncwarp();        // every lane's copies of this block have landed; the previous stage is free
+        const bool got = mbar_wait(wbar + 8u * cs, (ph >> cs) & 1u);
+        if (!__all_sync(0xffffffffu, got)) {
+            drain();
+            return false;
+        }
+        ph ^= 1u << cs;
+        consumed++;
+        __syncwarp();        // every lane is past the previous block: its stage may be refilled
         issue();
         const unsigned char *st = ring + cs * kStage;
-        const long long row0 = (it >> plog) * 16;
-        const int b = (int)(it & (P - 1)) * nbp + bi;
+        const int b = b0 + bi;
         if (!Q6) {
             q4_mma_block(st + L.g * kSlot, st + (L.g + 8) * kSlot, bcol + b * bstep, xsum + b * 8, f, L, acc_a,
                          acc_b);
         } else {
-            const int ma = (int)(((row0 + L.g) * rb + 210 * b) & 15);
-            const int mb = (int)(((row0 + L.g + 8) * rb + 210 * b) & 15);
-            q6_mma_block(st + L.g * kSlot + ma, st + (L.g + 8) * kSlot + mb, bcol + b * bstep, xsum + b * 16, f, L,
+            const int mis = (210 * b) & 15;                // the block's offset in its box (same every row)
+            q6_mma_block(st + L.g * kSlot + mis, st + (L.g + 8) * kSlot + mis, bcol + b * bstep, xsum + b * 16, f, L,
                          acc_a, acc_b);
         }
         cs = cs + 1 == S ? 0 : cs + 1;
@@ -519,45 +523,44 @@ __device__ __forceinline__ bool run_segment(const SJob &J, long long it0, long l
             acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
             acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
             acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
-            if (P == 1) {
-                if (L.t == 0) {
-                    if (row0 + L.g < J.rows)
-                        J.y[row0 + L.g] = acc_a;
-                    if (row0 + L.g + 8 < J.rows)
-                        J.y[row0 + L.g + 8] = acc_b;
+            if (L.t == 0) {
+                if (P == 1) {
+                    if (row0 + L.g < rows)
+                        y[row0 + L.g] = acc_a;
+                    if (row0 + L.g + 8 < rows)
+                        y[row0 + L.g + 8] = acc_b;
+                } else {
+                    float *pp = partials + (row0 * P + 16 * part);
+                    __stcg(pp + L.g, acc_a);
+                    __stcg(pp + L.g + 8, acc_b);
                 }
-            } else if (L.t == 0) {
-                float *pp = J.part + ((it >> plog) * P + (it & (P - 1))) * 16;
-                __stcg(pp + L.g, acc_a);
-                __stcg(pp + L.g + 8, acc_b);
             }
             acc_a = acc_b = 0.f;
             bi = 0;
-            it += kCWarps;
+            row0 += trow;
             left--;
         }
     }
-    cp_async_wait<0>();
-    // split tiles: arrive once the warp's copies are done (the acquire-release waits for the
-    // warp's outstanding memory operations); the last part of a tile sums the partials in order
+    // split tiles: arrive once the warp's partial stores are issued; the last part of a tile sums
+    // the partials in order
     if (P > 1) {
         __syncwarp();        // the partial stores of every lane precede lane 0's release
-        for (long long i = first; i < it1; i += kCWarps) {
-            const long long tile = i >> plog;
+        long long r0 = (first >> plog) * 16;
+        for (int n = 0; n < nitems; n++, r0 += trow) {
+            const long long tile = r0 >> 4;
             int last = 0;
             if (lane == 0)
-                last = arrive_acq_rel(J.cnt + tile) == P - 1;
+                last = arrive_acq_rel(cnt + tile) == P - 1;
             if (__shfl_sync(0xffffffffu, last, 0)) {   // lane 0's acquire covers the other parts
-                const long long row0 = tile * 16;
-                if (lane < 16 && row0 + lane < J.rows) {
-                    const float *tp = J.part + tile * P * 16 + lane;
+                if (lane < 16 && r0 + lane < rows) {
+                    const float *tp = partials + r0 * P + lane;
                     float v = 0.f;
                     for (int q = 0; q < P; q++)
-                        v += __ldcg(tp + q * 16);
-                    J.y[row0 + lane] = v;
+                        v += __ldcg(tp + 16 * q);
+                    y[r0 + lane] = v;
                 }
                 if (lane == 0)
-                    J.cnt[tile] = 0;
+                    cnt[tile] = 0;
             }
         }
     }
@@ -578,10 +581,14 @@ __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const 
     }
     if (tid < 64)
         reinterpret_cast<uint4 *>(sm + kOffZero)[tid] = make_uint4(0, 0, 0, 0);
-    if (tid == 0) {
+    const uint32_t wbar = smem_addr(sm + kOffWBar) + 64u * warp;   // this warp's stage barriers
+    if (lane < 8)
+        mbar_init(wbar + 8u * lane, 1);
+    if (tid == 0)
         mbar_init(jb, kCWarps);
+    __syncwarp();
+    if (lane == 0)
         mbar_init_fence();
-    }
     __syncthreads();
     Lane L;
     L.g = lane >> 2;
@@ -590,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const 
     L.l8 = 2 * L.t + (L.g & 1);
     L.sel = 0x7650u | (uint32_t)L.t;
     unsigned char *ring = sm + warp * kRingBytes;
-    uint32_t jph = 0;
+    uint32_t jph = 0, ph = 0;
     long long t = p.cta_item[blockIdx.x];
     const long long t1 = p.cta_item[blockIdx.x + 1];
     while (t < t1) {
@@ -599,8 +606,9 @@ __global__ void __launch_bounds__(kThreads, 1) quant_matvec_staged_kernel(const 
         const long long jend = j + 1 < p.njobs ? jobs[j + 1].item0 : p.items;
         const long long send = min(t1, jend);
         const bool ok = J.is_q6
-            ? run_segment<kQ6Stages, true>(J, t - J.item0, send - J.item0, sm, ring, jb, jph, L, warp, lane)
-            : run_segment<kQ4Stages, false>(J, t - J.item0, send - J.item0, sm, ring, jb, jph, L, warp, lane);
+            ? run_segment<kQ6Stages, true>(J, t - J.item0, send - J.item0, sm, ring, wbar, ph, jb, jph, L, warp, lane)
+            : run_segment<kQ4Stages, false>(J, t - J.item0, send - J.item0, sm, ring, wbar, ph, jb, jph, L, warp,
+                                            lane);
         if (!ok) {
             if (tid == 0)
                 atomicOr(p.err, kErrWaitTimeout);
@@ -726,6 +734,69 @@ __global__ void __launch_bounds__(kRowWarps * 32) quant_matvec_row_kernel(const 
 
 // ---------------------------------------------------------------- host
 
+// Tensor maps of the matrices, cached per device: weights stay resident between calls, so a
+// matrix's map is encoded and uploaded once. A map holds only the address and the shape.
+constexpr int kMapCap = 4096;
+
+struct MapKey {
+    uintptr_t w;
+    long long rows;
+    int rb, slot;
+    bool operator==(const MapKey &o) const { return w == o.w && rows == o.rows && rb == o.rb && slot == o.slot; }
+};
+
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const
+    {
+        return std::hash<uintptr_t>()(k.w) ^ (std::hash<long long>()(k.rows) * 31u) ^ ((size_t)k.rb << 20) ^
+               (size_t)k.slot;
+    }
+};
+
+struct MapCache {
+    CUtensorMap *dev = nullptr;          // kMapCap maps in device memory
+    std::vector<CUtensorMap> host;       // their host copies (sources of the uploads)
+    int used = 0;
+    std::unordered_map<MapKey, int, MapKeyHash> idx;
+};
+
+MapCache g_maps[64];
+
+const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int slot)
+{
+    Runtime &R = rt();
+    if (R.device < 0 || R.device >= 64) {
+        fail("kernel_cuda_matvec_quant_batch: device %d out of range", R.device);
+        return nullptr;
+    }
+    MapCache &mc = g_maps[R.device];
+    if (!mc.dev) {
+        if (check(cudaMalloc(&mc.dev, kMapCap * sizeof(CUtensorMap)), "cudaMalloc(matvec tensor maps)") != 0)
+            return nullptr;
+        mc.host.resize(kMapCap);
+    }
+    const MapKey key{reinterpret_cast<uintptr_t>(w), rows, rb, slot};
+    const auto it = mc.idx.find(key);
+    if (it != mc.idx.end())
+        return mc.dev + it->second;
+    if (mc.used == kMapCap) {
+        // full: start over once no queued kernel can still read the old maps
+        if (check(cudaStreamSynchronize(R.stream), "cudaStreamSynchronize(matvec tensor maps)") != 0)
+            return nullptr;
+        mc.idx.clear();
+        mc.used = 0;
+    }
+    const int i = mc.used;
+    if (encode_tmap_u8_2d(&mc.host[i], w, (uint64_t)rb, (uint64_t)rows, (uint64_t)rb, (uint32_t)slot, 16) != 0)
+        return nullptr;
+    if (check(cudaMemcpyAsync(mc.dev + i, &mc.host[i], sizeof(CUtensorMap), cudaMemcpyHostToDevice, R.stream),
+              "upload matvec tensor map") != 0)
+        return nullptr;
+    mc.used++;
+    mc.idx.emplace(key, i);
+    return mc.dev + i;
+}
+
 int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
 {
     static bool attr_set = false;
@@ -751,18 +822,19 @@ int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
         const int nb = (int)(j.cols / 256);
         const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
         const unsigned char *w = static_cast<const unsigned char *>(j.matrix);
+        // staged rows: the matrix as a 2-D byte array needs 16-byte alignment and a row length that
+        // is a multiple of 16 bytes (Q6_K: a multiple of 8 blocks)
         long long srows = 0;
-        if (aligned16(j.matrix) && nb <= kMaxNb) {
+        if (aligned16(j.matrix) && nb <= kMaxNb && rb % 16 == 0 && rb <= 0x7FFFFFFF / 16 &&
+            (long long)j.rows < 0x7FFFFFFF)
             srows = (long long)j.rows;
-            // the copies read whole 16-byte windows: a Q6_K matrix whose end is not 16-byte
-            // aligned keeps its last row out of the tiles, so no window reaches past the matrix
-            if (j.is_q6 && ((long long)j.rows * nb) % 8 != 0)
-                srows -= 1;
-        }
         if (srows > 0) {
             tiles[sp.njobs] = (srows + 15) / 16;
             total_tiles += tiles[sp.njobs];
-            sp.jobs[sp.njobs++] = SJob{w, j.vector, j.output, nullptr, nullptr, 0, srows, nb, j.is_q6 ? 1 : 0, 0};
+            const CUtensorMap *map = job_map(w, srows, (int)rb, j.is_q6 ? kQ6Slot : kQ4Slot);
+            if (!map)
+                return -1;
+            sp.jobs[sp.njobs++] = SJob{map, w, j.vector, j.output, nullptr, nullptr, 0, srows, nb, j.is_q6 ? 1 : 0, 0};
         }
         if (srows < (long long)j.rows) {
             dp.jobs[dp.njobs++] = DJob{w + srows * rb, j.vector, j.output + srows, dp.drows,

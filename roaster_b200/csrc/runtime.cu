@@ -78,27 +78,54 @@ int ensure()
     return check(cudaSetDevice(g_rt.device), "cudaSetDevice");
 }
 
-int encode_tmap_f16_3d(CUtensorMap *map, const void *base, const uint64_t dims[3], const uint64_t strides[2],
-                       const uint32_t box[3])
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
 {
-    typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-    static EncodeFn encode = nullptr;
+    static EncodeTiledFn encode = nullptr;
     if (!encode) {
         void *fn = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
             q != cudaDriverEntryPointSuccess)
-            return fail("cuTensorMapEncodeTiled is not available from the driver");
-        encode = reinterpret_cast<EncodeFn>(fn);
+            return nullptr;
+        encode = reinterpret_cast<EncodeTiledFn>(fn);
     }
+    return encode;
+}
+
+int encode_tmap_f16_3d(CUtensorMap *map, const void *base, const uint64_t dims[3], const uint64_t strides[2],
+                       const uint32_t box[3])
+{
+    const EncodeTiledFn encode = encode_fn();
+    if (!encode)
+        return fail("cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t gd[3] = {dims[0], dims[1], dims[2]};
     const cuuint64_t gs[2] = {strides[0], strides[1]};
     const cuuint32_t bd[3] = {box[0], box[1], box[2]};
     const cuuint32_t es[3] = {1, 1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), gd, gs, bd, es,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+int encode_tmap_u8_2d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t stride1,
+                      uint32_t box0, uint32_t box1)
+{
+    const EncodeTiledFn encode = encode_fn();
+    if (!encode)
+        return fail("cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t gd[2] = {dim0, dim1};
+    const cuuint64_t gs[1] = {stride1};
+    const cuuint32_t bd[2] = {box0, box1};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), gd, gs, bd, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail("cuTensorMapEncodeTiled failed (%d)", (int)r);

@@ -56,6 +56,10 @@ void *pinned(size_t bytes);
 // plain data (128 bytes) that kernels read from global memory. 0 = ok.
 int encode_tmap_f16_3d(CUtensorMap *map, const void *base, const uint64_t dims[3], const uint64_t strides[2],
                        const uint32_t box[3]);
+// Encode a tiled tensor map for a 2-D byte array (dim0 bytes per row, dim1 rows, rows stride1
+// bytes apart, a multiple of 16), no swizzle, zero fill outside the array. 0 = ok.
+int encode_tmap_u8_2d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t stride1,
+                      uint32_t box0, uint32_t box1);
 // 16-byte alignment check for pointers handed to bulk-copy engines.
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
