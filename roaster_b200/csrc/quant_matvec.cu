@@ -18,9 +18,10 @@
 // m16n8k16, f16 inputs, fp32 accumulation):
 //
 //  * Sixteen warps per CTA, each streaming its own tiles of 16 rows one block at a time through a
-//    private ring of shared memory with 16-byte cp.async copies (Q4_K: 5 stages of 16 x 144 B;
-//    Q6_K: 3 stages of 16 x 240 B, each row slot the 16-byte-aligned window around its block).
-//    Warps never wait on one another inside a job, and each keeps about 8 KB in flight.
+//    private ring of shared memory, one tensor-map box copy per block (16 rows x the block's
+//    16-byte-aligned window; Q4_K: 5 stages of 16 x 144 B; Q6_K: 3 stages of 16 x 240 B; rows
+//    past the matrix arrive as zeros). Warps never wait on one another inside a job, and each
+//    keeps about 8 KB in flight.
 //  * Lane (g, t) holds rows g and g + 8 of the tile. Weights enter the A fragment as exact f16
 //    subnormals: a Q4_K nibble field ANDed in place is q 2^-24 (low) or q 2^-20 (high), a Q6_K
 //    6-bit field q 2^-24 - one AND per two weights, no conversion.
@@ -35,9 +36,14 @@
 //    of about equal cost. When a call has fewer than two tiles per warp, tiles split into 2-16 parts
 //    along the blocks; parts leave fp32 partials and the last one of a tile sums them in order.
 //
-// Rows the staged kernel does not take (a matrix not 16-byte aligned, rows longer than 4096
-// weights, the last row of a Q6_K matrix whose end is not 16-byte aligned) run in the row kernel:
-// one warp per row reading global memory directly.
+// Matrices the staged kernel does not take (not 16-byte aligned, rows longer than 4096 weights,
+// Q6_K rows that are not a multiple of 16 bytes) run in the row kernel: one warp per row reading
+// global memory directly.
+//
+// Multi-token products (kernel_matmul_quant_batch, kernels.h:51-64) of 8 or more tokens run in
+// quant_matmul_kernel: a CTA multiplies 256 rows by 32 tokens, so each weight block is read and
+// decoded once per 32 tokens, with the scales folded into the A fragments (exact f16 products)
+// and each token's activation split hi + lo in B; described where the kernel is defined.
 #include "ptx.cuh"
 #include "runtime.h"
 #include "../../include/roaster_cuda.h"
@@ -433,7 +439,6 @@ __device__ __forceinline__ bool run_segment(const SJob &Jsm, long long it0, long
 {
     constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
     constexpr int kStage = 16 * kSlot;
-    constexpr int kBsz = Q6 ? 210 : 144;
     // the job's fields in registers (the table in shared memory would be re-read every block)
     const CUtensorMap *const map = Jsm.map;
     const long long rows = Jsm.rows;
@@ -732,6 +737,396 @@ __global__ void __launch_bounds__(kRowWarps * 32) quant_matvec_row_kernel(const 
     }
 }
 
+// ---------------------------------------------------------------- multi-token (prefill) kernel
+//
+// Y[t][r] = W[r] . X[t] for T tokens. The products run on the warp MMA with the scales folded
+// into A, so B carries four tokens x (hi, lo) in its eight columns:
+//   Q4_K: A = sc_j q 2^-24 (exact f16 subnormals: sc q <= 945; a high nibble, ANDed in place, is
+//         q 2^-20 and is multiplied by sc / 16), one fp32 accumulator per block and token scaled
+//         by d; the min term runs as one more MMA per block, A = m_j (f16 integers) against the
+//         tokens' sub-block sums.
+//   Q6_K: A = (q - 32) sc 2^-24 as two exact MMAs per 16 weights, sc = 2 s' + r: A1 = (q-32) 2s'
+//         2^-24 (even integers up to 4096) and A2 = (q-32) r 2^-24.
+// A CTA takes 256 rows (16 warps x a 16-row tile) and 32 tokens; all warps walk the blocks
+// together through two shared-memory stages, each holding the block's 16 weight boxes (the
+// matrix's tensor map) and its B fragments (prepared once per call by quant_mm_prep_kernel:
+// each token's activation scaled by its own 2^e and split f16 hi + lo, in fragment order).
+
+constexpr int kMmRows = 256;                     // rows per CTA
+constexpr int kMmMaxNb = 128;                    // up to 32768 weights a row
+constexpr int kMmTok = 32;                       // tokens per CTA (8 groups of 4)
+constexpr int kMmBfBytes = 8 * 16 * 32 * 8;      // B fragments of one block: [group][mma][lane] uint2
+constexpr int kMmBmBytes = 8 * 32 * 8;           // min-term B fragments: [group][lane] uint2
+constexpr int kMmStageW = 16 * 16 * kQ6Slot;     // 16 boxes of 16 rows x slot (Q6_K size)
+constexpr int kMmStage = kMmStageW + kMmBfBytes + kMmBmBytes;
+constexpr int kMmSmem = 2 * kMmStage + 64;
+static_assert(kMmSmem <= 232448, "matmul exceeds the shared memory of a CTA");
+static_assert(kMmStage % 128 == 0 && kMmStageW % 128 == 0, "matmul stage alignment");
+
+struct MJob {
+    const CUtensorMap *map;      // the matrix (box slot x 16 rows)
+    const uint2 *bf;             // B fragments of X: [chunk][block][group][mma][lane]
+    const uint2 *bm;             // min-term fragments: [chunk][block][group][lane]
+    const int *e;                // per token: activation scale exponent
+    float *y;                    // [T][rows]
+    float *part;                 // split jobs: unscaled partial products [P][T][rows]
+    long long item0;             // first CTA item of the job
+    int rows, nb, T, is_q6, rgroups, chunks, P;   // CTAs along the rows, token chunks, block parts
+};
+
+struct MParams {
+    MJob jobs[kMaxJobs];
+    int njobs;
+    long long items;
+    unsigned *err;
+};
+
+// Per padded token (one CTA each): the activation's scale exponent and its B fragments.
+__global__ void __launch_bounds__(256) quant_mm_prep_kernel(const float *X, int T, int cols, uint2 *bf, uint2 *bm,
+                                                            int *eout)
+{
+    __shared__ float red[8];
+    __shared__ float xs[8 * kMmMaxNb];             // sub-block sums, scaled by 2^(e-5) to stay in f16 range
+    const int tok = blockIdx.x, nb = cols / 256;
+    const bool real = tok < T;
+    const float *x = X + (size_t)(real ? tok : 0) * cols;
+    float mx = 0.f;
+    if (real)
+        for (int i = threadIdx.x; i < cols / 4; i += 256) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < 8; i++)
+        mx = fmaxf(mx, red[i]);
+    int E = 0;
+    if (mx > 0.f && mx < 3.0e38f)
+        frexpf(mx, &E);
+    const int e = max(-100, min(100, 14 - E));
+    const float scale = ldexpf(1.f, e);
+    if (threadIdx.x == 0 && real)
+        eout[tok] = e;
+    for (int i = threadIdx.x; i < nb * 8; i += 256) {
+        float acc = 0.f;
+        if (real) {
+            const float4 *xp = reinterpret_cast<const float4 *>(x + 32 * i);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float4 v = __ldg(xp + k);
+                acc += (v.x + v.y) + (v.z + v.w);
+            }
+        }
+        xs[i] = acc * scale * 0x1p-5f;
+    }
+    __syncthreads();
+    const int c = tok / kMmTok, grp = (tok % kMmTok) / 4, tg = tok & 3;
+    auto hl = [](float v, int lo) -> uint32_t {
+        const __half h = __float2half_rn(v);
+        return (uint32_t)__half_as_ushort(lo ? __float2half_rn(v - __half2float(h)) : h);
+    };
+    // B fragments: lane 8 tg + 4 hl + t holds, for MMA s of block b, weights 16 s + 4 t + {0,2} (b0)
+    // and {1,3} (b1) of this token, hi or lo
+    for (int q = threadIdx.x; q < nb * 16 * 8; q += 256) {
+        const int b = q / 128, s = (q / 8) % 16, lo = (q / 4) & 1, t = q & 3;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (real) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(x + 256 * b + 16 * s + 4 * t));
+            v[0] = a.x * scale; v[1] = a.y * scale; v[2] = a.z * scale; v[3] = a.w * scale;
+        }
+        const int lane = 8 * tg + 4 * lo + t;
+        bf[((((size_t)c * nb + b) * 8 + grp) * 16 + s) * 32 + lane] =
+            make_uint2(hl(v[0], lo) | (hl(v[2], lo) << 16), hl(v[1], lo) | (hl(v[3], lo) << 16));
+    }
+    // min-term fragments: k-slots 2t, 2t+1 hold sub-blocks 2t, 2t+1
+    for (int q = threadIdx.x; q < nb * 8; q += 256) {
+        const int b = q / 8, lo = (q / 4) & 1, t = q & 3;
+        const int lane = 8 * tg + 4 * lo + t;
+        bm[(((size_t)c * nb + b) * 8 + grp) * 32 + lane] =
+            make_uint2(hl(xs[8 * b + 2 * t], lo) | (hl(xs[8 * b + 2 * t + 1], lo) << 16), 0u);
+    }
+}
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b)
+{
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b)
+{
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// (v, v) as an f16 pair for the byte `sel` of a word (a small non-negative integer): the byte
+// under the exponent of 1024, less 1024.
+__device__ __forceinline__ uint32_t byte_pair_f16(uint32_t w, uint32_t k)
+{
+    const uint32_t sel = 0x4040u | (k << 8) | k;     // [b_k, 0x64, b_k, 0x64]
+    return hsub2u(__byte_perm(w, 0x64646464u, sel), 0x64006400u);
+}
+
+// Multiply the warp's 16-row tile by one block for the CTA's 32 tokens. The 16 MMA slices of the
+// block run in the outer loop and the 8 token groups in the inner one, each group on its own
+// accumulator (d scales the whole block), so a warp keeps 8 independent MMA chains in flight.
+// acc[grp][0/1]: rows g, g+8.
+__device__ __forceinline__ void mm_q4_block(const unsigned char *pa, const unsigned char *pb, const uint2 *bf,
+                                            const uint2 *bmn, const Lane &L, int lane, float (&acc)[8][2])
+{
+    const uint4 ha = lds128(pa), hb = lds128(pb);
+    const float2 da = __half22float2(*reinterpret_cast<const __half2 *>(&ha.x));
+    const float2 db = __half22float2(*reinterpret_cast<const __half2 *>(&hb.x));
+    // 6-bit scales and mins as bytes: j 0..3 in *l, 4..7 in *h (q4_k_get_scales)
+    const uint32_t scla = ha.y & 0x3F3F3F3Fu, scha = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+    const uint32_t mnla = ha.z & 0x3F3F3F3Fu, mnha = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+    const uint32_t sclb = hb.y & 0x3F3F3F3Fu, schb = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+    const uint32_t mnlb = hb.z & 0x3F3F3F3Fu, mnhb = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+    const uint32_t sixteenth = 0x2C002C00u;          // (1/16, 1/16)
+    float c[8][4];
+#pragma unroll
+    for (int grp = 0; grp < 8; grp++)
+        c[grp][0] = c[grp][1] = c[grp][2] = c[grp][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int j = s >> 1, e = s & 1, G = j >> 1, H = j & 1;
+        uint32_t sa = byte_pair_f16(j < 4 ? scla : scha, j & 3), sb = byte_pair_f16(j < 4 ? sclb : schb, j & 3);
+        if (H) {
+            sa = hmul2u(sa, sixteenth);
+            sb = hmul2u(sb, sixteenth);
+        }
+        const uint32_t mask = H ? 0x00F000F0u : 0x000F000Fu;
+        const uint32_t wa = lds32(pa + 16 + 32 * G + 16 * e + 4 * L.t), wb = lds32(pb + 16 + 32 * G + 16 * e + 4 * L.t);
+        const uint32_t a0 = hmul2u(wa & mask, sa), a1 = hmul2u(wb & mask, sb);
+        const uint32_t a2 = hmul2u((wa >> 8) & mask, sa), a3 = hmul2u((wb >> 8) & mask, sb);
+        const uint2 *bs = bf + s * 32 + lane;
+#pragma unroll
+        for (int grp = 0; grp < 8; grp++) {
+            const uint2 bb = bs[grp * 16 * 32];
+            mma16816(c[grp], a0, a1, a2, a3, bb.x, bb.y);
+        }
+    }
+    // min term: A = (m_2t, m_2t+1) of rows g and g + 8 against the sub-block sums (2^-5 of them)
+    const uint32_t ka = 2 * (L.t & 1);
+    const uint32_t mwa = L.t < 2 ? mnla : mnha, mwb = L.t < 2 ? mnlb : mnhb;
+    const uint32_t sel_m = 0x4040u | ((ka + 1) << 8) | ka;
+    const uint32_t ama = hsub2u(__byte_perm(mwa, 0x64646464u, sel_m), 0x64006400u);
+    const uint32_t amb = hsub2u(__byte_perm(mwb, 0x64646464u, sel_m), 0x64006400u);
+    const float das = da.x * 0x1p24f, dbs = db.x * 0x1p24f;
+    const float dma = da.y * 32.f, dmb = db.y * 32.f;
+#pragma unroll
+    for (int grp = 0; grp < 8; grp++) {
+        float m[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint2 bb = bmn[grp * 32 + lane];
+        mma16816(m, ama, amb, 0u, 0u, bb.x, bb.y);
+        acc[grp][0] += fmaf(das, c[grp][0] + c[grp][1], -dma * (m[0] + m[1]));
+        acc[grp][1] += fmaf(dbs, c[grp][2] + c[grp][3], -dmb * (m[2] + m[3]));
+    }
+}
+
+// One logical word at byte offset `off` of a Q6_K block starting at `bp` (any even address).
+__device__ __forceinline__ uint32_t q6_word(const unsigned char *bp, int off)
+{
+    const unsigned char *a = bp + off;
+    const unsigned char *al = reinterpret_cast<const unsigned char *>(reinterpret_cast<uintptr_t>(a) & ~(uintptr_t)3);
+    return __funnelshift_r(lds32(al), lds32(al + 4), 8u * (uint32_t)(reinterpret_cast<uintptr_t>(a) & 3));
+}
+
+// Q6_K: `pa`, `pb` point at the block in its box (offset (210 b) & 15, the same on every row).
+// Slices outer, token groups inner, as for Q4_K.
+__device__ __forceinline__ void mm_q6_block(const unsigned char *pa, const unsigned char *pb, const uint2 *bf,
+                                            const Lane &L, int lane, float (&acc)[8][2])
+{
+    const float da = __half2float(*reinterpret_cast<const __half *>(pa + 208)) * 0x1p24f;
+    const float db = __half2float(*reinterpret_cast<const __half *>(pb + 208)) * 0x1p24f;
+    const uint32_t off32 = 0x00200020u;              // (32 2^-24, 32 2^-24) as f16 subnormals
+    float c[8][4];
+#pragma unroll
+    for (int grp = 0; grp < 8; grp++)
+        c[grp][0] = c[grp][1] = c[grp][2] = c[grp][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int n = s >> 3, q = (s >> 1) & 3, h = s & 1;
+        // scale s: sc = 2 s' + r as f16 pairs (2 s', 2 s') and (r, r)
+        const int sca = *reinterpret_cast<const signed char *>(pa + 192 + s);
+        const int scb = *reinterpret_cast<const signed char *>(pb + 192 + s);
+        const uint32_t ea = __half_as_ushort(__short2half_rn((short)(sca & ~1)));
+        const uint32_t eb = __half_as_ushort(__short2half_rn((short)(scb & ~1)));
+        const uint32_t ra = (sca & 1) ? 0x3C003C00u : 0u, rbq = (scb & 1) ? 0x3C003C00u : 0u;
+        const uint32_t la = q6_word(pa, 64 * n + 32 * (q & 1) + 16 * h + 4 * L.t);
+        const uint32_t lb = q6_word(pb, 64 * n + 32 * (q & 1) + 16 * h + 4 * L.t);
+        const uint32_t qa = q6_word(pa, 128 + 32 * n + 16 * h + 4 * L.t);
+        const uint32_t qb = q6_word(pb, 128 + 32 * n + 16 * h + 4 * L.t);
+        const uint32_t Qa = ((la >> (4 * (q >> 1))) & 0x0F0F0F0Fu) | (((qa >> (2 * q)) << 4) & 0x30303030u);
+        const uint32_t Qb = ((lb >> (4 * (q >> 1))) & 0x0F0F0F0Fu) | (((qb >> (2 * q)) << 4) & 0x30303030u);
+        const uint32_t v0a = hsub2u(Qa & 0x003F003Fu, off32), v1a = hsub2u((Qa >> 8) & 0x003F003Fu, off32);
+        const uint32_t v0b = hsub2u(Qb & 0x003F003Fu, off32), v1b = hsub2u((Qb >> 8) & 0x003F003Fu, off32);
+        const uint32_t s2a = ea | (ea << 16), s2b = eb | (eb << 16);
+        const uint32_t x0 = hmul2u(v0a, s2a), x1 = hmul2u(v0b, s2b), x2 = hmul2u(v1a, s2a), x3 = hmul2u(v1b, s2b);
+        const uint32_t y0 = hmul2u(v0a, ra), y1 = hmul2u(v0b, rbq), y2 = hmul2u(v1a, ra), y3 = hmul2u(v1b, rbq);
+        const uint2 *bs = bf + s * 32 + lane;
+#pragma unroll
+        for (int grp = 0; grp < 8; grp++) {
+            const uint2 bb = bs[grp * 16 * 32];
+            mma16816(c[grp], x0, x1, x2, x3, bb.x, bb.y);
+            mma16816(c[grp], y0, y1, y2, y3, bb.x, bb.y);
+        }
+    }
+#pragma unroll
+    for (int grp = 0; grp < 8; grp++) {
+        acc[grp][0] = fmaf(da, c[grp][0] + c[grp][1], acc[grp][0]);
+        acc[grp][1] = fmaf(db, c[grp][2] + c[grp][3], acc[grp][1]);
+    }
+}
+
+__device__ __forceinline__ int mm_item_job(const MParams &p, long long u)
+{
+    int lo = 0, hi = p.njobs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.jobs[mid].item0 <= u)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) quant_matmul_kernel(const __grid_constant__ MParams p)
+{
+    extern __shared__ __align__(128) unsigned char sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const uint32_t full = smem_addr(sm + 2 * kMmStage);   // full[s] = full + 8 s
+    const int j = mm_item_job(p, blockIdx.x);
+    const MJob J = p.jobs[j];
+    const long long it = blockIdx.x - J.item0;
+    const int rg = (int)(it % J.rgroups), ch = (int)((it / J.rgroups) % J.chunks);
+    const int part = (int)(it / ((long long)J.rgroups * J.chunks));
+    const int slot = J.is_q6 ? kQ6Slot : kQ4Slot;
+    // this CTA's blocks: b0 .. b0 + nb - 1, part `part` of P near-equal ranges
+    const int b0 = (int)((long long)part * J.nb / J.P);
+    const int nb = (int)((long long)(part + 1) * J.nb / J.P) - b0;
+    if (tid < 2)
+        mbar_init(full + 8u * tid, 1);
+    __syncwarp();
+    if (tid == 0)
+        mbar_init_fence();
+    __syncthreads();
+    // stage s: 16 weight boxes, then the block's B fragments and min-term fragments
+    auto issue = [&](int bi, int s) {
+        const int b = b0 + bi;
+        const uint32_t st = smem_addr(sm + s * kMmStage);
+        if (lane == 0)
+            mbar_arrive_expect_tx(full + 8u * s, (uint32_t)(16 * 16 * slot + kMmBfBytes + kMmBmBytes));
+        __syncwarp();
+        if (lane < 16) {
+            const int x = J.is_q6 ? (210 * b) & ~15 : 144 * b;
+            tma_load_2d(st + lane * 16 * slot, J.map, x, rg * kMmRows + 16 * lane, full + 8u * s);
+        } else if (lane == 16) {
+            const size_t f = (size_t)ch * J.nb + b;
+            bulk_g2s(st + kMmStageW, J.bf + f * (kMmBfBytes / 8), kMmBfBytes, full + 8u * s);
+            bulk_g2s(st + kMmStageW + kMmBfBytes, J.bm + f * (kMmBmBytes / 8), kMmBmBytes, full + 8u * s);
+        }
+    };
+    if (warp == 0) {
+        issue(0, 0);
+        if (nb > 1)
+            issue(1, 1);
+    }
+    Lane L;
+    L.g = lane >> 2;
+    L.t = lane & 3;
+    float acc[8][2];
+#pragma unroll
+    for (int g = 0; g < 8; g++)
+        acc[g][0] = acc[g][1] = 0.f;
+    int bi = 0;
+    for (; bi < nb; bi++) {
+        const int s = bi & 1;
+        const bool got = mbar_wait(full + 8u * s, (uint32_t)((bi >> 1) & 1));
+        if (!bar_all(1, kThreads, got))
+            break;
+        const unsigned char *st = sm + s * kMmStage;
+        const unsigned char *pa = st + (warp * 16 + L.g) * slot, *pb = pa + 8 * slot;
+        const uint2 *bf = reinterpret_cast<const uint2 *>(st + kMmStageW);
+        const uint2 *bmn = reinterpret_cast<const uint2 *>(st + kMmStageW + kMmBfBytes);
+        if (J.is_q6) {
+            const int mis = (210 * (b0 + bi)) & 15;
+            mm_q6_block(pa + mis, pb + mis, bf, L, lane, acc);
+        } else {
+            mm_q4_block(pa, pb, bf, bmn, L, lane, acc);
+        }
+        named_bar_sync(2, kThreads);     // every warp is done with stage s
+        if (warp == 0 && bi + 2 < nb) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(bi + 2, s);
+        }
+    }
+    if (bi < nb) {
+        // a wait ran out: record it and let the copies already issued land before exiting
+        if (tid == 0) {
+            atomicOr(p.err, kErrWaitTimeout);
+            for (int k = bi; k < bi + 2 && k < nb; k++)
+                mbar_wait(full + 8u * (k & 1), (uint32_t)((k >> 1) & 1), 20000000ll);
+        }
+        return;
+    }
+    // acc[grp] of lane (g, t): token 4 grp + t, rows g and g + 8 of the warp's tile
+    const int r0 = rg * kMmRows + warp * 16 + L.g;
+    float *out = J.P > 1 ? J.part + (size_t)part * J.T * J.rows : J.y;
+#pragma unroll
+    for (int grp = 0; grp < 8; grp++) {
+        const int tok = ch * kMmTok + 4 * grp + L.t;
+        if (tok < J.T) {
+            const float f = J.P > 1 ? 1.f : ldexpf(1.f, -J.e[tok]);
+            if (r0 < J.rows)
+                out[(size_t)tok * J.rows + r0] = acc[grp][0] * f;
+            if (r0 + 8 < J.rows)
+                out[(size_t)tok * J.rows + r0 + 8] = acc[grp][1] * f;
+        }
+    }
+}
+
+// Split jobs: Y[t][r] = 2^-e_t (part 0 + part 1 + ... + part P-1), summed in part order.
+struct RJob {
+    const float *part;
+    float *y;
+    const int *e;
+    long long n0;                // first element of the job in the launch
+    int rows, T, P;
+};
+
+struct RParams {
+    RJob jobs[kMaxJobs];
+    int njobs;
+    long long n;
+};
+
+__global__ void __launch_bounds__(256) quant_mm_reduce_kernel(const __grid_constant__ RParams p)
+{
+    for (long long u = blockIdx.x * 256ll + threadIdx.x; u < p.n; u += (long long)gridDim.x * 256) {
+        int lo = 0, hi = p.njobs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.jobs[mid].n0 <= u)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        const RJob &J = p.jobs[lo];
+        const long long i = u - J.n0, plane = (long long)J.T * J.rows;
+        float v = 0.f;
+        for (int q = 0; q < J.P; q++)
+            v += __ldcs(J.part + q * plane + i);
+        J.y[i] = v * ldexpf(1.f, -J.e[i / J.rows]);
+    }
+}
+
 // ---------------------------------------------------------------- host
 
 // Tensor maps of the matrices, cached per device: weights stay resident between calls, so a
@@ -918,6 +1313,154 @@ int matvec_chunk(const KernelCudaMatvecJob *jobs, int n)
     return 0;
 }
 
+
+// Multi-token jobs: the staged matmul kernel for the jobs it takes (8 or more tokens, a 16-byte
+// aligned matrix whose rows are a multiple of 16 bytes, 16-byte aligned X), per-token matrix-vector
+// products for the rest. Jobs with the same X share its prepared fragments.
+int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatvecJob> &rest)
+{
+    static bool attr_set = false;
+    Runtime &R = rt();
+    MParams mp;
+    memset(static_cast<void *>(&mp), 0, sizeof(mp));
+    struct XEnt {
+        const float *X;
+        size_t cols, T;
+        size_t off_bf, off_bm, off_e;
+    };
+    std::vector<XEnt> xe;
+    std::vector<int> xidx;
+    long long tiles = 0;
+    for (int i = 0; i < n; i++) {
+        const KernelCudaMatmulJob &j = jobs[i];
+        const int nb = (int)(j.cols / 256);
+        const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
+        const bool staged = j.T >= 8 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && nb <= kMmMaxNb &&
+                            j.rows < (1u << 30) && j.T < (1u << 30);
+        if (!staged) {
+            for (size_t t = 0; t < j.T; t++)
+                rest.push_back(KernelCudaMatvecJob{j.is_q6, j.matrix, j.X + t * j.cols, j.Y + t * j.rows, j.rows, j.cols});
+            continue;
+        }
+        int x = -1;
+        for (size_t q = 0; q < xe.size(); q++)
+            if (xe[q].X == j.X && xe[q].cols == j.cols && xe[q].T == j.T)
+                x = (int)q;
+        if (x < 0) {
+            xe.push_back(XEnt{j.X, j.cols, j.T, 0, 0, 0});
+            x = (int)xe.size() - 1;
+        }
+        const CUtensorMap *map = job_map(static_cast<const unsigned char *>(j.matrix), (long long)j.rows, (int)rb,
+                                         j.is_q6 ? kQ6Slot : kQ4Slot);
+        if (!map)
+            return -1;
+        const int rgroups = (int)((j.rows + kMmRows - 1) / kMmRows);
+        const int chunks = (int)((j.T + kMmTok - 1) / kMmTok);
+        mp.jobs[mp.njobs] = MJob{map, nullptr, nullptr, nullptr, j.Y, nullptr, 0, (int)j.rows, nb, (int)j.T,
+                                 j.is_q6 ? 1 : 0, rgroups, chunks, 1};
+        xidx.push_back(x);
+        mp.njobs++;
+        tiles += (long long)rgroups * chunks;
+    }
+    if (mp.njobs == 0)
+        return 0;
+    // Few tiles (small T, few rows): split each tile's blocks into P parts, summed afterwards by
+    // quant_mm_reduce_kernel. P minimises an estimate of the call's time: waves of one CTA per SM
+    // x blocks per part x the measured time of one block per CTA (about 4.5 us Q4_K, 9 us Q6_K),
+    // plus, when split, the reduce launch and the partial products written and read at HBM speed.
+    int nb_max = 1;
+    double block_us = 4.5, out_elems = 0;
+    for (int q = 0; q < mp.njobs; q++) {
+        nb_max = std::max(nb_max, mp.jobs[q].nb);
+        if (mp.jobs[q].is_q6)
+            block_us = 9.0;
+        out_elems += (double)mp.jobs[q].rows * mp.jobs[q].T;
+    }
+    int want_p = 1;
+    double best = 1e300;
+    for (int P = 1; P <= std::min(16, nb_max); P++) {
+        const double waves = (double)((tiles * P + R.num_sms - 1) / R.num_sms);
+        const double cost = waves * ((nb_max + P - 1) / P) * block_us + (P > 1 ? 3.0 + P * out_elems * 8.0 / 6.0e6 : 0.0);
+        if (cost < best) {
+            best = cost;
+            want_p = P;
+        }
+    }
+    RParams rp;
+    memset(static_cast<void *>(&rp), 0, sizeof(rp));
+    size_t part_bytes = 0;
+    for (int q = 0; q < mp.njobs; q++) {
+        MJob &J = mp.jobs[q];
+        J.P = std::max(1, std::min(want_p, J.nb));
+        J.item0 = mp.items;
+        mp.items += (long long)J.rgroups * J.chunks * J.P;
+        if (J.P > 1) {
+            rp.jobs[rp.njobs] = RJob{nullptr, J.y, nullptr, rp.n, J.rows, J.T, J.P};
+            rp.n += (long long)J.rows * J.T;
+            rp.njobs++;
+            part_bytes += ((size_t)J.P * J.rows * J.T * sizeof(float) + 255) / 256 * 256;
+        }
+    }
+    if (mp.items >= (1ll << 31))
+        return fail("kernel_cuda_matmul_quant_batch: too many tiles in one call");
+    // scratch: per distinct X, B fragments [chunk][block][group][mma][lane], min-term fragments
+    // [chunk][block][group][lane], scale exponents [T]
+    size_t total = 0;
+    for (XEnt &e : xe) {
+        const size_t chunks = (e.T + kMmTok - 1) / kMmTok, nb = e.cols / 256;
+        e.off_bf = total;
+        total += chunks * nb * kMmBfBytes;
+        e.off_bm = total;
+        total += chunks * nb * kMmBmBytes;
+        e.off_e = total;
+        total += (e.T * sizeof(int) + 255) / 256 * 256;
+    }
+    const size_t off_part = total;
+    total += part_bytes;
+    unsigned char *ws = static_cast<unsigned char *>(scratch(total));
+    if (!ws)
+        return -1;
+    size_t pos = off_part;
+    for (int q = 0, r = 0; q < mp.njobs; q++) {
+        MJob &J = mp.jobs[q];
+        const XEnt &e = xe[xidx[q]];
+        J.bf = reinterpret_cast<const uint2 *>(ws + e.off_bf);
+        J.bm = reinterpret_cast<const uint2 *>(ws + e.off_bm);
+        J.e = reinterpret_cast<const int *>(ws + e.off_e);
+        if (J.P > 1) {
+            J.part = reinterpret_cast<float *>(ws + pos);
+            rp.jobs[r].part = J.part;
+            rp.jobs[r].e = J.e;
+            r++;
+            pos += ((size_t)J.P * J.rows * J.T * sizeof(float) + 255) / 256 * 256;
+        }
+    }
+    for (const XEnt &e : xe) {
+        const unsigned padded = (unsigned)((e.T + kMmTok - 1) / kMmTok * kMmTok);
+        quant_mm_prep_kernel<<<padded, 256, 0, R.stream>>>(e.X, (int)e.T, (int)e.cols,
+                                                           reinterpret_cast<uint2 *>(ws + e.off_bf),
+                                                           reinterpret_cast<uint2 *>(ws + e.off_bm),
+                                                           reinterpret_cast<int *>(ws + e.off_e));
+        if (launched("quant_mm_prep_kernel") != 0)
+            return -1;
+    }
+    if (!attr_set) {
+        if (check(cudaFuncSetAttribute(quant_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmSmem),
+                  "matmul shared memory") != 0)
+            return -1;
+        attr_set = true;
+    }
+    mp.err = R.err_word;
+    quant_matmul_kernel<<<(unsigned)mp.items, kThreads, kMmSmem, R.stream>>>(mp);
+    if (launched("quant_matmul_kernel") != 0)
+        return -1;
+    if (rp.njobs == 0)
+        return 0;
+    const long long blocks = std::min<long long>((rp.n + 255) / 256, 8ll * R.num_sms);
+    quant_mm_reduce_kernel<<<(unsigned)blocks, 256, 0, R.stream>>>(rp);
+    return launched("quant_mm_reduce_kernel");
+}
+
 }  // namespace
 }  // namespace rb
 
@@ -941,7 +1484,6 @@ extern "C" int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, i
         return -1;
     if (n < 0 || (n > 0 && !jobs))
         return fail("kernel_cuda_matmul_quant_batch: bad job array");
-    std::vector<KernelCudaMatvecJob> mv;
     for (int i = 0; i < n; i++) {
         const KernelCudaMatmulJob &j = jobs[i];
         // the reference's mm_job_valid (kernels.c:1916-1920)
@@ -949,8 +1491,10 @@ extern "C" int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, i
             j.rows > 0xFFFFFFFFull || j.cols > 0xFFFFFFFFull || j.T > 0xFFFFFFFFull)
             return fail("kernel_cuda_matmul_quant_batch: job %d invalid (null pointer, zero size, or cols not "
                         "a multiple of 256)", i);
-        for (size_t t = 0; t < j.T; t++)
-            mv.push_back(KernelCudaMatvecJob{j.is_q6, j.matrix, j.X + t * j.cols, j.Y + t * j.rows, j.rows, j.cols});
     }
-    return kernel_cuda_matvec_quant_batch(mv.data(), (int)mv.size());
+    std::vector<KernelCudaMatvecJob> rest;
+    for (int i = 0; i < n; i += kMaxJobs)
+        if (matmul_chunk(jobs + i, std::min(kMaxJobs, n - i), rest) != 0)
+            return -1;
+    return rest.empty() ? 0 : kernel_cuda_matvec_quant_batch(rest.data(), (int)rest.size());
 }

@@ -57,3 +57,69 @@ def test_rejects_invalid(rb):
     for bad in [(False, m, X, Y, 1, 300, 1), (False, m, X, Y, 1, 256, 0), (False, m, X, Y, 0, 256, 1)]:
         with pytest.raises(RuntimeError, match="invalid"):
             rb.matmul_quant_batch([bad])
+
+
+@pytest.mark.parametrize("q6", [False, True])
+def test_matmul_many_tiles(rb, oracle_lib, q6):
+    """Several 32-token chunks and 256-row groups, ragged at both ends, and a repeat that must
+    give the same bits."""
+    rows, cols, T = 1000, 8192, 70
+    m = synth.quant_matrix(900 + int(q6), rows, cols, q6)
+    X = np.random.default_rng(17).standard_normal((T, cols)).astype(np.float32)
+    dm, dX = dev(m), dev(X)
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dm, dX, Y, rows, cols, T)])
+    first = Y.clone()
+    rb.matmul_quant_batch([(q6, dm, dX, Y, rows, cols, T)])
+    assert torch.equal(first, Y)
+    assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
+
+
+@pytest.mark.parametrize("q6", [False, True])
+def test_matmul_activation_range(rb, oracle_lib, q6):
+    """Each token is scaled on its own: magnitudes from 1e-4 to 1e4 side by side, a zero token,
+    and a token of equal positive values (its sub-block sums are 32x its largest entry)."""
+    rows, cols, T = 96, 4096, 12
+    m = synth.quant_matrix(31 + int(q6), rows, cols, q6)
+    rng = np.random.default_rng(3)
+    X = rng.standard_normal((T, cols)).astype(np.float32)
+    X *= (10.0 ** np.linspace(-4, 4, T)).astype(np.float32)[:, None]
+    X[5] = 0
+    X[7] = 3.0e4
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dev(m), dev(X), Y, rows, cols, T)])
+    ref = _ref(q6, m, X, rows, cols)
+    got = host(Y)
+    for t in range(T):
+        assert O.maxrel(got[t], ref[t]) < TOL, t
+
+
+@pytest.mark.parametrize("q6", [False, True])
+@pytest.mark.parametrize("cols", [32768, 33024])
+def test_matmul_wide_rows(rb, oracle_lib, q6, cols):
+    """128 blocks a row is the widest the staged kernel takes; 129 goes token by token."""
+    rows, T = 40, 9
+    m = synth.quant_matrix(cols + int(q6), rows, cols, q6)
+    X = np.random.default_rng(cols).uniform(-1, 1, (T, cols)).astype(np.float32)
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dev(m), dev(X), Y, rows, cols, T)])
+    assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
+
+
+def test_matmul_mixed_batch(rb, oracle_lib):
+    """One call mixing staged jobs of different widths (block counts that do not divide evenly
+    into the split parts) with jobs that go token by token (T < 8, a Q6_K row that is not a
+    multiple of 16 bytes)."""
+    specs = [(False, 300, 2816, 20), (True, 100, 6144, 33), (False, 64, 512, 8), (True, 50, 512, 10),
+             (False, 70, 2048, 3)]
+    keep, jobs, refs = [], [], []
+    for i, (q6, rows, cols, T) in enumerate(specs):
+        m = synth.quant_matrix(700 + i, rows, cols, q6)
+        X = np.random.default_rng(i).standard_normal((T, cols)).astype(np.float32)
+        dm, dX, Y = dev(m), dev(X), torch.zeros(T, rows, device="cuda")
+        keep.append((dm, dX, Y))
+        jobs.append((q6, dm, dX, Y, rows, cols, T))
+        refs.append(_ref(q6, m, X, rows, cols))
+    rb.matmul_quant_batch(jobs)
+    for (_, _, Y), ref in zip(keep, refs):
+        assert O.maxrel(host(Y), ref) < TOL
