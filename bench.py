@@ -339,6 +339,76 @@ def proj_cpu_reference(seconds: float = 1.5) -> dict:
             "sample_MB": proj_bytes(shapes) / 1e6}
 
 
+PREFILL_PROJ_T = 256      # one prefill chunk (the reference's MM_MAX_T, kernels.c:1837)
+
+
+def proj_flops(shapes, T: int) -> float:
+    return 2.0 * T * sum(r * c for _, r, c in shapes)
+
+
+def run_prefill_projections(R, torch, dev, stream, steps: int, rank: int):
+    """One 256-token prefill chunk through every projection of the stack in one
+    kernel_cuda_matmul_quant_batch call (190 jobs; the projections of a layer that read the same
+    input share one X, as in the reference's batched prefill). Random k-quant blocks, N(0,1)
+    activations. Returns (ms per step, launches)."""
+    T = PREFILL_PROJ_T
+    keep, jobs = [], []
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7100 + rank)
+    layers = [PROJ_ATT] * 10 + [PROJ_DN] * 30
+    for shapes in layers:
+        xs = {}
+        for q6, r, c in shapes:
+            if c not in xs or c == 4096:        # the o / ssm_out projections read their own input
+                xs[c] = torch.randn(T, c, device=dev, generator=gen)
+            m = torch.randint(0, 256, (r * (c // 256) * (210 if q6 else 144),), dtype=torch.uint8, device=dev,
+                              generator=gen)
+            y = torch.empty(T, r, device=dev)
+            keep.append((m, xs[c], y))
+            jobs.append(R.KernelCudaMatmulJob(int(q6), m.data_ptr(), xs[c].data_ptr(), y.data_ptr(), r, c, T))
+    arr = (R.KernelCudaMatmulJob * len(jobs))(*jobs)
+    lib = R.lib()
+    for _ in range(3):
+        if lib.kernel_cuda_matmul_quant_batch(arr, len(jobs)) != 0:
+            raise RuntimeError(R.last_error())
+    R.synchronize()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = R.launch_count()
+    e0.record(stream)
+    for _ in range(steps):
+        lib.kernel_cuda_matmul_quant_batch(arr, len(jobs))
+    e1.record(stream)
+    R.synchronize()
+    torch.cuda.synchronize()
+    launches = R.launch_count() - n0
+    del keep
+    return e0.elapsed_time(e1) / steps, launches
+
+
+def prefill_proj_cpu_reference(seconds: float = 2.0) -> dict:
+    """The reference's own CPU prefill matmul (matmul_quant_cpu under OpenMP) on one attention
+    layer's and one DeltaNet layer's projections for a 256-token chunk, repeated for about
+    `seconds`."""
+    import numpy as np
+    import oracle as O
+    from roaster_b200 import synth
+    shapes = PROJ_ATT + PROJ_DN
+    T = PREFILL_PROJ_T
+    mats = [(q6, synth.quant_matrix(21 + i, r, c, q6),
+             np.random.default_rng(i).standard_normal((T, c)).astype(np.float32), r, c)
+            for i, (q6, r, c) in enumerate(shapes)]
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for q6, m, X, r, c in mats:
+            O.matmul_q(q6, m, X, r, c, impl="ref")
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > seconds:
+            break
+    return {"TFLOPs": proj_flops(shapes, T) * reps / el / 1e12, "threads": os.cpu_count(), "reps": reps}
+
+
 # ------------------------------------------------------------------------------ long context (config 4)
 
 LONG_SLOTS = 16
@@ -710,6 +780,39 @@ def run_ours(a):
             except Exception as e:  # reported, not fatal
                 proj["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
 
+    pproj = None
+    if not a.no_proj:
+        pms, plaunch = run_prefill_projections(R, torch, dev, stream, a.proj_steps, rank)
+        tq = torch.tensor([pms], device=dev)
+        if world > 1:
+            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
+        pms = float(tq.item())
+        pflop = proj_flops(PROJ_SHAPES, PREFILL_PROJ_T)
+        _, tens_p, src_p = peaks()
+        tfs = pflop / (pms / 1e3) / 1e12
+        pproj = {"metric": "prefill projections TFLOP/s (one 256-token chunk through the 40-layer stack's "
+                           "Q4_K/Q6_K attention + DeltaNet projections, one kernel_cuda_matmul_quant_batch call)",
+                 "value": round(tfs * world, 2), "unit": "TFLOP/s", "ms_per_step": round(pms, 4),
+                 "tokens_per_s": round(PREFILL_PROJ_T / (pms / 1e3) * world, 1),
+                 "steps": a.proj_steps, "gpu_launches": int(plaunch), "jobs": len(PROJ_SHAPES),
+                 "algorithmic_flop_per_step": pflop,
+                 "data": "synthetic: uniform random k-quant blocks, N(0,1) activations",
+                 "roofline": {"bound": "tensor", "kernel": "quant_matmul_kernel",
+                              "achieved": round(tfs, 2), "peak": tens_p, "unit": "TFLOP/s",
+                              "frac": round(tfs / tens_p, 4),
+                              "peak_source": f"{src_p} bf16_tflops (burst)",
+                              "note": "warp MMA (mma.sync m16n8k16); each product runs as 2 f16 MMAs "
+                                      "(activation hi + lo; Q6_K 4: the scale split in two exact halves)"}}
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            try:
+                c = prefill_proj_cpu_reference()
+                pproj["cpu_baseline"] = {"value": round(c["TFLOPs"], 4), "unit": "TFLOP/s", "cores": c["threads"],
+                                         "kind": "reference",
+                                         "sample": f"{c['reps']} x one attention + one DeltaNet layer's projections "
+                                                   f"for 256 tokens, the reference's matmul_quant_cpu under OpenMP"}
+            except Exception as e:  # reported, not fatal
+                pproj["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
+
     long_ctx = None
     if not a.no_long:
         long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window,
@@ -753,7 +856,7 @@ def run_ours(a):
                 "deltanet_step_kernel": {"ms": round(dn_avg, 4), "GB/s": round(dn_gbs, 1),
                                          "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
-            "prefill": prefill, "long_context": long_ctx, "projections": proj,
+            "prefill": prefill, "long_context": long_ctx, "projections": proj, "prefill_projections": pproj,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

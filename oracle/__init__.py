@@ -88,6 +88,8 @@ def _load(which: str):
         lib.ref_delta_layer_prefill.restype = C.c_int
         lib.ref_matvec_q.argtypes = [C.c_int, C.c_void_p, _fp, _fp, C.c_size_t, C.c_size_t]
         lib.ref_matvec_q.restype = None
+        lib.ref_matmul_q.argtypes = [C.c_int, C.c_void_p, _fp, _fp, C.c_size_t, C.c_size_t, C.c_size_t]
+        lib.ref_matmul_q.restype = None
         lib.ref_kvw_new.argtypes = [C.c_size_t, C.c_int, C.c_size_t, C.c_size_t, C.c_char_p]
         lib.ref_kvw_new.restype = C.c_void_p
         lib.ref_kvw_free.argtypes = [C.c_void_p]
@@ -405,6 +407,22 @@ def matvec_q(is_q6: bool, m, x, rows: int, cols: int, impl: str = "port"):
     fn = _load("port").orc_matvec_q if impl == "port" else _load("ref").ref_matvec_q
     fn(int(bool(is_q6)), m.ctypes.data_as(C.c_void_p), _f(x), _f(out), rows, cols)
     return out
+
+
+def matmul_q(is_q6: bool, m, X, rows: int, cols: int, impl: str = "port"):
+    """Multi-token k-quant projection Y[t] = W X[t] for X [T][cols] -> [T][rows]. impl "ref" runs the
+    reference's CPU prefill matmul itself (matmul_quant_cpu, kernels.c:1877-1913: each block
+    dequantised to fp32 once per 32-row tile, then dotted with every token); "port" runs the
+    oracle's per-row restatement once per token."""
+    m = np.ascontiguousarray(m, np.uint8)
+    X = np.ascontiguousarray(X, np.float32)
+    T = X.shape[0]
+    assert m.size == rows * (cols // 256) * (210 if is_q6 else 144) and X.shape == (T, cols)
+    if impl == "port":
+        return np.stack([matvec_q(is_q6, m, X[t], rows, cols) for t in range(T)])
+    Y = np.zeros((T, rows), np.float32)
+    _load("ref").ref_matmul_q(int(bool(is_q6)), m.ctypes.data_as(C.c_void_p), _f(X), _f(Y), rows, cols, T)
+    return Y
 
 
 def ref_lib():

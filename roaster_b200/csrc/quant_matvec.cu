@@ -781,13 +781,33 @@ struct MParams {
     unsigned *err;
 };
 
+// The activations of one call: each distinct X with its fragment buffers.
+struct PJob {
+    const float *X;
+    uint2 *bf, *bm;
+    int *e;
+    int T, cols, cta0;           // cta0: first CTA of this X (one CTA per padded token)
+};
+
+struct PParams {
+    PJob jobs[kMaxJobs];
+    int njobs;
+};
+
 // Per padded token (one CTA each): the activation's scale exponent and its B fragments.
-__global__ void __launch_bounds__(256) quant_mm_prep_kernel(const float *X, int T, int cols, uint2 *bf, uint2 *bm,
-                                                            int *eout)
+__global__ void __launch_bounds__(256) quant_mm_prep_kernel(const __grid_constant__ PParams pp)
 {
     __shared__ float red[8];
     __shared__ float xs[8 * kMmMaxNb];             // sub-block sums, scaled by 2^(e-5) to stay in f16 range
-    const int tok = blockIdx.x, nb = cols / 256;
+    int jx = 0;
+    while (jx + 1 < pp.njobs && pp.jobs[jx + 1].cta0 <= (int)blockIdx.x)
+        jx++;
+    const PJob &P = pp.jobs[jx];
+    const float *X = P.X;
+    uint2 *bf = P.bf, *bm = P.bm;
+    int *eout = P.e;
+    const int T = P.T, cols = P.cols;
+    const int tok = blockIdx.x - P.cta0, nb = cols / 256;
     const bool real = tok < T;
     const float *x = X + (size_t)(real ? tok : 0) * cols;
     float mx = 0.f;
@@ -1435,15 +1455,19 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
             pos += ((size_t)J.P * J.rows * J.T * sizeof(float) + 255) / 256 * 256;
         }
     }
+    PParams pp;
+    memset(static_cast<void *>(&pp), 0, sizeof(pp));
+    long long ctas = 0;
     for (const XEnt &e : xe) {
-        const unsigned padded = (unsigned)((e.T + kMmTok - 1) / kMmTok * kMmTok);
-        quant_mm_prep_kernel<<<padded, 256, 0, R.stream>>>(e.X, (int)e.T, (int)e.cols,
-                                                           reinterpret_cast<uint2 *>(ws + e.off_bf),
-                                                           reinterpret_cast<uint2 *>(ws + e.off_bm),
-                                                           reinterpret_cast<int *>(ws + e.off_e));
-        if (launched("quant_mm_prep_kernel") != 0)
-            return -1;
+        pp.jobs[pp.njobs++] = PJob{e.X, reinterpret_cast<uint2 *>(ws + e.off_bf), reinterpret_cast<uint2 *>(ws + e.off_bm),
+                                   reinterpret_cast<int *>(ws + e.off_e), (int)e.T, (int)e.cols, (int)ctas};
+        ctas += (long long)((e.T + kMmTok - 1) / kMmTok * kMmTok);
     }
+    if (ctas >= (1ll << 31))
+        return fail("kernel_cuda_matmul_quant_batch: too many tokens in one call");
+    quant_mm_prep_kernel<<<(unsigned)ctas, 256, 0, R.stream>>>(pp);
+    if (launched("quant_mm_prep_kernel") != 0)
+        return -1;
     if (!attr_set) {
         if (check(cudaFuncSetAttribute(quant_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmSmem),
                   "matmul shared memory") != 0)

@@ -144,3 +144,18 @@ def test_port_vs_reference_matvec_q(oracle_lib, q6, rows, cols):
     a = O.matvec_q(q6, m, x, rows, cols, impl="port")
     b = O.matvec_q(q6, m, x, rows, cols, impl="ref")
     assert O.maxrel(a, b) < 2e-6
+
+
+@pytest.mark.parametrize("q6", [False, True])
+@pytest.mark.parametrize("rows,cols,T", [(37, 2048, 3), (300, 512, 40), (64, 4096, 257)])
+def test_port_vs_reference_matmul_q(oracle_lib, q6, rows, cols, T):
+    """The oracle's per-token matvec against the reference's own CPU prefill matmul
+    (matmul_quant_cpu: dequantise a block to fp32, then dot it with each token; more than 256
+    tokens run as 256-token chunks). Same fp32 terms summed in another order: 2e-6 maxrel."""
+    if not O.have_ref():
+        pytest.skip("reference build (oracle/_ref) not present")
+    m = synth.quant_matrix(rows + T, rows, cols, q6)
+    X = np.random.default_rng(T).standard_normal((T, cols)).astype(np.float32)
+    a = O.matmul_q(q6, m, X, rows, cols, impl="port")
+    b = O.matmul_q(q6, m, X, rows, cols, impl="ref")
+    assert O.maxrel(a, b) < 2e-6

@@ -1,9 +1,8 @@
 """Multi-token k-quant projections (kernel_cuda_matmul_quant_batch) on the reference's own test
 shapes (src/test_kernels.c:42-70: T in 1, 3, 8, 9, 16, 17, 100, 257; rows 512, 2048, 37; cols
-2048 or 512; Q4_K and Q6_K; several jobs sharing X), against the reference's CPU dot per row and
-token (oracle/_ref; the oracle restatement where it is absent). The reference's matmul dequantises
-a block then dots it (kernels.c:1877-1905), the same fp32 math in another order; its own test bar
-is 2e-4 maxrel, this one 1e-5."""
+2048 or 512; Q4_K and Q6_K; several jobs sharing X), against the reference's own CPU prefill
+matmul (matmul_quant_cpu, kernels.c:1877-1913, built into oracle/_ref; the oracle restatement
+token by token where that build is absent). Its own test bar is 2e-4 maxrel, this one 1e-5."""
 import numpy as np
 import pytest
 import torch
@@ -17,8 +16,7 @@ TOL = 1e-5
 
 
 def _ref(q6, m, X, rows, cols):
-    impl = "ref" if O.have_ref() else "port"
-    return np.stack([O.matvec_q(q6, m, X[t], rows, cols, impl=impl) for t in range(X.shape[0])])
+    return O.matmul_q(q6, m, X, rows, cols, impl="ref" if O.have_ref() else "port")
 
 
 @pytest.mark.parametrize("q6", [False, True])
@@ -123,3 +121,15 @@ def test_matmul_mixed_batch(rb, oracle_lib):
     rb.matmul_quant_batch(jobs)
     for (_, _, Y), ref in zip(keep, refs):
         assert O.maxrel(host(Y), ref) < TOL
+
+
+@pytest.mark.parametrize("q6,rows,cols", [(False, 8192, 2048), (True, 2048, 4096)])
+def test_matmul_prefill_chunk(rb, oracle_lib, q6, rows, cols):
+    """One 256-token prefill chunk (the reference's MM_MAX_T) through a full-size projection of
+    the stack (q+gate Q4_K; o / ssm_out Q6_K): every tile full, no split."""
+    T = 256
+    m = synth.quant_matrix(rows + int(q6), rows, cols, q6)
+    X = np.random.default_rng(256).standard_normal((T, cols)).astype(np.float32)
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dev(m), dev(X), Y, rows, cols, T)])
+    assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
