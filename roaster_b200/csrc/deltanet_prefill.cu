@@ -23,8 +23,8 @@
 //   (d2) Delta^T M^T                                  128 x 64
 //   (e) Delta''^T K                                   128 x 128 (state update)
 // The fp32 state S^T stays in TMEM for the whole prompt (128 columns). T = (I + L)^-1 is formed
-// on the CUDA cores (16 x 16 diagonal blocks by substitution, then three levels of block
-// products).
+// on the CUDA cores of the producer warps (16 x 16 diagonal blocks by substitution, then three
+// levels of block products between hardware barriers).
 //
 // Precision: every operand is split into two f16 parts, x = hi + lo, and each product is
 // hi*hi + hi*lo + lo*hi with fp32 accumulation -- about 22 significant bits, which keeps the
@@ -36,7 +36,9 @@
 // Roles (384 threads): warps 0-3 own TMEM lanes 0-127 and do the chunk arithmetic; thread 0
 // also issues every tcgen05.mma. Warps 4-11 load the next chunk's q/k/v rows into registers
 // while the current chunk runs, then scale, split and store them once the chunk's last MMA
-// has committed.
+// has committed, then write the finished chunk's outputs from tensor memory (two warps per TMEM
+// lane quarter, 32 tokens each), and form the new chunk's T block once (a) lands -- L from the K
+// rows of (a), T = (I + L)^-1, and the B operands of (b) -- while the arithmetic warps build M.
 #include "ptx.cuh"
 #include "runtime.h"
 #include "tcgen05.cuh"
@@ -77,7 +79,7 @@ constexpr uint32_t kOffB = 98304;      // BV hi, BV lo, BK hi, BK lo (8 KB each)
 constexpr uint32_t kOffW = 131072;     // T (fp32 scratch), later W' hi|lo
 constexpr uint32_t kOffM = 163840;     // M hi, M lo (8 KB each)
 constexpr uint32_t kOffConst = 180224; // ChunkConst[2]
-constexpr int kLd = 65;                // fp32 scratch row stride (floats)
+constexpr int kLd = 68;                // fp32 scratch row stride of L and T (floats; rows 16-byte aligned)
 
 struct ChunkConst {
     float glf[kC];                     // G_j * log2(e) (summed in double, rounded once)
@@ -93,11 +95,13 @@ struct ChunkConst {
 static_assert(sizeof(ChunkConst) % 16 == 0, "");
 constexpr uint32_t kOffCons = kOffConst + 2 * sizeof(ChunkConst);   // consumer scratch
 struct ConsScratch {
-    float iu_v[kC], iu_k[kC], imu[kC];
+    float iu_v[kC], iu_k[kC];
+    float imu[2][kC];                  // M row scales, by chunk parity (read by the output epilogue)
+    float sig[2][kD], rho[2][kD];      // per value row: 1 / scale of S_0 and of Delta, by chunk parity
     float red[4];
 };
 constexpr uint32_t kOffBars = kOffCons + ((sizeof(ConsScratch) + 15) / 16) * 16;
-constexpr size_t kSmemBytes = kOffBars + 64 + 1024;
+constexpr size_t kSmemBytes = kOffBars + 128 + 1024;
 
 struct DJob {
     float *state;
@@ -193,49 +197,93 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[kC])
     }
 }
 
-// The off-diagonal blocks of T = (I + L)^-1 (16 x 16 blocks, fp32 scratch with row stride kLd),
-// by distance d = 1..3: X_ij = sum_{m=16j}^{16i-1} L[16i+rr][m] T[m][16j+cc], T_ij = -D_i X_ij
-// (D_i = the inverted diagonal block). Run by all 384 threads (q = thread index); the steps meet
-// on a CTA-wide mbarrier with bounded waits. Returns false on a wait timeout.
-__device__ __forceinline__ bool inv_levels(const float *Lm, float *Tm, float *Xs, int q, uint32_t lvbar,
-                                           uint32_t &lvphase)
+// T = (I + L)^-1 for the 64 x 64 strictly lower L in 16 x 16 blocks (fp32 scratch, row stride
+// kLd), by the 256 producer threads; the threads always reach the same barriers (named barrier
+// BAR): no step here waits on anything else.
+//  1. Forward substitution through each diagonal block (I + L_ii), one right-hand-side column per
+//     thread: the unit columns give T_ii = (I + L_ii)^-1, the columns of the blocks L_im (m < i)
+//     give L'_im = T_ii L_im, written over L_im (160 columns; L_ii itself is only read).
+//  2. By distance d = 1..3: T_ij = -sum_{m=j}^{i-1} L'_im T_mj, one step per distance with the
+//     (4 - d) blocks split into 1 x 4 strips, one per thread (k = q / 64, rr = q / 4 % 16,
+//     cc = 4 (q % 4)): T and the results move as 16-byte words and L' as a broadcast.
+__device__ __forceinline__ void fma4(float4 &a, float s, const float4 &t)
 {
-    auto sync = [&]() -> bool {
-        __syncwarp();                        // the warp's writes, then one arrival per warp
-        if ((q & 31) == 0)
-            mbar_arrive(lvbar);
-        const bool ok = mbar_wait(lvbar, lvphase & 1u);
-        lvphase++;
-        return ok;
-    };
-#pragma unroll 1
-    for (int d = 1; d <= 3; d++) {
-        const int nel = (4 - d) * 256;
-        for (int e = q; e < nel; e += kThreads) {
-            const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
-            float acc = 0.f;
-            const float *lrow_p = Lm + (16 * bi + rr) * kLd;
-#pragma unroll 4
-            for (int m = 16 * bj; m < 16 * bi; m++)
-                acc = fmaf(lrow_p[m], Tm[m * kLd + 16 * bj + c2], acc);
-            Xs[e] = acc;
-        }
-        if (!sync())
-            return false;
-        for (int e = q; e < nel; e += kThreads) {
-            const int blk = e >> 8, bi = blk + d, bj = blk, rr = (e >> 4) & 15, c2 = e & 15;
-            float acc = 0.f;
-            const float *drow = Tm + (16 * bi + rr) * kLd + 16 * bi;
-            const float *xb = Xs + (e & ~255);
+    a.x = fmaf(s, t.x, a.x);
+    a.y = fmaf(s, t.y, a.y);
+    a.z = fmaf(s, t.z, a.z);
+    a.w = fmaf(s, t.w, a.w);
+}
+
+template <int D, int BAR>
+__device__ __forceinline__ void inv_level(const float *Lp, float *Tm, int q)
+{
+    constexpr int NB = 4 - D;                        // blocks at distance D
+    const int k = q >> 6, rr = (q >> 2) & 15, c4 = 4 * (q & 3);
+    if (k < NB) {
+        const float *lrow = Lp + (16 * (k + D) + rr) * kLd + 16 * k;
+        const float *tcol = Tm + 16 * k * kLd + 16 * k + c4;
+        float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
 #pragma unroll
-            for (int m = 0; m < 16; m++)
-                acc = fmaf(m <= rr ? drow[m] : 0.f, xb[m * 16 + c2], acc);
-            Tm[(16 * bi + rr) * kLd + 16 * bj + c2] = -acc;
+        for (int m = 0; m < 16 * D; m += 2) {
+            fma4(a0, lrow[m], *reinterpret_cast<const float4 *>(tcol + m * kLd));
+            fma4(a1, lrow[m + 1], *reinterpret_cast<const float4 *>(tcol + (m + 1) * kLd));
         }
-        if (!sync())
-            return false;
+        *reinterpret_cast<float4 *>(Tm + (16 * (k + D) + rr) * kLd + 16 * k + c4) =
+            make_float4(-(a0.x + a1.x), -(a0.y + a1.y), -(a0.z + a1.z), -(a0.w + a1.w));
     }
-    return true;
+    named_bar_sync(BAR, 256);
+}
+
+template <int BAR>
+__device__ __forceinline__ void tri_inverse(float *Lw, float *Tm, int q)
+{
+    if (q < 160) {
+        int i, c;                                    // block row, column within [0, 16 i + 16)
+        bool unit;
+        if (q < 64) {
+            i = q >> 4;
+            c = 16 * i + (q & 15);
+            unit = true;
+        } else {
+            const int u = q - 64;
+            i = u < 16 ? 1 : (u < 48 ? 2 : 3);
+            c = u - (i == 1 ? 0 : (i == 2 ? 16 : 48));
+            unit = false;
+        }
+        const float *Lii = Lw + 16 * i * kLd + 16 * i;
+        float y[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; rr++) {
+            float acc = unit ? (16 * i + rr == c ? 1.f : 0.f) : Lw[(16 * i + rr) * kLd + c];
+#pragma unroll
+            for (int m = 0; m < rr; m++)
+                acc = fmaf(-Lii[rr * kLd + m], y[m], acc);
+            y[rr] = acc;
+        }
+        float *dst = unit ? Tm : Lw;
+#pragma unroll
+        for (int rr = 0; rr < 16; rr++)
+            dst[(16 * i + rr) * kLd + c] = y[rr];
+    }
+    named_bar_sync(BAR, 256);
+    inv_level<1, BAR>(Lw, Tm, q);
+    inv_level<2, BAR>(Lw, Tm, q);
+    inv_level<3, BAR>(Lw, Tm, q);
+}
+
+// Half (32 values, times s) of row r of a K-major swizzled tile pair (hi, lo): units 4h .. 4h+3.
+__device__ __forceinline__ void store_half_split(uint32_t hi, uint32_t lo, int r, int h, const float (&x)[32], float s)
+{
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+            split2(x[8 * u + 2 * p] * s, x[8 * u + 2 * p + 1] * s, hw[p], lw[p]);
+        const uint32_t off = (uint32_t)r * 128u + ((((uint32_t)(4 * h + u)) ^ (uint32_t)(r & 7)) << 4);
+        sts128(hi + off, hw[0], hw[1], hw[2], hw[3]);
+        sts128(lo + off, lw[0], lw[1], lw[2], lw[3]);
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __grid_constant__ DPParams p)
@@ -250,7 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
     const uint32_t done_bar = smem_addr(&bars[2]), drain_bar = smem_addr(&bars[3]);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[4]);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(&bars[5]);
-    const uint32_t lv_bar = smem_addr(&bars[6]);      // all 384 threads meet here for T's levels
+    const uint32_t out_bar = smem_addr(&bars[6]);     // producers have read a chunk's outputs from TMEM
+    const uint32_t a_bar = smem_addr(&bars[7]);       // (a) of the chunk has landed in TMEM
+    const uint32_t t_bar = smem_addr(&bars[8]);       // producers have stored the B operands of (b)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int vh = blockIdx.x, kh = vh & 15;
@@ -263,7 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         mbar_init(mma_bar, 1);
         mbar_init(done_bar, 1);
         mbar_init(drain_bar, 1);
-        mbar_init(lv_bar, kThreads / 32);
+        mbar_init(out_bar, kProdThreads / 32);
+        mbar_init(a_bar, 1);
+        mbar_init(t_bar, kProdThreads / 32);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -315,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
             }
         };
-        uint32_t lvphase = 0;
         issue_loads(0);
         for (int n = 0; n < nchunks; n++) {
             bool ok = true;
@@ -400,31 +451,117 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(in_full);
+            if (n > 0) {
+                // outputs of chunk n - 1 (a full chunk: only the last can be short), whose MMAs
+                // completed before done_bar's phase n - 1; the arithmetic warps wait on out_bar
+                // before the MMAs that overwrite these columns
+                tc::fence_after_sync();
+                const int q4 = warp & 3, half = pw >> 2;          // TMEM lane quarter, 32-token half
+                const int rr = 32 * q4 + lane;                     // value row
+                const uint32_t lq = (uint32_t)(32 * q4) << 16;
+                const int pb = (n - 1) & 1;
+                const ChunkConst &Cp = cc[pb];
+                const float sg = cs->sig[pb][rr] * kOutScale, rh = cs->rho[pb][rr] * kOutScale;
+#pragma unroll 1
+                for (int h = 0; h < 2; h++) {
+                    const int c0 = 32 * half + 16 * h;             // first token of this group
+                    float d1[16], d2[16];
+                    tc::tmem_ld16(tb + lq + kColD1 + c0, d1);
+                    tc::tmem_ld16(tb + lq + kColU + c0, d2);
+                    tc::tmem_wait_ld();
+                    float *o = J.out + (((long long)(n - 1) * kC + c0) * 32 + vh) * kD + rr;
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        o[(long long)i * 32 * kD] = Cp.gq[c0 + i] * sg * d1[i] + cs->imu[pb][c0 + i] * rh * d2[i];
+                }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(out_bar);
+            }
+            // ---- T block of chunk n: L from the K rows of (a), T = (I + L)^-1, B operands of (b)
+            {
+                const bool w = mbar_wait_sleep(a_bar, (uint32_t)n & 1u, 64);
+                if (!bar_all(3, kProdThreads, w && !*abort_flag)) {
+                    if (tid == kThreads - kProdThreads)
+                        set_abort();
+                    break;
+                }
+                tc::fence_after_sync();
+                const int pq = tid - (kThreads - kProdThreads);   // 0..255
+                float *Lw = reinterpret_cast<float *>(gbase + kOffB);
+                float *Tm = reinterpret_cast<float *>(gbase + kOffW);
+                const int q4 = warp & 3, half = pw >> 2;
+                if (q4 < 2) {
+                    // row i of L, columns 32 half .. 32 half + 31 (TMEM lanes 0-63 hold (a)'s K rows)
+                    const int i = 32 * q4 + lane;
+                    float x[32];
+                    tc::tmem_ld32(tb + ((uint32_t)(32 * q4) << 16) + kColA + 32 * half, x);
+                    tc::tmem_wait_ld();
+                    const float gi = C.glf[i];
+                    const float f = C.beta[i] * C.isk[i];
+#pragma unroll
+                    for (int j4 = 0; j4 < 32; j4 += 4) {
+                        const int j = 32 * half + j4;
+                        const float4 g4 = *reinterpret_cast<const float4 *>(&C.glf[j]);
+                        const float4 s4 = *reinterpret_cast<const float4 *>(&C.isk[j]);
+                        float4 l;
+                        l.x = j < i ? f * ex2(gi - g4.x) * x[j4] * s4.x : 0.f;
+                        l.y = j + 1 < i ? f * ex2(gi - g4.y) * x[j4 + 1] * s4.y : 0.f;
+                        l.z = j + 2 < i ? f * ex2(gi - g4.z) * x[j4 + 2] * s4.z : 0.f;
+                        l.w = j + 3 < i ? f * ex2(gi - g4.w) * x[j4 + 3] * s4.w : 0.f;
+                        *reinterpret_cast<float4 *>(Lw + i * kLd + j) = l;
+                    }
+                }
+                tc::fence_before_sync();
+                named_bar_sync(3, kProdThreads);
+                tri_inverse<3>(Lw, Tm, pq);
+                {
+                    // B operands of (b): rows of T diag(beta / s^v) (tasks 0-63) and
+                    // T diag(beta gamma / s^k) (tasks 64-127), two threads (adjacent lanes) per row
+                    const int task = pq >> 1, h = pq & 1, i = task & 63;
+                    const bool isv = task < kC;
+                    float x[32];
+                    const float *bsrc = isv ? C.bv : C.bk;
+#pragma unroll
+                    for (int j4 = 0; j4 < 32; j4 += 4) {
+                        const int j = 32 * h + j4;
+                        const float4 t4 = *reinterpret_cast<const float4 *>(Tm + i * kLd + j);
+                        const float4 b4 = *reinterpret_cast<const float4 *>(bsrc + j);
+                        x[j4] = j <= i ? t4.x * b4.x : 0.f;
+                        x[j4 + 1] = j + 1 <= i ? t4.y * b4.y : 0.f;
+                        x[j4 + 2] = j + 2 <= i ? t4.z * b4.z : 0.f;
+                        x[j4 + 3] = j + 3 <= i ? t4.w * b4.w : 0.f;
+                    }
+                    float m = 0.f;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++)
+                        m = fmaxf(m, fabsf(x[jj]));
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                    const float u = pow2_scale(m);
+                    const uint32_t hi = base + kOffB + (isv ? 0u : 16384u);
+                    store_half_split(hi, hi + 8192, i, h, x, u);
+                    if (h == 0) {
+                        if (isv)
+                            cs->iu_v[i] = pow2_inv(u);
+                        else
+                            cs->iu_k[i] = pow2_inv(u);
+                    }
+                    fence_proxy_async();
+                }
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(t_bar);
+            }
+            // keep the next chunk's loads (96 registers) from being hoisted above the work before
+            asm volatile("" ::: "memory");
             if (n + 1 < nchunks)
                 issue_loads(n + 1);
-            // help with this chunk's triangular inverse once its diagonal blocks are ready
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(lv_bar);
-            bool lv = mbar_wait_sleep(lv_bar, lvphase & 1u, 64);
-            lvphase++;
-            lv = lv && inv_levels(reinterpret_cast<const float *>(gbase + kOffB),
-                                  reinterpret_cast<float *>(gbase + kOffW),
-                                  reinterpret_cast<float *>(gbase + kOffB) + kC * kLd, tid, lv_bar, lvphase);
-            if (!lv) {
-                if (tid == kThreads - kProdThreads)
-                    set_abort();
-                break;
-            }
         }
     } else {
         // ============================================================ chunk arithmetic
         const int r = tid;                                  // TMEM lane: value (or key) index
         const uint32_t lrow = (uint32_t)(32 * warp) << 16;  // lane offset of this warp
-        const float *Lm = reinterpret_cast<const float *>(gbase + kOffB);
-        float *Lw = reinterpret_cast<float *>(gbase + kOffB);
-        float *Xs = reinterpret_cast<float *>(gbase + kOffB) + kC * kLd;
-        float *Tm = reinterpret_cast<float *>(gbase + kOffW);
         // shared-memory operand descriptors (the layout is static; MMAs add compile-time offsets)
         const uint64_t dKQH = tc::smem_desc(base + kOffKQH, 16, 1024), dKQL = tc::smem_desc(base + kOffKQL, 16, 1024);
         const uint64_t dKQHm = tc::smem_desc(base + kOffKQH, 16384, 1024);     // K' as MN-major operand
@@ -435,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         const uint64_t dWm = tc::smem_desc(base + kOffW, 8192, 1024);          // W' (MN-major)
         const uint64_t dM = tc::smem_desc(base + kOffM, 16, 1024);
         float inv_sigma = 1.f, inv_rho = 1.f, inv_rho2 = 1.f, inv_omega = 1.f;
-        uint32_t mphase = 0, lvphase = 0;
+        uint32_t mphase = 0;
         bool ok = true;
 
         auto wait_mma = [&]() -> bool {
@@ -449,8 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             return all;
         };
 
-        // S_0^T split into TMEM columns [128, 256) from the master, with row scale sigma.
-        auto write_s0 = [&]() {
+        // S_0^T of chunk m split into TMEM columns [128, 256) from the master, with row scale sigma
+        // (its inverse also kept for the output epilogue).
+        auto write_s0 = [&](int m) {
             float amax = 0.f;
 #pragma unroll 1
             for (int c = 0; c < kD; c += 32) {
@@ -463,6 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             }
             const float sg = pow2_scale(amax);
             inv_sigma = pow2_inv(sg);
+            cs->sig[m & 1][r] = inv_sigma;
 #pragma unroll 1
             for (int c = 0; c < kD; c += 32) {
                 float x[32];
@@ -490,7 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             const ChunkConst &C = cc[n & 1];
             const long long t0 = (long long)n * kC;
             const int tcn = (int)(T - t0 < kC ? T - t0 : kC);
-            {
+            if (last) {
+                // the last chunk's outputs (the producer warps write the others)
                 float d1[kC], d2[kC];
                 tmem_ld64(tb + lrow + kColD1, d1);
                 tmem_ld64(tb + lrow + kColU, d2);
@@ -499,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 for (int i = 0; i < kC; i++) {
                     if (i < tcn)
                         o[(long long)i * 32 * kD] =
-                            kOutScale * (C.gq[i] * inv_sigma * d1[i] + cs->imu[i] * inv_rho * d2[i]);
+                            kOutScale * (C.gq[i] * inv_sigma * d1[i] + cs->imu[n & 1][i] * inv_rho * d2[i]);
                 }
             }
             const float gC = C.gC;
@@ -517,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             }
             tc::tmem_wait_st();
             if (!last)
-                write_s0();
+                write_s0(n + 1);
             tc::fence_before_sync();
             return true;
         };
@@ -534,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tc::tmem_st32(tb + lrow + kColS + c, w32);
             }
             tc::tmem_wait_st();
-            write_s0();
+            write_s0(0);
             tc::fence_before_sync();
         }
 
@@ -571,89 +711,43 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                     }
                 }
                 tc::commit(mma_bar);
+                tc::commit(a_bar);
             }
-            // ---- L (warps 0-1) and M (warps 2-3) from (a)
             if (!wait_mma()) {
                 ok = false;
                 break;
             }
-            {
+            // ---- M from the Q rows of (a) (warps 2-3; the producers take the K rows: L and T)
+            if (r >= kC) {
                 float x[kC];
                 tmem_ld64(tb + lrow + kColA, x);
-                if (r < kC) {
-                    const int i = r;
-                    const float gi = C.glf[i];
-                    const float f = C.beta[i] * C.isk[i];
+                const int i = r - kC;
+                const float gi = C.glf[i];
+                const float f = C.isq[i];
 #pragma unroll
-                    for (int j = 0; j < kC; j++) {
-                        float l = 0.f;
-                        if (j < i)
-                            l = f * ex2(gi - C.glf[j]) * x[j] * C.isk[j];
-                        Lw[i * kLd + j] = l;
-                    }
-                    named_bar_sync(2, 64);
-                    // diagonal 16x16 blocks of T by forward substitution (thread = column)
-                    const int col = r, b16 = col >> 4, cl = col & 15;
-                    float y[16];
-#pragma unroll
-                    for (int rr = 0; rr < 16; rr++) {
-                        float acc = 0.f;
-#pragma unroll
-                        for (int m = 0; m < rr; m++)
-                            acc = fmaf(Lm[(16 * b16 + rr) * kLd + 16 * b16 + m], y[m], acc);
-                        y[rr] = rr < cl ? 0.f : (rr == cl ? 1.f : -acc);
-                    }
-#pragma unroll
-                    for (int rr = 0; rr < 16; rr++)
-                        Tm[(16 * b16 + rr) * kLd + col] = y[rr];
-                } else {
-                    const int i = r - kC;
-                    const float gi = C.glf[i];
-                    const float f = C.isq[i];
-#pragma unroll
-                    for (int j = 0; j < kC; j++)
-                        x[j] = j <= i ? f * ex2(gi - C.glf[j]) * x[j] * C.isk[j] : 0.f;
-                    const float mu = pow2_scale(row_amax(x));
-                    store_row_split(base + kOffM, base + kOffM + 8192, i, x, mu);
-                    cs->imu[i] = pow2_inv(mu);
-                }
+                for (int j = 0; j < kC; j++)
+                    x[j] = j <= i ? f * ex2(gi - C.glf[j]) * x[j] * C.isk[j] : 0.f;
+                const float mu = pow2_scale(row_amax(x));
+                store_row_split(base + kOffM, base + kOffM + 8192, i, x, mu);
+                cs->imu[n & 1][i] = pow2_inv(mu);
+                fence_proxy_async();
             }
-            named_bar_sync(1, 128);
-            // ---- off-diagonal blocks of T, with the producer warps (entry + 6 steps on lv_bar)
+            // the producers have stored the B operands of (b) and read chunk n - 1's outputs from the
+            // columns (b) and (d1) overwrite
             {
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive(lv_bar);
-                bool lv = mbar_wait(lv_bar, lvphase & 1u);
-                lvphase++;
-                lv = lv && inv_levels(Lm, Tm, Xs, r, lv_bar, lvphase);
-                if (!bar_all(1, 128, lv && !*abort_flag)) {
+                bool ob = true;
+                if (tid == 0) {
+                    ob = mbar_wait_sleep(t_bar, (uint32_t)n & 1u, 64);
+                    if (n > 0)
+                        ob = ob && mbar_wait_sleep(out_bar, (uint32_t)(n - 1) & 1u, 64);
+                }
+                if (!bar_all(1, 128, ob && !*abort_flag)) {
                     if (tid == 0)
                         set_abort();
                     ok = false;
                     break;
                 }
             }
-            // ---- B operands of (b): rows of T diag(beta / s^v) and T diag(beta gamma / s^k)
-            {
-                const int i = r & 63;
-                const bool isv = r < kC;
-                float x[kC];
-#pragma unroll
-                for (int j = 0; j < kC; j++) {
-                    const float t = j <= i ? Tm[i * kLd + j] : 0.f;
-                    x[j] = t * (isv ? C.bv[j] : C.bk[j]);
-                }
-                const float u = pow2_scale(row_amax(x));
-                const uint32_t hi = base + kOffB + (isv ? 0u : 16384u);
-                store_row_split(hi, hi + 8192, i, x, u);
-                if (isv)
-                    cs->iu_v[i] = pow2_inv(u);
-                else
-                    cs->iu_k[i] = pow2_inv(u);
-                fence_proxy_async();
-            }
-            named_bar_sync(1, 128);
             // ---- (b): U^T = V'^T BV'^T, W^T = K'^T BK'^T
             if (tid == 0) {
                 tc::fence_after_sync();
@@ -730,6 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
                 const float rho = pow2_scale(row_amax(dl));
                 inv_rho = pow2_inv(rho);
+                cs->rho[n & 1][r] = inv_rho;
                 store_row_split(base + kOffB, base + kOffB + 16384, r, dl, rho);
 #pragma unroll
                 for (int j = 0; j < kC; j++)
