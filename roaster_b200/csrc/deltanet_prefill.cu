@@ -73,10 +73,10 @@ constexpr uint32_t kColD1 = 448;       // (d1)
 // [rows][128 B] blocks; a "half" is 8 KB (64 rows) or 16 KB (128 rows).
 constexpr uint32_t kOffKQH = 0;        // [K c0 | Q c0 | K c1 | Q c1] hi, 4 x 8 KB
 constexpr uint32_t kOffKQL = 32768;    // same, lo
-constexpr uint32_t kOffV = 65536;      // V hi [c0|c1] 16 KB, V lo 16 KB;  later Delta''^T hi|lo
+constexpr uint32_t kOffV = 65536;      // V hi [c0|c1] 16 KB, V lo 16 KB
 constexpr uint32_t kOffB = 98304;      // BV hi, BV lo, BK hi, BK lo (8 KB each); L + X scratch;
                                        // later Delta^T hi|lo
-constexpr uint32_t kOffW = 131072;     // T (fp32 scratch), later W' hi|lo
+constexpr uint32_t kOffW = 131072;     // T (fp32 scratch), then W' hi|lo, then Delta''^T hi|lo
 constexpr uint32_t kOffM = 163840;     // M hi, M lo (8 KB each)
 constexpr uint32_t kOffConst = 180224; // ChunkConst[2]
 constexpr int kLd = 68;                // fp32 scratch row stride of L and T (floats; rows 16-byte aligned)
@@ -301,6 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
     const uint32_t out_bar = smem_addr(&bars[6]);     // producers have read a chunk's outputs from TMEM
     const uint32_t a_bar = smem_addr(&bars[7]);       // (a) of the chunk has landed in TMEM
     const uint32_t t_bar = smem_addr(&bars[8]);       // producers have stored the B operands of (b)
+    const uint32_t b_bar = smem_addr(&bars[9]);       // (b) has finished reading V
+    const uint32_t cd_bar = smem_addr(&bars[10]);     // (c, d1) have finished reading Q (and W')
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int vh = blockIdx.x, kh = vh & 15;
@@ -316,6 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         mbar_init(out_bar, kProdThreads / 32);
         mbar_init(a_bar, 1);
         mbar_init(t_bar, kProdThreads / 32);
+        mbar_init(b_bar, 1);
+        mbar_init(cd_bar, 1);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -369,46 +373,61 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         };
         issue_loads(0);
         for (int n = 0; n < nchunks; n++) {
-            bool ok = true;
-            if (n > 0)
-                ok = mbar_wait_sleep(done_bar, (uint32_t)(n - 1) & 1u, 256);
-            if (!bar_all(3, kProdThreads, ok && !*abort_flag)) {
-                if (tid == kThreads - kProdThreads)
-                    set_abort();
-                break;
-            }
             ChunkConst &C = cc[n & 1];
-            // scale, split and store this chunk's rows
+            // scale, split and store this chunk's rows s0 .. s0 + 7 of the 24 a warp holds
+            // (rows pw + 8 s: s 0-7 K, 8-15 Q, 16-23 V)
+            auto stage = [&](int s0) {
 #pragma unroll
-            for (int s = 0; s < 24; s++) {
-                const int rr = pw + 8 * s, which = rr >> 6, j = rr & 63;
-                const float4 x = buf[s];
-                // non-negative floats order like their bit patterns: one warp max-reduction
-                const float m0 = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
-                const float sc = pow2_scale(__uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m0))));
-                uint32_t h0, l0, h1, l1;
-                split2(x.x * sc, x.y * sc, h0, l0);
-                split2(x.z * sc, x.w * sc, h1, l1);
-                const uint32_t c = (uint32_t)lane >> 4;                    // 64-column chunk
-                const uint32_t unit = ((uint32_t)(lane & 15) >> 1) ^ (uint32_t)(j & 7);
-                const uint32_t inner = (uint32_t)j * 128u + (unit << 4) + (uint32_t)(lane & 1) * 8u;
-                uint32_t hi, lo;
-                if (which == 2) {
-                    hi = base + kOffV + c * 8192u;
-                    lo = hi + 16384u;
-                } else {
-                    hi = base + kOffKQH + c * 16384u + (uint32_t)which * 8192u;
-                    lo = hi + (kOffKQL - kOffKQH);
+                for (int s = s0; s < s0 + 8; s++) {
+                    const int rr = pw + 8 * s, which = rr >> 6, j = rr & 63;
+                    const float4 x = buf[s];
+                    // non-negative floats order like their bit patterns: one warp max-reduction
+                    const float m0 = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+                    const float sc = pow2_scale(__uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m0))));
+                    uint32_t h0, l0, h1, l1;
+                    split2(x.x * sc, x.y * sc, h0, l0);
+                    split2(x.z * sc, x.w * sc, h1, l1);
+                    const uint32_t c = (uint32_t)lane >> 4;                    // 64-column chunk
+                    const uint32_t unit = ((uint32_t)(lane & 15) >> 1) ^ (uint32_t)(j & 7);
+                    const uint32_t inner = (uint32_t)j * 128u + (unit << 4) + (uint32_t)(lane & 1) * 8u;
+                    uint32_t hi, lo;
+                    if (which == 2) {
+                        hi = base + kOffV + c * 8192u;
+                        lo = hi + 16384u;
+                    } else {
+                        hi = base + kOffKQH + c * 16384u + (uint32_t)which * 8192u;
+                        lo = hi + (kOffKQL - kOffKQH);
+                    }
+                    sts64(hi + inner, h0, h1);
+                    sts64(lo + inner, l0, l1);
+                    if (lane == 0) {
+                        const float inv = pow2_inv(sc);
+                        if (which == 0) C.isk[j] = inv;
+                        else if (which == 1) C.isq[j] = inv;
+                        else C.isv[j] = inv;
+                    }
                 }
-                sts64(hi + inner, h0, h1);
-                sts64(lo + inner, l0, l1);
-                if (lane == 0) {
-                    const float inv = pow2_inv(sc);
-                    if (which == 0) C.isk[j] = inv;
-                    else if (which == 1) C.isq[j] = inv;
-                    else C.isv[j] = inv;
+            };
+            // V once (b) of chunk n - 1 has read it, Q once (c, d1) have, K once the chunk's last
+            // MMAs (d2, e) have committed
+            auto gate = [&](uint32_t bar) -> bool {
+                const bool w = n == 0 || mbar_wait_sleep(bar, (uint32_t)(n - 1) & 1u, 64);
+                if (!bar_all(3, kProdThreads, w && !*abort_flag)) {
+                    if (tid == kThreads - kProdThreads)
+                        set_abort();
+                    return false;
                 }
-            }
+                return true;
+            };
+            if (!gate(b_bar))
+                break;
+            stage(16);
+            if (!gate(cd_bar))
+                break;
+            stage(8);
+            if (!gate(done_bar))
+                break;
+            stage(0);
             if (pw == 0) {
                 // prefix sums of g * log2(e) in double
                 double a = (double)gv0 * kLog2eD, b = (double)gv1 * kLog2eD;
@@ -567,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
         const uint64_t dKQHm = tc::smem_desc(base + kOffKQH, 16384, 1024);     // K' as MN-major operand
         const uint64_t dKQLm = tc::smem_desc(base + kOffKQL, 16384, 1024);
         const uint64_t dVm = tc::smem_desc(base + kOffV, 8192, 1024);          // V' (MN-major); lo at +16 KB
-        const uint64_t dVk = tc::smem_desc(base + kOffV, 16, 1024);            // Delta''^T (K-major)
+        const uint64_t dVk = tc::smem_desc(base + kOffW, 16, 1024);            // Delta''^T (K-major)
         const uint64_t dB = tc::smem_desc(base + kOffB, 16, 1024);             // BV, BK; later Delta^T
         const uint64_t dWm = tc::smem_desc(base + kOffW, 8192, 1024);          // W' (MN-major)
         const uint64_t dM = tc::smem_desc(base + kOffM, 16, 1024);
@@ -680,13 +699,6 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
 
         for (int n = 0; n < nchunks && ok; n++) {
             const ChunkConst &C = cc[n & 1];
-            // ---- outputs + state update of the previous chunk (overlaps the producers staging
-            //      this chunk's inputs)
-            if (n > 0 && !finish(n - 1, false)) {
-                ok = false;
-                break;
-            }
-            named_bar_sync(1, 128);
             // ---- inputs of chunk n staged
             {
                 const bool w = mbar_wait_sleep(in_full, (uint32_t)n & 1u, 64);
@@ -713,6 +725,39 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tc::commit(mma_bar);
                 tc::commit(a_bar);
             }
+            // ---- state update of the previous chunk and S_0 of this one, while (a) runs and the
+            //      producers form the T block
+            if (n > 0 && !finish(n - 1, false)) {
+                ok = false;
+                break;
+            }
+            // ---- (d1) S_0^T Q'^T (A = S_0^T from TMEM) as soon as S_0 is split and the producers
+            //      have read chunk n - 1's outputs from its columns
+            {
+                bool ob = true;
+                if (n > 0 && tid == 0)
+                    ob = mbar_wait_sleep(out_bar, (uint32_t)(n - 1) & 1u, 64);
+                if (!bar_all(1, 128, ob && !*abort_flag)) {
+                    if (tid == 0)
+                        set_abort();
+                    ok = false;
+                    break;
+                }
+            }
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
+#pragma unroll
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint32_t Aa = tb + kColS0 + (pp == 2 ? 64u : 0u);
+                    const uint64_t Qb = tc::desc_adv(pp == 1 ? dKQL : dKQH, 8192u);
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++)
+                        tc::mma_ts_f16(tb + kColD1, Aa + kk * 8u,
+                                       tc::desc_adv(Qb, (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u), idd,
+                                       (pp | kk) ? 1u : 0u);
+                }
+            }
             if (!wait_mma()) {
                 ok = false;
                 break;
@@ -732,15 +777,11 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 cs->imu[n & 1][i] = pow2_inv(mu);
                 fence_proxy_async();
             }
-            // the producers have stored the B operands of (b) and read chunk n - 1's outputs from the
-            // columns (b) and (d1) overwrite
+            // the producers have stored the B operands of (b)
             {
                 bool ob = true;
-                if (tid == 0) {
+                if (tid == 0)
                     ob = mbar_wait_sleep(t_bar, (uint32_t)n & 1u, 64);
-                    if (n > 0)
-                        ob = ob && mbar_wait_sleep(out_bar, (uint32_t)(n - 1) & 1u, 64);
-                }
                 if (!bar_all(1, 128, ob && !*abort_flag)) {
                     if (tid == 0)
                         set_abort();
@@ -754,18 +795,24 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 const uint32_t id = tc::idesc_f16(128, 64, 1, 0);
 #pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
-                    const uint64_t Va = tc::desc_adv(dVm, pp == 2 ? 16384u : 0u);
                     const uint64_t Ka = pp == 2 ? dKQLm : dKQHm;
-                    const uint64_t Bv = tc::desc_adv(dB, pp == 1 ? 8192u : 0u);
                     const uint64_t Bk = tc::desc_adv(dB, pp == 1 ? 24576u : 16384u);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        const uint32_t acc = (pp | kk) ? 1u : 0u;
-                        tc::mma_ss_f16(tb + kColU, tc::desc_adv(Va, kk * 2048u), tc::desc_adv(Bv, kk * 32u), id, acc);
-                        tc::mma_ss_f16(tb + kColW, tc::desc_adv(Ka, kk * 2048u), tc::desc_adv(Bk, kk * 32u), id, acc);
-                    }
+                    for (int kk = 0; kk < 4; kk++)
+                        tc::mma_ss_f16(tb + kColW, tc::desc_adv(Ka, kk * 2048u), tc::desc_adv(Bk, kk * 32u), id,
+                                       (pp | kk) ? 1u : 0u);
                 }
-                tc::commit(mma_bar);
+                tc::commit(mma_bar);             // W^T first: its split overlaps the U^T products
+#pragma unroll
+                for (int pp = 0; pp < 3; pp++) {
+                    const uint64_t Va = tc::desc_adv(dVm, pp == 2 ? 16384u : 0u);
+                    const uint64_t Bv = tc::desc_adv(dB, pp == 1 ? 8192u : 0u);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        tc::mma_ss_f16(tb + kColU, tc::desc_adv(Va, kk * 2048u), tc::desc_adv(Bv, kk * 32u), id,
+                                       (pp | kk) ? 1u : 0u);
+                }
+                tc::commit(b_bar);
             }
             if (!wait_mma()) {
                 ok = false;
@@ -786,25 +833,20 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 tc::fence_before_sync();
             }
             named_bar_sync(1, 128);
-            // ---- (c) S_0^T W'  and  (d1) S_0^T Q'^T, A = S_0^T from TMEM
+            // ---- (c) S_0^T W', A = S_0^T from TMEM (its commit also covers (d1) and the U^T half of (b))
             if (tid == 0) {
                 tc::fence_after_sync();
                 const uint32_t idc = tc::idesc_f16(128, 64, 0, 1);
-                const uint32_t idd = tc::idesc_f16(128, 64, 0, 0);
 #pragma unroll
                 for (int pp = 0; pp < 3; pp++) {
                     const uint32_t Aa = tb + kColS0 + (pp == 2 ? 64u : 0u);
                     const uint64_t Wb = tc::desc_adv(dWm, pp == 1 ? 16384u : 0u);
-                    const uint64_t Qb = tc::desc_adv(pp == 1 ? dKQL : dKQH, 8192u);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t acc = (pp | kk) ? 1u : 0u;
-                        tc::mma_ts_f16(tb + kColA, Aa + kk * 8u, tc::desc_adv(Wb, kk * 2048u), idc, acc);
-                        tc::mma_ts_f16(tb + kColD1, Aa + kk * 8u,
-                                       tc::desc_adv(Qb, (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u), idd, acc);
-                    }
+                    for (int kk = 0; kk < 8; kk++)
+                        tc::mma_ts_f16(tb + kColA, Aa + kk * 8u, tc::desc_adv(Wb, kk * 2048u), idc, (pp | kk) ? 1u : 0u);
                 }
                 tc::commit(mma_bar);
+                tc::commit(cd_bar);
             }
             if (!wait_mma()) {
                 ok = false;
@@ -831,7 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                     dl[j] *= C.df[j];
                 const float rho2 = pow2_scale(row_amax(dl));
                 inv_rho2 = pow2_inv(rho2);
-                store_row_split(base + kOffV, base + kOffV + 16384, r, dl, rho2);
+                store_row_split(base + kOffW, base + kOffW + 16384, r, dl, rho2);
                 fence_proxy_async();
                 tc::fence_before_sync();
             }
