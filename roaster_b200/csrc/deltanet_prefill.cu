@@ -74,7 +74,7 @@ constexpr uint32_t kColD1 = 448;       // (d1)
 constexpr uint32_t kOffKQH = 0;        // [K c0 | Q c0 | K c1 | Q c1] hi, 4 x 8 KB
 constexpr uint32_t kOffKQL = 32768;    // same, lo
 constexpr uint32_t kOffV = 65536;      // V hi [c0|c1] 16 KB, V lo 16 KB
-constexpr uint32_t kOffB = 98304;      // BV hi, BV lo, BK hi, BK lo (8 KB each); L + X scratch;
+constexpr uint32_t kOffB = 98304;      // BV hi, BV lo, BK hi, BK lo (8 KB each);
                                        // later Delta^T hi|lo
 constexpr uint32_t kOffW = 131072;     // T (fp32 scratch), then W' hi|lo, then Delta''^T hi|lo
 constexpr uint32_t kOffM = 163840;     // M hi, M lo (8 KB each)
@@ -101,7 +101,11 @@ struct ConsScratch {
     float red[4];
 };
 constexpr uint32_t kOffBars = kOffCons + ((sizeof(ConsScratch) + 15) / 16) * 16;
-constexpr size_t kSmemBytes = kOffBars + 128 + 1024;
+constexpr uint32_t kOffL = 188416;     // L, then L' (fp32, row stride kLd) while T is formed
+constexpr uint32_t kOffE = kOffL + 64 * kLd * 4;   // decay factors 2^(G_i - G_j), j <= i (fp32, stride kLd)
+constexpr size_t kSmemBytes = kOffE + 64 * kLd * 4 + 1024;
+static_assert(kOffBars + 128 <= kOffL, "barriers overlap L");
+static_assert(kSmemBytes <= 232448, "shared memory exceeds a CTA's");
 
 struct DJob {
     float *state;
@@ -214,12 +218,11 @@ __device__ __forceinline__ void fma4(float4 &a, float s, const float4 &t)
     a.w = fmaf(s, t.w, a.w);
 }
 
-template <int D, int BAR>
+template <int D>
 __device__ __forceinline__ void inv_level(const float *Lp, float *Tm, int q)
 {
-    constexpr int NB = 4 - D;                        // blocks at distance D
     const int k = q >> 6, rr = (q >> 2) & 15, c4 = 4 * (q & 3);
-    if (k < NB) {
+    {
         const float *lrow = Lp + (16 * (k + D) + rr) * kLd + 16 * k;
         const float *tcol = Tm + 16 * k * kLd + 16 * k + c4;
         float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
@@ -231,11 +234,69 @@ __device__ __forceinline__ void inv_level(const float *Lp, float *Tm, int q)
         *reinterpret_cast<float4 *>(Tm + (16 * (k + D) + rr) * kLd + 16 * k + c4) =
             make_float4(-(a0.x + a1.x), -(a0.y + a1.y), -(a0.z + a1.z), -(a0.w + a1.w));
     }
-    named_bar_sync(BAR, 256);
+}
+
+// NU 16-byte units (8 values each, times s) of row r of a K-major swizzled tile pair (hi, lo),
+// starting at unit u0.
+template <int NU>
+__device__ __forceinline__ void store_units(uint32_t hi, uint32_t lo, int r, int u0, const float (&x)[8 * NU], float s)
+{
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+            split2(x[8 * u + 2 * p] * s, x[8 * u + 2 * p + 1] * s, hw[p], lw[p]);
+        const uint32_t off = (uint32_t)r * 128u + ((((uint32_t)(u0 + u)) ^ (uint32_t)(r & 7)) << 4);
+        sts128(hi + off, hw[0], hw[1], hw[2], hw[3]);
+        sts128(lo + off, lw[0], lw[1], lw[2], lw[3]);
+    }
+}
+
+// B operands of (b) for the 16 rows of block rb: rows of T diag(beta / s^v) (BV, tasks 0-15) and
+// T diag(beta gamma / s^k) (BK, tasks 16-31), each split hi + lo with its own power-of-two scale;
+// G threads (adjacent lanes, t = G task + h) per row, 64 / G columns each.
+template <int G>
+__device__ __forceinline__ void b_rows(const float *Tm, const ChunkConst &C, ConsScratch *cs, uint32_t bbase, int rb,
+                                       int t)
+{
+    constexpr int NV = 64 / G;
+    const int task = t / G, h = t % G, i = 16 * rb + (task & 15);
+    const bool isv = task < 16;
+    const float *bsrc = isv ? C.bv : C.bk;
+    float x[NV];
+#pragma unroll
+    for (int j4 = 0; j4 < NV; j4 += 4) {
+        const int j = NV * h + j4;
+        const float4 t4 = *reinterpret_cast<const float4 *>(Tm + i * kLd + j);
+        const float4 b4 = *reinterpret_cast<const float4 *>(bsrc + j);
+        x[j4] = j <= i ? t4.x * b4.x : 0.f;
+        x[j4 + 1] = j + 1 <= i ? t4.y * b4.y : 0.f;
+        x[j4 + 2] = j + 2 <= i ? t4.z * b4.z : 0.f;
+        x[j4 + 3] = j + 3 <= i ? t4.w * b4.w : 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < NV; jj++)
+        m = fmaxf(m, fabsf(x[jj]));
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float u = pow2_scale(m);
+    const uint32_t hi = bbase + (isv ? 0u : 16384u);
+    store_units<NV / 8>(hi, hi + 8192, i, (NV / 8) * h, x, u);
+    if (h == 0) {
+        if (isv)
+            cs->iu_v[i] = pow2_inv(u);
+        else
+            cs->iu_k[i] = pow2_inv(u);
+    }
+    fence_proxy_async();
 }
 
 template <int BAR>
-__device__ __forceinline__ void tri_inverse(float *Lw, float *Tm, int q)
+__device__ __forceinline__ void tri_inverse(float *Lw, float *Tm, int q, const ChunkConst &C, ConsScratch *cs,
+                                            uint32_t bbase)
 {
     if (q < 160) {
         int i, c;                                    // block row, column within [0, 16 i + 16)
@@ -266,24 +327,17 @@ __device__ __forceinline__ void tri_inverse(float *Lw, float *Tm, int q)
             dst[(16 * i + rr) * kLd + c] = y[rr];
     }
     named_bar_sync(BAR, 256);
-    inv_level<1, BAR>(Lw, Tm, q);
-    inv_level<2, BAR>(Lw, Tm, q);
-    inv_level<3, BAR>(Lw, Tm, q);
-}
-
-// Half (32 values, times s) of row r of a K-major swizzled tile pair (hi, lo): units 4h .. 4h+3.
-__device__ __forceinline__ void store_half_split(uint32_t hi, uint32_t lo, int r, int h, const float (&x)[32], float s)
-{
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int p = 0; p < 4; p++)
-            split2(x[8 * u + 2 * p] * s, x[8 * u + 2 * p + 1] * s, hw[p], lw[p]);
-        const uint32_t off = (uint32_t)r * 128u + ((((uint32_t)(4 * h + u)) ^ (uint32_t)(r & 7)) << 4);
-        sts128(hi + off, hw[0], hw[1], hw[2], hw[3]);
-        sts128(lo + off, lw[0], lw[1], lw[2], lw[3]);
-    }
+    if (q < 192)
+        inv_level<1>(Lw, Tm, q);
+    named_bar_sync(BAR, 256);
+    if (q < 128)
+        inv_level<2>(Lw, Tm, q);
+    named_bar_sync(BAR, 256);
+    if (q < 64)
+        inv_level<3>(Lw, Tm, q);
+    named_bar_sync(BAR, 256);
+    // the B operands of (b): 64 threads per 16-row block, two per row
+    b_rows<2>(Tm, C, cs, bbase, q >> 6, q & 63);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __grid_constant__ DPParams p)
@@ -421,13 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
             };
             if (!gate(b_bar))
                 break;
-            stage(16);
-            if (!gate(cd_bar))
-                break;
-            stage(8);
-            if (!gate(done_bar))
-                break;
-            stage(0);
+            // g prefix sums (pw == 0) and, after the V rows, the chunk's decay factors E (the
+            // arithmetic warps finished reading chunk n - 1's E, in M, before they issued its (b))
             if (pw == 0) {
                 // prefix sums of g * log2(e) in double
                 double a = (double)gv0 * kLog2eD, b = (double)gv1 * kLog2eD;
@@ -453,6 +502,23 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 if (lane == 0)
                     C.gC = ex2((float)gl_last);
             }
+            stage(16);
+            named_bar_sync(3, kProdThreads);
+            {
+                float *Ew = reinterpret_cast<float *>(gbase + kOffE);
+                const int pq = tid - (kThreads - kProdThreads);
+#pragma unroll 4
+                for (int e = pq; e < kC * kC; e += kProdThreads) {
+                    const int i = e >> 6, j = e & 63;
+                    Ew[i * kLd + j] = j <= i ? ex2(C.glf[i] - C.glf[j]) : 0.f;
+                }
+            }
+            if (!gate(cd_bar))
+                break;
+            stage(8);
+            if (!gate(done_bar))
+                break;
+            stage(0);
             named_bar_sync(3, kProdThreads);
             if (pw == 0) {
                 // per-token factors that need every row scale
@@ -508,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 }
                 tc::fence_after_sync();
                 const int pq = tid - (kThreads - kProdThreads);   // 0..255
-                float *Lw = reinterpret_cast<float *>(gbase + kOffB);
+                float *Lw = reinterpret_cast<float *>(gbase + kOffL);
+                const float *Ew = reinterpret_cast<const float *>(gbase + kOffE);
                 float *Tm = reinterpret_cast<float *>(gbase + kOffW);
                 const int q4 = warp & 3, half = pw >> 2;
                 if (q4 < 2) {
@@ -517,57 +584,23 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                     float x[32];
                     tc::tmem_ld32(tb + ((uint32_t)(32 * q4) << 16) + kColA + 32 * half, x);
                     tc::tmem_wait_ld();
-                    const float gi = C.glf[i];
                     const float f = C.beta[i] * C.isk[i];
 #pragma unroll
                     for (int j4 = 0; j4 < 32; j4 += 4) {
                         const int j = 32 * half + j4;
-                        const float4 g4 = *reinterpret_cast<const float4 *>(&C.glf[j]);
+                        const float4 e4 = *reinterpret_cast<const float4 *>(Ew + i * kLd + j);
                         const float4 s4 = *reinterpret_cast<const float4 *>(&C.isk[j]);
                         float4 l;
-                        l.x = j < i ? f * ex2(gi - g4.x) * x[j4] * s4.x : 0.f;
-                        l.y = j + 1 < i ? f * ex2(gi - g4.y) * x[j4 + 1] * s4.y : 0.f;
-                        l.z = j + 2 < i ? f * ex2(gi - g4.z) * x[j4 + 2] * s4.z : 0.f;
-                        l.w = j + 3 < i ? f * ex2(gi - g4.w) * x[j4 + 3] * s4.w : 0.f;
+                        l.x = j < i ? f * e4.x * x[j4] * s4.x : 0.f;
+                        l.y = j + 1 < i ? f * e4.y * x[j4 + 1] * s4.y : 0.f;
+                        l.z = j + 2 < i ? f * e4.z * x[j4 + 2] * s4.z : 0.f;
+                        l.w = j + 3 < i ? f * e4.w * x[j4 + 3] * s4.w : 0.f;
                         *reinterpret_cast<float4 *>(Lw + i * kLd + j) = l;
                     }
                 }
                 tc::fence_before_sync();
                 named_bar_sync(3, kProdThreads);
-                tri_inverse<3>(Lw, Tm, pq);
-                {
-                    // B operands of (b): rows of T diag(beta / s^v) (tasks 0-63) and
-                    // T diag(beta gamma / s^k) (tasks 64-127), two threads (adjacent lanes) per row
-                    const int task = pq >> 1, h = pq & 1, i = task & 63;
-                    const bool isv = task < kC;
-                    float x[32];
-                    const float *bsrc = isv ? C.bv : C.bk;
-#pragma unroll
-                    for (int j4 = 0; j4 < 32; j4 += 4) {
-                        const int j = 32 * h + j4;
-                        const float4 t4 = *reinterpret_cast<const float4 *>(Tm + i * kLd + j);
-                        const float4 b4 = *reinterpret_cast<const float4 *>(bsrc + j);
-                        x[j4] = j <= i ? t4.x * b4.x : 0.f;
-                        x[j4 + 1] = j + 1 <= i ? t4.y * b4.y : 0.f;
-                        x[j4 + 2] = j + 2 <= i ? t4.z * b4.z : 0.f;
-                        x[j4 + 3] = j + 3 <= i ? t4.w * b4.w : 0.f;
-                    }
-                    float m = 0.f;
-#pragma unroll
-                    for (int jj = 0; jj < 32; jj++)
-                        m = fmaxf(m, fabsf(x[jj]));
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-                    const float u = pow2_scale(m);
-                    const uint32_t hi = base + kOffB + (isv ? 0u : 16384u);
-                    store_half_split(hi, hi + 8192, i, h, x, u);
-                    if (h == 0) {
-                        if (isv)
-                            cs->iu_v[i] = pow2_inv(u);
-                        else
-                            cs->iu_k[i] = pow2_inv(u);
-                    }
-                    fence_proxy_async();
-                }
+                tri_inverse<3>(Lw, Tm, pq, C, cs, base + kOffB);
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive(t_bar);
@@ -767,11 +800,17 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_prefill_kernel(const __g
                 float x[kC];
                 tmem_ld64(tb + lrow + kColA, x);
                 const int i = r - kC;
-                const float gi = C.glf[i];
                 const float f = C.isq[i];
+                const float *Er = reinterpret_cast<const float *>(gbase + kOffE) + i * kLd;
 #pragma unroll
-                for (int j = 0; j < kC; j++)
-                    x[j] = j <= i ? f * ex2(gi - C.glf[j]) * x[j] * C.isk[j] : 0.f;
+                for (int j4 = 0; j4 < kC; j4 += 4) {
+                    const float4 e4 = *reinterpret_cast<const float4 *>(Er + j4);
+                    const float4 s4 = *reinterpret_cast<const float4 *>(&C.isk[j4]);
+                    x[j4] = j4 <= i ? f * e4.x * x[j4] * s4.x : 0.f;
+                    x[j4 + 1] = j4 + 1 <= i ? f * e4.y * x[j4 + 1] * s4.y : 0.f;
+                    x[j4 + 2] = j4 + 2 <= i ? f * e4.z * x[j4 + 2] * s4.z : 0.f;
+                    x[j4 + 3] = j4 + 3 <= i ? f * e4.w * x[j4 + 3] * s4.w : 0.f;
+                }
                 const float mu = pow2_scale(row_amax(x));
                 store_row_split(base + kOffM, base + kOffM + 8192, i, x, mu);
                 cs->imu[n & 1][i] = pow2_inv(mu);
