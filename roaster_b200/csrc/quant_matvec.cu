@@ -46,6 +46,7 @@
 // and each token's activation split hi + lo in B; described where the kernel is defined.
 #include "ptx.cuh"
 #include "runtime.h"
+#include "tcgen05.cuh"
 #include "../../include/roaster_cuda.h"
 
 #include <cuda_fp16.h>
@@ -1147,6 +1148,597 @@ __global__ void __launch_bounds__(256) quant_mm_reduce_kernel(const __grid_const
     }
 }
 
+// ---------------------------------------------------------------- multi-token kernel on tcgen05
+//
+// Y[t] = W X[t] for 64 or more tokens on the 5th-generation tensor cores. A CTA computes 128 rows
+// x 64 tokens: D (128 x 128 fp32 in tensor memory) = A (128 rows x K, f16) B^T, B = the 64
+// tokens' activations scaled by 2^e_t and split f16 hi (B rows 0-63) + lo (rows 64-127), one
+// accumulator per 256-weight block (two in turn), so the block's d -- and the Q4_K min term --
+// apply when the block is read back.
+//  * 8 decode warps build A a quarter block (64 weights) at a time straight into tensor memory
+//    (one row per TMEM lane, f16 pairs; A never touches shared memory, whose bandwidth the B
+//    tiles need), with the scales folded in exactly: Q4_K sc q 2^-24; Q6_K two tiles (q - 32) 2s'
+//    2^-24 and (q - 32) r 2^-24 (sc = 2s' + r). They also write each row's (d, dmin) and, for
+//    Q4_K, an A operand of the mins m_j (f16 integers, K = 16).
+//  * One warp issues the copies: the raw blocks of the 128 rows (tensor-map box), B quarter
+//    tiles and the Q4_K sub-block sums (bulk copies of images quant_mm_tc_prep_kernel made).
+//  * One thread issues the MMAs (M = N = 128, K = 16, A from tensor memory): 4 per quarter block
+//    (Q6_K 8), and for Q4_K one more per block into a second accumulator, mins against the
+//    sub-block sums (shared memory).
+//  * 8 epilogue warps (two per TMEM lane quarter, 32 tokens each) keep
+//    y += d (hi + lo) - dmin (min hi + min lo) in registers; 2^-e_t at the end.
+// Every hand-off between the roles is an mbarrier with a bounded wait.
+
+namespace tcm {
+constexpr int kRows = 128, kTok = 64;
+constexpr int kThreads = 576;           // 18 warps: copies, MMA, 8 epilogue, 8 decode
+constexpr int kTile = 16384;            // 128 rows x 64 K f16, swizzled
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColMain = 0, kColMin = 256;   // accumulators: main 0 / 128 (by block parity), min 256
+constexpr uint32_t kColA = 384;                   // A ring: Q4_K 3 x 32 columns; Q6_K (no min) 2 x 64 at 256
+// barrier slots (A ring up to 4 stages, B ring up to 8, 3 raw buffers)
+constexpr int kAFull = 0, kAEmpty = 4, kBFull = 8, kBEmpty = 16, kRawFull = 24, kRawEmpty = 27, kMnFullA = 30,
+              kMnFullB = 32, kMnEmpty = 34, kAccFull = 36, kAccEmpty = 38, kSclFull = 40, kSclEmpty = 42, kDrain = 44,
+              kSlot = 45;
+}  // namespace tcm
+
+template <bool Q6>
+struct TcCfg {
+    static constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
+    static constexpr int kStA = Q6 ? 2 : 3;                 // A ring (decoded quarters, in tensor memory)
+    static constexpr uint32_t kColA = Q6 ? 256u : tcm::kColA;
+    static constexpr uint32_t kAcols = Q6 ? 64u : 32u;      // TMEM columns of a decoded quarter
+    static constexpr int kStB = 8;                          // B ring (copied quarters: covers the copy latency)
+    static constexpr int kOffB = 0;
+    static constexpr int kRawN = 2;                         // raw block buffers
+    static constexpr int kRaw = 128 * kSlot;
+    static constexpr int kOffRaw = kOffB + kStB * tcm::kTile;
+    static constexpr int kOffMin = kOffRaw + kRawN * kRaw;
+    static constexpr int kMin = Q6 ? 0 : 8192;              // A of the mins 4 KB + sums tile 4 KB
+    static constexpr int kOffScl = kOffMin + 2 * kMin;
+    static constexpr int kOffBar = kOffScl + 2 * 128 * 8;
+    static constexpr int kSmem = kOffBar + 512 + 1024;
+    static_assert(kRaw % 1024 == 0, "tile alignment");
+    static_assert(kColA + kStA * kAcols <= tcm::kTmemCols, "tensor memory");
+    static_assert(kStA <= 4 && kStB <= 8 && kRawN <= 3, "barrier slots");
+    static_assert(kSmem <= 232448, "shared memory");
+};
+
+struct TJob {
+    const CUtensorMap *map;     // the matrix, boxes of slot x 128 rows
+    const uint4 *bq;            // B quarter tiles [token tile][quarter][16 KB]
+    const uint4 *bsum;          // Q4_K sums tiles [token tile][block][4 KB]
+    const int *e;               // per token: activation scale exponent
+    float *y;                   // [T][rows]
+    long long item0;
+    int rows, nb, T, rtiles, ctiles;
+};
+
+struct TParams {
+    TJob jobs[kMaxJobs];
+    int njobs;
+    long long items;
+    unsigned *err;
+};
+
+// The activations of a call for the tensor-core kernel: each distinct X with its images.
+struct PJobTc {
+    const float *X;
+    uint4 *bq, *bsum;
+    int *e;
+    int T, cols, cta0;
+};
+
+struct PParamsTc {
+    PJobTc jobs[kMaxJobs];
+    int njobs;
+};
+
+__device__ __forceinline__ void sts128u(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+// (byte k0, byte k1) of w as an f16 pair of small integers (the byte under the exponent of 1024,
+// less 1024).
+__device__ __forceinline__ uint32_t f16pair_bytes(uint32_t w, uint32_t k0, uint32_t k1)
+{
+    return hsub2u(__byte_perm(w, 0x64646464u, 0x4040u | (k1 << 8) | k0), 0x64006400u);
+}
+
+__device__ __forceinline__ uint32_t hi_lo_f16(float v, bool lo)
+{
+    const __half h = __float2half_rn(v);
+    return (uint32_t)__half_as_ushort(lo ? __float2half_rn(v - __half2float(h)) : h);
+}
+
+// Per padded token (one CTA each): its scale 2^e; its rows of the B quarter tiles (hi at row t,
+// lo at row 64 + t of its token tile, 128-byte swizzle); its rows of the Q4_K sums tiles
+// (sub-block sums x 2^(e-5), hi / lo, K = 16 with 8 zeros, core matrices of 8 rows x 16 bytes).
+__global__ void __launch_bounds__(256) quant_mm_tc_prep_kernel(const __grid_constant__ PParamsTc pp)
+{
+    __shared__ float red[8];
+    int jx = 0;
+    while (jx + 1 < pp.njobs && pp.jobs[jx + 1].cta0 <= (int)blockIdx.x)
+        jx++;
+    const PJobTc &P = pp.jobs[jx];
+    const int tok = blockIdx.x - P.cta0, T = P.T, cols = P.cols, nq = cols / 64, nb = cols / 256;
+    const bool real = tok < T;
+    const float *x = P.X + (size_t)(real ? tok : 0) * cols;
+    float mx = 0.f;
+    if (real)
+        for (int i = threadIdx.x; i < cols / 4; i += 256) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < 8; i++)
+        mx = fmaxf(mx, red[i]);
+    int E = 0;
+    if (mx > 0.f && mx < 3.0e38f)
+        frexpf(mx, &E);
+    const int e = max(-100, min(100, 14 - E));
+    const float scale = ldexpf(1.f, e);
+    if (threadIdx.x == 0 && real)
+        P.e[tok] = e;
+    const int ct = tok >> 6, tl = tok & 63;
+    for (int idx = threadIdx.x; idx < nq * 8; idx += 256) {
+        const int g = idx >> 3, u = idx & 7;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (real) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(x + 64 * g + 8 * u));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(x + 64 * g + 8 * u + 4));
+            v[0] = a.x * scale; v[1] = a.y * scale; v[2] = a.z * scale; v[3] = a.w * scale;
+            v[4] = b.x * scale; v[5] = b.y * scale; v[6] = b.z * scale; v[7] = b.w * scale;
+        }
+        uint4 *tile = P.bq + ((size_t)ct * nq + g) * (tcm::kTile / 16);
+        const int pos = u ^ (tl & 7);
+#pragma unroll
+        for (int lo = 0; lo < 2; lo++) {
+            uint4 w;
+            w.x = hi_lo_f16(v[0], lo) | (hi_lo_f16(v[1], lo) << 16);
+            w.y = hi_lo_f16(v[2], lo) | (hi_lo_f16(v[3], lo) << 16);
+            w.z = hi_lo_f16(v[4], lo) | (hi_lo_f16(v[5], lo) << 16);
+            w.w = hi_lo_f16(v[6], lo) | (hi_lo_f16(v[7], lo) << 16);
+            tile[(64 * lo + tl) * 8 + pos] = w;
+        }
+    }
+    if (P.bsum) {
+        const float sscale = scale * 0x1p-5f;        // the sums stay inside the f16 range
+        for (int b = threadIdx.x; b < nb; b += 256) {
+            float sv[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+                float acc = 0.f;
+                if (real) {
+                    const float4 *xp = reinterpret_cast<const float4 *>(x + 256 * b + 32 * jj);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        const float4 q = __ldg(xp + k);
+                        acc += (q.x + q.y) + (q.z + q.w);
+                    }
+                }
+                sv[jj] = acc * sscale;
+            }
+            uint4 *tile = P.bsum + ((size_t)ct * nb + b) * 256;
+#pragma unroll
+            for (int lo = 0; lo < 2; lo++) {
+                const int row = 64 * lo + tl;
+                uint4 w;
+                w.x = hi_lo_f16(sv[0], lo) | (hi_lo_f16(sv[1], lo) << 16);
+                w.y = hi_lo_f16(sv[2], lo) | (hi_lo_f16(sv[3], lo) << 16);
+                w.z = hi_lo_f16(sv[4], lo) | (hi_lo_f16(sv[5], lo) << 16);
+                w.w = hi_lo_f16(sv[6], lo) | (hi_lo_f16(sv[7], lo) << 16);
+                tile[(row >> 3) * 16 + (row & 7)] = w;                       // K 0-7
+                tile[(row >> 3) * 16 + 8 + (row & 7)] = make_uint4(0u, 0u, 0u, 0u);   // K 8-15
+            }
+        }
+    }
+}
+
+template <bool Q6>
+__global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __grid_constant__ TParams p)
+{
+    using Cfg = TcCfg<Q6>;
+    using namespace tcm;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    unsigned char *gb = smem_raw + (base - smem_addr(smem_raw));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int j = 0;
+    {
+        int lo = 0, hi = p.njobs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.jobs[mid].item0 <= (long long)blockIdx.x)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        j = lo;
+    }
+    const TJob &J = p.jobs[j];
+    const long long it = (long long)blockIdx.x - J.item0;
+    const int rt = (int)(it % J.rtiles), ct = (int)(it / J.rtiles);
+    const int nb = J.nb, nq = 4 * nb;
+    unsigned long long *bars = reinterpret_cast<unsigned long long *>(gb + Cfg::kOffBar);
+    auto BAR = [&](int i) -> uint32_t { return smem_addr(&bars[i]); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[kSlot]);
+    if (tid == 0) {
+        for (int s = 0; s < Cfg::kStA; s++) {
+            mbar_init(BAR(kAFull + s), 8);
+            mbar_init(BAR(kAEmpty + s), 1);
+        }
+        for (int s = 0; s < Cfg::kStB; s++) {
+            mbar_init(BAR(kBFull + s), 1);
+            mbar_init(BAR(kBEmpty + s), 1);
+        }
+        for (int r = 0; r < 3; r++) {
+            mbar_init(BAR(kRawFull + r), 1);
+            mbar_init(BAR(kRawEmpty + r), 8);
+        }
+        for (int x = 0; x < 2; x++) {
+            mbar_init(BAR(kMnFullA + x), 8);
+            mbar_init(BAR(kMnFullB + x), 1);
+            mbar_init(BAR(kMnEmpty + x), 1);
+            mbar_init(BAR(kAccFull + x), 1);
+            mbar_init(BAR(kAccEmpty + x), 8);
+            mbar_init(BAR(kSclFull + x), 8);
+            mbar_init(BAR(kSclEmpty + x), 8);
+        }
+        mbar_init(BAR(kDrain), 1);
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(smem_addr(tmem_slot), kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tb = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ============================================================ copies
+        // three independent streams, one lane each, so none waits behind another's buffer:
+        // lane 0 the B quarter tiles, lane 1 the raw blocks, lane 2 (Q4_K) the sums tiles
+        if (lane == 0) {
+            int nst[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int g = 0; g < nq; g++) {
+                const int s = g % Cfg::kStB;
+                if (g >= Cfg::kStB && !mbar_wait(BAR(kBEmpty + s), (uint32_t)(g / Cfg::kStB - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(BAR(kBFull + s), (uint32_t)kTile);
+                bulk_g2s(base + Cfg::kOffB + s * kTile, J.bq + ((size_t)ct * nq + g) * (kTile / 16), (uint32_t)kTile,
+                         BAR(kBFull + s));
+                nst[s]++;
+            }
+            if (!ok)
+                atomicOr(p.err, kErrWaitTimeout);
+            // every copy issued lands before the CTA ends (a wait on its buffer's last phase)
+            for (int s = 0; s < Cfg::kStB; s++)
+                if (nst[s])
+                    mbar_wait(BAR(kBFull + s), (uint32_t)(nst[s] - 1) & 1u, 20000000ll);
+        } else if (lane == 1) {
+            const int row0 = rt * kRows;
+            int nraw[3] = {0, 0, 0};
+            for (int b = 0; b < nb; b++) {
+                const int r = b % Cfg::kRawN;
+                if (b >= Cfg::kRawN && !mbar_wait(BAR(kRawEmpty + r), (uint32_t)(b / Cfg::kRawN - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(BAR(kRawFull + r), (uint32_t)Cfg::kRaw);
+                const int x = Q6 ? (210 * b) & ~15 : 144 * b;
+                tma_load_2d(base + Cfg::kOffRaw + r * Cfg::kRaw, J.map, x, row0, BAR(kRawFull + r));
+                nraw[r]++;
+            }
+            if (!ok)
+                atomicOr(p.err, kErrWaitTimeout);
+            for (int r = 0; r < Cfg::kRawN; r++)
+                if (nraw[r])
+                    mbar_wait(BAR(kRawFull + r), (uint32_t)(nraw[r] - 1) & 1u, 20000000ll);
+        } else if (lane == 2 && !Q6) {
+            int nsum[2] = {0, 0};
+            for (int b = 0; b < nb; b++) {
+                if (b >= 2 && !mbar_wait(BAR(kMnEmpty + (b & 1)), (uint32_t)((b >> 1) - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(BAR(kMnFullB + (b & 1)), 4096u);
+                bulk_g2s(base + Cfg::kOffMin + (b & 1) * Cfg::kMin + 4096, J.bsum + ((size_t)ct * nb + b) * 256, 4096u,
+                         BAR(kMnFullB + (b & 1)));
+                nsum[b & 1]++;
+            }
+            if (!ok)
+                atomicOr(p.err, kErrWaitTimeout);
+            for (int x = 0; x < 2; x++)
+                if (nsum[x])
+                    mbar_wait(BAR(kMnFullB + x), (uint32_t)(nsum[x] - 1) & 1u, 20000000ll);
+        }
+    } else if (warp == 1) {
+        // ============================================================ MMA issue
+        if (lane == 0) {
+            const uint32_t id = tc::idesc_f16(128, 128, 0, 0);
+            for (int b = 0; b < nb && ok; b++) {
+                const uint32_t dmain = tb + kColMain + (uint32_t)(b & 1) * 128u;
+                if (b >= 2 && !mbar_wait(BAR(kAccEmpty + (b & 1)), (uint32_t)((b >> 1) - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                for (int q = 0; q < 4; q++) {
+                    const int g = 4 * b + q, sa = g % Cfg::kStA, sb = g % Cfg::kStB;
+                    if (!mbar_wait(BAR(kAFull + sa), (uint32_t)(g / Cfg::kStA) & 1u) ||
+                        !mbar_wait(BAR(kBFull + sb), (uint32_t)(g / Cfg::kStB) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t ta = tb + Cfg::kColA + (uint32_t)sa * Cfg::kAcols;
+                    const uint64_t dB = tc::smem_desc(base + Cfg::kOffB + sb * kTile, 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        tc::mma_ts_f16(dmain, ta + 8u * kk, tc::desc_adv(dB, kk * 32u), id, (q | kk) ? 1u : 0u);
+                        if (Q6)
+                            tc::mma_ts_f16(dmain, ta + 32u + 8u * kk, tc::desc_adv(dB, kk * 32u), id, 1u);
+                    }
+                    tc::commit(BAR(kAEmpty + sa));
+                    tc::commit(BAR(kBEmpty + sb));
+                }
+                if (!ok)
+                    break;
+                if (!Q6) {
+                    // the min accumulator is single: the epilogue has read block b - 1's
+                    const uint32_t ph = (uint32_t)(b >> 1) & 1u;
+                    if (!mbar_wait(BAR(kMnFullA + (b & 1)), ph) || !mbar_wait(BAR(kMnFullB + (b & 1)), ph) ||
+                        (b >= 1 && !mbar_wait(BAR(kAccEmpty + ((b - 1) & 1)), (uint32_t)((b - 1) >> 1) & 1u))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t mb = base + Cfg::kOffMin + (uint32_t)(b & 1) * Cfg::kMin;
+                    tc::mma_ss_f16(tb + kColMin, tc::smem_desc_plain(mb, 128, 256), tc::smem_desc_plain(mb + 4096, 128, 256),
+                                   id, 0u);
+                    tc::commit(BAR(kMnEmpty + (b & 1)));
+                }
+                tc::commit(BAR(kAccFull + (b & 1)));
+            }
+            if (!ok)
+                atomicOr(p.err, kErrWaitTimeout);
+            // every MMA issued finishes before tensor memory is released
+            tc::commit(BAR(kDrain));
+            mbar_wait(BAR(kDrain), 0, 20000000ll);
+        }
+    } else if (warp < 10) {
+        // ============================================================ epilogue
+        const int qd = warp & 3, half = (warp - 2) >> 2;
+        const int r = 32 * qd + lane;
+        const uint32_t lq = (uint32_t)(32 * qd) << 16;
+        const float2 *scl = reinterpret_cast<const float2 *>(gb + Cfg::kOffScl);
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            acc[i] = 0.f;
+        for (int b = 0; b < nb && ok; b++) {
+            const uint32_t ph = (uint32_t)(b >> 1) & 1u;
+            if (!mbar_wait_sleep(BAR(kAccFull + (b & 1)), ph, 32) || !mbar_wait(BAR(kSclFull + (b & 1)), ph)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const float2 sd = scl[(b & 1) * 128 + r];           // (d 2^24, 32 dmin)
+            const uint32_t cm = tb + lq + kColMain + (uint32_t)(b & 1) * 128u + 32u * half;
+            const uint32_t cn = tb + lq + kColMin + 32u * half;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float h[8], l[8];
+                tc::tmem_ld8(cm + 8 * c, h);
+                tc::tmem_ld8(cm + 64 + 8 * c, l);
+                if (Q6) {
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        acc[8 * c + i] = fmaf(sd.x, h[i] + l[i], acc[8 * c + i]);
+                } else {
+                    float mh[8], ml[8];
+                    tc::tmem_ld8(cn + 8 * c, mh);
+                    tc::tmem_ld8(cn + 64 + 8 * c, ml);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        acc[8 * c + i] = fmaf(sd.x, h[i] + l[i], fmaf(-sd.y, mh[i] + ml[i], acc[8 * c + i]));
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(BAR(kAccEmpty + (b & 1)));
+                mbar_arrive(BAR(kSclEmpty + (b & 1)));
+            }
+        }
+        if (ok) {
+            const int row = rt * kRows + r;
+            if (row < J.rows) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int t = ct * kTok + 32 * half + i;
+                    if (t < J.T)
+                        J.y[(size_t)t * J.rows + row] = acc[i] * ldexpf(1.f, -J.e[t]);
+                }
+            }
+        } else if (lane == 0) {
+            atomicOr(p.err, kErrWaitTimeout);
+        }
+    } else {
+        // ============================================================ decode
+        const int dq = tid - 320;                             // 0..255
+        float2 *scl = reinterpret_cast<float2 *>(gb + Cfg::kOffScl);
+        for (int b = 0; b < nb && ok; b++) {
+            const int rr = b % Cfg::kRawN;
+            if (!mbar_wait(BAR(kRawFull + rr), (uint32_t)(b / Cfg::kRawN) & 1u)) {
+                ok = false;
+                break;
+            }
+            const unsigned char *raw = gb + Cfg::kOffRaw + rr * Cfg::kRaw;
+            const int mis = Q6 ? (210 * b) & 15 : 0;
+            // per-row tables of the block
+            if (b >= 2) {
+                const uint32_t ph = (uint32_t)((b >> 1) - 1) & 1u;
+                if (!mbar_wait(BAR(kSclEmpty + (b & 1)), ph) || (!Q6 && !mbar_wait(BAR(kMnEmpty + (b & 1)), ph))) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (dq < kRows) {
+                const unsigned char *blk = raw + dq * Cfg::kSlot + mis;
+                if (Q6) {
+                    const float d = __half2float(*reinterpret_cast<const __half *>(blk + 208));
+                    scl[(b & 1) * 128 + dq] = make_float2(d * 0x1p24f, 0.f);
+                } else {
+                    const uint4 hd = lds128(blk);
+                    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
+                    scl[(b & 1) * 128 + dq] = make_float2(dd.x * 0x1p24f, dd.y * 32.f);
+                    // the row's mins m_0..m_7 (q4_k_get_scales) and 8 zeros, K = 16
+                    const uint32_t mnl = hd.z & 0x3F3F3F3Fu;
+                    const uint32_t mnh = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+                    const uint32_t am = base + Cfg::kOffMin + (uint32_t)(b & 1) * Cfg::kMin + (uint32_t)(dq >> 3) * 256u +
+                                        (uint32_t)(dq & 7) * 16u;
+                    sts128u(am, f16pair_bytes(mnl, 0, 1), f16pair_bytes(mnl, 2, 3), f16pair_bytes(mnh, 0, 1),
+                            f16pair_bytes(mnh, 2, 3));
+                    sts128u(am + 128u, 0u, 0u, 0u, 0u);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(BAR(kSclFull + (b & 1)));
+                if (!Q6)
+                    mbar_arrive(BAR(kMnFullA + (b & 1)));
+            }
+            // each thread: the row of its TMEM lane (warp quarter), units 4h .. 4h + 3 of every quarter
+            // block (h = which of the quarter's two decode warps), i.e. TMEM columns 16h .. 16h + 15
+            const int row = 32 * (warp & 3) + lane, h = (warp - 10) >> 2;
+            const unsigned char *rblk = raw + row * Cfg::kSlot + mis;
+            const uint32_t tl = tb + ((uint32_t)(32 * (warp & 3)) << 16) + 16u * (uint32_t)h;
+            uint32_t s4[4];                                   // Q4_K: the scale pair of each quarter
+            if (!Q6) {
+                const uint4 hd = lds128(rblk);
+                const uint32_t scl4 = hd.y & 0x3F3F3F3Fu, sch4 = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int jj = 2 * q + h;
+                    uint32_t s2 = f16pair_bytes(jj < 4 ? scl4 : sch4, (uint32_t)(jj & 3), (uint32_t)(jj & 3));
+                    s4[q] = h ? hmul2u(s2, 0x2C002C00u) : s2;   // sc / 16 for the high nibbles
+                }
+            }
+            for (int q = 0; q < 4; q++) {
+                const int g = 4 * b + q, s = g % Cfg::kStA;
+                if (g >= Cfg::kStA && !mbar_wait(BAR(kAEmpty + s), (uint32_t)(g / Cfg::kStA - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t ta = tl + Cfg::kColA + (uint32_t)s * Cfg::kAcols;
+                uint32_t w1[16], w2[16];
+                if (Q6) {
+                    const int n = q >> 1, qq = 2 * (q & 1) + h;
+                    // 32 bytes of ql (nibble qq / 2) and of qh (bits 2 qq), from a 2-byte-aligned start
+                    uint32_t L[8], Hh[8];
+                    {
+                        const unsigned char *a = rblk + 64 * n + 32 * (qq & 1);
+                        const unsigned char *al = reinterpret_cast<const unsigned char *>(reinterpret_cast<uintptr_t>(a) & ~(uintptr_t)3);
+                        const uint32_t sh = 8u * (uint32_t)(reinterpret_cast<uintptr_t>(a) & 3);
+                        uint32_t w[9];
+#pragma unroll
+                        for (int i = 0; i < 9; i++)
+                            w[i] = lds32(al + 4 * i);
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            L[i] = __funnelshift_r(w[i], w[i + 1], sh);
+                    }
+                    {
+                        const unsigned char *a = rblk + 128 + 32 * n;
+                        const unsigned char *al = reinterpret_cast<const unsigned char *>(reinterpret_cast<uintptr_t>(a) & ~(uintptr_t)3);
+                        const uint32_t sh = 8u * (uint32_t)(reinterpret_cast<uintptr_t>(a) & 3);
+                        uint32_t w[9];
+#pragma unroll
+                        for (int i = 0; i < 9; i++)
+                            w[i] = lds32(al + 4 * i);
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            Hh[i] = __funnelshift_r(w[i], w[i + 1], sh);
+                    }
+                    const int ls = 4 * (qq >> 1), hs = 2 * qq;
+                    const int scA = *reinterpret_cast<const signed char *>(rblk + 192 + 8 * n + 2 * qq);
+                    const int scB = *reinterpret_cast<const signed char *>(rblk + 192 + 8 * n + 2 * qq + 1);
+                    const uint32_t off32 = 0x00200020u;          // (32 2^-24, 32 2^-24)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int sc = k < 2 ? scA : scB;        // weights 8k .. 8k + 7: scale group k / 2
+                        const uint32_t e1 = __half_as_ushort(__short2half_rn((short)(sc & ~1)));
+                        const uint32_t s2 = e1 | (e1 << 16), r2 = (sc & 1) ? 0x3C003C00u : 0u;
+                        const uint32_t Qx = ((L[2 * k] >> ls) & 0x0F0F0F0Fu) | (((Hh[2 * k] >> hs) << 4) & 0x30303030u);
+                        const uint32_t Qy =
+                            ((L[2 * k + 1] >> ls) & 0x0F0F0F0Fu) | (((Hh[2 * k + 1] >> hs) << 4) & 0x30303030u);
+                        const uint32_t p0 = hsub2u(__byte_perm(Qx, 0u, 0x4140u) & 0x003F003Fu, off32);
+                        const uint32_t p1 = hsub2u(__byte_perm(Qx, 0u, 0x4342u) & 0x003F003Fu, off32);
+                        const uint32_t p2 = hsub2u(__byte_perm(Qy, 0u, 0x4140u) & 0x003F003Fu, off32);
+                        const uint32_t p3 = hsub2u(__byte_perm(Qy, 0u, 0x4342u) & 0x003F003Fu, off32);
+                        w1[4 * k] = hmul2u(p0, s2);
+                        w1[4 * k + 1] = hmul2u(p1, s2);
+                        w1[4 * k + 2] = hmul2u(p2, s2);
+                        w1[4 * k + 3] = hmul2u(p3, s2);
+                        w2[4 * k] = hmul2u(p0, r2);
+                        w2[4 * k + 1] = hmul2u(p1, r2);
+                        w2[4 * k + 2] = hmul2u(p2, r2);
+                        w2[4 * k + 3] = hmul2u(p3, r2);
+                    }
+                    tc::tmem_st16(ta, w1);
+                    tc::tmem_st16(ta + 32u, w2);
+                } else {
+                    const uint4 qa = lds128(rblk + 16 + 32 * q), qb = lds128(rblk + 32 + 32 * q);
+                    const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu, s2 = s4[q];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        w1[4 * k] = hmul2u(__byte_perm(W[2 * k], 0u, 0x4140u) & mask, s2);
+                        w1[4 * k + 1] = hmul2u(__byte_perm(W[2 * k], 0u, 0x4342u) & mask, s2);
+                        w1[4 * k + 2] = hmul2u(__byte_perm(W[2 * k + 1], 0u, 0x4140u) & mask, s2);
+                        w1[4 * k + 3] = hmul2u(__byte_perm(W[2 * k + 1], 0u, 0x4342u) & mask, s2);
+                    }
+                    tc::tmem_st16(ta, w1);
+                    (void)w2;
+                }
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(BAR(kAFull + s));
+            }
+            if (!ok)
+                break;
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(BAR(kRawEmpty + rr));
+        }
+        if (!ok && lane == 0)
+            atomicOr(p.err, kErrWaitTimeout);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 1)
+        tc::tmem_dealloc(tb, kTmemCols);
+}
+
 // ---------------------------------------------------------------- host
 
 // Tensor maps of the matrices, cached per device: weights stay resident between calls, so a
@@ -1156,15 +1748,18 @@ constexpr int kMapCap = 4096;
 struct MapKey {
     uintptr_t w;
     long long rows;
-    int rb, slot;
-    bool operator==(const MapKey &o) const { return w == o.w && rows == o.rows && rb == o.rb && slot == o.slot; }
+    int rb, slot, box;                   // box: rows per copy
+    bool operator==(const MapKey &o) const
+    {
+        return w == o.w && rows == o.rows && rb == o.rb && slot == o.slot && box == o.box;
+    }
 };
 
 struct MapKeyHash {
     size_t operator()(const MapKey &k) const
     {
         return std::hash<uintptr_t>()(k.w) ^ (std::hash<long long>()(k.rows) * 31u) ^ ((size_t)k.rb << 20) ^
-               (size_t)k.slot;
+               (size_t)k.slot ^ ((size_t)k.box << 12);
     }
 };
 
@@ -1177,7 +1772,7 @@ struct MapCache {
 
 MapCache g_maps[64];
 
-const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int slot)
+const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int slot, int box = 16)
 {
     Runtime &R = rt();
     if (R.device < 0 || R.device >= 64) {
@@ -1190,7 +1785,7 @@ const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int s
             return nullptr;
         mc.host.resize(kMapCap);
     }
-    const MapKey key{reinterpret_cast<uintptr_t>(w), rows, rb, slot};
+    const MapKey key{reinterpret_cast<uintptr_t>(w), rows, rb, slot, box};
     const auto it = mc.idx.find(key);
     if (it != mc.idx.end())
         return mc.dev + it->second;
@@ -1202,7 +1797,7 @@ const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int s
         mc.used = 0;
     }
     const int i = mc.used;
-    if (encode_tmap_u8_2d(&mc.host[i], w, (uint64_t)rb, (uint64_t)rows, (uint64_t)rb, (uint32_t)slot, 16) != 0)
+    if (encode_tmap_u8_2d(&mc.host[i], w, (uint64_t)rb, (uint64_t)rows, (uint64_t)rb, (uint32_t)slot, (uint32_t)box) != 0)
         return nullptr;
     if (check(cudaMemcpyAsync(mc.dev + i, &mc.host[i], sizeof(CUtensorMap), cudaMemcpyHostToDevice, R.stream),
               "upload matvec tensor map") != 0)
@@ -1485,6 +2080,111 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
     return launched("quant_mm_reduce_kernel");
 }
 
+
+// Jobs of 64 or more tokens on a 16-byte-aligned matrix whose rows are a multiple of 16 bytes
+// (and 16-byte-aligned X): the tensor-core kernel, one launch per format after one prep launch for
+// every distinct X. The others go to `others`.
+int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others)
+{
+    static bool attr[2] = {false, false};
+    Runtime &R = rt();
+    TParams tp[2];
+    memset(static_cast<void *>(tp), 0, sizeof(tp));
+    struct XEnt {
+        const float *X;
+        size_t cols, T, off_bq, off_bsum, off_e;
+    };
+    std::vector<XEnt> xe;
+    std::vector<int> xidx[2];
+    for (int i = 0; i < n; i++) {
+        const KernelCudaMatmulJob &j = jobs[i];
+        const int nb = (int)(j.cols / 256);
+        const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
+        const bool tc = j.T >= 64 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && j.rows < (1u << 30) &&
+                        j.T < (1u << 30);
+        if (!tc) {
+            others.push_back(j);
+            continue;
+        }
+        int x = -1;
+        for (size_t q = 0; q < xe.size(); q++)
+            if (xe[q].X == j.X && xe[q].cols == j.cols && xe[q].T == j.T)
+                x = (int)q;
+        if (x < 0) {
+            xe.push_back(XEnt{j.X, j.cols, j.T, 0, 0, 0});
+            x = (int)xe.size() - 1;
+        }
+        const CUtensorMap *map = job_map(static_cast<const unsigned char *>(j.matrix), (long long)j.rows, (int)rb,
+                                         j.is_q6 ? kQ6Slot : kQ4Slot, tcm::kRows);
+        if (!map)
+            return -1;
+        TParams &P = tp[j.is_q6 ? 1 : 0];
+        const int rtiles = (int)((j.rows + tcm::kRows - 1) / tcm::kRows), ctiles = (int)((j.T + tcm::kTok - 1) / tcm::kTok);
+        P.jobs[P.njobs++] = TJob{map, nullptr, nullptr, nullptr, j.Y, P.items, (int)j.rows, nb, (int)j.T, rtiles, ctiles};
+        P.items += (long long)rtiles * ctiles;
+        xidx[j.is_q6 ? 1 : 0].push_back(x);
+    }
+    if (xe.empty())
+        return 0;
+    if (tp[0].items >= (1ll << 31) || tp[1].items >= (1ll << 31))
+        return fail("kernel_cuda_matmul_quant_batch: too many tiles in one call");
+    // scratch per distinct X: B quarter tiles [token tile][quarter][16 KB], sums tiles
+    // [token tile][block][4 KB], scale exponents [T]
+    size_t total = 0;
+    for (XEnt &e : xe) {
+        const size_t ct = (e.T + tcm::kTok - 1) / tcm::kTok;
+        e.off_bq = total;
+        total += ct * (e.cols / 64) * tcm::kTile;
+        e.off_bsum = total;
+        total += ct * (e.cols / 256) * 4096;
+        e.off_e = total;
+        total += (e.T * sizeof(int) + 255) / 256 * 256;
+    }
+    unsigned char *ws = static_cast<unsigned char *>(scratch(total));
+    if (!ws)
+        return -1;
+    PParamsTc pp;
+    memset(static_cast<void *>(&pp), 0, sizeof(pp));
+    long long ctas = 0;
+    for (const XEnt &e : xe) {
+        pp.jobs[pp.njobs++] = PJobTc{e.X, reinterpret_cast<uint4 *>(ws + e.off_bq), reinterpret_cast<uint4 *>(ws + e.off_bsum),
+                                     reinterpret_cast<int *>(ws + e.off_e), (int)e.T, (int)e.cols, (int)ctas};
+        ctas += (long long)((e.T + tcm::kTok - 1) / tcm::kTok * tcm::kTok);
+    }
+    if (ctas >= (1ll << 31))
+        return fail("kernel_cuda_matmul_quant_batch: too many tokens in one call");
+    quant_mm_tc_prep_kernel<<<(unsigned)ctas, 256, 0, R.stream>>>(pp);
+    if (launched("quant_mm_tc_prep_kernel") != 0)
+        return -1;
+    for (int k = 0; k < 2; k++) {
+        TParams &P = tp[k];
+        if (P.njobs == 0)
+            continue;
+        for (int q = 0; q < P.njobs; q++) {
+            const XEnt &e = xe[xidx[k][q]];
+            P.jobs[q].bq = reinterpret_cast<const uint4 *>(ws + e.off_bq);
+            P.jobs[q].bsum = reinterpret_cast<const uint4 *>(ws + e.off_bsum);
+            P.jobs[q].e = reinterpret_cast<const int *>(ws + e.off_e);
+        }
+        P.err = R.err_word;
+        const int smem = k ? TcCfg<true>::kSmem : TcCfg<false>::kSmem;
+        if (!attr[k]) {
+            const cudaError_t ce = k ? cudaFuncSetAttribute(quant_mm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+                                     : cudaFuncSetAttribute(quant_mm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (check(ce, "tensor-core matmul shared memory") != 0)
+                return -1;
+            attr[k] = true;
+        }
+        if (k)
+            quant_mm_tc_kernel<true><<<(unsigned)P.items, tcm::kThreads, smem, R.stream>>>(P);
+        else
+            quant_mm_tc_kernel<false><<<(unsigned)P.items, tcm::kThreads, smem, R.stream>>>(P);
+        if (launched("quant_mm_tc_kernel") != 0)
+            return -1;
+    }
+    return 0;
+}
+
 }  // namespace
 }  // namespace rb
 
@@ -1517,8 +2217,12 @@ extern "C" int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, i
                         "a multiple of 256)", i);
     }
     std::vector<KernelCudaMatvecJob> rest;
-    for (int i = 0; i < n; i += kMaxJobs)
-        if (matmul_chunk(jobs + i, std::min(kMaxJobs, n - i), rest) != 0)
+    for (int i = 0; i < n; i += kMaxJobs) {
+        std::vector<KernelCudaMatmulJob> small;
+        if (matmul_tc_chunk(jobs + i, std::min(kMaxJobs, n - i), small) != 0)
             return -1;
+        if (!small.empty() && matmul_chunk(small.data(), (int)small.size(), rest) != 0)
+            return -1;
+    }
     return rest.empty() ? 0 : kernel_cuda_matvec_quant_batch(rest.data(), (int)rest.size());
 }

@@ -25,6 +25,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return d;
 }
 
+// Shared-memory matrix descriptor without swizzle (K-major core matrices of 8 rows x 16 bytes):
+// lbo = byte distance between core matrices along K, sbo = along M / N.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;                        // descriptor version for sm_100
+    return d;                                      // layout 0: no swizzle
+}
+
 // The same descriptor moved `bytes` further (16-byte multiple; stays inside the shared window,
 // so the 14-bit address field cannot carry). Building a descriptor once per tile and advancing
 // it by compile-time offsets keeps the issuing thread's work per MMA to one add; rebuilding
@@ -141,6 +153,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
         : "r"(taddr));
 #pragma unroll
     for (int i = 0; i < 32; i++)
+        v[i] = __uint_as_float(r[i]);
+}
+
+// Each thread of the warp loads 8 consecutive fp32 columns of its lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8])
+{
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; i++)
         v[i] = __uint_as_float(r[i]);
 }
 
