@@ -345,10 +345,11 @@ int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, int n);
  * job validity as the reference (non-null pointers, rows, cols, T > 0, cols a multiple of 256,
  * each dimension at most 2^32 - 1; -1 otherwise) plus the alignment of
  * kernel_cuda_matvec_quant_batch (X 16-byte aligned). Device pointers, asynchronous. Jobs whose
- * matrix is 16-byte aligned with rows a multiple of 16 bytes run token-batched: 64 or more
- * tokens on the tcgen05 tensor cores (128 rows x 64 tokens per CTA), 8-63 tokens (at most 128
- * blocks a row) on the warp MMA (256 rows x 32 tokens per CTA, split along the blocks when there
- * are few tiles); the rest run as T matrix-vector products sharing the (L2-resident) weights.
+ * matrix is 16-byte aligned with rows a multiple of 16 bytes run token-batched: jobs of 64 or
+ * more tokens on the tcgen05 tensor cores (a CTA per tile of 128 rows x 64 tokens) when together
+ * they make at least 64 tiles, the other jobs of 8 or more tokens (at most 128 blocks a row) on
+ * the warp MMA (256 rows x 32 tokens per CTA, split along the blocks when there are few tiles);
+ * the rest run as T matrix-vector products sharing the (L2-resident) weights.
  * Results do not depend on the route beyond fp32 summation order, and repeat bit for bit. */
 typedef struct {
     int is_q6;                  /* 0 = Q4_K, 1 = Q6_K */

@@ -1200,6 +1200,7 @@ struct TcCfg {
     static constexpr int kSmem = kOffBar + 512 + 1024;
     static_assert(kRaw % 1024 == 0, "tile alignment");
     static_assert(kColA + kStA * kAcols <= tcm::kTmemCols, "tensor memory");
+    static_assert(kStA < kStB, "the A ring is released through the B ring's barriers");
     static_assert(kStA <= 4 && kStB <= 8 && kRawN <= 3, "barrier slots");
     static_assert(kSmem <= 232448, "shared memory");
 };
@@ -1371,10 +1372,8 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
     auto BAR = [&](int i) -> uint32_t { return smem_addr(&bars[i]); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[kSlot]);
     if (tid == 0) {
-        for (int s = 0; s < Cfg::kStA; s++) {
+        for (int s = 0; s < Cfg::kStA; s++)
             mbar_init(BAR(kAFull + s), 8);
-            mbar_init(BAR(kAEmpty + s), 1);
-        }
         for (int s = 0; s < Cfg::kStB; s++) {
             mbar_init(BAR(kBFull + s), 1);
             mbar_init(BAR(kBEmpty + s), 1);
@@ -1491,7 +1490,8 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                         if (Q6)
                             tc::mma_ts_f16(dmain, ta + 32u + 8u * kk, tc::desc_adv(dB, kk * 32u), id, 1u);
                     }
-                    tc::commit(BAR(kAEmpty + sa));
+                    // one commit per quarter frees both its B slot and (quarters complete in order)
+                    // its A slot: the decode warps wait on the B-slot barrier of quarter g - kStA
                     tc::commit(BAR(kBEmpty + sb));
                 }
                 if (!ok)
@@ -1641,8 +1641,8 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                 }
             }
             for (int q = 0; q < 4; q++) {
-                const int g = 4 * b + q, s = g % Cfg::kStA;
-                if (g >= Cfg::kStA && !mbar_wait(BAR(kAEmpty + s), (uint32_t)(g / Cfg::kStA - 1) & 1u)) {
+                const int g = 4 * b + q, s = g % Cfg::kStA, gp = g - Cfg::kStA;   // gp: the slot's previous quarter
+                if (g >= Cfg::kStA && !mbar_wait(BAR(kBEmpty + gp % Cfg::kStB), (uint32_t)(gp / Cfg::kStB) & 1u)) {
                     ok = false;
                     break;
                 }
@@ -2081,9 +2081,11 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
 }
 
 
-// Jobs of 64 or more tokens on a 16-byte-aligned matrix whose rows are a multiple of 16 bytes
-// (and 16-byte-aligned X): the tensor-core kernel, one launch per format after one prep launch for
-// every distinct X. The others go to `others`.
+// Jobs of 64 or more tokens on a 16-byte-aligned matrix whose rows are a multiple of 16 bytes (and
+// 16-byte-aligned X), when together they make at least 64 tiles of 128 rows x 64 tokens (with
+// fewer, most SMs would idle and the warp-MMA kernel, which splits tiles along the blocks, is
+// faster): the tensor-core kernel, one launch per format after one prep launch for every
+// distinct X. The others go to `others`.
 int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others)
 {
     static bool attr[2] = {false, false};
@@ -2096,13 +2098,22 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
     };
     std::vector<XEnt> xe;
     std::vector<int> xidx[2];
+    auto eligible = [](const KernelCudaMatmulJob &j) {
+        const long long rb = (long long)(j.cols / 256) * (j.is_q6 ? 210 : 144);
+        return j.T >= 64 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && j.rows < (1u << 30) &&
+               j.T < (1u << 30);
+    };
+    long long tiles = 0;
+    for (int i = 0; i < n; i++)
+        if (eligible(jobs[i]))
+            tiles += (long long)((jobs[i].rows + tcm::kRows - 1) / tcm::kRows) *
+                     (long long)((jobs[i].T + tcm::kTok - 1) / tcm::kTok);
+    const bool use_tc = tiles >= 64;
     for (int i = 0; i < n; i++) {
         const KernelCudaMatmulJob &j = jobs[i];
         const int nb = (int)(j.cols / 256);
         const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
-        const bool tc = j.T >= 64 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && j.rows < (1u << 30) &&
-                        j.T < (1u << 30);
-        if (!tc) {
+        if (!use_tc || !eligible(j)) {
             others.push_back(j);
             continue;
         }

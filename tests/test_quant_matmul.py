@@ -133,3 +133,38 @@ def test_matmul_prefill_chunk(rb, oracle_lib, q6, rows, cols):
     Y = torch.zeros(T, rows, device="cuda")
     rb.matmul_quant_batch([(q6, dev(m), dev(X), Y, rows, cols, T)])
     assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
+
+
+@pytest.mark.parametrize("q6,rows,cols,T", [(False, 1000, 4096, 513), (True, 2000, 2048, 600), (False, 8200, 512, 64)])
+def test_matmul_tensor_core_path(rb, oracle_lib, q6, rows, cols, T):
+    """Shapes for the tcgen05 kernel (64 or more tokens, at least 64 tiles of 128 rows x 64
+    tokens), ragged in rows and tokens, and a repeat that must give the same bits."""
+    m = synth.quant_matrix(rows + T + int(q6), rows, cols, q6)
+    X = np.random.default_rng(T).standard_normal((T, cols)).astype(np.float32)
+    dm, dX = dev(m), dev(X)
+    Y = torch.zeros(T, rows, device="cuda")
+    rb.matmul_quant_batch([(q6, dm, dX, Y, rows, cols, T)])
+    first = Y.clone()
+    rb.matmul_quant_batch([(q6, dm, dX, Y, rows, cols, T)])
+    assert torch.equal(first, Y)
+    assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
+
+
+def test_matmul_mixed_sizes_one_call(rb, oracle_lib):
+    """One call with jobs of very different sizes sharing one X (4096, 200 and 3 rows; both
+    formats): the call's tiles are enough for the tcgen05 kernel, which takes all three, the
+    smallest filling one partial tile."""
+    T, cols = 300, 2048
+    X = np.random.default_rng(77).standard_normal((T, cols)).astype(np.float32)
+    dX = dev(X)
+    specs = [(False, 4096), (True, 200), (False, 3)]   # 32 x 5, 2 x 5 and 1 x 5 tiles
+    keep, jobs, refs = [], [], []
+    for i, (q6, rows) in enumerate(specs):
+        m = synth.quant_matrix(90 + i, rows, cols, q6)
+        dm, Y = dev(m), torch.zeros(T, rows, device="cuda")
+        keep.append((dm, Y))
+        jobs.append((q6, dm, dX, Y, rows, cols, T))
+        refs.append(_ref(q6, m, X, rows, cols))
+    rb.matmul_quant_batch(jobs)
+    for (_, Y), ref in zip(keep, refs):
+        assert O.maxrel(host(Y), ref) < TOL
