@@ -1175,17 +1175,17 @@ constexpr int kThreads = 576;           // 18 warps: copies, MMA, 8 epilogue, 8 
 constexpr int kTile = 16384;            // 128 rows x 64 K f16, swizzled
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColMain = 0, kColMin = 256;   // accumulators: main 0 / 128 (by block parity), min 256
-constexpr uint32_t kColA = 384;                   // A ring: Q4_K 3 x 32 columns; Q6_K (no min) 2 x 64 at 256
-// barrier slots (A ring up to 4 stages, B ring up to 8, 3 raw buffers)
-constexpr int kAFull = 0, kAEmpty = 4, kBFull = 8, kBEmpty = 16, kRawFull = 24, kRawEmpty = 27, kMnFullA = 30,
-              kMnFullB = 32, kMnEmpty = 34, kAccFull = 36, kAccEmpty = 38, kSclFull = 40, kSclEmpty = 42, kDrain = 44,
-              kSlot = 45;
+constexpr uint32_t kColA = 384;                   // A ring: Q4_K 4 x 32 columns; Q6_K (no min) 4 x 64 at 256
+// barrier slots (A ring 4 stages, released through the B ring's barriers; B ring 8; 3 raw buffers)
+constexpr int kAFull = 0, kBFull = 8, kBEmpty = 16, kRawFull = 24, kRawEmpty = 27, kMnFullA = 30, kMnFullB = 32,
+              kMnEmpty = 34, kAccFull = 36, kAccEmpty = 38, kSclFull = 40, kSclEmpty = 42, kDrain = 44, kSlot = 45;
 }  // namespace tcm
 
 template <bool Q6>
 struct TcCfg {
     static constexpr int kSlot = Q6 ? kQ6Slot : kQ4Slot;
-    static constexpr int kStA = Q6 ? 2 : 3;                 // A ring (decoded quarters, in tensor memory)
+    static constexpr int kStA = 4;                          // A ring (decoded quarters, in tensor memory): deep
+                                                            // enough to cover the MMAs' completion latency
     static constexpr uint32_t kColA = Q6 ? 256u : tcm::kColA;
     static constexpr uint32_t kAcols = Q6 ? 64u : 32u;      // TMEM columns of a decoded quarter
     static constexpr int kStB = 8;                          // B ring (copied quarters: covers the copy latency)
@@ -1466,24 +1466,35 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
         }
     } else if (warp == 1) {
         // ============================================================ MMA issue
+        // One thread; the issue path is kept short (the tensor pipe idles whenever the thread spends
+        // longer between quarters than a quarter's MMAs take): with a 4-deep A ring and an 8-deep B
+        // ring every slot and parity in a block is a constant or one AND of the block index, and
+        // the descriptors are built once.
+        static_assert(Cfg::kStA == 4 && Cfg::kStB == 8, "the issue loop's slot arithmetic");
         if (lane == 0) {
             const uint32_t id = tc::idesc_f16(128, 128, 0, 0);
+            const uint64_t dB0 = tc::smem_desc(base + Cfg::kOffB, 16, 1024);
+            const uint32_t ta0 = tb + Cfg::kColA;
+            const uint32_t mb0 = base + Cfg::kOffMin;
+            const uint64_t dAm0 = tc::smem_desc_plain(mb0, 128, 256), dBm0 = tc::smem_desc_plain(mb0 + 4096, 128, 256);
             for (int b = 0; b < nb && ok; b++) {
-                const uint32_t dmain = tb + kColMain + (uint32_t)(b & 1) * 128u;
-                if (b >= 2 && !mbar_wait(BAR(kAccEmpty + (b & 1)), (uint32_t)((b >> 1) - 1) & 1u)) {
+                const uint32_t odd = (uint32_t)(b & 1);
+                const uint32_t dmain = tb + kColMain + odd * 128u;
+                if (b >= 2 && !mbar_wait(BAR(kAccEmpty + odd), (uint32_t)((b >> 1) - 1) & 1u)) {
                     ok = false;
                     break;
                 }
+                const uint32_t pa = odd, pb = (uint32_t)(b >> 1) & 1u;   // A / B ring phases of this block
+#pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    const int g = 4 * b + q, sa = g % Cfg::kStA, sb = g % Cfg::kStB;
-                    if (!mbar_wait(BAR(kAFull + sa), (uint32_t)(g / Cfg::kStA) & 1u) ||
-                        !mbar_wait(BAR(kBFull + sb), (uint32_t)(g / Cfg::kStB) & 1u)) {
+                    const uint32_t sb = 4u * odd + (uint32_t)q;          // B slot; the A slot is q
+                    if (!mbar_wait(BAR(kAFull + q), pa) || !mbar_wait(BAR(kBFull + sb), pb)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t ta = tb + Cfg::kColA + (uint32_t)sa * Cfg::kAcols;
-                    const uint64_t dB = tc::smem_desc(base + Cfg::kOffB + sb * kTile, 16, 1024);
+                    const uint32_t ta = ta0 + (uint32_t)q * Cfg::kAcols;
+                    const uint64_t dB = tc::desc_adv(dB0, sb * (uint32_t)kTile);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
                         tc::mma_ts_f16(dmain, ta + 8u * kk, tc::desc_adv(dB, kk * 32u), id, (q | kk) ? 1u : 0u);
@@ -1498,19 +1509,17 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                     break;
                 if (!Q6) {
                     // the min accumulator is single: the epilogue has read block b - 1's
-                    const uint32_t ph = (uint32_t)(b >> 1) & 1u;
-                    if (!mbar_wait(BAR(kMnFullA + (b & 1)), ph) || !mbar_wait(BAR(kMnFullB + (b & 1)), ph) ||
-                        (b >= 1 && !mbar_wait(BAR(kAccEmpty + ((b - 1) & 1)), (uint32_t)((b - 1) >> 1) & 1u))) {
+                    if (!mbar_wait(BAR(kMnFullA + odd), pb) || !mbar_wait(BAR(kMnFullB + odd), pb) ||
+                        (b >= 1 && !mbar_wait(BAR(kAccEmpty + (odd ^ 1u)), (uint32_t)((b - 1) >> 1) & 1u))) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t mb = base + Cfg::kOffMin + (uint32_t)(b & 1) * Cfg::kMin;
-                    tc::mma_ss_f16(tb + kColMin, tc::smem_desc_plain(mb, 128, 256), tc::smem_desc_plain(mb + 4096, 128, 256),
-                                   id, 0u);
-                    tc::commit(BAR(kMnEmpty + (b & 1)));
+                    tc::mma_ss_f16(tb + kColMin, tc::desc_adv(dAm0, odd * (uint32_t)Cfg::kMin),
+                                   tc::desc_adv(dBm0, odd * (uint32_t)Cfg::kMin), id, 0u);
+                    tc::commit(BAR(kMnEmpty + odd));
                 }
-                tc::commit(BAR(kAccFull + (b & 1)));
+                tc::commit(BAR(kAccFull + odd));
             }
             if (!ok)
                 atomicOr(p.err, kErrWaitTimeout);
