@@ -54,6 +54,7 @@ def args_parse():
     ap.add_argument("--long-window", type=int, default=262144)
     ap.add_argument("--no-proj", action="store_true", help="skip the k-quant projection measurement")
     ap.add_argument("--proj-steps", type=int, default=20)
+    ap.add_argument("--step-rounds", type=int, default=10, help="timed rounds of the batched-step measurement")
     ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
     ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
     ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
@@ -384,6 +385,96 @@ def run_prefill_projections(R, torch, dev, stream, steps: int, rank: int):
     launches = R.launch_count() - n0
     del keep
     return e0.elapsed_time(e1) / steps, launches
+
+
+# ------------------------------------------------------------------- cross-slot batched step (section 8f row 4)
+
+STEP_SLOTS = 64           # config 2's slots per GPU
+
+
+def run_batched_step(R, torch, dev, stream, steps: int, rank: int, slots: int = STEP_SLOTS):
+    """`slots` native slot threads (libslot_threads.so) step one token each through the step group,
+    layer by layer: per layer one kernel_step_group_matvec with that layer's projections (site =
+    layer). The group merges the slots' jobs on each shared matrix into one `slots`-token product.
+    Compared with the per-slot form of the reference's step lock: one
+    kernel_cuda_matvec_quant_batch per slot carrying all 190 of its projections, slots one after
+    another. Returns a dict of timings."""
+    import ctypes as C
+    import time
+    from roaster_b200 import build as B
+    drv = C.CDLL(B.SLOT_LIB)
+    drv.slot_threads_run.restype = C.c_int
+    drv.slot_threads_run.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int,
+                                     C.POINTER(C.c_int), C.POINTER(R.KernelCudaMatvecJob), C.c_int]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7200 + rank)
+    mats = [torch.randint(0, 256, (r * (c // 256) * (210 if q6 else 144),), dtype=torch.uint8, device=dev,
+                          generator=gen) for q6, r, c in PROJ_SHAPES]
+    per_site = [len(PROJ_ATT)] * 10 + [len(PROJ_DN)] * 30
+    total = len(PROJ_SHAPES)
+    xcols = sum(c for _, _, c in PROJ_SHAPES)
+    yrows = sum(r for _, r, _ in PROJ_SHAPES)
+    X = torch.randn(slots, xcols, device=dev, generator=gen)
+    Y = torch.zeros(slots, yrows + 4 * total, device=dev)
+    jobs = (R.KernelCudaMatvecJob * (slots * total))()
+    for i in range(slots):
+        xo = yo = 0
+        for j, (q6, r, c) in enumerate(PROJ_SHAPES):
+            jobs[i * total + j] = R.KernelCudaMatvecJob(int(q6), mats[j].data_ptr(), X[i, xo:].data_ptr(),
+                                                        Y[i, yo:].data_ptr(), r, c)
+            xo += c
+            yo += (r + 3) // 4 * 4              # 16-byte aligned outputs
+    ps = (C.c_int * len(per_site))(*per_site)
+    g = R.StepGroup(slots, straggler_us=2000, call_timeout_ms=20000)
+    ids_l = [g.join() for _ in range(slots)]
+    ids = (C.c_int * slots)(*ids_l)
+    lib = R.lib()
+
+    def group_rounds(n):
+        if drv.slot_threads_run(C.c_void_p(g._h), slots, ids, n, len(per_site), ps, jobs, total) != 0:
+            raise RuntimeError("step group: " + R.last_error())
+
+    group_rounds(2)
+    R.synchronize()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = R.launch_count()
+    st0 = g.stats()
+    t0 = time.perf_counter()
+    e0.record(stream)
+    group_rounds(steps)
+    e1.record(stream)
+    R.synchronize()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / steps
+    gms = e0.elapsed_time(e1) / steps
+    launches = R.launch_count() - n0
+    st1 = g.stats()
+    for m in ids_l:
+        g.leave(m)
+    g.close()
+
+    # the per-slot form: one call per slot, slots in turn
+    per = [C.cast(C.addressof(jobs) + i * total * C.sizeof(R.KernelCudaMatvecJob), C.POINTER(R.KernelCudaMatvecJob))
+           for i in range(slots)]
+    for i in range(slots):
+        lib.kernel_cuda_matvec_quant_batch(per[i], total)
+    R.synchronize()
+    torch.cuda.synchronize()
+    psteps = max(1, steps // 2)
+    e0.record(stream)
+    for _ in range(psteps):
+        for i in range(slots):
+            if lib.kernel_cuda_matvec_quant_batch(per[i], total) != 0:
+                raise RuntimeError(R.last_error())
+    e1.record(stream)
+    R.synchronize()
+    torch.cuda.synchronize()
+    sms = e0.elapsed_time(e1) / psteps
+    del mats, X, Y
+    return {"group_ms": gms, "group_wall_ms": wall, "serial_ms": sms, "launches": launches,
+            "rounds": st1["rounds"] - st0["rounds"], "calls": st1["calls"] - st0["calls"],
+            "products": st1["products"] - st0["products"], "max_round": st1["max_round"]}
 
 
 def prefill_proj_cpu_reference(seconds: float = 2.0) -> dict:
@@ -797,12 +888,13 @@ def run_ours(a):
                  "steps": a.proj_steps, "gpu_launches": int(plaunch), "jobs": len(PROJ_SHAPES),
                  "algorithmic_flop_per_step": pflop,
                  "data": "synthetic: uniform random k-quant blocks, N(0,1) activations",
-                 "roofline": {"bound": "tensor", "kernel": "quant_matmul_kernel",
+                 "roofline": {"bound": "tensor", "kernel": "quant_mm_tc_kernel",
                               "achieved": round(tfs, 2), "peak": tens_p, "unit": "TFLOP/s",
                               "frac": round(tfs / tens_p, 4),
                               "peak_source": f"{src_p} bf16_tflops (burst)",
-                              "note": "warp MMA (mma.sync m16n8k16); each product runs as 2 f16 MMAs "
-                                      "(activation hi + lo; Q6_K 4: the scale split in two exact halves)"}}
+                              "note": "tcgen05 (A from tensor memory, M = N = 128); each product runs as 2 "
+                                      "f16 MMAs (activation hi + lo; Q6_K 4: the scale split in two exact "
+                                      "halves), plus the Q4_K min term"}}
         if rank == 0 and world == 1 and not a.no_cpu_baseline:
             try:
                 c = prefill_proj_cpu_reference()
@@ -812,6 +904,34 @@ def run_ours(a):
                                                    f"for 256 tokens, the reference's matmul_quant_cpu under OpenMP"}
             except Exception as e:  # reported, not fatal
                 pproj["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
+
+    bstep = None
+    if not a.no_proj:
+        r = run_batched_step(R, torch, dev, stream, a.step_rounds, rank)
+        tq = torch.tensor([r["group_ms"], r["serial_ms"]], device=dev)
+        if world > 1:
+            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
+        gms, sms = float(tq[0].item()), float(tq[1].item())
+        flop = proj_flops(PROJ_SHAPES, STEP_SLOTS)
+        _, tens_p, src_p = peaks()
+        tfs = flop / (gms / 1e3) / 1e12
+        bstep = {"metric": "batched decode step tok/s (64 slot threads, one token each through the 40-layer "
+                           "stack's Q4_K/Q6_K projections via the step group, one combined call per layer)",
+                 "value": round(STEP_SLOTS / (gms / 1e3) * world, 1), "unit": "tok/s",
+                 "ms_per_step": round(gms, 4), "wall_ms_per_step": round(r["group_wall_ms"], 4),
+                 "steps": a.step_rounds, "gpu_launches": int(r["launches"]), "slots": STEP_SLOTS,
+                 "rounds": r["rounds"], "combined_calls": r["calls"], "merged_products": r["products"],
+                 "max_round": r["max_round"],
+                 "per_slot_form": {"ms_per_step": round(sms, 4),
+                                   "value": round(STEP_SLOTS / (sms / 1e3) * world, 1), "unit": "tok/s",
+                                   "what": "one kernel_cuda_matvec_quant_batch per slot (all 190 of its "
+                                           "projections), slots in turn, as under the reference's step lock"},
+                 "data": "synthetic: uniform random k-quant blocks, N(0,1) activations; native pthreads "
+                         "(libslot_threads.so) as the slot threads",
+                 "roofline": {"bound": "tensor", "kernel": "quant_mm_tc_kernel",
+                              "achieved": round(tfs, 2), "peak": tens_p, "unit": "TFLOP/s",
+                              "frac": round(tfs / tens_p, 4), "peak_source": f"{src_p} bf16_tflops (burst)",
+                              "algorithmic_flop_per_step": flop}}
 
     long_ctx = None
     if not a.no_long:
@@ -857,6 +977,7 @@ def run_ours(a):
                                          "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
             "prefill": prefill, "long_context": long_ctx, "projections": proj, "prefill_projections": pproj,
+            "batched_step": bstep,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -361,6 +361,59 @@ typedef struct {
 
 int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, int n);
 
+/* ------------------------------------------------------------ cross-slot batched step
+ * The batched counterpart of the reference's step lock (FairLock, slots.c:77-105, taken once
+ * per token by step_forward, slots.c:864-880): instead of running one slot's model step at a
+ * time, the slot threads that are decoding meet in rounds, and the i-th hot-path call of every
+ * member of a round becomes ONE device batch -- the members' attention jobs one
+ * kernel_attn_decode_batch, their DeltaNet jobs one kernel_deltanet_step_batch, their k-quant
+ * projections one kernel_cuda_matmul_quant_batch in which the members' vectors for the same
+ * weight matrix form the tokens of one multi-token product (the weights are read once per round
+ * instead of once per slot).
+ *
+ * Protocol, per slot thread: kernel_step_group_join once when the slot starts decoding; per
+ * token, kernel_step_group_begin, the layer calls in model order, kernel_step_group_end;
+ * kernel_step_group_leave when the slot stops. A round forms when every joined member has
+ * called begin, or `straggler_us` after the first begin, with whoever has begun; the others
+ * take the next round. Every member of a round must make the same calls in the same order
+ * (`site` names the call, e.g. layer * 16 + op, and must agree); a call runs once every member
+ * of the round that has not ended has reached it, on the thread that arrives last. Jobs hold
+ * device pointers; the batch is asynchronous on the library stream, like the calls it replaces.
+ * A call returns the device batch's status to every member of it (0 / -1). A member that does
+ * not reach a call within `call_timeout_ms` fails that call for all (-1, message in
+ * kernel_cuda_last_error) and the rest of the round's calls (they return -1 at once); the
+ * round still ends normally. Work outside rounds (prefill chunks, rollbacks) takes
+ * kernel_step_group_lock / unlock, the FIFO lock the group's own batches also run under, which
+ * keeps the single-stream, non-overlapping rule of this library. All functions are thread-safe;
+ * none may be called with the group lock held except kernel_step_group_unlock. */
+typedef struct KernelStepGroup KernelStepGroup;
+
+typedef struct {
+    unsigned long long rounds;       /* rounds formed */
+    unsigned long long calls;        /* combined calls run (one device batch each) */
+    unsigned long long jobs;         /* member jobs those calls carried */
+    unsigned long long products;     /* projections merged: weight matrices shared by 2+ members */
+    unsigned long long merged_jobs;  /* member projection jobs inside those merged products */
+    unsigned long long errors;       /* calls that returned -1 */
+    int max_round;                   /* largest round */
+    int members;                     /* members joined now */
+} KernelStepGroupStats;
+
+/* max_members >= 1; straggler_us >= 0; call_timeout_ms > 0. NULL on bad arguments. */
+KernelStepGroup *kernel_step_group_create(int max_members, long long straggler_us, long long call_timeout_ms);
+/* Waits for no one: destroy only when no thread is inside the group. Frees its device buffers. */
+void kernel_step_group_destroy(KernelStepGroup *g);
+int  kernel_step_group_join(KernelStepGroup *g);                /* member id >= 0, -1 when full */
+int  kernel_step_group_leave(KernelStepGroup *g, int member);   /* outside a round only */
+int  kernel_step_group_begin(KernelStepGroup *g, int member);   /* size of the round joined, or -1 */
+int  kernel_step_group_end(KernelStepGroup *g, int member);
+int  kernel_step_group_attn(KernelStepGroup *g, int member, int site, const KernelAttnDecodeJob *job);
+int  kernel_step_group_delta(KernelStepGroup *g, int member, int site, const KernelDeltaStepJob *job);
+int  kernel_step_group_matvec(KernelStepGroup *g, int member, int site, const KernelCudaMatvecJob *jobs, int n);
+int  kernel_step_group_lock(KernelStepGroup *g);
+int  kernel_step_group_unlock(KernelStepGroup *g);
+int  kernel_step_group_stats(const KernelStepGroup *g, KernelStepGroupStats *out);
+
 #ifdef __cplusplus
 }
 #endif

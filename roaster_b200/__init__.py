@@ -87,6 +87,13 @@ class KernelCudaMatvecJob(C.Structure):
                 ("cols", _sz)]
 
 
+class KernelStepGroupStats(C.Structure):
+    """Mirror of ``KernelStepGroupStats`` (include/roaster_cuda.h)."""
+    _fields_ = [("rounds", C.c_ulonglong), ("calls", C.c_ulonglong), ("jobs", C.c_ulonglong),
+                ("products", C.c_ulonglong), ("merged_jobs", C.c_ulonglong), ("errors", C.c_ulonglong),
+                ("max_round", C.c_int), ("members", C.c_int)]
+
+
 _lib = None
 
 
@@ -151,6 +158,18 @@ def lib():
         "kernel_deltanet_layer_prefill": (C.c_int, [_vp] * 6 + [_sz] + [_vp] * 5),
         "kernel_cuda_matvec_quant_batch": (C.c_int, [C.POINTER(KernelCudaMatvecJob), C.c_int]),
         "kernel_cuda_matmul_quant_batch": (C.c_int, [C.POINTER(KernelCudaMatmulJob), C.c_int]),
+        "kernel_step_group_create": (_vp, [C.c_int, C.c_longlong, C.c_longlong]),
+        "kernel_step_group_destroy": (None, [_vp]),
+        "kernel_step_group_join": (C.c_int, [_vp]),
+        "kernel_step_group_leave": (C.c_int, [_vp, C.c_int]),
+        "kernel_step_group_begin": (C.c_int, [_vp, C.c_int]),
+        "kernel_step_group_end": (C.c_int, [_vp, C.c_int]),
+        "kernel_step_group_attn": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(KernelAttnDecodeJob)]),
+        "kernel_step_group_delta": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(KernelDeltaStepJob)]),
+        "kernel_step_group_matvec": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(KernelCudaMatvecJob), C.c_int]),
+        "kernel_step_group_lock": (C.c_int, [_vp]),
+        "kernel_step_group_unlock": (C.c_int, [_vp]),
+        "kernel_step_group_stats": (C.c_int, [_vp, C.POINTER(KernelStepGroupStats)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -310,3 +329,62 @@ def matmul_quant_batch(jobs) -> None:
           for j in jobs]
     arr, n = _arr(KernelCudaMatmulJob, js)
     check(lib().kernel_cuda_matmul_quant_batch(arr, n), "kernel_cuda_matmul_quant_batch")
+
+
+class StepGroup:
+    """Cross-slot batched step (``kernel_step_group_*``): the batched counterpart of the
+    reference's per-token step lock (src/slots.c:77-105, 864-880). Each slot thread joins once,
+    then per token calls begin(), its hot-path calls in model order, end(). The calls return the
+    combined device batch's status (0 / -1); ``raise_on_error`` turns -1 into RuntimeError."""
+
+    def __init__(self, max_members: int, straggler_us: int = 200, call_timeout_ms: int = 10000):
+        self._h = lib().kernel_step_group_create(int(max_members), int(straggler_us), int(call_timeout_ms))
+        if not self._h:
+            raise RuntimeError(f"kernel_step_group_create failed: {last_error()}")
+
+    def close(self) -> None:
+        if self._h:
+            lib().kernel_step_group_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def join(self) -> int:
+        m = lib().kernel_step_group_join(self._h)
+        if m < 0:
+            raise RuntimeError(f"kernel_step_group_join failed: {last_error()}")
+        return m
+
+    def leave(self, member: int) -> int:
+        return lib().kernel_step_group_leave(self._h, member)
+
+    def begin(self, member: int) -> int:
+        return lib().kernel_step_group_begin(self._h, member)
+
+    def end(self, member: int) -> int:
+        return lib().kernel_step_group_end(self._h, member)
+
+    def attn(self, member: int, site: int, job: KernelAttnDecodeJob) -> int:
+        return lib().kernel_step_group_attn(self._h, member, site, C.byref(job))
+
+    def delta(self, member: int, site: int, job: KernelDeltaStepJob) -> int:
+        return lib().kernel_step_group_delta(self._h, member, site, C.byref(job))
+
+    def matvec(self, member: int, site: int, jobs) -> int:
+        js = [j if isinstance(j, KernelCudaMatvecJob) else
+              KernelCudaMatvecJob(int(bool(j[0])), _ptr(j[1]), _ptr(j[2]), _ptr(j[3]), int(j[4]), int(j[5]))
+              for j in jobs]
+        arr, n = _arr(KernelCudaMatvecJob, js)
+        return lib().kernel_step_group_matvec(self._h, member, site, arr, n)
+
+    def lock(self) -> None:
+        check(lib().kernel_step_group_lock(self._h), "kernel_step_group_lock")
+
+    def unlock(self) -> None:
+        check(lib().kernel_step_group_unlock(self._h), "kernel_step_group_unlock")
+
+    def stats(self) -> dict:
+        st = KernelStepGroupStats()
+        check(lib().kernel_step_group_stats(self._h, C.byref(st)), "kernel_step_group_stats")
+        return {name: getattr(st, name) for name, _ in KernelStepGroupStats._fields_}

@@ -40,6 +40,9 @@ def _stale() -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
+        if not os.path.exists(SLOT_LIB) or os.path.getmtime(SLOT_LIB) < max(os.path.getmtime(SLOT_SRC),
+                                                                            os.path.getmtime(LIB)):
+            build_slot_threads()
         return LIB
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
@@ -68,7 +71,26 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if out.returncode != 0:
         raise RuntimeError("link failed:\n" + out.stdout + out.stderr)
     os.replace(tmp, LIB)
+    build_slot_threads()
     return LIB
+
+
+SLOT_SRC = os.path.join(HERE, "slot_threads.c")
+SLOT_LIB = os.path.join(HERE, "libslot_threads.so")
+
+
+def build_slot_threads() -> str:
+    """libslot_threads.so: native slot threads for driving the step group (slot_threads.c),
+    linked against libroaster_b200.so in the same folder."""
+    inc = os.path.join(HERE, "..", "include")
+    tmp = SLOT_LIB + ".tmp"
+    cmd = ["gcc", "-O2", "-std=c11", "-Wall", "-Werror", "-fPIC", "-shared", "-I", inc, SLOT_SRC,
+           "-o", tmp, "-L", HERE, "-l:libroaster_b200.so", "-Wl,-rpath,$ORIGIN", "-lpthread"]
+    out = subprocess.run(cmd, capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("slot_threads build failed:\n" + out.stdout + out.stderr)
+    os.replace(tmp, SLOT_LIB)
+    return SLOT_LIB
 
 
 if __name__ == "__main__":

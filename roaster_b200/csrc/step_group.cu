@@ -1,0 +1,563 @@
+// Cross-slot batched step (the KernelStepGroup part of include/roaster_cuda.h).
+//
+// The reference runs one slot's model step at a time: step_forward (slots.c:864-880) takes the
+// round-robin FairLock (slots.c:77-105) around model_forward, so with N slots decoding every
+// hot-path call carries one slot's job and every projection reads its weights once per slot.
+// Here the decoding slot threads meet in rounds; the i-th call of each member of a round is
+// combined into one device batch, run by the member that arrives last (a combining barrier).
+// Projections are regrouped by weight matrix: members that multiply the same matrix become the
+// tokens of one multi-token product, gathered into a contiguous [T][cols] block by one copy-list
+// launch, multiplied by kernel_cuda_matmul_quant_batch, and scattered back by a second launch.
+//
+// Host side: one mutex guards the membership, the round and the open call. Members waiting for
+// a call to complete sleep on a futex on the call generation, so the completion wakes them all at
+// once without each re-taking the mutex (with tens of slot threads, waking them one by one
+// through a condition variable's mutex cost more than the device work of a layer). Every wait is
+// bounded (straggler limit for a round to form, call timeout for a call to fill, the same timeout
+// for a round to end). Device batches run with the group mutex released
+// and the group's FIFO lock (the FairLock counterpart) held, so work outside rounds that takes
+// the same lock never overlaps them.
+#include "runtime.h"
+#include "../../include/roaster_cuda.h"
+
+#include <linux/futex.h>
+#include <sys/syscall.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
+#include <climits>
+#include <condition_variable>
+#include <cstring>
+#include <ctime>
+#include <mutex>
+#include <vector>
+
+using namespace rb;
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+constexpr int kCopyMax = 256;   // copy-list entries per launch (6 KB of parameters)
+
+struct CopyList {
+    const float *src[kCopyMax];
+    float *dst[kCopyMax];
+    unsigned n[kCopyMax];       // floats
+};
+
+// One CTA per entry; 16-byte accesses when both ends and the length allow, else floats.
+__global__ void __launch_bounds__(256) group_copy_kernel(const __grid_constant__ CopyList L)
+{
+    const int e = blockIdx.x;
+    const float *s = L.src[e];
+    float *d = L.dst[e];
+    const unsigned n = L.n[e];
+    if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0 && (n & 3u) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(s);
+        float4 *d4 = reinterpret_cast<float4 *>(d);
+        for (unsigned i = threadIdx.x; i < n / 4; i += blockDim.x)
+            d4[i] = s4[i];
+    } else {
+        for (unsigned i = threadIdx.x; i < n; i += blockDim.x)
+            d[i] = s[i];
+    }
+}
+
+enum Kind { kAttn = 1, kDelta = 2, kMatvec = 3 };
+
+struct Entry {
+    int member;
+    KernelCudaMatvecJob job;
+};
+
+}  // namespace
+
+struct KernelStepGroup {
+    int max_members = 0;
+    long long straggler_us = 0;
+    long long timeout_us = 0;
+
+    mutable std::mutex m;
+    std::condition_variable cv;
+    std::vector<char> joined, pending, in_round;
+    int n_joined = 0, n_pending = 0;
+    Clock::time_point first_pending;
+
+    bool round_active = false;
+    bool round_failed = false;
+    int round_left = 0;              // members of the round that have not ended
+    uint64_t round_id = 0;
+
+    // the open call of the round (at most one: a member moves on only when its call completes)
+    bool call_open = false;
+    bool call_running = false;
+    int call_kind = 0, call_site = 0, call_arrived = 0;
+    uint64_t call_gen = 0;           // completed calls
+    int call_status[16] = {};        // status of call generation g at [g & 15]
+    std::atomic<uint32_t> gen_word{0};   // low bits of call_gen, the futex the call waiters sleep on
+    Clock::time_point call_deadline;
+    std::vector<KernelAttnDecodeJob> attn;
+    std::vector<KernelDeltaStepJob> delta;
+    std::vector<Entry> mv;
+
+    // FIFO lock (ticket), the counterpart of the reference's FairLock
+    std::mutex lm;
+    std::condition_variable lc;
+    unsigned long long next_ticket = 0, serving = 0;
+
+    // device staging of merged projections (grow-only)
+    float *xbuf = nullptr, *ybuf = nullptr;
+    size_t xcap = 0, ycap = 0;
+
+    KernelStepGroupStats st{};
+};
+
+namespace {
+
+void fifo_lock(KernelStepGroup *g)
+{
+    std::unique_lock<std::mutex> l(g->lm);
+    const unsigned long long t = g->next_ticket++;
+    g->lc.wait(l, [&] { return g->serving == t; });
+}
+
+void fifo_unlock(KernelStepGroup *g)
+{
+    std::lock_guard<std::mutex> l(g->lm);
+    g->serving++;
+    g->lc.notify_all();
+}
+
+void futex_wait(std::atomic<uint32_t> *w, uint32_t v, long ns)
+{
+    timespec ts;
+    ts.tv_sec = ns / 1000000000L;
+    ts.tv_nsec = ns % 1000000000L;
+    syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAIT_PRIVATE, v, &ts, nullptr, 0);
+}
+
+void futex_wake_all(std::atomic<uint32_t> *w)
+{
+    syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAKE_PRIVATE, INT_MAX, nullptr, nullptr, 0);
+}
+
+// Close the open call with status rc and wake its waiters. Group mutex held.
+void complete(KernelStepGroup *g, int rc)
+{
+    g->call_gen++;
+    g->call_status[g->call_gen & 15] = rc;
+    g->call_open = false;
+    g->call_running = false;
+    g->call_arrived = 0;
+    g->gen_word.store((uint32_t)g->call_gen, std::memory_order_release);
+    futex_wake_all(&g->gen_word);
+    g->cv.notify_all();   // begin() watches the progress of a running round
+}
+
+bool valid_member(const KernelStepGroup *g, int member)
+{
+    return member >= 0 && member < g->max_members && g->joined[member];
+}
+
+int grow(float **buf, size_t *cap, size_t floats)
+{
+    if (floats <= *cap)
+        return 0;
+    // the previous buffer may still be read by queued work
+    if (*buf) {
+        if (check(cudaStreamSynchronize(rt().stream), "step group: stream sync") != 0)
+            return -1;
+        cudaFree(*buf);
+        *buf = nullptr;
+        *cap = 0;
+    }
+    size_t want = floats + floats / 2;
+    if (check(cudaMalloc(reinterpret_cast<void **>(buf), want * sizeof(float)), "step group: cudaMalloc") != 0)
+        return -1;
+    *cap = want;
+    return 0;
+}
+
+int copy_list(const std::vector<const float *> &src, const std::vector<float *> &dst, const std::vector<unsigned> &n)
+{
+    for (size_t i0 = 0; i0 < src.size(); i0 += kCopyMax) {
+        CopyList L;
+        memset(static_cast<void *>(&L), 0, sizeof(L));
+        const size_t cnt = src.size() - i0 < (size_t)kCopyMax ? src.size() - i0 : (size_t)kCopyMax;
+        for (size_t i = 0; i < cnt; i++) {
+            L.src[i] = src[i0 + i];
+            L.dst[i] = dst[i0 + i];
+            L.n[i] = n[i0 + i];
+        }
+        group_copy_kernel<<<(unsigned)cnt, 256, 0, rt().stream>>>(L);
+        if (launched("group_copy_kernel") != 0)
+            return -1;
+    }
+    return 0;
+}
+
+// Regroup the members' projections by weight matrix; a matrix shared by T >= 2 members becomes
+// one T-token product over gathered vectors. Counts go to `st` before any device work, so the
+// plan is observable without a GPU.
+int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroupStats *st)
+{
+    struct Group {
+        KernelCudaMatvecJob key;
+        std::vector<int> idx;
+    };
+    std::vector<Group> groups;
+    for (int i = 0; i < (int)mv.size(); i++) {
+        const KernelCudaMatvecJob &j = mv[i].job;
+        bool found = false;
+        for (Group &gr : groups)
+            if (gr.key.matrix == j.matrix && gr.key.is_q6 == j.is_q6 && gr.key.rows == j.rows && gr.key.cols == j.cols) {
+                gr.idx.push_back(i);
+                found = true;
+                break;
+            }
+        if (!found)
+            groups.push_back(Group{j, {i}});
+    }
+    size_t xfl = 0, yfl = 0;
+    for (const Group &gr : groups)
+        if (gr.idx.size() >= 2) {
+            st->products++;
+            st->merged_jobs += gr.idx.size();
+            xfl += gr.idx.size() * gr.key.cols;
+            yfl += ((gr.idx.size() * gr.key.rows + 3) & ~(size_t)3);
+        }
+    if (ensure() != 0)
+        return -1;
+    for (const Entry &e : mv)
+        if (!e.job.matrix || !e.job.vector || !e.job.output || e.job.rows == 0 || e.job.cols == 0 || e.job.cols % 256 != 0)
+            return fail("kernel_step_group_matvec: member %d has an invalid job", e.member);
+    if (grow(&g->xbuf, &g->xcap, xfl) != 0 || grow(&g->ybuf, &g->ycap, yfl) != 0)
+        return -1;
+    std::vector<KernelCudaMatmulJob> jobs;
+    std::vector<const float *> gs, ss;
+    std::vector<float *> gd, sd;
+    std::vector<unsigned> gn, sn;
+    size_t xo = 0, yo = 0;
+    for (const Group &gr : groups) {
+        const KernelCudaMatvecJob &k = gr.key;
+        if (gr.idx.size() == 1) {
+            const KernelCudaMatvecJob &j = mv[gr.idx[0]].job;
+            jobs.push_back(KernelCudaMatmulJob{j.is_q6, j.matrix, j.vector, j.output, j.rows, j.cols, 1});
+            continue;
+        }
+        const size_t T = gr.idx.size();
+        float *X = g->xbuf + xo, *Y = g->ybuf + yo;
+        for (size_t t = 0; t < T; t++) {
+            const KernelCudaMatvecJob &j = mv[gr.idx[t]].job;
+            gs.push_back(j.vector);
+            gd.push_back(X + t * k.cols);
+            gn.push_back((unsigned)k.cols);
+            ss.push_back(Y + t * k.rows);
+            sd.push_back(j.output);
+            sn.push_back((unsigned)k.rows);
+        }
+        jobs.push_back(KernelCudaMatmulJob{k.is_q6, k.matrix, X, Y, k.rows, k.cols, T});
+        xo += T * k.cols;
+        yo += (T * k.rows + 3) & ~(size_t)3;
+    }
+    if (copy_list(gs, gd, gn) != 0)
+        return -1;
+    if (kernel_cuda_matmul_quant_batch(jobs.data(), (int)jobs.size()) != 0)
+        return -1;
+    return copy_list(ss, sd, sn);
+}
+
+// Run the open call's batch. Called with the group mutex held by `l`; releases it around the
+// device work (every member of the call is waiting, so nothing changes the call meanwhile).
+void run_call(KernelStepGroup *g, std::unique_lock<std::mutex> &l)
+{
+    g->call_running = true;
+    const int kind = g->call_kind;
+    std::vector<KernelAttnDecodeJob> attn;
+    std::vector<KernelDeltaStepJob> delta;
+    std::vector<Entry> mv;
+    attn.swap(g->attn);
+    delta.swap(g->delta);
+    mv.swap(g->mv);
+    g->attn.reserve(attn.size());      // the next call of the round is usually the same size
+    g->delta.reserve(delta.size());
+    g->mv.reserve(mv.size());
+    const size_t njobs = kind == kAttn ? attn.size() : kind == kDelta ? delta.size() : mv.size();
+    KernelStepGroupStats plan{};
+    l.unlock();
+    fifo_lock(g);
+    int rc = 0;
+    if (kind == kAttn)
+        rc = kernel_attn_decode_batch(attn.data(), (int)attn.size());
+    else if (kind == kDelta)
+        rc = kernel_deltanet_step_batch(delta.data(), (int)delta.size());
+    else
+        rc = run_matvec(g, mv, &plan);
+    fifo_unlock(g);
+    l.lock();
+    g->st.calls++;
+    g->st.jobs += njobs;
+    g->st.products += plan.products;
+    g->st.merged_jobs += plan.merged_jobs;
+    if (rc != 0)
+        g->st.errors++;
+    complete(g, rc);
+}
+
+// Fail the open call for every member in it and the rest of the round.
+void fail_call(KernelStepGroup *g)
+{
+    g->round_failed = true;
+    g->attn.clear();
+    g->delta.clear();
+    g->mv.clear();
+    g->st.errors++;
+    complete(g, -1);
+}
+
+template <typename Add>
+int rendezvous(KernelStepGroup *g, int member, int kind, int site, const char *what, Add add)
+{
+    if (!g)
+        return fail("%s: null group", what);
+    std::unique_lock<std::mutex> l(g->m);
+    if (!valid_member(g, member) || !g->in_round[member])
+        return fail("%s: member %d is not in a round", what, member);
+    if (g->round_failed)
+        return fail("%s: an earlier call of this round failed", what);
+    if (g->call_open && (g->call_kind != kind || g->call_site != site)) {
+        fail("%s: members reached different calls (kind %d site %d vs kind %d site %d)", what, kind, site,
+             g->call_kind, g->call_site);
+        fail_call(g);
+        return -1;
+    }
+    if (!g->call_open) {
+        g->call_open = true;
+        g->call_kind = kind;
+        g->call_site = site;
+        g->call_arrived = 0;
+        g->call_deadline = Clock::now() + std::chrono::microseconds(g->timeout_us);
+    }
+    add(g);
+    g->call_arrived++;
+    const uint64_t gen = g->call_gen;
+    if (g->call_arrived == g->round_left) {
+        run_call(g, l);
+        return g->call_status[(gen + 1) & 15];
+    }
+    const Clock::time_point deadline = g->call_deadline;
+    l.unlock();
+    // the status of call gen + 1 is written before gen_word moves (release / acquire)
+    while (g->gen_word.load(std::memory_order_acquire) == (uint32_t)gen) {
+        futex_wait(&g->gen_word, (uint32_t)gen, 2000000L);   // 2 ms slices
+        if (g->gen_word.load(std::memory_order_acquire) != (uint32_t)gen || Clock::now() < deadline)
+            continue;
+        l.lock();
+        if (g->call_gen == gen && !g->call_running) {   // a running batch always completes
+            fail("%s: not every member reached call site %d within the call timeout", what, site);
+            fail_call(g);
+        }
+        l.unlock();
+    }
+    return g->call_status[(gen + 1) & 15];
+}
+
+}  // namespace
+
+extern "C" KernelStepGroup *kernel_step_group_create(int max_members, long long straggler_us, long long call_timeout_ms)
+{
+    if (max_members < 1 || max_members > 4096 || straggler_us < 0 || call_timeout_ms <= 0) {
+        fail("kernel_step_group_create: bad arguments");
+        return nullptr;
+    }
+    KernelStepGroup *g = new KernelStepGroup;
+    g->max_members = max_members;
+    g->straggler_us = straggler_us;
+    g->timeout_us = call_timeout_ms * 1000;
+    g->joined.assign(max_members, 0);
+    g->pending.assign(max_members, 0);
+    g->in_round.assign(max_members, 0);
+    return g;
+}
+
+extern "C" void kernel_step_group_destroy(KernelStepGroup *g)
+{
+    if (!g)
+        return;
+    if (g->xbuf || g->ybuf) {
+        if (rt().device >= 0)
+            cudaStreamSynchronize(rt().stream);
+        cudaFree(g->xbuf);
+        cudaFree(g->ybuf);
+    }
+    delete g;
+}
+
+extern "C" int kernel_step_group_join(KernelStepGroup *g)
+{
+    if (!g)
+        return fail("kernel_step_group_join: null group");
+    std::lock_guard<std::mutex> l(g->m);
+    for (int i = 0; i < g->max_members; i++)
+        if (!g->joined[i]) {
+            g->joined[i] = 1;
+            g->n_joined++;
+            g->st.members = g->n_joined;
+            g->cv.notify_all();
+            return i;
+        }
+    return fail("kernel_step_group_join: all %d member places are taken", g->max_members);
+}
+
+extern "C" int kernel_step_group_leave(KernelStepGroup *g, int member)
+{
+    if (!g)
+        return fail("kernel_step_group_leave: null group");
+    std::lock_guard<std::mutex> l(g->m);
+    if (!valid_member(g, member))
+        return fail("kernel_step_group_leave: member %d is not joined", member);
+    if (g->in_round[member])
+        return fail("kernel_step_group_leave: member %d is inside a round (end it first)", member);
+    if (g->pending[member]) {
+        g->pending[member] = 0;
+        g->n_pending--;
+    }
+    g->joined[member] = 0;
+    g->n_joined--;
+    g->st.members = g->n_joined;
+    g->cv.notify_all();   // the waiting members may now be everyone
+    return 0;
+}
+
+extern "C" int kernel_step_group_begin(KernelStepGroup *g, int member)
+{
+    if (!g)
+        return fail("kernel_step_group_begin: null group");
+    std::unique_lock<std::mutex> l(g->m);
+    if (!valid_member(g, member))
+        return fail("kernel_step_group_begin: member %d is not joined", member);
+    if (g->in_round[member] || g->pending[member])
+        return fail("kernel_step_group_begin: member %d has already begun", member);
+    g->pending[member] = 1;
+    if (g->n_pending++ == 0)
+        g->first_pending = Clock::now();
+    g->cv.notify_all();
+    // bound on waiting for a running round: a call timeout without any progress of that round
+    Clock::time_point give_up = Clock::now() + std::chrono::microseconds(g->timeout_us);
+    uint64_t seen_gen = g->call_gen, seen_round = g->round_id;
+    for (;;) {
+        if (g->call_gen != seen_gen || g->round_id != seen_round) {
+            seen_gen = g->call_gen;
+            seen_round = g->round_id;
+            give_up = Clock::now() + std::chrono::microseconds(g->timeout_us);
+        }
+        if (g->in_round[member])
+            return g->round_left;
+        if (!g->round_active) {
+            const Clock::time_point form = g->first_pending + std::chrono::microseconds(g->straggler_us);
+            if (g->n_pending == g->n_joined || Clock::now() >= form) {
+                g->round_active = true;
+                g->round_failed = false;
+                g->round_id++;
+                g->round_left = g->n_pending;
+                for (int i = 0; i < g->max_members; i++)
+                    if (g->pending[i]) {
+                        g->pending[i] = 0;
+                        g->in_round[i] = 1;
+                    }
+                g->n_pending = 0;
+                g->st.rounds++;
+                if (g->round_left > g->st.max_round)
+                    g->st.max_round = g->round_left;
+                g->cv.notify_all();
+                return g->round_left;
+            }
+            g->cv.wait_until(l, form);
+        } else {
+            if (g->cv.wait_until(l, give_up) == std::cv_status::timeout && !g->in_round[member] && g->round_active &&
+                g->call_gen == seen_gen && g->round_id == seen_round) {
+                g->pending[member] = 0;
+                if (--g->n_pending == 0)
+                    g->first_pending = Clock::time_point();
+                return fail("kernel_step_group_begin: the running round did not end within the call timeout");
+            }
+        }
+    }
+}
+
+extern "C" int kernel_step_group_end(KernelStepGroup *g, int member)
+{
+    if (!g)
+        return fail("kernel_step_group_end: null group");
+    std::unique_lock<std::mutex> l(g->m);
+    if (!valid_member(g, member) || !g->in_round[member])
+        return fail("kernel_step_group_end: member %d is not in a round", member);
+    g->in_round[member] = 0;
+    g->round_left--;
+    if (g->round_left == 0) {
+        g->round_active = false;
+        g->call_open = false;
+        g->call_arrived = 0;
+        // members that began meanwhile count their straggler limit from now
+        if (g->n_pending > 0)
+            g->first_pending = Clock::now();
+    } else if (g->call_open && !g->call_running && !g->round_failed && g->call_arrived == g->round_left) {
+        // the members still in the round are all waiting at the open call: run it here
+        run_call(g, l);
+    }
+    g->cv.notify_all();
+    return 0;
+}
+
+extern "C" int kernel_step_group_attn(KernelStepGroup *g, int member, int site, const KernelAttnDecodeJob *job)
+{
+    if (!job)
+        return fail("kernel_step_group_attn: null job");
+    return rendezvous(g, member, kAttn, site, "kernel_step_group_attn",
+                      [&](KernelStepGroup *G) { G->attn.push_back(*job); });
+}
+
+extern "C" int kernel_step_group_delta(KernelStepGroup *g, int member, int site, const KernelDeltaStepJob *job)
+{
+    if (!job)
+        return fail("kernel_step_group_delta: null job");
+    return rendezvous(g, member, kDelta, site, "kernel_step_group_delta",
+                      [&](KernelStepGroup *G) { G->delta.push_back(*job); });
+}
+
+extern "C" int kernel_step_group_matvec(KernelStepGroup *g, int member, int site, const KernelCudaMatvecJob *jobs, int n)
+{
+    if (!jobs || n < 1)
+        return fail("kernel_step_group_matvec: bad job array");
+    return rendezvous(g, member, kMatvec, site, "kernel_step_group_matvec", [&](KernelStepGroup *G) {
+        for (int i = 0; i < n; i++)
+            G->mv.push_back(Entry{member, jobs[i]});
+    });
+}
+
+extern "C" int kernel_step_group_lock(KernelStepGroup *g)
+{
+    if (!g)
+        return fail("kernel_step_group_lock: null group");
+    fifo_lock(g);
+    return 0;
+}
+
+extern "C" int kernel_step_group_unlock(KernelStepGroup *g)
+{
+    if (!g)
+        return fail("kernel_step_group_unlock: null group");
+    fifo_unlock(g);
+    return 0;
+}
+
+extern "C" int kernel_step_group_stats(const KernelStepGroup *g, KernelStepGroupStats *out)
+{
+    if (!g || !out)
+        return fail("kernel_step_group_stats: null argument");
+    std::lock_guard<std::mutex> l(g->m);
+    *out = g->st;
+    return 0;
+}
