@@ -9,14 +9,18 @@
 // tokens of one multi-token product, gathered into a contiguous [T][cols] block by one copy-list
 // launch, multiplied by kernel_cuda_matmul_quant_batch, and scattered back by a second launch.
 //
-// Host side: one mutex guards the membership, the round and the open call. Members waiting for
-// a call to complete sleep on a futex on the call generation, so the completion wakes them all at
-// once without each re-taking the mutex (with tens of slot threads, waking them one by one
-// through a condition variable's mutex cost more than the device work of a layer). Every wait is
-// bounded (straggler limit for a round to form, call timeout for a call to fill, the same timeout
-// for a round to end). Device batches run with the group mutex released
-// and the group's FIFO lock (the FairLock counterpart) held, so work outside rounds that takes
-// the same lock never overlaps them.
+// Host side. Arrival at a call is lock-free: a member writes its jobs into its own slot, then
+// adds one to a single atomic word that packs (failed bit, members left in the round, members
+// arrived at the open call); the arrival that makes arrived == left runs the batch, and so does
+// an early kernel_step_group_end that makes left == arrived. Members waiting for a call sleep on
+// a futex on the call generation, so its completion wakes them all at once. (With 64 slot
+// threads on 16 host cores, arrivals through a mutex cost about 2.5 us each, in series: more
+// than the device work of a layer.) A mutex guards only membership and round formation. Every
+// wait is bounded: the straggler limit for a round to form, the call timeout for a call to fill
+// (a waiter past it marks the call failed with a compare-and-swap that cannot succeed once the
+// batch has a runner), the same timeout without progress for a running round to end. Device
+// batches run under the group's FIFO lock (the FairLock counterpart), so work outside rounds
+// that takes the same lock never overlaps them.
 #include "runtime.h"
 #include "../../include/roaster_cuda.h"
 
@@ -39,7 +43,7 @@ namespace {
 
 using Clock = std::chrono::steady_clock;
 
-constexpr int kCopyMax = 256;   // copy-list entries per launch (6 KB of parameters)
+constexpr int kCopyMax = 512;   // copy-list entries per launch (10 KB of parameters)
 
 struct CopyList {
     const float *src[kCopyMax];
@@ -72,6 +76,20 @@ struct Entry {
     KernelCudaMatvecJob job;
 };
 
+// One member's submission to the open call (its own cache lines: no false sharing).
+struct alignas(64) MemberSlot {
+    uint64_t gen = ~0ull;            // call generation these jobs belong to
+    int kind = 0, site = 0;
+    KernelAttnDecodeJob attn;
+    KernelDeltaStepJob delta;
+    std::vector<KernelCudaMatvecJob> mv;
+};
+
+constexpr uint64_t kFailed = 1ull << 63;
+constexpr uint64_t kLeftOne = 1ull << 32;
+inline uint32_t w_arrived(uint64_t w) { return (uint32_t)w; }
+inline uint32_t w_left(uint64_t w) { return (uint32_t)(w >> 32) & 0x7FFFFFFFu; }
+
 }  // namespace
 
 struct KernelStepGroup {
@@ -79,39 +97,34 @@ struct KernelStepGroup {
     long long straggler_us = 0;
     long long timeout_us = 0;
 
+    // membership and round formation (mutex)
     mutable std::mutex m;
     std::condition_variable cv;
     std::vector<char> joined, pending, in_round;
     int n_joined = 0, n_pending = 0;
     Clock::time_point first_pending;
-
     bool round_active = false;
-    bool round_failed = false;
-    int round_left = 0;              // members of the round that have not ended
-    uint64_t round_id = 0;
+    int round_size = 0, round_ended = 0;
+    std::atomic<uint64_t> round_id{0};
 
-    // the open call of the round (at most one: a member moves on only when its call completes)
-    bool call_open = false;
-    bool call_running = false;
-    int call_kind = 0, call_site = 0, call_arrived = 0;
-    uint64_t call_gen = 0;           // completed calls
-    int call_status[16] = {};        // status of call generation g at [g & 15]
-    std::atomic<uint32_t> gen_word{0};   // low bits of call_gen, the futex the call waiters sleep on
-    Clock::time_point call_deadline;
-    std::vector<KernelAttnDecodeJob> attn;
-    std::vector<KernelDeltaStepJob> delta;
-    std::vector<Entry> mv;
+    // calls (lock-free arrival)
+    std::vector<MemberSlot> slot;
+    std::atomic<uint64_t> word{0};           // kFailed | left << 32 | arrived
+    std::atomic<bool> round_failed{false};
+    std::atomic<uint64_t> call_gen{0};       // completed (or failed) calls
+    std::atomic<uint32_t> gen_word{0};       // low bits of call_gen: the futex call waiters sleep on
+    int call_status[16] = {};                // status of call generation c at [c & 15]
 
     // FIFO lock (ticket), the counterpart of the reference's FairLock
     std::mutex lm;
     std::condition_variable lc;
     unsigned long long next_ticket = 0, serving = 0;
 
-    // device staging of merged projections (grow-only)
+    // device staging of merged projections (grow-only; used by the runner under the FIFO lock)
     float *xbuf = nullptr, *ybuf = nullptr;
     size_t xcap = 0, ycap = 0;
 
-    KernelStepGroupStats st{};
+    KernelStepGroupStats st{};               // under m
 };
 
 namespace {
@@ -143,22 +156,16 @@ void futex_wake_all(std::atomic<uint32_t> *w)
     syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAKE_PRIVATE, INT_MAX, nullptr, nullptr, 0);
 }
 
-// Close the open call with status rc and wake its waiters. Group mutex held.
-void complete(KernelStepGroup *g, int rc)
+// Publish the result of call generation `gen` and wake its waiters. Only the call's runner (or
+// the waiter that failed it) calls this, once per call.
+void complete(KernelStepGroup *g, uint64_t gen, int rc, uint64_t next_word)
 {
-    g->call_gen++;
-    g->call_status[g->call_gen & 15] = rc;
-    g->call_open = false;
-    g->call_running = false;
-    g->call_arrived = 0;
-    g->gen_word.store((uint32_t)g->call_gen, std::memory_order_release);
+    g->call_status[(gen + 1) & 15] = rc;
+    g->call_gen.store(gen + 1, std::memory_order_release);
+    g->word.store(next_word, std::memory_order_release);
+    g->gen_word.store((uint32_t)(gen + 1), std::memory_order_release);
     futex_wake_all(&g->gen_word);
     g->cv.notify_all();   // begin() watches the progress of a running round
-}
-
-bool valid_member(const KernelStepGroup *g, int member)
-{
-    return member >= 0 && member < g->max_members && g->joined[member];
 }
 
 int grow(float **buf, size_t *cap, size_t floats)
@@ -269,99 +276,123 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
     return copy_list(ss, sd, sn);
 }
 
-// Run the open call's batch. Called with the group mutex held by `l`; releases it around the
-// device work (every member of the call is waiting, so nothing changes the call meanwhile).
-void run_call(KernelStepGroup *g, std::unique_lock<std::mutex> &l)
+// Run call generation `gen`: every member still in the round has submitted to its slot. The
+// caller is the unique runner (its atomic update of the word made arrived == left).
+void run_call(KernelStepGroup *g, uint64_t gen)
 {
-    g->call_running = true;
-    const int kind = g->call_kind;
     std::vector<KernelAttnDecodeJob> attn;
     std::vector<KernelDeltaStepJob> delta;
     std::vector<Entry> mv;
-    attn.swap(g->attn);
-    delta.swap(g->delta);
-    mv.swap(g->mv);
-    g->attn.reserve(attn.size());      // the next call of the round is usually the same size
-    g->delta.reserve(delta.size());
-    g->mv.reserve(mv.size());
-    const size_t njobs = kind == kAttn ? attn.size() : kind == kDelta ? delta.size() : mv.size();
+    int kind = 0, site = 0, mismatch = 0, n = 0;
+    for (int i = 0; i < g->max_members; i++) {
+        const MemberSlot &s = g->slot[i];
+        if (s.gen != gen)
+            continue;
+        if (n++ == 0) {
+            kind = s.kind;
+            site = s.site;
+        } else if (s.kind != kind || s.site != site) {
+            mismatch = 1;
+        }
+        if (s.kind == kAttn)
+            attn.push_back(s.attn);
+        else if (s.kind == kDelta)
+            delta.push_back(s.delta);
+        else
+            for (const KernelCudaMatvecJob &j : s.mv)
+                mv.push_back(Entry{i, j});
+    }
     KernelStepGroupStats plan{};
-    l.unlock();
-    fifo_lock(g);
     int rc = 0;
-    if (kind == kAttn)
-        rc = kernel_attn_decode_batch(attn.data(), (int)attn.size());
-    else if (kind == kDelta)
-        rc = kernel_deltanet_step_batch(delta.data(), (int)delta.size());
-    else
-        rc = run_matvec(g, mv, &plan);
-    fifo_unlock(g);
-    l.lock();
-    g->st.calls++;
-    g->st.jobs += njobs;
-    g->st.products += plan.products;
-    g->st.merged_jobs += plan.merged_jobs;
-    if (rc != 0)
-        g->st.errors++;
-    complete(g, rc);
+    if (mismatch) {
+        rc = fail("kernel_step_group: members of a round reached different calls (site %d and others)", site);
+        g->round_failed.store(true, std::memory_order_release);
+    } else {
+        fifo_lock(g);
+        if (kind == kAttn)
+            rc = kernel_attn_decode_batch(attn.data(), (int)attn.size());
+        else if (kind == kDelta)
+            rc = kernel_deltanet_step_batch(delta.data(), (int)delta.size());
+        else
+            rc = run_matvec(g, mv, &plan);
+        fifo_unlock(g);
+    }
+    {
+        std::lock_guard<std::mutex> l(g->m);
+        if (!mismatch) {
+            g->st.calls++;
+            g->st.jobs += kind == kAttn ? attn.size() : kind == kDelta ? delta.size() : mv.size();
+            g->st.products += plan.products;
+            g->st.merged_jobs += plan.merged_jobs;
+        }
+        if (rc != 0)
+            g->st.errors++;
+    }
+    // nobody else can change the word now: every member still in the round is waiting here
+    const uint64_t w = g->word.load(std::memory_order_acquire);
+    complete(g, gen, rc, w & ~(uint64_t)0xFFFFFFFFu);
 }
 
-// Fail the open call for every member in it and the rest of the round.
-void fail_call(KernelStepGroup *g)
+// A waiter past its deadline: fail call `gen` unless it completed or has its runner.
+void try_fail(KernelStepGroup *g, uint64_t gen, int site, const char *what)
 {
-    g->round_failed = true;
-    g->attn.clear();
-    g->delta.clear();
-    g->mv.clear();
-    g->st.errors++;
-    complete(g, -1);
+    for (;;) {
+        uint64_t w = g->word.load(std::memory_order_acquire);
+        if (g->call_gen.load(std::memory_order_acquire) != gen)
+            return;                                  // completed meanwhile
+        if ((w & kFailed) || w_arrived(w) == w_left(w))
+            return;                                  // already failed, or the batch is running
+        const uint64_t seen = w;
+        if (g->word.compare_exchange_weak(w, seen | kFailed, std::memory_order_acq_rel)) {
+            fail("%s: not every member reached call site %d within the call timeout", what, site);
+            g->round_failed.store(true, std::memory_order_release);
+            {
+                std::lock_guard<std::mutex> l(g->m);
+                g->st.errors++;
+            }
+            // the failed bit stays until the round ends: late arrivals return at once
+            complete(g, gen, -1, (seen & ~(uint64_t)0xFFFFFFFFu) | kFailed);
+            return;
+        }
+    }
 }
 
-template <typename Add>
-int rendezvous(KernelStepGroup *g, int member, int kind, int site, const char *what, Add add)
+template <typename Fill>
+int rendezvous(KernelStepGroup *g, int member, int kind, int site, const char *what, Fill fill)
 {
     if (!g)
         return fail("%s: null group", what);
-    std::unique_lock<std::mutex> l(g->m);
-    if (!valid_member(g, member) || !g->in_round[member])
+    // joined / in_round of this member change only on this member's own thread
+    if (member < 0 || member >= g->max_members || !g->joined[member] || !g->in_round[member])
         return fail("%s: member %d is not in a round", what, member);
-    if (g->round_failed)
+    if (g->round_failed.load(std::memory_order_acquire))
         return fail("%s: an earlier call of this round failed", what);
-    if (g->call_open && (g->call_kind != kind || g->call_site != site)) {
-        fail("%s: members reached different calls (kind %d site %d vs kind %d site %d)", what, kind, site,
-             g->call_kind, g->call_site);
-        fail_call(g);
-        return -1;
+    // the open call cannot complete before this member arrives (it can only fail)
+    const uint64_t gen = g->call_gen.load(std::memory_order_acquire);
+    MemberSlot &s = g->slot[member];
+    s.kind = kind;
+    s.site = site;
+    fill(s);
+    s.gen = gen;
+    const uint64_t w = g->word.fetch_add(1, std::memory_order_acq_rel) + 1;
+    if (w & kFailed) {
+        s.gen = ~0ull;   // never part of a later call (the next round forms after this member ends)
+        return fail("%s: an earlier call of this round failed", what);
     }
-    if (!g->call_open) {
-        g->call_open = true;
-        g->call_kind = kind;
-        g->call_site = site;
-        g->call_arrived = 0;
-        g->call_deadline = Clock::now() + std::chrono::microseconds(g->timeout_us);
-    }
-    add(g);
-    g->call_arrived++;
-    const uint64_t gen = g->call_gen;
-    if (g->call_arrived == g->round_left) {
-        run_call(g, l);
+    if (w_arrived(w) == w_left(w)) {
+        run_call(g, gen);
         return g->call_status[(gen + 1) & 15];
     }
-    const Clock::time_point deadline = g->call_deadline;
-    l.unlock();
-    // the status of call gen + 1 is written before gen_word moves (release / acquire)
+    const Clock::time_point deadline = Clock::now() + std::chrono::microseconds(g->timeout_us);
     while (g->gen_word.load(std::memory_order_acquire) == (uint32_t)gen) {
         futex_wait(&g->gen_word, (uint32_t)gen, 2000000L);   // 2 ms slices
-        if (g->gen_word.load(std::memory_order_acquire) != (uint32_t)gen || Clock::now() < deadline)
-            continue;
-        l.lock();
-        if (g->call_gen == gen && !g->call_running) {   // a running batch always completes
-            fail("%s: not every member reached call site %d within the call timeout", what, site);
-            fail_call(g);
-        }
-        l.unlock();
+        if (g->gen_word.load(std::memory_order_acquire) == (uint32_t)gen && Clock::now() >= deadline)
+            try_fail(g, gen, site, what);
     }
-    return g->call_status[(gen + 1) & 15];
+    const int rc = g->call_status[(gen + 1) & 15];
+    if (rc != 0)
+        fail("%s: the combined call failed", what);
+    return rc;
 }
 
 }  // namespace
@@ -379,6 +410,7 @@ extern "C" KernelStepGroup *kernel_step_group_create(int max_members, long long 
     g->joined.assign(max_members, 0);
     g->pending.assign(max_members, 0);
     g->in_round.assign(max_members, 0);
+    g->slot = std::vector<MemberSlot>(max_members);
     return g;
 }
 
@@ -416,7 +448,7 @@ extern "C" int kernel_step_group_leave(KernelStepGroup *g, int member)
     if (!g)
         return fail("kernel_step_group_leave: null group");
     std::lock_guard<std::mutex> l(g->m);
-    if (!valid_member(g, member))
+    if (member < 0 || member >= g->max_members || !g->joined[member])
         return fail("kernel_step_group_leave: member %d is not joined", member);
     if (g->in_round[member])
         return fail("kernel_step_group_leave: member %d is inside a round (end it first)", member);
@@ -436,7 +468,7 @@ extern "C" int kernel_step_group_begin(KernelStepGroup *g, int member)
     if (!g)
         return fail("kernel_step_group_begin: null group");
     std::unique_lock<std::mutex> l(g->m);
-    if (!valid_member(g, member))
+    if (member < 0 || member >= g->max_members || !g->joined[member])
         return fail("kernel_step_group_begin: member %d is not joined", member);
     if (g->in_round[member] || g->pending[member])
         return fail("kernel_step_group_begin: member %d has already begun", member);
@@ -446,38 +478,44 @@ extern "C" int kernel_step_group_begin(KernelStepGroup *g, int member)
     g->cv.notify_all();
     // bound on waiting for a running round: a call timeout without any progress of that round
     Clock::time_point give_up = Clock::now() + std::chrono::microseconds(g->timeout_us);
-    uint64_t seen_gen = g->call_gen, seen_round = g->round_id;
+    uint64_t seen_gen = g->call_gen.load(), seen_round = g->round_id.load();
     for (;;) {
-        if (g->call_gen != seen_gen || g->round_id != seen_round) {
-            seen_gen = g->call_gen;
-            seen_round = g->round_id;
+        const uint64_t cg = g->call_gen.load(), rid = g->round_id.load();
+        if (cg != seen_gen || rid != seen_round) {
+            seen_gen = cg;
+            seen_round = rid;
             give_up = Clock::now() + std::chrono::microseconds(g->timeout_us);
         }
         if (g->in_round[member])
-            return g->round_left;
+            return g->round_size;
         if (!g->round_active) {
             const Clock::time_point form = g->first_pending + std::chrono::microseconds(g->straggler_us);
             if (g->n_pending == g->n_joined || Clock::now() >= form) {
                 g->round_active = true;
-                g->round_failed = false;
-                g->round_id++;
-                g->round_left = g->n_pending;
+                g->round_size = g->n_pending;
+                g->round_ended = 0;
                 for (int i = 0; i < g->max_members; i++)
                     if (g->pending[i]) {
                         g->pending[i] = 0;
                         g->in_round[i] = 1;
                     }
                 g->n_pending = 0;
+                g->round_failed.store(false, std::memory_order_relaxed);
+                g->word.store((uint64_t)g->round_size << 32, std::memory_order_release);
+                g->round_id.fetch_add(1);
                 g->st.rounds++;
-                if (g->round_left > g->st.max_round)
-                    g->st.max_round = g->round_left;
+                if (g->round_size > g->st.max_round)
+                    g->st.max_round = g->round_size;
                 g->cv.notify_all();
-                return g->round_left;
+                return g->round_size;
             }
             g->cv.wait_until(l, form);
         } else {
-            if (g->cv.wait_until(l, give_up) == std::cv_status::timeout && !g->in_round[member] && g->round_active &&
-                g->call_gen == seen_gen && g->round_id == seen_round) {
+            // completions notify without the mutex, so poll in short slices as well
+            const Clock::time_point slice = Clock::now() + std::chrono::milliseconds(2);
+            g->cv.wait_until(l, give_up < slice ? give_up : slice);
+            if (Clock::now() >= give_up && !g->in_round[member] && g->round_active &&
+                g->call_gen.load() == seen_gen && g->round_id.load() == seen_round) {
                 g->pending[member] = 0;
                 if (--g->n_pending == 0)
                     g->first_pending = Clock::time_point();
@@ -492,22 +530,24 @@ extern "C" int kernel_step_group_end(KernelStepGroup *g, int member)
     if (!g)
         return fail("kernel_step_group_end: null group");
     std::unique_lock<std::mutex> l(g->m);
-    if (!valid_member(g, member) || !g->in_round[member])
+    if (member < 0 || member >= g->max_members || !g->joined[member] || !g->in_round[member])
         return fail("kernel_step_group_end: member %d is not in a round", member);
     g->in_round[member] = 0;
-    g->round_left--;
-    if (g->round_left == 0) {
+    const uint64_t w = g->word.fetch_sub(kLeftOne, std::memory_order_acq_rel) - kLeftOne;
+    if (++g->round_ended == g->round_size) {
         g->round_active = false;
-        g->call_open = false;
-        g->call_arrived = 0;
-        // members that began meanwhile count their straggler limit from now
-        if (g->n_pending > 0)
+        g->word.store(0, std::memory_order_release);
+        if (g->n_pending > 0)   // members that began meanwhile count their straggler limit from now
             g->first_pending = Clock::now();
-    } else if (g->call_open && !g->call_running && !g->round_failed && g->call_arrived == g->round_left) {
-        // the members still in the round are all waiting at the open call: run it here
-        run_call(g, l);
+        g->cv.notify_all();
+        return 0;
     }
     g->cv.notify_all();
+    const bool runner = !(w & kFailed) && w_arrived(w) > 0 && w_arrived(w) == w_left(w);
+    const uint64_t gen = g->call_gen.load(std::memory_order_acquire);
+    l.unlock();
+    if (runner)   // the members still in the round are all waiting at the open call
+        run_call(g, gen);
     return 0;
 }
 
@@ -515,26 +555,22 @@ extern "C" int kernel_step_group_attn(KernelStepGroup *g, int member, int site, 
 {
     if (!job)
         return fail("kernel_step_group_attn: null job");
-    return rendezvous(g, member, kAttn, site, "kernel_step_group_attn",
-                      [&](KernelStepGroup *G) { G->attn.push_back(*job); });
+    return rendezvous(g, member, kAttn, site, "kernel_step_group_attn", [&](MemberSlot &s) { s.attn = *job; });
 }
 
 extern "C" int kernel_step_group_delta(KernelStepGroup *g, int member, int site, const KernelDeltaStepJob *job)
 {
     if (!job)
         return fail("kernel_step_group_delta: null job");
-    return rendezvous(g, member, kDelta, site, "kernel_step_group_delta",
-                      [&](KernelStepGroup *G) { G->delta.push_back(*job); });
+    return rendezvous(g, member, kDelta, site, "kernel_step_group_delta", [&](MemberSlot &s) { s.delta = *job; });
 }
 
 extern "C" int kernel_step_group_matvec(KernelStepGroup *g, int member, int site, const KernelCudaMatvecJob *jobs, int n)
 {
     if (!jobs || n < 1)
         return fail("kernel_step_group_matvec: bad job array");
-    return rendezvous(g, member, kMatvec, site, "kernel_step_group_matvec", [&](KernelStepGroup *G) {
-        for (int i = 0; i < n; i++)
-            G->mv.push_back(Entry{member, jobs[i]});
-    });
+    return rendezvous(g, member, kMatvec, site, "kernel_step_group_matvec",
+                      [&](MemberSlot &s) { s.mv.assign(jobs, jobs + n); });
 }
 
 extern "C" int kernel_step_group_lock(KernelStepGroup *g)

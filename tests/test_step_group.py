@@ -241,6 +241,36 @@ def test_many_members_many_rounds():
     g.close()
 
 
+def test_members_ending_at_random_points():
+    """Members end their step after a random number of calls (a slot whose step failed). The
+    others never wait for them: call c of a round runs once, as soon as every member still in
+    the round has reached it, so a round runs max(calls made) batches carrying sum(calls made)."""
+    M, ROUNDS, CALLS = 32, 20, 6
+    g = R.StepGroup(M, straggler_us=10_000_000, call_timeout_ms=20000)
+    ids = [g.join() for _ in range(M)]
+    rng = np.random.default_rng(1)
+    made = rng.integers(0, CALLS + 1, size=(ROUNDS, M))
+    made[:, 0] = CALLS                      # at least one member makes every call
+    jitter = rng.uniform(0, 0.002, size=(ROUNDS, M))
+
+    def member(i):
+        m = ids[i]
+        for r in range(ROUNDS):
+            assert g.begin(m) == M
+            for c in range(int(made[r, i])):
+                if c == 2:
+                    time.sleep(jitter[r, i])
+                assert g.delta(m, c, R.KernelDeltaStepJob()) == -1
+            assert g.end(m) == 0
+
+    _run(M, member)
+    st = g.stats()
+    assert st["rounds"] == ROUNDS
+    assert st["calls"] == ROUNDS * CALLS
+    assert st["jobs"] == int(made.sum())
+    g.close()
+
+
 # ----------------------------------------------------------------------------------- GPU
 
 def _slots(torch, n, seed):
