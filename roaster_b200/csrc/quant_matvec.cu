@@ -1210,9 +1210,10 @@ struct TJob {
     const uint4 *bq;            // B quarter tiles [token tile][quarter][16 KB]
     const uint4 *bsum;          // Q4_K sums tiles [token tile][block][4 KB]
     const int *e;               // per token: activation scale exponent
-    float *y;                   // [T][rows]
+    float *y;                   // [T][rows]: the result, or (raw) this part's unscaled partial plane
     long long item0;
     int rows, nb, T, rtiles, ctiles;
+    int kb0, nbt, raw;          // first block of this part, blocks per row, 1 = partial plane
 };
 
 struct TParams {
@@ -1367,7 +1368,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
     const TJob &J = p.jobs[j];
     const long long it = (long long)blockIdx.x - J.item0;
     const int rt = (int)(it % J.rtiles), ct = (int)(it / J.rtiles);
-    const int nb = J.nb, nq = 4 * nb;
+    const int nb = J.nb, nq = 4 * nb, kb0 = J.kb0, nqt = 4 * J.nbt;   // this part's blocks kb0 .. kb0 + nb - 1
     unsigned long long *bars = reinterpret_cast<unsigned long long *>(gb + Cfg::kOffBar);
     auto BAR = [&](int i) -> uint32_t { return smem_addr(&bars[i]); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[kSlot]);
@@ -1417,8 +1418,8 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                     break;
                 }
                 mbar_arrive_expect_tx(BAR(kBFull + s), (uint32_t)kTile);
-                bulk_g2s(base + Cfg::kOffB + s * kTile, J.bq + ((size_t)ct * nq + g) * (kTile / 16), (uint32_t)kTile,
-                         BAR(kBFull + s));
+                bulk_g2s(base + Cfg::kOffB + s * kTile, J.bq + ((size_t)ct * nqt + 4 * kb0 + g) * (kTile / 16),
+                         (uint32_t)kTile, BAR(kBFull + s));
                 nst[s]++;
             }
             if (!ok)
@@ -1437,7 +1438,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                     break;
                 }
                 mbar_arrive_expect_tx(BAR(kRawFull + r), (uint32_t)Cfg::kRaw);
-                const int x = Q6 ? (210 * b) & ~15 : 144 * b;
+                const int x = Q6 ? (210 * (kb0 + b)) & ~15 : 144 * (kb0 + b);
                 tma_load_2d(base + Cfg::kOffRaw + r * Cfg::kRaw, J.map, x, row0, BAR(kRawFull + r));
                 nraw[r]++;
             }
@@ -1454,8 +1455,8 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                     break;
                 }
                 mbar_arrive_expect_tx(BAR(kMnFullB + (b & 1)), 4096u);
-                bulk_g2s(base + Cfg::kOffMin + (b & 1) * Cfg::kMin + 4096, J.bsum + ((size_t)ct * nb + b) * 256, 4096u,
-                         BAR(kMnFullB + (b & 1)));
+                bulk_g2s(base + Cfg::kOffMin + (b & 1) * Cfg::kMin + 4096, J.bsum + ((size_t)ct * J.nbt + kb0 + b) * 256,
+                         4096u, BAR(kMnFullB + (b & 1)));
                 nsum[b & 1]++;
             }
             if (!ok)
@@ -1581,7 +1582,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                 for (int i = 0; i < 32; i++) {
                     const int t = ct * kTok + 32 * half + i;
                     if (t < J.T)
-                        J.y[(size_t)t * J.rows + row] = acc[i] * ldexpf(1.f, -J.e[t]);
+                        J.y[(size_t)t * J.rows + row] = J.raw ? acc[i] : acc[i] * ldexpf(1.f, -J.e[t]);
                 }
             }
         } else if (lane == 0) {
@@ -1598,7 +1599,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
                 break;
             }
             const unsigned char *raw = gb + Cfg::kOffRaw + rr * Cfg::kRaw;
-            const int mis = Q6 ? (210 * b) & 15 : 0;
+            const int mis = Q6 ? (210 * (kb0 + b)) & 15 : 0;
             // per-row tables of the block
             if (b >= 2) {
                 const uint32_t ph = (uint32_t)((b >> 1) - 1) & 1u;
@@ -2106,7 +2107,6 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         size_t cols, T, off_bq, off_bsum, off_e;
     };
     std::vector<XEnt> xe;
-    std::vector<int> xidx[2];
     auto eligible = [](const KernelCudaMatmulJob &j) {
         const long long rb = (long long)(j.cols / 256) * (j.is_q6 ? 210 : 144);
         return j.T >= 64 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && j.rows < (1u << 30) &&
@@ -2118,6 +2118,13 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
             tiles += (long long)((jobs[i].rows + tcm::kRows - 1) / tcm::kRows) *
                      (long long)((jobs[i].T + tcm::kTok - 1) / tcm::kTok);
     const bool use_tc = tiles >= 64;
+    struct Sel {
+        const KernelCudaMatmulJob *j;
+        const CUtensorMap *map;
+        int x, nb, rtiles, ctiles;
+    };
+    std::vector<Sel> sel[2];
+    long long ftiles[2] = {0, 0};
     for (int i = 0; i < n; i++) {
         const KernelCudaMatmulJob &j = jobs[i];
         const int nb = (int)(j.cols / 256);
@@ -2138,14 +2145,31 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
                                          j.is_q6 ? kQ6Slot : kQ4Slot, tcm::kRows);
         if (!map)
             return -1;
-        TParams &P = tp[j.is_q6 ? 1 : 0];
         const int rtiles = (int)((j.rows + tcm::kRows - 1) / tcm::kRows), ctiles = (int)((j.T + tcm::kTok - 1) / tcm::kTok);
-        P.jobs[P.njobs++] = TJob{map, nullptr, nullptr, nullptr, j.Y, P.items, (int)j.rows, nb, (int)j.T, rtiles, ctiles};
-        P.items += (long long)rtiles * ctiles;
-        xidx[j.is_q6 ? 1 : 0].push_back(x);
+        sel[j.is_q6 ? 1 : 0].push_back(Sel{&j, map, x, nb, rtiles, ctiles});
+        ftiles[j.is_q6 ? 1 : 0] += (long long)rtiles * ctiles;
     }
     if (xe.empty())
         return 0;
+    // Split along the blocks when a format's launch has fewer tiles than SMs (a few jobs of 64
+    // tokens, e.g. one layer's projections for a round of slots): part h of a job takes blocks
+    // [h nb / P, (h + 1) nb / P), at least 2 each, and writes an unscaled partial plane; the
+    // reduce launch sums the planes in part order, so results repeat bit for bit.
+    int split[2] = {1, 1};
+    size_t part_floats = 0;
+    for (int k = 0; k < 2; k++) {
+        if (sel[k].empty() || ftiles[k] >= R.num_sms)
+            continue;
+        int minb = 1 << 30;
+        for (const Sel &q : sel[k])
+            minb = std::min(minb, q.nb);
+        int P = (int)std::min<long long>(R.num_sms / ftiles[k], minb / 2);
+        P = std::min(P, kMaxJobs / (int)sel[k].size());
+        split[k] = std::max(1, P);
+        if (split[k] > 1)
+            for (const Sel &q : sel[k])
+                part_floats += (size_t)split[k] * q.j->T * q.j->rows;
+    }
     if (tp[0].items >= (1ll << 31) || tp[1].items >= (1ll << 31))
         return fail("kernel_cuda_matmul_quant_batch: too many tiles in one call");
     // scratch per distinct X: B quarter tiles [token tile][quarter][16 KB], sums tiles
@@ -2160,9 +2184,40 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         e.off_e = total;
         total += (e.T * sizeof(int) + 255) / 256 * 256;
     }
+    const size_t off_part = total;
+    total += part_floats * sizeof(float);
     unsigned char *ws = static_cast<unsigned char *>(scratch(total));
     if (!ws)
         return -1;
+    RParams rp;
+    memset(static_cast<void *>(&rp), 0, sizeof(rp));
+    {
+        float *part = reinterpret_cast<float *>(ws + off_part);
+        for (int k = 0; k < 2; k++) {
+            TParams &P = tp[k];
+            const int S = split[k];
+            for (const Sel &q : sel[k]) {
+                const KernelCudaMatmulJob &j = *q.j;
+                const XEnt &e = xe[q.x];
+                const long long plane = (long long)j.T * j.rows;
+                for (int h = 0; h < S; h++) {
+                    const int b0 = h * q.nb / S, b1 = (h + 1) * q.nb / S;
+                    P.jobs[P.njobs++] = TJob{q.map, reinterpret_cast<const uint4 *>(ws + e.off_bq),
+                                             reinterpret_cast<const uint4 *>(ws + e.off_bsum),
+                                             reinterpret_cast<const int *>(ws + e.off_e), S > 1 ? part + h * plane : j.Y,
+                                             P.items, (int)j.rows, b1 - b0, (int)j.T, q.rtiles, q.ctiles, b0, q.nb,
+                                             S > 1 ? 1 : 0};
+                    P.items += (long long)q.rtiles * q.ctiles;
+                }
+                if (S > 1) {
+                    rp.jobs[rp.njobs++] = RJob{part, j.Y, reinterpret_cast<const int *>(ws + e.off_e), rp.n, (int)j.rows,
+                                               (int)j.T, S};
+                    rp.n += plane;
+                    part += S * plane;
+                }
+            }
+        }
+    }
     PParamsTc pp;
     memset(static_cast<void *>(&pp), 0, sizeof(pp));
     long long ctas = 0;
@@ -2180,12 +2235,6 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         TParams &P = tp[k];
         if (P.njobs == 0)
             continue;
-        for (int q = 0; q < P.njobs; q++) {
-            const XEnt &e = xe[xidx[k][q]];
-            P.jobs[q].bq = reinterpret_cast<const uint4 *>(ws + e.off_bq);
-            P.jobs[q].bsum = reinterpret_cast<const uint4 *>(ws + e.off_bsum);
-            P.jobs[q].e = reinterpret_cast<const int *>(ws + e.off_e);
-        }
         P.err = R.err_word;
         const int smem = k ? TcCfg<true>::kSmem : TcCfg<false>::kSmem;
         if (!attr[k]) {
@@ -2202,7 +2251,11 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         if (launched("quant_mm_tc_kernel") != 0)
             return -1;
     }
-    return 0;
+    if (rp.njobs == 0)
+        return 0;
+    const long long blocks = std::min<long long>((rp.n + 255) / 256, 8ll * R.num_sms);
+    quant_mm_reduce_kernel<<<(unsigned)blocks, 256, 0, R.stream>>>(rp);
+    return launched("quant_mm_reduce_kernel");
 }
 
 }  // namespace

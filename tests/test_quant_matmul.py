@@ -150,6 +150,34 @@ def test_matmul_tensor_core_path(rb, oracle_lib, q6, rows, cols, T):
     assert O.maxrel(host(Y), _ref(q6, m, X, rows, cols)) < TOL
 
 
+@pytest.mark.parametrize("layer", ["deltanet", "attention"])
+def test_matmul_layer_for_a_round_of_slots(rb, oracle_lib, layer):
+    """One layer's projections for 64 tokens (a round of 64 slots through the step group): the
+    tcgen05 launches have fewer tiles than SMs, so each job is split along its blocks into
+    parts whose partial planes are summed in part order (DeltaNet: the Q6_K ssm_out in 8 parts;
+    attention: Q4_K in 2, Q6_K in 4). Same bits on a repeat."""
+    T = 64
+    shapes = ([(False, 8192, 2048), (False, 4096, 2048), (False, 32, 2048), (False, 32, 2048), (True, 2048, 4096)]
+              if layer == "deltanet" else
+              [(False, 8192, 2048), (False, 512, 2048), (True, 512, 2048), (True, 2048, 4096)])
+    rng = np.random.default_rng(3)
+    Xs = {c: rng.standard_normal((T, c)).astype(np.float32) for c in (2048, 4096)}
+    dXs = {c: dev(x) for c, x in Xs.items()}
+    keep, jobs, refs = [], [], []
+    for i, (q6, rows, cols) in enumerate(shapes):
+        m = synth.quant_matrix(200 + i, rows, cols, q6)
+        dm, Y = dev(m), torch.zeros(T, rows, device="cuda")
+        keep.append((dm, Y))
+        jobs.append((q6, dm, dXs[cols], Y, rows, cols, T))
+        refs.append(_ref(q6, m, Xs[cols], rows, cols))
+    rb.matmul_quant_batch(jobs)
+    first = [Y.clone() for _, Y in keep]
+    rb.matmul_quant_batch(jobs)
+    for (_, Y), f, ref in zip(keep, first, refs):
+        assert torch.equal(f, Y)
+        assert O.maxrel(host(Y), ref) < TOL
+
+
 def test_matmul_mixed_sizes_one_call(rb, oracle_lib):
     """One call with jobs of very different sizes sharing one X (4096, 200 and 3 rows; both
     formats): the call's tiles are enough for the tcgen05 kernel, which takes all three, the
