@@ -12,10 +12,11 @@
 // Host side. Arrival at a call is lock-free: a member writes its jobs into its own slot, then
 // adds one to a single atomic word that packs (failed bit, members left in the round, members
 // arrived at the open call); the arrival that makes arrived == left runs the batch, and so does
-// an early kernel_step_group_end that makes left == arrived. Members waiting for a call sleep on
-// a futex on the call generation, so its completion wakes them all at once. (With 64 slot
-// threads on 16 host cores, arrivals through a mutex cost about 2.5 us each, in series: more
-// than the device work of a layer.) A mutex guards only membership and round formation. Every
+// an early kernel_step_group_end that makes left == arrived. Each waiting member sleeps on a
+// futex word in its own slot; the runner releases the first kWakeFan waiters and every released
+// member releases the next kWakeFan, so the wake-ups fan out over the host cores instead of
+// queueing inside one thread's wake call. (With 64 slot threads on 16 host cores, arrivals
+// through a mutex cost about 2.5 us each, in series: more than the device work of a layer.) A mutex guards only membership and round formation. Every
 // wait is bounded: the straggler limit for a round to form, the call timeout for a call to fill
 // (a waiter past it marks the call failed with a compare-and-swap that cannot succeed once the
 // batch has a runner), the same timeout without progress for a running round to end. Device
@@ -78,6 +79,8 @@ struct Entry {
 
 // One member's submission to the open call (its own cache lines: no false sharing).
 struct alignas(64) MemberSlot {
+    std::atomic<uint32_t> go{0};     // futex: low bits of gen + 1 once this member's call is done
+    int pos = 0;                     // place in the call's wake list
     uint64_t gen = ~0ull;            // call generation these jobs belong to
     int kind = 0, site = 0;
     KernelAttnDecodeJob attn;
@@ -112,8 +115,9 @@ struct KernelStepGroup {
     std::atomic<uint64_t> word{0};           // kFailed | left << 32 | arrived
     std::atomic<bool> round_failed{false};
     std::atomic<uint64_t> call_gen{0};       // completed (or failed) calls
-    std::atomic<uint32_t> gen_word{0};       // low bits of call_gen: the futex call waiters sleep on
     int call_status[16] = {};                // status of call generation c at [c & 15]
+    std::vector<int> wake_list;              // the waiters of the last call run, in release order
+    std::atomic<uint64_t> tree_gen{~0ull};   // the call generation wake_list belongs to
 
     // FIFO lock (ticket), the counterpart of the reference's FairLock
     std::mutex lm;
@@ -151,20 +155,46 @@ void futex_wait(std::atomic<uint32_t> *w, uint32_t v, long ns)
     syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAIT_PRIVATE, v, &ts, nullptr, 0);
 }
 
-void futex_wake_all(std::atomic<uint32_t> *w)
+constexpr int kWakeFan = 4;
+
+void release(KernelStepGroup *g, int member, uint64_t gen)
 {
-    syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAKE_PRIVATE, INT_MAX, nullptr, nullptr, 0);
+    MemberSlot &s = g->slot[member];
+    s.go.store((uint32_t)(gen + 1), std::memory_order_release);
+    syscall(SYS_futex, reinterpret_cast<uint32_t *>(&s.go), FUTEX_WAKE_PRIVATE, 1, nullptr, nullptr, 0);
 }
 
-// Publish the result of call generation `gen` and wake its waiters. Only the call's runner (or
-// the waiter that failed it) calls this, once per call.
-void complete(KernelStepGroup *g, uint64_t gen, int rc, uint64_t next_word)
+// A released waiter at place p of the wake list releases places kWakeFan (p + 1) .. + kWakeFan - 1
+// (the runner took places 0 .. kWakeFan - 1).
+void release_children(KernelStepGroup *g, int p, uint64_t gen)
+{
+    const int n = (int)g->wake_list.size();
+    for (int c = kWakeFan * (p + 1); c < kWakeFan * (p + 2) && c < n; c++)
+        release(g, g->wake_list[c], gen);
+}
+
+// Publish the result of call generation `gen` and release its waiters: through the wake tree
+// when `waiters` lists them, else (a failed call) every member whose slot is in the call. Only
+// the call's runner, or the waiter that failed it, calls this, once per call.
+void complete(KernelStepGroup *g, uint64_t gen, int rc, uint64_t next_word, std::vector<int> *waiters)
 {
     g->call_status[(gen + 1) & 15] = rc;
+    if (waiters) {
+        g->wake_list.swap(*waiters);
+        for (int k = 0; k < (int)g->wake_list.size(); k++)
+            g->slot[g->wake_list[k]].pos = k;
+        g->tree_gen.store(gen, std::memory_order_release);
+    }
     g->call_gen.store(gen + 1, std::memory_order_release);
     g->word.store(next_word, std::memory_order_release);
-    g->gen_word.store((uint32_t)(gen + 1), std::memory_order_release);
-    futex_wake_all(&g->gen_word);
+    if (waiters) {
+        for (int k = 0; k < kWakeFan && k < (int)g->wake_list.size(); k++)
+            release(g, g->wake_list[k], gen);
+    } else {
+        for (int i = 0; i < g->max_members; i++)
+            if (g->slot[i].gen == gen)
+                release(g, i, gen);
+    }
     g->cv.notify_all();   // begin() watches the progress of a running round
 }
 
@@ -278,16 +308,19 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
 
 // Run call generation `gen`: every member still in the round has submitted to its slot. The
 // caller is the unique runner (its atomic update of the word made arrived == left).
-void run_call(KernelStepGroup *g, uint64_t gen)
+void run_call(KernelStepGroup *g, uint64_t gen, int self)
 {
     std::vector<KernelAttnDecodeJob> attn;
     std::vector<KernelDeltaStepJob> delta;
     std::vector<Entry> mv;
+    std::vector<int> waiters;
     int kind = 0, site = 0, mismatch = 0, n = 0;
     for (int i = 0; i < g->max_members; i++) {
         const MemberSlot &s = g->slot[i];
         if (s.gen != gen)
             continue;
+        if (i != self)
+            waiters.push_back(i);
         if (n++ == 0) {
             kind = s.kind;
             site = s.site;
@@ -330,7 +363,7 @@ void run_call(KernelStepGroup *g, uint64_t gen)
     }
     // nobody else can change the word now: every member still in the round is waiting here
     const uint64_t w = g->word.load(std::memory_order_acquire);
-    complete(g, gen, rc, w & ~(uint64_t)0xFFFFFFFFu);
+    complete(g, gen, rc, w & ~(uint64_t)0xFFFFFFFFu, &waiters);
 }
 
 // A waiter past its deadline: fail call `gen` unless it completed or has its runner.
@@ -351,7 +384,7 @@ void try_fail(KernelStepGroup *g, uint64_t gen, int site, const char *what)
                 g->st.errors++;
             }
             // the failed bit stays until the round ends: late arrivals return at once
-            complete(g, gen, -1, (seen & ~(uint64_t)0xFFFFFFFFu) | kFailed);
+            complete(g, gen, -1, (seen & ~(uint64_t)0xFFFFFFFFu) | kFailed, nullptr);
             return;
         }
     }
@@ -380,15 +413,21 @@ int rendezvous(KernelStepGroup *g, int member, int kind, int site, const char *w
         return fail("%s: an earlier call of this round failed", what);
     }
     if (w_arrived(w) == w_left(w)) {
-        run_call(g, gen);
+        run_call(g, gen, member);
         return g->call_status[(gen + 1) & 15];
     }
     const Clock::time_point deadline = Clock::now() + std::chrono::microseconds(g->timeout_us);
-    while (g->gen_word.load(std::memory_order_acquire) == (uint32_t)gen) {
-        futex_wait(&g->gen_word, (uint32_t)gen, 2000000L);   // 2 ms slices
-        if (g->gen_word.load(std::memory_order_acquire) == (uint32_t)gen && Clock::now() >= deadline)
+    const uint32_t done = (uint32_t)(gen + 1);
+    for (;;) {
+        const uint32_t v = s.go.load(std::memory_order_acquire);
+        if (v == done)
+            break;
+        futex_wait(&s.go, v, 2000000L);   // 2 ms slices
+        if (s.go.load(std::memory_order_acquire) != done && Clock::now() >= deadline)
             try_fail(g, gen, site, what);
     }
+    if (g->tree_gen.load(std::memory_order_acquire) == gen)
+        release_children(g, s.pos, gen);
     const int rc = g->call_status[(gen + 1) & 15];
     if (rc != 0)
         fail("%s: the combined call failed", what);
@@ -547,7 +586,7 @@ extern "C" int kernel_step_group_end(KernelStepGroup *g, int member)
     const uint64_t gen = g->call_gen.load(std::memory_order_acquire);
     l.unlock();
     if (runner)   // the members still in the round are all waiting at the open call
-        run_call(g, gen);
+        run_call(g, gen, -1);
     return 0;
 }
 
