@@ -35,6 +35,7 @@
 #include <condition_variable>
 #include <cstring>
 #include <ctime>
+#include <sched.h>
 #include <mutex>
 #include <vector>
 
@@ -80,6 +81,7 @@ struct Entry {
 // One member's submission to the open call (its own cache lines: no false sharing).
 struct alignas(64) MemberSlot {
     std::atomic<uint32_t> go{0};     // futex: low bits of gen + 1 once this member's call is done
+    std::atomic<int> sleeping{0};    // 1 while the member may be asleep on `go`
     int pos = 0;                     // place in the call's wake list
     uint64_t gen = ~0ull;            // call generation these jobs belong to
     int kind = 0, site = 0;
@@ -155,13 +157,37 @@ void futex_wait(std::atomic<uint32_t> *w, uint32_t v, long ns)
     syscall(SYS_futex, reinterpret_cast<uint32_t *>(w), FUTEX_WAIT_PRIVATE, v, &ts, nullptr, 0);
 }
 
-constexpr int kWakeFan = 4;
+#ifndef STEP_GROUP_WAKE_FAN
+#define STEP_GROUP_WAKE_FAN 4
+#endif
+constexpr int kWakeFan = STEP_GROUP_WAKE_FAN;
+#ifndef STEP_GROUP_SPIN_US
+#define STEP_GROUP_SPIN_US 100
+#endif
+#ifndef STEP_GROUP_SPIN_YIELD
+#define STEP_GROUP_SPIN_YIELD 1
+#endif
+constexpr long long kSpinUs = STEP_GROUP_SPIN_US;     // spin before sleeping on a call
+constexpr bool kSpinYield = STEP_GROUP_SPIN_YIELD;   // yield the core on each spin
 
+inline void cpu_relax()
+{
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_ia32_pause();
+#elif defined(__aarch64__)
+    asm volatile("yield" ::: "memory");
+#endif
+}
+
+// Release one waiter. The wake system call is made only when the waiter may be asleep: with
+// sequentially consistent stores and loads on both sides (go then sleeping here, sleeping then
+// go in the waiter), either the waiter sees go or this side sees sleeping.
 void release(KernelStepGroup *g, int member, uint64_t gen)
 {
     MemberSlot &s = g->slot[member];
-    s.go.store((uint32_t)(gen + 1), std::memory_order_release);
-    syscall(SYS_futex, reinterpret_cast<uint32_t *>(&s.go), FUTEX_WAKE_PRIVATE, 1, nullptr, nullptr, 0);
+    s.go.store((uint32_t)(gen + 1), std::memory_order_seq_cst);
+    if (s.sleeping.load(std::memory_order_seq_cst))
+        syscall(SYS_futex, reinterpret_cast<uint32_t *>(&s.go), FUTEX_WAKE_PRIVATE, 1, nullptr, nullptr, 0);
 }
 
 // A released waiter at place p of the wake list releases places kWakeFan (p + 1) .. + kWakeFan - 1
@@ -418,11 +444,25 @@ int rendezvous(KernelStepGroup *g, int member, int kind, int site, const char *w
     }
     const Clock::time_point deadline = Clock::now() + std::chrono::microseconds(g->timeout_us);
     const uint32_t done = (uint32_t)(gen + 1);
+    // Spin first: a thread woken from a futex takes tens of microseconds to run again, which on a
+    // combined call of tens of members costs more than the device work of a layer.
+    const Clock::time_point spin_end = Clock::now() + std::chrono::microseconds(kSpinUs);
+    for (int i = 1; s.go.load(std::memory_order_acquire) != done; i++) {
+        if (kSpinYield)
+            sched_yield();
+        else
+            cpu_relax();
+        if ((i & 63) == 0 && Clock::now() >= spin_end)
+            break;
+    }
     for (;;) {
         const uint32_t v = s.go.load(std::memory_order_acquire);
         if (v == done)
             break;
-        futex_wait(&s.go, v, 2000000L);   // 2 ms slices
+        s.sleeping.store(1, std::memory_order_seq_cst);
+        if (s.go.load(std::memory_order_seq_cst) == v)
+            futex_wait(&s.go, v, 2000000L);   // 2 ms slices
+        s.sleeping.store(0, std::memory_order_relaxed);
         if (s.go.load(std::memory_order_acquire) != done && Clock::now() >= deadline)
             try_fail(g, gen, site, what);
     }
