@@ -75,14 +75,14 @@ def test_rounds_combine_every_call():
 
 def test_straggler_takes_next_round():
     """A round forms after the straggler limit with the members that have begun."""
-    g = R.StepGroup(3, straggler_us=50_000)
+    g = R.StepGroup(3, straggler_us=300_000)
     a, b, c = g.join(), g.join(), g.join()
     got = {}
 
     def member(i):
         m = (a, b, c)[i]
         if m == c:
-            time.sleep(0.4)
+            time.sleep(1.5)
         got[m] = g.begin(m)
         assert g.attn(m, 7, R.KernelAttnDecodeJob()) == -1
         assert g.end(m) == 0
