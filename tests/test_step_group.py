@@ -203,7 +203,7 @@ def test_fifo_lock_serves_in_arrival_order():
     g.lock()
 
     def taker(i):
-        time.sleep(0.05 * i)                 # arrive in index order while the lock is held
+        time.sleep(0.1 * i)                  # arrive in index order while the lock is held
         g.lock()
         order.append(i)
         g.unlock()
@@ -211,7 +211,7 @@ def test_fifo_lock_serves_in_arrival_order():
     ts = [threading.Thread(target=taker, args=(i,)) for i in range(4)]
     for t in ts:
         t.start()
-    time.sleep(0.4)
+    time.sleep(0.7)
     g.unlock()
     for t in ts:
         t.join(10)
