@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libroaster_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3,-fopenmp", "--expt-relaxed-constexpr"]
 
 
 def nvcc() -> str:
@@ -66,7 +66,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError("nvcc failed:\n" + "\n".join(failed))
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-Xcompiler", "-fPIC"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-Xcompiler", "-fPIC", "-lgomp"]
     out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("link failed:\n" + out.stdout + out.stderr)

@@ -1046,7 +1046,12 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
         const KernelAttnDecodeJob &s = jobs[i];
         if (!s.q || !s.gate || !s.out || !s.q_norm || (s.append && (!s.k_new || !s.v_new || !s.k_norm)))
             return fail("kernel_attn_decode_batch_host: job %d has a null pointer", i);
-        float *b = h + (size_t)i * in_f;
+    }
+    float *dev_in = static_cast<float *>(dstage(total * sizeof(float)));
+    if (!dev_in)
+        return -1;
+    const int in_ok = stage_in(h, dev_in, n, in_f, [&](int i, float *b) {
+        const KernelAttnDecodeJob &s = jobs[i];
         for (int r = 0; r < 16; r++) {
             memcpy(b + r * 256, s.q + r * s.qg_stride, 256 * 4);
             memcpy(b + 4096 + r * 256, s.gate + r * s.qg_stride, 256 * 4);
@@ -1057,12 +1062,8 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
             memcpy(b + 9472, s.k_norm, 256 * 4);
         }
         memcpy(b + 9216, s.q_norm, 256 * 4);
-    }
-    float *dev_in = static_cast<float *>(dstage(total * sizeof(float)));
-    if (!dev_in)
-        return -1;
-    cudaStream_t st = rt().stream;
-    if (check(cudaMemcpyAsync(dev_in, h, (size_t)n * in_f * 4, cudaMemcpyHostToDevice, st), "stage in") != 0)
+    });
+    if (in_ok != 0)
         return -1;
     float *dout = dev_in + (size_t)n * in_f;
     for (int i = 0; i < n; i++) {
@@ -1078,14 +1079,10 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
     }
     if (attn_decode_batch(dj.data(), n, nullptr) != 0)
         return -1;
-    float *hout = h + (size_t)n * in_f;
-    if (check(cudaMemcpyAsync(hout, dout, (size_t)n * out_f * 4, cudaMemcpyDeviceToHost, st), "stage out") != 0)
+    if (stage_out(h + (size_t)n * in_f, dout, n, out_f,
+                  [&](int i, const float *b) { memcpy(jobs[i].out, b, out_f * 4); }) != 0)
         return -1;
-    if (kernel_cuda_synchronize() != 0)
-        return -1;
-    for (int i = 0; i < n; i++)
-        memcpy(jobs[i].out, hout + (size_t)i * out_f, out_f * 4);
-    return 0;
+    return kernel_cuda_synchronize() != 0 ? -1 : 0;
 }
 
 extern "C" int kernel_attn_decode(const float *q_gate, const float *k_new, const float *v_new,

@@ -173,12 +173,6 @@ extern "C" int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, i
         const KernelDeltaStepJob &s = jobs[i];
         if (!s.state || !s.q || !s.k || !s.v || !s.g || !s.beta || !s.out)
             return fail("kernel_deltanet_step_batch_host: job %d has a null pointer", i);
-        float *b = h + (size_t)i * in_f;
-        memcpy(b, s.q, nq * 4);
-        memcpy(b + nq, s.k, nq * 4);
-        memcpy(b + 2 * nq, s.v, nv * 4);
-        memcpy(b + 2 * nq + nv, s.g, nh * 4);
-        memcpy(b + 2 * nq + nv + nh, s.beta, nh * 4);
         float *db = d + (size_t)i * in_f;
         dj[i].q = db;
         dj[i].k = db + nq;
@@ -187,20 +181,21 @@ extern "C" int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, i
         dj[i].beta = db + 2 * nq + nv + nh;
         dj[i].out = d + (size_t)n * in_f + (size_t)i * out_f;
     }
-    cudaStream_t st = rt().stream;
-    if (check(cudaMemcpyAsync(d, h, (size_t)n * in_f * 4, cudaMemcpyHostToDevice, st), "stage in") != 0)
+    const int in_ok = stage_in(h, d, n, in_f, [&](int i, float *b) {
+        const KernelDeltaStepJob &s = jobs[i];
+        memcpy(b, s.q, nq * 4);
+        memcpy(b + nq, s.k, nq * 4);
+        memcpy(b + 2 * nq, s.v, nv * 4);
+        memcpy(b + 2 * nq + nv, s.g, nh * 4);
+        memcpy(b + 2 * nq + nv + nh, s.beta, nh * 4);
+    });
+    if (in_ok != 0 || deltanet_step_batch(dj.data(), n) != 0)
         return -1;
-    if (deltanet_step_batch(dj.data(), n) != 0)
+    const int ok = stage_out(h + (size_t)n * in_f, d + (size_t)n * in_f, n, out_f,
+                             [&](int i, const float *b) { memcpy(jobs[i].out, b, out_f * 4); });
+    if (ok != 0)
         return -1;
-    float *hout = h + (size_t)n * in_f;
-    if (check(cudaMemcpyAsync(hout, d + (size_t)n * in_f, (size_t)n * out_f * 4, cudaMemcpyDeviceToHost, st),
-              "stage out") != 0)
-        return -1;
-    if (kernel_cuda_synchronize() != 0)
-        return -1;
-    for (int i = 0; i < n; i++)
-        memcpy(jobs[i].out, hout + (size_t)i * out_f, out_f * 4);
-    return 0;
+    return kernel_cuda_synchronize() != 0 ? -1 : 0;
 }
 
 extern "C" int kernel_deltanet_step(float *state, const float *q, const float *k, const float *v,

@@ -3,6 +3,9 @@
 #include "ptx.cuh"
 #include "../../include/roaster_cuda.h"
 
+#include <omp.h>
+
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -68,6 +71,77 @@ static int init_device(int device)
     // (apply_rope_64, model.c:765), so both sides rotate by bit-identical angles.
     for (int j = 0; j < 32; j++)
         g_rt.inv_freq[j] = powf(10000000.0f, -2.0f * (float)j / 64.0f);
+    return 0;
+}
+
+// Jobs [i0, i1) on up to 8 host threads (OpenMP, like the reference's own host code); serial
+// for a handful of jobs, where starting threads costs more than the copies.
+static void par_jobs(int i0, int i1, const std::function<void(int)> &f)
+{
+    const int n = i1 - i0;
+    const int nt = std::min(std::min(8, omp_get_max_threads()), n / 2);
+    if (nt <= 1) {
+        for (int i = i0; i < i1; i++)
+            f(i);
+        return;
+    }
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int i = i0; i < i1; i++)
+        f(i);
+}
+
+constexpr int kStageChunks = 4;
+
+static int stage_events(cudaEvent_t **out)
+{
+    static cudaEvent_t ev[kStageChunks];
+    static int made = -1;                      // device the events were made on
+    if (made != g_rt.device) {
+        for (int c = 0; c < kStageChunks; c++)
+            if (check(cudaEventCreateWithFlags(&ev[c], cudaEventDisableTiming), "cudaEventCreate") != 0)
+                return -1;
+        made = g_rt.device;
+    }
+    *out = ev;
+    return 0;
+}
+
+static inline int stage_chunks(int n) { return n >= 4 * kStageChunks ? kStageChunks : 1; }
+
+int stage_in(float *h, float *d, int n, size_t per, const std::function<void(int, float *)> &fill)
+{
+    const int chunks = stage_chunks(n);
+    for (int c = 0; c < chunks; c++) {
+        const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
+        par_jobs(i0, i1, [&](int i) { fill(i, h + (size_t)i * per); });
+        if (check(cudaMemcpyAsync(d + (size_t)i0 * per, h + (size_t)i0 * per, (size_t)(i1 - i0) * per * sizeof(float),
+                                  cudaMemcpyHostToDevice, g_rt.stream),
+                  "stage in") != 0)
+            return -1;
+    }
+    return 0;
+}
+
+int stage_out(float *h, const float *d, int n, size_t per, const std::function<void(int, const float *)> &drain)
+{
+    const int chunks = stage_chunks(n);
+    cudaEvent_t *ev = nullptr;
+    if (stage_events(&ev) != 0)
+        return -1;
+    for (int c = 0; c < chunks; c++) {
+        const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
+        if (check(cudaMemcpyAsync(h + (size_t)i0 * per, d + (size_t)i0 * per, (size_t)(i1 - i0) * per * sizeof(float),
+                                  cudaMemcpyDeviceToHost, g_rt.stream),
+                  "stage out") != 0 ||
+            check(cudaEventRecord(ev[c], g_rt.stream), "cudaEventRecord") != 0)
+            return -1;
+    }
+    for (int c = 0; c < chunks; c++) {
+        const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
+        if (check(cudaEventSynchronize(ev[c]), "stage out") != 0)
+            return -1;
+        par_jobs(i0, i1, [&](int i) { drain(i, h + (size_t)i * per); });
+    }
     return 0;
 }
 

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 
 namespace rb {
 
@@ -62,5 +63,15 @@ int encode_tmap_u8_2d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_
                       uint32_t box0, uint32_t box1);
 // 16-byte alignment check for pointers handed to bulk-copy engines.
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Host staging of the host-buffer entry points. A batch of n jobs of `per` floats each lives
+// contiguously in pinned memory `h` and device memory `d`. stage_in fills the pinned copy job by
+// job with fill(i, h + i * per) on several host threads, in chunks of jobs, and queues each
+// chunk's host-to-device copy as soon as the chunk is filled, so the copies overlap the filling
+// of the next chunk. stage_out queues the device-to-host copies by chunks and hands each chunk
+// to drain(i, h + i * per) (several host threads) as soon as that chunk has arrived. Both use
+// the library stream; 0 = ok.
+int stage_in(float *h, float *d, int n, size_t per, const std::function<void(int, float *)> &fill);
+int stage_out(float *h, const float *d, int n, size_t per, const std::function<void(int, const float *)> &drain);
 
 }  // namespace rb
