@@ -1344,8 +1344,9 @@ __global__ void __launch_bounds__(256) quant_mm_tc_prep_kernel(const __grid_cons
     }
 }
 
+// One CTA's work: tile `item` of the format's job table.
 template <bool Q6>
-__global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __grid_constant__ TParams p)
+__device__ __forceinline__ void tc_tile(const TParams &p, long long item)
 {
     using Cfg = TcCfg<Q6>;
     using namespace tcm;
@@ -1358,7 +1359,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
         int lo = 0, hi = p.njobs - 1;
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if (p.jobs[mid].item0 <= (long long)blockIdx.x)
+            if (p.jobs[mid].item0 <= item)
                 lo = mid;
             else
                 hi = mid - 1;
@@ -1366,7 +1367,7 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
         j = lo;
     }
     const TJob &J = p.jobs[j];
-    const long long it = (long long)blockIdx.x - J.item0;
+    const long long it = item - J.item0;
     const int rt = (int)(it % J.rtiles), ct = (int)(it / J.rtiles);
     const int nb = J.nb, nq = 4 * nb, kb0 = J.kb0, nqt = 4 * J.nbt;   // this part's blocks kb0 .. kb0 + nb - 1
     unsigned long long *bars = reinterpret_cast<unsigned long long *>(gb + Cfg::kOffBar);
@@ -1749,6 +1750,22 @@ __global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __g
         tc::tmem_dealloc(tb, kTmemCols);
 }
 
+// Both formats' tiles in one launch: the Q4_K items first, then the Q6_K items. A call's two
+// formats then share the SMs instead of running one after the other, which matters when each
+// has fewer tiles than SMs (one layer's projections for a round of slots).
+struct TParams2 {
+    TParams f[2];               // [0] Q4_K, [1] Q6_K
+};
+
+__global__ void __launch_bounds__(tcm::kThreads, 1) quant_mm_tc_kernel(const __grid_constant__ TParams2 p)
+{
+    const long long b = blockIdx.x;
+    if (b < p.f[0].items)
+        tc_tile<false>(p.f[0], b);
+    else
+        tc_tile<true>(p.f[1], b - p.f[0].items);
+}
+
 // ---------------------------------------------------------------- host
 
 // Tensor maps of the matrices, cached per device: weights stay resident between calls, so a
@@ -2098,7 +2115,7 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
 // distinct X. The others go to `others`.
 int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others)
 {
-    static bool attr[2] = {false, false};
+    static bool attr = false;
     Runtime &R = rt();
     TParams tp[2];
     memset(static_cast<void *>(tp), 0, sizeof(tp));
@@ -2231,23 +2248,22 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
     quant_mm_tc_prep_kernel<<<(unsigned)ctas, 256, 0, R.stream>>>(pp);
     if (launched("quant_mm_tc_prep_kernel") != 0)
         return -1;
-    for (int k = 0; k < 2; k++) {
-        TParams &P = tp[k];
-        if (P.njobs == 0)
-            continue;
-        P.err = R.err_word;
-        const int smem = k ? TcCfg<true>::kSmem : TcCfg<false>::kSmem;
-        if (!attr[k]) {
-            const cudaError_t ce = k ? cudaFuncSetAttribute(quant_mm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                                     : cudaFuncSetAttribute(quant_mm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (check(ce, "tensor-core matmul shared memory") != 0)
+    {
+        const int smem = std::max(TcCfg<true>::kSmem, TcCfg<false>::kSmem);
+        if (!attr) {
+            if (check(cudaFuncSetAttribute(quant_mm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                      "tensor-core matmul shared memory") != 0)
                 return -1;
-            attr[k] = true;
+            attr = true;
         }
-        if (k)
-            quant_mm_tc_kernel<true><<<(unsigned)P.items, tcm::kThreads, smem, R.stream>>>(P);
-        else
-            quant_mm_tc_kernel<false><<<(unsigned)P.items, tcm::kThreads, smem, R.stream>>>(P);
+        tp[0].err = tp[1].err = R.err_word;
+        const long long items = tp[0].items + tp[1].items;
+        if (items >= (1ll << 31))
+            return fail("kernel_cuda_matmul_quant_batch: too many tiles in one call");
+        TParams2 p2;
+        p2.f[0] = tp[0];
+        p2.f[1] = tp[1];
+        quant_mm_tc_kernel<<<(unsigned)items, tcm::kThreads, smem, R.stream>>>(p2);
         if (launched("quant_mm_tc_kernel") != 0)
             return -1;
     }
