@@ -2111,8 +2111,9 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
 // Jobs of 64 or more tokens on a 16-byte-aligned matrix whose rows are a multiple of 16 bytes (and
 // 16-byte-aligned X), when together they make at least 64 tiles of 128 rows x 64 tokens (with
 // fewer, most SMs would idle and the warp-MMA kernel, which splits tiles along the blocks, is
-// faster): the tensor-core kernel, one launch per format after one prep launch for every
-// distinct X. The others go to `others`.
+// faster): the tensor-core kernel, one launch for both formats after one prep launch for every
+// distinct X (plus a reduce launch when tiles are split along the blocks). The others go to
+// `others`.
 int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others)
 {
     static bool attr = false;
