@@ -2140,6 +2140,7 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         const KernelCudaMatmulJob *j;
         const CUtensorMap *map;
         int x, nb, rtiles, ctiles;
+        int parts;
     };
     std::vector<Sel> sel[2];
     long long ftiles[2] = {0, 0};
@@ -2164,29 +2165,52 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         if (!map)
             return -1;
         const int rtiles = (int)((j.rows + tcm::kRows - 1) / tcm::kRows), ctiles = (int)((j.T + tcm::kTok - 1) / tcm::kTok);
-        sel[j.is_q6 ? 1 : 0].push_back(Sel{&j, map, x, nb, rtiles, ctiles});
+        sel[j.is_q6 ? 1 : 0].push_back(Sel{&j, map, x, nb, rtiles, ctiles, 1});
         ftiles[j.is_q6 ? 1 : 0] += (long long)rtiles * ctiles;
     }
     if (xe.empty())
         return 0;
-    // Split along the blocks when a format's launch has fewer tiles than SMs (a few jobs of 64
-    // tokens, e.g. one layer's projections for a round of slots): part h of a job takes blocks
-    // [h nb / P, (h + 1) nb / P), at least 2 each, and writes an unscaled partial plane; the
-    // reduce launch sums the planes in part order, so results repeat bit for bit.
-    int split[2] = {1, 1};
+    // Split along the blocks when the call has fewer tiles than SMs (a few jobs of 64 tokens, e.g.
+    // one layer's projections for a round of slots): part h of a job takes blocks
+    // [h nb / P, (h + 1) nb / P), at least 2 of them, and writes an unscaled partial plane; the
+    // reduce launch sums the planes in part order, so results repeat bit for bit. A CTA's time is
+    // a fixed set-up and drain plus a cost per block of about the same size for both formats, so
+    // with every CTA in one wave the call takes as long as its largest part: P_j is chosen per job
+    // as the split that makes the largest part smallest while all CTAs still fit one wave.
     size_t part_floats = 0;
-    for (int k = 0; k < 2; k++) {
-        if (sel[k].empty() || ftiles[k] >= R.num_sms)
-            continue;
-        int minb = 1 << 30;
-        for (const Sel &q : sel[k])
-            minb = std::min(minb, q.nb);
-        int P = (int)std::min<long long>(R.num_sms / ftiles[k], minb / 2);
-        P = std::min(P, kMaxJobs / (int)sel[k].size());
-        split[k] = std::max(1, P);
-        if (split[k] > 1)
+    if (ftiles[0] + ftiles[1] < R.num_sms) {
+        std::vector<int> cand;
+        for (int k = 0; k < 2; k++)
             for (const Sel &q : sel[k])
-                part_floats += (size_t)split[k] * q.j->T * q.j->rows;
+                for (int p = 1; p <= std::max(1, q.nb / 2); p++)
+                    cand.push_back((q.nb + p - 1) / p);
+        std::sort(cand.begin(), cand.end());
+        cand.erase(std::unique(cand.begin(), cand.end()), cand.end());
+        for (const int w : cand) {
+            long long ctas = 0;
+            int ent[2] = {0, 0};
+            bool fits = true;
+            for (int k = 0; k < 2 && fits; k++)
+                for (const Sel &q : sel[k]) {
+                    const int p = std::min(std::max(1, q.nb / 2), (q.nb + w - 1) / w);
+                    if ((q.nb + p - 1) / p > w) {
+                        fits = false;
+                        break;
+                    }
+                    ctas += (long long)q.rtiles * q.ctiles * p;
+                    ent[k] += p;
+                }
+            if (!fits || ctas > R.num_sms || ent[0] > kMaxJobs || ent[1] > kMaxJobs)
+                continue;
+            for (int k = 0; k < 2; k++)
+                for (Sel &q : sel[k])
+                    q.parts = std::min(std::max(1, q.nb / 2), (q.nb + w - 1) / w);
+            break;
+        }
+        for (int k = 0; k < 2; k++)
+            for (const Sel &q : sel[k])
+                if (q.parts > 1)
+                    part_floats += (size_t)q.parts * q.j->T * q.j->rows;
     }
     if (tp[0].items >= (1ll << 31) || tp[1].items >= (1ll << 31))
         return fail("kernel_cuda_matmul_quant_batch: too many tiles in one call");
@@ -2213,8 +2237,8 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         float *part = reinterpret_cast<float *>(ws + off_part);
         for (int k = 0; k < 2; k++) {
             TParams &P = tp[k];
-            const int S = split[k];
             for (const Sel &q : sel[k]) {
+                const int S = q.parts;
                 const KernelCudaMatmulJob &j = *q.j;
                 const XEnt &e = xe[q.x];
                 const long long plane = (long long)j.T * j.rows;

@@ -153,9 +153,9 @@ def test_matmul_tensor_core_path(rb, oracle_lib, q6, rows, cols, T):
 @pytest.mark.parametrize("layer", ["deltanet", "attention"])
 def test_matmul_layer_for_a_round_of_slots(rb, oracle_lib, layer):
     """One layer's projections for 64 tokens (a round of 64 slots through the step group): the
-    tcgen05 launches have fewer tiles than SMs, so each job is split along its blocks into
-    parts whose partial planes are summed in part order (DeltaNet: the Q6_K ssm_out in 8 parts;
-    attention: Q4_K in 2, Q6_K in 4). Same bits on a repeat."""
+    call has fewer tcgen05 tiles than SMs, so the jobs with the most blocks are split along
+    their blocks into parts whose partial planes are summed in part order (both layers: the
+    2048 x 4096 Q6_K job in 2 parts, so that every CTA fits one wave). Same bits on a repeat."""
     T = 64
     shapes = ([(False, 8192, 2048), (False, 4096, 2048), (False, 32, 2048), (False, 32, 2048), (True, 2048, 4096)]
               if layer == "deltanet" else
