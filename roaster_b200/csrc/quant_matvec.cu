@@ -248,9 +248,16 @@ __device__ __forceinline__ void q4_mma_block(const unsigned char *pa, const unsi
 
 // Four consecutive logical words at byte offset `off` of a Q6_K block starting at `bp` (any even
 // address): aligned loads, shifted by 16 bits when the words straddle.
+template <bool kAligned>
 __device__ __forceinline__ void q6_words(const unsigned char *bp, int off, uint32_t (&w)[4])
 {
     const unsigned char *a = bp + off;
+    if (kAligned) {                  // the block starts on a 4-byte boundary: plain word loads
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            w[i] = lds32(a + 4 * i);
+        return;
+    }
     const unsigned char *al = reinterpret_cast<const unsigned char *>(reinterpret_cast<uintptr_t>(a) & ~(uintptr_t)3);
     const uint32_t sh = 8u * (uint32_t)(reinterpret_cast<uintptr_t>(a) & 3);
     uint32_t prev = lds32(al);
@@ -264,6 +271,7 @@ __device__ __forceinline__ void q6_words(const unsigned char *bp, int off, uint3
 
 // One Q6_K block of rows (g, g + 8): window (n, h) covers scale groups 8n + 2q + h, q = 0..3;
 // lane t's k-slots hold group q = t (16 weights 128n + 32t + 16h + l), four MMAs per window.
+template <bool kAligned>
 __device__ __forceinline__ void q6_mma_block(const unsigned char *pa, const unsigned char *pb, const uint4 *bt,
                                              const float *xs, float f6, const Lane &L, float &acc_a, float &acc_b)
 {
@@ -280,10 +288,10 @@ __device__ __forceinline__ void q6_mma_block(const unsigned char *pa, const unsi
     for (int win = 0; win < 4; win++) {
         const int n = win >> 1, h = win & 1;
         uint32_t la[4], lb[4], ha[4], hb[4];
-        q6_words(pa, 64 * n + 32 * (L.t & 1) + 16 * h, la);
-        q6_words(pb, 64 * n + 32 * (L.t & 1) + 16 * h, lb);
-        q6_words(pa, 128 + 32 * n + 16 * h, ha);
-        q6_words(pb, 128 + 32 * n + 16 * h, hb);
+        q6_words<kAligned>(pa, 64 * n + 32 * (L.t & 1) + 16 * h, la);
+        q6_words<kAligned>(pb, 64 * n + 32 * (L.t & 1) + 16 * h, lb);
+        q6_words<kAligned>(pa, 128 + 32 * n + 16 * h, ha);
+        q6_words<kAligned>(pb, 128 + 32 * n + 16 * h, hb);
         const uint4 bf[2] = {bt[(win * 2 + 0) * 8], bt[(win * 2 + 1) * 8]};
         float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -520,8 +528,12 @@ __device__ __forceinline__ bool run_segment(const SJob &Jsm, long long it0, long
                          acc_b);
         } else {
             const int mis = (210 * b) & 15;                // the block's offset in its box (same every row)
-            q6_mma_block(st + L.g * kSlot + mis, st + (L.g + 8) * kSlot + mis, bcol + b * bstep, xsum + b * 16, f, L,
-                         acc_a, acc_b);
+            if ((mis & 3) == 0)                            // half the blocks: word-aligned, no shifts
+                q6_mma_block<true>(st + L.g * kSlot + mis, st + (L.g + 8) * kSlot + mis, bcol + b * bstep,
+                                   xsum + b * 16, f, L, acc_a, acc_b);
+            else
+                q6_mma_block<false>(st + L.g * kSlot + mis, st + (L.g + 8) * kSlot + mis, bcol + b * bstep,
+                                    xsum + b * 16, f, L, acc_a, acc_b);
         }
         cs = cs + 1 == S ? 0 : cs + 1;
         if (++bi == nbp) {
