@@ -17,7 +17,9 @@
  * serialises model steps with its slot step lock, slots.c:864-891). All work goes to one CUDA
  * stream per process (kernel_cuda_set_stream). "Device" entry points are asynchronous on that
  * stream; "host" entry points stage their small per-step inputs/outputs through pinned memory
- * and return when the results are in the caller's buffers.
+ * and return when the results are in the caller's buffers. The batched host entry points copy
+ * into and out of that staging on up to 8 OpenMP threads (libgomp, as the reference's own host
+ * code uses), in chunks that overlap the host-device copies.
  *
  * Device faults are never used for error reporting: kernels record failures (e.g. a bounded
  * wait that ran out) in a device error word, reported by kernel_cuda_synchronize().
