@@ -395,7 +395,8 @@ STEP_SLOTS = 64           # config 2's slots per GPU
 def run_batched_step(R, torch, dev, stream, steps: int, rank: int, slots: int = STEP_SLOTS):
     """`slots` native slot threads (libslot_threads.so) step one token each through the step group,
     layer by layer: per layer one kernel_step_group_matvec with that layer's projections (site =
-    layer). The group merges the slots' jobs on each shared matrix into one `slots`-token product.
+    layer; the projections of a layer that read the same input share it, as in the model). The
+    group merges the slots' jobs on each shared matrix into one `slots`-token product.
     Compared with the per-slot form of the reference's step lock: one
     kernel_cuda_matvec_quant_batch per slot carrying all 190 of its projections, slots one after
     another. Returns a dict of timings."""
@@ -410,20 +411,29 @@ def run_batched_step(R, torch, dev, stream, steps: int, rank: int, slots: int = 
     gen.manual_seed(7200 + rank)
     mats = [torch.randint(0, 256, (r * (c // 256) * (210 if q6 else 144),), dtype=torch.uint8, device=dev,
                           generator=gen) for q6, r, c in PROJ_SHAPES]
-    per_site = [len(PROJ_ATT)] * 10 + [len(PROJ_DN)] * 30
+    layers = [PROJ_ATT] * 10 + [PROJ_DN] * 30
+    per_site = [len(shapes) for shapes in layers]
     total = len(PROJ_SHAPES)
-    xcols = sum(c for _, _, c in PROJ_SHAPES)
+    # a layer's projections that read the same input share it (q/k/v; qkv/z/alpha/beta), the
+    # output projection (o / ssm_out, 4096 columns) reads its own: one 2048 and one 4096 vector
+    xcols = sum(sum({c for _, _, c in shapes}) for shapes in layers)
     yrows = sum(r for _, r, _ in PROJ_SHAPES)
     X = torch.randn(slots, xcols, device=dev, generator=gen)
     Y = torch.zeros(slots, yrows + 4 * total, device=dev)
     jobs = (R.KernelCudaMatvecJob * (slots * total))()
     for i in range(slots):
         xo = yo = 0
-        for j, (q6, r, c) in enumerate(PROJ_SHAPES):
-            jobs[i * total + j] = R.KernelCudaMatvecJob(int(q6), mats[j].data_ptr(), X[i, xo:].data_ptr(),
-                                                        Y[i, yo:].data_ptr(), r, c)
-            xo += c
-            yo += (r + 3) // 4 * 4              # 16-byte aligned outputs
+        j = 0
+        for shapes in layers:
+            xoff = {}
+            for c in sorted({c for _, _, c in shapes}):
+                xoff[c] = xo
+                xo += c
+            for q6, r, c in shapes:
+                jobs[i * total + j] = R.KernelCudaMatvecJob(int(q6), mats[j].data_ptr(), X[i, xoff[c]:].data_ptr(),
+                                                            Y[i, yo:].data_ptr(), r, c)
+                yo += (r + 3) // 4 * 4          # 16-byte aligned outputs
+                j += 1
     ps = (C.c_int * len(per_site))(*per_site)
     g = R.StepGroup(slots, straggler_us=2000, call_timeout_ms=20000)
     ids_l = [g.join() for _ in range(slots)]

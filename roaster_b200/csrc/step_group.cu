@@ -283,14 +283,38 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
         if (!found)
             groups.push_back(Group{j, {i}});
     }
+    // A layer's projections usually read the same input (q/k/v, or qkv/z/alpha/beta): matrices
+    // whose members bring the same vectors, in the same order, share one gathered block, and the
+    // matmul then prepares that block's activations once.
+    struct XBlock {
+        size_t cols, off;
+        std::vector<const float *> vecs;
+        bool gathered;
+    };
+    std::vector<XBlock> xblocks;
+    std::vector<int> gxb(groups.size(), -1);
     size_t xfl = 0, yfl = 0;
-    for (const Group &gr : groups)
-        if (gr.idx.size() >= 2) {
-            st->products++;
-            st->merged_jobs += gr.idx.size();
+    for (size_t q = 0; q < groups.size(); q++) {
+        const Group &gr = groups[q];
+        if (gr.idx.size() < 2)
+            continue;
+        st->products++;
+        st->merged_jobs += gr.idx.size();
+        yfl += ((gr.idx.size() * gr.key.rows + 3) & ~(size_t)3);
+        std::vector<const float *> vecs;
+        for (int i : gr.idx)
+            vecs.push_back(mv[i].job.vector);
+        int b = -1;
+        for (size_t k = 0; k < xblocks.size() && b < 0; k++)
+            if (xblocks[k].cols == gr.key.cols && xblocks[k].vecs == vecs)
+                b = (int)k;
+        if (b < 0) {
+            xblocks.push_back(XBlock{gr.key.cols, xfl, std::move(vecs), false});
+            b = (int)xblocks.size() - 1;
             xfl += gr.idx.size() * gr.key.cols;
-            yfl += ((gr.idx.size() * gr.key.rows + 3) & ~(size_t)3);
         }
+        gxb[q] = b;
+    }
     if (ensure() != 0)
         return -1;
     for (const Entry &e : mv)
@@ -302,8 +326,9 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
     std::vector<const float *> gs, ss;
     std::vector<float *> gd, sd;
     std::vector<unsigned> gn, sn;
-    size_t xo = 0, yo = 0;
-    for (const Group &gr : groups) {
+    size_t yo = 0;
+    for (size_t q = 0; q < groups.size(); q++) {
+        const Group &gr = groups[q];
         const KernelCudaMatvecJob &k = gr.key;
         if (gr.idx.size() == 1) {
             const KernelCudaMatvecJob &j = mv[gr.idx[0]].job;
@@ -311,18 +336,21 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
             continue;
         }
         const size_t T = gr.idx.size();
-        float *X = g->xbuf + xo, *Y = g->ybuf + yo;
+        XBlock &xb = xblocks[gxb[q]];
+        float *X = g->xbuf + xb.off, *Y = g->ybuf + yo;
         for (size_t t = 0; t < T; t++) {
             const KernelCudaMatvecJob &j = mv[gr.idx[t]].job;
-            gs.push_back(j.vector);
-            gd.push_back(X + t * k.cols);
-            gn.push_back((unsigned)k.cols);
+            if (!xb.gathered) {
+                gs.push_back(j.vector);
+                gd.push_back(X + t * k.cols);
+                gn.push_back((unsigned)k.cols);
+            }
             ss.push_back(Y + t * k.rows);
             sd.push_back(j.output);
             sn.push_back((unsigned)k.rows);
         }
+        xb.gathered = true;
         jobs.push_back(KernelCudaMatmulJob{k.is_q6, k.matrix, X, Y, k.rows, k.cols, T});
-        xo += T * k.cols;
         yo += (T * k.rows + 3) & ~(size_t)3;
     }
     if (copy_list(gs, gd, gn) != 0)

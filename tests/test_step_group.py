@@ -308,9 +308,10 @@ def _jobs(s):
 
 @pytest.mark.gpu
 def test_group_step_matches_per_slot_step(rb, oracle_lib):
-    """8 slots decode one token through the group (attention, DeltaNet, and 3 projections of
-    which 2 share their weights across slots); the same slots run one call per slot as under
-    the reference's step lock. Same results; the shared projections ran as multi-token products."""
+    """8 slots decode one token through the group (attention, DeltaNet, and 4 projections of
+    which 3 share their weights across slots, two of those also reading the same input vector,
+    like a layer's q and k); the same slots run one call per slot as under the reference's step
+    lock. Same results; the shared projections ran as multi-token products."""
     import torch
     import oracle as O
     from roaster_b200 import synth
@@ -319,16 +320,17 @@ def test_group_step_matches_per_slot_step(rb, oracle_lib):
     base = _slots(torch, N, 11)
     ref = _clone(torch, base)
     shared = [(False, synth.quant_matrix(1, 512, 2048, False), 512, 2048),
-              (True, synth.quant_matrix(2, 256, 1024, True), 256, 1024)]
+              (True, synth.quant_matrix(2, 256, 1024, True), 256, 1024),
+              (False, synth.quant_matrix(3, 256, 2048, False), 256, 2048)]
+    xin = [0, 1, 0]                          # the third matrix reads the first one's input
     dshared = [(q6, dev(m), r, c) for q6, m, r, c in shared]
     priv = [dev(synth.quant_matrix(30 + i, 96, 512, False)) for i in range(N)]
     rng = np.random.default_rng(5)
-    xs = [[dev(rng.standard_normal(c).astype(np.float32)) for (_, _, _, c) in dshared] +
-          [dev(rng.standard_normal(512).astype(np.float32))] for _ in range(N)]
+    xs = [[dev(rng.standard_normal(c).astype(np.float32)) for c in (2048, 1024, 512)] for _ in range(N)]
 
     def mv_jobs(i, outs):
-        js = [(q6, m, xs[i][k], outs[k], r, c) for k, (q6, m, r, c) in enumerate(dshared)]
-        js.append((False, priv[i], xs[i][2], outs[2], 96, 512))
+        js = [(q6, m, xs[i][xin[k]], outs[k], r, c) for k, (q6, m, r, c) in enumerate(dshared)]
+        js.append((False, priv[i], xs[i][2], outs[3], 96, 512))
         return js
 
     g_out = [[torch.zeros(r, device="cuda") for (_, _, r, _) in dshared] + [torch.zeros(96, device="cuda")]
@@ -359,8 +361,8 @@ def test_group_step_matches_per_slot_step(rb, oracle_lib):
     _run(N, member)
     rb.synchronize()
     st = g.stats()
-    assert st["calls"] == 3 and st["jobs"] == N * 5 and st["errors"] == 0
-    assert st["products"] == 2 and st["merged_jobs"] == 2 * N
+    assert st["calls"] == 3 and st["jobs"] == N * 6 and st["errors"] == 0
+    assert st["products"] == 3 and st["merged_jobs"] == 3 * N
     for s, r in zip(base, ref):
         assert O.maxrel(host(s["out"]), host(r["out"])) <= 2e-3
         L = s["d"]["length"]
@@ -371,9 +373,10 @@ def test_group_step_matches_per_slot_step(rb, oracle_lib):
         for a, b in zip(g_out[i], r_out[i]):
             assert O.maxrel(host(a), host(b)) <= 1e-5
     # and against the reference's own matvec for one slot's shared projection
-    q6, m, r, c = shared[0]
-    want = O.matvec_q(q6, m, host(xs[3][0]), r, c, impl="ref" if O.have_ref() else "port")
-    assert O.maxrel(host(g_out[3][0]), want) <= 1e-5
+    for k in (0, 2):                         # both readers of the shared input block
+        q6, m, r, c = shared[k]
+        want = O.matvec_q(q6, m, host(xs[3][0]), r, c, impl="ref" if O.have_ref() else "port")
+        assert O.maxrel(host(g_out[3][k]), want) <= 1e-5
     for m_ in ids:
         g.leave(m_)
     g.close()
