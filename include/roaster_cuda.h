@@ -348,8 +348,10 @@ int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, int n);
  * each dimension at most 2^32 - 1; -1 otherwise) plus the alignment of
  * kernel_cuda_matvec_quant_batch (X 16-byte aligned). Device pointers, asynchronous. Jobs whose
  * matrix is 16-byte aligned with rows a multiple of 16 bytes run token-batched: jobs of 64 or
- * more tokens on the tcgen05 tensor cores (a CTA per tile of 128 rows x 64 tokens) when together
- * they make at least 64 tiles, the other jobs of 8 or more tokens (at most 128 blocks a row) on
+ * more tokens on the tcgen05 tensor cores (a CTA per tile of 128 rows x 64 tokens; a call with
+ * fewer tiles than SMs splits its larger jobs along the blocks into parts summed in a fixed
+ * order) when together they make at least 64 tiles, the other jobs of 8 or more tokens (at most
+ * 128 blocks a row) on
  * the warp MMA (256 rows x 32 tokens per CTA, split along the blocks when there are few tiles);
  * the rest run as T matrix-vector products sharing the (L2-resident) weights.
  * Results do not depend on the route beyond fp32 summation order, and repeat bit for bit. */
