@@ -1,20 +1,23 @@
 #!/usr/bin/env python
 """Hybrid-attention decode benchmark on B200.
 
-One step = one decode token for every slot: per slot one gated-attention layer (16 q / 2 kv heads,
-d 256, q/k RMSNorm, partial RoPE, sigmoid gate) over an f16 KV window of L ~ U[1k, 32k] tokens
-that grows by the appended token each step, plus 3 Gated DeltaNet layers (32 x 128 x 128 fp32
-state each). 64 slots per GPU; slots shard across GPUs with no communication (weak scaling).
+One step = one decode token for every one of the 64 slots: per slot one gated-attention layer
+(16 q / 2 kv heads, d 256, q/k RMSNorm, partial RoPE, sigmoid gate) over an f16 KV window of
+L ~ U[1k, 32k] tokens that grows by the appended token each step, plus 3 Gated DeltaNet layers
+(32 x 128 x 128 fp32 state each). The 64 slots are sharded across the N GPUs (longest windows
+first onto the least-loaded GPU, equal slot counts) with no communication: strong scaling, the
+configuration as stated. A secondary object keeps 64 slots per GPU (weak scaling) at N > 1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 The device-timed `value` runs both kernels on resident inputs (CUDA events on the launching
 stream, max over ranks). `e2e` runs the same step through the host-buffer C-ABI entry points
-(inputs copied host->device and outputs device->host inside the timed region). `cpu_baseline`
-and `--impl reference` time the reference's own CPU code (compiled from its sources into
-oracle/_ref) on this host's cores. Inputs are seeded synthetic data (no dataset exists for the
-path); the KV windows (2.2 GB) and states (0.4 GB) per GPU exceed the 126 MB L2, so no flush is
-needed between steps.
+(inputs copied host->device and outputs device->host inside the timed region). `parity` checks
+one more step of the same batch (a sample of slots, after the timed region) against the
+reference's own CPU code. `cpu_baseline` and `--impl reference` time the reference's own CPU code
+(compiled from its sources into oracle/_ref) on this host's cores. Inputs are seeded synthetic
+data (no dataset exists for the path); the KV windows (2.2 GB) and states (0.4 GB) exceed the
+126 MB L2, so no flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -24,19 +27,21 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-SLOTS = 64
+SLOTS = 64                      # config 2's slots (global)
 DN_LAYERS = 3
-METRIC = "hybrid-attn decode tok/s (config 2: 64 slots/GPU, 1 gated-attn + 3 DeltaNet layers)"
+METRIC = "hybrid-attn decode tok/s (config 2: 64 slots sharded over the GPUs, 1 gated-attn + 3 DeltaNet layers)"
 # DRAM bytes per launch / algorithmic bytes for the decode-attention kernel, from one ncu capture
 # of a 64-slot launch with windows U[1024, 4096] (dram__bytes_read 338.06 MB + write 6.69 MB for
 # 338.31 MB algorithmic). Traffic grows with the KV positions streamed, so the ratio scales to
 # the full launch.
 ATTN_TRAFFIC_RATIO = (338.057984e6 + 6.689792e6) / 338309120
+CPU_BUDGET_S = 90.0             # bound on the reference arm's timed CPU work
 
 
 def args_parse():
@@ -47,6 +52,7 @@ def args_parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity check of the timed batch")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context decode")
@@ -55,6 +61,7 @@ def args_parse():
     ap.add_argument("--no-proj", action="store_true", help="skip the k-quant projection measurement")
     ap.add_argument("--proj-steps", type=int, default=20)
     ap.add_argument("--step-rounds", type=int, default=10, help="timed rounds of the batched-step measurement")
+    ap.add_argument("--no-shards", action="store_true", help="skip the per-GPU shard sweep at N=1")
     ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
     ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
     ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
@@ -70,18 +77,43 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def slot_lengths(rank: int, lo: int = 1024, hi: int = 32768):
+def slot_lengths(seed: int = 1000, lo: int = 1024, hi: int = 32768, n: int = SLOTS):
     from roaster_b200 import synth
-    return [int(x) for x in synth.slot_lengths(1000 + rank, SLOTS, lo, hi)]
+    return [int(x) for x in synth.slot_lengths(seed, n, lo, hi)]
 
 
-# ------------------------------------------------------------------------------ CPU reference leg
+def assign_slots(lens, world: int):
+    """Shard the slots over `world` GPUs: equal slot counts (the DeltaNet work per slot is fixed),
+    windows longest first onto the GPU with the least attention work so far. Returns each rank's
+    slot indices in ascending order."""
+    per = -(-len(lens) // world)
+    load, cnt, out = [0] * world, [0] * world, [[] for _ in range(world)]
+    for s in sorted(range(len(lens)), key=lambda i: (-lens[i], i)):
+        r = min((r for r in range(world) if cnt[r] < per), key=lambda r: (load[r], r))
+        out[r].append(s)
+        cnt[r] += 1
+        load[r] += lens[s]
+    return [sorted(x) for x in out]
 
-def cpu_reference(lens, tokens: int, warmup: int, threads: int) -> dict:
-    """Time the reference's own CPU path (oracle/_ref): per token one slot's full_attention (its
-    four projection matvecs timed separately and subtracted) + 3 recurrent_delta_step calls, the
-    slots served one at a time as the reference's step lock does (slots.c:864-891). Runs
-    `tokens` slot-steps, cycling through the slots. Returns tok/s."""
+
+def config2_desc(world: int, a) -> dict:
+    """The `config` object of the config-2 line; both arms print the same one."""
+    return {"workload": "config 2: batched hybrid-layer decode, 64 slots sharded over the GPUs",
+            "global_slots": SLOTS, "slots_per_gpu": -(-SLOTS // world),
+            "kv_len": f"U[{a.kv_lo}, {a.kv_hi}] per slot (seed 1000), +1 per step",
+            "deltanet_layers_per_slot": DN_LAYERS,
+            "parallelism": f"slot-sharded x{world} (balanced by window length, no collective)",
+            "l2": "inputs (>2.5 GB at N=1) exceed L2; no flush needed"}
+
+
+# ------------------------------------------------------------------------------ CPU legs (subprocess)
+
+def cpu_reference(lens, steps: int, warmup: int, threads: int, budget_s: float) -> dict:
+    """Time the reference's own CPU path (oracle/_ref): one step = every slot once, in turn as the
+    reference's step lock serves them (slots.c:864-891): its full_attention over the slot's
+    window (the four projection matvecs it also runs are timed separately and subtracted) + 3
+    recurrent_delta_step calls; windows grow by one token per step as on the GPU. Runs the
+    warm-up steps, then timed steps until `steps` or `budget_s` of CPU work."""
     import ctypes as C
 
     import numpy as np
@@ -89,7 +121,7 @@ def cpu_reference(lens, tokens: int, warmup: int, threads: int) -> dict:
     import oracle
     lib = oracle.ref_lib()
     rng = np.random.default_rng(5)
-    cap = max(lens) + 2
+    cap = max(lens) + steps + warmup + 2
     qn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
     kn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
     fp = C.POINTER(C.c_float)
@@ -98,26 +130,13 @@ def cpu_reference(lens, tokens: int, warmup: int, threads: int) -> dict:
         raise RuntimeError("reference rig allocation failed")
     kw = np.ctypeslib.as_array(lib.ref_decode_ctx_k(ctx), shape=(cap * 512,))
     vw = np.ctypeslib.as_array(lib.ref_decode_ctx_v(ctx), shape=(cap * 512,))
-    kw[:] = rng.standard_normal(cap * 512).astype(np.float16).astype(np.float32)
-    vw[:] = rng.standard_normal(cap * 512).astype(np.float16).astype(np.float32)
-    state = (0.02 * rng.standard_normal((DN_LAYERS, 32, 128, 128))).astype(np.float32)
+    kw[:] = rng.standard_normal(cap * 512, dtype=np.float32).astype(np.float16).astype(np.float32)
+    vw[:] = rng.standard_normal(cap * 512, dtype=np.float32).astype(np.float16).astype(np.float32)
+    state = (0.02 * rng.standard_normal((DN_LAYERS, 32, 128, 128), dtype=np.float32)).astype(np.float32)
     from roaster_b200 import synth
     dn = synth.delta_step_inputs(rng, DN_LAYERS)
     out = np.zeros((32, 128), np.float32)
     args = [np.ascontiguousarray(dn[k]) for k in ("q", "k", "v", "g", "beta")]
-
-    def one(slot):
-        L = lens[slot % len(lens)]
-        t0 = time.perf_counter()
-        if lib.ref_decode_ctx_step(ctx, L, L) != 0:
-            raise RuntimeError("reference full_attention failed")
-        for l in range(DN_LAYERS):
-            lib.ref_delta_step(state[l].ctypes.data_as(fp),
-                               *[a[l].ctypes.data_as(fp) for a in args], out.ctypes.data_as(fp))
-        return time.perf_counter() - t0
-
-    for i in range(warmup):
-        one(i)
     # projection matvecs full_attention runs (W_q 8192x2048, W_k, W_v 512x2048, W_o 2048x4096)
     pt = []
     for _ in range(5):
@@ -125,24 +144,212 @@ def cpu_reference(lens, tokens: int, warmup: int, threads: int) -> dict:
         lib.ref_decode_ctx_projections(ctx)
         pt.append(time.perf_counter() - t0)
     proj = statistics.median(pt)
-    total = 0.0
-    for i in range(tokens):
-        total += max(one(i) - proj, 1e-9)
+
+    def one_step(i):
+        tot = 0.0
+        for L0 in lens:
+            L = L0 + i
+            t0 = time.perf_counter()
+            if lib.ref_decode_ctx_step(ctx, L, L) != 0:
+                raise RuntimeError("reference full_attention failed")
+            for l in range(DN_LAYERS):
+                lib.ref_delta_step(state[l].ctypes.data_as(fp),
+                                   *[a[l].ctypes.data_as(fp) for a in args], out.ctypes.data_as(fp))
+            tot += max(time.perf_counter() - t0 - proj, 1e-9)
+        return tot
+
+    est = None
+    for i in range(warmup):
+        est = one_step(i)
+    n_timed = steps
+    if est is not None:
+        n_timed = max(1, min(steps, int(budget_s / max(est, 1e-9))))
+    total, done = 0.0, 0
+    for i in range(n_timed):
+        total += one_step(warmup + i)
+        done += 1
+        if est is None and total * (i + 2) / (i + 1) > budget_s:
+            break
     lib.ref_decode_ctx_free(ctx)
-    return {"tok_s": tokens / total, "seconds": total, "tokens": tokens, "threads": threads,
+    return {"tok_s": len(lens) * done / total, "seconds": total, "steps": done, "slots": len(lens),
+            "threads": threads, "projection_ms_subtracted": proj * 1e3}
+
+
+def cpu_parity(path: str) -> dict:
+    """Check a sample of one config-2 step of the GPU batch (saved by the GPU arm) against the
+    reference's own CPU code: full_attention's math per slot (oracle impl "ref") on the same f16
+    window, and recurrent_delta_step on the saved states."""
+    import numpy as np
+
+    import oracle as O
+    z = np.load(path)
+    impl = "ref" if O.have_ref() else "port"
+    attn, st_err, out_err = [], [], []
+    for i in range(int(z["n"])):
+        L = int(z[f"len{i}"])
+        ref, ka, va = O.attn_decode(z[f"q{i}"], z[f"gate{i}"], z[f"kn{i}"], z[f"vn{i}"], z["qn"], z["kw"],
+                                    z[f"kc{i}"], z[f"vc{i}"], L, L, impl=impl)
+        attn.append(O.maxrel(z[f"out{i}"], ref))
+        for l in range(DN_LAYERS):
+            st = np.ascontiguousarray(z[f"st{i}"][l])
+            o = O.delta_step(st, *[np.ascontiguousarray(z[f"d{k}{i}"][l]) for k in ("q", "k", "v", "g", "beta")],
+                             impl=impl)
+            st_err.append(O.maxrel(z[f"st_after{i}"][l], st))
+            out_err.append(O.maxrel(z[f"dout{i}"][l], o))
+    return {"impl": impl, "attn_maxrel": max(attn), "state_maxrel": max(st_err), "deltanet_out_maxrel": max(out_err),
+            "slots": [int(z[f"len{i}"]) for i in range(int(z["n"]))]}
+
+
+PREFILL_CHUNK = 256             # the reference's PF_MAX_T (model.c:1401)
+
+
+def cpu_prefill(threads: int) -> dict:
+    """The reference's own prefill path for ONE config-3 prompt of 8192 tokens on the host:
+    pf_attention (model.c:1536-1602) chunk by chunk, 256 tokens each, and the delta_head
+    recurrence of pf_ssm (model.c:1644-1658) over all 8192 tokens for one DeltaNet layer.
+    Attention: a chunk's attention work is proportional to the keys its rows attend to
+    (start + 128.5 on average), while its projections and per-token prep do not depend on the
+    start. So the first and the last chunk are timed, their difference gives the time per
+    attended key, and the 32 chunks' attention time is that rate times the keys they attend to
+    (sum over chunks of start + 128.5). The result is extrapolated x8 to the configuration's 8
+    prompts (stated in the sample)."""
+    import ctypes as C
+
+    import numpy as np
+
+    import oracle
+    from roaster_b200 import synth
+    lib = oracle.ref_lib()
+    T = 8192
+    rng = np.random.default_rng(6)
+    qn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    fp = C.POINTER(C.c_float)
+    ctx = lib.ref_prefill_ctx_new(T, qn.ctypes.data_as(fp), kn.ctypes.data_as(fp))
+    if not ctx:
+        raise RuntimeError("reference prefill rig allocation failed")
+    kw = np.ctypeslib.as_array(lib.ref_prefill_ctx_k(ctx), shape=(T * 512,))
+    vw = np.ctypeslib.as_array(lib.ref_prefill_ctx_v(ctx), shape=(T * 512,))
+    kw[:] = rng.standard_normal(T * 512, dtype=np.float32)
+    vw[:] = rng.standard_normal(T * 512, dtype=np.float32)
+    C_ = PREFILL_CHUNK
+    nchunks = T // C_
+
+    def timed(fn):
+        t0 = time.perf_counter()
+        if fn() != 0:
+            raise RuntimeError("reference prefill call failed")
+        return time.perf_counter() - t0
+
+    timed(lambda: lib.ref_prefill_ctx_chunk(ctx, C_, 0, 0))                   # warm-up
+    last_kb = T - C_
+    first = statistics.median([timed(lambda: lib.ref_prefill_ctx_chunk(ctx, C_, 0, 0)) for _ in range(3)])
+    last = statistics.median([timed(lambda: lib.ref_prefill_ctx_chunk(ctx, C_, last_kb, last_kb))
+                              for _ in range(2)])
+    proj = statistics.median([timed(lambda: lib.ref_prefill_ctx_projections(ctx, C_)) for _ in range(2)])
+    per_key = (last - first) / last_kb                 # seconds per attended key of a chunk
+    keys = sum(c * C_ + (C_ + 1) / 2 for c in range(nchunks))
+    attn_s = per_key * keys
+    lib.ref_prefill_ctx_free(ctx)
+    del kw, vw
+    p = synth.delta_prompt(7, T)
+    st = np.zeros((32, 128, 128), np.float32)
+    out = np.zeros((T, 32, 128), np.float32)
+    t0 = time.perf_counter()
+    lib.ref_delta_prefill(st.ctypes.data_as(fp), T, *[np.ascontiguousarray(p[k]).ctypes.data_as(fp)
+                                                       for k in ("q", "k", "v", "g", "beta")],
+                          out.ctypes.data_as(fp))
+    dn_s = time.perf_counter() - t0
+    return {"attn_s_per_prompt": attn_s, "deltanet_s_per_prompt": dn_s, "first_chunk_s": first,
+            "last_chunk_s": last, "projections_s_per_chunk": proj, "threads": threads}
+
+
+def cpu_long(window: int, slots: int, threads: int) -> dict:
+    """The reference's own decode for config 4: one slot-step of full_attention over a window of
+    `window` cached tokens (projection matvecs subtracted) + 3 recurrent_delta_step, timed twice;
+    a step serves all `slots` slots in turn (the reference's step lock)."""
+    import ctypes as C
+
+    import numpy as np
+
+    import oracle
+    lib = oracle.ref_lib()
+    rng = np.random.default_rng(8)
+    cap = window + 4
+    qn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    fp = C.POINTER(C.c_float)
+    ctx = lib.ref_decode_ctx_new(cap, qn.ctypes.data_as(fp), kn.ctypes.data_as(fp))
+    if not ctx:
+        raise RuntimeError("reference rig allocation failed")
+    kw = np.ctypeslib.as_array(lib.ref_decode_ctx_k(ctx), shape=(cap * 512,))
+    vw = np.ctypeslib.as_array(lib.ref_decode_ctx_v(ctx), shape=(cap * 512,))
+    kw[:] = rng.standard_normal(cap * 512, dtype=np.float32)
+    vw[:] = rng.standard_normal(cap * 512, dtype=np.float32)
+    from roaster_b200 import synth
+    dn = synth.delta_step_inputs(rng, DN_LAYERS)
+    state = (0.02 * rng.standard_normal((DN_LAYERS, 32, 128, 128), dtype=np.float32)).astype(np.float32)
+    out = np.zeros((32, 128), np.float32)
+    args = [np.ascontiguousarray(dn[k]) for k in ("q", "k", "v", "g", "beta")]
+    proj = statistics.median([(lambda t0: (lib.ref_decode_ctx_projections(ctx), time.perf_counter() - t0)[1])(
+        time.perf_counter()) for _ in range(3)])
+    ts = []
+    for i in range(3):
+        t0 = time.perf_counter()
+        if lib.ref_decode_ctx_step(ctx, window + i, window + i) != 0:
+            raise RuntimeError("reference full_attention failed")
+        for l in range(DN_LAYERS):
+            lib.ref_delta_step(state[l].ctypes.data_as(fp), *[x[l].ctypes.data_as(fp) for x in args],
+                               out.ctypes.data_as(fp))
+        ts.append(time.perf_counter() - t0 - proj)
+    lib.ref_decode_ctx_free(ctx)
+    slot_s = statistics.median(ts[1:])
+    return {"slot_step_s": slot_s, "tok_s": 1.0 / slot_s, "slots": slots, "threads": threads,
             "projection_ms_subtracted": proj * 1e3}
 
 
-def cpu_leg(lens, tokens, warmup):
-    """Run cpu_reference in a fresh process (its OpenMP runtime never meets torch's)."""
-    threads = os.cpu_count() or 1
-    env = dict(os.environ, OMP_NUM_THREADS=str(threads), CUDA_VISIBLE_DEVICES="")
-    spec = json.dumps({"lens": lens, "tokens": tokens, "warmup": warmup, "threads": threads})
+def cpu_leg(task: str, threads: int | None = None, timeout: int = 1800, native: bool = False, **kw):
+    """Run one CPU task in a fresh process (its OpenMP runtime never meets torch's)."""
+    threads = threads or os.cpu_count() or 1
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), CUDA_VISIBLE_DEVICES="",
+               ROASTER_REF_NATIVE="1" if native else "0")
+    spec = json.dumps(dict(kw, task=task, threads=threads))
     out = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-json", spec],
-                         capture_output=True, text=True, env=env, timeout=1800)
+                         capture_output=True, text=True, env=env, timeout=timeout)
     if out.returncode != 0:
-        raise RuntimeError("CPU reference leg failed: " + out.stderr[-2000:])
+        raise RuntimeError(f"CPU leg '{task}' failed (rc {out.returncode}): " + out.stderr[-1500:])
     return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def cpu_leg_ref(task: str, **kw):
+    """The reference CPU leg with the reference's own flags (-march of the GPU host) when that
+    build exists and runs here, else the portable build; says which in `build`."""
+    import oracle
+    if oracle.native_ref_available():
+        try:
+            r = cpu_leg(task, native=True, **kw)
+            r["build"] = f"reference sources, -O3 -march={oracle.native_ref_march()} -fopenmp"
+            return r
+        except Exception as e:  # e.g. the host CPU lacks an instruction of that -march
+            note = f"-march build failed here ({str(e)[:120]}); "
+    else:
+        note = ""
+    r = cpu_leg(task, native=False, **kw)
+    r["build"] = note + "reference sources, -O3 -mavx2 -mfma -mf16c -fopenmp (portable)"
+    return r
+
+
+def cpu_main(spec: dict) -> dict:
+    t = spec["task"]
+    if t == "decode":
+        return cpu_reference(spec["lens"], spec["steps"], spec["warmup"], spec["threads"], spec["budget_s"])
+    if t == "parity":
+        return cpu_parity(spec["path"])
+    if t == "prefill":
+        return cpu_prefill(spec["threads"])
+    if t == "long":
+        return cpu_long(spec["window"], spec["slots"], spec["threads"])
+    raise ValueError(t)
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -201,6 +408,9 @@ class ClockSampler:
 
 PREFILL_PROMPTS = 8
 PREFILL_T = 8192
+DN_PREFILL_KERNELS = "deltanet_prefill_kernel"
+DN_PREFILL_NOTE = ("each product runs as three f16 MMAs (hi*hi + hi*lo + lo*hi) to keep the fp32 state "
+                   "within 1e-4")
 
 
 def run_prefill(R, torch, dev, stream, steps: int, rank: int):
@@ -625,17 +835,200 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
             "gpu_launches": int(launches)}
 
 
+# ------------------------------------------------------------------------------ config 2 (GPU arm)
+
+def attn_step_bytes(n: int, mean_L: float) -> float:
+    """Algorithmic bytes of one decode-attention launch over n slots of mean window mean_L:
+    the f16 K/V rows (2 kv heads x K,V x 256 x 2 B per position), the appended row, q/gate/out."""
+    return n * (mean_L * 2048 + 2048 + 3 * 16 * 256 * 4 + 2 * 2 * 256 * 4)
+
+
+def dn_step_bytes(n_states: int) -> float:
+    """Algorithmic bytes of one DeltaNet step launch: state read + write, inputs and outputs."""
+    return n_states * (2 * 32 * 128 * 128 * 4 + (2 * 16 + 2 * 32) * 128 * 4 + 2 * 32 * 4)
+
+
+def run_config2(R, torch, dev, stream, lens, K: int, W: int, seed: int, world: int, barrier,
+                clocks=None, e2e: bool = False, parity: bool = False):
+    """Time K steps (after W warm-up steps) of the config-2 decode over this GPU's slots `lens`:
+    one kernel_attn_decode_batch + one kernel_deltanet_step_batch per step, windows growing by
+    one token per step. Optionally: the same steps through the host-buffer entry points (e2e),
+    and one more step whose inputs and outputs for a sample of slots are saved for the CPU
+    parity check. Returns per-rank figures (the caller takes the max over ranks)."""
+    import numpy as np
+
+    from roaster_b200 import synth
+    n = len(lens)
+    grow = K + W + 8
+    caps = [L + grow for L in lens]
+    offs = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
+    # KV windows of all slots in one pool (per slot [cap][2][256] f16, 1 KB per position)
+    kpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), seed, dev, torch.float16)
+    vpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), seed + 1, dev, torch.float16)
+    states = synth.device_normal(torch, (n, DN_LAYERS, 32, 128, 128), seed + 2, dev, torch.float32, std=0.02)
+    NP = 4                                            # rotating pools of per-step inputs
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 3)
+    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    q, gate = rn(NP, n, 16, 256), rn(NP, n, 16, 256)
+    kn, vn = rn(NP, n, 2, 256), rn(NP, n, 2, 256)
+    qn = 1 + 0.1 * rn(256)
+    kw = 1 + 0.1 * rn(256)
+    dq = torch.nn.functional.normalize(rn(NP, n, DN_LAYERS, 16, 128), dim=-1)
+    dk = torch.nn.functional.normalize(rn(NP, n, DN_LAYERS, 16, 128), dim=-1)
+    dv = rn(NP, n, DN_LAYERS, 32, 128)
+    dbeta = torch.sigmoid(rn(NP, n, DN_LAYERS, 32))
+    dgl = -torch.exp(-1 + 0.5 * rn(NP, n, DN_LAYERS, 32)) * torch.nn.functional.softplus(
+        rn(NP, n, DN_LAYERS, 32))
+    aout = torch.empty(n, 16, 256, device=dev)
+    dout = torch.empty(n, DN_LAYERS, 32, 128, device=dev)
+    es = kpool.element_size()
+    kaddr = [kpool.data_ptr() + int(offs[s]) * 512 * es for s in range(n)]
+    vaddr = [vpool.data_ptr() + int(offs[s]) * 512 * es for s in range(n)]
+
+    attn_arrs, dn_arrs = [], []
+    for pi in range(NP):
+        jobs = [R.attn_job(q[pi, s], gate[pi, s], kn[pi, s], vn[pi, s], qn, kw, kaddr[s], vaddr[s],
+                           lens[s], lens[s], aout[s], capacity=caps[s]) for s in range(n)]
+        attn_arrs.append((R.KernelAttnDecodeJob * n)(*jobs))
+        dj = [R.delta_job(states[s, l], dq[pi, s, l], dk[pi, s, l], dv[pi, s, l], dgl[pi, s, l],
+                          dbeta[pi, s, l], dout[s, l]) for s in range(n) for l in range(DN_LAYERS)]
+        dn_arrs.append((R.KernelDeltaStepJob * len(dj))(*dj))
+    lib = R.lib()
+    cur = list(lens)
+
+    def step(i, ev=None):
+        arr = attn_arrs[i % NP]
+        for s in range(n):
+            arr[s].length = cur[s]
+            arr[s].position = cur[s]
+        if ev:
+            ev[0].record(stream)
+        rc = lib.kernel_attn_decode_batch(arr, n)
+        if ev:
+            ev[1].record(stream)
+        rc |= lib.kernel_deltanet_step_batch(dn_arrs[i % NP], n * DN_LAYERS)
+        if ev:
+            ev[2].record(stream)
+        if rc != 0:
+            raise RuntimeError(R.last_error())
+        for s in range(n):
+            cur[s] += 1
+
+    for i in range(W):
+        step(i)
+    R.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    launches0 = R.launch_count()
+    lens_at_start = list(cur)
+    t_start.record(stream)
+    for i in range(K):
+        step(W + i, evs[i])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = R.launch_count() - launches0
+    clk = clocks.stop() if clocks else None
+    R.synchronize()
+    res = {"ms": t_start.elapsed_time(t_end),
+           "attn_ms": statistics.mean(e[0].elapsed_time(e[1]) for e in evs),
+           "dn_ms": statistics.mean(e[1].elapsed_time(e[2]) for e in evs),
+           "launches": launches, "clocks": clk,
+           "mean_L": statistics.mean(lens_at_start) + (K - 1) / 2, "n": n}
+
+    # ---------------------------------------------------------------- parity sample (untimed)
+    if parity:
+        order = sorted(range(n), key=lambda s: lens[s])
+        pick = sorted({order[0], order[-1], order[len(order) // 2], *order[:: max(1, n // 4)]})[:6]
+        pi = (W + K) % NP
+        z = {"n": np.int64(len(pick)), "qn": qn.cpu().numpy(), "kw": kw.cpu().numpy()}
+        for j, s in enumerate(pick):
+            L = cur[s]
+            z[f"len{j}"] = np.int64(L)
+            z[f"kc{j}"] = kpool[int(offs[s]):int(offs[s]) + L].cpu().numpy()
+            z[f"vc{j}"] = vpool[int(offs[s]):int(offs[s]) + L].cpu().numpy()
+            z[f"q{j}"], z[f"gate{j}"] = q[pi, s].cpu().numpy(), gate[pi, s].cpu().numpy()
+            z[f"kn{j}"], z[f"vn{j}"] = kn[pi, s].cpu().numpy(), vn[pi, s].cpu().numpy()
+            z[f"st{j}"] = states[s].cpu().numpy()
+            for nm, t in (("q", dq), ("k", dk), ("v", dv), ("g", dgl), ("beta", dbeta)):
+                z[f"d{nm}{j}"] = t[pi, s].cpu().numpy()
+        step(W + K)                                   # the same two launches as a timed step
+        R.synchronize()
+        for j, s in enumerate(pick):
+            z[f"out{j}"] = aout[s].cpu().numpy()
+            z[f"dout{j}"] = dout[s].cpu().numpy()
+            z[f"st_after{j}"] = states[s].cpu().numpy()
+        fd, path = tempfile.mkstemp(suffix=".npz", prefix="roaster_parity_")
+        os.close(fd)
+        np.savez(path, **z)
+        res["parity_file"] = path
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    if e2e:
+        hq, hg = q.cpu().numpy(), gate.cpu().numpy()
+        hkn, hvn = kn.cpu().numpy(), vn.cpu().numpy()
+        hqn, hkw = qn.cpu().numpy(), kw.cpu().numpy()
+        hdq, hdk, hdv = dq.cpu().numpy(), dk.cpu().numpy(), dv.cpu().numpy()
+        hdg, hdb = dgl.cpu().numpy(), dbeta.cpu().numpy()
+        hao = np.zeros((n, 16, 256), np.float32)
+        hdo = np.zeros((n, DN_LAYERS, 32, 128), np.float32)
+        ha, hd = [], []
+        for pi in range(NP):
+            jobs = [R.attn_job(hq[pi, s].ctypes.data, hg[pi, s].ctypes.data, hkn[pi, s].ctypes.data,
+                               hvn[pi, s].ctypes.data, hqn.ctypes.data, hkw.ctypes.data, kaddr[s], vaddr[s],
+                               0, 0, hao[s].ctypes.data, capacity=caps[s]) for s in range(n)]
+            ha.append((R.KernelAttnDecodeJob * n)(*jobs))
+            dj = [R.delta_job(states[s, l], hdq[pi, s, l].ctypes.data, hdk[pi, s, l].ctypes.data,
+                              hdv[pi, s, l].ctypes.data, hdg[pi, s, l].ctypes.data,
+                              hdb[pi, s, l].ctypes.data, hdo[s, l].ctypes.data)
+                  for s in range(n) for l in range(DN_LAYERS)]
+            hd.append((R.KernelDeltaStepJob * len(dj))(*dj))
+        KE = max(1, min(K, 200))
+
+        def estep(i):
+            arr = ha[i % NP]
+            for s in range(n):
+                arr[s].length = cur[s]
+                arr[s].position = cur[s]
+            rc = lib.kernel_attn_decode_batch_host(arr, n)
+            rc |= lib.kernel_deltanet_step_batch_host(hd[i % NP], n * DN_LAYERS)
+            if rc != 0:
+                raise RuntimeError(R.last_error())
+            for s in range(n):
+                cur[s] += 1
+
+        # windows were sized for K+W+8 appends: wind them back and append again (KE <= K)
+        for s in range(n):
+            cur[s] = lens[s]
+        for i in range(2):
+            estep(i)
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(KE):
+            estep(i)
+        res["e2e_s"] = time.perf_counter() - t0
+        res["e2e_steps"] = KE
+        res["h2d"] = n * (4096 * 2 + 512 * 2 + 256 * 2) * 4 + n * DN_LAYERS * (2 * 2048 + 4096 + 64) * 4
+        res["d2h"] = n * 4096 * 4 + n * DN_LAYERS * 4096 * 4
+    del kpool, vpool, states
+    return res
+
+
+
 # ------------------------------------------------------------------------------ GPU arm
 
 def run_ours(a):
     # NCCL prints its banner to stdout; keep stdout for the one JSON line
     os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-    import numpy as np
     import torch
     import torch.distributed as dist
 
     import roaster_b200 as R
-    from roaster_b200 import synth
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -649,177 +1042,92 @@ def run_ours(a):
     stream = torch.cuda.current_stream()
     R.set_stream(stream)
 
-    K, W = a.steps, a.warmup
-    lens = slot_lengths(rank, a.kv_lo, a.kv_hi)
-    grow = K + W + 8
-    caps = [L + grow for L in lens]
-    offs = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
-    # KV windows of all slots in one pool (per slot [cap][2][256] f16, 1 KB per position)
-    kpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), 11 + rank, dev, torch.float16)
-    vpool = synth.device_normal(torch, (int(offs[-1]), 2, 256), 12 + rank, dev, torch.float16)
-    states = synth.device_normal(torch, (SLOTS, DN_LAYERS, 32, 128, 128), 13 + rank, dev,
-                                 torch.float32, std=0.02)
-    NP = 4                                            # rotating pools of per-step inputs
-    g = torch.Generator(device=dev)
-    g.manual_seed(14 + rank)
-    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
-    q, gate = rn(NP, SLOTS, 16, 256), rn(NP, SLOTS, 16, 256)
-    kn, vn = rn(NP, SLOTS, 2, 256), rn(NP, SLOTS, 2, 256)
-    qn = 1 + 0.1 * rn(256)
-    kw = 1 + 0.1 * rn(256)
-    dq = torch.nn.functional.normalize(rn(NP, SLOTS, DN_LAYERS, 16, 128), dim=-1)
-    dk = torch.nn.functional.normalize(rn(NP, SLOTS, DN_LAYERS, 16, 128), dim=-1)
-    dv = rn(NP, SLOTS, DN_LAYERS, 32, 128)
-    dbeta = torch.sigmoid(rn(NP, SLOTS, DN_LAYERS, 32))
-    dgl = -torch.exp(-1 + 0.5 * rn(NP, SLOTS, DN_LAYERS, 32)) * torch.nn.functional.softplus(
-        rn(NP, SLOTS, DN_LAYERS, 32))
-    aout = torch.empty(SLOTS, 16, 256, device=dev)
-    dout = torch.empty(SLOTS, DN_LAYERS, 32, 128, device=dev)
-    es = kpool.element_size()
-
-    attn_arrs, dn_arrs = [], []
-    for pi in range(NP):
-        jobs = [R.attn_job(q[pi, s], gate[pi, s], kn[pi, s], vn[pi, s], qn, kw,
-                           kpool.data_ptr() + int(offs[s]) * 512 * es,
-                           vpool.data_ptr() + int(offs[s]) * 512 * es, lens[s], lens[s], aout[s],
-                           capacity=caps[s]) for s in range(SLOTS)]
-        attn_arrs.append((R.KernelAttnDecodeJob * SLOTS)(*jobs))
-        dj = [R.delta_job(states[s, l], dq[pi, s, l], dk[pi, s, l], dv[pi, s, l], dgl[pi, s, l],
-                          dbeta[pi, s, l], dout[s, l]) for s in range(SLOTS) for l in range(DN_LAYERS)]
-        dn_arrs.append((R.KernelDeltaStepJob * len(dj))(*dj))
-    lib = R.lib()
-    cur = list(lens)
-
-    def step(i, ev=None):
-        arr = attn_arrs[i % NP]
-        for s in range(SLOTS):
-            arr[s].length = cur[s]
-            arr[s].position = cur[s]
-        if ev:
-            ev[0].record(stream)
-        rc = lib.kernel_attn_decode_batch(arr, SLOTS)
-        if ev:
-            ev[1].record(stream)
-        rc |= lib.kernel_deltanet_step_batch(dn_arrs[i % NP], SLOTS * DN_LAYERS)
-        if ev:
-            ev[2].record(stream)
-        if rc != 0:
-            raise RuntimeError(R.last_error())
-        for s in range(SLOTS):
-            cur[s] += 1
-
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for i in range(W):
-        step(i)
-    R.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def allmax(vals):
+        t = torch.tensor([float(v) for v in vals], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
+    K, W = a.steps, a.warmup
+    hbm, _, src = peaks()
+    glens = slot_lengths(1000, a.kv_lo, a.kv_hi)
+    mine = assign_slots(glens, world)[rank]
+    lens = [glens[s] for s in mine]
     clocks = ClockSampler(local if not os.environ.get("CUDA_VISIBLE_DEVICES") else
                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
-    clocks.start()
-    time.sleep(0.3)
-    launches0 = R.launch_count()
-    lens_at_start = list(cur)
-    t_start.record(stream)
-    for i in range(K):
-        step(W + i, evs[i])
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    launches = R.launch_count() - launches0
-    clk = clocks.stop()
-    R.synchronize()
-    ms = t_start.elapsed_time(t_end)
-    attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    dn_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    t = torch.tensor([ms, statistics.mean(attn_ms), statistics.mean(dn_ms)], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, attn_avg, dn_avg = [float(x) for x in t.tolist()]
+    want_parity = rank == 0 and not a.no_parity and not a.no_cpu_baseline
+    c2 = run_config2(R, torch, dev, stream, lens, K, W, 11, world, barrier, clocks=clocks,
+                     e2e=not a.no_e2e, parity=want_parity)
+    ms, attn_avg, dn_avg = allmax([c2["ms"], c2["attn_ms"], c2["dn_ms"]])
     ms_step = ms / K
-    value = SLOTS * world / (ms_step / 1e3)
-
-    # algorithmic bytes per launch (mean over the timed steps: windows grow by 1 per step)
-    mean_L = statistics.mean(lens_at_start) + (K - 1) / 2
-    attn_bytes = SLOTS * (mean_L * 2048 + 2048 + 3 * 16 * 256 * 4 + 2 * 2 * 256 * 4)
-    dn_bytes = SLOTS * DN_LAYERS * (2 * 32 * 128 * 128 * 4 + (2 * 16 + 2 * 32) * 128 * 4 + 2 * 32 * 4)
-    hbm, _, src = peaks()
-    attn_gbs = attn_bytes / (attn_avg / 1e3) / 1e9
-    dn_gbs = dn_bytes / (dn_avg / 1e3) / 1e9
-
-    # ---------------------------------------------------------------- end to end (host buffers)
+    value = SLOTS / (ms_step / 1e3)
+    # algorithmic bytes per launch on the slowest rank's shard are not the same for every rank:
+    # report rank 0's kernels against rank 0's own time
+    attn_bytes = attn_step_bytes(c2["n"], c2["mean_L"])
+    dn_bytes = dn_step_bytes(c2["n"] * DN_LAYERS)
+    attn_gbs = attn_bytes / (c2["attn_ms"] / 1e3) / 1e9
+    dn_gbs = dn_bytes / (c2["dn_ms"] / 1e3) / 1e9
     e2e = None
     if not a.no_e2e:
-        hq = q.cpu().numpy()
-        hg = gate.cpu().numpy()
-        hkn, hvn = kn.cpu().numpy(), vn.cpu().numpy()
-        hqn, hkw = qn.cpu().numpy(), kw.cpu().numpy()
-        hdq, hdk, hdv = dq.cpu().numpy(), dk.cpu().numpy(), dv.cpu().numpy()
-        hdg, hdb = dgl.cpu().numpy(), dbeta.cpu().numpy()
-        hao = np.zeros((SLOTS, 16, 256), np.float32)
-        hdo = np.zeros((SLOTS, DN_LAYERS, 32, 128), np.float32)
-        ha, hd = [], []
-        for pi in range(NP):
-            jobs = [R.attn_job(hq[pi, s].ctypes.data, hg[pi, s].ctypes.data, hkn[pi, s].ctypes.data,
-                               hvn[pi, s].ctypes.data, hqn.ctypes.data, hkw.ctypes.data,
-                               kpool.data_ptr() + int(offs[s]) * 512 * es,
-                               vpool.data_ptr() + int(offs[s]) * 512 * es, 0, 0,
-                               hao[s].ctypes.data, capacity=caps[s]) for s in range(SLOTS)]
-            ha.append((R.KernelAttnDecodeJob * SLOTS)(*jobs))
-            dj = [R.delta_job(states[s, l], hdq[pi, s, l].ctypes.data, hdk[pi, s, l].ctypes.data,
-                              hdv[pi, s, l].ctypes.data, hdg[pi, s, l].ctypes.data,
-                              hdb[pi, s, l].ctypes.data, hdo[s, l].ctypes.data)
-                  for s in range(SLOTS) for l in range(DN_LAYERS)]
-            hd.append((R.KernelDeltaStepJob * len(dj))(*dj))
-        # e2e continues the windows from where the device run left them; same K
-        KE = max(1, min(K, 200))
-
-        def estep(i):
-            arr = ha[i % NP]
-            for s in range(SLOTS):
-                arr[s].length = cur[s]
-                arr[s].position = cur[s]
-            rc = lib.kernel_attn_decode_batch_host(arr, SLOTS)
-            rc |= lib.kernel_deltanet_step_batch_host(hd[i % NP], SLOTS * DN_LAYERS)
-            if rc != 0:
-                raise RuntimeError(R.last_error())
-            for s in range(SLOTS):
-                cur[s] += 1
-
-        # windows were sized for K+W+8 appends: wind them back and append again (KE <= K)
-        for s in range(SLOTS):
-            cur[s] = lens[s]
-        for i in range(2):
-            estep(i)
-        barrier()
-        t0 = time.perf_counter()
-        for i in range(KE):
-            estep(i)
-        el = time.perf_counter() - t0
-        te = torch.tensor([el], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        el = float(te.item())
-        h2d = SLOTS * (4096 * 2 + 512 * 2 + 256 * 2) * 4 + SLOTS * DN_LAYERS * (
-            2 * 2048 + 4096 + 64) * 4
-        d2h = SLOTS * 4096 * 4 + SLOTS * DN_LAYERS * 4096 * 4
-        e2e = {"value": round(SLOTS * world * KE / el, 1), "unit": "tok/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": KE,
+        (el,) = allmax([c2["e2e_s"]])
+        e2e = {"value": round(SLOTS * c2["e2e_steps"] / el, 1), "unit": "tok/s",
+               "h2d_bytes_per_step": c2["h2d"] * world, "d2h_bytes_per_step": c2["d2h"] * world,
+               "steps": c2["e2e_steps"],
                "api": "kernel_attn_decode_batch_host + kernel_deltanet_step_batch_host"}
+
+    # per-GPU efficiency of the shards the strong split gives each GPU at N = 2, 4, 8 (one GPU)
+    shards = None
+    if world == 1 and not a.no_shards:
+        shards = {}
+        for nr in (2, 4, 8):
+            sl = [glens[s] for s in assign_slots(glens, nr)[0]]
+            r = run_config2(R, torch, dev, stream, sl, min(K, 100), 3, 21, 1, barrier)
+            ab = attn_step_bytes(r["n"], r["mean_L"])
+            db = dn_step_bytes(r["n"] * DN_LAYERS)
+            shards[f"{r['n']}_slots"] = {
+                "as_rank0_of": nr, "ms_per_step": round(r["ms"] / min(K, 100), 4),
+                "attn_ms": round(r["attn_ms"], 4), "attn_frac": round(ab / (r["attn_ms"] / 1e3) / 1e9 / hbm, 4),
+                "deltanet_ms": round(r["dn_ms"], 4), "deltanet_frac": round(db / (r["dn_ms"] / 1e3) / 1e9 / hbm, 4),
+                "step_frac": round((ab + db) / (r["ms"] / min(K, 100) / 1e3) / 1e9 / hbm, 4)}
+
+    # 64 slots per GPU (weak scaling), the form measured before the strong split
+    weak = None
+    if world > 1:
+        wl = slot_lengths(1000 + rank, a.kv_lo, a.kv_hi)
+        KW = min(K, 100)
+        r = run_config2(R, torch, dev, stream, wl, KW, 3, 31 + rank, world, barrier)
+        wms, wattn = allmax([r["ms"], r["attn_ms"]])
+        weak = {"metric": "config-2 decode with 64 slots per GPU (weak scaling)",
+                "value": round(SLOTS * world / (wms / KW / 1e3), 1), "unit": "tok/s",
+                "ms_per_step": round(wms / KW, 4), "steps": KW, "scaling": "weak",
+                "attn_frac_rank0": round(attn_step_bytes(r["n"], r["mean_L"]) / (r["attn_ms"] / 1e3) / 1e9 / hbm, 4)}
+
+    parity = None
+    if want_parity:
+        try:
+            parity = cpu_leg("parity", path=c2["parity_file"], timeout=900)
+            parity["pass"] = parity["attn_maxrel"] <= 2e-3 and parity["state_maxrel"] <= 1e-4 \
+                and parity["deltanet_out_maxrel"] <= 1e-4
+            parity["what"] = ("one more step of the timed batch (rank 0's shard, same launches), sampled "
+                              "slots vs the reference's own CPU code; bars 2e-3 attention, 1e-4 DeltaNet")
+        except Exception as e:  # reported, not fatal
+            parity = {"pass": None, "error": str(e)[:300]}
+        finally:
+            try:
+                os.remove(c2["parity_file"])
+            except OSError:
+                pass
 
     prefill = None
     if not a.no_prefill:
         ams, dms, pl = run_prefill(R, torch, dev, stream, a.prefill_steps, rank)
-        tp = torch.tensor([ams, dms], device=dev)
-        if world > 1:
-            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
-        ams, dms = (float(x) for x in tp.tolist())
+        ams, dms = allmax([ams, dms])
         pms = ams + dms
-        _, tflops, src = peaks()
+        _, tflops, srcp = peaks()
         flop = 2.0 * PREFILL_T * PREFILL_T * 256 * 16 * PREFILL_PROMPTS     # causal QK^T + PV
         achieved = flop / (ams / 1e3) / 1e12
         # chunked DeltaNet: per (chunk, value head) 10 C^2 d + 6 C d^2 flops (C = 64, d = 128)
@@ -836,25 +1144,36 @@ def run_ours(a):
                                               "kernel": "prefill_attn_kernel (+ prefill_prep_kernel)",
                                               "achieved": round(achieved, 1), "peak": tflops, "unit": "TFLOP/s",
                                               "frac": round(achieved / tflops, 4),
-                                              "peak_source": f"{src} bf16_tflops (burst; f16 operands run at the same rate)",
+                                              "peak_source": f"{srcp} bf16_tflops (burst; f16 operands run at the same rate)",
                                               "algorithmic_flop_per_step": flop}},
                    "deltanet": {"ms_per_step": round(dms, 4), "tok_s": round(ntok / (dms / 1e3), 1),
-                                "roofline": {"bound": "tensor", "kernel": "deltanet_prefill_kernel",
+                                "roofline": {"bound": "tensor", "kernel": DN_PREFILL_KERNELS,
                                              "achieved": round(dach, 1), "peak": tflops, "unit": "TFLOP/s",
                                              "frac": round(dach / tflops, 4),
-                                             "peak_source": f"{src} bf16_tflops (burst)",
+                                             "peak_source": f"{srcp} bf16_tflops (burst)",
                                              "algorithmic_flop_per_step": dflop,
-                                             "executed_tensor_flop_per_step": 3 * dflop,
-                                             "note": "each product runs as three f16 MMAs (hi*hi + hi*lo + lo*hi) "
-                                                     "to keep the fp32 state within 1e-4"}}}
+                                             "note": DN_PREFILL_NOTE}}}
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            try:
+                c = cpu_leg_ref("prefill", timeout=1200)
+                per_prompt = c["attn_s_per_prompt"] + c["deltanet_s_per_prompt"]
+                prefill["cpu_baseline"] = {
+                    "value": round(PREFILL_T / per_prompt, 2), "unit": "tok/s", "cores": c["threads"],
+                    "kind": "reference", "build": c["build"],
+                    "attention_s_per_prompt": round(c["attn_s_per_prompt"], 3),
+                    "deltanet_s_per_prompt": round(c["deltanet_s_per_prompt"], 3),
+                    "sample": "ONE 8192-token prompt (the other 7 are the same work: x8 extrapolated, tok/s "
+                              "unchanged): pf_attention in 256-token chunks, first and last chunk timed, "
+                              "their difference giving the time per attended key (projections and prep "
+                              "cancel), times the keys the 32 chunks attend to; delta_head over all 8192 "
+                              "tokens for one DeltaNet layer"}
+            except Exception as e:  # reported, not fatal
+                prefill["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
 
     proj = None
     if not a.no_proj:
         pms, plaunch = run_projections(R, torch, dev, stream, a.proj_steps, rank)
-        tq = torch.tensor([pms], device=dev)
-        if world > 1:
-            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
-        pms = float(tq.item())
+        (pms,) = allmax([pms])
         pbytes = proj_bytes(PROJ_SHAPES)
         hbm_p, _, src_p = peaks()
         gbs = pbytes / (pms / 1e3) / 1e9
@@ -884,10 +1203,7 @@ def run_ours(a):
     pproj = None
     if not a.no_proj:
         pms, plaunch = run_prefill_projections(R, torch, dev, stream, a.proj_steps, rank)
-        tq = torch.tensor([pms], device=dev)
-        if world > 1:
-            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
-        pms = float(tq.item())
+        (pms,) = allmax([pms])
         pflop = proj_flops(PROJ_SHAPES, PREFILL_PROJ_T)
         _, tens_p, src_p = peaks()
         tfs = pflop / (pms / 1e3) / 1e12
@@ -918,10 +1234,7 @@ def run_ours(a):
     bstep = None
     if not a.no_proj:
         r = run_batched_step(R, torch, dev, stream, a.step_rounds, rank)
-        tq = torch.tensor([r["group_ms"], r["serial_ms"]], device=dev)
-        if world > 1:
-            dist.all_reduce(tq, op=dist.ReduceOp.MAX)
-        gms, sms = float(tq[0].item()), float(tq[1].item())
+        gms, sms = allmax([r["group_ms"], r["serial_ms"]])
         flop = proj_flops(PROJ_SHAPES, STEP_SLOTS)
         _, tens_p, src_p = peaks()
         tfs = flop / (gms / 1e3) / 1e12
@@ -945,19 +1258,32 @@ def run_ours(a):
 
     long_ctx = None
     if not a.no_long:
-        long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window,
-                                    a.long_steps)
+        long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window, a.long_steps)
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            try:
+                c = cpu_leg_ref("long", window=a.long_window, slots=LONG_SLOTS, timeout=1200)
+                long_ctx["cpu_baseline"] = {
+                    "value": round(c["tok_s"], 3), "unit": "tok/s", "cores": c["threads"], "kind": "reference",
+                    "build": c["build"],
+                    "sample": f"2 timed slot-steps of full_attention over {a.long_window} cached tokens (projection "
+                              f"matvecs subtracted) + 3 recurrent_delta_step; the reference serves the "
+                              f"{LONG_SLOTS} slots in turn, so tok/s = 1 / slot-step time"}
+            except Exception as e:  # reported, not fatal
+                long_ctx["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
-            r = cpu_leg(lens, tokens=SLOTS, warmup=2)
+            r = cpu_leg_ref("decode", lens=glens, steps=1, warmup=0, budget_s=CPU_BUDGET_S)
+            r1 = cpu_leg_ref("decode", lens=glens[:8], steps=1, warmup=0, budget_s=CPU_BUDGET_S, threads=1)
             cpu = {"value": round(r["tok_s"], 3), "unit": "tok/s", "cores": r["threads"],
-                   "kind": "reference",
-                   "sample": f"{r['tokens']} slot-steps (every slot once, lengths of this run), "
+                   "kind": "reference", "build": r["build"],
+                   "sample": f"{r['steps']} step of all {r['slots']} slots (every slot once, windows of this run), "
                              f"reference full_attention minus its projection matvecs "
                              f"({r['projection_ms_subtracted']:.2f} ms) + 3 recurrent_delta_step, "
-                             f"OpenMP {r['threads']} threads, slots serialised as in slots.c"}
+                             f"OpenMP {r['threads']} threads, slots serialised as in slots.c",
+                   "one_thread": {"value": round(r1["tok_s"], 3), "unit": "tok/s", "cores": 1,
+                                  "sample": "the same, 1 OpenMP thread, the first 8 slots of the step"}}
         except Exception as e:  # reported, not fatal
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                    "sample": f"failed: {e}"[:300]}
@@ -967,25 +1293,25 @@ def run_ours(a):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV / fp32 state",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 KV / fp32 state",
             "data": "synthetic (seeded N(0,1) KV and inputs; no dataset exists for this path)",
-            "config": {"workload": "config 2: batched hybrid-layer decode", "slots_per_gpu": SLOTS,
-                       "global_slots": SLOTS * world,
-                       "kv_len": f"U[{a.kv_lo}, {a.kv_hi}] per slot, +1 per step",
-                       "mean_kv_len": round(mean_L, 1), "deltanet_layers_per_slot": DN_LAYERS,
-                       "parallelism": f"slot-sharded x{world} (no collective)",
-                       "l2": "inputs (>2.5 GB per GPU) exceed L2; no flush needed"},
+            "config": dict(config2_desc(world, a), mean_kv_len_rank0=round(c2["mean_L"], 1),
+                           slots_rank0=c2["n"]),
             "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel",
                          "achieved": round(attn_gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(attn_gbs / hbm, 4), "traffic": traffic,
                          "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
-                         "algorithmic_bytes_per_launch": round(attn_bytes)},
+                         "algorithmic_bytes_per_launch": round(attn_bytes),
+                         "scope": "rank 0's launch against rank 0's own kernel time"},
             "kernels": {
-                "attn_decode_kernel": {"ms": round(attn_avg, 4), "GB/s": round(attn_gbs, 1),
+                "attn_decode_kernel": {"ms": round(c2["attn_ms"], 4), "GB/s": round(attn_gbs, 1),
                                        "frac": round(attn_gbs / hbm, 4), "bytes": round(attn_bytes)},
-                "deltanet_step_kernel": {"ms": round(dn_avg, 4), "GB/s": round(dn_gbs, 1),
-                                         "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)}},
-            "e2e": e2e, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
+                "deltanet_step_kernel": {"ms": round(c2["dn_ms"], 4), "GB/s": round(dn_gbs, 1),
+                                         "frac": round(dn_gbs / hbm, 4), "bytes": round(dn_bytes)},
+                "max_over_ranks_ms": {"attn": round(attn_avg, 4), "deltanet": round(dn_avg, 4)}},
+            "parity": parity, "e2e": e2e, "cpu_baseline": cpu, "clocks": c2["clocks"],
+            "gpu_launches": int(c2["launches"]),
+            "shards": shards, "weak_64_per_gpu": weak,
             "prefill": prefill, "long_context": long_ctx, "projections": proj, "prefill_projections": pproj,
             "batched_step": bstep,
         }
@@ -999,23 +1325,24 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return
-    lens = slot_lengths(0, a.kv_lo, a.kv_hi)
-    r = cpu_leg(lens, tokens=max(1, a.steps), warmup=max(0, a.warmup))
     world = int(os.environ.get("WORLD_SIZE", 1))
+    glens = slot_lengths(1000, a.kv_lo, a.kv_hi)
+    r = cpu_leg_ref("decode", lens=glens, steps=max(1, a.steps), warmup=max(0, min(a.warmup, 2)),
+                    budget_s=CPU_BUDGET_S, timeout=3600)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["tok_s"], 3), "unit": "tok/s",
         "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(1e3 * r["seconds"] / r["tokens"], 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
+        "ms_per_step": round(1e3 * r["seconds"] / r["steps"], 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
         "data": "synthetic (seeded)",
-        "config": {"workload": "config 2: batched hybrid-layer decode", "slots_per_gpu": SLOTS,
-                   "kv_len": "U[1024, 32768] per slot", "deltanet_layers_per_slot": DN_LAYERS,
-                   "parallelism": "host CPU, slots serialised (reference step lock)"},
+        "config": config2_desc(world, a),
         "cpu_baseline": {"value": round(r["tok_s"], 3), "unit": "tok/s", "cores": r["threads"],
-                         "kind": "reference",
-                         "sample": f"each step = one slot-step (cycling the 64 slots): reference "
-                                   f"full_attention minus its projection matvecs + 3 "
-                                   f"recurrent_delta_step; OpenMP {r['threads']} threads"},
+                         "kind": "reference", "build": r["build"],
+                         "sample": f"{r['steps']} timed steps of the {a.steps} requested (bounded to "
+                                   f"{CPU_BUDGET_S:.0f} s of CPU work; min(2, W) warm-up steps), each step = all "
+                                   f"{r['slots']} slots once, windows +1 per step as on the GPU: reference "
+                                   f"full_attention minus its projection matvecs + 3 recurrent_delta_step; "
+                                   f"OpenMP {r['threads']} threads; slots served in turn (slots.c step lock)"},
         "e2e": {"value": round(r["tok_s"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -1025,9 +1352,7 @@ def run_reference(a):
 def main():
     a = args_parse()
     if a.cpu_json:
-        spec = json.loads(a.cpu_json)
-        r = cpu_reference(spec["lens"], spec["tokens"], spec["warmup"], spec["threads"])
-        print(json.dumps(r))
+        print(json.dumps(cpu_main(json.loads(a.cpu_json))))
         return
     if a.impl == "reference":
         run_reference(a)

@@ -24,15 +24,27 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 _PORT = os.path.join(HERE, "liboracle.so")
 _REF = os.path.join(HERE, "_ref", "libroaster_ref.so")
+_REF_NATIVE = os.path.join(HERE, "_ref", "libroaster_ref_native.so")
 
 _fp = C.POINTER(C.c_float)
 _u16p = C.POINTER(C.c_uint16)
 _libs: dict = {}
 
 
+# Where the reference checkout lives (its src/ holds model.c); ROASTER_REFERENCE overrides.
+REFERENCE_ROOT = os.environ.get("ROASTER_REFERENCE", "/root/reference")
+# CPU architecture of the GPU host (what -march=native selects there), for the reference build
+# with the reference's own flags; ROASTER_REF_MARCH overrides.
+REF_MARCH = os.environ.get("ROASTER_REF_MARCH", "sapphirerapids")
+
+
 def build(quiet: bool = True) -> None:
     """Compile liboracle.so and, when the reference sources are present, _ref (make)."""
-    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    cmd = ["make", "-C", HERE]
+    src = os.path.join(REFERENCE_ROOT, "src")
+    if os.path.exists(os.path.join(src, "model.c")):
+        cmd += [f"REF={src}", f"REF_MARCH={REF_MARCH}"]
+    out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:
@@ -43,10 +55,25 @@ def have_ref() -> bool:
     return os.path.exists(_REF)
 
 
+def native_ref_available() -> bool:
+    """Whether the reference build with -march=<GPU host CPU> exists (see REF_MARCH)."""
+    return os.path.exists(_REF_NATIVE)
+
+
+def native_ref_march() -> str | None:
+    try:
+        with open(os.path.join(HERE, "_ref", "native_march.txt")) as f:
+            return f.read().strip()
+    except OSError:
+        return None
+
+
 def _load(which: str):
     if which in _libs:
         return _libs[which]
-    path = _PORT if which == "port" else _REF
+    # ROASTER_REF_NATIVE=1 selects the -march build of the reference (timed CPU baseline only)
+    native = which == "ref" and os.environ.get("ROASTER_REF_NATIVE") == "1" and native_ref_available()
+    path = _PORT if which == "port" else (_REF_NATIVE if native else _REF)
     if not os.path.exists(path):
         raise FileNotFoundError(f"oracle library missing: {path} (run make -C oracle)")
     lib = C.CDLL(path)
@@ -120,6 +147,18 @@ def _load(which: str):
         lib.ref_decode_ctx_projections.restype = None
         lib.ref_decode_ctx_free.argtypes = [C.c_void_p]
         lib.ref_decode_ctx_free.restype = None
+        lib.ref_prefill_ctx_new.argtypes = [C.c_size_t, _fp, _fp]
+        lib.ref_prefill_ctx_new.restype = C.c_void_p
+        lib.ref_prefill_ctx_k.argtypes = [C.c_void_p]
+        lib.ref_prefill_ctx_k.restype = _fp
+        lib.ref_prefill_ctx_v.argtypes = [C.c_void_p]
+        lib.ref_prefill_ctx_v.restype = _fp
+        lib.ref_prefill_ctx_chunk.argtypes = [C.c_void_p, C.c_int, C.c_size_t, C.c_size_t]
+        lib.ref_prefill_ctx_chunk.restype = C.c_int
+        lib.ref_prefill_ctx_projections.argtypes = [C.c_void_p, C.c_int]
+        lib.ref_prefill_ctx_projections.restype = C.c_int
+        lib.ref_prefill_ctx_free.argtypes = [C.c_void_p]
+        lib.ref_prefill_ctx_free.restype = None
         lib.ref_max_threads.argtypes = []
         lib.ref_max_threads.restype = C.c_int
     _libs[which] = lib

@@ -265,6 +265,61 @@ void ref_decode_ctx_projections(RefDecodeCtx *c)
     kernel_matvec_f32(W_o, qg, c->g.residual, MODEL_HIDDEN_SIZE, 4096);
 }
 
+/* A reusable pf_attention rig for the timed prefill CPU baseline (model.c:1536-1602): the caller
+ * fills the fp32 window once (ref_prefill_ctx_k / _v) and times ref_prefill_ctx_chunk, one
+ * prompt chunk of T <= 256 tokens appended after `kbase` cached tokens. The chunk's normed rows
+ * are zero, so its projections return zeros; the attention work does not depend on the values.
+ * ref_prefill_ctx_projections runs the same Q/K/V and O projection calls (pf_mm / pf_mm1 on the
+ * f32 weights) so the baseline can subtract their time and report the attention work alone. */
+typedef struct RefPrefillCtx { Rig g; } RefPrefillCtx;
+
+RefPrefillCtx *ref_prefill_ctx_new(size_t capacity, const float *qnorm, const float *knorm)
+{
+    if (ensure_weights() != 0 || pf_ensure(capacity) != 0)
+        return NULL;
+    RefPrefillCtx *c = calloc(1, sizeof(*c));
+    if (!c)
+        return NULL;
+    if (rig_init(&c->g, capacity, NULL, NULL, 0, qnorm, knorm) != 0) {
+        rig_free(&c->g);
+        free(c);
+        return NULL;
+    }
+    memset(g_pf.nrm, 0, (size_t)PF_MAX_T * PF_H * sizeof(float));
+    return c;
+}
+
+float *ref_prefill_ctx_k(RefPrefillCtx *c) { return c->g.kv[ATT_LAYER].k; }
+float *ref_prefill_ctx_v(RefPrefillCtx *c) { return c->g.kv[ATT_LAYER].v; }
+
+void ref_prefill_ctx_free(RefPrefillCtx *c)
+{
+    if (!c)
+        return;
+    rig_free(&c->g);
+    free(c);
+}
+
+int ref_prefill_ctx_chunk(RefPrefillCtx *c, int T, size_t kbase, size_t base)
+{
+    if (T <= 0 || T > PF_MAX_T || kbase + (size_t)T > c->g.kv[ATT_LAYER].capacity)
+        return -1;
+    c->g.kv[ATT_LAYER].length = kbase;
+    return pf_attention(&c->g.m, ATT_LAYER, T, base);
+}
+
+int ref_prefill_ctx_projections(RefPrefillCtx *c, int T)
+{
+    (void)c;
+    const LayerRefs *L = &R->layer[ATT_LAYER];
+    const TRef *refs[3] = { &L->q, &L->k, &L->v };
+    float *outs[3] = { g_pf.qkv, g_pf.k, g_pf.v };
+    const size_t rws[3] = { MODEL_ATTN_Q_SIZE, MODEL_ATTN_K_SIZE, MODEL_ATTN_V_SIZE };
+    if (pf_mm(refs, outs, rws, 3, g_pf.nrm, PF_H, T) != 0)
+        return -1;
+    return pf_mm1(&L->o, g_pf.res, MODEL_HIDDEN_SIZE, g_pf.rec, 4096, T);
+}
+
 /* recurrent_delta_step on a caller state [32][128][128]. */
 void ref_delta_step(float *state, const float *q, const float *k, const float *v,
                     const float *g, const float *beta, float *out)
