@@ -82,3 +82,92 @@ def test_noalloc_rejects_more_than_64_slots(rb):
     out = torch.zeros(65, 16, 256, device="cuda")
     with pytest.raises(RuntimeError, match="64"):
         rb.attn_decode_batch_noalloc(_jobs(rb, slots, [t] * 65, out, 0))
+
+
+# The check below runs in a fresh process: there the allocating decode entry point is never
+# called, so a no-alloc path that fell back to library scratch would show up as device memory
+# taken during a call. The first call loads the module that holds the static array (the driver
+# places the array then), so the free-memory reading brackets the second call.
+_CHILD = r"""
+import json, os, sys
+sys.path.insert(0, os.environ["ROASTER_ROOT"])
+import numpy as np, torch
+import oracle as O
+import roaster_b200 as R
+from roaster_b200 import synth
+torch.cuda.init()
+R.init(0)
+R.set_stream(torch.cuda.current_stream())
+lens = [int(x) for x in np.random.default_rng(5).integers(16, 3000, size=40)]
+slots = []
+for i, L in enumerate(lens):
+    d = synth.attn_decode_inputs(seed=900 + i, length=L)
+    kc = torch.zeros(L + 3, 2, 256, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    kc[:L] = torch.from_numpy(d["k_cache"]).cuda()
+    vc[:L] = torch.from_numpy(d["v_cache"]).cuda()
+    t = {k: torch.from_numpy(np.ascontiguousarray(d[k])).cuda()
+         for k in ("q", "gate", "k_new", "v_new", "q_norm", "k_norm")}
+    slots.append((d, kc, vc, t))
+out = torch.zeros(len(lens), 16, 256, device="cuda")
+jobs = [R.attn_job(t["q"], t["gate"], t["k_new"], t["v_new"], t["q_norm"], t["k_norm"], kc, vc,
+                   d["length"], d["position"], out[i]) for i, (d, kc, vc, t) in enumerate(slots)]
+arr = (R.KernelAttnDecodeJob * len(jobs))(*jobs)
+lib = R.lib()
+torch.cuda.synchronize()
+free = []
+for call in range(2):
+    # the same step twice: the second call rewrites the same appended row
+    f0 = torch.cuda.mem_get_info()[0]
+    rc = lib.kernel_attn_decode_batch_noalloc(arr, len(jobs))
+    assert rc == 0, R.last_error()
+    assert R.lib().kernel_cuda_synchronize() == 0, R.last_error()
+    free.append((f0, torch.cuda.mem_get_info()[0]))
+res = out.cpu().numpy()
+errs = []
+for i, (d, kc, vc, t) in enumerate(slots):
+    ref, _, _ = O.attn_decode(d["q"], d["gate"], d["k_new"], d["v_new"], d["q_norm"], d["k_norm"],
+                              d["k_cache"], d["v_cache"], d["length"], d["position"])
+    errs.append(O.maxrel(res[i], ref))
+print(json.dumps({"free": free, "maxrel": max(errs), "finite": bool(np.isfinite(res).all()),
+                  "total": int(sum(lens)), "n": len(lens)}))
+"""
+
+
+def _plan_items(lens, items_per_sm, sms=148, cap=None):
+    """Items the decode planner makes for these windows (its split rule, restated)."""
+    total = sum(lens)
+    target = max(int(total / (sms * items_per_sm)) + 1, 64)
+    while True:
+        items = 0
+        for L in lens:
+            ns = min(max((L + target // 2) // target, 1), 256)
+            ch = max(-(-L // ns), 1)
+            ch = max(-(-ch // 32) * 32, 32)
+            items += 2 * max(-(-L // ch), 1)
+        if cap is None or items <= cap:
+            return items
+        target *= 2
+
+
+def test_noalloc_fresh_process_allocates_nothing_and_matches_oracle():
+    """In a fresh process, with more items per SM requested than the static array holds (the
+    planner then doubles the split size until the partials fit), two calls in a row: device free
+    memory is the same before and after the second call, and every slot matches the oracle."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, ROASTER_ROOT=root, ROASTER_DECODE_ITEMS_PER_SM="6")
+    lens = [int(x) for x in np.random.default_rng(5).integers(16, 3000, size=40)]
+    # the allocating path's plan at this setting holds more items than the static array (887)
+    assert _plan_items(lens, 6.0) > 887
+    r = subprocess.run([sys.executable, "-c", _CHILD], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert res["finite"]
+    assert res["maxrel"] <= TOL, res
+    f0, f1 = res["free"][1]
+    assert f0 == f1, f"device free memory changed during a no-alloc call: {f0} -> {f1}"
