@@ -2,12 +2,12 @@
 // f16 K/V held in device memory, with the evicted tokens kept in a spill store of kvspill.c's
 // format (reference src/kvwindow.c, src/kvspill.c).
 //
-// Window model (kvwindow.c:1-268): every attention layer holds the same `len` rows; absolute
-// positions are [0, head) kept at the start, [head, head + spilled) in the spill store,
-// [head + spilled, position) the rest of the window. The policy functions below restate the
-// reference's arithmetic step by step (head choice with keep / pin, slide in blocks of a quarter
-// of the free window, restore and rollback through the store's stack order); the data movement
-// becomes device work:
+// Window model (kvwindow.c:1-268): every attention layer holds the same `len` rows; the
+// layout invariant stated above the policy functions says where each token lives (a fixed
+// prefix, the spill store, the recent rows). The policy functions derive each operation from
+// that invariant and select the same tokens as the reference (head from keep / pin, slides in
+// blocks of a quarter of the window beyond the prefix, restore and rollback through the store's
+// stack order); the data movement becomes device work:
 //   - row moves inside a layer: device-to-device copies in chunks that never overlap their own
 //     source (or through scratch when the shift is short);
 //   - eviction: f16 rows -> fp32 on the device -> pinned staging -> the store;
@@ -317,133 +317,151 @@ int spill_pop(W *w, size_t n, size_t dst)
     return 0;
 }
 
-// ---------------------------------------------------------------- policy (kvwindow.c)
+// ---------------------------------------------------------------- window policy
+//
+// Layout invariant. With P = position (tokens seen), S = count (tokens in the store) and
+// H = head (the prefix length fixed when the store went from empty to non-empty), token t is
+//   in row t          for t < H           (the prefix, which does not move while S > 0),
+//   in the store      for H <= t < H + S  (a stack: the latest eviction on top),
+//   in row t - S      for t >= H + S      (the recent part),
+// so len = P - S rows are occupied. Each operation below keeps the invariant and selects the
+// same tokens to keep, spill and bring back as the reference's policy (kvwindow.c), since the
+// attention must see the same keys.
 
-size_t head_for(const W *w, size_t cap)
+// Rows at the start of a window of `rows` rows that stay in place when it slides. While tokens
+// are spilled it is the recorded head. Otherwise it is the larger of two requests, capped by the
+// occupied rows: the configured keep, at most half the window; the pinned prompt, which must
+// leave an eighth of the window (at least one row) free to slide through.
+size_t prefix_rows(const W *w, size_t rows)
 {
     if (w->count > 0)
-        return w->head;                                    // fixed while anything is spilled
-    size_t h = w->keep;
-    if (h > cap / 2)
-        h = cap / 2;
-    size_t pin = w->pin;
-    const size_t room = cap / 8 > 1 ? cap / 8 : 1;        // always leave room to slide
-    if (pin > cap - room)
-        pin = cap > room ? cap - room : 0;
-    if (pin > h)
-        h = pin;
-    return h > w->len ? w->len : h;
+        return w->head;
+    const size_t keep_part = std::min(w->keep, rows / 2);
+    const size_t must_free = std::max<size_t>(rows / 8, 1);
+    size_t pin_part = w->pin;
+    if (rows >= must_free && pin_part > rows - must_free)
+        pin_part = rows > must_free ? rows - must_free : 0;
+    return std::min(std::max(keep_part, pin_part), w->len);
 }
 
-int evict_at(W *w, size_t h, size_t n)
+// Pushes the `n` rows that follow the first `at` rows onto the store and shifts the rows after
+// them down over the gap.
+int spill_rows(W *w, size_t at, size_t n)
 {
     if (n == 0)
         return 0;
-    if (h > w->len || n > w->len - h)
-        return fail("kv window: evicting %zu tokens after %zu of %zu", n, h, w->len);
-    if (spill_push(w, h, n) != 0)
+    if (at > w->len || n > w->len - at)
+        return fail("kv window: evicting %zu tokens after %zu of %zu", n, at, w->len);
+    if (spill_push(w, at, n) != 0)
         return -1;
-    const size_t tail = w->len - h - n;
-    if (move_rows(w, h, h + n, tail) != 0)
+    if (move_rows(w, at, at + n, w->len - at - n) != 0)
         return -1;
     w->len -= n;
     return 0;
 }
 
+// Pops the `n` most recently spilled tokens and puts them back right after the prefix, shifting
+// the recent rows up first to open the gap (and back again if the store cannot deliver).
 int restore(W *w, size_t n)
 {
     if (n == 0)
         return 0;
     if (n > w->count)
         return fail("kv window: restoring %zu of %zu spilled tokens", n, w->count);
-    const size_t h = w->head;
-    if (h > w->len || w->len + n > w->capacity)
+    const size_t at = w->head;
+    if (at > w->len || w->len + n > w->capacity)
         return fail("kv window: no room to restore %zu tokens", n);
-    const size_t tail = w->len - h;
-    if (move_rows(w, h + n, h, tail) != 0)
+    const size_t recent = w->len - at;
+    if (move_rows(w, at + n, at, recent) != 0)
         return -1;
-    if (spill_pop(w, n, h) != 0) {
-        move_rows(w, h, h + n, tail);                       // undo the shift
+    if (spill_pop(w, n, at) != 0) {
+        move_rows(w, at, at + n, recent);
         return -1;
     }
     w->len += n;
     return 0;
 }
 
+// Room for `need` more rows in the window (w->ctx rows). If they do not fit and sliding is on,
+// the oldest rows after the prefix go to the store: the overflow, rounded up to a quarter of the
+// rows beyond the prefix so the window slides in blocks and not one token at a time.
 int ensure_room(W *w, size_t need)
 {
-    const size_t cap = w->ctx;
-    if (w->len + need <= cap)
+    const size_t rows = w->ctx;
+    if (w->len + need <= rows)
         return 0;
     if (!w->slide)
-        return fail("kv window: full (%zu + %zu > %zu) and sliding is off", w->len, need, cap);
-    const size_t h = head_for(w, cap);
-    if (need > cap - h)
+        return fail("kv window: full (%zu + %zu > %zu) and sliding is off", w->len, need, rows);
+    const size_t pre = prefix_rows(w, rows);
+    if (need > rows - pre)
         return fail("kv window: %zu tokens do not fit beside the kept head", need);
-    const size_t over = w->len + need - cap;
-    const size_t block = (cap - h) / 4;                     // slide in blocks
-    size_t n = over > block ? over : block;
-    if (n > w->len - h)
-        n = w->len - h;
-    if (n < over)
-        return fail("kv window: cannot free %zu tokens", over);
-    return evict_at(w, h, n);
+    const size_t overflow = w->len + need - rows;
+    const size_t n = std::min(std::max(overflow, (rows - pre) / 4), w->len - pre);
+    if (n < overflow)
+        return fail("kv window: cannot free %zu tokens", overflow);
+    return spill_rows(w, pre, n);
 }
 
-// Absolute positions: head [0,h), spilled [h,h+s), window tail [h+s,p). Target: every
-// position < p0 except those spilled at the snapshot, [h, h+s0).
+// Back to a snapshot taken at position p0 with s0 tokens spilled. At the snapshot the window held
+// every token below p0 except the run then spilled, [H, H + s0) (the run only grows upwards from
+// H while the store is non-empty). Relative to the invariant's layout that means:
+//   - store entries for tokens at or above max(p0, H) did not exist then: drop them;
+//   - store entries for tokens in [H + s0, min(p0, H + S)) were rows then: bring them back;
+//   - recent rows for tokens in [H + S, p0) stay, rows for tokens from p0 on go;
+//   - if p0 < H the snapshot had no store at all: only the first p0 rows stay.
 int rollback(W *w, size_t p0, size_t s0)
 {
-    const size_t p = w->position, s = w->count;
-    if (p0 > p || s < s0)
+    if (p0 > w->position || w->count < s0)
         return fail("kv window: cannot roll back to position %zu", p0);
-    const size_t cap = w->capacity;
-    if (s == 0) {
-        if (p0 > cap)
+    if (w->count == 0) {
+        if (p0 > w->capacity)
             return fail("kv window: rollback target beyond the window");
         w->len = p0;
         w->position = p0;
         return 0;
     }
-    const size_t h = w->head, sp_end = h + s;
-    const size_t tk = p0 > sp_end ? p0 - sp_end : 0;        // tail tokens to keep
-    const size_t hk = p0 < h ? p0 : h;                      // head tokens to keep
-    const size_t lim = p0 > h ? p0 : h;
-    const size_t dc = sp_end > lim ? sp_end - lim : 0;      // spilled tokens newer than p0
-    const size_t top = p0 < sp_end ? p0 : sp_end;
-    const size_t r = top > h + s0 ? top - (h + s0) : 0;     // spilled tokens to bring back
-    if (dc + r > s || hk + r + tk > cap)
+    const size_t H = w->head, S = w->count;
+    const size_t run_end = H + S;                                // first token after the spilled run
+    const size_t drop = run_end - std::min(run_end, std::max(p0, H));
+    const size_t back_end = std::min(p0, run_end);
+    const size_t back = back_end > H + s0 ? back_end - (H + s0) : 0;
+    const size_t recent_keep = p0 > run_end ? p0 - run_end : 0;
+    const size_t prefix_keep = std::min(p0, H);
+    if (drop + back > S || prefix_keep + back + recent_keep > w->capacity)
         return fail("kv window: rollback does not fit");
-    if (dc && spill_pop(w, dc, (size_t)-1) != 0)
+    if (drop && spill_pop(w, drop, (size_t)-1) != 0)
         return -1;
-    if (hk < h) {                                           // p0 lies inside the head
-        w->len = hk;
+    if (p0 < H) {
+        w->len = p0;
         w->position = p0;
         return 0;
     }
-    if (r && tk && move_rows(w, h + r, h, tk) != 0)
-        return -1;
-    if (r && spill_pop(w, r, h) != 0)
-        return -1;
-    w->len = hk + r + tk;
+    if (back) {
+        if (recent_keep && move_rows(w, H + back, H, recent_keep) != 0)
+            return -1;
+        if (spill_pop(w, back, H) != 0)
+            return -1;
+    }
+    w->len = H + back + recent_keep;
     w->position = p0;
     return 0;
 }
 
-int shrink_to_fit(W *w, size_t new_ctx)
+// Fits the occupied rows into a smaller window of `rows` rows (a context change): the overflow
+// goes to the store plus a quarter of the new window beyond the prefix, so the first appends
+// after the change find room.
+int shrink_to_fit(W *w, size_t rows)
 {
-    if (w->len <= new_ctx)
+    if (w->len <= rows)
         return 0;
-    const size_t h = head_for(w, new_ctx);
-    if (h >= new_ctx)
-        return fail("kv window: head does not fit a window of %zu", new_ctx);
-    const size_t need = w->len - new_ctx;
-    size_t n = need + (new_ctx - h) / 4;
-    if (n > w->len - h)
-        n = w->len - h;
-    if (n < need)
-        return fail("kv window: cannot shrink to %zu", new_ctx);
-    return evict_at(w, h, n);
+    const size_t pre = prefix_rows(w, rows);
+    if (pre >= rows)
+        return fail("kv window: head does not fit a window of %zu", rows);
+    const size_t overflow = w->len - rows;
+    const size_t n = std::min(overflow + (rows - pre) / 4, w->len - pre);
+    if (n < overflow)
+        return fail("kv window: cannot shrink to %zu", rows);
+    return spill_rows(w, pre, n);
 }
 
 int realloc_rows(W *w, size_t new_ctx)
@@ -481,20 +499,20 @@ int realloc_rows(W *w, size_t new_ctx)
     return 0;
 }
 
-// After the window grew: bring spilled tokens back, leaving one slide block of headroom if
-// not everything fits.
+// After the window grew: spilled tokens come back, all of them when they fit, else as many as
+// leave a quarter of the window beyond the prefix free (the next appends would evict them again).
 int refill(W *w)
 {
-    const size_t s = w->count, cap = w->ctx;
-    if (!s || w->len >= cap)
+    const size_t rows = w->ctx;
+    if (w->count == 0 || w->len >= rows)
         return 0;
-    const size_t avail = cap - w->len;
-    size_t r = s;
-    if (r > avail) {
-        const size_t block = cap > w->head ? (cap - w->head) / 4 : 0;
-        r = avail > block ? avail - block : 0;
+    const size_t free_rows = rows - w->len;
+    size_t n = w->count;
+    if (n > free_rows) {
+        const size_t headroom = rows > w->head ? (rows - w->head) / 4 : 0;
+        n = free_rows > headroom ? free_rows - headroom : 0;
     }
-    return r ? restore(w, r) : 0;
+    return n ? restore(w, n) : 0;
 }
 
 void destroy(W *w)
@@ -562,7 +580,7 @@ extern "C" uint16_t *kernel_kvw_v(KernelKvWindow *w, int layer)
 
 extern "C" size_t kernel_kvw_len(const KernelKvWindow *w) { return w ? w->len : 0; }
 extern "C" size_t kernel_kvw_spilled(const KernelKvWindow *w) { return w ? w->count : 0; }
-extern "C" size_t kernel_kvw_head(const KernelKvWindow *w) { return w ? head_for(w, w->ctx) : 0; }
+extern "C" size_t kernel_kvw_head(const KernelKvWindow *w) { return w ? prefix_rows(w, w->ctx) : 0; }
 extern "C" size_t kernel_kvw_position(const KernelKvWindow *w) { return w ? w->position : 0; }
 extern "C" size_t kernel_kvw_context(const KernelKvWindow *w) { return w ? w->ctx : 0; }
 
@@ -571,7 +589,7 @@ extern "C" size_t kernel_kvw_max_chunk(const KernelKvWindow *w)
     if (!w)
         return 0;
     if (w->slide)
-        return w->ctx - head_for(w, w->ctx);
+        return w->ctx - prefix_rows(w, w->ctx);
     return w->ctx > w->len ? w->ctx - w->len : 0;
 }
 
@@ -607,7 +625,7 @@ extern "C" int kernel_kvw_evict(KernelKvWindow *w, size_t n)
 {
     if (ensure() != 0 || !w)
         return -1;
-    return evict_at(w, head_for(w, w->ctx), n);
+    return spill_rows(w, prefix_rows(w, w->ctx), n);
 }
 
 extern "C" int kernel_kvw_restore(KernelKvWindow *w, size_t n)
