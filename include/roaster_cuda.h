@@ -109,15 +109,21 @@ int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n);
  * exists for callers that must not allocate device memory once they are serving -- a host
  * running under a device-memory budget fixed at start-up, or code that may not enter the CUDA
  * allocator (or an allocating library such as torch's caching allocator) at decode time.
- * It never calls cudaMalloc/cudaFree: its scratch (split softmax partials, completion counters,
- * an error word) is one statically sized 8 MiB device array that every GPU loading this library
- * holds until the process exits. Limits: at most 64 slots per call (more is rejected with an
- * error); windows of any length (the split size grows so the partials fit the array).
+ * It never calls cudaMalloc/cudaFree: its scratch (split softmax partials, completion counters)
+ * is one statically sized 8 MiB device array that every GPU loading this library holds until
+ * the process exits. Limits: at most 64 slots per call (more is rejected with an error);
+ * windows of any length (the split size grows so the partials fit the array).
+ * Device: the call runs on the current device, which must be the one kernel_cuda_init chose;
+ * kernel_cuda_init (which allocates the library's 256-byte error word) must run once at
+ * start-up, and a call made with another device current is rejected with an error. Failures a
+ * kernel records (a bounded wait that ran out, an argument it cannot process) land in that
+ * error word and are reported by kernel_cuda_synchronize, as for kernel_attn_decode_batch.
  * The first call on each device does a one-time set-up (it looks up the array's device address
  * and the SM count) and should come before any stream capture. Every call shares the one array
  * and clears its counters at the start, so calls whose work overlaps on the GPU (different
  * streams, or different threads) race and must be serialised by the caller. Same job semantics,
- * results and asynchrony as kernel_attn_decode_batch; all pointers device memory. */
+ * results and asynchrony as kernel_attn_decode_batch, on the library stream; all pointers device
+ * memory. */
 int kernel_attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n);
 
 /* Drop-in for full_attention's core (model.c:801-861) with model.c's own host buffers:
@@ -143,6 +149,36 @@ int kernel_attn_decode_partial_batch(const KernelAttnDecodeJob *jobs, int n, flo
 int kernel_attn_merge_partials(const float *partials, int nparts, int n,
                                const float *const *gates, size_t qg_stride,
                                float *const *outs);
+
+/* Split-KV decode with the combine fused into the kernels (long-context decode across GPUs,
+ * the exchange step of model.c:825-856 when the window is split): like
+ * kernel_attn_decode_partial_batch, but job i's merged partial goes straight to dst[i] (two
+ * records of KERNEL_ATTN_PARTIAL_FLOATS floats, kv head 0 then 1; 16-byte aligned), which may
+ * be another GPU's memory opened with kernel_cuda_ipc_open (plain peer stores over NVLink), and
+ * once both records are visible to every GPU, tags[i][0..1] are set to `epoch`. No collective
+ * library call: the home GPU of a slot waits on the tags in kernel_attn_merge_wait. Async. */
+int kernel_attn_decode_partial_push(const KernelAttnDecodeJob *jobs, int n, float *const *dst,
+                                    unsigned *const *tags, unsigned epoch);
+
+/* The home GPU's half of the fused combine: recv [nparts][n][2][KERNEL_ATTN_PARTIAL_FLOATS]
+ * and tags [nparts][n][2] in this GPU's memory, filled by kernel_attn_decode_partial_push on
+ * the nparts GPUs. Each (job, kv head) waits until its nparts tags equal `epoch` (bounded: a
+ * wait that runs out sets the error word kernel_cuda_synchronize reports, and that output is
+ * not written), then merges as kernel_attn_merge_partials. A buffer may be reused for the
+ * step after next (double buffering by step parity keeps a fast GPU from overwriting records
+ * the home GPU has not merged yet). Async. */
+int kernel_attn_merge_wait(const float *recv, const unsigned *tags, int nparts, int n,
+                           const float *const *gates, size_t qg_stride, float *const *outs,
+                           unsigned epoch);
+
+/* Inter-process access to device memory (cudaIpcGetMemHandle / cudaIpcOpenMemHandle): the
+ * handle of a buffer from kernel_cuda_alloc, exchanged between the processes of a job by the
+ * caller, opens as a device pointer to that buffer on its GPU (peer access over NVLink).
+ * KERNEL_CUDA_IPC_HANDLE_BYTES bytes of handle. 0 = ok, -1 = error. */
+#define KERNEL_CUDA_IPC_HANDLE_BYTES 64
+int kernel_cuda_ipc_handle(void *dev_ptr, void *handle);
+int kernel_cuda_ipc_open(const void *handle, void **dev_ptr);
+int kernel_cuda_ipc_close(void *dev_ptr);
 
 /* ------------------------------------------------------------------ gated attention, prefill
  * Replaces pf_attention's attention part (model.c:1553-1600): per token q/k RMSNorm and partial

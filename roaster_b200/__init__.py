@@ -127,6 +127,13 @@ def lib():
                                                        _vp]),
         "kernel_attn_merge_partials": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp), _sz,
                                                  C.POINTER(_vp)]),
+        "kernel_attn_decode_partial_push": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int,
+                                                      C.POINTER(_vp), C.POINTER(_vp), C.c_uint]),
+        "kernel_attn_merge_wait": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp), _sz,
+                                             C.POINTER(_vp), C.c_uint]),
+        "kernel_cuda_ipc_handle": (C.c_int, [_vp, _vp]),
+        "kernel_cuda_ipc_open": (C.c_int, [_vp, C.POINTER(_vp)]),
+        "kernel_cuda_ipc_close": (C.c_int, [_vp]),
         "kernel_attn_prefill_batch": (C.c_int, [C.POINTER(KernelAttnPrefillJob), C.c_int]),
         "kernel_attn_prefill": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp]),
         "kernel_deltanet_step_batch": (C.c_int, [C.POINTER(KernelDeltaStepJob), C.c_int]),
@@ -273,6 +280,45 @@ def attn_merge_partials(partials, nparts: int, gates, outs, qg_stride: int = 256
     o = (_vp * n)(*[_ptr(x) for x in outs])
     check(lib().kernel_attn_merge_partials(_ptr(partials), nparts, n, g, qg_stride, o),
           "kernel_attn_merge_partials")
+
+
+def attn_decode_partial_push(jobs, dst, tags, epoch: int) -> None:
+    """Split-KV partials pushed to per-job record addresses (any GPU), tags set to `epoch`."""
+    arr, n = _arr(KernelAttnDecodeJob, jobs)
+    d = (_vp * n)(*[_ptr(x) for x in dst])
+    t = (_vp * n)(*[_ptr(x) for x in tags])
+    check(lib().kernel_attn_decode_partial_push(arr, n, d, t, int(epoch) & 0xFFFFFFFF),
+          "kernel_attn_decode_partial_push")
+
+
+def attn_merge_wait(recv, tags, nparts: int, gates, outs, epoch: int, qg_stride: int = 256) -> None:
+    n = len(gates)
+    g = (_vp * n)(*[_ptr(x) for x in gates])
+    o = (_vp * n)(*[_ptr(x) for x in outs])
+    check(lib().kernel_attn_merge_wait(_ptr(recv), _ptr(tags), nparts, n, g, qg_stride, o,
+                                       int(epoch) & 0xFFFFFFFF), "kernel_attn_merge_wait")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_handle(ptr) -> bytes:
+    """The inter-process handle of a kernel_cuda_alloc buffer."""
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    check(lib().kernel_cuda_ipc_handle(_ptr(ptr), buf), "kernel_cuda_ipc_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Open another process's buffer by its handle; returns the device address."""
+    out = _vp()
+    check(lib().kernel_cuda_ipc_open(C.create_string_buffer(handle, IPC_HANDLE_BYTES), C.byref(out)),
+          "kernel_cuda_ipc_open")
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().kernel_cuda_ipc_close(_ptr(ptr)), "kernel_cuda_ipc_close")
 
 
 def attn_prefill_batch(jobs) -> None:

@@ -72,6 +72,8 @@ struct DJob {
     const float *k_new, *v_new, *q_norm, *k_norm;
     __half *k_cache, *v_cache;
     float *out;
+    float *pdst;        // push mode: this job's merged records [2][kPF] (any GPU's memory), else null
+    unsigned *ptag;     // push mode: the 2 tag words set to `epoch` once the records are visible
     long long qg_stride, length, position, chunk;
     int item_base, nsplit, append, pad;
 };
@@ -87,6 +89,7 @@ struct DParams {
     float *pout;        // partial mode: [njobs][2][kPF], else null
     unsigned *err;
     int njobs, nitems;
+    unsigned epoch;     // push mode: tag value of this step
 };
 
 struct Smem {
@@ -245,7 +248,7 @@ __device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int 
         sm.lw[0][t] = L;
     }
     named_bar_sync(1, 128);
-    float *dst = p.pout ? p.pout + ((long long)jidx * 2 + kvh) * kPF : nullptr;
+    float *dst = J.pdst ? J.pdst + kvh * kPF : (p.pout ? p.pout + ((long long)jidx * 2 + kvh) * kPF : nullptr);
     if (dst && t < 8) {
         dst[t] = sm.mw[0][t];
         dst[8 + t] = sm.lw[0][t];
@@ -286,6 +289,14 @@ __device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int 
             for (int x = 0; x < 4; x++)
                 out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
         }
+    }
+    if (J.ptag) {
+        // Every writer makes its record stores visible system-wide before the tag goes out:
+        // the home GPU reads the record as soon as it sees the tag.
+        __threadfence_system();
+        named_bar_sync(1, 128);
+        if (t == 0)
+            st_release_sys(J.ptag + kvh, p.epoch);
     }
 }
 
@@ -586,6 +597,76 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__
     }
 }
 
+// Merge on the home GPU of records that every GPU pushed into its memory (push mode): grid
+// (n jobs x 2 kv heads), 256 threads. Warp 0 first waits (bounded) until each of the nparts
+// records of the block's (job, kv head) carries this step's tag; then the merge of
+// attn_merge_kernel. recv: [nparts][n][2][kPF]; tags: [nparts][n][2].
+struct MWParams {
+    const float *recv;
+    const unsigned *tags;
+    const float *gates[kMaxJobs];
+    float *outs[kMaxJobs];
+    long long qg_stride, budget;
+    unsigned *err;
+    int nparts, n, job0;
+    unsigned epoch;
+};
+
+__global__ void __launch_bounds__(256) attn_merge_wait_kernel(const __grid_constant__ MWParams p)
+{
+    __shared__ float w[64][8], Ms[8], Ls[8];
+    __shared__ int ready;
+    const int j = blockIdx.x >> 1, kvh = blockIdx.x & 1, t = threadIdx.x;
+    if (t < 32) {
+        bool ok = true;
+        for (int i = t; i < p.nparts; i += 32) {
+            const unsigned *tag = p.tags + ((long long)i * p.n + p.job0 + j) * 2 + kvh;
+            const long long t0 = clock64();
+            while (ld_acquire_sys(tag) != p.epoch) {
+                if (clock64() - t0 > p.budget) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (t == 0)
+            ready = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!ready) {
+        if (t == 0)
+            atomicOr(p.err, kErrWaitTimeout);
+        return;
+    }
+    const long long stride = (long long)p.n * 2 * kPF;
+    const float *rec0 = p.recv + ((long long)(p.job0 + j) * 2 + kvh) * kPF;
+    if (t < 8) {
+        float M = -INFINITY, L = 0.f;
+        for (int i = 0; i < p.nparts; i++)
+            M = fmaxf(M, __ldcg(rec0 + i * stride + t));
+        for (int i = 0; i < p.nparts; i++) {
+            const float m = __ldcg(rec0 + i * stride + t);
+            const float x = m == -INFINITY ? 0.f : __ldcg(rec0 + i * stride + 8 + t) * exp2f(m - M);
+            w[i][t] = x;
+            L += x;
+        }
+        Ms[t] = M;
+        Ls[t] = L;
+    }
+    __syncthreads();
+    for (int e = t; e < 8 * kHD; e += 256) {
+        const int h = e >> 8, d = e & (kHD - 1);
+        float acc = 0.f;
+        for (int i = 0; i < p.nparts; i++)
+            acc = fmaf(w[i][h], __ldcg(rec0 + i * stride + 16 + e), acc);
+        const float o = Ls[h] > 0.f ? acc / Ls[h] : 0.f;
+        const float g = p.gates[j][(long long)(kvh * 8 + h) * p.qg_stride + d];
+        p.outs[j][(kvh * 8 + h) * kHD + d] = o * (1.0f / (1.0f + expf(-g)));
+    }
+}
+
 int validate(const KernelAttnDecodeJob &j, int i, bool partial)
 {
     if (!j.q || !j.q_norm || !j.k_cache || !j.v_cache)
@@ -621,13 +702,22 @@ double decode_items_per_sm()
     return v;
 }
 
-// One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode.
-int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
+// One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode; `dst` + `tags`
+// select push mode (job i's merged records to dst[i], then tags[i][kvh] = epoch).
+int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *dst = nullptr,
+           unsigned *const *tags = nullptr, unsigned epoch = 0)
 {
+    if (dst) {
+        for (int i = 0; i < n; i++)
+            if (!dst[i] || !tags || !tags[i] || !aligned16(dst[i]))
+                return fail("attn decode push: job %d needs a 16-byte aligned record address and a tag", i);
+        pout = nullptr;
+    }
+    const bool partial = pout != nullptr || dst != nullptr;
     Runtime &R = rt();
     long long total = 0;
     for (int i = 0; i < n; i++) {
-        if (validate(jobs[i], i, pout != nullptr) != 0)
+        if (validate(jobs[i], i, partial) != 0)
             return -1;
         total += (long long)jobs[i].length;
     }
@@ -719,7 +809,10 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
         d.length = (long long)s.length;
         d.position = (long long)s.position;
         d.append = s.append ? 1 : 0;
+        d.pdst = dst ? dst[i] : nullptr;
+        d.ptag = dst ? tags[i] : nullptr;
     }
+    p.epoch = epoch;
     memcpy(p.inv_freq, R.inv_freq, sizeof(p.inv_freq));
     const size_t part_floats = (size_t)items * kPF, new_floats = (size_t)n * 2 * kPF;
     float *ws = static_cast<float *>(scratch((part_floats + new_floats) * sizeof(float)));
@@ -750,12 +843,14 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout)
 // allocating library, torch's caching allocator included) once serving has started, or a
 // process where allocation would serialise against other streams. For them,
 // kernel_attn_decode_batch_noalloc runs the same decode kernel with its scratch (the split
-// softmax partial records, the per-(slot, kv head) completion counters and an error word) in
-// this statically sized device array instead of library-allocated memory. Every GPU that loads
-// the library holds the array until the process exits.
+// softmax partial records and the per-(slot, kv head) completion counters) in this statically
+// sized device array instead of library-allocated memory. Every GPU that loads the library
+// holds the array until the process exits. Kernel-recorded failures go to the library's error
+// word, which kernel_cuda_init allocates once at start-up, so kernel_cuda_synchronize reports
+// them exactly as for the allocating entry point.
 constexpr size_t kNoAllocBytes = 8u << 20;                     // 8 MiB per device
-constexpr int kNoAllocCounterInts = 2 * kMaxJobs + 64;         // counters, then the error word
-constexpr size_t kNoAllocHeadBytes = 1024;                     // counters + error word, padded
+constexpr int kNoAllocCounterInts = 2 * kMaxJobs;              // one counter per (slot, kv head)
+constexpr size_t kNoAllocHeadBytes = 1024;                     // counters, padded
 constexpr size_t kNoAllocNewFloats = (size_t)kMaxJobs * 2 * kPF;
 constexpr int kNoAllocMaxItems =
     (int)((kNoAllocBytes - kNoAllocHeadBytes - kNoAllocNewFloats * sizeof(float)) / (kPF * sizeof(float)));
@@ -818,6 +913,12 @@ int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
         return -1;
     if (device < 0 || device >= 64)
         return fail("kernel_attn_decode_batch_noalloc: device %d out of range", device);
+    // The call runs on the current device, which must be the one kernel_cuda_init chose: the
+    // library's stream and error word belong to that device.
+    if (rt().device != device)
+        return fail("kernel_attn_decode_batch_noalloc: the current device is %d but the library is "
+                    "initialised on %d; call kernel_cuda_init(%d) once at start-up (the only step "
+                    "that allocates) and keep that device current", device, rt().device, device);
     if (noalloc_setup(device) != 0)
         return -1;
     const NoAllocDevice &dev = g_noalloc_dev[device];
@@ -931,20 +1032,18 @@ int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
     for (int j = 0; j < 32; j++)           // same host libm powf the reference uses
         p.inv_freq[j] = powf(10000000.0f, -2.0f * (float)j / 64.0f);
     int *cnt = reinterpret_cast<int *>(dev.base);
-    unsigned *own_err = reinterpret_cast<unsigned *>(dev.base) + 2 * kMaxJobs;
     float *ws = reinterpret_cast<float *>(dev.base + kNoAllocHeadBytes);
     p.newpart = ws;
     p.part = ws + kNoAllocNewFloats;
     p.counters = cnt;
     p.pout = nullptr;
-    // Kernel-recorded failures go to the library's error word when the caller initialised the
-    // library (so kernel_cuda_synchronize reports them), else to the array's own word.
-    p.err = rt().err_word ? rt().err_word : own_err;
+    p.err = rt().err_word;          // reported by kernel_cuda_synchronize
     p.njobs = n;
     p.nitems = items;
     cudaStream_t st = rt().stream;
     // The array keeps whatever the previous call left: the counters must start at zero.
-    if (check(cudaMemsetAsync(dev.base, 0, kNoAllocHeadBytes, st), "clear noalloc counters") != 0)
+    if (check(cudaMemsetAsync(dev.base, 0, kNoAllocCounterInts * sizeof(int), st),
+              "clear noalloc counters") != 0)
         return -1;
     attn_decode_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
     return launched("attn_decode_kernel (noalloc)");
@@ -959,6 +1058,50 @@ int attn_decode_batch(const KernelAttnDecodeJob *jobs, int n, float *pout)
     for (int i = 0; i < n; i += kMaxJobs) {
         const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
         if (launch(jobs + i, m, pout ? pout + (size_t)i * 2 * kPF : nullptr) != 0)
+            return -1;
+    }
+    return 0;
+}
+
+int attn_decode_push(const KernelAttnDecodeJob *jobs, int n, float *const *dst, unsigned *const *tags,
+                     unsigned epoch)
+{
+    if (n < 0 || (n > 0 && (!jobs || !dst || !tags)))
+        return fail("kernel_attn_decode_partial_push: bad arguments");
+    for (int i = 0; i < n; i += kMaxJobs) {
+        const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
+        if (launch(jobs + i, m, nullptr, dst + i, tags + i, epoch) != 0)
+            return -1;
+    }
+    return 0;
+}
+
+int attn_merge_wait(const float *recv, const unsigned *tags, int nparts, int n, const float *const *gates,
+                    size_t qg_stride, float *const *outs, unsigned epoch)
+{
+    if (nparts < 1 || nparts > 64 || n < 0 || !recv || !tags || (n && (!gates || !outs)))
+        return fail("attn merge wait: bad arguments (nparts %d, n %d)", nparts, n);
+    for (int i = 0; i < n; i += kMaxJobs) {
+        MWParams p;
+        memset(&p, 0, sizeof(p));
+        const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
+        for (int k = 0; k < m; k++) {
+            p.gates[k] = gates[i + k];
+            p.outs[k] = outs[i + k];
+            if (!p.gates[k] || !p.outs[k])
+                return fail("attn merge wait: null gate/out for job %d", i + k);
+        }
+        p.recv = recv;
+        p.tags = tags;
+        p.qg_stride = (long long)qg_stride;
+        p.budget = 2000000000ll;
+        p.err = rt().err_word;
+        p.nparts = nparts;
+        p.n = n;
+        p.job0 = i;
+        p.epoch = epoch;
+        attn_merge_wait_kernel<<<m * 2, 256, 0, rt().stream>>>(p);
+        if (launched("attn_merge_wait_kernel") != 0)
             return -1;
     }
     return 0;
@@ -1023,6 +1166,23 @@ extern "C" int kernel_attn_merge_partials(const float *partials, int nparts, int
     if (ensure() != 0)
         return -1;
     return attn_merge(partials, nparts, n, gates, qg_stride, outs);
+}
+
+extern "C" int kernel_attn_decode_partial_push(const KernelAttnDecodeJob *jobs, int n, float *const *dst,
+                                               unsigned *const *tags, unsigned epoch)
+{
+    if (ensure() != 0)
+        return -1;
+    return attn_decode_push(jobs, n, dst, tags, epoch);
+}
+
+extern "C" int kernel_attn_merge_wait(const float *recv, const unsigned *tags, int nparts, int n,
+                                      const float *const *gates, size_t qg_stride, float *const *outs,
+                                      unsigned epoch)
+{
+    if (ensure() != 0)
+        return -1;
+    return attn_merge_wait(recv, tags, nparts, n, gates, qg_stride, outs, epoch);
 }
 
 // Host-buffer batch: pack every job's q/gate rows, new K/V, norms into one pinned block, one

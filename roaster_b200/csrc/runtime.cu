@@ -445,6 +445,41 @@ int kernel_cuda_memmove(void *dst, const void *src, size_t bytes)
     return 0;
 }
 
+int kernel_cuda_ipc_handle(void *dev_ptr, void *handle)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!dev_ptr || !handle)
+        return fail("kernel_cuda_ipc_handle: null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == KERNEL_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    if (check(cudaIpcGetMemHandle(&h, dev_ptr), "cudaIpcGetMemHandle") != 0)
+        return -1;
+    memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+int kernel_cuda_ipc_open(const void *handle, void **dev_ptr)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!handle || !dev_ptr)
+        return fail("kernel_cuda_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *dev_ptr = nullptr;
+    return check(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int kernel_cuda_ipc_close(void *dev_ptr)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!dev_ptr)
+        return 0;
+    return check(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------- bounded-wait probe

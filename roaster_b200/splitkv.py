@@ -14,6 +14,15 @@ token. One step is:
 
 The operations are passed in, so the same host logic runs with the CUDA kernels + NCCL and, in
 tests, with CPU stand-ins over gloo.
+
+Fused form (``push_step``), with no collective call in the step: each slot has a home rank
+(``home_of``). Every rank's partial kernel writes the slot's record straight into the home
+rank's receive buffer (peer stores over NVLink into memory opened through CUDA IPC) and then
+sets a tag word to the step's epoch; the home rank's merge kernel waits on the tags of its own
+slots only, merges and gates. The receive buffer of a rank holds two halves (step parity), each
+``[world][n_home][2][PARTIAL_FLOATS]`` floats, plus tags ``[2][world][n_home][2]``: a rank can be
+at most one step ahead of a home rank that has not merged yet, so a half is never overwritten
+before it is read.
 """
 from __future__ import annotations
 
@@ -65,3 +74,61 @@ def merge_reference(gathered, gates):
             gate = np.asarray(gates[j], np.float64)[8 * kvh:8 * kvh + 8]
             out[j, 8 * kvh:8 * kvh + 8] = res / (1.0 + np.exp(-gate))
     return out.astype(np.float32)
+
+
+# ----------------------------------------------------------------------------- fused (push) form
+
+def home_of(slot: int, world: int) -> int:
+    """Rank that merges (and owns the recurrent layers of) `slot`."""
+    return slot % world
+
+
+def home_slots(n_slots: int, world: int, rank: int) -> list[int]:
+    """Slots whose home is `rank`, in the order of that rank's receive buffer."""
+    return [s for s in range(n_slots) if home_of(s, world) == rank]
+
+
+def home_count(n_slots: int, world: int, rank: int) -> int:
+    """Slots whose home is `rank` (the `n` of its receive buffer)."""
+    return len(home_slots(n_slots, world, rank))
+
+
+def recv_floats(n_slots: int, world: int, rank: int) -> int:
+    """Floats of `rank`'s receive buffer (both parity halves)."""
+    return 2 * world * home_count(n_slots, world, rank) * 2 * PARTIAL_FLOATS
+
+
+def tag_words(n_slots: int, world: int, rank: int) -> int:
+    """Tag words of `rank`'s receive buffer (both parity halves)."""
+    return 2 * world * home_count(n_slots, world, rank) * 2
+
+
+def push_targets(n_slots: int, world: int, rank: int, epoch: int, recv_bases, tag_bases):
+    """Per slot, where `rank` writes its records this step: (record address, tag address) in the
+    home rank's buffers (recv_bases / tag_bases: device addresses of every rank's receive buffer
+    and tags, this rank's own included), in the half of the step's parity."""
+    half = epoch & 1
+    dst, tags = [], []
+    for s in range(n_slots):
+        h = home_of(s, world)
+        nh = home_count(n_slots, world, h)
+        i = home_slots(n_slots, world, h).index(s)
+        rec = ((half * world + rank) * nh + i) * 2
+        dst.append(recv_bases[h] + rec * PARTIAL_FLOATS * 4)
+        tags.append(tag_bases[h] + rec * 4)
+    return dst, tags
+
+
+def merge_view(n_slots: int, world: int, rank: int, epoch: int, recv_base: int, tag_base: int):
+    """(records, tags) addresses of `rank`'s half for the step's parity: records
+    [world][n_home][2][PARTIAL_FLOATS], tags [world][n_home][2]."""
+    nh = home_count(n_slots, world, rank)
+    half = epoch & 1
+    return (recv_base + half * world * nh * 2 * PARTIAL_FLOATS * 4, tag_base + half * world * nh * 2 * 4)
+
+
+def push_step(push_fn, merge_fn):
+    """One fused split-KV step: push_fn() writes this rank's partials of every slot to the home
+    ranks (and sets the tags); merge_fn() merges this rank's home slots once all tags arrive."""
+    push_fn()
+    return merge_fn()

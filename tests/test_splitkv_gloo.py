@@ -137,3 +137,45 @@ def test_lost_rank_surfaces_as_error(tmp_path):
     assert procs[0].exitcode == 0
     assert open(tmp_path / "rank0.txt").read().startswith("error")
 
+
+
+def test_push_layout_covers_every_record_once():
+    """The fused form's buffer layout (CPU): for every world size up to 8 and both parity
+    halves, the records all ranks push land at distinct addresses inside their home rank's
+    buffer, exactly at the places that rank's merge view reads, and a numpy merge over those
+    views equals the merge of the gathered form."""
+    from roaster_b200 import splitkv
+    PF = splitkv.PARTIAL_FLOATS
+    rng = np.random.default_rng(3)
+    for world in range(1, 9):
+        for n_slots in (1, 5, 16):
+            bases = [(r + 1) << 32 for r in range(world)]           # disjoint fake address spaces
+            tbases = [(r + 1) << 40 for r in range(world)]
+            for epoch in (1, 2):
+                seen = set()
+                bufs = [np.zeros(splitkv.recv_floats(n_slots, world, r), np.float32) for r in range(world)]
+                part = rng.standard_normal((world, n_slots, 2, PF)).astype(np.float32)
+                part[..., :8] = rng.standard_normal((world, n_slots, 2, 8))
+                part[..., 8:16] = rng.uniform(0.5, 2.0, (world, n_slots, 2, 8))
+                for r in range(world):
+                    dst, tags = splitkv.push_targets(n_slots, world, r, epoch, bases, tbases)
+                    for s in range(n_slots):
+                        h = splitkv.home_of(s, world)
+                        off = dst[s] - bases[h]
+                        assert off % 16 == 0 and (dst[s], tags[s]) not in seen
+                        seen.add((dst[s], tags[s]))
+                        fo = off // 4
+                        assert 0 <= fo and fo + 2 * PF <= bufs[h].size
+                        assert (tags[s] - tbases[h]) // 4 + 2 <= splitkv.tag_words(n_slots, world, h)
+                        bufs[h][fo:fo + 2 * PF] = part[r, s].reshape(-1)
+                gates = rng.standard_normal((n_slots, 16, 256)).astype(np.float32)
+                want = splitkv.merge_reference(part, gates)
+                for h in range(world):
+                    mine = splitkv.home_slots(n_slots, world, h)
+                    if not mine:
+                        continue
+                    rv, _ = splitkv.merge_view(n_slots, world, h, epoch, bases[h], tbases[h])
+                    fo = (rv - bases[h]) // 4
+                    view = bufs[h][fo:fo + world * len(mine) * 2 * PF].reshape(world, len(mine), 2, PF)
+                    got = splitkv.merge_reference(view, gates[mine])
+                    assert np.allclose(got, want[mine], rtol=1e-5, atol=1e-6)
