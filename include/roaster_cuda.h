@@ -73,6 +73,17 @@ int   kernel_cuda_download(void *dst_host, const void *src_dev, size_t bytes); /
 int   kernel_cuda_memmove(void *dst_dev, const void *src_dev, size_t bytes);   /* overlap-safe, async */
 int   kernel_cuda_memset(void *dst_dev, int value, size_t bytes);              /* async (model_reset) */
 
+/* Register a long-lived host buffer (the model's attn_q / attn_k / attn_v / attn_out,
+ * DeltaNet q / k / v / g / beta / out, model.c:801-861 and 1291-1343) once: its pages are
+ * pinned (cudaHostRegister). When every buffer of a call to the host-buffer entry points
+ * (kernel_attn_decode_batch_host, kernel_deltanet_step_batch_host) lies in registered memory,
+ * the copy engine moves them directly, a few large copies per call (the buffers' contiguous
+ * runs), with no staging memcpy on the host; other calls go through pinned staging as before.
+ * A buffer must not be freed while registered. 0 = ok, -1 = error (e.g. pages already
+ * registered). */
+int   kernel_cuda_host_register(void *ptr, size_t bytes);
+int   kernel_cuda_host_unregister(void *ptr);
+
 /* ------------------------------------------------------------------ gated attention, decode
  * Replaces model.c:801-861 (Q|G split, q/k RMSNorm, partial RoPE, KV append, GQA softmax
  * attention over the window, sigmoid output gate) for one token per slot. */
@@ -109,9 +120,9 @@ int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n);
  * exists for callers that must not allocate device memory once they are serving -- a host
  * running under a device-memory budget fixed at start-up, or code that may not enter the CUDA
  * allocator (or an allocating library such as torch's caching allocator) at decode time.
- * It never calls cudaMalloc/cudaFree: its scratch (split softmax partials, completion counters)
- * is one statically sized 8 MiB device array that every GPU loading this library holds until
- * the process exits. Limits: at most 64 slots per call (more is rejected with an error);
+ * It never calls cudaMalloc/cudaFree: its scratch (the split softmax partial records) is one
+ * statically sized 8 MiB device array that every GPU loading this library holds until the
+ * process exits. Limits: at most 64 slots per call (more is rejected with an error);
  * windows of any length (the split size grows so the partials fit the array).
  * Device: the call runs on the current device, which must be the one kernel_cuda_init chose;
  * kernel_cuda_init (which allocates the library's 256-byte error word) must run once at
@@ -120,8 +131,9 @@ int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, int n);
  * error word and are reported by kernel_cuda_synchronize, as for kernel_attn_decode_batch.
  * The first call on each device does a one-time set-up (it looks up the array's device address
  * and the SM count) and should come before any stream capture. Every call shares the one array
- * and clears its counters at the start, so calls whose work overlaps on the GPU (different
- * streams, or different threads) race and must be serialised by the caller. Same job semantics,
+ * (each call writes every record it reads, so nothing needs clearing between calls), so calls
+ * whose work overlaps on the GPU (different streams, or different threads) race and must be
+ * serialised by the caller. Same job semantics,
  * results and asynchrony as kernel_attn_decode_batch, on the library stream; all pointers device
  * memory. */
 int kernel_attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n);

@@ -43,7 +43,6 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
-#include <queue>
 #include <utility>
 #include <vector>
 
@@ -85,7 +84,6 @@ struct DParams {
     float inv_freq[32];
     float *part;        // [nitems][kPF]
     float *newpart;     // [njobs][2][kPF]
-    int *counters;      // [njobs][2]
     float *pout;        // partial mode: [njobs][2][kPF], else null
     unsigned *err;
     int njobs, nitems;
@@ -94,20 +92,19 @@ struct DParams {
 
 struct Smem {
     unsigned char stage[kStages][kStageBytes];   // [K|V][4 chunks][32 pos][128 B], swizzled
-    float qf[8][kHD];                     // prepped q (fp32) of the current item
+    float qf[2][8][kHD];                  // prepped q (fp32), double-buffered by item parity
     float kf[kHD];                        // prepped new k
     union {
         float ow[kCons][8][kOStride];     // per-warp O (merge of the 4 warps)
-        struct {                          // combine of all partials of a (slot, kv head)
-            float m[kMaxSplits + 1][8], l[kMaxSplits + 1][8], w[kMaxSplits + 1][8];
-        } c;
     } u;
     float mw[kCons][8], lw[kCons][8];
     float red[8];
     alignas(8) unsigned long long full[kStages], empty[kStages];
-    int flag, abort;
+    alignas(8) unsigned long long qready[2], qfree[2];   // qf hand-off: producers -> consumers
+    int abort;
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 128;   // + alignment slack
+static_assert(kSmemBytes <= 232448, "decode kernel shared memory exceeds a CTA's");
 
 __device__ __forceinline__ void item_decode(const DParams &p, int idx, int &j, int &kvh, int &split, int &item)
 {
@@ -137,41 +134,53 @@ __device__ __forceinline__ bool aborted(Smem &sm)
     return *reinterpret_cast<volatile int *>(&sm.abort) != 0;
 }
 
-// RMSNorm * w then RoPE of the 8 query heads of kv head `kvh` into sm.qf (128 consumer threads).
-__device__ void prep_q(const DParams &p, const DJob &J, int kvh, Smem &sm, int t)
+// RMSNorm * w then RoPE (dims 0..63) of query heads 2*pw and 2*pw + 1 of kv head `kvh` into qf,
+// by one warp with shuffles only: lane l holds elements l + 32 i of a head, so the RoPE pair
+// (d, d + 32) of d = lane sits in one lane. The four producer warps together prepare the 8 heads.
+__device__ void prep_q_warp(const DParams &p, const DJob &J, int kvh, float (*qf)[kHD], int pw, int lane)
 {
-    const int h = t >> 4, g = t & 15;
-    const float *src = J.q + (long long)(kvh * 8 + h) * J.qg_stride;
-    float x[16], ss = 0.f;
+    // every load first (both heads' rows and the norm weights: one memory round trip)
+    float x[2][8], w[8];
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        x[i] = __ldg(src + g + 16 * i);
-        ss = fmaf(x[i], x[i], ss);
+    for (int hh = 0; hh < 2; hh++) {
+        const float *src = J.q + (long long)(kvh * 8 + 2 * pw + hh) * J.qg_stride;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            x[hh][i] = __ldg(src + lane + 32 * i);
     }
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1)
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = 1.0f / sqrtf(ss / (float)kHD + 1e-6f);
+    for (int i = 0; i < 8; i++)
+        w[i] = __ldg(J.q_norm + lane + 32 * i);
+    float sn, cs;
+    sincosf((float)J.position * p.inv_freq[lane], &sn, &cs);
 #pragma unroll
-    for (int i = 0; i < 16; i++)
-        sm.qf[h][g + 16 * i] = x[i] * inv * __ldg(J.q_norm + g + 16 * i);
-    named_bar_sync(1, 128);
-    const float pos = (float)J.position;
+    for (int hh = 0; hh < 2; hh++) {
+        const int h = 2 * pw + hh;
+        float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-        const int pi = t + 128 * k, hh = pi >> 5, jj = pi & 31;
-        float sn, cs;
-        sincosf(pos * p.inv_freq[jj], &sn, &cs);
-        const float a = sm.qf[hh][jj], b = sm.qf[hh][jj + 32];
-        sm.qf[hh][jj] = a * cs - b * sn;
-        sm.qf[hh][jj + 32] = b * cs + a * sn;
+        for (int i = 0; i < 8; i++)
+            ss = fmaf(x[hh][i], x[hh][i], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / (float)kHD + 1e-6f);
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            y[i] = x[hh][i] * inv * w[i];
+        const float a = y[0], b = y[1];
+        y[0] = a * cs - b * sn;
+        y[1] = b * cs + a * sn;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            qf[h][lane + 32 * i] = y[i];
     }
-    named_bar_sync(1, 128);
 }
 
 // New token of (job, kvh): normalise + rotate k, append K/V (f16) at index `length`, and write
 // its fp32 softmax partial (m = q.k/16 in log2 units, l = 1, o = v).
-__device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, Smem &sm, int t)
+__device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, const float (*qf)[kHD], Smem &sm,
+                          int t)
 {
     const float *kn = J.k_new + kvh * kHD;
     const float x0 = __ldg(kn + t), x1 = __ldg(kn + t + 128);
@@ -207,7 +216,7 @@ __device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, Sm
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; i++)
-        s = fmaf(sm.qf[h][g + 16 * i], sm.kf[g + 16 * i], s);
+        s = fmaf(qf[h][g + 16 * i], sm.kf[g + 16 * i], s);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1)
         s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -220,81 +229,116 @@ __device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, Sm
         rec[16 + e] = __ldg(vn + (e & (kHD - 1)));
 }
 
-// Merge `nparts` partial records (pointers from `rec_at`) of one (job, kvh) into either the
-// gated output (p.pout == null) or one merged record. All loads of a pass are independent, so a
-// pass costs one memory round trip rather than one per part.
-template <typename RecAt>
-__device__ void combine(const DParams &p, const DJob &J, int jidx, int kvh, int nparts, RecAt rec_at,
-                        Smem &sm, int t)
+// Combine of one launch's partial records. Grid: (n jobs x 2 kv heads x 8 query heads), or
+// (n jobs x 2) in push mode, where one block covers the 8 heads of a record before releasing
+// its tag. 256 threads = 4 part groups x 64 threads of 4 output dims. Each (job, kv head) merges
+// its nsplit split records plus the new token's record: M = max m_i, w_i = l_i 2^(m_i - M),
+// o = sum w_i o_i / sum w_i. Part group g takes parts g, g + 4, ... (up to 8 per batch, every
+// load of a batch issued before its arithmetic) and the four groups' sums are added in group
+// order, so a block costs about two memory round trips and the result does not depend on
+// timing. Output: the gated result (o * sigmoid(gate)), or in partial / push mode one merged
+// record (m = M, l = sum w_i, o) to p.pout / the job's push address, then the push tag.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant__ DParams p)
 {
-    for (int idx = t; idx < nparts * 8; idx += 128) {
-        const int i = idx >> 3, h = idx & 7;
-        sm.u.c.m[i][h] = __ldcg(rec_at(i) + h);
-        sm.u.c.l[i][h] = __ldcg(rec_at(i) + 8 + h);
-    }
-    named_bar_sync(1, 128);
-    if (t < 8) {               // per head: M = max m_i, w_i = l_i exp2(m_i - M), L = sum w_i
-        float M = -INFINITY;
-        for (int i = 0; i < nparts; i++)
-            M = fmaxf(M, sm.u.c.m[i][t]);
+    __shared__ float red[8];
+    __shared__ float4 gacc[4][64];
+    __shared__ float gl[4];
+    griddep_wait();
+    griddep_launch_dependents();
+    const bool push = p.jobs[0].ptag != nullptr;
+    const int j = push ? blockIdx.x >> 1 : blockIdx.x >> 4;
+    const int kvh = push ? blockIdx.x & 1 : (blockIdx.x >> 3) & 1;
+    const DJob &J = p.jobs[j];
+    const int t = threadIdx.x, grp = t >> 6, d = (t & 63) * 4;
+    const int ns = J.nsplit, np = ns + (J.append ? 1 : 0);
+    const float *part0 = p.part + (long long)(J.item_base + kvh) * kPF;
+    const float *newp = p.newpart + ((long long)j * 2 + kvh) * kPF;
+    auto rec = [&](int i) { return i < ns ? part0 + (long long)i * 2 * kPF : newp; };
+    float *dst = J.pdst ? J.pdst + kvh * kPF : (p.pout ? p.pout + ((long long)j * 2 + kvh) * kPF : nullptr);
+    const int h0 = push ? 0 : (blockIdx.x & 7), h1 = push ? 8 : h0 + 1;
+    for (int h = h0; h < h1; h++) {
+        float m = -INFINITY;
+        for (int i = t; i < np; i += 256)
+            m = fmaxf(m, __ldcg(rec(i) + h));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((t & 31) == 0)
+            red[t >> 5] = m;
+        __syncthreads();
+        float M = red[0];
+#pragma unroll
+        for (int w = 1; w < 8; w++)
+            M = fmaxf(M, red[w]);
+        constexpr int B = 8;
         float L = 0.f;
-        for (int i = 0; i < nparts; i++) {
-            const float m = sm.u.c.m[i][t];
-            const float w = (m == -INFINITY) ? 0.f : sm.u.c.l[i][t] * exp2f(m - M);
-            sm.u.c.w[i][t] = w;
-            L += w;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i0 = grp; i0 < np; i0 += 4 * B) {
+            float mv[B], lv[B];
+            float4 vv[B];
+#pragma unroll
+            for (int u = 0; u < B; u++) {
+                const int i = i0 + 4 * u;
+                if (i < np) {
+                    const float *r = rec(i);
+                    mv[u] = __ldcg(r + h);
+                    lv[u] = __ldcg(r + 8 + h);
+                    vv[u] = __ldcg(reinterpret_cast<const float4 *>(r + 16 + h * kHD + d));
+                } else {
+                    mv[u] = -INFINITY;
+                    lv[u] = 0.f;
+                    vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < B; u++) {
+                const float w = (mv[u] == -INFINITY) ? 0.f : lv[u] * exp2f(mv[u] - M);
+                L += w;
+                acc.x = fmaf(w, vv[u].x, acc.x);
+                acc.y = fmaf(w, vv[u].y, acc.y);
+                acc.z = fmaf(w, vv[u].z, acc.z);
+                acc.w = fmaf(w, vv[u].w, acc.w);
+            }
         }
-        sm.mw[0][t] = M;
-        sm.lw[0][t] = L;
-    }
-    named_bar_sync(1, 128);
-    float *dst = J.pdst ? J.pdst + kvh * kPF : (p.pout ? p.pout + ((long long)jidx * 2 + kvh) * kPF : nullptr);
-    if (dst && t < 8) {
-        dst[t] = sm.mw[0][t];
-        dst[8 + t] = sm.lw[0][t];
-    }
-    // thread t owns float4 groups e = 4t + 512k (k = 0..3): head (t >> 6) + 2k, dims 4t % 256
-    float4 acc[4];
+        gacc[grp][t & 63] = acc;
+        if ((t & 63) == 0)
+            gl[grp] = L;
+        __syncthreads();
+        if (grp == 0) {
+            float4 a = gacc[0][t];
+            float Lt = gl[0];
 #pragma unroll
-    for (int k = 0; k < 4; k++)
-        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
-    for (int i = 0; i < nparts; i++) {
-        const float *rec = rec_at(i) + 16;
-        float4 v[4];
+            for (int g2 = 1; g2 < 4; g2++) {
+                const float4 b = gacc[g2][t];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+                Lt += gl[g2];
+            }
+            const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+            const float o[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};
+            if (dst) {
+                if (t == 0) {
+                    dst[h] = M;
+                    dst[8 + h] = Lt;
+                }
+                *reinterpret_cast<float4 *>(dst + 16 + h * kHD + d) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+                const float *g = J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d;
+                float *out = J.out + (kvh * 8 + h) * kHD + d;
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            v[k] = __ldcg(reinterpret_cast<const float4 *>(rec + 4 * t + 512 * k));
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float w = sm.u.c.w[i][(t >> 6) + 2 * k];
-            acc[k].x = fmaf(w, v[k].x, acc[k].x);
-            acc[k].y = fmaf(w, v[k].y, acc[k].y);
-            acc[k].z = fmaf(w, v[k].z, acc[k].z);
-            acc[k].w = fmaf(w, v[k].w, acc[k].w);
+                for (int x = 0; x < 4; x++)
+                    out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
+            }
         }
+        __syncthreads();                   // red / gacc are reused by the next head
     }
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const int h = (t >> 6) + 2 * k, d = (4 * t) & (kHD - 1);
-        const float L = sm.lw[0][h];
-        const float inv = L > 0.f ? 1.0f / L : 0.f;
-        float o[4] = {acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv};
-        if (dst) {
-            *reinterpret_cast<float4 *>(dst + 16 + h * kHD + d) = make_float4(o[0], o[1], o[2], o[3]);
-        } else {
-            const float *g = J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d;
-            float *out = J.out + (kvh * 8 + h) * kHD + d;
-#pragma unroll
-            for (int x = 0; x < 4; x++)
-                out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
-        }
-    }
-    if (J.ptag) {
+    if (push) {
         // Every writer makes its record stores visible system-wide before the tag goes out:
         // the home GPU reads the record as soon as it sees the tag.
         __threadfence_system();
-        named_bar_sync(1, 128);
+        __syncthreads();
         if (t == 0)
             st_release_sys(J.ptag + kvh, p.epoch);
     }
@@ -312,10 +356,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             mbar_init(smem_addr(&sm.full[s]), kProd * 32);   // one cp.async arrival per producer thread
             mbar_init(smem_addr(&sm.empty[s]), 1);           // the consuming warp
         }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(smem_addr(&sm.qready[b]), kProd);      // one arrival per producer warp
+            mbar_init(smem_addr(&sm.qfree[b]), kCons);       // one arrival per consumer warp
+        }
         sm.abort = 0;
         mbar_init_fence();
     }
     __syncthreads();
+    griddep_wait();                  // inputs are written by the kernels before this one
+    griddep_launch_dependents();     // the combine's blocks wait (griddep_wait) for this grid's end
 
     if (warp >= kCons) {
         // ------------------------------------------------------------ producers (128 threads)
@@ -325,9 +375,29 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         const int pw = warp - kCons;
         const uint32_t ldst = (uint32_t)(lane >> 3) * kChunkBytes;
         unsigned seq = 0;
-        for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1] && !aborted(sm); idx++) {
+        const int i0 = p.cta_off[blockIdx.x], i1 = p.cta_off[blockIdx.x + 1];
+        // Prepare the q of this CTA's k-th item into qf[k & 1] once the consumers released that
+        // buffer (its use two items earlier).
+        auto prep = [&](int k) -> bool {
+            const int b = k & 1;
+            const unsigned u = (unsigned)k >> 1;
+            if (u > 0 && !mbar_wait(smem_addr(&sm.qfree[b]), (u - 1) & 1)) {
+                if (lane == 0)
+                    set_error(p, kErrWaitTimeout, sm);
+                return false;
+            }
+            int jj, kh, sp, it;
+            item_decode(p, i0 + k, jj, kh, sp, it);
+            prep_q_warp(p, p.jobs[jj], kh, sm.qf[b], pw, lane);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(smem_addr(&sm.qready[b]));
+            return true;
+        };
+        bool ok = true;
+        for (int k = 0; i0 + k < i1 && ok && !aborted(sm); k++) {
             int j, kvh, split, item;
-            item_decode(p, idx, j, kvh, split, item);
+            item_decode(p, i0 + k, j, kvh, split, item);
             const DJob &J = p.jobs[j];
             long long t0, t1;
             item_range(J, split, t0, t1);
@@ -335,8 +405,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             const long long avail = J.length - t0;          // rows that exist from t0 on
             const __half *kg = J.k_cache + (t0 * 2 + kvh) * kHD + lane * 8;
             const __half *vg = J.v_cache + (t0 * 2 + kvh) * kHD + lane * 8;
-            bool ok = true;
-            for (int i = 0; i < ntiles; i++, seq++) {
+            // the first item's q is prepared once its first stages are on their way
+            const int early = ntiles < kStages ? ntiles : kStages;
+            if (k == 0 && early == 0)
+                ok = prep(0);
+            for (int i = 0; i < ntiles && ok; i++, seq++) {
                 const int s = seq % kStages;
                 const unsigned f = seq / kStages;
                 if (f > 0 && !mbar_wait(smem_addr(&sm.empty[s]), (f - 1) & 1)) {
@@ -347,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 }
                 const uint32_t st = smem_addr(&sm.stage[s][0]) + ldst;
 #pragma unroll
-                for (int k = 0; k < kTile / kProd; k++) {
-                    const int pos = pw + kProd * k;
+                for (int kk = 0; kk < kTile / kProd; kk++) {
+                    const int pos = pw + kProd * kk;
                     const long long row = (long long)i * kTile + pos;
                     if (row < avail) {
                         const uint32_t d = st + pos * 128 + (((lane & 7) ^ (pos & 7)) << 4);
@@ -357,9 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                     }
                 }
                 cp_async_arrive(smem_addr(&sm.full[s]));
+                if (k == 0 && i == early - 1)
+                    ok = prep(0);
             }
-            if (!ok)
-                break;
+            // the next item's q, ready while the consumers finish this item from the ring
+            if (ok && i0 + k + 1 < i1)
+                ok = prep(k + 1);
         }
         cp_async_wait_all();     // nothing of ours may still be landing when the CTA retires
         return;
@@ -379,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const uint32_t krow = (uint32_t)(lane & 15) * 128;
     const uint32_t vrow = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * 128;
 
-    for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1]; idx++) {
+    int kq = 0;                                  // this CTA's item counter
+    for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1]; idx++, kq++) {
         int j, kvh, split, item;
         item_decode(p, idx, j, kvh, split, item);
         const DJob &J = p.jobs[j];
@@ -387,17 +464,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         item_range(J, split, t0, t1);
         const int ntiles = (int)((t1 - t0 + kTile - 1) / kTile);
 
-        prep_q(p, J, kvh, sm, t);
+        // the producers prepared this item's q into qf[kq & 1]; a wait that runs out records the
+        // error and goes on, so every consumer warp still meets the barriers below
+        const int qbuf = kq & 1;
+        if (!mbar_wait(smem_addr(&sm.qready[qbuf]), ((unsigned)kq >> 1) & 1) && lane == 0)
+            set_error(p, kErrWaitTimeout, sm);
         if (split == 0 && J.append)
-            new_token(p, J, j, kvh, sm, t);
+            new_token(p, J, j, kvh, sm.qf[qbuf], sm, t);
 
         uint32_t qb[16][2];
 #pragma unroll
         for (int ks = 0; ks < 16; ks++) {
-            const float *qr = &sm.qf[r][ks * 16 + cpair];
+            const float *qr = &sm.qf[qbuf][r][ks * 16 + cpair];
             qb[ks][0] = pack_f16x2(qr[0], qr[1]);
             qb[ks][1] = pack_f16x2(qr[8], qr[9]);
         }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(smem_addr(&sm.qfree[qbuf]));
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
         float o[16][4];
 #pragma unroll
@@ -532,25 +616,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 rec[8 + h] = L;
             }
         }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (t == 0) {
-            const int prev = atomicAdd(p.counters + j * 2 + kvh, 1);
-            sm.flag = (prev == J.nsplit - 1);
-        }
-        named_bar_sync(1, 128);
-        if (sm.flag) {
-            __threadfence();
-            const int ns = J.nsplit;
-            const float *part0 = p.part + (long long)(J.item_base + kvh) * kPF;
-            const float *np = p.newpart + ((long long)j * 2 + kvh) * kPF;
-            auto rec_at = [&](int i) -> const float * {
-                return i < ns ? part0 + (long long)i * 2 * kPF : np;
-            };
-            combine(p, J, j, kvh, ns + (J.append ? 1 : 0), rec_at, sm, t);
-            if (t == 0)
-                p.counters[j * 2 + kvh] = 0;
-        }
         named_bar_sync(1, 128);
         if (aborted(sm))
             break;
@@ -568,7 +633,7 @@ struct MParams {
 
 __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__ MParams p)
 {
-    __shared__ float w[64][8], Ms[8], Ls[8];
+    __shared__ float w[64][8], Ls[8];
     const int j = blockIdx.x >> 1, kvh = blockIdx.x & 1, t = threadIdx.x;
     const long long stride = (long long)p.n * 2 * kPF;
     const float *rec0 = p.partials + ((long long)(p.job0 + j) * 2 + kvh) * kPF;
@@ -582,7 +647,6 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__
             w[i][t] = x;
             L += x;
         }
-        Ms[t] = M;
         Ls[t] = L;
     }
     __syncthreads();
@@ -614,7 +678,7 @@ struct MWParams {
 
 __global__ void __launch_bounds__(256) attn_merge_wait_kernel(const __grid_constant__ MWParams p)
 {
-    __shared__ float w[64][8], Ms[8], Ls[8];
+    __shared__ float w[64][8], Ls[8];
     __shared__ int ready;
     const int j = blockIdx.x >> 1, kvh = blockIdx.x & 1, t = threadIdx.x;
     if (t < 32) {
@@ -652,7 +716,6 @@ __global__ void __launch_bounds__(256) attn_merge_wait_kernel(const __grid_const
             w[i][t] = x;
             L += x;
         }
-        Ms[t] = M;
         Ls[t] = L;
     }
     __syncthreads();
@@ -691,6 +754,17 @@ int validate(const KernelAttnDecodeJob &j, int i, bool partial)
 
 bool g_attr_set = false;
 
+// The decode kernel, then the combine kernel, each as a programmatic dependent of the kernel
+// before it (the combine's blocks are scheduled as decode CTAs retire and wait in griddep_wait
+// for the whole decode grid).
+int launch_pair(const DParams &p, int grid, cudaStream_t st)
+{
+    if (launch_dependent(attn_decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, "attn_decode_kernel", p) != 0)
+        return -1;
+    return launch_dependent(attn_combine_kernel, dim3((unsigned)p.njobs * (p.jobs[0].ptag ? 2 : 16)), dim3(256), 0,
+                            st, "attn_combine_kernel", p);
+}
+
 // Items per SM the planner aims for (per kv head pair). ROASTER_DECODE_ITEMS_PER_SM overrides.
 double decode_items_per_sm()
 {
@@ -702,43 +776,34 @@ double decode_items_per_sm()
     return v;
 }
 
-// One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode; `dst` + `tags`
-// select push mode (job i's merged records to dst[i], then tags[i][kvh] = epoch).
-int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *dst = nullptr,
-           unsigned *const *tags = nullptr, unsigned epoch = 0)
+struct PlanItem {
+    long long cost;
+    unsigned short code;      // (job << 9) | (split << 1) | kv head
+    short cta;
+};
+
+// Split plan and CTA assignment of one launch, shared by every entry point. Each slot's window
+// is cut into equal splits of about `target` positions, target = total / (SMs x items per SM),
+// doubled until the (slot, kv head, split) items fit `cap_items`; the items then go longest
+// first (ties in item order) onto the least-loaded of the grid's CTAs (ties to the lower id),
+// an item costing its positions plus a fixed 256 for its set-up and record. Fills
+// p.jobs[i].chunk / nsplit / item_base, p.sched, p.cta_off and p.nitems; returns the grid size,
+// or -1 when the batch cannot be planned. Allocates no heap memory.
+int plan(const KernelAttnDecodeJob *jobs, int n, int num_sms, int cap_items, DParams &p)
 {
-    if (dst) {
-        for (int i = 0; i < n; i++)
-            if (!dst[i] || !tags || !tags[i] || !aligned16(dst[i]))
-                return fail("attn decode push: job %d needs a 16-byte aligned record address and a tag", i);
-        pout = nullptr;
-    }
-    const bool partial = pout != nullptr || dst != nullptr;
-    Runtime &R = rt();
     long long total = 0;
-    for (int i = 0; i < n; i++) {
-        if (validate(jobs[i], i, partial) != 0)
-            return -1;
+    for (int i = 0; i < n; i++)
         total += (long long)jobs[i].length;
-    }
-    // Equal splits of about `target` positions per slot, then longest-first assignment of the
-    // (slot, kv head, split) items onto the least-loaded CTA.
-    const double per_sm = decode_items_per_sm();
-    long long target = (long long)((double)total / ((double)R.num_sms * per_sm)) + 1;
+    long long target = (long long)((double)total / ((double)num_sms * decode_items_per_sm())) + 1;
     if (target < 2 * kTile)
         target = 2 * kTile;
-    DParams p;
-    memset(static_cast<void *>(&p), 0, sizeof(p));
     int items = 0;
     for (int attempt = 0;; attempt++) {
         items = 0;
         for (int i = 0; i < n; i++) {
             const long long L = (long long)jobs[i].length;
             long long ns = (L + target / 2) / target;
-            if (ns < 1)
-                ns = 1;
-            if (ns > kMaxSplits)
-                ns = kMaxSplits;
+            ns = ns < 1 ? 1 : (ns > kMaxSplits ? kMaxSplits : ns);
             long long ch = (L + ns - 1) / ns;
             ch = (ch + kTile - 1) / kTile * kTile;
             if (ch < kTile)
@@ -751,48 +816,73 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *ds
             p.jobs[i].item_base = items;
             items += 2 * (int)ns;
         }
-        if (items <= kMaxItems)
+        if (items <= cap_items)
             break;
-        if (attempt > 40)
-            return fail("attn decode: cannot plan %d slots within %d items", n, kMaxItems);
+        if (attempt > 40) {
+            fail("attn decode: cannot plan %d slots within %d items", n, cap_items);
+            return -1;
+        }
         target *= 2;
     }
-    const int grid = items < R.num_sms ? items : (R.num_sms < kMaxCtas ? R.num_sms : kMaxCtas);
-    {
-        // cost of an item ~ its positions plus a fixed per-item overhead
-        std::vector<std::pair<long long, unsigned short>> order;
-        order.reserve(items);
-        for (int i = 0; i < n; i++) {
-            const DJob &d = p.jobs[i];
-            for (int sp = 0; sp < d.nsplit; sp++) {
-                long long t0 = (long long)sp * d.chunk, t1 = std::min<long long>(t0 + d.chunk, (long long)jobs[i].length);
-                const long long cost = (t1 > t0 ? t1 - t0 : 0) + 256;
-                for (int kvh = 0; kvh < 2; kvh++)
-                    order.emplace_back(cost, (unsigned short)((i << 9) | (sp << 1) | kvh));
-            }
+    const int ctas = num_sms < kMaxCtas ? num_sms : kMaxCtas;
+    const int grid = items < ctas ? items : ctas;
+    PlanItem order[kMaxItems];
+    int k = 0;
+    for (int i = 0; i < n; i++) {
+        const DJob &d = p.jobs[i];
+        for (int sp = 0; sp < d.nsplit; sp++) {
+            const long long t0 = (long long)sp * d.chunk;
+            const long long t1 = std::min<long long>(t0 + d.chunk, (long long)jobs[i].length);
+            for (int kvh = 0; kvh < 2; kvh++)
+                order[k++] = PlanItem{(t1 > t0 ? t1 - t0 : 0) + 256, (unsigned short)((i << 9) | (sp << 1) | kvh), 0};
         }
-        std::stable_sort(order.begin(), order.end(),
-                         [](const std::pair<long long, unsigned short> &a,
-                            const std::pair<long long, unsigned short> &b) { return a.first > b.first; });
-        std::vector<std::vector<unsigned short>> per(grid);
-        std::priority_queue<std::pair<long long, int>, std::vector<std::pair<long long, int>>,
-                            std::greater<std::pair<long long, int>>> heap;
-        for (int c = 0; c < grid; c++)
-            heap.emplace(0ll, c);
-        for (const auto &it : order) {
-            auto top = heap.top();
-            heap.pop();
-            per[top.second].push_back(it.second);
-            heap.emplace(top.first + it.first, top.second);
-        }
-        int k = 0;
-        for (int c = 0; c < grid; c++) {
-            p.cta_off[c] = (unsigned short)k;
-            for (unsigned short e : per[c])
-                p.sched[k++] = e;
-        }
-        p.cta_off[grid] = (unsigned short)k;
     }
+    std::sort(order, order + items, [](const PlanItem &a, const PlanItem &b) {
+        return a.cost != b.cost ? a.cost > b.cost : a.code < b.code;
+    });
+    long long load[kMaxCtas] = {0};
+    int heap[kMaxCtas];                      // binary min-heap of CTA ids by (load, id)
+    auto less = [&](int a, int b) { return load[a] != load[b] ? load[a] < load[b] : a < b; };
+    for (int c = 0; c < grid; c++) {
+        load[c] = 0;
+        heap[c] = c;
+    }
+    for (int it = 0; it < items; it++) {
+        const int c = heap[0];
+        order[it].cta = (short)c;
+        load[c] += order[it].cost;
+        int pos = 0;                          // sift the grown root down
+        for (;;) {
+            const int l = 2 * pos + 1, r = l + 1;
+            int m = pos;
+            if (l < grid && less(heap[l], heap[m]))
+                m = l;
+            if (r < grid && less(heap[r], heap[m]))
+                m = r;
+            if (m == pos)
+                break;
+            std::swap(heap[pos], heap[m]);
+            pos = m;
+        }
+    }
+    int count[kMaxCtas + 1];
+    for (int c = 0; c <= grid; c++)
+        count[c] = 0;
+    for (int it = 0; it < items; it++)
+        count[order[it].cta + 1]++;
+    for (int c = 0; c < grid; c++)
+        count[c + 1] += count[c];
+    for (int c = 0; c <= grid; c++)
+        p.cta_off[c] = (unsigned short)count[c];
+    for (int it = 0; it < items; it++)
+        p.sched[count[order[it].cta]++] = order[it].code;
+    p.nitems = items;
+    return grid;
+}
+
+// The jobs' pointers and scalars into the kernel's job table.
+void fill_jobs(const KernelAttnDecodeJob *jobs, int n, DParams &p, float *const *dst, unsigned *const *tags)
+{
     for (int i = 0; i < n; i++) {
         const KernelAttnDecodeJob &s = jobs[i];
         DJob &d = p.jobs[i];
@@ -812,28 +902,49 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *ds
         d.pdst = dst ? dst[i] : nullptr;
         d.ptag = dst ? tags[i] : nullptr;
     }
+    p.njobs = n;
+}
+
+// One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode; `dst` + `tags`
+// select push mode (job i's merged records to dst[i], then tags[i][kvh] = epoch).
+int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *dst = nullptr,
+           unsigned *const *tags = nullptr, unsigned epoch = 0)
+{
+    if (dst) {
+        for (int i = 0; i < n; i++)
+            if (!dst[i] || !tags || !tags[i] || !aligned16(dst[i]))
+                return fail("attn decode push: job %d needs a 16-byte aligned record address and a tag", i);
+        pout = nullptr;
+    }
+    const bool partial = pout != nullptr || dst != nullptr;
+    Runtime &R = rt();
+    for (int i = 0; i < n; i++)
+        if (validate(jobs[i], i, partial) != 0)
+            return -1;
+    DParams p;
+    memset(static_cast<void *>(&p), 0, sizeof(p));
+    const int grid = plan(jobs, n, R.num_sms, kMaxItems, p);
+    if (grid < 0)
+        return -1;
+    const int items = p.nitems;
+    fill_jobs(jobs, n, p, dst, tags);
     p.epoch = epoch;
     memcpy(p.inv_freq, R.inv_freq, sizeof(p.inv_freq));
     const size_t part_floats = (size_t)items * kPF, new_floats = (size_t)n * 2 * kPF;
     float *ws = static_cast<float *>(scratch((part_floats + new_floats) * sizeof(float)));
-    int *cnt = counters((size_t)kMaxJobs * 2);
-    if (!ws || !cnt)
+    if (!ws)
         return -1;
     p.part = ws;
     p.newpart = ws + part_floats;
-    p.counters = cnt;
     p.pout = pout;
     p.err = R.err_word;
-    p.njobs = n;
-    p.nitems = items;
     if (!g_attr_set) {
         if (check(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes), "attn decode smem attribute") != 0)
             return -1;
         g_attr_set = true;
     }
-    attn_decode_kernel<<<grid, kThreads, kSmemBytes, R.stream>>>(p);
-    return launched("attn_decode_kernel");
+    return launch_pair(p, grid, R.stream);
 }
 
 // ---------------------------------------------------------------- allocation-free variant
@@ -842,19 +953,16 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *ds
 // device-memory budget handed out up front, code that must not enter the CUDA allocator (or any
 // allocating library, torch's caching allocator included) once serving has started, or a
 // process where allocation would serialise against other streams. For them,
-// kernel_attn_decode_batch_noalloc runs the same decode kernel with its scratch (the split
-// softmax partial records and the per-(slot, kv head) completion counters) in this statically
-// sized device array instead of library-allocated memory. Every GPU that loads the library
+// kernel_attn_decode_batch_noalloc runs the same decode and combine kernels with their scratch
+// (the split softmax partial records) in this statically sized device array instead of
+// library-allocated memory. Every GPU that loads the library
 // holds the array until the process exits. Kernel-recorded failures go to the library's error
 // word, which kernel_cuda_init allocates once at start-up, so kernel_cuda_synchronize reports
 // them exactly as for the allocating entry point.
 constexpr size_t kNoAllocBytes = 8u << 20;                     // 8 MiB per device
-constexpr int kNoAllocCounterInts = 2 * kMaxJobs;              // one counter per (slot, kv head)
-constexpr size_t kNoAllocHeadBytes = 1024;                     // counters, padded
 constexpr size_t kNoAllocNewFloats = (size_t)kMaxJobs * 2 * kPF;
 constexpr int kNoAllocMaxItems =
-    (int)((kNoAllocBytes - kNoAllocHeadBytes - kNoAllocNewFloats * sizeof(float)) / (kPF * sizeof(float)));
-static_assert(kNoAllocCounterInts * sizeof(int) <= kNoAllocHeadBytes, "head too small");
+    (int)((kNoAllocBytes - kNoAllocNewFloats * sizeof(float)) / (kPF * sizeof(float)));
 static_assert(kNoAllocMaxItems >= 4 * kMaxJobs, "static scratch too small for a full batch");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
@@ -891,12 +999,6 @@ int noalloc_setup(int device)
     return 0;
 }
 
-struct NoAllocItem {
-    long long cost;
-    unsigned short code;
-    short cta;
-};
-
 }  // namespace
 
 int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
@@ -922,131 +1024,26 @@ int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
     if (noalloc_setup(device) != 0)
         return -1;
     const NoAllocDevice &dev = g_noalloc_dev[device];
-    long long total = 0;
-    for (int i = 0; i < n; i++) {
+    for (int i = 0; i < n; i++)
         if (validate(jobs[i], i, false) != 0)
             return -1;
-        total += (long long)jobs[i].length;
-    }
-    // Same split rule as the allocating path, capped at the items the static array holds.
-    long long target = (long long)((double)total / ((double)dev.num_sms * decode_items_per_sm())) + 1;
-    if (target < 2 * kTile)
-        target = 2 * kTile;
     DParams p;
     memset(static_cast<void *>(&p), 0, sizeof(p));
-    const int cap_items = kNoAllocMaxItems < kMaxItems ? kNoAllocMaxItems : kMaxItems;
-    int items = 0;
-    for (int attempt = 0;; attempt++) {
-        items = 0;
-        for (int i = 0; i < n; i++) {
-            const long long L = (long long)jobs[i].length;
-            long long ns = (L + target / 2) / target;
-            ns = ns < 1 ? 1 : (ns > kMaxSplits ? kMaxSplits : ns);
-            long long ch = (L + ns - 1) / ns;
-            ch = (ch + kTile - 1) / kTile * kTile;
-            if (ch < kTile)
-                ch = kTile;
-            ns = (L + ch - 1) / ch;
-            if (ns < 1)
-                ns = 1;
-            p.jobs[i].chunk = ch;
-            p.jobs[i].nsplit = (int)ns;
-            p.jobs[i].item_base = items;
-            items += 2 * (int)ns;
-        }
-        if (items <= cap_items)
-            break;
-        if (attempt > 40)
-            return fail("kernel_attn_decode_batch_noalloc: cannot plan within %d items", cap_items);
-        target *= 2;
-    }
-    const int grid = items < dev.num_sms ? items : dev.num_sms;
-    // Longest-first onto the least-loaded CTA, with fixed-size arrays only (no heap use).
-    NoAllocItem order[kMaxItems];
-    int k = 0;
-    for (int i = 0; i < n; i++) {
-        const DJob &d = p.jobs[i];
-        for (int sp = 0; sp < d.nsplit; sp++) {
-            const long long t0 = (long long)sp * d.chunk;
-            const long long t1 = std::min<long long>(t0 + d.chunk, (long long)jobs[i].length);
-            for (int kvh = 0; kvh < 2; kvh++)
-                order[k++] = NoAllocItem{(t1 > t0 ? t1 - t0 : 0) + 256,
-                                         (unsigned short)((i << 9) | (sp << 1) | kvh), 0};
-        }
-    }
-    std::sort(order, order + items, [](const NoAllocItem &a, const NoAllocItem &b) {
-        return a.cost != b.cost ? a.cost > b.cost : a.code < b.code;
-    });
-    long long load[kMaxCtas] = {0};
-    int heap[kMaxCtas];                      // binary min-heap of CTA ids by (load, id)
-    auto less = [&](int a, int b) { return load[a] != load[b] ? load[a] < load[b] : a < b; };
-    for (int c = 0; c < grid; c++) {
-        load[c] = 0;
-        heap[c] = c;
-    }
-    for (int it = 0; it < items; it++) {
-        const int c = heap[0];
-        order[it].cta = (short)c;
-        load[c] += order[it].cost;
-        int pos = 0;                          // sift the grown root down
-        for (;;) {
-            int l = 2 * pos + 1, r = l + 1, m = pos;
-            if (l < grid && less(heap[l], heap[m]))
-                m = l;
-            if (r < grid && less(heap[r], heap[m]))
-                m = r;
-            if (m == pos)
-                break;
-            std::swap(heap[pos], heap[m]);
-            pos = m;
-        }
-    }
-    int count[kMaxCtas + 1];
-    for (int c = 0; c <= grid; c++)
-        count[c] = 0;
-    for (int it = 0; it < items; it++)
-        count[order[it].cta + 1]++;
-    for (int c = 0; c < grid; c++)
-        count[c + 1] += count[c];
-    for (int c = 0; c <= grid; c++)
-        p.cta_off[c] = (unsigned short)count[c];
-    for (int it = 0; it < items; it++)
-        p.sched[count[order[it].cta]++] = order[it].code;
-    for (int i = 0; i < n; i++) {
-        const KernelAttnDecodeJob &s = jobs[i];
-        DJob &d = p.jobs[i];
-        d.q = s.q;
-        d.gate = s.gate;
-        d.k_new = s.k_new;
-        d.v_new = s.v_new;
-        d.q_norm = s.q_norm;
-        d.k_norm = s.k_norm;
-        d.k_cache = reinterpret_cast<__half *>(s.k_cache);
-        d.v_cache = reinterpret_cast<__half *>(s.v_cache);
-        d.out = s.out;
-        d.qg_stride = (long long)s.qg_stride;
-        d.length = (long long)s.length;
-        d.position = (long long)s.position;
-        d.append = s.append ? 1 : 0;
-    }
+    // Same plan as the allocating path, capped at the items the static array holds.
+    const int grid = plan(jobs, n, dev.num_sms, kNoAllocMaxItems < kMaxItems ? kNoAllocMaxItems : kMaxItems, p);
+    if (grid < 0)
+        return -1;
+    fill_jobs(jobs, n, p, nullptr, nullptr);
     for (int j = 0; j < 32; j++)           // same host libm powf the reference uses
         p.inv_freq[j] = powf(10000000.0f, -2.0f * (float)j / 64.0f);
-    int *cnt = reinterpret_cast<int *>(dev.base);
-    float *ws = reinterpret_cast<float *>(dev.base + kNoAllocHeadBytes);
+    // Every record the kernels read is written earlier in the same call, so nothing left in the
+    // array by a previous call is read and nothing needs clearing.
+    float *ws = reinterpret_cast<float *>(dev.base);
     p.newpart = ws;
     p.part = ws + kNoAllocNewFloats;
-    p.counters = cnt;
     p.pout = nullptr;
     p.err = rt().err_word;          // reported by kernel_cuda_synchronize
-    p.njobs = n;
-    p.nitems = items;
-    cudaStream_t st = rt().stream;
-    // The array keeps whatever the previous call left: the counters must start at zero.
-    if (check(cudaMemsetAsync(dev.base, 0, kNoAllocCounterInts * sizeof(int), st),
-              "clear noalloc counters") != 0)
-        return -1;
-    attn_decode_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
-    return launched("attn_decode_kernel (noalloc)");
+    return launch_pair(p, grid, rt().stream);
 }
 
 }  // namespace
@@ -1207,6 +1204,57 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
         if (!s.q || !s.gate || !s.out || !s.q_norm || (s.append && (!s.k_new || !s.v_new || !s.k_norm)))
             return fail("kernel_attn_decode_batch_host: job %d has a null pointer", i);
     }
+    // Registered buffers: when every host buffer of every job lies in memory registered with
+    // kernel_cuda_host_register, the copy engine moves the buffers' contiguous runs straight
+    // between host and device (a few large copies per call, no staging memcpy on the host).
+    {
+        HostRuns in, out;
+        bool reg = true;
+        for (int i = 0; i < n && reg; i++) {
+            const KernelAttnDecodeJob &s = jobs[i];
+            const size_t rows = (15 * s.qg_stride + 256) * sizeof(float);
+            reg = host_registered(s.q, rows) && host_registered(s.gate, rows) &&
+                  host_registered(s.q_norm, 1024) && host_registered(s.out, 4096 * sizeof(float)) &&
+                  (!s.append || (host_registered(s.k_new, 2048) && host_registered(s.v_new, 2048) &&
+                                 host_registered(s.k_norm, 1024)));
+            in.add(s.q, rows);
+            in.add(s.gate, rows);
+            in.add(s.q_norm, 1024);
+            if (s.append) {
+                in.add(s.k_new, 2048);
+                in.add(s.v_new, 2048);
+                in.add(s.k_norm, 1024);
+            }
+            out.add(s.out, 4096 * sizeof(float));
+        }
+        if (reg) {
+            in.build(64 << 10);
+            out.build(0);
+            const size_t in_bytes = (in.bytes + 15) & ~(size_t)15;
+            char *d = static_cast<char *>(dstage(in_bytes + out.bytes + 16));
+            if (!d || runs_h2d(in, d) != 0)
+                return -1;
+            char *dout = d + in_bytes;
+            for (int i = 0; i < n; i++) {
+                const KernelAttnDecodeJob &s = jobs[i];
+                KernelAttnDecodeJob &t = dj[i];
+                auto at = [&](const float *p) { return reinterpret_cast<const float *>(d + in.offset(p)); };
+                t.q = at(s.q);
+                t.gate = at(s.gate);
+                t.q_norm = at(s.q_norm);
+                if (s.append) {
+                    t.k_new = at(s.k_new);
+                    t.v_new = at(s.v_new);
+                    t.k_norm = at(s.k_norm);
+                }
+                t.out = reinterpret_cast<float *>(dout + out.offset(s.out));
+            }
+            if (attn_decode_batch(dj.data(), n, nullptr) != 0 || runs_d2h(out, dout) != 0)
+                return -1;
+            return kernel_cuda_synchronize() != 0 ? -1 : 0;
+        }
+    }
+    dj.assign(jobs, jobs + n);
     float *dev_in = static_cast<float *>(dstage(total * sizeof(float)));
     if (!dev_in)
         return -1;

@@ -10,6 +10,7 @@
 // column c), so a CTA owns a 128-row x 32-column block: it streams the block in once with
 // 128-bit loads, reduces A/B over the rows in shared memory, and writes the block back once.
 // The kernel is HBM-bound: 2 x 4 bytes per state element per step.
+#include "ptx.cuh"
 #include "runtime.h"
 #include "../../include/roaster_cuda.h"
 
@@ -40,6 +41,8 @@ template <int MAXJ>
 __global__ void __launch_bounds__(kThreads) deltanet_step_kernel(const __grid_constant__ DeltaParams<MAXJ> p)
 {
     __shared__ float sA[16][kCB], sB[16][kCB], sKQ[16], sDelta[kCB];
+    griddep_wait();                  // inputs are written by the kernels before this one
+    griddep_launch_dependents();
     const DeltaJob &J = p.jobs[blockIdx.y];
     const int vh = blockIdx.x / (kD / kCB);
     const int cb = blockIdx.x % (kD / kCB);
@@ -113,9 +116,8 @@ int launch_chunk(const KernelDeltaStepJob *jobs, int n)
             return fail("kernel_deltanet_step_batch: job %d has a null or misaligned pointer", i);
         p.jobs[i] = DeltaJob{j.state, j.q, j.k, j.v, j.g, j.beta, j.out};
     }
-    dim3 grid(32 * (kD / kCB), n);
-    deltanet_step_kernel<MAXJ><<<grid, kThreads, 0, rt().stream>>>(p);
-    return launched("deltanet_step_kernel");
+    return launch_dependent(deltanet_step_kernel<MAXJ>, dim3(32 * (kD / kCB), n), dim3(kThreads), 0, rt().stream,
+                            "deltanet_step_kernel", p);
 }
 
 }  // namespace
@@ -141,6 +143,80 @@ int deltanet_step_batch(const KernelDeltaStepJob *jobs, int n)
     return 0;
 }
 
+// Host buffers all registered: the jobs in up to 4 chunks, pipelined over two streams. Chunk c's
+// inputs (their contiguous runs) copy in on the library's copy stream while chunk c - 1 computes
+// on the work stream; chunk c's step launch waits for its copy (an event) and its outputs copy
+// back on the work stream right behind it, on the other copy engine.
+int step_registered(const KernelDeltaStepJob *jobs, int n)
+{
+    const size_t nq = 16 * 128, nv = 32 * 128, nh = 32;
+    const int chunks = n >= 64 ? 4 : 1;
+    cudaStream_t cs = rt().stream;                 // may be the legacy default stream (null)
+    if (chunks > 1 && !(cs = copy_stream()))
+        return -1;
+    static cudaEvent_t ev[5];
+    static int made = -1;
+    if (made != rt().device) {
+        for (auto &e : ev)
+            if (check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate") != 0)
+                return -1;
+        made = rt().device;
+    }
+    std::vector<HostRuns> in(chunks), out(chunks);
+    std::vector<size_t> base(chunks + 1, 0);
+    for (int c = 0; c < chunks; c++) {
+        const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
+        for (int i = i0; i < i1; i++) {
+            const KernelDeltaStepJob &s = jobs[i];
+            in[c].add(s.q, nq * 4);
+            in[c].add(s.k, nq * 4);
+            in[c].add(s.v, nv * 4);
+            in[c].add(s.g, nh * 4);
+            in[c].add(s.beta, nh * 4);
+            out[c].add(s.out, nv * 4);
+        }
+        in[c].build(64 << 10);
+        out[c].build(0);
+        base[c + 1] = base[c] + ((in[c].bytes + 15) & ~(size_t)15) + ((out[c].bytes + 15) & ~(size_t)15) + 32;
+    }
+    char *d = static_cast<char *>(dstage(base[chunks]));
+    if (!d)
+        return -1;
+    // the copy stream starts after everything queued on the work stream so far
+    if (chunks > 1 && (check(cudaEventRecord(ev[4], rt().stream), "cudaEventRecord") != 0 ||
+                       check(cudaStreamWaitEvent(cs, ev[4], 0), "cudaStreamWaitEvent") != 0))
+        return -1;
+    std::vector<KernelDeltaStepJob> dj(jobs, jobs + n);
+    for (int c = 0; c < chunks; c++) {
+        char *din = d + base[c];
+        if (runs_copy(in[c], din, cudaMemcpyHostToDevice, cs) != 0)
+            return -1;
+        if (chunks > 1 && check(cudaEventRecord(ev[c], cs), "cudaEventRecord") != 0)
+            return -1;
+    }
+    for (int c = 0; c < chunks; c++) {
+        const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
+        char *din = d + base[c];
+        char *dout = din + ((in[c].bytes + 15) & ~(size_t)15) + 16;
+        for (int i = i0; i < i1; i++) {
+            const KernelDeltaStepJob &s = jobs[i];
+            auto at = [&](const float *p) { return reinterpret_cast<const float *>(din + in[c].offset(p)); };
+            dj[i].q = at(s.q);
+            dj[i].k = at(s.k);
+            dj[i].v = at(s.v);
+            dj[i].g = at(s.g);
+            dj[i].beta = at(s.beta);
+            dj[i].out = reinterpret_cast<float *>(dout + out[c].offset(s.out));
+        }
+        if (chunks > 1 && check(cudaStreamWaitEvent(rt().stream, ev[c], 0), "cudaStreamWaitEvent") != 0)
+            return -1;
+        if (deltanet_step_batch(dj.data() + i0, i1 - i0) != 0 ||
+            runs_copy(out[c], dout, cudaMemcpyDeviceToHost, rt().stream) != 0)
+            return -1;
+    }
+    return kernel_cuda_synchronize() != 0 ? -1 : 0;
+}
+
 }  // namespace rb
 
 using namespace rb;
@@ -164,6 +240,22 @@ extern "C" int kernel_deltanet_step_batch_host(const KernelDeltaStepJob *jobs, i
     const size_t nq = 16 * 128, nv = 32 * 128, nh = 32;
     const size_t in_f = 2 * nq + nv + 2 * nh, out_f = nv;
     const size_t total = (size_t)n * (in_f + out_f);
+    // Registered buffers: when every job's host buffers lie in memory registered with
+    // kernel_cuda_host_register, the copy engine moves their contiguous runs straight between
+    // host and device, with no staging memcpy on the host.
+    {
+        bool reg = true;
+        for (int i = 0; i < n && reg; i++) {
+            const KernelDeltaStepJob &s = jobs[i];
+            if (!s.state || !s.q || !s.k || !s.v || !s.g || !s.beta || !s.out)
+                return fail("kernel_deltanet_step_batch_host: job %d has a null pointer", i);
+            reg = host_registered(s.q, nq * 4) && host_registered(s.k, nq * 4) && host_registered(s.v, nv * 4) &&
+                  host_registered(s.g, nh * 4) && host_registered(s.beta, nh * 4) &&
+                  host_registered(s.out, out_f * 4);
+        }
+        if (reg)
+            return step_registered(jobs, n);
+    }
     float *h = static_cast<float *>(pinned(total * sizeof(float)));
     float *d = static_cast<float *>(dstage(total * sizeof(float)));
     if (!h || !d)

@@ -12,6 +12,18 @@ __device__ __forceinline__ uint32_t smem_addr(const void *p)
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+
+// A kernel launched as a programmatic dependent (launch_dependent in runtime.h) may have its
+// blocks scheduled while the previous kernel on the stream drains; griddep_wait() returns once
+// that kernel has completed and its memory operations are visible, so it precedes every read of
+// an input. griddep_launch_dependents() lets the next kernel's launch begin early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- flags between GPUs
 
 // A flag word written after data that other GPUs read: the store is a release at system scope,

@@ -7,9 +7,12 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
+#include <vector>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 namespace rb {
@@ -19,6 +22,15 @@ static char g_err[512] = "";
 static std::atomic<uint64_t> g_launches{0};
 
 Runtime &rt() { return g_rt; }
+
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char *e = getenv("ROASTER_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 int fail(const char *fmt, ...)
 {
@@ -64,9 +76,15 @@ static int init_device(int device)
         cudaFree(err);
         return -1;
     }
+    unsigned *err_host = nullptr;
+    if (check(cudaHostAlloc(&err_host, 64, cudaHostAllocDefault), "cudaHostAlloc(error word copy)") != 0) {
+        cudaFree(err);
+        return -1;
+    }
     g_rt.device = device;
     g_rt.num_sms = prop.multiProcessorCount;
     g_rt.err_word = err;
+    g_rt.err_host = err_host;
     // RoPE inverse frequencies with the host libm powf, the same call the reference makes
     // (apply_rope_64, model.c:765), so both sides rotate by bit-identical angles.
     for (int j = 0; j < 32; j++)
@@ -244,6 +262,14 @@ void *dstage(size_t bytes)
     return p;
 }
 
+cudaStream_t copy_stream()
+{
+    if (!g_rt.copy_stream &&
+        check(cudaStreamCreateWithFlags(&g_rt.copy_stream, cudaStreamNonBlocking), "cudaStreamCreate(copy)") != 0)
+        return nullptr;
+    return g_rt.copy_stream;
+}
+
 int *counters(size_t n)
 {
     if (n <= g_rt.counters_n)
@@ -287,11 +313,109 @@ void *pinned(size_t bytes)
 }
 
 
+// Host buffers registered by the caller (pinned), sorted by start address. The host-buffer entry
+// points move such buffers with the copy engine directly, without a staging memcpy.
+struct HostRange {
+    uintptr_t lo, hi;
+};
+static std::mutex g_reg_mu;
+static std::vector<HostRange> g_reg;
+
+bool host_registered(const void *p, size_t bytes)
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    auto it = std::upper_bound(g_reg.begin(), g_reg.end(), a,
+                               [](uintptr_t x, const HostRange &r) { return x < r.lo; });
+    if (it == g_reg.begin())
+        return false;
+    --it;
+    return a >= it->lo && a + bytes <= it->hi && a + bytes >= a;
+}
+
+void HostRuns::build(size_t gap)
+{
+    std::sort(segs.begin(), segs.end());
+    runs.clear();
+    for (const auto &s : segs) {
+        if (!runs.empty() && s.first <= runs.back().hi + gap)
+            runs.back().hi = std::max(runs.back().hi, s.second);
+        else
+            runs.push_back(Run{s.first, s.second, 0});
+    }
+    // each run starts in staging at its host address modulo 16, so pointers keep their alignment
+    bytes = 0;
+    for (auto &r : runs) {
+        r.off = ((bytes + 15) & ~(size_t)15) + (r.lo & 15);
+        bytes = r.off + (r.hi - r.lo);
+    }
+}
+
+size_t HostRuns::offset(const void *p) const
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    auto it = std::upper_bound(runs.begin(), runs.end(), a, [](uintptr_t x, const Run &r) { return x < r.lo; });
+    --it;                                        // every pointer asked for lies in some run
+    return it->off + (a - it->lo);
+}
+
+int runs_copy(const HostRuns &r, char *d, cudaMemcpyKind kind, cudaStream_t st)
+{
+    for (const auto &x : r.runs) {
+        void *h = reinterpret_cast<void *>(x.lo);
+        const cudaError_t e = kind == cudaMemcpyHostToDevice
+                                  ? cudaMemcpyAsync(d + x.off, h, x.hi - x.lo, kind, st)
+                                  : cudaMemcpyAsync(h, d + x.off, x.hi - x.lo, kind, st);
+        if (check(e, kind == cudaMemcpyHostToDevice ? "copy in" : "copy out") != 0)
+            return -1;
+    }
+    return 0;
+}
+
+int runs_h2d(const HostRuns &r, char *d) { return runs_copy(r, d, cudaMemcpyHostToDevice, g_rt.stream); }
+
+int runs_d2h(const HostRuns &r, const char *d)
+{
+    return runs_copy(r, const_cast<char *>(d), cudaMemcpyDeviceToHost, g_rt.stream);
+}
+
 }  // namespace rb
 
 using namespace rb;
 
 extern "C" {
+
+int kernel_cuda_host_register(void *ptr, size_t bytes)
+{
+    if (ensure() != 0)
+        return -1;
+    if (!ptr || bytes == 0)
+        return fail("kernel_cuda_host_register: empty range");
+    if (check(cudaHostRegister(ptr, bytes, cudaHostRegisterPortable), "cudaHostRegister") != 0)
+        return -1;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(ptr);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    HostRange r{lo, lo + bytes};
+    g_reg.insert(std::upper_bound(g_reg.begin(), g_reg.end(), r,
+                                  [](const HostRange &x, const HostRange &y) { return x.lo < y.lo; }),
+                 r);
+    return 0;
+}
+
+int kernel_cuda_host_unregister(void *ptr)
+{
+    if (ensure() != 0)
+        return -1;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(ptr);
+    {
+        std::lock_guard<std::mutex> lk(g_reg_mu);
+        auto it = std::find_if(g_reg.begin(), g_reg.end(), [&](const HostRange &r) { return r.lo == lo; });
+        if (it == g_reg.end())
+            return fail("kernel_cuda_host_unregister: %p was not registered", ptr);
+        g_reg.erase(it);
+    }
+    return check(cudaHostUnregister(ptr), "cudaHostUnregister");
+}
 
 int kernel_cuda_init(int device)
 {
@@ -329,6 +453,10 @@ void kernel_cuda_shutdown(void)
     kernel_cuda_trim_scratch();
     if (g_rt.err_word)
         cudaFree(g_rt.err_word);
+    if (g_rt.err_host)
+        cudaFreeHost(g_rt.err_host);
+    if (g_rt.copy_stream)
+        cudaStreamDestroy(g_rt.copy_stream);
     if (g_rt.counters)
         cudaFree(g_rt.counters);
     g_rt = Runtime();
@@ -346,12 +474,12 @@ int kernel_cuda_synchronize(void)
 {
     if (ensure() != 0)
         return -1;
-    if (check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize") != 0)
+    // the error word travels behind the stream's work, so one wait covers both
+    if (check(cudaMemcpyAsync(g_rt.err_host, g_rt.err_word, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                              g_rt.stream), "read error word") != 0 ||
+        check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize") != 0)
         return -1;
-    unsigned word = 0;
-    if (check(cudaMemcpy(&word, g_rt.err_word, sizeof(word), cudaMemcpyDeviceToHost),
-              "read error word") != 0)
-        return -1;
+    const unsigned word = *reinterpret_cast<volatile unsigned *>(g_rt.err_host);
     if (word) {
         cudaMemset(g_rt.err_word, 0, sizeof(unsigned));
         return fail("kernel-recorded failure 0x%x (%s%s)", word,

@@ -8,6 +8,8 @@
 #include <cstddef>
 #include <cstdint>
 #include <functional>
+#include <utility>
+#include <vector>
 
 namespace rb {
 
@@ -31,6 +33,8 @@ struct Runtime {
     void *pinned = nullptr;            // host pinned, grow-only
     size_t pinned_bytes = 0;
     float inv_freq[32];                // RoPE inverse frequencies, computed with host powf
+    unsigned *err_host = nullptr;      // pinned copy of the error word (read by synchronize)
+    cudaStream_t copy_stream = nullptr;   // input copies that overlap kernels on `stream`
 };
 
 Runtime &rt();
@@ -45,6 +49,9 @@ int check(cudaError_t e, const char *what);
 int launched(const char *what);
 // Device scratch of at least `bytes` (grow-only; growing synchronises the stream).
 void *scratch(size_t bytes);
+// The library's second stream, for input copies that overlap kernels on the work stream
+// (created on first use; null on failure, with the error recorded).
+cudaStream_t copy_stream();
 // Zero-initialised device int counters (grow-only, separate from scratch). Kernels that use
 // them return every counter to zero before they exit.
 int *counters(size_t n);
@@ -61,8 +68,63 @@ int encode_tmap_f16_3d(CUtensorMap *map, const void *base, const uint64_t dims[3
 // bytes apart, a multiple of 16), no swizzle, zero fill outside the array. 0 = ok.
 int encode_tmap_u8_2d(CUtensorMap *map, const void *base, uint64_t dim0, uint64_t dim1, uint64_t stride1,
                       uint32_t box0, uint32_t box1);
+// Whether the host range [p, p + bytes) lies inside one buffer registered with
+// kernel_cuda_host_register (pinned, so the copy engine moves it at full rate).
+bool host_registered(const void *p, size_t bytes);
+
+// The host buffers of one batch call, moved by the copy engine in as few copies as their layout
+// allows. Segments are sorted by address and merged into runs. Input runs may bridge gaps of up
+// to `gap` bytes, whose bytes are copied along; output runs merge only touching or overlapping
+// segments, so a copy back never writes host bytes outside the outputs. Each run is one
+// cudaMemcpyAsync to or from a device staging area laid out run after run; dev() gives the
+// staging address of a host pointer inside a run.
+struct HostRuns {
+    struct Run {
+        uintptr_t lo, hi;
+        size_t off;
+    };
+    std::vector<std::pair<uintptr_t, uintptr_t>> segs;
+    std::vector<Run> runs;
+    size_t bytes = 0;
+    void add(const void *p, size_t n) { segs.emplace_back(reinterpret_cast<uintptr_t>(p), reinterpret_cast<uintptr_t>(p) + n); }
+    void build(size_t gap);
+    size_t offset(const void *p) const;
+};
+// Copy every run host -> device (staging base `d`) or device -> host, on the library stream.
+int runs_h2d(const HostRuns &r, char *d);
+int runs_d2h(const HostRuns &r, const char *d);
+// The same on stream `st` in direction `kind`.
+int runs_copy(const HostRuns &r, char *d, cudaMemcpyKind kind, cudaStream_t st);
 // 16-byte alignment check for pointers handed to bulk-copy engines.
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch `kernel` as a programmatic dependent of the work before it on stream `st` (its launch
+// overlaps the previous kernel's tail; the kernel calls griddep_wait() before reading any
+// input), or as an ordinary launch where the attribute is not accepted. Counts the launch.
+// ROASTER_PDL=0 in the environment makes every such launch an ordinary one.
+bool pdl_enabled();
+template <typename... Params, typename... Args>
+int launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     const char *what, Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) != cudaSuccess) {
+        (void)cudaGetLastError();
+        cfg.numAttrs = 0;
+        if (check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what) != 0)
+            return -1;
+    }
+    return launched(what);
+}
 
 // Host staging of the host-buffer entry points. A batch of n jobs of `per` floats each lives
 // contiguously in pinned memory `h` and device memory `d`. stage_in fills the pinned copy job by
