@@ -726,11 +726,18 @@ LONG_SLOTS = 16
 
 
 def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window: int, steps: int,
-                     warmup: int = 3):
+                     warmup: int = 3, mode: str = "push"):
     """Config 4: 16 slots x `window` f16 KV positions, each window split into contiguous slices
-    across the ranks (no data exchange except one all-gather of 8.3 KB softmax partials per slot
-    and kv head per step); the rank holding the newest slice appends. Plus 3 DeltaNet layers per
-    slot on the slot's home rank (slot % world). Strong scaling: the job is fixed, ranks split it."""
+    across the ranks; the rank holding the newest slice appends. Plus 3 DeltaNet layers per slot
+    on the slot's home rank (slot % world). Strong scaling: the job is fixed, ranks split it.
+    The per-(slot, kv head) softmax partials (8.3 KB each) are combined on the slot's home rank:
+      mode "push":   the partial kernel stores them straight into the home rank's memory (peer
+                     stores over NVLink, buffers opened through CUDA IPC) with a tag per record;
+                     the home rank's merge kernel waits on the tags; no collective in the step;
+      mode "gather": an NCCL all-gather of every rank's partials, then every rank merges all
+                     slots (kernel_attn_merge_partials)."""
+    import ctypes as C
+
     from roaster_b200 import splitkv, synth
     lo, hi = splitkv.slice_bounds(window, world, rank)
     app = splitkv.appends(world, rank)
@@ -747,15 +754,15 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
     qn = 1 + 0.1 * torch.randn(256, generator=g, device=dev)
     kw = 1 + 0.1 * torch.randn(256, generator=g, device=dev)
     out = torch.empty(LONG_SLOTS, 16, 256, device=dev)
-    home = [s for s in range(LONG_SLOTS) if s % world == rank]
-    states = synth.device_normal(torch, (max(1, len(home)), DN_LAYERS, 32, 128, 128), 800 + rank, dev,
-                                 torch.float32, std=0.02)
-    dq = torch.nn.functional.normalize(torch.randn(max(1, len(home)), DN_LAYERS, 16, 128, device=dev), dim=-1)
-    dk = torch.nn.functional.normalize(torch.randn(max(1, len(home)), DN_LAYERS, 16, 128, device=dev), dim=-1)
-    dv = torch.randn(max(1, len(home)), DN_LAYERS, 32, 128, device=dev)
-    db = torch.sigmoid(torch.randn(max(1, len(home)), DN_LAYERS, 32, device=dev))
-    dg = -torch.rand(max(1, len(home)), DN_LAYERS, 32, device=dev)
-    dout = torch.empty(max(1, len(home)), DN_LAYERS, 32, 128, device=dev)
+    home = splitkv.home_slots(LONG_SLOTS, world, rank)
+    nh = max(1, len(home))
+    states = synth.device_normal(torch, (nh, DN_LAYERS, 32, 128, 128), 800 + rank, dev, torch.float32, std=0.02)
+    dq = torch.nn.functional.normalize(torch.randn(nh, DN_LAYERS, 16, 128, device=dev), dim=-1)
+    dk = torch.nn.functional.normalize(torch.randn(nh, DN_LAYERS, 16, 128, device=dev), dim=-1)
+    dv = torch.randn(nh, DN_LAYERS, 32, 128, device=dev)
+    db = torch.sigmoid(torch.randn(nh, DN_LAYERS, 32, device=dev))
+    dg = -torch.rand(nh, DN_LAYERS, 32, device=dev)
+    dout = torch.empty(nh, DN_LAYERS, 32, 128, device=dev)
     es = kpool.element_size()
     jobs = [R.attn_job(q[s], gate[s], kn[s], vn[s], qn, kw,
                        kpool.data_ptr() + s * cap * 512 * es, vpool.data_ptr() + s * cap * 512 * es,
@@ -764,22 +771,74 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
     dj = [R.delta_job(states[i, l], dq[i, l], dk[i, l], dv[i, l], dg[i, l], db[i, l], dout[i, l])
           for i in range(len(home)) for l in range(DN_LAYERS)]
     darr = (R.KernelDeltaStepJob * max(1, len(dj)))(*dj) if dj else None
-    part = torch.empty(LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
-    gathered = torch.empty(world, LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
     lib = R.lib()
-    import ctypes as C
-    gates_p = (C.c_void_p * LONG_SLOTS)(*[gate[s].data_ptr() for s in range(LONG_SLOTS)])
-    outs_p = (C.c_void_p * LONG_SLOTS)(*[out[s].data_ptr() for s in range(LONG_SLOTS)])
+    vp = C.c_void_p
+    opened, owned = [], []
+    if world > 1 and mode == "push":
+        # The push form's merge waits on kernels of the other ranks: every rank must be on a GPU
+        # of its own (two ranks sharing one would wait on each other within one GPU).
+        ids = [None] * world
+        dist.all_gather_object(ids, str(torch.cuda.get_device_properties(dev).uuid))
+        if len(set(ids)) != world:
+            mode = "gather"
+    if world > 1 and mode == "push":
+        nbytes = splitkv.recv_floats(LONG_SLOTS, world, rank) * 4
+        tbytes = splitkv.tag_words(LONG_SLOTS, world, rank) * 4
+        recv, tags = lib.kernel_cuda_alloc(nbytes), lib.kernel_cuda_alloc(tbytes)   # zeroed
+        if not recv or not tags:
+            raise RuntimeError(R.last_error())
+        owned = [recv, tags]
+        mine = (R.ipc_handle(recv), R.ipc_handle(tags))
+        allh = [None] * world
+        dist.all_gather_object(allh, mine)
+        rbases, tbases = [], []
+        for r in range(world):
+            if r == rank:
+                rbases.append(recv)
+                tbases.append(tags)
+            else:
+                a_, b_ = R.ipc_open(allh[r][0]), R.ipc_open(allh[r][1])
+                opened += [a_, b_]
+                rbases.append(a_)
+                tbases.append(b_)
+        targets = []
+        for par in (0, 1):            # push addresses of both parity halves (epoch parity)
+            d_, t_ = splitkv.push_targets(LONG_SLOTS, world, rank, par, rbases, tbases)
+            targets.append(((vp * LONG_SLOTS)(*d_), (vp * LONG_SLOTS)(*t_),
+                            splitkv.merge_view(LONG_SLOTS, world, rank, par, recv, tags)))
+        gates_h = (vp * nh)(*[gate[s].data_ptr() for s in home])
+        outs_h = (vp * nh)(*[out[s].data_ptr() for s in home])
+    else:
+        part = torch.empty(LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
+        gathered = torch.empty(world, LONG_SLOTS, 2, splitkv.PARTIAL_FLOATS, device=dev)
+        gates_p = (vp * LONG_SLOTS)(*[gate[s].data_ptr() for s in range(LONG_SLOTS)])
+        outs_p = (vp * LONG_SLOTS)(*[out[s].data_ptr() for s in range(LONG_SLOTS)])
     pos = [window]
+    epoch = [0]
 
     def one():
         for s in range(LONG_SLOTS):
             arr[s].position = pos[0]
+        epoch[0] += 1
         if world == 1:
             rc = lib.kernel_attn_decode_batch(arr, LONG_SLOTS)
+        elif mode == "push":
+            dst_a, tag_a, (rv, tv) = targets[epoch[0] & 1]
+
+            def push_fn():
+                if lib.kernel_attn_decode_partial_push(arr, LONG_SLOTS, dst_a, tag_a, epoch[0]) != 0:
+                    raise RuntimeError(R.last_error())
+
+            def merge_fn():
+                if home and lib.kernel_attn_merge_wait(vp(rv), vp(tv), world, len(home), gates_h, 256, outs_h,
+                                                       epoch[0]) != 0:
+                    raise RuntimeError(R.last_error())
+
+            splitkv.push_step(push_fn, merge_fn)
+            rc = 0
         else:
             def partial_fn():
-                if lib.kernel_attn_decode_partial_batch(arr, LONG_SLOTS, C.c_void_p(part.data_ptr())) != 0:
+                if lib.kernel_attn_decode_partial_batch(arr, LONG_SLOTS, vp(part.data_ptr())) != 0:
                     raise RuntimeError(R.last_error())
                 return part
 
@@ -788,8 +847,7 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
                 return gathered
 
             def merge_fn(gt, w):
-                if lib.kernel_attn_merge_partials(C.c_void_p(gt.data_ptr()), w, LONG_SLOTS, gates_p, 256,
-                                                  outs_p) != 0:
+                if lib.kernel_attn_merge_partials(vp(gt.data_ptr()), w, LONG_SLOTS, gates_p, 256, outs_p) != 0:
                     raise RuntimeError(R.last_error())
 
             splitkv.step(world, partial_fn, gather_fn, merge_fn)
@@ -809,6 +867,7 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = R.launch_count()
     e0.record(stream)
@@ -822,16 +881,33 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
     ms = float(t.item())
+    for ptr in opened:
+        R.ipc_close(ptr)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+    for ptr in owned:
+        lib.kernel_cuda_free(vp(ptr))
     kv_bytes = LONG_SLOTS * local * 2048
     dn_bytes = len(home) * DN_LAYERS * (2 * 32 * 128 * 128 * 4)
+    hbm, _, src = peaks()
+    gbs = (kv_bytes + dn_bytes) / (ms / 1e3) / 1e9
     del kpool, vpool
     return {"metric": "long-context decode tok/s (config 4: 16 slots x 262144 f16 KV + 3 DeltaNet layers)",
             "value": round(LONG_SLOTS / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
             "steps": steps, "scaling": "strong", "window": window,
-            "kv_split": f"{world} contiguous slices per slot; NCCL all-gather of softmax partials",
+            "kv_split": (f"{world} contiguous slices per slot; " +
+                         ("one GPU, no split" if world == 1 else
+                          "partials pushed into the home GPU's memory by the partial kernel (peer stores, "
+                          "tagged), merged there; no collective" if mode == "push" else
+                          "NCCL all-gather of softmax partials, every GPU merges every slot")),
             "kv_bytes_per_gpu_per_step": kv_bytes + dn_bytes,
-            "achieved_GBps_per_gpu": round((kv_bytes + dn_bytes) / (ms / 1e3) / 1e9, 1),
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel (+ deltanet_step_kernel)",
+                         "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                         "peak_source": f"{src} hbm_gbs (a copy: read + write; this step only reads KV)",
+                         "scope": "per GPU, the whole step (max over ranks)"},
             "gpu_launches": int(launches)}
 
 
@@ -970,22 +1046,31 @@ def run_config2(R, torch, dev, stream, lens, K: int, W: int, seed: int, world: i
 
     # ---------------------------------------------------------------- end to end (host buffers)
     if e2e:
-        hq, hg = q.cpu().numpy(), gate.cpu().numpy()
-        hkn, hvn = kn.cpu().numpy(), vn.cpu().numpy()
-        hqn, hkw = qn.cpu().numpy(), kw.cpu().numpy()
-        hdq, hdk, hdv = dq.cpu().numpy(), dk.cpu().numpy(), dv.cpu().numpy()
-        hdg, hdb = dgl.cpu().numpy(), dbeta.cpu().numpy()
-        hao = np.zeros((n, 16, 256), np.float32)
-        hdo = np.zeros((n, DN_LAYERS, 32, 128), np.float32)
+        # All host inputs and outputs in one allocation, so the caller registers one range
+        # (kernel_cuda_host_register) once, outside the timed region, as a serving host would
+        # its long-lived step buffers.
+        shapes = {"q": (NP, n, 16, 256), "gate": (NP, n, 16, 256), "kn": (NP, n, 2, 256), "vn": (NP, n, 2, 256),
+                  "qn": (256,), "kw": (256,), "dq": (NP, n, DN_LAYERS, 16, 128), "dk": (NP, n, DN_LAYERS, 16, 128),
+                  "dv": (NP, n, DN_LAYERS, 32, 128), "dg": (NP, n, DN_LAYERS, 32), "db": (NP, n, DN_LAYERS, 32),
+                  "ao": (n, 16, 256), "do": (n, DN_LAYERS, 32, 128)}
+        sizes = {k: int(np.prod(v)) for k, v in shapes.items()}
+        host = np.zeros(sum(sizes.values()), np.float32)
+        H, o_ = {}, 0
+        for k, shp in shapes.items():
+            H[k] = host[o_:o_ + sizes[k]].reshape(shp)
+            o_ += sizes[k]
+        for k, t in (("q", q), ("gate", gate), ("kn", kn), ("vn", vn), ("qn", qn), ("kw", kw), ("dq", dq),
+                     ("dk", dk), ("dv", dv), ("dg", dgl), ("db", dbeta)):
+            H[k][...] = t.cpu().numpy()
         ha, hd = [], []
         for pi in range(NP):
-            jobs = [R.attn_job(hq[pi, s].ctypes.data, hg[pi, s].ctypes.data, hkn[pi, s].ctypes.data,
-                               hvn[pi, s].ctypes.data, hqn.ctypes.data, hkw.ctypes.data, kaddr[s], vaddr[s],
-                               0, 0, hao[s].ctypes.data, capacity=caps[s]) for s in range(n)]
+            jobs = [R.attn_job(H["q"][pi, s].ctypes.data, H["gate"][pi, s].ctypes.data, H["kn"][pi, s].ctypes.data,
+                               H["vn"][pi, s].ctypes.data, H["qn"].ctypes.data, H["kw"].ctypes.data, kaddr[s],
+                               vaddr[s], 0, 0, H["ao"][s].ctypes.data, capacity=caps[s]) for s in range(n)]
             ha.append((R.KernelAttnDecodeJob * n)(*jobs))
-            dj = [R.delta_job(states[s, l], hdq[pi, s, l].ctypes.data, hdk[pi, s, l].ctypes.data,
-                              hdv[pi, s, l].ctypes.data, hdg[pi, s, l].ctypes.data,
-                              hdb[pi, s, l].ctypes.data, hdo[s, l].ctypes.data)
+            dj = [R.delta_job(states[s, l], H["dq"][pi, s, l].ctypes.data, H["dk"][pi, s, l].ctypes.data,
+                              H["dv"][pi, s, l].ctypes.data, H["dg"][pi, s, l].ctypes.data,
+                              H["db"][pi, s, l].ctypes.data, H["do"][s, l].ctypes.data)
                   for s in range(n) for l in range(DN_LAYERS)]
             hd.append((R.KernelDeltaStepJob * len(dj))(*dj))
         KE = max(1, min(K, 200))
@@ -1002,16 +1087,25 @@ def run_config2(R, torch, dev, stream, lens, K: int, W: int, seed: int, world: i
             for s in range(n):
                 cur[s] += 1
 
-        # windows were sized for K+W+8 appends: wind them back and append again (KE <= K)
-        for s in range(n):
-            cur[s] = lens[s]
-        for i in range(2):
-            estep(i)
-        barrier()
-        t0 = time.perf_counter()
-        for i in range(KE):
-            estep(i)
-        res["e2e_s"] = time.perf_counter() - t0
+        def timed_e2e():
+            # windows were sized for K+W+8 appends: wind them back and append again (KE <= K)
+            for s in range(n):
+                cur[s] = lens[s]
+            for i in range(2):
+                estep(i)
+            barrier()
+            t0 = time.perf_counter()
+            for i in range(KE):
+                estep(i)
+            return time.perf_counter() - t0
+
+        if lib.kernel_cuda_host_register(host.ctypes.data, host.nbytes) != 0:
+            raise RuntimeError(R.last_error())
+        try:
+            res["e2e_s"] = timed_e2e()
+        finally:
+            lib.kernel_cuda_host_unregister(host.ctypes.data)
+        res["e2e_staged_s"] = timed_e2e()
         res["e2e_steps"] = KE
         res["h2d"] = n * (4096 * 2 + 512 * 2 + 256 * 2) * 4 + n * DN_LAYERS * (2 * 2048 + 4096 + 64) * 4
         res["d2h"] = n * 4096 * 4 + n * DN_LAYERS * 4096 * 4
@@ -1073,11 +1167,16 @@ def run_ours(a):
     dn_gbs = dn_bytes / (c2["dn_ms"] / 1e3) / 1e9
     e2e = None
     if not a.no_e2e:
-        (el,) = allmax([c2["e2e_s"]])
+        el, els = allmax([c2["e2e_s"], c2["e2e_staged_s"]])
         e2e = {"value": round(SLOTS * c2["e2e_steps"] / el, 1), "unit": "tok/s",
                "h2d_bytes_per_step": c2["h2d"] * world, "d2h_bytes_per_step": c2["d2h"] * world,
                "steps": c2["e2e_steps"],
-               "api": "kernel_attn_decode_batch_host + kernel_deltanet_step_batch_host"}
+               "api": "kernel_attn_decode_batch_host + kernel_deltanet_step_batch_host",
+               "host_buffers": "one numpy allocation registered once with kernel_cuda_host_register (outside "
+                               "the timed region): each call's buffers move as a few large copy-engine "
+                               "copies (their contiguous runs), no staging memcpy",
+               "staged": {"value": round(SLOTS * c2["e2e_steps"] / els, 1), "unit": "tok/s",
+                          "what": "the same calls with the buffers unregistered: pinned staging copies"}}
 
     # per-GPU efficiency of the shards the strong split gives each GPU at N = 2, 4, 8 (one GPU)
     shards = None
@@ -1259,6 +1358,10 @@ def run_ours(a):
     long_ctx = None
     if not a.no_long:
         long_ctx = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window, a.long_steps)
+        if world > 1:
+            gl = run_long_context(R, torch, dist, dev, stream, world, rank, a.long_window, a.long_steps,
+                                  mode="gather")
+            long_ctx["nccl_gather_form"] = {k: gl[k] for k in ("value", "ms_per_step", "kv_split")}
         if rank == 0 and world == 1 and not a.no_cpu_baseline:
             try:
                 c = cpu_leg_ref("long", window=a.long_window, slots=LONG_SLOTS, timeout=1200)

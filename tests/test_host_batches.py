@@ -73,3 +73,98 @@ def test_deltanet_host_batch_matches_device_batch(rb, oracle_lib):
         ref = O.delta_step(st, hs["q"][l], hs["k"][l], hs["v"][l], hs["g"][l], hs["beta"][l])
         assert O.maxrel(hout[l], ref) < 1e-5
         assert O.maxrel(host(dst_h)[l], st) < 1e-5
+
+
+def test_registered_host_buffers_run_in_place(rb, oracle_lib):
+    """With the host buffers registered (kernel_cuda_host_register), both host-batch entry points
+    move the buffers' contiguous runs with the copy engine directly (no staging memcpy); the
+    results equal, bit for bit, the device-pointer batches on the same inputs, over two calls in
+    a row, and unregistering falls back to the staging path with the same results."""
+    import ctypes as C
+    lib = rb.lib()
+    N, L = 12, 900
+    ds = [synth.attn_decode_inputs(seed=500 + i, length=L + 37 * i) for i in range(N)]
+    NL = 3 * N
+    st0 = synth.delta_state(501, NL)
+    seq = synth.delta_sequence(502, 1, NL)
+    # one allocation for every host input and output, registered once
+    sizes = {"q": N * 4096, "gate": N * 4096, "kn": N * 512, "vn": N * 512, "norms": 512, "out": N * 4096,
+             "dq": NL * 2048, "dk": NL * 2048, "dv": NL * 4096, "dg": NL * 32, "db": NL * 32, "dout": NL * 4096}
+    host_buf = np.zeros(sum(sizes.values()), np.float32)
+    H, o = {}, 0
+    for k, n in sizes.items():
+        H[k] = host_buf[o:o + n]
+        o += n
+    H["q"] = H["q"].reshape(N, 16, 256)
+    H["gate"] = H["gate"].reshape(N, 16, 256)
+    H["kn"] = H["kn"].reshape(N, 2, 256)
+    H["vn"] = H["vn"].reshape(N, 2, 256)
+    H["out"] = H["out"].reshape(N, 16, 256)
+    for i, d in enumerate(ds):
+        H["q"][i], H["gate"][i], H["kn"][i], H["vn"][i] = d["q"], d["gate"], d["k_new"], d["v_new"]
+    H["norms"][:256], H["norms"][256:] = ds[0]["q_norm"], ds[0]["k_norm"]
+    for k, src in (("dq", "q"), ("dk", "k"), ("dv", "v"), ("dg", "g"), ("db", "beta")):
+        H[k][...] = seq[src][0].reshape(-1)
+    H["dq"], H["dk"] = H["dq"].reshape(NL, 16, 128), H["dk"].reshape(NL, 16, 128)
+    H["dv"], H["dout"] = H["dv"].reshape(NL, 32, 128), H["dout"].reshape(NL, 32, 128)
+    H["dg"], H["db"] = H["dg"].reshape(NL, 32), H["db"].reshape(NL, 32)
+
+    def caches():
+        out = []
+        for d in ds:
+            Ld = d["length"]
+            kc = torch.zeros(Ld + 4, 2, 256, dtype=torch.float16, device="cuda")
+            vc = torch.zeros_like(kc)
+            kc[:Ld] = dev(d["k_cache"])
+            vc[:Ld] = dev(d["v_cache"])
+            out.append((kc, vc))
+        return out
+
+    def run_host(cs, st):
+        outs = []
+        for step in range(2):
+            jobs = [rb.attn_job(H["q"][i].ctypes.data, H["gate"][i].ctypes.data, H["kn"][i].ctypes.data,
+                                H["vn"][i].ctypes.data, H["norms"].ctypes.data, H["norms"][256:].ctypes.data,
+                                cs[i][0], cs[i][1], d["length"] + step, d["length"] + step, H["out"][i].ctypes.data)
+                    for i, d in enumerate(ds)]
+            rb.attn_decode_batch_host(jobs)
+            rb.deltanet_step_batch_host([rb.delta_job(st[l], H["dq"][l].ctypes.data, H["dk"][l].ctypes.data,
+                                                      H["dv"][l].ctypes.data, H["dg"][l].ctypes.data,
+                                                      H["db"][l].ctypes.data, H["dout"][l].ctypes.data)
+                                         for l in range(NL)])
+            outs.append((H["out"].copy(), H["dout"].copy()))
+        return outs
+
+    # device-pointer reference
+    cs_d, st_d = caches(), dev(st0)
+    dq = {k: dev(np.ascontiguousarray(H[k])) for k in ("q", "gate", "kn", "vn", "norms", "dq", "dk", "dv", "dg", "db")}
+    ref_outs = []
+    for step in range(2):
+        ao = torch.zeros(N, 16, 256, device="cuda")
+        do = torch.zeros(NL, 32, 128, device="cuda")
+        rb.attn_decode_batch([rb.attn_job(dq["q"][i], dq["gate"][i], dq["kn"][i], dq["vn"][i], dq["norms"][:256],
+                                          dq["norms"][256:], cs_d[i][0], cs_d[i][1], d["length"] + step,
+                                          d["length"] + step, ao[i]) for i, d in enumerate(ds)])
+        rb.deltanet_step_batch([rb.delta_job(st_d[l], dq["dq"][l], dq["dk"][l], dq["dv"][l], dq["dg"][l],
+                                             dq["db"][l], do[l]) for l in range(NL)])
+        ref_outs.append((host(ao), host(do)))
+
+    assert lib.kernel_cuda_host_register(C.c_void_p(host_buf.ctypes.data), host_buf.nbytes) == 0, rb.last_error()
+    try:
+        cs_r, st_r = caches(), dev(st0)
+        got = run_host(cs_r, st_r)
+    finally:
+        assert lib.kernel_cuda_host_unregister(C.c_void_p(host_buf.ctypes.data)) == 0, rb.last_error()
+    cs_s, st_s = caches(), dev(st0)
+    staged = run_host(cs_s, st_s)
+    for step in range(2):
+        for a, b, c in zip(got[step], staged[step], ref_outs[step]):
+            assert np.array_equal(a, c) and np.array_equal(b, c)
+    assert torch.equal(st_r, st_d) and torch.equal(st_s, st_d)
+    for i, d in enumerate(ds):
+        Ld = d["length"]
+        assert torch.equal(cs_r[i][0][:Ld + 2], cs_d[i][0][:Ld + 2])
+        assert torch.equal(cs_r[i][1][:Ld + 2], cs_d[i][1][:Ld + 2])
+    ref, _, _ = O.attn_decode(ds[0]["q"], ds[0]["gate"], ds[0]["k_new"], ds[0]["v_new"], ds[0]["q_norm"],
+                              ds[0]["k_norm"], ds[0]["k_cache"], ds[0]["v_cache"], ds[0]["length"], ds[0]["length"])
+    assert O.maxrel(got[0][0][0], ref) <= 2e-3
