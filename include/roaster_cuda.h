@@ -167,16 +167,17 @@ int kernel_attn_merge_partials(const float *partials, int nparts, int n,
  * kernel_attn_decode_partial_batch, but job i's merged partial goes straight to dst[i] (two
  * records of KERNEL_ATTN_PARTIAL_FLOATS floats, kv head 0 then 1; 16-byte aligned), which may
  * be another GPU's memory opened with kernel_cuda_ipc_open (plain peer stores over NVLink), and
- * once both records are visible to every GPU, tags[i][0..1] are set to `epoch`. No collective
- * library call: the home GPU of a slot waits on the tags in kernel_attn_merge_wait. Async. */
+ * once a query head's part of a record is visible to every GPU, its tag
+ * tags[i][kv_head * 8 + head] (16 words per job) is set to `epoch`. No collective library call:
+ * the home GPU of a slot waits on the tags in kernel_attn_merge_wait. Async. */
 int kernel_attn_decode_partial_push(const KernelAttnDecodeJob *jobs, int n, float *const *dst,
                                     unsigned *const *tags, unsigned epoch);
 
 /* The home GPU's half of the fused combine: recv [nparts][n][2][KERNEL_ATTN_PARTIAL_FLOATS]
- * and tags [nparts][n][2] in this GPU's memory, filled by kernel_attn_decode_partial_push on
- * the nparts GPUs. Each (job, kv head) waits until its nparts tags equal `epoch` (bounded: a
- * wait that runs out sets the error word kernel_cuda_synchronize reports, and that output is
- * not written), then merges as kernel_attn_merge_partials. A buffer may be reused for the
+ * and tags [nparts][n][2][8] in this GPU's memory, filled by kernel_attn_decode_partial_push
+ * on the nparts GPUs. Each (job, kv head, query head) waits until its nparts tags equal `epoch`
+ * (bounded: a wait that runs out sets the error word kernel_cuda_synchronize reports, and that
+ * output is not written), then merges as kernel_attn_merge_partials. A buffer may be reused for the
  * step after next (double buffering by step parity keeps a fast GPU from overwriting records
  * the home GPU has not merged yet). Async. */
 int kernel_attn_merge_wait(const float *recv, const unsigned *tags, int nparts, int n,

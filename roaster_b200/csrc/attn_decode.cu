@@ -229,15 +229,15 @@ __device__ void new_token(const DParams &p, const DJob &J, int jidx, int kvh, co
         rec[16 + e] = __ldg(vn + (e & (kHD - 1)));
 }
 
-// Combine of one launch's partial records. Grid: (n jobs x 2 kv heads x 8 query heads), or
-// (n jobs x 2) in push mode, where one block covers the 8 heads of a record before releasing
-// its tag. 256 threads = 4 part groups x 64 threads of 4 output dims. Each (job, kv head) merges
+// Combine of one launch's partial records. Grid: (n jobs x 2 kv heads x 8 query heads);
+// 256 threads = 4 part groups x 64 threads of 4 output dims. Each (job, kv head) merges
 // its nsplit split records plus the new token's record: M = max m_i, w_i = l_i 2^(m_i - M),
 // o = sum w_i o_i / sum w_i. Part group g takes parts g, g + 4, ... (up to 8 per batch, every
 // load of a batch issued before its arithmetic) and the four groups' sums are added in group
 // order, so a block costs about two memory round trips and the result does not depend on
-// timing. Output: the gated result (o * sigmoid(gate)), or in partial / push mode one merged
-// record (m = M, l = sum w_i, o) to p.pout / the job's push address, then the push tag.
+// timing. Output: the gated result (o * sigmoid(gate)), or in partial / push mode the head's
+// part of one merged record (m = M, l = sum w_i, o) to p.pout / the job's push address, then in
+// push mode the head's tag.
 __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant__ DParams p)
 {
     __shared__ float red[8];
@@ -245,9 +245,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
     __shared__ float gl[4];
     griddep_wait();
     griddep_launch_dependents();
-    const bool push = p.jobs[0].ptag != nullptr;
-    const int j = push ? blockIdx.x >> 1 : blockIdx.x >> 4;
-    const int kvh = push ? blockIdx.x & 1 : (blockIdx.x >> 3) & 1;
+    const int j = blockIdx.x >> 4, kvh = (blockIdx.x >> 3) & 1, h = blockIdx.x & 7;
     const DJob &J = p.jobs[j];
     const int t = threadIdx.x, grp = t >> 6, d = (t & 63) * 4;
     const int ns = J.nsplit, np = ns + (J.append ? 1 : 0);
@@ -255,8 +253,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
     const float *newp = p.newpart + ((long long)j * 2 + kvh) * kPF;
     auto rec = [&](int i) { return i < ns ? part0 + (long long)i * 2 * kPF : newp; };
     float *dst = J.pdst ? J.pdst + kvh * kPF : (p.pout ? p.pout + ((long long)j * 2 + kvh) * kPF : nullptr);
-    const int h0 = push ? 0 : (blockIdx.x & 7), h1 = push ? 8 : h0 + 1;
-    for (int h = h0; h < h1; h++) {
+    {
         float m = -INFINITY;
         for (int i = t; i < np; i += 256)
             m = fmaxf(m, __ldcg(rec(i) + h));
@@ -332,15 +329,14 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
                     out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
             }
         }
-        __syncthreads();                   // red / gacc are reused by the next head
     }
-    if (push) {
+    if (J.ptag) {
         // Every writer makes its record stores visible system-wide before the tag goes out:
-        // the home GPU reads the record as soon as it sees the tag.
+        // the home GPU reads the head's record part as soon as it sees the tag.
         __threadfence_system();
         __syncthreads();
         if (t == 0)
-            st_release_sys(J.ptag + kvh, p.epoch);
+            st_release_sys(J.ptag + kvh * 8 + h, p.epoch);
     }
 }
 
@@ -661,10 +657,11 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const __grid_constant__
     }
 }
 
-// Merge on the home GPU of records that every GPU pushed into its memory (push mode): grid
-// (n jobs x 2 kv heads), 256 threads. Warp 0 first waits (bounded) until each of the nparts
-// records of the block's (job, kv head) carries this step's tag; then the merge of
-// attn_merge_kernel. recv: [nparts][n][2][kPF]; tags: [nparts][n][2].
+// Merge on the home GPU of the records every GPU pushed into its memory (push mode): grid
+// (n jobs x 2 kv heads x 8 query heads), 256 threads. The first warp waits (bounded) until each
+// of the nparts records carries this step's tag for the block's head, then the merge of
+// attn_combine_kernel over the parts (4 part groups x 64 threads of 4 dims). recv:
+// [nparts][n][2][kPF]; tags: [nparts][n][2][8].
 struct MWParams {
     const float *recv;
     const unsigned *tags;
@@ -678,20 +675,24 @@ struct MWParams {
 
 __global__ void __launch_bounds__(256) attn_merge_wait_kernel(const __grid_constant__ MWParams p)
 {
-    __shared__ float w[64][8], Ls[8];
+    __shared__ float red[8];
+    __shared__ float4 gacc[4][64];
+    __shared__ float gl[4];
     __shared__ int ready;
-    const int j = blockIdx.x >> 1, kvh = blockIdx.x & 1, t = threadIdx.x;
+    griddep_wait();
+    const int j = blockIdx.x >> 4, kvh = (blockIdx.x >> 3) & 1, h = blockIdx.x & 7;
+    const int t = threadIdx.x, grp = t >> 6, d = (t & 63) * 4;
     if (t < 32) {
         bool ok = true;
         for (int i = t; i < p.nparts; i += 32) {
-            const unsigned *tag = p.tags + ((long long)i * p.n + p.job0 + j) * 2 + kvh;
+            const unsigned *tag = p.tags + (((long long)i * p.n + p.job0 + j) * 2 + kvh) * 8 + h;
             const long long t0 = clock64();
             while (ld_acquire_sys(tag) != p.epoch) {
                 if (clock64() - t0 > p.budget) {
                     ok = false;
                     break;
                 }
-                __nanosleep(100);
+                __nanosleep(32);
             }
         }
         ok = __all_sync(0xffffffffu, ok);
@@ -706,27 +707,55 @@ __global__ void __launch_bounds__(256) attn_merge_wait_kernel(const __grid_const
     }
     const long long stride = (long long)p.n * 2 * kPF;
     const float *rec0 = p.recv + ((long long)(p.job0 + j) * 2 + kvh) * kPF;
-    if (t < 8) {
-        float M = -INFINITY, L = 0.f;
-        for (int i = 0; i < p.nparts; i++)
-            M = fmaxf(M, __ldcg(rec0 + i * stride + t));
-        for (int i = 0; i < p.nparts; i++) {
-            const float m = __ldcg(rec0 + i * stride + t);
-            const float x = m == -INFINITY ? 0.f : __ldcg(rec0 + i * stride + 8 + t) * exp2f(m - M);
-            w[i][t] = x;
-            L += x;
-        }
-        Ls[t] = L;
-    }
+    float m = -INFINITY;
+    for (int i = t; i < p.nparts; i += 256)
+        m = fmaxf(m, __ldcg(rec0 + i * stride + h));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((t & 31) == 0)
+        red[t >> 5] = m;
     __syncthreads();
-    for (int e = t; e < 8 * kHD; e += 256) {
-        const int h = e >> 8, d = e & (kHD - 1);
-        float acc = 0.f;
-        for (int i = 0; i < p.nparts; i++)
-            acc = fmaf(w[i][h], __ldcg(rec0 + i * stride + 16 + e), acc);
-        const float o = Ls[h] > 0.f ? acc / Ls[h] : 0.f;
-        const float g = p.gates[j][(long long)(kvh * 8 + h) * p.qg_stride + d];
-        p.outs[j][(kvh * 8 + h) * kHD + d] = o * (1.0f / (1.0f + expf(-g)));
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++)
+        M = fmaxf(M, red[w]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = grp; i < p.nparts; i += 4) {
+        const float *r = rec0 + i * stride;
+        const float mi = __ldcg(r + h), li = __ldcg(r + 8 + h);
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(r + 16 + h * kHD + d));
+        const float w = (mi == -INFINITY) ? 0.f : li * exp2f(mi - M);
+        L += w;
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+    }
+    gacc[grp][t & 63] = acc;
+    if ((t & 63) == 0)
+        gl[grp] = L;
+    __syncthreads();
+    if (grp == 0) {
+        float4 a = gacc[0][t];
+        float Lt = gl[0];
+#pragma unroll
+        for (int g2 = 1; g2 < 4; g2++) {
+            const float4 b = gacc[g2][t];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+            Lt += gl[g2];
+        }
+        const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+        const float o[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};
+        const float *g = p.gates[j] + (long long)(kvh * 8 + h) * p.qg_stride + d;
+        float *out = p.outs[j] + (kvh * 8 + h) * kHD + d;
+#pragma unroll
+        for (int x = 0; x < 4; x++)
+            out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
     }
 }
 
@@ -761,8 +790,8 @@ int launch_pair(const DParams &p, int grid, cudaStream_t st)
 {
     if (launch_dependent(attn_decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, "attn_decode_kernel", p) != 0)
         return -1;
-    return launch_dependent(attn_combine_kernel, dim3((unsigned)p.njobs * (p.jobs[0].ptag ? 2 : 16)), dim3(256), 0,
-                            st, "attn_combine_kernel", p);
+    return launch_dependent(attn_combine_kernel, dim3((unsigned)p.njobs * 16), dim3(256), 0, st,
+                            "attn_combine_kernel", p);
 }
 
 // Items per SM the planner aims for (per kv head pair). ROASTER_DECODE_ITEMS_PER_SM overrides.
@@ -913,7 +942,7 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *ds
     if (dst) {
         for (int i = 0; i < n; i++)
             if (!dst[i] || !tags || !tags[i] || !aligned16(dst[i]))
-                return fail("attn decode push: job %d needs a 16-byte aligned record address and a tag", i);
+                return fail("attn decode push: job %d needs a 16-byte aligned record address and tags", i);
         pout = nullptr;
     }
     const bool partial = pout != nullptr || dst != nullptr;
@@ -1097,8 +1126,8 @@ int attn_merge_wait(const float *recv, const unsigned *tags, int nparts, int n, 
         p.n = n;
         p.job0 = i;
         p.epoch = epoch;
-        attn_merge_wait_kernel<<<m * 2, 256, 0, rt().stream>>>(p);
-        if (launched("attn_merge_wait_kernel") != 0)
+        if (launch_dependent(attn_merge_wait_kernel, dim3(m * 16), dim3(256), 0, rt().stream,
+                             "attn_merge_wait_kernel", p) != 0)
             return -1;
     }
     return 0;

@@ -20,13 +20,15 @@ Fused form (``push_step``), with no collective call in the step: each slot has a
 rank's receive buffer (peer stores over NVLink into memory opened through CUDA IPC) and then
 sets a tag word to the step's epoch; the home rank's merge kernel waits on the tags of its own
 slots only, merges and gates. The receive buffer of a rank holds two halves (step parity), each
-``[world][n_home][2][PARTIAL_FLOATS]`` floats, plus tags ``[2][world][n_home][2]``: a rank can be
+``[world][n_home][2][PARTIAL_FLOATS]`` floats, plus tags ``[2][world][n_home][2][8]`` (one per
+record and query head): a rank can be
 at most one step ahead of a home rank that has not merged yet, so a half is never overwritten
 before it is read.
 """
 from __future__ import annotations
 
 PARTIAL_FLOATS = 8 + 8 + 8 * 256
+TAGS_PER_RECORD = 8             # one release tag per query head of a pushed record
 
 
 def slice_bounds(window: int, world: int, rank: int) -> tuple[int, int]:
@@ -99,8 +101,8 @@ def recv_floats(n_slots: int, world: int, rank: int) -> int:
 
 
 def tag_words(n_slots: int, world: int, rank: int) -> int:
-    """Tag words of `rank`'s receive buffer (both parity halves)."""
-    return 2 * world * home_count(n_slots, world, rank) * 2
+    """Tag words of `rank`'s receive buffer (both parity halves; one per record and query head)."""
+    return 2 * world * home_count(n_slots, world, rank) * 2 * TAGS_PER_RECORD
 
 
 def push_targets(n_slots: int, world: int, rank: int, epoch: int, recv_bases, tag_bases):
@@ -115,16 +117,17 @@ def push_targets(n_slots: int, world: int, rank: int, epoch: int, recv_bases, ta
         i = home_slots(n_slots, world, h).index(s)
         rec = ((half * world + rank) * nh + i) * 2
         dst.append(recv_bases[h] + rec * PARTIAL_FLOATS * 4)
-        tags.append(tag_bases[h] + rec * 4)
+        tags.append(tag_bases[h] + rec * TAGS_PER_RECORD * 4)
     return dst, tags
 
 
 def merge_view(n_slots: int, world: int, rank: int, epoch: int, recv_base: int, tag_base: int):
     """(records, tags) addresses of `rank`'s half for the step's parity: records
-    [world][n_home][2][PARTIAL_FLOATS], tags [world][n_home][2]."""
+    [world][n_home][2][PARTIAL_FLOATS], tags [world][n_home][2][8]."""
     nh = home_count(n_slots, world, rank)
     half = epoch & 1
-    return (recv_base + half * world * nh * 2 * PARTIAL_FLOATS * 4, tag_base + half * world * nh * 2 * 4)
+    return (recv_base + half * world * nh * 2 * PARTIAL_FLOATS * 4,
+            tag_base + half * world * nh * 2 * TAGS_PER_RECORD * 4)
 
 
 def push_step(push_fn, merge_fn):

@@ -166,7 +166,9 @@ def test_push_layout_covers_every_record_once():
                         seen.add((dst[s], tags[s]))
                         fo = off // 4
                         assert 0 <= fo and fo + 2 * PF <= bufs[h].size
-                        assert (tags[s] - tbases[h]) // 4 + 2 <= splitkv.tag_words(n_slots, world, h)
+                        tw = (tags[s] - tbases[h]) // 4
+                        assert tw % (2 * splitkv.TAGS_PER_RECORD) == 0
+                        assert tw + 2 * splitkv.TAGS_PER_RECORD <= splitkv.tag_words(n_slots, world, h)
                         bufs[h][fo:fo + 2 * PF] = part[r, s].reshape(-1)
                 gates = rng.standard_normal((n_slots, 16, 256)).astype(np.float32)
                 want = splitkv.merge_reference(part, gates)
