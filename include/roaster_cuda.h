@@ -72,6 +72,12 @@ int   kernel_cuda_upload(void *dst_dev, const void *src_host, size_t bytes);   /
 int   kernel_cuda_download(void *dst_host, const void *src_dev, size_t bytes); /* synchronous */
 int   kernel_cuda_memmove(void *dst_dev, const void *src_dev, size_t bytes);   /* overlap-safe, async */
 int   kernel_cuda_memset(void *dst_dev, int value, size_t bytes);              /* async (model_reset) */
+/* n f16 values of a device window (KVCache.k / .v rows) to host fp32, and host fp32 to device
+ * f16 (round to nearest even): the state file's KV blocks (state.c:39 and 66 write and read
+ * fp32 rows; the device window holds them as f16, and values that came from it convert back
+ * exactly). Synchronous. */
+int   kernel_cuda_download_f16_f32(float *dst_host, const uint16_t *src_dev, size_t n);
+int   kernel_cuda_upload_f32_f16(uint16_t *dst_dev, const float *src_host, size_t n);
 
 /* Register a long-lived host buffer (the model's attn_q / attn_k / attn_v / attn_out,
  * DeltaNet q / k / v / g / beta / out, model.c:801-861 and 1291-1343) once: its pages are

@@ -159,6 +159,26 @@ def _load(which: str):
         lib.ref_prefill_ctx_projections.restype = C.c_int
         lib.ref_prefill_ctx_free.argtypes = [C.c_void_p]
         lib.ref_prefill_ctx_free.restype = None
+        lib.ref_state_new.argtypes = [C.c_size_t]
+        lib.ref_state_new.restype = C.c_void_p
+        lib.ref_state_free.argtypes = [C.c_void_p]
+        lib.ref_state_free.restype = None
+        for nm in ("k", "v", "ssm", "conv"):
+            getattr(lib, "ref_state_" + nm).argtypes = [C.c_void_p, C.c_int]
+            getattr(lib, "ref_state_" + nm).restype = _fp
+        lib.ref_state_is_attention.argtypes = [C.c_int]
+        lib.ref_state_is_attention.restype = C.c_int
+        lib.ref_state_layers.argtypes = []
+        lib.ref_state_layers.restype = C.c_int
+        lib.ref_state_set_len.argtypes = [C.c_void_p, C.c_size_t]
+        lib.ref_state_set_len.restype = None
+        lib.ref_state_len.argtypes = [C.c_void_p, C.c_int]
+        lib.ref_state_len.restype = C.c_size_t
+        lib.ref_state_position.argtypes = [C.c_void_p]
+        lib.ref_state_position.restype = C.c_size_t
+        for nm in ("save", "load"):
+            getattr(lib, "ref_state_" + nm).argtypes = [C.c_void_p, C.c_char_p]
+            getattr(lib, "ref_state_" + nm).restype = C.c_int
         lib.ref_max_threads.argtypes = []
         lib.ref_max_threads.restype = C.c_int
     _libs[which] = lib
@@ -462,6 +482,53 @@ def matmul_q(is_q6: bool, m, X, rows: int, cols: int, impl: str = "port"):
     Y = np.zeros((T, rows), np.float32)
     _load("ref").ref_matmul_q(int(bool(is_q6)), m.ctypes.data_as(C.c_void_p), _f(X), _f(Y), rows, cols, T)
     return Y
+
+
+class RefState:
+    """The reference's state file (state.c, "RSTA" v2) through its own model_state_save /
+    model_state_load on a Model rig of host fp32 windows (`ctx` rows) and DeltaNet states."""
+
+    def __init__(self, ctx: int):
+        self.lib = _load("ref")
+        self.ctx = ctx
+        self.h = self.lib.ref_state_new(ctx)
+        if not self.h:
+            raise MemoryError("ref_state_new")
+        self.layers = self.lib.ref_state_layers()
+
+    def is_attention(self, layer: int) -> bool:
+        return bool(self.lib.ref_state_is_attention(layer))
+
+    def kv(self, layer: int):
+        """(K, V) views [ctx][512] of an attention layer's window."""
+        n = self.ctx * 512
+        return (np.ctypeslib.as_array(self.lib.ref_state_k(self.h, layer), shape=(n,)).reshape(self.ctx, 512),
+                np.ctypeslib.as_array(self.lib.ref_state_v(self.h, layer), shape=(n,)).reshape(self.ctx, 512))
+
+    def ssm(self, layer: int):
+        """(state [32][128][128], conv history [3][8192]) views of a recurrent layer."""
+        return (np.ctypeslib.as_array(self.lib.ref_state_ssm(self.h, layer), shape=(32 * 128 * 128,)).reshape(32, 128, 128),
+                np.ctypeslib.as_array(self.lib.ref_state_conv(self.h, layer), shape=(3 * 8192,)).reshape(3, 8192))
+
+    def set_len(self, n: int) -> None:
+        self.lib.ref_state_set_len(self.h, n)
+
+    def length(self, layer: int) -> int:
+        return self.lib.ref_state_len(self.h, layer)
+
+    def position(self) -> int:
+        return self.lib.ref_state_position(self.h)
+
+    def save(self, path: str) -> int:
+        return self.lib.ref_state_save(self.h, path.encode())
+
+    def load(self, path: str) -> int:
+        return self.lib.ref_state_load(self.h, path.encode())
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ref_state_free(self.h)
+            self.h = None
 
 
 def ref_lib():

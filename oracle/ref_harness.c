@@ -532,3 +532,98 @@ void ref_matvec_q(int is_q6, const void *matrix, const float *x, float *out, siz
     for (size_t r = 0; r < rows; r++)
         out[r] = is_q6 ? kernel_dot_q6_k(m + r * rb, x, cols) : kernel_dot_q4_k(m + r * rb, x, cols);
 }
+
+/* ---- the reference's state file ("RSTA" v2, state.c:7-81) through its own model_state_save /
+ * model_state_load, on a Model rig with host fp32 windows of `ctx` rows for the attention
+ * layers and the DeltaNet state + conv history of the recurrent layers (the sizes of
+ * kv_cache_init / ssm_state_init, model.c:355-461). No spill store: the window holds every
+ * token, so `position` equals the window length. */
+#include "state.h"
+
+typedef struct RefState {
+    Model m;
+    KVCache kv[MODEL_NUM_LAYERS];
+    SSMState ss[MODEL_NUM_LAYERS];
+} RefState;
+
+void ref_state_free(RefState *r)
+{
+    if (!r)
+        return;
+    for (int l = 0; l < MODEL_NUM_LAYERS; l++) {
+        free(r->kv[l].k);
+        free(r->kv[l].v);
+        free(r->ss[l].state);
+        free(r->ss[l].conv_state);
+    }
+    free(r);
+}
+
+RefState *ref_state_new(size_t ctx)
+{
+    RefState *r = calloc(1, sizeof(*r));
+    if (!r)
+        return NULL;
+    for (int l = 0; l < MODEL_NUM_LAYERS; l++) {
+        if (model_is_attention_layer(l)) {
+            r->kv[l].k = calloc(ctx * KV_FLOATS_PER_TOKEN, sizeof(float));
+            r->kv[l].v = calloc(ctx * KV_FLOATS_PER_TOKEN, sizeof(float));
+            r->kv[l].capacity = ctx;
+            if (!r->kv[l].k || !r->kv[l].v) {
+                ref_state_free(r);
+                return NULL;
+            }
+        } else {
+            r->ss[l].state_elements = (size_t)MODEL_LINEAR_V_HEADS * MODEL_LINEAR_HEAD_DIM * MODEL_LINEAR_HEAD_DIM;
+            r->ss[l].conv_elements = (size_t)(MODEL_SSM_CONV_KERNEL - 1) * MODEL_LINEAR_QKV_SIZE;
+            r->ss[l].state = calloc(r->ss[l].state_elements, sizeof(float));
+            r->ss[l].conv_state = calloc(r->ss[l].conv_elements, sizeof(float));
+            if (!r->ss[l].state || !r->ss[l].conv_state) {
+                ref_state_free(r);
+                return NULL;
+            }
+        }
+    }
+    r->m.kv_cache = r->kv;
+    r->m.ssm_state = r->ss;
+    r->m.context_length = ctx;
+    r->m.initialized = true;
+    return r;
+}
+
+float *ref_state_k(RefState *r, int layer) { return r->kv[layer].k; }
+float *ref_state_v(RefState *r, int layer) { return r->kv[layer].v; }
+float *ref_state_ssm(RefState *r, int layer) { return r->ss[layer].state; }
+float *ref_state_conv(RefState *r, int layer) { return r->ss[layer].conv_state; }
+int ref_state_is_attention(int layer) { return model_is_attention_layer(layer) ? 1 : 0; }
+int ref_state_layers(void) { return MODEL_NUM_LAYERS; }
+
+void ref_state_set_len(RefState *r, size_t len)
+{
+    for (int l = 0; l < MODEL_NUM_LAYERS; l++)
+        if (model_is_attention_layer(l))
+            r->kv[l].length = len;
+    r->m.position = len;
+}
+
+size_t ref_state_len(const RefState *r, int layer) { return r->kv[layer].length; }
+size_t ref_state_position(const RefState *r) { return r->m.position; }
+
+int ref_state_save(RefState *r, const char *path)
+{
+    FILE *f = fopen(path, "wb");
+    if (!f)
+        return -1;
+    const int rc = model_state_save(&r->m, f);
+    return fclose(f) == 0 ? rc : -1;
+}
+
+int ref_state_load(RefState *r, const char *path)
+{
+    FILE *f = fopen(path, "rb");
+    if (!f)
+        return -1;
+    const int rc = model_state_load(&r->m, f);
+    fclose(f);
+    return rc;
+}

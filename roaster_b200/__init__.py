@@ -120,6 +120,8 @@ def lib():
         "kernel_cuda_memmove": (C.c_int, [_vp, _vp, _sz]),
         "kernel_cuda_memset": (C.c_int, [_vp, C.c_int, _sz]),
         "kernel_cuda_host_register": (C.c_int, [_vp, _sz]),
+        "kernel_cuda_download_f16_f32": (C.c_int, [_vp, _vp, _sz]),
+        "kernel_cuda_upload_f32_f16": (C.c_int, [_vp, _vp, _sz]),
         "kernel_cuda_host_unregister": (C.c_int, [_vp]),
         "kernel_attn_decode_batch": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),
         "kernel_attn_decode_batch_host": (C.c_int, [C.POINTER(KernelAttnDecodeJob), C.c_int]),

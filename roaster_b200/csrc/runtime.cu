@@ -1,5 +1,6 @@
 // Runtime and the lifecycle / residency part of the C-ABI (include/roaster_cuda.h).
 #include "runtime.h"
+#include <cuda_fp16.h>
 #include "ptx.cuh"
 #include "../../include/roaster_cuda.h"
 
@@ -609,6 +610,73 @@ int kernel_cuda_ipc_close(void *dev_ptr)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- f16 window rows <-> host fp32
+
+namespace {
+
+__global__ void f16_to_f32_copy_kernel(const __half *s, float *d, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        d[i] = __half2float(s[i]);
+}
+
+__global__ void f32_to_f16_copy_kernel(const float *s, __half *d, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        d[i] = __float2half_rn(s[i]);
+}
+
+constexpr size_t kConvPiece = (size_t)1 << 22;     // values per staged piece (16 MB of fp32)
+
+}  // namespace
+
+extern "C" int kernel_cuda_download_f16_f32(float *dst_host, const uint16_t *src_dev, size_t n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n && (!dst_host || !src_dev))
+        return fail("kernel_cuda_download_f16_f32: null pointer");
+    for (size_t off = 0; off < n; off += kConvPiece) {
+        const size_t m = n - off < kConvPiece ? n - off : kConvPiece;
+        float *d = static_cast<float *>(dstage(m * sizeof(float)));
+        float *h = static_cast<float *>(pinned(m * sizeof(float)));
+        if (!d || !h)
+            return -1;
+        f16_to_f32_copy_kernel<<<(unsigned)std::min<size_t>((m + 255) / 256, 4096), 256, 0, g_rt.stream>>>(
+            reinterpret_cast<const __half *>(src_dev) + off, d, m);
+        if (launched("f16_to_f32_copy_kernel") != 0 ||
+            check(cudaMemcpyAsync(h, d, m * sizeof(float), cudaMemcpyDeviceToHost, g_rt.stream), "download") != 0 ||
+            check(cudaStreamSynchronize(g_rt.stream), "download sync") != 0)
+            return -1;
+        memcpy(dst_host + off, h, m * sizeof(float));
+    }
+    return 0;
+}
+
+extern "C" int kernel_cuda_upload_f32_f16(uint16_t *dst_dev, const float *src_host, size_t n)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n && (!dst_dev || !src_host))
+        return fail("kernel_cuda_upload_f32_f16: null pointer");
+    for (size_t off = 0; off < n; off += kConvPiece) {
+        const size_t m = n - off < kConvPiece ? n - off : kConvPiece;
+        float *d = static_cast<float *>(dstage(m * sizeof(float)));
+        float *h = static_cast<float *>(pinned(m * sizeof(float)));
+        if (!d || !h)
+            return -1;
+        memcpy(h, src_host + off, m * sizeof(float));
+        if (check(cudaMemcpyAsync(d, h, m * sizeof(float), cudaMemcpyHostToDevice, g_rt.stream), "upload") != 0)
+            return -1;
+        f32_to_f16_copy_kernel<<<(unsigned)std::min<size_t>((m + 255) / 256, 4096), 256, 0, g_rt.stream>>>(
+            d, reinterpret_cast<__half *>(dst_dev) + off, m);
+        // the pinned piece is refilled next: wait for its copy (and the conversion) first
+        if (launched("f32_to_f16_copy_kernel") != 0 || check(cudaStreamSynchronize(g_rt.stream), "upload sync") != 0)
+            return -1;
+    }
+    return 0;
+}
 
 // ---------------------------------------------------------------- bounded-wait probe
 
