@@ -38,8 +38,8 @@ DN_LAYERS = 3
 METRIC = "hybrid-attn decode tok/s (config 2: 64 slots sharded over the GPUs, 1 gated-attn + 3 DeltaNet layers)"
 # DRAM bytes per launch / algorithmic bytes for the decode-attention kernel, from one ncu capture
 # of a 64-slot launch with windows U[1024, 4096] (dram__bytes_read 336.07 MB + write 6.81 MB for
-# 338.31 MB algorithmic; profiles/attn_decode_kernel.md). Traffic grows with the KV positions
-# streamed, so the ratio scales to the full launch.
+# 338.31 MB algorithmic). Traffic grows with the KV positions streamed, so the ratio scales to
+# the full launch.
 ATTN_TRAFFIC_RATIO = (336.069888e6 + 6.806784e6) / 338309120
 CPU_BUDGET_S = 90.0             # bound on the reference arm's timed CPU work
 

@@ -2,7 +2,7 @@
 states resident on the device: the writer and reader below are state.c's model_state_save /
 model_state_load with their KV memcpys replaced by kernel_cuda_download_f16_f32 /
 kernel_cuda_upload_f32_f16 and their state memcpys by kernel_cuda_download / kernel_cuda_upload
-(the edit INTEGRATION.md shows). Checked against the reference's own model_state_load and
+(the edit state.c needs once its buffers live on the device). Checked against the reference's own model_state_load and
 model_state_save (oracle/_ref, state.c compiled from its sources): a file written from device
 state loads in the reference bit for bit, a file the reference writes restores the device state
 bit for bit, and decoding continues from a restored state exactly as from the original."""
