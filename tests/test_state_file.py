@@ -2,11 +2,11 @@
 states resident on the device: the writer and reader below are state.c's model_state_save /
 model_state_load with their KV memcpys replaced by kernel_cuda_download_f16_f32 /
 kernel_cuda_upload_f32_f16 and their state memcpys by kernel_cuda_download / kernel_cuda_upload
-(the edit state.c needs once its buffers live on the device). Checked against the reference's own model_state_load and
-model_state_save (oracle/_ref, state.c compiled from its sources): a file written from device
+(the edit state.c needs once its buffers live on the device). Checked against the reference's
+own model_state_load and model_state_save (oracle/_ref, state.c compiled from its sources): a
+file written from device
 state loads in the reference bit for bit, a file the reference writes restores the device state
 bit for bit, and decoding continues from a restored state exactly as from the original."""
-import ctypes as C
 import os
 import struct
 
@@ -82,7 +82,6 @@ def _device_model(ctx, L, seed, layers):
 def _step(rb, kv, states, inputs, layers):
     """One decode token on every attention layer (appending) and every DeltaNet layer."""
     d, dn = inputs
-    outs = {}
     att = [l for l, a in enumerate(layers) if a]
     out = torch.zeros(len(att), 16, 256, device="cuda")
     rb.attn_decode_batch([rb.attn_job(d["q"], d["gate"], d["k_new"], d["v_new"], d["q_norm"], d["k_norm"],
