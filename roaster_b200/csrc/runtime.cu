@@ -356,7 +356,9 @@ size_t HostRuns::offset(const void *p) const
 {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
     auto it = std::upper_bound(runs.begin(), runs.end(), a, [](uintptr_t x, const Run &r) { return x < r.lo; });
-    --it;                                        // every pointer asked for lies in some run
+    if (it == runs.begin())                      // callers only ask for pointers they added
+        return 0;
+    --it;
     return it->off + (a - it->lo);
 }
 
