@@ -786,9 +786,13 @@ bool g_attr_set = false;
 // The decode kernel, then the combine kernel, each as a programmatic dependent of the kernel
 // before it (the combine's blocks are scheduled as decode CTAs retire and wait in griddep_wait
 // for the whole decode grid).
-int launch_pair(const DParams &p, int grid, cudaStream_t st)
+// `before_combine`, when set, is an event the combine waits for (the gates' input copy, which
+// the decode kernel does not read, overlaps the decode kernel).
+int launch_pair(const DParams &p, int grid, cudaStream_t st, cudaEvent_t before_combine = nullptr)
 {
     if (launch_dependent(attn_decode_kernel, dim3(grid), dim3(kThreads), kSmemBytes, st, "attn_decode_kernel", p) != 0)
+        return -1;
+    if (before_combine && check(cudaStreamWaitEvent(st, before_combine, 0), "cudaStreamWaitEvent") != 0)
         return -1;
     return launch_dependent(attn_combine_kernel, dim3((unsigned)p.njobs * 16), dim3(256), 0, st,
                             "attn_combine_kernel", p);
@@ -937,7 +941,7 @@ void fill_jobs(const KernelAttnDecodeJob *jobs, int n, DParams &p, float *const 
 // One launch over jobs[0..n), n <= kMaxJobs. `pout` selects partial mode; `dst` + `tags`
 // select push mode (job i's merged records to dst[i], then tags[i][kvh] = epoch).
 int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *dst = nullptr,
-           unsigned *const *tags = nullptr, unsigned epoch = 0)
+           unsigned *const *tags = nullptr, unsigned epoch = 0, cudaEvent_t before_combine = nullptr)
 {
     if (dst) {
         for (int i = 0; i < n; i++)
@@ -973,7 +977,7 @@ int launch(const KernelAttnDecodeJob *jobs, int n, float *pout, float *const *ds
             return -1;
         g_attr_set = true;
     }
-    return launch_pair(p, grid, R.stream);
+    return launch_pair(p, grid, R.stream, before_combine);
 }
 
 // ---------------------------------------------------------------- allocation-free variant
@@ -1077,13 +1081,14 @@ int attn_decode_batch_noalloc(const KernelAttnDecodeJob *jobs, int n)
 
 }  // namespace
 
-int attn_decode_batch(const KernelAttnDecodeJob *jobs, int n, float *pout)
+int attn_decode_batch(const KernelAttnDecodeJob *jobs, int n, float *pout, cudaEvent_t before_combine = nullptr)
 {
     if (n < 0 || (n > 0 && !jobs))
         return fail("attn decode: bad job array");
     for (int i = 0; i < n; i += kMaxJobs) {
         const int m = n - i < kMaxJobs ? n - i : kMaxJobs;
-        if (launch(jobs + i, m, pout ? pout + (size_t)i * 2 * kPF : nullptr) != 0)
+        if (launch(jobs + i, m, pout ? pout + (size_t)i * 2 * kPF : nullptr, nullptr, nullptr, 0,
+                   i == 0 ? before_combine : nullptr) != 0)
             return -1;
     }
     return 0;
@@ -1235,9 +1240,12 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
     }
     // Registered buffers: when every host buffer of every job lies in memory registered with
     // kernel_cuda_host_register, the copy engine moves the buffers' contiguous runs straight
-    // between host and device (a few large copies per call, no staging memcpy on the host).
+    // between host and device (a few large copies per call, no staging memcpy on the host). The
+    // gates are read only by the combine kernel: when their runs are apart from the other inputs'
+    // (separate q and gate buffers), they copy in on the copy stream while the decode kernel
+    // runs, and the combine waits for them. Interleaved q|gate rows form one run set.
     {
-        HostRuns in, out;
+        HostRuns in, late, out;
         bool reg = true;
         for (int i = 0; i < n && reg; i++) {
             const KernelAttnDecodeJob &s = jobs[i];
@@ -1247,7 +1255,7 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
                   (!s.append || (host_registered(s.k_new, 2048) && host_registered(s.v_new, 2048) &&
                                  host_registered(s.k_norm, 1024)));
             in.add(s.q, rows);
-            in.add(s.gate, rows);
+            late.add(s.gate, rows);
             in.add(s.q_norm, 1024);
             if (s.append) {
                 in.add(s.k_new, 2048);
@@ -1258,18 +1266,45 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
         }
         if (reg) {
             in.build(64 << 10);
-            out.build(0);
-            const size_t in_bytes = (in.bytes + 15) & ~(size_t)15;
-            char *d = static_cast<char *>(dstage(in_bytes + out.bytes + 16));
-            if (!d || runs_h2d(in, d) != 0)
+            late.build(64 << 10);
+            cudaStream_t cs = nullptr;
+            static cudaEvent_t ev[2];               // decode inputs queued, gates landed
+            static int made = -1;
+            bool split = !runs_overlap(in, late);
+            if (split && made != rt().device) {
+                for (auto &e : ev)
+                    if (check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate") != 0)
+                        return -1;
+                made = rt().device;
+            }
+            if (split && !(cs = copy_stream()))
                 return -1;
-            char *dout = d + in_bytes;
+            if (!split) {
+                for (const auto &g : late.segs)
+                    in.segs.push_back(g);
+                in.build(64 << 10);
+                late = HostRuns();
+            }
+            out.build(0);
+            const size_t in_bytes = (in.bytes + 15) & ~(size_t)15, late_bytes = (late.bytes + 15) & ~(size_t)15;
+            char *d = static_cast<char *>(dstage(in_bytes + late_bytes + out.bytes + 32));
+            if (!d)
+                return -1;
+            char *dlate = d + in_bytes, *dout = dlate + late_bytes + 16;
+            // the gates follow the decode kernel's inputs on the host link, not beside them
+            if (runs_h2d(in, d) != 0)
+                return -1;
+            if (split && (check(cudaEventRecord(ev[0], rt().stream), "cudaEventRecord") != 0 ||
+                          check(cudaStreamWaitEvent(cs, ev[0], 0), "cudaStreamWaitEvent") != 0 ||
+                          runs_copy(late, dlate, cudaMemcpyHostToDevice, cs) != 0 ||
+                          check(cudaEventRecord(ev[1], cs), "cudaEventRecord") != 0))
+                return -1;
             for (int i = 0; i < n; i++) {
                 const KernelAttnDecodeJob &s = jobs[i];
                 KernelAttnDecodeJob &t = dj[i];
                 auto at = [&](const float *p) { return reinterpret_cast<const float *>(d + in.offset(p)); };
                 t.q = at(s.q);
-                t.gate = at(s.gate);
+                t.gate = split ? reinterpret_cast<const float *>(dlate + late.offset(s.gate)) : at(s.gate);
                 t.q_norm = at(s.q_norm);
                 if (s.append) {
                     t.k_new = at(s.k_new);
@@ -1278,7 +1313,7 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
                 }
                 t.out = reinterpret_cast<float *>(dout + out.offset(s.out));
             }
-            if (attn_decode_batch(dj.data(), n, nullptr) != 0 || runs_d2h(out, dout) != 0)
+            if (attn_decode_batch(dj.data(), n, nullptr, split ? ev[1] : nullptr) != 0 || runs_d2h(out, dout) != 0)
                 return -1;
             return kernel_cuda_synchronize() != 0 ? -1 : 0;
         }

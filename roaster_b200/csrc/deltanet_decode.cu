@@ -15,6 +15,7 @@
 #include "../../include/roaster_cuda.h"
 
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -143,18 +144,28 @@ int deltanet_step_batch(const KernelDeltaStepJob *jobs, int n)
     return 0;
 }
 
-// Host buffers all registered: the jobs in up to 4 chunks, pipelined over two streams. Chunk c's
-// inputs (their contiguous runs) copy in on the library's copy stream while chunk c - 1 computes
-// on the work stream; chunk c's step launch waits for its copy (an event) and its outputs copy
-// back on the work stream right behind it, on the other copy engine.
+// Host buffers all registered: pipelined over three streams. The copy engine spends a few
+// microseconds on every copy whatever its size, so the call makes few: first the small
+// per-head inputs (g, beta) of every job, as the runs they form, then each chunk's q, k, v runs,
+// in at most kDnChunks chunks of at least 32 jobs. Chunk c's step launch waits for its inputs
+// (an event); its outputs copy back on the out stream (the other copy engine) once its launch is
+// done, so the next chunk's launch never waits behind an output copy. The work stream waits for
+// the last output copy, so synchronising it covers the whole call.
+#ifndef DN_HOST_CHUNKS
+#define DN_HOST_CHUNKS 3
+#endif
 int step_registered(const KernelDeltaStepJob *jobs, int n)
 {
+    constexpr int kDnChunks = DN_HOST_CHUNKS;
     const size_t nq = 16 * 128, nv = 32 * 128, nh = 32;
-    const int chunks = n >= 64 ? 4 : 1;
-    cudaStream_t cs = rt().stream;                 // may be the legacy default stream (null)
-    if (chunks > 1 && !(cs = copy_stream()))
+    const int chunks = std::max(1, std::min(kDnChunks, n / 32));
+    cudaStream_t ws = rt().stream;                 // may be the legacy default stream (null)
+    cudaStream_t cs = ws, os = ws;
+    if (chunks > 1 && (!(cs = copy_stream()) || !(os = out_stream())))
         return -1;
-    static cudaEvent_t ev[5];
+    // events: [0, kDnChunks) inputs landed, [kDnChunks, 2 kDnChunks) chunk launch done,
+    // 2 kDnChunks: work stream start, 2 kDnChunks + 1: last output copy done
+    static cudaEvent_t ev[2 * kDnChunks + 2];
     static int made = -1;
     if (made != rt().device) {
         for (auto &e : ev)
@@ -162,8 +173,21 @@ int step_registered(const KernelDeltaStepJob *jobs, int n)
                 return -1;
         made = rt().device;
     }
+    cudaEvent_t *ev_in = ev, *ev_done = ev + kDnChunks, ev_start = ev[2 * kDnChunks],
+                ev_out = ev[2 * kDnChunks + 1];
+    auto rec = [](cudaEvent_t e, cudaStream_t st) { return check(cudaEventRecord(e, st), "cudaEventRecord"); };
+    auto wait = [](cudaStream_t st, cudaEvent_t e) {
+        return check(cudaStreamWaitEvent(st, e, 0), "cudaStreamWaitEvent");
+    };
+    auto up16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    HostRuns small;
+    for (int i = 0; i < n; i++) {
+        small.add(jobs[i].g, nh * 4);
+        small.add(jobs[i].beta, nh * 4);
+    }
+    small.build(64 << 10);
     std::vector<HostRuns> in(chunks), out(chunks);
-    std::vector<size_t> base(chunks + 1, 0);
+    std::vector<size_t> base(chunks + 1, up16(small.bytes) + 16);
     for (int c = 0; c < chunks; c++) {
         const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
         for (int i = i0; i < i1; i++) {
@@ -171,49 +195,52 @@ int step_registered(const KernelDeltaStepJob *jobs, int n)
             in[c].add(s.q, nq * 4);
             in[c].add(s.k, nq * 4);
             in[c].add(s.v, nv * 4);
-            in[c].add(s.g, nh * 4);
-            in[c].add(s.beta, nh * 4);
             out[c].add(s.out, nv * 4);
         }
         in[c].build(64 << 10);
         out[c].build(0);
-        base[c + 1] = base[c] + ((in[c].bytes + 15) & ~(size_t)15) + ((out[c].bytes + 15) & ~(size_t)15) + 32;
+        base[c + 1] = base[c] + up16(in[c].bytes) + up16(out[c].bytes) + 32;
     }
     char *d = static_cast<char *>(dstage(base[chunks]));
     if (!d)
         return -1;
-    // the copy stream starts after everything queued on the work stream so far
-    if (chunks > 1 && (check(cudaEventRecord(ev[4], rt().stream), "cudaEventRecord") != 0 ||
-                       check(cudaStreamWaitEvent(cs, ev[4], 0), "cudaStreamWaitEvent") != 0))
+    // both side streams start after everything queued on the work stream so far
+    if (chunks > 1 && (rec(ev_start, ws) != 0 || wait(cs, ev_start) != 0 || wait(os, ev_start) != 0))
         return -1;
-    std::vector<KernelDeltaStepJob> dj(jobs, jobs + n);
+    if (runs_copy(small, d, cudaMemcpyHostToDevice, cs) != 0)
+        return -1;
     for (int c = 0; c < chunks; c++) {
-        char *din = d + base[c];
-        if (runs_copy(in[c], din, cudaMemcpyHostToDevice, cs) != 0)
+        if (runs_copy(in[c], d + base[c], cudaMemcpyHostToDevice, cs) != 0)
             return -1;
-        if (chunks > 1 && check(cudaEventRecord(ev[c], cs), "cudaEventRecord") != 0)
+        if (chunks > 1 && rec(ev_in[c], cs) != 0)
             return -1;
     }
+    std::vector<KernelDeltaStepJob> dj(jobs, jobs + n);
     for (int c = 0; c < chunks; c++) {
         const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);
         char *din = d + base[c];
-        char *dout = din + ((in[c].bytes + 15) & ~(size_t)15) + 16;
+        char *dout = din + up16(in[c].bytes) + 16;
         for (int i = i0; i < i1; i++) {
             const KernelDeltaStepJob &s = jobs[i];
             auto at = [&](const float *p) { return reinterpret_cast<const float *>(din + in[c].offset(p)); };
             dj[i].q = at(s.q);
             dj[i].k = at(s.k);
             dj[i].v = at(s.v);
-            dj[i].g = at(s.g);
-            dj[i].beta = at(s.beta);
+            dj[i].g = reinterpret_cast<const float *>(d + small.offset(s.g));
+            dj[i].beta = reinterpret_cast<const float *>(d + small.offset(s.beta));
             dj[i].out = reinterpret_cast<float *>(dout + out[c].offset(s.out));
         }
-        if (chunks > 1 && check(cudaStreamWaitEvent(rt().stream, ev[c], 0), "cudaStreamWaitEvent") != 0)
+        if (chunks > 1 && wait(ws, ev_in[c]) != 0)
             return -1;
-        if (deltanet_step_batch(dj.data() + i0, i1 - i0) != 0 ||
-            runs_copy(out[c], dout, cudaMemcpyDeviceToHost, rt().stream) != 0)
+        if (deltanet_step_batch(dj.data() + i0, i1 - i0) != 0)
+            return -1;
+        if (chunks > 1 && (rec(ev_done[c], ws) != 0 || wait(os, ev_done[c]) != 0))
+            return -1;
+        if (runs_copy(out[c], dout, cudaMemcpyDeviceToHost, os) != 0)
             return -1;
     }
+    if (chunks > 1 && (rec(ev_out, os) != 0 || wait(ws, ev_out) != 0))
+        return -1;
     return kernel_cuda_synchronize() != 0 ? -1 : 0;
 }
 

@@ -271,6 +271,14 @@ cudaStream_t copy_stream()
     return g_rt.copy_stream;
 }
 
+cudaStream_t out_stream()
+{
+    if (!g_rt.out_stream &&
+        check(cudaStreamCreateWithFlags(&g_rt.out_stream, cudaStreamNonBlocking), "cudaStreamCreate(out)") != 0)
+        return nullptr;
+    return g_rt.out_stream;
+}
+
 int *counters(size_t n)
 {
     if (n <= g_rt.counters_n)
@@ -360,6 +368,20 @@ size_t HostRuns::offset(const void *p) const
         return 0;
     --it;
     return it->off + (a - it->lo);
+}
+
+bool runs_overlap(const HostRuns &a, const HostRuns &b)
+{
+    size_t i = 0, j = 0;                          // both run lists are sorted and disjoint
+    while (i < a.runs.size() && j < b.runs.size()) {
+        if (a.runs[i].hi <= b.runs[j].lo)
+            i++;
+        else if (b.runs[j].hi <= a.runs[i].lo)
+            j++;
+        else
+            return true;
+    }
+    return false;
 }
 
 int runs_copy(const HostRuns &r, char *d, cudaMemcpyKind kind, cudaStream_t st)
@@ -460,6 +482,8 @@ void kernel_cuda_shutdown(void)
         cudaFreeHost(g_rt.err_host);
     if (g_rt.copy_stream)
         cudaStreamDestroy(g_rt.copy_stream);
+    if (g_rt.out_stream)
+        cudaStreamDestroy(g_rt.out_stream);
     if (g_rt.counters)
         cudaFree(g_rt.counters);
     g_rt = Runtime();

@@ -35,6 +35,7 @@ struct Runtime {
     float inv_freq[32];                // RoPE inverse frequencies, computed with host powf
     unsigned *err_host = nullptr;      // pinned copy of the error word (read by synchronize)
     cudaStream_t copy_stream = nullptr;   // input copies that overlap kernels on `stream`
+    cudaStream_t out_stream = nullptr;    // output copies that overlap later kernels on `stream`
 };
 
 Runtime &rt();
@@ -52,6 +53,9 @@ void *scratch(size_t bytes);
 // The library's second stream, for input copies that overlap kernels on the work stream
 // (created on first use; null on failure, with the error recorded).
 cudaStream_t copy_stream();
+// Non-blocking stream for device-to-host output copies (the other copy engine), created on
+// first use.
+cudaStream_t out_stream();
 // Zero-initialised device int counters (grow-only, separate from scratch). Kernels that use
 // them return every counter to zero before they exit.
 int *counters(size_t n);
@@ -90,6 +94,8 @@ struct HostRuns {
     void build(size_t gap);
     size_t offset(const void *p) const;
 };
+// Whether any run of `a` shares a byte with a run of `b` (both built).
+bool runs_overlap(const HostRuns &a, const HostRuns &b);
 // Copy every run host -> device (staging base `d`) or device -> host, on the library stream.
 int runs_h2d(const HostRuns &r, char *d);
 int runs_d2h(const HostRuns &r, const char *d);

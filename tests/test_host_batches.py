@@ -79,12 +79,14 @@ def test_registered_host_buffers_run_in_place(rb, oracle_lib):
     """With the host buffers registered (kernel_cuda_host_register), both host-batch entry points
     move the buffers' contiguous runs with the copy engine directly (no staging memcpy); the
     results equal, bit for bit, the device-pointer batches on the same inputs, over two calls in
-    a row, and unregistering falls back to the staging path with the same results."""
+    a row, and unregistering falls back to the staging path with the same results. The attention
+    gates here are a buffer of their own, so they copy in beside the decode kernel; the 120
+    DeltaNet jobs copy in and out in pipelined chunks."""
     import ctypes as C
     lib = rb.lib()
     N, L = 12, 900
     ds = [synth.attn_decode_inputs(seed=500 + i, length=L + 37 * i) for i in range(N)]
-    NL = 3 * N
+    NL = 120                                  # enough DeltaNet jobs for the pipelined (chunked) copies
     st0 = synth.delta_state(501, NL)
     seq = synth.delta_sequence(502, 1, NL)
     # one allocation for every host input and output, registered once
@@ -168,3 +170,54 @@ def test_registered_host_buffers_run_in_place(rb, oracle_lib):
     ref, _, _ = O.attn_decode(ds[0]["q"], ds[0]["gate"], ds[0]["k_new"], ds[0]["v_new"], ds[0]["q_norm"],
                               ds[0]["k_norm"], ds[0]["k_cache"], ds[0]["v_cache"], ds[0]["length"], ds[0]["length"])
     assert O.maxrel(got[0][0][0], ref) <= 2e-3
+
+
+def test_registered_interleaved_q_gate(rb, oracle_lib):
+    """The reference's projection layout: each head's q row followed by its gate row
+    (qg_stride 512, model.c:801-805), registered. The gates share the q rows' run, so the whole
+    block copies in before the decode kernel; the output equals the device-pointer batch on the
+    same values bit for bit."""
+    import ctypes as C
+    lib = rb.lib()
+    N = 6
+    ds = [synth.attn_decode_inputs(seed=700 + i, length=500 + 91 * i) for i in range(N)]
+    host_buf = np.zeros(N * 8192 + 512 + N * 4096 + N * 1024, np.float32)   # every buffer registered
+    qg = host_buf[:N * 8192].reshape(N, 16, 512)
+    norms = host_buf[N * 8192:N * 8192 + 512]
+    out = host_buf[N * 8192 + 512:N * 12288 + 512].reshape(N, 16, 256)
+    kv_new = host_buf[N * 12288 + 512:].reshape(N, 2, 2, 256)
+    for i, d in enumerate(ds):
+        qg[i, :, :256], qg[i, :, 256:] = d["q"], d["gate"]
+        kv_new[i, 0], kv_new[i, 1] = d["k_new"], d["v_new"]
+    norms[:256], norms[256:] = ds[0]["q_norm"], ds[0]["k_norm"]
+
+    def caches():
+        res = []
+        for d in ds:
+            kc = torch.zeros(d["length"] + 2, 2, 256, dtype=torch.float16, device="cuda")
+            vc = torch.zeros_like(kc)
+            kc[:d["length"]] = dev(d["k_cache"])
+            vc[:d["length"]] = dev(d["v_cache"])
+            res.append((kc, vc))
+        return res
+
+    cs_d = caches()
+    dqg, dn, dkv = dev(qg), dev(norms), dev(kv_new)
+    ao = torch.zeros(N, 16, 256, device="cuda")
+    rb.attn_decode_batch([rb.attn_job(dqg[i], dqg[i, 0, 256:], dkv[i, 0], dkv[i, 1], dn[:256], dn[256:],
+                                      cs_d[i][0], cs_d[i][1], d["length"], d["length"], ao[i], qg_stride=512)
+                          for i, d in enumerate(ds)])
+    ref = host(ao)
+    assert lib.kernel_cuda_host_register(C.c_void_p(host_buf.ctypes.data), host_buf.nbytes) == 0, rb.last_error()
+    try:
+        cs_r = caches()
+        jobs = [rb.attn_job(qg[i].ctypes.data, qg[i, 0, 256:].ctypes.data, kv_new[i, 0].ctypes.data,
+                            kv_new[i, 1].ctypes.data, norms.ctypes.data, norms[256:].ctypes.data, cs_r[i][0],
+                            cs_r[i][1], d["length"], d["length"], out[i].ctypes.data, qg_stride=512)
+                for i, d in enumerate(ds)]
+        rb.attn_decode_batch_host(jobs)
+    finally:
+        assert lib.kernel_cuda_host_unregister(C.c_void_p(host_buf.ctypes.data)) == 0, rb.last_error()
+    assert np.array_equal(out, ref)
+    for i, d in enumerate(ds):
+        assert torch.equal(cs_r[i][0][:d["length"] + 1], cs_d[i][0][:d["length"] + 1])
