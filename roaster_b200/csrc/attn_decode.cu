@@ -1265,8 +1265,8 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
             out.add(s.out, 4096 * sizeof(float));
         }
         if (reg) {
-            in.build(64 << 10);
-            late.build(64 << 10);
+            in.build(kRunGap);
+            late.build(kRunGap);
             cudaStream_t cs = nullptr;
             static cudaEvent_t ev[2];               // decode inputs queued, gates landed
             static int made = -1;
@@ -1282,7 +1282,7 @@ extern "C" int kernel_attn_decode_batch_host(const KernelAttnDecodeJob *jobs, in
             if (!split) {
                 for (const auto &g : late.segs)
                     in.segs.push_back(g);
-                in.build(64 << 10);
+                in.build(kRunGap);
                 late = HostRuns();
             }
             out.build(0);

@@ -145,12 +145,14 @@ int deltanet_step_batch(const KernelDeltaStepJob *jobs, int n)
 }
 
 // Host buffers all registered: pipelined over three streams. The copy engine spends a few
-// microseconds on every copy whatever its size, so the call makes few: first the small
-// per-head inputs (g, beta) of every job, as the runs they form, then each chunk's q, k, v runs,
-// in at most kDnChunks chunks of at least 32 jobs. Chunk c's step launch waits for its inputs
-// (an event); its outputs copy back on the out stream (the other copy engine) once its launch is
-// done, so the next chunk's launch never waits behind an output copy. The work stream waits for
-// the last output copy, so synchronising it covers the whole call.
+// microseconds on every copy whatever its size (about the link time of 150 KB), so the call
+// makes few: runs closer than 128 KB copy as one, first the small per-head inputs (g, beta) of
+// every job, then each chunk's q, k, v runs, in at most kDnChunks chunks of at least 32 jobs.
+// Chunk c's step launch waits for its inputs (an event). Outputs copy back on the out stream
+// (the other copy engine), each chunk's once its launch is done and none before the last input
+// has landed: device-to-host copies beside the input copies slow them down, and the inputs are
+// the critical path. The work stream waits for the last output copy, so synchronising it covers
+// the whole call.
 #ifndef DN_HOST_CHUNKS
 #define DN_HOST_CHUNKS 3
 #endif
@@ -185,7 +187,7 @@ int step_registered(const KernelDeltaStepJob *jobs, int n)
         small.add(jobs[i].g, nh * 4);
         small.add(jobs[i].beta, nh * 4);
     }
-    small.build(64 << 10);
+    small.build(kRunGap);
     std::vector<HostRuns> in(chunks), out(chunks);
     std::vector<size_t> base(chunks + 1, up16(small.bytes) + 16);
     for (int c = 0; c < chunks; c++) {
@@ -197,7 +199,7 @@ int step_registered(const KernelDeltaStepJob *jobs, int n)
             in[c].add(s.v, nv * 4);
             out[c].add(s.out, nv * 4);
         }
-        in[c].build(64 << 10);
+        in[c].build(kRunGap);
         out[c].build(0);
         base[c + 1] = base[c] + up16(in[c].bytes) + up16(out[c].bytes) + 32;
     }
@@ -215,6 +217,8 @@ int step_registered(const KernelDeltaStepJob *jobs, int n)
         if (chunks > 1 && rec(ev_in[c], cs) != 0)
             return -1;
     }
+    if (chunks > 1 && wait(os, ev_in[chunks - 1]) != 0)
+        return -1;
     std::vector<KernelDeltaStepJob> dj(jobs, jobs + n);
     for (int c = 0; c < chunks; c++) {
         const int i0 = (int)((long long)n * c / chunks), i1 = (int)((long long)n * (c + 1) / chunks);

@@ -82,6 +82,9 @@ bool host_registered(const void *p, size_t bytes);
 // segments, so a copy back never writes host bytes outside the outputs. Each run is one
 // cudaMemcpyAsync to or from a device staging area laid out run after run; dev() gives the
 // staging address of a host pointer inside a run.
+// Host runs closer than this copy as one: a copy costs the engine a few microseconds whatever
+// its size, about the link time of 150 KB.
+constexpr size_t kRunGap = 128 << 10;
 struct HostRuns {
     struct Run {
         uintptr_t lo, hi;
