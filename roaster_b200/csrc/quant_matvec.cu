@@ -1142,6 +1142,7 @@ struct RParams {
 
 __global__ void __launch_bounds__(256) quant_mm_reduce_kernel(const __grid_constant__ RParams p)
 {
+    griddep_wait();                 // launched as a dependent of the matmul that wrote the planes
     for (long long u = blockIdx.x * 256ll + threadIdx.x; u < p.n; u += (long long)gridDim.x * 256) {
         int lo = 0, hi = p.njobs - 1;
         while (lo < hi) {
@@ -1272,6 +1273,9 @@ __device__ __forceinline__ uint32_t hi_lo_f16(float v, bool lo)
 __global__ void __launch_bounds__(256) quant_mm_tc_prep_kernel(const __grid_constant__ PParamsTc pp)
 {
     __shared__ float red[8];
+    // the matmul launch that follows may start now: only its activation copies and its epilogue
+    // read what this kernel writes, and they wait for it (griddepcontrol.wait)
+    griddep_launch_dependents();
     int jx = 0;
     while (jx + 1 < pp.njobs && pp.jobs[jx + 1].cta0 <= (int)blockIdx.x)
         jx++;
@@ -1423,6 +1427,7 @@ __device__ __forceinline__ void tc_tile(const TParams &p, long long item)
         // three independent streams, one lane each, so none waits behind another's buffer:
         // lane 0 the B quarter tiles, lane 1 the raw blocks, lane 2 (Q4_K) the sums tiles
         if (lane == 0) {
+            griddep_wait();                               // the activation tiles are the prep kernel's
             int nst[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             for (int g = 0; g < nq; g++) {
                 const int s = g % Cfg::kStB;
@@ -1461,6 +1466,7 @@ __device__ __forceinline__ void tc_tile(const TParams &p, long long item)
                 if (nraw[r])
                     mbar_wait(BAR(kRawFull + r), (uint32_t)(nraw[r] - 1) & 1u, 20000000ll);
         } else if (lane == 2 && !Q6) {
+            griddep_wait();                               // so are the sums tiles
             int nsum[2] = {0, 0};
             for (int b = 0; b < nb; b++) {
                 if (b >= 2 && !mbar_wait(BAR(kMnEmpty + (b & 1)), (uint32_t)((b >> 1) - 1) & 1u)) {
@@ -1588,6 +1594,7 @@ __device__ __forceinline__ void tc_tile(const TParams &p, long long item)
                 mbar_arrive(BAR(kSclEmpty + (b & 1)));
             }
         }
+        griddep_wait();                                   // the token exponents are the prep kernel's
         if (ok) {
             const int row = rt * kRows + r;
             if (row < J.rows) {
@@ -1755,6 +1762,7 @@ __device__ __forceinline__ void tc_tile(const TParams &p, long long item)
         if (!ok && lane == 0)
             atomicOr(p.err, kErrWaitTimeout);
     }
+    griddep_launch_dependents();                          // this CTA's outputs are written
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -2115,8 +2123,8 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
     if (rp.njobs == 0)
         return 0;
     const long long blocks = std::min<long long>((rp.n + 255) / 256, 8ll * R.num_sms);
-    quant_mm_reduce_kernel<<<(unsigned)blocks, 256, 0, R.stream>>>(rp);
-    return launched("quant_mm_reduce_kernel");
+    return launch_dependent(quant_mm_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, R.stream,
+                            "quant_mm_reduce_kernel", rp);
 }
 
 
@@ -2300,15 +2308,17 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         TParams2 p2;
         p2.f[0] = tp[0];
         p2.f[1] = tp[1];
-        quant_mm_tc_kernel<<<(unsigned)items, tcm::kThreads, smem, R.stream>>>(p2);
-        if (launched("quant_mm_tc_kernel") != 0)
+        // a programmatic dependent of the prep kernel: set-up, the weight stream and the decode
+        // start while the prep kernel finishes
+        if (launch_dependent(quant_mm_tc_kernel, dim3((unsigned)items), dim3(tcm::kThreads), (size_t)smem, R.stream,
+                             "quant_mm_tc_kernel", p2) != 0)
             return -1;
     }
     if (rp.njobs == 0)
         return 0;
     const long long blocks = std::min<long long>((rp.n + 255) / 256, 8ll * R.num_sms);
-    quant_mm_reduce_kernel<<<(unsigned)blocks, 256, 0, R.stream>>>(rp);
-    return launched("quant_mm_reduce_kernel");
+    return launch_dependent(quant_mm_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, R.stream,
+                            "quant_mm_reduce_kernel", rp);
 }
 
 }  // namespace
