@@ -84,7 +84,9 @@ int   kernel_cuda_upload_f32_f16(uint16_t *dst_dev, const float *src_host, size_
  * pinned (cudaHostRegister). When every buffer of a call to the host-buffer entry points
  * (kernel_attn_decode_batch_host, kernel_deltanet_step_batch_host) lies in registered memory,
  * the copy engine moves them directly, a few large copies per call (the buffers' contiguous
- * runs), with no staging memcpy on the host; other calls go through pinned staging as before.
+ * runs), with no staging memcpy on the host, overlapped with the call's kernels where the data
+ * allows (gates beside the decode kernel; DeltaNet inputs and outputs in chunks on two more
+ * streams); other calls go through pinned staging as before.
  * A buffer must not be freed while registered. 0 = ok, -1 = error (e.g. pages already
  * registered). */
 int   kernel_cuda_host_register(void *ptr, size_t bytes);
