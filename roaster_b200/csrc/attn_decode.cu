@@ -401,10 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             const long long avail = J.length - t0;          // rows that exist from t0 on
             const __half *kg = J.k_cache + (t0 * 2 + kvh) * kHD + lane * 8;
             const __half *vg = J.v_cache + (t0 * 2 + kvh) * kHD + lane * 8;
-            // the first item's q is prepared once its first stages are on their way
-            const int early = ntiles < kStages ? ntiles : kStages;
-            if (k == 0 && early == 0)
-                ok = prep(0);
+            // (the first item's q is the consumers' to prepare: they are idle until it is ready)
             for (int i = 0; i < ntiles && ok; i++, seq++) {
                 const int s = seq % kStages;
                 const unsigned f = seq / kStages;
@@ -426,8 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                     }
                 }
                 cp_async_arrive(smem_addr(&sm.full[s]));
-                if (k == 0 && i == early - 1)
-                    ok = prep(0);
             }
             // the next item's q, ready while the consumers finish this item from the ring
             if (ok && i0 + k + 1 < i1)
@@ -450,6 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const uint32_t vx = (uint32_t)(((lane >> 3) & 1) ^ (lane & 7));
     const uint32_t krow = (uint32_t)(lane & 15) * 128;
     const uint32_t vrow = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * 128;
+
+    // The first item's q: the four consumer warps prepare it (two heads each) while the producers'
+    // first stages are in flight, and arrive on its hand-off barrier in the producers' place
+    // (same count), so the later items' phases are unchanged.
+    if (p.cta_off[blockIdx.x] < p.cta_off[blockIdx.x + 1]) {
+        int j, kvh, split, item;
+        item_decode(p, p.cta_off[blockIdx.x], j, kvh, split, item);
+        prep_q_warp(p, p.jobs[j], kvh, sm.qf[0], warp, lane);
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(smem_addr(&sm.qready[0]));
+    }
 
     int kq = 0;                                  // this CTA's item counter
     for (int idx = p.cta_off[blockIdx.x]; idx < p.cta_off[blockIdx.x + 1]; idx++, kq++) {
