@@ -254,21 +254,12 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
     auto rec = [&](int i) { return i < ns ? part0 + (long long)i * 2 * kPF : newp; };
     float *dst = J.pdst ? J.pdst + kvh * kPF : (p.pout ? p.pout + ((long long)j * 2 + kvh) * kPF : nullptr);
     {
-        float m = -INFINITY;
-        for (int i = t; i < np; i += 256)
-            m = fmaxf(m, __ldcg(rec(i) + h));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if ((t & 31) == 0)
-            red[t >> 5] = m;
-        __syncthreads();
-        float M = red[0];
-#pragma unroll
-        for (int w = 1; w < 8; w++)
-            M = fmaxf(M, red[w]);
+        // One pass over the records: part group g merges parts g, g + 4, ... with a running
+        // maximum (every load of a batch issued before its arithmetic), then group 0 rescales the
+        // four groups' sums to the overall maximum. One memory round trip per batch instead of a
+        // first pass for the maximum.
         constexpr int B = 8;
-        float L = 0.f;
+        float Mg = -INFINITY, L = 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int i0 = grp; i0 < np; i0 += 4 * B) {
             float mv[B], lv[B];
@@ -287,31 +278,50 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
                     vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
+            float mb = Mg;
+#pragma unroll
+            for (int u = 0; u < B; u++)
+                mb = fmaxf(mb, mv[u]);
+            if (mb == -INFINITY)
+                continue;
+            const float sc = Mg == -INFINITY ? 0.f : exp2f(Mg - mb);
+            L *= sc;
+            acc.x *= sc;
+            acc.y *= sc;
+            acc.z *= sc;
+            acc.w *= sc;
 #pragma unroll
             for (int u = 0; u < B; u++) {
-                const float w = (mv[u] == -INFINITY) ? 0.f : lv[u] * exp2f(mv[u] - M);
+                const float w = (mv[u] == -INFINITY) ? 0.f : lv[u] * exp2f(mv[u] - mb);
                 L += w;
                 acc.x = fmaf(w, vv[u].x, acc.x);
                 acc.y = fmaf(w, vv[u].y, acc.y);
                 acc.z = fmaf(w, vv[u].z, acc.z);
                 acc.w = fmaf(w, vv[u].w, acc.w);
             }
+            Mg = mb;
         }
         gacc[grp][t & 63] = acc;
-        if ((t & 63) == 0)
+        if ((t & 63) == 0) {
             gl[grp] = L;
+            red[grp] = Mg;
+        }
         __syncthreads();
         if (grp == 0) {
-            float4 a = gacc[0][t];
-            float Lt = gl[0];
+            const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            float Lt = 0.f;
 #pragma unroll
-            for (int g2 = 1; g2 < 4; g2++) {
+            for (int g2 = 0; g2 < 4; g2++) {
+                if (red[g2] == -INFINITY)
+                    continue;
+                const float f = exp2f(red[g2] - M);
                 const float4 b = gacc[g2][t];
-                a.x += b.x;
-                a.y += b.y;
-                a.z += b.z;
-                a.w += b.w;
-                Lt += gl[g2];
+                a.x = fmaf(f, b.x, a.x);
+                a.y = fmaf(f, b.y, a.y);
+                a.z = fmaf(f, b.z, a.z);
+                a.w = fmaf(f, b.w, a.w);
+                Lt = fmaf(f, gl[g2], Lt);
             }
             const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
             const float o[4] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv};
