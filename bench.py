@@ -62,6 +62,8 @@ def args_parse():
     ap.add_argument("--proj-steps", type=int, default=20)
     ap.add_argument("--step-rounds", type=int, default=10, help="timed rounds of the batched-step measurement")
     ap.add_argument("--no-shards", action="store_true", help="skip the per-GPU shard sweep at N=1")
+    ap.add_argument("--no-recurrent", action="store_true", help="skip the config-1 recurrent decode (rank 0)")
+    ap.add_argument("--recurrent-steps", type=int, default=RECUR_STEPS)
     ap.add_argument("--kv-lo", type=int, default=1024, help="smallest slot window (config 2: 1024)")
     ap.add_argument("--kv-hi", type=int, default=32768, help="largest slot window (config 2: 32768)")
     ap.add_argument("--cpu-json", help=argparse.SUPPRESS)       # internal: CPU leg in a subprocess
@@ -308,6 +310,58 @@ def cpu_long(window: int, slots: int, threads: int) -> dict:
             "projection_ms_subtracted": proj * 1e3}
 
 
+RECUR_LAYERS = 30               # config 1: one slot, 30 Gated DeltaNet layers
+RECUR_STEPS = 1024              # ... stepped 1024 times in sequence
+
+
+def cpu_recurrent(threads: int, steps: int) -> dict:
+    """The reference's own config-1 decode: per step, recurrent_delta_step (kernels.c, through
+    oracle/_ref) for each of the 30 layers of one slot, `steps` timed steps after one warm-up
+    step. The step's cost does not depend on the values, so one seeded input set serves every
+    step; the states evolve."""
+    import ctypes as C
+
+    import numpy as np
+
+    import oracle
+    from roaster_b200 import synth
+    lib = oracle.ref_lib()
+    rng = np.random.default_rng(11)
+    dn = synth.delta_step_inputs(rng, RECUR_LAYERS)
+    state = (0.02 * rng.standard_normal((RECUR_LAYERS, 32, 128, 128), dtype=np.float32)).astype(np.float32)
+    out = np.zeros((32, 128), np.float32)
+    fp = C.POINTER(C.c_float)
+    args = [np.ascontiguousarray(dn[k]) for k in ("q", "k", "v", "g", "beta")]
+    ts = []
+    for _ in range(steps + 1):
+        t0 = time.perf_counter()
+        for l in range(RECUR_LAYERS):
+            lib.ref_delta_step(state[l].ctypes.data_as(fp), *[x[l].ctypes.data_as(fp) for x in args],
+                               out.ctypes.data_as(fp))
+        ts.append(time.perf_counter() - t0)
+    step_s = statistics.median(ts[1:])
+    return {"step_s": step_s, "tok_s": 1.0 / step_s, "steps": steps, "threads": threads}
+
+
+def cpu_parity1(path: str) -> dict:
+    """Config-1 parity: the sampled layers' whole sequences (saved by the GPU arm) through the
+    reference's recurrence (oracle impl "ref": delta_head as pf_ssm runs it, one token at a
+    time) from the same initial states; final states and every step's outputs compared."""
+    import numpy as np
+
+    import oracle as O
+    z = np.load(path)
+    impl = "ref" if O.have_ref() else "port"
+    st_err, out_err = [], []
+    for i in range(int(z["n"])):
+        st = np.ascontiguousarray(z[f"st0_{i}"])
+        o = O.delta_prefill(st, *[z[f"{k}{i}"] for k in ("q", "k", "v", "g", "beta")], impl=impl)
+        st_err.append(O.maxrel(z[f"st_end{i}"], st))
+        out_err.append(O.maxrel(z[f"out{i}"], o))
+    return {"impl": impl, "state_maxrel": max(st_err), "out_maxrel": max(out_err),
+            "layers": [int(x) for x in z["layers"]], "steps": int(z["steps"])}
+
+
 def cpu_leg(task: str, threads: int | None = None, timeout: int = 1800, native: bool = False, **kw):
     """Run one CPU task in a fresh process (its OpenMP runtime never meets torch's)."""
     threads = threads or os.cpu_count() or 1
@@ -349,6 +403,10 @@ def cpu_main(spec: dict) -> dict:
         return cpu_prefill(spec["threads"])
     if t == "long":
         return cpu_long(spec["window"], spec["slots"], spec["threads"])
+    if t == "recurrent":
+        return cpu_recurrent(spec["threads"], spec["steps"])
+    if t == "parity1":
+        return cpu_parity1(spec["path"])
     raise ValueError(t)
 
 
@@ -913,6 +971,73 @@ def run_long_context(R, torch, dist, dev, stream, world: int, rank: int, window:
 
 # ------------------------------------------------------------------------------ config 2 (GPU arm)
 
+def run_recurrent(R, torch, dev, stream, steps: int, warmup: int, parity: bool) -> dict:
+    """Config 1: one slot's 30 Gated DeltaNet layers stepped `steps` times in sequence (after
+    `warmup` untimed steps), one kernel_deltanet_step_batch of 30 jobs (one per layer) per step,
+    each step's inputs drawn with config 1's distributions. The 30 states (63 MB) would stay in
+    the 126 MB L2, so a 256 MB device write precedes every timed step and each step is timed
+    alone (CUDA events on the launching stream). With `parity`, layers 0 and 29 are saved for
+    the CPU check against the reference's recurrence over the whole sequence."""
+    import numpy as np
+
+    from roaster_b200 import synth
+    L, n = RECUR_LAYERS, steps + warmup
+    g = torch.Generator(device=dev)
+    g.manual_seed(9100)
+    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    nz = torch.nn.functional.normalize
+    q = nz(rn(n, L, 16, 128), dim=-1).contiguous()
+    k = nz(rn(n, L, 16, 128), dim=-1).contiguous()
+    v = rn(n, L, 32, 128)
+    beta = torch.sigmoid(rn(n, L, 32))
+    gl = (-torch.exp(-1 + 0.5 * rn(n, L, 32)) * torch.nn.functional.softplus(rn(n, L, 32))).contiguous()
+    states = synth.device_normal(torch, (L, 32, 128, 128), 9101, dev, torch.float32, std=0.02)
+    pick = [0, L - 1]
+    st0 = states[pick].cpu().numpy() if parity else None
+    out = torch.empty(n, L, 32, 128, device=dev)
+    # job arrays from raw addresses (30 x (steps + warmup) jobs)
+    qa, ka, va, ga, ba, oa, sa = (t.data_ptr() for t in (q, k, v, gl, beta, out, states))
+    arrs = []
+    for s in range(n):
+        jobs = [R.delta_job(sa + l * 32 * 128 * 128 * 4, qa + (s * L + l) * 2048 * 4, ka + (s * L + l) * 2048 * 4,
+                            va + (s * L + l) * 4096 * 4, ga + (s * L + l) * 32 * 4, ba + (s * L + l) * 32 * 4,
+                            oa + (s * L + l) * 4096 * 4) for l in range(L)]
+        arrs.append((R.KernelDeltaStepJob * L)(*jobs))
+    lib = R.lib()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)          # 256 MB > L2
+    for s in range(warmup):
+        if lib.kernel_deltanet_step_batch(arrs[s], L) != 0:
+            raise RuntimeError(R.last_error())
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    launches0 = R.launch_count()
+    for i in range(steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        rc = lib.kernel_deltanet_step_batch(arrs[warmup + i], L)
+        evs[i][1].record(stream)
+        if rc != 0:
+            raise RuntimeError(R.last_error())
+    torch.cuda.synchronize()
+    launches = R.launch_count() - launches0
+    R.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    res = {"ms": ms, "launches": launches}
+    if parity:
+        z = {"n": np.int64(len(pick)), "layers": np.array(pick), "steps": np.int64(n)}
+        for i, l in enumerate(pick):
+            z[f"st0_{i}"] = st0[i]
+            z[f"st_end{i}"] = states[l].cpu().numpy()
+            for nm, t in (("q", q), ("k", k), ("v", v), ("g", gl), ("beta", beta), ("out", out)):
+                z[f"{nm}{i}"] = np.ascontiguousarray(t[:, l].cpu().numpy())
+        fd, path = tempfile.mkstemp(suffix=".npz", prefix="roaster_parity1_")
+        os.close(fd)
+        np.savez(path, **z)
+        res["parity_file"] = path
+    del q, k, v, beta, gl, states, out, flush
+    return res
+
+
 def attn_step_bytes(n: int, mean_L: float) -> float:
     """Algorithmic bytes of one decode-attention launch over n slots of mean window mean_L:
     the f16 K/V rows (2 kv heads x K,V x 256 x 2 B per position), the appended row, q/gate/out."""
@@ -1374,6 +1499,46 @@ def run_ours(a):
             except Exception as e:  # reported, not fatal
                 long_ctx["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
 
+    recur = None
+    if not a.no_recurrent and rank == 0:
+        # config 1 is one slot: it does not shard; rank 0 runs it on its GPU
+        r1 = run_recurrent(R, torch, dev, stream, a.recurrent_steps, 3, not a.no_parity)
+        rbytes = RECUR_LAYERS * (32 * 128 * 128 * 4 * 2 + (2 * 2048 + 4096 + 64) * 4 + 4096 * 4)
+        hbm_r, _, src_r = peaks()
+        gbs_r = rbytes / (r1["ms"] * 1e-3) / 1e9
+        recur = {"metric": "recurrent decode tok/s (config 1: 1 slot, 30 Gated DeltaNet layers, sequential steps)",
+                 "value": round(1e3 / r1["ms"], 1), "unit": "tok/s", "ms_per_step": round(r1["ms"], 5),
+                 "steps": a.recurrent_steps, "warmup": 3, "gpu_launches": int(r1["launches"]),
+                 "config": {"workload": "config 1", "layers": RECUR_LAYERS, "slots": 1,
+                            "launch": "one kernel_deltanet_step_batch of 30 jobs per step",
+                            "l2": "states 63 MB < L2: a 256 MB device write before every timed step, each "
+                                  "step timed alone"},
+                 "roofline": {"bound": "hbm", "kernel": "deltanet_step_kernel", "achieved": round(gbs_r, 1),
+                              "peak": hbm_r, "unit": "GB/s", "frac": round(gbs_r / hbm_r, 4),
+                              "peak_source": f"{src_r} hbm_gbs",
+                              "algorithmic_bytes_per_step": rbytes,
+                              "scope": "state read + write, inputs and outputs of the 30 layers per step"},
+                 "scope": "rank 0 only (one slot does not shard)"}
+        if "parity_file" in r1:
+            try:
+                pr = cpu_leg("parity1", path=r1["parity_file"], timeout=900)
+                recur["parity"] = dict(pr, tolerance=1e-4, **{"pass": max(pr["state_maxrel"], pr["out_maxrel"]) <= 1e-4},
+                                       what="layers 0 and 29 over every step (warm-up + timed) from the same "
+                                            "initial states, against the reference's recurrence")
+            except Exception as e:  # reported, not fatal
+                recur["parity"] = {"pass": None, "what": f"failed: {e}"[:300]}
+            finally:
+                os.unlink(r1["parity_file"])
+        if world == 1 and not a.no_cpu_baseline:
+            try:
+                c = cpu_leg_ref("recurrent", steps=20, timeout=900)
+                recur["cpu_baseline"] = {"value": round(c["tok_s"], 3), "unit": "tok/s", "cores": c["threads"],
+                                         "kind": "reference", "build": c["build"],
+                                         "sample": "20 timed steps (after 1 warm-up) of recurrent_delta_step over "
+                                                   "the 30 layers of one slot"}
+            except Exception as e:  # reported, not fatal
+                recur["cpu_baseline"] = {"value": None, "sample": f"failed: {e}"[:300]}
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
@@ -1416,7 +1581,7 @@ def run_ours(a):
             "gpu_launches": int(c2["launches"]),
             "shards": shards, "weak_64_per_gpu": weak,
             "prefill": prefill, "long_context": long_ctx, "projections": proj, "prefill_projections": pproj,
-            "batched_step": bstep,
+            "batched_step": bstep, "recurrent": recur,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

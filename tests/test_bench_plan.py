@@ -48,3 +48,17 @@ def test_reference_cpu_leg_steps_every_slot_with_growth(oracle_lib):
     res = json.loads(r.stdout.strip().splitlines()[-1])
     assert res["steps"] == 2 and res["slots"] == 3
     assert res["tok_s"] > 0 and res["seconds"] > 0
+
+
+def test_reference_recurrent_leg_steps_thirty_layers(oracle_lib):
+    """Config 1's CPU leg in its own process: the reference's recurrent_delta_step over the 30
+    layers of one slot, 2 timed steps."""
+    if not oracle_lib.have_ref():
+        pytest.skip("reference build not present")
+    spec = json.dumps({"task": "recurrent", "steps": 2, "threads": 2})
+    env = dict(os.environ, OMP_NUM_THREADS="2", CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--cpu-json", spec],
+                       capture_output=True, text=True, env=env, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert res["steps"] == 2 and res["tok_s"] > 0 and res["step_s"] > 0
