@@ -31,8 +31,10 @@ _u16p = C.POINTER(C.c_uint16)
 _libs: dict = {}
 
 
-# Where the reference checkout lives (its src/ holds model.c); ROASTER_REFERENCE overrides.
-REFERENCE_ROOT = os.environ.get("ROASTER_REFERENCE", "/root/reference")
+# Where the reference checkout lives (its src/ holds model.c): by default a directory named
+# `reference` beside this repository's root; ROASTER_REFERENCE overrides.
+REFERENCE_ROOT = os.environ.get("ROASTER_REFERENCE",
+                                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 # CPU architecture of the GPU host (what -march=native selects there), for the reference build
 # with the reference's own flags; ROASTER_REF_MARCH overrides.
 REF_MARCH = os.environ.get("ROASTER_REF_MARCH", "sapphirerapids")
