@@ -694,9 +694,12 @@ int prefill_launch(const KernelAttnPrefillJob *jobs, int n)
                 items.emplace_back(nt + 2, ((unsigned)i << 26) | ((unsigned)h << 22) | (unsigned)qt);
         }
     }
+    // prompt by prompt, each prompt's items longest first: the CTAs then work on one or two
+    // prompts' K/V at a time, which stays in L2, instead of every prompt's at once
     std::stable_sort(items.begin(), items.end(),
                      [](const std::pair<long long, unsigned> &a, const std::pair<long long, unsigned> &b) {
-                         return a.first > b.first;
+                         const unsigned ja = a.second >> 26, jb = b.second >> 26;
+                         return ja != jb ? ja < jb : a.first > b.first;
                      });
     const int grid = (int)std::min<size_t>(items.size(), (size_t)R.num_sms);
     std::vector<std::vector<unsigned>> per(grid);
