@@ -243,11 +243,21 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
     __shared__ float red[8];
     __shared__ float4 gacc[4][64];
     __shared__ float gl[4];
-    griddep_wait();
-    griddep_launch_dependents();
     const int j = blockIdx.x >> 4, kvh = (blockIdx.x >> 3) & 1, h = blockIdx.x & 7;
     const DJob &J = p.jobs[j];
     const int t = threadIdx.x, grp = t >> 6, d = (t & 63) * 4;
+    // The gates are inputs, not the decode kernel's output: this grid starts only once every
+    // decode CTA has passed its own griddepcontrol.wait (the kernels that wrote the inputs have
+    // completed), so they are read before the wait, off the merge's critical path.
+    float gv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (grp == 0 && !J.pdst && !p.pout) {
+        const float *g = J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d;
+#pragma unroll
+        for (int x = 0; x < 4; x++)
+            gv[x] = __ldg(g + x);
+    }
+    griddep_wait();
+    griddep_launch_dependents();
     const int ns = J.nsplit, np = ns + (J.append ? 1 : 0);
     const float *part0 = p.part + (long long)(J.item_base + kvh) * kPF;
     const float *newp = p.newpart + ((long long)j * 2 + kvh) * kPF;
@@ -332,11 +342,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
                 }
                 *reinterpret_cast<float4 *>(dst + 16 + h * kHD + d) = make_float4(o[0], o[1], o[2], o[3]);
             } else {
-                const float *g = J.gate + (long long)(kvh * 8 + h) * J.qg_stride + d;
                 float *out = J.out + (kvh * 8 + h) * kHD + d;
 #pragma unroll
                 for (int x = 0; x < 4; x++)
-                    out[x] = o[x] * (1.0f / (1.0f + expf(-__ldg(g + x))));
+                    out[x] = o[x] * (1.0f / (1.0f + expf(-gv[x])));
             }
         }
     }
