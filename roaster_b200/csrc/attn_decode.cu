@@ -137,7 +137,10 @@ __device__ __forceinline__ bool aborted(Smem &sm)
 // RMSNorm * w then RoPE (dims 0..63) of query heads 2*pw and 2*pw + 1 of kv head `kvh` into qf,
 // by one warp with shuffles only: lane l holds elements l + 32 i of a head, so the RoPE pair
 // (d, d + 32) of d = lane sits in one lane. The four producer warps together prepare the 8 heads.
-__device__ void prep_q_warp(const DParams &p, const DJob &J, int kvh, float (*qf)[kHD], int pw, int lane)
+// `after_loads` runs once every load is issued (before any of them is used).
+template <typename AfterLoads>
+__device__ void prep_q_warp(const DParams &p, const DJob &J, int kvh, float (*qf)[kHD], int pw, int lane,
+                            AfterLoads after_loads)
 {
     // every load first (both heads' rows and the norm weights: one memory round trip)
     float x[2][8], w[8];
@@ -151,6 +154,7 @@ __device__ void prep_q_warp(const DParams &p, const DJob &J, int kvh, float (*qf
 #pragma unroll
     for (int i = 0; i < 8; i++)
         w[i] = __ldg(J.q_norm + lane + 32 * i);
+    after_loads();
     float sn, cs;
     sincosf((float)J.position * p.inv_freq[lane], &sn, &cs);
 #pragma unroll
@@ -403,13 +407,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             }
             int jj, kh, sp, it;
             item_decode(p, i0 + k, jj, kh, sp, it);
-            prep_q_warp(p, p.jobs[jj], kh, sm.qf[b], pw, lane);
+            prep_q_warp(p, p.jobs[jj], kh, sm.qf[b], pw, lane, [] {});
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(smem_addr(&sm.qready[b]));
             return true;
         };
         bool ok = true;
+        // the consumers' loads of the first item's q go out before the first stages' copies,
+        // ahead of them in the memory system (named barrier 2: 128 arrivals, 128 waits)
+        if (i0 < i1)
+            named_bar_sync(2, 2 * 128);
         for (int k = 0; i0 + k < i1 && ok && !aborted(sm); k++) {
             int j, kvh, split, item;
             item_decode(p, i0 + k, j, kvh, split, item);
@@ -467,11 +475,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 
     // The first item's q: the four consumer warps prepare it (two heads each) while the producers'
     // first stages are in flight, and arrive on its hand-off barrier in the producers' place
-    // (same count), so the later items' phases are unchanged.
+    // (same count), so the later items' phases are unchanged. The producers start their copies
+    // once these loads are issued (named barrier 2), so the loads do not queue behind them.
     if (p.cta_off[blockIdx.x] < p.cta_off[blockIdx.x + 1]) {
         int j, kvh, split, item;
         item_decode(p, p.cta_off[blockIdx.x], j, kvh, split, item);
-        prep_q_warp(p, p.jobs[j], kvh, sm.qf[0], warp, lane);
+        prep_q_warp(p, p.jobs[j], kvh, sm.qf[0], warp, lane, [] { named_bar_arrive(2, 2 * 128); });
         __syncwarp();
         if (lane == 0)
             mbar_arrive(smem_addr(&sm.qready[0]));

@@ -190,6 +190,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Arrive on named barrier `id` without waiting (the threads that wait use named_bar_sync with
+// the same count).
+__device__ __forceinline__ void named_bar_arrive(int id, int threads)
+{
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // AND of `ok` over the `n` threads of named barrier `id` (also a barrier).
 __device__ __forceinline__ bool bar_all(int id, int n, bool ok)
 {
