@@ -752,7 +752,8 @@ def run_batched_step(R, torch, dev, stream, steps: int, rank: int, slots: int = 
     del mats, X, Y
     return {"group_ms": gms, "group_wall_ms": wall, "serial_ms": sms, "launches": launches,
             "rounds": st1["rounds"] - st0["rounds"], "calls": st1["calls"] - st0["calls"],
-            "products": st1["products"] - st0["products"], "max_round": st1["max_round"]}
+            "products": st1["products"] - st0["products"], "max_round": st1["max_round"],
+            "replayed": st1["replayed"] - st0["replayed"]}
 
 
 def prefill_proj_cpu_reference(seconds: float = 2.0) -> dict:
@@ -1468,6 +1469,7 @@ def run_ours(a):
                  "ms_per_step": round(gms, 4), "wall_ms_per_step": round(r["group_wall_ms"], 4),
                  "steps": a.step_rounds, "gpu_launches": int(r["launches"]), "slots": STEP_SLOTS,
                  "rounds": r["rounds"], "combined_calls": r["calls"], "merged_products": r["products"],
+                 "replayed_calls": r["replayed"],
                  "max_round": r["max_round"],
                  "per_slot_form": {"ms_per_step": round(sms, 4),
                                    "value": round(STEP_SLOTS / (sms / 1e3) * world, 1), "unit": "tok/s",

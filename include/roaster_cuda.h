@@ -446,7 +446,13 @@ int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, int n);
  * round still ends normally. Work outside rounds (prefill chunks, rollbacks) takes
  * kernel_step_group_lock / unlock, the FIFO lock the group's own batches also run under, which
  * keeps the single-stream, non-overlapping rule of this library. All functions are thread-safe;
- * none may be called with the group lock held except kernel_step_group_unlock. */
+ * none may be called with the group lock held except kernel_step_group_unlock.
+ * Projection calls are recorded: slots that keep their buffers bring the same job list
+ * (matrices, vectors, outputs, shapes, in member order) every token, so the second occurrence of
+ * a list is captured into a CUDA graph on a stream of the group's own and later ones replay it
+ * (one graph launch instead of the call's host work and launches), as long as the library's
+ * own buffers are the ones the recording used; a list that cannot be recorded runs as plain
+ * launches. The environment variable ROASTER_STEP_GRAPHS=0 turns recording off. */
 typedef struct KernelStepGroup KernelStepGroup;
 
 typedef struct {
@@ -458,6 +464,8 @@ typedef struct {
     unsigned long long errors;       /* calls that returned -1 */
     int max_round;                   /* largest round */
     int members;                     /* members joined now */
+    unsigned long long replayed;     /* projection calls replayed from a recording (a CUDA graph
+                                        of the same job list's earlier launches) */
 } KernelStepGroupStats;
 
 /* max_members >= 1; straggler_us >= 0; call_timeout_ms > 0. NULL on bad arguments. */

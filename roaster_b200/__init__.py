@@ -91,7 +91,7 @@ class KernelStepGroupStats(C.Structure):
     """Mirror of ``KernelStepGroupStats`` (include/roaster_cuda.h)."""
     _fields_ = [("rounds", C.c_ulonglong), ("calls", C.c_ulonglong), ("jobs", C.c_ulonglong),
                 ("products", C.c_ulonglong), ("merged_jobs", C.c_ulonglong), ("errors", C.c_ulonglong),
-                ("max_round", C.c_int), ("members", C.c_int)]
+                ("max_round", C.c_int), ("members", C.c_int), ("replayed", C.c_ulonglong)]
 
 
 _lib = None

@@ -1842,6 +1842,7 @@ const CUtensorMap *job_map(const unsigned char *w, long long rows, int rb, int s
             return nullptr;
         mc.idx.clear();
         mc.used = 0;
+        R.gen++;                         // recorded work may point to the reused map slots
     }
     const int i = mc.used;
     if (encode_tmap_u8_2d(&mc.host[i], w, (uint64_t)rb, (uint64_t)rows, (uint64_t)rb, (uint32_t)slot, (uint32_t)box) != 0)

@@ -49,6 +49,8 @@ int check(cudaError_t e, const char *what)
     return fail("%s: %s", what, cudaGetErrorString(e));
 }
 
+void count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
 int launched(const char *what)
 {
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -240,6 +242,7 @@ void *scratch(size_t bytes)
     if (check(cudaMalloc(&p, want), "cudaMalloc(scratch)") != 0)
         return nullptr;
     g_rt.scratch = p;
+    g_rt.gen++;
     g_rt.scratch_bytes = want;
     return p;
 }
@@ -259,6 +262,7 @@ void *dstage(size_t bytes)
     if (check(cudaMalloc(&p, want), "cudaMalloc(staging)") != 0)
         return nullptr;
     g_rt.dstage = p;
+    g_rt.gen++;
     g_rt.dstage_bytes = want;
     return p;
 }
@@ -298,6 +302,7 @@ int *counters(size_t n)
         return nullptr;
     }
     g_rt.counters = p;
+    g_rt.gen++;
     g_rt.counters_n = want;
     return p;
 }

@@ -36,6 +36,10 @@ struct Runtime {
     unsigned *err_host = nullptr;      // pinned copy of the error word (read by synchronize)
     cudaStream_t copy_stream = nullptr;   // input copies that overlap kernels on `stream`
     cudaStream_t out_stream = nullptr;    // output copies that overlap later kernels on `stream`
+    // Bumped whenever a library-owned device buffer or table that queued work may point to is
+    // replaced (scratch, counters, staging, a reset of the tensor-map table): work recorded
+    // earlier (a CUDA graph) is valid only while it is unchanged.
+    uint64_t gen = 0;
 };
 
 Runtime &rt();
@@ -48,6 +52,8 @@ int fail(const char *fmt, ...);
 int check(cudaError_t e, const char *what);
 // Check for a launch error after a kernel launch and count the launch.
 int launched(const char *what);
+// Add `n` to the launch count (kernels launched as part of a CUDA graph).
+void count_launches(uint64_t n);
 // Device scratch of at least `bytes` (grow-only; growing synchronises the stream).
 void *scratch(size_t bytes);
 // The library's second stream, for input copies that overlap kernels on the work stream

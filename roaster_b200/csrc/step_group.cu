@@ -37,6 +37,7 @@
 #include <ctime>
 #include <sched.h>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 using namespace rb;
@@ -131,6 +132,20 @@ struct KernelStepGroup {
     size_t xcap = 0, ycap = 0;
 
     KernelStepGroupStats st{};               // under m
+
+    // Projection calls recorded as CUDA graphs (runner, under the FIFO lock). A call's key is its
+    // job list: matrices, vectors, outputs and shapes in member order. Slots that keep their
+    // buffers bring the same list every token, so from its third occurrence a layer's call
+    // replays one graph instead of enqueueing its copy lists and matmul launches again.
+    struct Recorded {
+        std::vector<uintptr_t> key;
+        cudaGraphExec_t exec = nullptr;
+        uint64_t gen = 0;                    // Runtime::gen when recorded
+        uint64_t launches = 0, products = 0, merged_jobs = 0;
+        int seen = 0;
+    };
+    std::unordered_map<uint64_t, Recorded> recorded;
+    cudaStream_t rec_stream = nullptr;       // the stream recording happens on
 };
 
 namespace {
@@ -240,6 +255,7 @@ int grow(float **buf, size_t *cap, size_t floats)
     if (check(cudaMalloc(reinterpret_cast<void **>(buf), want * sizeof(float)), "step group: cudaMalloc") != 0)
         return -1;
     *cap = want;
+    rt().gen++;                      // recorded calls pointed to the old buffer
     return 0;
 }
 
@@ -264,7 +280,7 @@ int copy_list(const std::vector<const float *> &src, const std::vector<float *> 
 // Regroup the members' projections by weight matrix; a matrix shared by T >= 2 members becomes
 // one T-token product over gathered vectors. Counts go to `st` before any device work, so the
 // plan is observable without a GPU.
-int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroupStats *st)
+int enqueue_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroupStats *st)
 {
     struct Group {
         KernelCudaMatvecJob key;
@@ -360,6 +376,111 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
     return copy_list(ss, sd, sn);
 }
 
+bool recording_enabled()
+{
+    static const bool on = [] {
+        const char *e = getenv("ROASTER_STEP_GRAPHS");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+void drop_recorded(KernelStepGroup *g)
+{
+    for (auto &kv : g->recorded)
+        if (kv.second.exec)
+            cudaGraphExecDestroy(kv.second.exec);
+    g->recorded.clear();
+}
+
+// A projection call: the first occurrence of a job list runs as plain launches (it sets up the
+// buffers and tensor maps it needs), the second is recorded into a CUDA graph and launched, later
+// ones replay the graph while the library's buffers are the ones it was recorded with. Where
+// recording fails the call runs as plain launches.
+int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroupStats *st)
+{
+    if (!recording_enabled())
+        return enqueue_matvec(g, mv, st);
+    std::vector<uintptr_t> key;
+    key.reserve(mv.size() * 6);
+    for (const Entry &e : mv) {
+        const KernelCudaMatvecJob &j = e.job;
+        key.push_back(reinterpret_cast<uintptr_t>(j.matrix));
+        key.push_back(reinterpret_cast<uintptr_t>(j.vector));
+        key.push_back(reinterpret_cast<uintptr_t>(j.output));
+        key.push_back((uintptr_t)j.rows);
+        key.push_back((uintptr_t)j.cols);
+        key.push_back((uintptr_t)j.is_q6);
+    }
+    uint64_t h = 1469598103934665603ull;                 // FNV-1a over the key words
+    for (const uintptr_t v : key) {
+        h ^= (uint64_t)v;
+        h *= 1099511628211ull;
+    }
+    if (g->recorded.size() >= 512 && !g->recorded.count(h))
+        drop_recorded(g);
+    KernelStepGroup::Recorded &r = g->recorded[h];
+    if (r.key != key) {                                  // new, or another list with the same hash
+        if (r.exec)
+            cudaGraphExecDestroy(r.exec);
+        r = KernelStepGroup::Recorded();
+        r.key = std::move(key);
+    }
+    Runtime &R = rt();
+    const uint64_t gen = R.gen;
+    if (r.exec && r.gen == gen) {
+        if (check(cudaGraphLaunch(r.exec, R.stream), "step group: graph launch") != 0)
+            return -1;
+        count_launches(r.launches);
+        st->products += r.products;
+        st->merged_jobs += r.merged_jobs;
+        st->replayed++;
+        return 0;
+    }
+    if (r.exec) {                                        // recorded with buffers since replaced
+        cudaGraphExecDestroy(r.exec);
+        r.exec = nullptr;
+    }
+    if (r.seen++ == 0)
+        return enqueue_matvec(g, mv, st);
+    if (!g->rec_stream && cudaStreamCreateWithFlags(&g->rec_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        (void)cudaGetLastError();
+        g->rec_stream = nullptr;
+        return enqueue_matvec(g, mv, st);
+    }
+    KernelStepGroupStats loc{};
+    const uint64_t l0 = kernel_cuda_launch_count();
+    bool ok = cudaStreamBeginCapture(g->rec_stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (ok) {
+        const cudaStream_t saved = R.stream;
+        R.stream = g->rec_stream;                        // the launches below go into the recording
+        const int rc = enqueue_matvec(g, mv, &loc);
+        R.stream = saved;
+        cudaGraph_t graph = nullptr;
+        const bool ended = cudaStreamEndCapture(g->rec_stream, &graph) == cudaSuccess;
+        ok = rc == 0 && ended && graph && R.gen == gen &&
+             cudaGraphInstantiate(&r.exec, graph, 0) == cudaSuccess;
+        if (graph)
+            cudaGraphDestroy(graph);
+    }
+    (void)cudaGetLastError();                            // a failed recording leaves no error behind
+    const uint64_t recorded_launches = kernel_cuda_launch_count() - l0;
+    if (!ok) {
+        if (r.exec)
+            cudaGraphExecDestroy(r.exec);
+        r.exec = nullptr;
+        count_launches((uint64_t)0 - recorded_launches);  // nothing of the recording ran
+        return enqueue_matvec(g, mv, st);
+    }
+    r.gen = gen;
+    r.launches = recorded_launches;                      // counted already, run by the launch below
+    r.products = loc.products;
+    r.merged_jobs = loc.merged_jobs;
+    st->products += loc.products;
+    st->merged_jobs += loc.merged_jobs;
+    return check(cudaGraphLaunch(r.exec, R.stream), "step group: graph launch");
+}
+
 // Run call generation `gen`: every member still in the round has submitted to its slot. The
 // caller is the unique runner (its atomic update of the word made arrived == left).
 void run_call(KernelStepGroup *g, uint64_t gen, int self)
@@ -411,6 +532,7 @@ void run_call(KernelStepGroup *g, uint64_t gen, int self)
             g->st.jobs += kind == kAttn ? attn.size() : kind == kDelta ? delta.size() : mv.size();
             g->st.products += plan.products;
             g->st.merged_jobs += plan.merged_jobs;
+            g->st.replayed += plan.replayed;
         }
         if (rc != 0)
             g->st.errors++;
@@ -525,12 +647,15 @@ extern "C" void kernel_step_group_destroy(KernelStepGroup *g)
 {
     if (!g)
         return;
-    if (g->xbuf || g->ybuf) {
+    if (g->xbuf || g->ybuf || !g->recorded.empty()) {
         if (rt().device >= 0)
             cudaStreamSynchronize(rt().stream);
+        drop_recorded(g);
         cudaFree(g->xbuf);
         cudaFree(g->ybuf);
     }
+    if (g->rec_stream)
+        cudaStreamDestroy(g->rec_stream);
     delete g;
 }
 

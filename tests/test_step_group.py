@@ -420,3 +420,56 @@ def test_group_rounds_over_tokens(rb, oracle_lib):
         assert O.maxrel(host(dst[i]), st) < 1e-4
         assert O.maxrel(host(outs[i]), ref) < 1e-4
     g.close()
+
+
+@pytest.mark.gpu
+def test_group_projections_recorded_and_replayed(rb, oracle_lib):
+    """Projection calls whose job lists repeat are recorded and replayed. Each slot feeds its
+    output back as its next input (buffers A and B in turn, so two job lists alternate; a second
+    matrix reads the same input into C): over 6 tokens each list runs once plain, once recorded
+    and once replayed, with new values every token. The final buffers match the same chain run
+    one call per slot."""
+    import torch
+    import oracle as O
+    from roaster_b200 import synth
+    from tests.gpu_util import dev, host
+    N, T = 8, 6
+    w4 = dev(synth.quant_matrix(71, 512, 512, False))
+    w6 = dev(synth.quant_matrix(72, 256, 512, True))
+    rng = np.random.default_rng(9)
+    x0 = [rng.standard_normal(512).astype(np.float32) for _ in range(N)]
+
+    def buffers():
+        return [{"A": dev(x0[i]), "B": torch.zeros(512, device="cuda"), "C": torch.zeros(256, device="cuda")}
+                for i in range(N)]
+
+    def jobs(b, t):
+        src, dst = (b["A"], b["B"]) if t % 2 == 0 else (b["B"], b["A"])
+        return [(False, w4, src, dst, 512, 512), (True, w6, src, b["C"], 256, 512)]
+
+    ref = buffers()
+    for t in range(T):
+        for i in range(N):
+            rb.matvec_quant_batch(jobs(ref[i], t))
+    grp = buffers()
+    torch.cuda.synchronize()
+    g = R.StepGroup(N, straggler_us=5_000_000)
+    ids = [g.join() for _ in range(N)]
+
+    def member(i):
+        for t in range(T):
+            assert g.begin(ids[i]) == N
+            assert g.matvec(ids[i], t % 2, jobs(grp[i], t)) == 0, R.last_error()
+            assert g.end(ids[i]) == 0
+
+    _run(N, member)
+    rb.synchronize()
+    st = g.stats()
+    assert st["calls"] == T and st["errors"] == 0 and st["products"] == 2 * T
+    assert st["replayed"] == 2                   # the third occurrence of each list
+    for i in range(N):
+        for k in ("A", "B", "C"):
+            assert O.maxrel(host(grp[i][k]), host(ref[i][k])) <= 1e-4, (i, k)
+    for m in ids:
+        g.leave(m)
+    g.close()
