@@ -60,6 +60,10 @@ namespace rb {
 namespace {
 
 constexpr int kMaxJobs = 64;
+// Per-token row pointers a tensor-core call may carry in each parameter block (the activations'
+// rows, the results' rows): a job with a table reads or writes token t's row through entry
+// `first + t` instead of one contiguous [T][cols] / [T][rows] block.
+constexpr int kRowTab = 320;
 
 // ---------------------------------------------------------------- staged kernel geometry
 
@@ -1132,12 +1136,14 @@ struct RJob {
     const int *e;
     long long n0;                // first element of the job in the launch
     int rows, T, P;
+    int yr0;                     // >= 0: token t's result row is p.yr[yr0 + t]
 };
 
 struct RParams {
     RJob jobs[kMaxJobs];
     int njobs;
     long long n;
+    float *yr[kRowTab];
 };
 
 __global__ void __launch_bounds__(256) quant_mm_reduce_kernel(const __grid_constant__ RParams p)
@@ -1157,7 +1163,9 @@ __global__ void __launch_bounds__(256) quant_mm_reduce_kernel(const __grid_const
         float v = 0.f;
         for (int q = 0; q < J.P; q++)
             v += __ldcs(J.part + q * plane + i);
-        J.y[i] = v * ldexpf(1.f, -J.e[i / J.rows]);
+        const long long t = i / J.rows;
+        float *y = J.yr0 >= 0 ? p.yr[J.yr0 + t] + (i - t * J.rows) : J.y + i;
+        *y = v * ldexpf(1.f, -J.e[t]);
     }
 }
 
@@ -1227,6 +1235,7 @@ struct TJob {
     long long item0;
     int rows, nb, T, rtiles, ctiles;
     int kb0, nbt, raw;          // first block of this part, blocks per row, 1 = partial plane
+    int yr0;                    // >= 0 (results only): token t's result row is p.yr[yr0 + t]
 };
 
 struct TParams {
@@ -1234,6 +1243,7 @@ struct TParams {
     int njobs;
     long long items;
     unsigned *err;
+    float *yr[kRowTab];
 };
 
 // The activations of a call for the tensor-core kernel: each distinct X with its images.
@@ -1242,11 +1252,13 @@ struct PJobTc {
     uint4 *bq, *bsum;
     int *e;
     int T, cols, cta0;
+    int xr0;                    // >= 0: token t's activations are pp.xr[xr0 + t]
 };
 
 struct PParamsTc {
     PJobTc jobs[kMaxJobs];
     int njobs;
+    const float *xr[kRowTab];
 };
 
 __device__ __forceinline__ void sts128u(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w)
@@ -1282,7 +1294,7 @@ __global__ void __launch_bounds__(256) quant_mm_tc_prep_kernel(const __grid_cons
     const PJobTc &P = pp.jobs[jx];
     const int tok = blockIdx.x - P.cta0, T = P.T, cols = P.cols, nq = cols / 64, nb = cols / 256;
     const bool real = tok < T;
-    const float *x = P.X + (size_t)(real ? tok : 0) * cols;
+    const float *x = P.xr0 >= 0 ? pp.xr[P.xr0 + (real ? tok : 0)] : P.X + (size_t)(real ? tok : 0) * cols;
     float mx = 0.f;
     if (real)
         for (int i = threadIdx.x; i < cols / 4; i += 256) {
@@ -1602,7 +1614,8 @@ __device__ __forceinline__ void tc_tile(const TParams &p, long long item)
                 for (int i = 0; i < 32; i++) {
                     const int t = ct * kTok + 32 * half + i;
                     if (t < J.T)
-                        J.y[(size_t)t * J.rows + row] = J.raw ? acc[i] : acc[i] * ldexpf(1.f, -J.e[t]);
+                        (J.yr0 >= 0 ? p.yr[J.yr0 + t] : J.y + (size_t)t * J.rows)[row] =
+                            J.raw ? acc[i] : acc[i] * ldexpf(1.f, -J.e[t]);
                 }
             }
         } else if (lane == 0) {
@@ -2058,7 +2071,7 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
         J.item0 = mp.items;
         mp.items += (long long)J.rgroups * J.chunks * J.P;
         if (J.P > 1) {
-            rp.jobs[rp.njobs] = RJob{nullptr, J.y, nullptr, rp.n, J.rows, J.T, J.P};
+            rp.jobs[rp.njobs] = RJob{nullptr, J.y, nullptr, rp.n, J.rows, J.T, J.P, -1};
             rp.n += (long long)J.rows * J.T;
             rp.njobs++;
             part_bytes += ((size_t)J.P * J.rows * J.T * sizeof(float) + 255) / 256 * 256;
@@ -2135,7 +2148,11 @@ int matmul_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaM
 // faster): the tensor-core kernel, one launch for both formats after one prep launch for every
 // distinct X (plus a reduce launch when tiles are split along the blocks). The others go to
 // `others`.
-int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others)
+// `rows` (optional, one entry per job): per-token row pointers of a job's activations and
+// results. A job with them runs here or nowhere: when it cannot take the tensor-core path, or its
+// rows do not fit the parameter tables, the call returns 1 before launching anything.
+int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCudaMatmulJob> &others,
+                    const MmRows *rows = nullptr)
 {
     static bool attr = false;
     Runtime &R = rt();
@@ -2143,17 +2160,26 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
     memset(static_cast<void *>(tp), 0, sizeof(tp));
     struct XEnt {
         const float *X;
+        const float *const *xr;          // per-token activation rows, or null
         size_t cols, T, off_bq, off_bsum, off_e;
     };
     std::vector<XEnt> xe;
-    auto eligible = [](const KernelCudaMatmulJob &j) {
+    auto has_rows = [&](int i) { return rows && rows[i].x && rows[i].y; };
+    auto eligible = [&](int i) {
+        const KernelCudaMatmulJob &j = jobs[i];
         const long long rb = (long long)(j.cols / 256) * (j.is_q6 ? 210 : 144);
-        return j.T >= 64 && aligned16(j.matrix) && aligned16(j.X) && rb % 16 == 0 && j.rows < (1u << 30) &&
-               j.T < (1u << 30);
+        bool ok = j.T >= 64 && aligned16(j.matrix) && rb % 16 == 0 && j.rows < (1u << 30) && j.T < (1u << 30);
+        if (ok && has_rows(i)) {
+            for (size_t t = 0; t < j.T && ok; t++)
+                ok = rows[i].x[t] && aligned16(rows[i].x[t]) && rows[i].y[t];
+        } else if (ok) {
+            ok = aligned16(j.X);
+        }
+        return ok;
     };
     long long tiles = 0;
     for (int i = 0; i < n; i++)
-        if (eligible(jobs[i]))
+        if (eligible(i))
             tiles += (long long)((jobs[i].rows + tcm::kRows - 1) / tcm::kRows) *
                      (long long)((jobs[i].T + tcm::kTok - 1) / tcm::kTok);
     const bool use_tc = tiles >= 64;
@@ -2162,23 +2188,28 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         const CUtensorMap *map;
         int x, nb, rtiles, ctiles;
         int parts;
+        int idx;
     };
     std::vector<Sel> sel[2];
     long long ftiles[2] = {0, 0};
+    for (int i = 0; i < n; i++)
+        if (has_rows(i) && (!use_tc || !eligible(i)))
+            return 1;                        // nothing launched: the caller takes another route
     for (int i = 0; i < n; i++) {
         const KernelCudaMatmulJob &j = jobs[i];
         const int nb = (int)(j.cols / 256);
         const long long rb = (long long)nb * (j.is_q6 ? 210 : 144);
-        if (!use_tc || !eligible(j)) {
+        if (!use_tc || !eligible(i)) {
             others.push_back(j);
             continue;
         }
+        const float *const *xr = has_rows(i) ? rows[i].x : nullptr;
         int x = -1;
         for (size_t q = 0; q < xe.size(); q++)
-            if (xe[q].X == j.X && xe[q].cols == j.cols && xe[q].T == j.T)
+            if (xe[q].xr == xr && (xr || xe[q].X == j.X) && xe[q].cols == j.cols && xe[q].T == j.T)
                 x = (int)q;
         if (x < 0) {
-            xe.push_back(XEnt{j.X, j.cols, j.T, 0, 0, 0});
+            xe.push_back(XEnt{j.X, xr, j.cols, j.T, 0, 0, 0});
             x = (int)xe.size() - 1;
         }
         const CUtensorMap *map = job_map(static_cast<const unsigned char *>(j.matrix), (long long)j.rows, (int)rb,
@@ -2186,7 +2217,7 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         if (!map)
             return -1;
         const int rtiles = (int)((j.rows + tcm::kRows - 1) / tcm::kRows), ctiles = (int)((j.T + tcm::kTok - 1) / tcm::kTok);
-        sel[j.is_q6 ? 1 : 0].push_back(Sel{&j, map, x, nb, rtiles, ctiles, 1});
+        sel[j.is_q6 ? 1 : 0].push_back(Sel{&j, map, x, nb, rtiles, ctiles, 1, i});
         ftiles[j.is_q6 ? 1 : 0] += (long long)rtiles * ctiles;
     }
     if (xe.empty())
@@ -2254,6 +2285,17 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
         return -1;
     RParams rp;
     memset(static_cast<void *>(&rp), 0, sizeof(rp));
+    int nyr[2] = {0, 0}, nry = 0, nxr = 0;  // row-table entries used: tp[k].yr, rp.yr, pp.xr
+    // a row table of T entries at the end of `tab` (capacity kRowTab); -1 when it does not fit
+    auto put_rows = [](auto *tab, int &used, auto *src, size_t T) -> int {
+        if (used + (long long)T > kRowTab)
+            return -1;
+        const int at = used;
+        for (size_t t = 0; t < T; t++)
+            tab[at + t] = src[t];
+        used += (int)T;
+        return at;
+    };
     {
         float *part = reinterpret_cast<float *>(ws + off_part);
         for (int k = 0; k < 2; k++) {
@@ -2263,18 +2305,22 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
                 const KernelCudaMatmulJob &j = *q.j;
                 const XEnt &e = xe[q.x];
                 const long long plane = (long long)j.T * j.rows;
+                int yr0 = -1;
+                if (has_rows(q.idx) && (yr0 = S > 1 ? put_rows(rp.yr, nry, rows[q.idx].y, j.T)
+                                                    : put_rows(P.yr, nyr[k], rows[q.idx].y, j.T)) < 0)
+                    return 1;                // tables full, nothing launched yet
                 for (int h = 0; h < S; h++) {
                     const int b0 = h * q.nb / S, b1 = (h + 1) * q.nb / S;
                     P.jobs[P.njobs++] = TJob{q.map, reinterpret_cast<const uint4 *>(ws + e.off_bq),
                                              reinterpret_cast<const uint4 *>(ws + e.off_bsum),
                                              reinterpret_cast<const int *>(ws + e.off_e), S > 1 ? part + h * plane : j.Y,
                                              P.items, (int)j.rows, b1 - b0, (int)j.T, q.rtiles, q.ctiles, b0, q.nb,
-                                             S > 1 ? 1 : 0};
+                                             S > 1 ? 1 : 0, S > 1 ? -1 : yr0};
                     P.items += (long long)q.rtiles * q.ctiles;
                 }
                 if (S > 1) {
                     rp.jobs[rp.njobs++] = RJob{part, j.Y, reinterpret_cast<const int *>(ws + e.off_e), rp.n, (int)j.rows,
-                                               (int)j.T, S};
+                                               (int)j.T, S, yr0};
                     rp.n += plane;
                     part += S * plane;
                 }
@@ -2285,8 +2331,11 @@ int matmul_tc_chunk(const KernelCudaMatmulJob *jobs, int n, std::vector<KernelCu
     memset(static_cast<void *>(&pp), 0, sizeof(pp));
     long long ctas = 0;
     for (const XEnt &e : xe) {
+        const int xr0 = e.xr ? put_rows(pp.xr, nxr, e.xr, e.T) : -1;
+        if (e.xr && xr0 < 0)
+            return 1;
         pp.jobs[pp.njobs++] = PJobTc{e.X, reinterpret_cast<uint4 *>(ws + e.off_bq), reinterpret_cast<uint4 *>(ws + e.off_bsum),
-                                     reinterpret_cast<int *>(ws + e.off_e), (int)e.T, (int)e.cols, (int)ctas};
+                                     reinterpret_cast<int *>(ws + e.off_e), (int)e.T, (int)e.cols, (int)ctas, xr0};
         ctas += (long long)((e.T + tcm::kTok - 1) / tcm::kTok * tcm::kTok);
     }
     if (ctas >= (1ll << 31))
@@ -2338,6 +2387,34 @@ extern "C" int kernel_cuda_matvec_quant_batch(const KernelCudaMatvecJob *jobs, i
             return -1;
     return 0;
 }
+
+namespace rb {
+
+int matmul_quant_rows(const KernelCudaMatmulJob *jobs, int n, const MmRows *rows)
+{
+    if (ensure() != 0)
+        return -1;
+    if (n < 0 || n > kMaxJobs || (n > 0 && (!jobs || !rows)))
+        return 1;
+    for (int i = 0; i < n; i++) {
+        const KernelCudaMatmulJob &j = jobs[i];
+        if (!j.matrix || !j.X || !j.Y || !j.rows || !j.cols || !j.T || j.cols % 256 != 0 ||
+            j.rows > 0xFFFFFFFFull || j.cols > 0xFFFFFFFFull || j.T > 0xFFFFFFFFull)
+            return fail("matmul with row tables: job %d invalid", i);
+    }
+    std::vector<KernelCudaMatmulJob> small;
+    const int rc = matmul_tc_chunk(jobs, n, small, rows);
+    if (rc != 0)
+        return rc;
+    std::vector<KernelCudaMatvecJob> rest;
+    if (!small.empty() && matmul_chunk(small.data(), (int)small.size(), rest) != 0)
+        return -1;
+    return rest.empty() ? 0 : kernel_cuda_matvec_quant_batch(rest.data(), (int)rest.size());
+}
+
+}  // namespace rb
+
+using namespace rb;
 
 extern "C" int kernel_cuda_matmul_quant_batch(const KernelCudaMatmulJob *jobs, int n)
 {

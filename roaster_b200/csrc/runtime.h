@@ -11,6 +11,8 @@
 #include <utility>
 #include <vector>
 
+#include "../../include/roaster_cuda.h"
+
 namespace rb {
 
 // Device error word bits, set by kernels instead of faulting.
@@ -54,6 +56,17 @@ int check(cudaError_t e, const char *what);
 int launched(const char *what);
 // Add `n` to the launch count (kernels launched as part of a CUDA graph).
 void count_launches(uint64_t n);
+
+// Per-token rows of one k-quant matmul job: x[t] (16-byte aligned) holds token t's activations,
+// y[t] receives its results. Both null: the job's contiguous X and Y.
+struct MmRows {
+    const float *const *x;
+    float *const *y;
+};
+// kernel_cuda_matmul_quant_batch with optional row tables (one MmRows per job). The jobs with
+// tables must all run on the tensor-core path; when one cannot, nothing is launched and 1 is
+// returned. 0 = launched, -1 = error.
+int matmul_quant_rows(const KernelCudaMatmulJob *jobs, int n, const MmRows *rows);
 // Device scratch of at least `bytes` (grow-only; growing synchronises the stream).
 void *scratch(size_t bytes);
 // The library's second stream, for input copies that overlap kernels on the work stream

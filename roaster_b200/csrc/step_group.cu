@@ -336,6 +336,36 @@ int enqueue_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepG
     for (const Entry &e : mv)
         if (!e.job.matrix || !e.job.vector || !e.job.output || e.job.rows == 0 || e.job.cols == 0 || e.job.cols % 256 != 0)
             return fail("kernel_step_group_matvec: member %d has an invalid job", e.member);
+    {
+        // First choice: the merged products read each member's vector and write each member's
+        // output in place (per-token row tables of the tensor-core matmul), with no gather into
+        // or scatter out of the group's staging. The matmul launches nothing and returns 1 when
+        // a product cannot run that way (too few tokens for the tensor-core path, a vector not
+        // 16-byte aligned); the gathered form below then runs instead.
+        std::vector<KernelCudaMatmulJob> rj;
+        std::vector<MmRows> rr;
+        std::vector<std::vector<float *>> youts(groups.size());
+        for (size_t q = 0; q < groups.size(); q++) {
+            const Group &gr = groups[q];
+            const KernelCudaMatvecJob &k = gr.key;
+            if (gr.idx.size() == 1) {
+                const KernelCudaMatvecJob &j = mv[gr.idx[0]].job;
+                rj.push_back(KernelCudaMatmulJob{j.is_q6, j.matrix, j.vector, j.output, j.rows, j.cols, 1});
+                rr.push_back(MmRows{nullptr, nullptr});
+                continue;
+            }
+            for (int i : gr.idx)
+                youts[q].push_back(mv[i].job.output);
+            const XBlock &xb = xblocks[gxb[q]];
+            // X and Y name the first token's rows; the tables carry every token's
+            rj.push_back(KernelCudaMatmulJob{k.is_q6, k.matrix, xb.vecs[0], youts[q][0], k.rows, k.cols,
+                                             gr.idx.size()});
+            rr.push_back(MmRows{xb.vecs.data(), youts[q].data()});
+        }
+        const int rc = matmul_quant_rows(rj.data(), (int)rj.size(), rr.data());
+        if (rc != 1)
+            return rc;
+    }
     if (grow(&g->xbuf, &g->xcap, xfl) != 0 || grow(&g->ybuf, &g->ycap, yfl) != 0)
         return -1;
     std::vector<KernelCudaMatmulJob> jobs;
