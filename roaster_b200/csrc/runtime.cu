@@ -473,6 +473,7 @@ void kernel_cuda_trim_scratch(void)
     g_rt.scratch = nullptr;
     g_rt.scratch_bytes = 0;
     g_rt.pinned = nullptr;
+    g_rt.gen++;                      // recorded work may not point into the freed buffers
     g_rt.pinned_bytes = 0;
 }
 
@@ -491,7 +492,10 @@ void kernel_cuda_shutdown(void)
         cudaStreamDestroy(g_rt.out_stream);
     if (g_rt.counters)
         cudaFree(g_rt.counters);
+    // the generation stays monotonic across a shutdown: recordings made before it never match
+    const uint64_t gen = g_rt.gen + 1;
     g_rt = Runtime();
+    g_rt.gen = gen;
 }
 
 int kernel_cuda_set_stream(void *stream)

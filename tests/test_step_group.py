@@ -523,3 +523,50 @@ def test_group_projections_in_place_at_64_members(rb, oracle_lib):
     for m in ids:
         g.leave(m)
     g.close()
+
+
+@pytest.mark.gpu
+def test_group_recording_not_replayed_after_the_scratch_moves(rb, oracle_lib):
+    """A recording points into the library's scratch. Between rounds the library's buffers are
+    released (kernel_cuda_trim_scratch, under the group's lock); the next occurrence of the job list
+    must be recorded again, not replayed into freed memory. Every round's outputs (zeroed before
+    it) match one call per slot."""
+    import torch
+    import oracle as O
+    from roaster_b200 import synth
+    from tests.gpu_util import dev, host
+    N = 8
+    w4 = dev(synth.quant_matrix(91, 512, 1024, False))
+    rng = np.random.default_rng(13)
+    xs = [dev(rng.standard_normal(1024).astype(np.float32)) for _ in range(N)]
+    ref = [torch.zeros(512, device="cuda") for _ in range(N)]
+    for i in range(N):
+        rb.matvec_quant_batch([(False, w4, xs[i], ref[i], 512, 1024)])
+    got = [torch.zeros(512, device="cuda") for _ in range(N)]
+    torch.cuda.synchronize()
+    g = R.StepGroup(N, straggler_us=5_000_000)
+    ids = [g.join() for _ in range(N)]
+
+    def rounds(n):
+        def member(i):
+            for _ in range(n):
+                got[i].zero_()
+                assert g.begin(ids[i]) == N
+                assert g.matvec(ids[i], 0, [(False, w4, xs[i], got[i], 512, 1024)]) == 0, R.last_error()
+                assert g.end(ids[i]) == 0
+        _run(N, member)
+        rb.synchronize()
+        for i in range(N):
+            assert O.maxrel(host(got[i]), host(ref[i])) <= 1e-5
+
+    rounds(3)                                    # plain, recorded, replayed
+    assert g.stats()["replayed"] == 1
+    g.lock()                                     # the library frees its scratch and staging
+    rb.lib().kernel_cuda_trim_scratch()
+    g.unlock()
+    rb.synchronize()
+    rounds(2)                                    # recorded again, then replayed
+    assert g.stats()["replayed"] == 2 and g.stats()["errors"] == 0
+    for m in ids:
+        g.leave(m)
+    g.close()
