@@ -712,7 +712,7 @@ def run_batched_step(R, torch, dev, stream, steps: int, rank: int, slots: int = 
         if drv.slot_threads_run(C.c_void_p(g._h), slots, ids, n, len(per_site), ps, jobs, total) != 0:
             raise RuntimeError("step group: " + R.last_error())
 
-    group_rounds(2)
+    group_rounds(3)          # warm-up: plain launches, then each layer's call recorded
     R.synchronize()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -141,8 +141,8 @@ struct KernelStepGroup {
         std::vector<uintptr_t> key;
         cudaGraphExec_t exec = nullptr;
         uint64_t gen = 0;                    // Runtime::gen when recorded
+        uint64_t plain_gen = ~0ull;          // Runtime::gen after its last plain run
         uint64_t launches = 0, products = 0, merged_jobs = 0;
-        int seen = 0;
     };
     std::unordered_map<uint64_t, Recorded> recorded;
     cudaStream_t rec_stream = nullptr;       // the stream recording happens on
@@ -425,8 +425,9 @@ void drop_recorded(KernelStepGroup *g)
 
 // A projection call: the first occurrence of a job list runs as plain launches (it sets up the
 // buffers and tensor maps it needs), the second is recorded into a CUDA graph and launched, later
-// ones replay the graph while the library's buffers are the ones it was recorded with. Where
-// recording fails the call runs as plain launches.
+// ones replay the graph while the library's buffers are the ones it was recorded with. After the
+// buffers change, the list runs plainly once more before it is recorded again. Where recording
+// fails the call runs as plain launches.
 int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroupStats *st)
 {
     if (!recording_enabled())
@@ -471,8 +472,14 @@ int run_matvec(KernelStepGroup *g, const std::vector<Entry> &mv, KernelStepGroup
         cudaGraphExecDestroy(r.exec);
         r.exec = nullptr;
     }
-    if (r.seen++ == 0)
-        return enqueue_matvec(g, mv, st);
+    if (r.plain_gen != gen) {
+        // Not yet run with the library's current buffers: run plainly (it allocates whatever it
+        // needs), so that a recording made at the next occurrence allocates nothing -- an
+        // allocation, a free or a synchronisation cannot be part of a capture.
+        const int rc = enqueue_matvec(g, mv, st);
+        r.plain_gen = R.gen;
+        return rc;
+    }
     if (!g->rec_stream && cudaStreamCreateWithFlags(&g->rec_stream, cudaStreamNonBlocking) != cudaSuccess) {
         (void)cudaGetLastError();
         g->rec_stream = nullptr;
