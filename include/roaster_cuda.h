@@ -51,7 +51,8 @@ extern "C" {
 int  kernel_cuda_init(int device);
 /* Free every library-owned device/pinned buffer. The library can be re-initialised. */
 void kernel_cuda_shutdown(void);
-/* Free the grow-only scratch (split-KV partials, staging); recreated on demand. */
+/* Free the grow-only scratch (split-KV partials, staging); recreated on demand. Step groups then
+ * run their recorded projection calls plainly once and record them again. */
 void kernel_cuda_trim_scratch(void);
 /* Stream for all subsequent work (a cudaStream_t; NULL = the legacy default stream). */
 int  kernel_cuda_set_stream(void *stream);
