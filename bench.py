@@ -1039,6 +1039,63 @@ def run_recurrent(R, torch, dev, stream, steps: int, warmup: int, parity: bool) 
     return res
 
 
+def run_layer_block(R, torch, dev, stream, steps: int, warmup: int) -> dict:
+    """Config 1 with the recurrent-layer block around the recurrence (model.c:1291-1343 without
+    the projections): per step, one kernel_deltanet_preop_batch (conv1d + SiLU + L2-norm + beta/g
+    and the history shift, 30 jobs), one kernel_deltanet_step_batch and one
+    kernel_deltanet_postop_batch (gated RMSNorm), timed like run_recurrent (a 256 MB device write
+    before every step, each step timed alone), so the difference from the recurrence alone is what
+    the pre/post-op launches cost per decode step."""
+    from roaster_b200 import synth
+    L = RECUR_LAYERS
+    d = synth.delta_layer_inputs(9200, 1)
+    rep = lambda x: torch.from_numpy(x).to(dev).expand(L, *x.shape).contiguous()  # noqa: E731
+    qkv, z, alpha, beta = (rep(d[k]) for k in ("qkv", "z", "alpha", "beta"))
+    conv_w, dt, av, norm_w = (rep(d[k]) for k in ("conv_w", "dt", "a", "ssm_norm"))
+    conv_state = rep(d["conv_state"])
+    states = synth.device_normal(torch, (L, 32, 128, 128), 9201, dev, torch.float32, std=0.02)
+    q = torch.empty(L, 16, 128, device=dev)
+    k = torch.empty(L, 16, 128, device=dev)
+    v = torch.empty(L, 32, 128, device=dev)
+    g = torch.empty(L, 32, device=dev)
+    b = torch.empty(L, 32, device=dev)
+    out = torch.empty(L, 32, 128, device=dev)
+    P = lambda t, l: t[l].data_ptr()  # noqa: E731
+    pre = (R.KernelDeltaPreopJob * L)(*[R.KernelDeltaPreopJob(
+        P(qkv, l), P(alpha, l), P(beta, l), P(conv_state, l), P(conv_w, l), P(dt, l), P(av, l),
+        P(q, l), P(k, l), P(v, l), P(g, l), P(b, l), 1) for l in range(L)])
+    stp = (R.KernelDeltaStepJob * L)(*[R.delta_job(P(states, l), P(q, l), P(k, l), P(v, l), P(g, l), P(b, l),
+                                                   P(out, l)) for l in range(L)])
+    post = (R.KernelDeltaPostopJob * L)(*[R.KernelDeltaPostopJob(P(out, l), P(z, l), P(norm_w, l), 1)
+                                          for l in range(L)])
+    lib = R.lib()
+
+    def step():
+        if (lib.kernel_deltanet_preop_batch(pre, L) != 0 or lib.kernel_deltanet_step_batch(stp, L) != 0
+                or lib.kernel_deltanet_postop_batch(post, L) != 0):
+            raise RuntimeError(R.last_error())
+
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)          # 256 MB > L2
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    launches0 = R.launch_count()
+    for i in range(steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    launches = R.launch_count() - launches0
+    R.synchronize()
+    if not bool(torch.isfinite(out).all()):
+        raise RuntimeError("layer block: non-finite outputs")
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    del qkv, z, alpha, beta, conv_w, dt, av, norm_w, conv_state, states, q, k, v, g, b, out, flush
+    return {"ms": ms, "launches": launches}
+
+
 def attn_step_bytes(n: int, mean_L: float) -> float:
     """Algorithmic bytes of one decode-attention launch over n slots of mean window mean_L:
     the f16 K/V rows (2 kv heads x K,V x 256 x 2 B per position), the appended row, q/gate/out."""
@@ -1521,6 +1578,18 @@ def run_ours(a):
                               "algorithmic_bytes_per_step": rbytes,
                               "scope": "state read + write, inputs and outputs of the 30 layers per step"},
                  "scope": "rank 0 only (one slot does not shard)"}
+        try:
+            lb = run_layer_block(R, torch, dev, stream, a.recurrent_steps, 3)
+            recur["layer_block"] = {
+                "ms_per_step": round(lb["ms"], 5), "value": round(1e3 / lb["ms"], 1), "unit": "tok/s",
+                "extra_ms_vs_recurrence": round(lb["ms"] - r1["ms"], 5),
+                "gpu_launches_per_step": round(lb["launches"] / a.recurrent_steps, 2),
+                "what": "per step the 30 layers' pre-ops (conv1d + SiLU + L2-norm + beta/g, history shift), "
+                        "the recurrence and the gated-RMSNorm post-op: kernel_deltanet_preop_batch + "
+                        "kernel_deltanet_step_batch + kernel_deltanet_postop_batch, timed as the recurrence "
+                        "alone is (L2 flushed before each step)"}
+        except Exception as e:  # reported, not fatal
+            recur["layer_block"] = {"ms_per_step": None, "what": f"failed: {e}"[:300]}
         if "parity_file" in r1:
             try:
                 pr = cpu_leg("parity1", path=r1["parity_file"], timeout=900)

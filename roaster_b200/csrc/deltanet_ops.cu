@@ -13,9 +13,13 @@
 //
 // deltanet_preop_kernel: one CTA per (128-channel block, token), one thread per channel; the 16
 // q and 16 k blocks are exactly one head each, so the L2 norm is a CTA reduction.
-// deltanet_history_kernel: the history shift, after every token has read the old history.
+// deltanet_history_kernel: the history shift of prompts (T > 1), after every token has read the
+// old history; a decode token's shift is done by the pre-op thread that read the rows.
 // deltanet_postop_kernel: one warp per (token, value head) row.
-// All three are HBM/latency-bound elementwise work; fp32 throughout.
+// All three are HBM/latency-bound elementwise work; fp32 throughout. They launch as programmatic
+// dependents, so a decode step's pre-op, recurrence and post-op launches overlap one another's
+// ramp and drain.
+#include "ptx.cuh"
 #include "runtime.h"
 #include "../../include/roaster_cuda.h"
 
@@ -36,7 +40,7 @@ constexpr int kMaxJobs = 64;
 
 struct PreJob {
     const float *qkv, *alpha, *beta;
-    const float *conv_state;
+    float *conv_state;                 // shifted here for a job of one token (T = 1)
     const float *conv_w, *dt, *a;
     float *q, *k, *v, *g, *b;
     long long T, tok0;
@@ -72,6 +76,10 @@ __device__ __forceinline__ float sigmoid_stable(float x)
 __global__ void __launch_bounds__(128) deltanet_preop_kernel(const __grid_constant__ PreParams p)
 {
     __shared__ float red[4];
+    // launched as a programmatic dependent (as are the history and post-op kernels): every input
+    // may be the previous kernel's output, so nothing is read or written before the wait
+    griddep_wait();
+    griddep_launch_dependents();
     const long long gtok = blockIdx.y;
     const PreJob &J = p.jobs[find_job(p, gtok)];
     const long long t = gtok - J.tok0;
@@ -82,7 +90,15 @@ __global__ void __launch_bounds__(128) deltanet_preop_kernel(const __grid_consta
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const long long s = t - 3 + j;
-        x[j] = s >= 0 ? __ldg(J.qkv + s * kQKV + c) : __ldg(J.conv_state + (s + 3) * kQKV + c);
+        x[j] = s >= 0 ? __ldg(J.qkv + s * kQKV + c) : J.conv_state[(s + 3) * kQKV + c];
+    }
+    if (J.T == 1) {
+        // a decode token: the new history is the old rows 1, 2 and this token's input. The thread
+        // that read channel c's rows is the only one to touch them, so it shifts them itself
+        // (prompts of several tokens leave it to deltanet_history_kernel, after every token's read).
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            J.conv_state[j * kQKV + c] = x[j + 1];
     }
     const float4 w = __ldg(reinterpret_cast<const float4 *>(J.conv_w) + c);
     float sum = x[0] * w.x;
@@ -127,6 +143,8 @@ struct HistParams {
 // New history rows = raw inputs of tokens T-3, T-2, T-1 (old rows where T < 3).
 __global__ void __launch_bounds__(256) deltanet_history_kernel(const __grid_constant__ HistParams p)
 {
+    griddep_wait();                  // the pre-op kernel reads the rows this kernel replaces
+    griddep_launch_dependents();
     const HistJob &J = p.jobs[blockIdx.y];
     const int c = blockIdx.x * 256 + threadIdx.x;
     float h[3];
@@ -154,6 +172,8 @@ struct PostParams {
 __global__ void __launch_bounds__(256) deltanet_postop_kernel(const __grid_constant__ PostParams p,
                                                               long long total_rows)
 {
+    griddep_wait();                  // `out` is the recurrence's output
+    griddep_launch_dependents();
     const long long grow = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (grow >= total_rows)
         return;
@@ -192,7 +212,7 @@ int preop_chunk(const KernelDeltaPreopJob *jobs, int n)
     memset(static_cast<void *>(&pp), 0, sizeof(pp));
     memset(static_cast<void *>(&hp), 0, sizeof(hp));
     long long tok = 0;
-    int m = 0;
+    int m = 0, mh = 0;                  // jobs; jobs of several tokens (history shifted apart)
     for (int i = 0; i < n; i++) {
         const KernelDeltaPreopJob &j = jobs[i];
         if (!j.qkv || !j.alpha || !j.beta || !j.conv_state || !j.conv_w || !j.dt || !j.a || !j.q || !j.k ||
@@ -204,7 +224,8 @@ int preop_chunk(const KernelDeltaPreopJob *jobs, int n)
             continue;
         pp.jobs[m] = PreJob{j.qkv, j.alpha, j.beta, j.conv_state, j.conv_w, j.dt, j.a,
                             j.q, j.k, j.v, j.g, j.beta_out, (long long)j.T, tok};
-        hp.jobs[m] = HistJob{j.qkv, j.conv_state, (long long)j.T};
+        if (j.T > 1)
+            hp.jobs[mh++] = HistJob{j.qkv, j.conv_state, (long long)j.T};
         tok += (long long)j.T;
         m++;
     }
@@ -222,12 +243,13 @@ int preop_chunk(const KernelDeltaPreopJob *jobs, int n)
         const unsigned ny = (unsigned)std::min<long long>(65535, tok - t0);
         // tokens before the slice map to negative indices in ps; find_job only sees
         // blockIdx.y >= 0, i.e. tokens t0 .. t0 + ny - 1
-        deltanet_preop_kernel<<<dim3(64, ny), 128, 0, st>>>(ps);
-        if (launched("deltanet_preop_kernel") != 0)
+        if (launch_dependent(deltanet_preop_kernel, dim3(64, ny), dim3(128), 0, st, "deltanet_preop_kernel", ps) != 0)
             return -1;
     }
-    deltanet_history_kernel<<<dim3(kQKV / 256, m), 256, 0, st>>>(hp);
-    return launched("deltanet_history_kernel");
+    if (mh == 0)
+        return 0;
+    return launch_dependent(deltanet_history_kernel, dim3(kQKV / 256, mh), dim3(256), 0, st, "deltanet_history_kernel",
+                            hp);
 }
 
 int postop_chunk(const KernelDeltaPostopJob *jobs, int n)
@@ -250,8 +272,8 @@ int postop_chunk(const KernelDeltaPostopJob *jobs, int n)
     if (m == 0)
         return 0;
     pp.njobs = m;
-    deltanet_postop_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, rt().stream>>>(pp, rows);
-    return launched("deltanet_postop_kernel");
+    return launch_dependent(deltanet_postop_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, rt().stream,
+                            "deltanet_postop_kernel", pp, rows);
 }
 
 }  // namespace
