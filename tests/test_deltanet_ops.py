@@ -59,6 +59,34 @@ def test_preop_ragged_batch(rb, oracle_lib):
         assert np.array_equal(conv, cs)
 
 
+def test_preop_decode_steps_in_sequence(rb, oracle_lib):
+    """Five decode steps of two layers, one batch of two one-token jobs per step, queued back to
+    back on the stream without a host sync between them: a decode token's history shift happens
+    inside the pre-op kernel, so each step's conv must read the rows the step before wrote."""
+    steps, layers = 5, 2
+    ds = [synth.delta_layer_inputs(60 + l, steps) for l in range(layers)]
+    dev_in = [{k: dev(d[k]) for k in ("qkv", "alpha", "beta", "conv_state", "conv_w", "dt", "a")} for d in ds]
+    outs = [[{"q": torch.zeros(1, 16, 128, device="cuda"), "k": torch.zeros(1, 16, 128, device="cuda"),
+              "v": torch.zeros(1, 32, 128, device="cuda"), "g": torch.zeros(1, 32, device="cuda"),
+              "beta": torch.zeros(1, 32, device="cuda")} for _ in range(layers)] for _ in range(steps)]
+    for s in range(steps):
+        jobs = []
+        for l in range(layers):
+            t, o = dev_in[l], outs[s][l]
+            jobs.append((t["qkv"][s:s + 1], t["alpha"][s:s + 1], t["beta"][s:s + 1], t["conv_state"], t["conv_w"],
+                         t["dt"], t["a"], o["q"], o["k"], o["v"], o["g"], o["beta"], 1))
+        rb.deltanet_preop_batch(jobs)
+    rb.synchronize()
+    for l, d in enumerate(ds):
+        cs = d["conv_state"].copy()
+        for s in range(steps):
+            ref = O.delta_preop(d["qkv"][s:s + 1], d["alpha"][s:s + 1], d["beta"][s:s + 1], cs, d["conv_w"],
+                                d["dt"], d["a"])
+            for k in ("q", "k", "v", "g", "beta"):
+                assert O.maxrel(host(outs[s][l][k]), ref[k]) < TOL_OP, (s, l, k)
+        assert np.array_equal(host(dev_in[l]["conv_state"]), cs)
+
+
 @pytest.mark.parametrize("T", [1, 70])
 def test_postop(rb, oracle_lib, T):
     rng = np.random.default_rng(40 + T)
